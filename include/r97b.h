@@ -1,0 +1,157 @@
+/* include/r97b.h -- the C ABI of libr97b200.so, the B200 (sm_100a) kernels of the LoRA-over-IQR
+ * training path.
+ *
+ * Conventions shared by every entry point:
+ *   - pointers are DEVICE pointers unless a comment says otherwise; sizes are element counts;
+ *   - `stream` is a cudaStream_t passed as void* (null = the legacy default stream);
+ *   - every call is asynchronous on `stream` and returns an int status (R97B_OK or an error code);
+ *   - bf16 tensors are passed as uint16_t* (raw bits), f32 as float*, row-major, dense unless a
+ *     leading dimension says otherwise.
+ * No torch, CUDA-runtime or C++ types cross this boundary.
+ *
+ * Each declaration names the reference interface it replaces (file:line in the reference tree).
+ */
+#ifndef R97B_H
+#define R97B_H
+
+#include <stdint.h>
+
+#include "r97b_iqr.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+    R97B_OK = 0,
+    R97B_EINVAL = 1,   /* arguments outside the kernel's rules (same meaning as the reference's 1) */
+    R97B_ELAUNCH = 2,  /* a launch failed */
+    R97B_EDEVICE = 3,  /* a device-side check fired (see r97b_device_error) */
+};
+
+/* ------------------------------------------------------------------------------ library */
+
+/* The library's ABI version (bumped on any signature change). */
+int r97b_abi_version(void);
+
+/* The device error word the kernels set (bit 0: a bounded wait expired; bit 1: a kernel rejected its
+ * arguments) -- read and cleared. Synchronises the current device. */
+int r97b_device_error(unsigned int* out_bits);
+
+/* ------------------------------------------------------------------------------ IQR decode */
+
+/* Reference-compatible decode: stored trellis/affine IQR codes -> int8 grid [rows, cols] plus bf16 scale
+ * bits [rows, cols/128], asynchronously on `stream`. Returns 0, or 1 when the description is outside
+ * the decode's rules (r97_iqr_validate) or `stream` cannot be launched on. All plane pointers and
+ * outputs are device pointers.
+ * Replaces: reference src/iqr_decode.h:378-386 (extern "C" int r97_iqr_decode) and its HIP kernel
+ * src/adjoint/device/iqr_decode.hip:32-56. */
+int r97_iqr_decode(const R97IqrDecodeDesc* desc, R97IqrStream stream);
+
+/* The GEMM operand form of the same decode: W[r, k] = bf16(code[r, k] * scale[r, k/128]) written as
+ * bf16 bits into `out_w` (row stride `ld_w` elements), for rows [row0, row0 + rows). The desc's
+ * out_codes / out_scale are ignored. One extra bf16 rounding of the product against the int8+scale
+ * pair the reference's kernels read (reference src/adjoint/host/linear.cpp:132-163 value_at).
+ * Replaces: the decode half of the reference's stored-weight dX path, linear.hip:601-622. */
+int r97b_iqr_dequant_bf16(const R97IqrDecodeDesc* desc, uint16_t* out_w, int64_t ld_w, void* stream);
+
+/* ------------------------------------------------------------------------------ GEMM */
+
+/* One bf16 operand of logical shape [rows, K]: K-major means stored row-major [rows, K] with row stride
+ * `ld`; MN-major means stored row-major [K, rows] with row stride `ld`. */
+typedef struct R97bMat {
+    const void* ptr;
+    int64_t ld;
+    int32_t mn_major;
+    int32_t _pad;
+} R97bMat;
+
+enum {
+    R97B_EPI_STORE_BF16 = 0,  /* out[m, n] = bf16(alpha * acc + beta * addend[m, n]) */
+    R97B_EPI_STORE_F32 = 1,   /* out[m, n] = alpha * acc + beta * addend[m, n]      */
+    R97B_EPI_ATOMIC_F32 = 2,  /* out[m, n] += alpha * acc  (f32, split-K allowed)   */
+    R97B_EPI_ATOMIC_F32T = 3, /* out[n, m] += alpha * acc  (f32, split-K allowed)   */
+};
+
+/* D[M, N] = alpha * (A1[M, K1] B1[N, K1]^T + A2[M, K2] B2[N, K2]^T) (+ beta * addend), on tcgen05 tensor
+ * cores with f32 accumulation in TMEM. K2 = 0 drops the second segment; when present, a2/b2 have the
+ * same majorness as a1/b1. `splits` > 1 splits the reduction (atomic epilogues only). `bn` picks the
+ * tile width (64, 128, 256; 0 = by N).
+ * Replaces: the reference's linear_dx_kernel (src/adjoint/device/linear.hip:172-285) and the LoRA
+ * kernels shrink_dx / shrink_da / expand_dt / expand_db (src/adjoint/device/lora.hip:268-399). */
+typedef struct R97bGemm {
+    int64_t M, N, K1, K2;
+    R97bMat a1, b1, a2, b2;
+    int32_t mode;
+    int32_t splits;
+    float alpha;
+    float beta;
+    void* out;
+    int64_t ldo;
+    const void* addend;
+    int64_t ld_add;
+    int32_t bn;
+    int32_t _pad;
+} R97bGemm;
+
+int r97b_gemm(const R97bGemm* g, void* stream);
+
+/* ------------------------------------------------------------------------------ norms */
+
+/* y = x * rsqrt(mean(x^2) + eps) * (w + wadd) * mult per row of n (x, y bf16 [rows, n]; w f32 [n] or null;
+ * rstd f32 [rows] or null receives the row's rsqrt). n a multiple of 8, pointers 16-byte aligned.
+ * Replaces: the forward the reference's rmsnorm twin states, src/adjoint/host/elementwise.cpp:459-528. */
+int r97b_rmsnorm_fwd(const uint16_t* x, const float* w, uint16_t* y, float* rstd, int64_t rows, int64_t n, float eps,
+                     float wadd, float mult, void* stream);
+
+/* dx = mult (s c dy - s^3 x / n sum(dy x c)) + addend, c = w + wadd (addend bf16 or null).
+ * Replaces: rmsnorm_adjoint_kernel, src/adjoint/device/elementwise.hip:258,707 (host row
+ * src/adjoint/host/elementwise.cpp:531-670). */
+int r97b_rmsnorm_bwd(const uint16_t* x, const float* w, const uint16_t* dy, const uint16_t* addend, uint16_t* dx,
+                     int64_t rows, int64_t n, float eps, float wadd, float mult, void* stream);
+
+/* o = x * rsqrt(mean(x^2) + eps) * w * act(z), act = silu (act_sigmoid = 0) or sigmoid; per row of n.
+ * Replaces: the gdn_gated_rmsnorm forward, src/adjoint/host/gdn_prep.cpp:501-531. */
+int r97b_gated_rmsnorm_fwd(const uint16_t* x, const uint16_t* z, const float* w, uint16_t* o, int64_t rows, int64_t n,
+                           float eps, int32_t act_sigmoid, void* stream);
+
+/* dx, dz of the gated norm for the cotangent dout. Replaces: gated_rmsnorm_adjoint_kernel,
+ * src/adjoint/device/gdn_prep.hip:643-731 (host row src/adjoint/host/gdn_prep.cpp:541-592). */
+int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, const float* w, const uint16_t* dout, uint16_t* dx,
+                           uint16_t* dz, int64_t rows, int64_t n, float eps, int32_t act_sigmoid, void* stream);
+
+/* ------------------------------------------------------------------------------ loss */
+
+/* Per logit row (bf16, row stride ld): CE = lse - x[target] into loss_ce[row] (target -1: not scored,
+ * loss 0, gradient 0), KL(softmax(teacher) || softmax(x)) into loss_kl[row] when teacher is given, and
+ * grad = grad_scale * (w_ce (softmax - onehot) + w_kl (softmax(x) - softmax(teacher))) as bf16; grad may
+ * equal logits (in place), targets may be null (KL only). loss_ce / loss_kl / grad may be null.
+ * Replaces: HeadCeKernel / head_ce_kernel, include/r97/head.h:28-55 and src/adjoint/device/head.hip:61-106;
+ * the KL term has no counterpart in the reference. */
+int r97b_ce_kld(const uint16_t* logits, const uint16_t* teacher, const int32_t* targets, uint16_t* grad,
+                float* loss_ce, float* loss_kl, int64_t rows, int64_t vocab, int64_t ld, int64_t ld_t,
+                float grad_scale, float w_ce, float w_kl, void* stream);
+
+/* ------------------------------------------------------------------------------ AdamW */
+
+/* One AdamW update of n f32 parameters, bit-identical to the reference's f32 update: g is scaled by inv_k
+ * and by *clip_scale (device f32, or null), then m, v and w are updated; zero_grad clears g afterwards.
+ * lr, bc1 = 1 - beta1^t and bc2 = 1 - beta2^t are the caller's (reference src/optim.cpp:223-307). */
+int r97b_adamw_step(float* w, float* m, float* v, float* g, int64_t n, float lr, float beta1, float beta2, float eps,
+                    float weight_decay, float bc1, float bc2, float inv_k, const float* clip_scale,
+                    int32_t zero_grad, void* stream);
+
+/* Bytes of scratch r97b_global_norm needs for n elements (one f64 per 4096). */
+int64_t r97b_global_norm_scratch_bytes(int64_t n);
+
+/* The global L2 norm of g * inv_k (bit-identical to the reference's chunked f64 sum,
+ * src/optim.cpp:132-176) into *out_norm, and the clip factor for max_norm into *out_scale (both device f32;
+ * out_scale may be null). `partials` is caller scratch of r97b_global_norm_scratch_bytes(n). */
+int r97b_global_norm(const float* g, int64_t n, float inv_k, float max_norm, double* partials, float* out_norm,
+                     float* out_scale, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* R97B_H */

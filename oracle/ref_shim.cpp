@@ -1,0 +1,267 @@
+// oracle/ref_shim.cpp -- TEST INFRASTRUCTURE ONLY. A flat C ABI over the reference's own host rows.
+//
+// This file is compiled together with the reference's radiance-free host sources (the adjoint
+// registry, the host twin/adjoint rows, loss.cpp, optim.cpp, stored_weight.cpp and the header-only
+// iqr_decode.h) into oracle/_ref/libr97ref.so by oracle/Makefile. Nothing of the reference is
+// copied here: the shim builds the reference's own OpRecord / AdValue / AdjointCall values from flat
+// arrays, looks the op up in the reference's registry (twin_find / adjoint_find, the rows registered
+// by R97_REGISTER_TWIN / R97_REGISTER_ADJOINT in src/adjoint/host/*.cpp) and runs it.
+//
+// Only tests/, bench.py's cpu_baseline leg and __graft_entry__.smoke() load this library, and only
+// as a checker or as the timed CPU baseline; the product path never does.
+#include "r97/adjoint.h"
+#include "r97/loss.h"
+#include "r97/optim.h"
+
+#include "iqr_decode.h"
+#include "stored_weight.h"
+
+#include <cstdint>
+#include <cstring>
+#include <exception>
+#include <string>
+#include <vector>
+
+namespace {
+
+struct RefOperand {
+    const char* buffer;
+    const char* dtype;
+    int32_t ndim;
+    const int64_t* shape;
+    int32_t written;
+    int32_t in_place;
+    // A stored IQR weight: codes [rows, cols] int8 and scale [rows, cols/128] bf16 bits. When set,
+    // the AdValue carries `raw`/`enc` instead of values, the way the device join hands a stored
+    // operand to a host row (reference src/stored_weight.h).
+    const int8_t* stored_codes;
+    const uint16_t* stored_scale;
+};
+
+struct RefParam {
+    const char* name;
+    int32_t is_int;
+    int64_t ival;
+    const char* sval;
+};
+
+thread_local std::string g_error;
+r97::ParamSet g_grads;
+
+int64_t numel(const RefOperand& o) {
+    int64_t n = 1;
+    for (int i = 0; i < o.ndim; ++i) n *= o.shape[i];
+    return n;
+}
+
+r97::OpRecord make_record(const char* op, const RefParam* params, int nparams,
+                          const RefOperand* ops, int nops) {
+    r97::OpRecord rec;
+    rec.op = op;
+    for (int i = 0; i < nparams; ++i) {
+        if (params[i].is_int)
+            rec.params.emplace_back(params[i].name, std::variant<int64_t, std::string>(params[i].ival));
+        else
+            rec.params.emplace_back(params[i].name,
+                                    std::variant<int64_t, std::string>(std::string(params[i].sval)));
+    }
+    for (int i = 0; i < nops; ++i) {
+        r97::Operand o;
+        o.buffer = ops[i].buffer;
+        o.dtype = ops[i].dtype;
+        o.shape.assign(ops[i].shape, ops[i].shape + ops[i].ndim);
+        o.written = ops[i].written != 0;
+        o.in_place = ops[i].in_place != 0;
+        rec.operands.push_back(std::move(o));
+    }
+    return rec;
+}
+
+// One key per stored operand: the address of a static byte is a unique encoding pointer.
+unsigned char g_enc_keys[64];
+
+r97::AdValue make_value(const RefOperand& o, const double* v, int slot) {
+    r97::AdValue a;
+    a.dtype = o.dtype;
+    a.shape.assign(o.shape, o.shape + o.ndim);
+    if (o.stored_codes) {
+        const int64_t rows = o.shape[0], cols = o.shape[1];
+        r97::StoredWeight w;
+        w.rows = rows;
+        w.cols = cols;
+        w.groups = cols / 128;
+        w.codes.assign(o.stored_codes, o.stored_codes + rows * cols);
+        w.scale.assign(o.stored_scale, o.stored_scale + rows * (cols / 128));
+        const void* key = &g_enc_keys[slot & 63];
+        r97::stored_weight_put(key, std::move(w));
+        a.raw = key;
+        a.enc = key;
+        return a;
+    }
+    const int64_t n = numel(o);
+    if (v) a.value.assign(v, v + n);
+    else a.value.assign((size_t)n, 0.0);
+    return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ref_last_error() { return g_error.c_str(); }
+
+// The reference host decode, r97_iqr_decode_host (src/iqr_decode.h), on a caller-built description.
+int ref_iqr_decode(const R97IqrDecodeDesc* d) { return r97_iqr_decode_host(*d); }
+
+// Runs the twin registered for `op`. `reads` holds one value array per READ operand in schema order
+// (null for a stored operand); `outs` one array per WRITTEN operand, each sized by its shape.
+int ref_twin(const char* op, const RefParam* params, int nparams, const RefOperand* ops, int nops,
+             const double* const* reads, double* const* outs) {
+    try {
+        g_error.clear();
+        r97::OpRecord rec = make_record(op, params, nparams, ops, nops);
+        std::string err;
+        r97::TwinFn fn = r97::twin_find(rec.op, rec.params, &err);
+        if (!fn) {
+            g_error = err.empty() ? "no twin" : err;
+            return 1;
+        }
+        std::vector<r97::AdValue> operands;
+        int r = 0;
+        for (int i = 0; i < nops; ++i) {
+            if (ops[i].written && !ops[i].in_place) continue;
+            operands.push_back(make_value(ops[i], reads[r], i));
+            ++r;
+        }
+        std::vector<r97::AdValue> out;
+        fn(rec, operands, &out);
+        int w = 0;
+        for (int i = 0; i < nops; ++i) {
+            if (!ops[i].written) continue;
+            if (w >= (int)out.size()) {
+                g_error = "twin produced fewer outputs than the record writes";
+                r97::stored_weight_clear();
+                return 2;
+            }
+            const int64_t n = numel(ops[i]);
+            if ((int64_t)out[(size_t)w].value.size() < n) {
+                g_error = "twin output smaller than its shape";
+                r97::stored_weight_clear();
+                return 3;
+            }
+            std::memcpy(outs[w], out[(size_t)w].value.data(), (size_t)n * sizeof(double));
+            ++w;
+        }
+        r97::stored_weight_clear();
+        return 0;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        r97::stored_weight_clear();
+        return 4;
+    }
+}
+
+// Runs the host adjoint registered for `op`. `fwd` holds every operand's forward value in schema
+// order (null for a stored one), `cots` the cotangent of each written operand in write order, and
+// `dc` one array per operand (schema order, sized by its shape) that the row adds into. Gradients
+// of trainable leaves land in a ParamSet read back with ref_grad_*.
+int ref_adjoint(const char* op, const RefParam* params, int nparams, const RefOperand* ops, int nops,
+                const double* const* fwd, const double* const* cots, double* const* dc,
+                const char* prefix, int fused_slots) {
+    try {
+        g_error.clear();
+        g_grads.clear();
+        r97::OpRecord rec = make_record(op, params, nparams, ops, nops);
+        std::string err;
+        r97::AdjointFn fn = r97::adjoint_find(rec.op, r97::Side::host, rec.params, &err);
+        if (!fn) {
+            g_error = err.empty() ? "no adjoint" : err;
+            return 1;
+        }
+        std::vector<r97::AdValue> f, c, d;
+        for (int i = 0; i < nops; ++i) f.push_back(make_value(ops[i], fwd[i], i));
+        int w = 0;
+        for (int i = 0; i < nops; ++i) {
+            if (!ops[i].written) continue;
+            RefOperand plain = ops[i];
+            plain.stored_codes = nullptr;
+            c.push_back(make_value(plain, cots[w], 100 + i));
+            ++w;
+        }
+        for (int i = 0; i < nops; ++i) {
+            RefOperand plain = ops[i];
+            plain.stored_codes = nullptr;
+            d.push_back(make_value(plain, dc[i], 200 + i));
+        }
+        r97::AdjointCall call{rec, f, c, &d, &g_grads, prefix};
+        call.fused_slots = fused_slots != 0;
+        fn(call);
+        for (int i = 0; i < nops; ++i) {
+            if (!dc[i]) continue;
+            std::memcpy(dc[i], d[(size_t)i].value.data(), d[(size_t)i].value.size() * sizeof(double));
+        }
+        r97::stored_weight_clear();
+        return 0;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        r97::stored_weight_clear();
+        return 4;
+    }
+}
+
+int ref_grad_count() { return (int)g_grads.size(); }
+const char* ref_grad_name(int i) { return g_grads[(size_t)i].name.c_str(); }
+int64_t ref_grad_numel(int i) { return (int64_t)g_grads[(size_t)i].value.size(); }
+void ref_grad_copy(int i, float* out) {
+    std::memcpy(out, g_grads[(size_t)i].value.data(), g_grads[(size_t)i].value.size() * sizeof(float));
+}
+
+// The reference CE of one position (src/loss.cpp ce_position): returns the loss, writes the
+// gradient row when `grad` is non-null.
+double ref_ce_position(const float* row, int64_t vocab, int32_t target, float* grad, double scale) {
+    return r97::ce_position(row, vocab, target, grad, scale);
+}
+
+// `steps` AdamW updates of one flat parameter through the reference Optimiser (src/optim.cpp).
+// `grads` holds `steps` consecutive gradient vectors of `n` floats; `w` is updated in place.
+int ref_adamw(float* w, int64_t n, const float* grads, int steps, float lr, float beta1, float beta2,
+              float eps, float weight_decay, float clip_norm, int warmup, int total, int threads) {
+    try {
+        g_error.clear();
+        r97::ParamSet params;
+        params.push_back(r97::Param{"adapter", {n}, std::vector<float>(w, w + n)});
+        r97::AdamWConfig cfg;
+        cfg.lr = lr;
+        cfg.beta1 = beta1;
+        cfg.beta2 = beta2;
+        cfg.eps = eps;
+        cfg.weight_decay = weight_decay;
+        cfg.clip_norm = clip_norm;
+        cfg.warmup_steps = warmup;
+        cfg.total_steps = total;
+        cfg.threads = threads;
+        r97::Optimiser opt(params, cfg);
+        for (int s = 0; s < steps; ++s) {
+            r97::ParamSet g;
+            g.push_back(r97::Param{"adapter", {n},
+                                   std::vector<float>(grads + (int64_t)s * n, grads + (int64_t)(s + 1) * n)});
+            opt.step(g);
+        }
+        std::memcpy(w, params[0].value.data(), (size_t)n * sizeof(float));
+        return 0;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return 4;
+    }
+}
+
+float ref_scheduled_lr(float lr, int warmup, int total, float floor_frac, int step) {
+    r97::AdamWConfig cfg;
+    cfg.lr = lr;
+    cfg.warmup_steps = warmup;
+    cfg.total_steps = total;
+    cfg.lr_floor_frac = floor_frac;
+    return r97::scheduled_lr(cfg, step);
+}
+
+}  // extern "C"

@@ -1,0 +1,103 @@
+"""Loads libr97b200.so (the sm_100a kernels) through its C ABI (include/r97b.h).
+
+There is no fallback: if the library cannot be built or loaded, every op raises. The library is
+built in-tree by ``r97training_b200.build`` (``__graft_entry__.build()``); when it is missing on a
+machine that has nvcc it is built on first use.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+from . import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+c_i32, c_i64, c_f32, c_vp = ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_void_p
+
+
+class R97bError(RuntimeError):
+    pass
+
+
+class R97bMat(ctypes.Structure):
+    _fields_ = [("ptr", c_vp), ("ld", c_i64), ("mn_major", c_i32), ("_pad", c_i32)]
+
+
+class R97bGemm(ctypes.Structure):
+    _fields_ = [("M", c_i64), ("N", c_i64), ("K1", c_i64), ("K2", c_i64),
+                ("a1", R97bMat), ("b1", R97bMat), ("a2", R97bMat), ("b2", R97bMat),
+                ("mode", c_i32), ("splits", c_i32), ("alpha", c_f32), ("beta", c_f32),
+                ("out", c_vp), ("ldo", c_i64), ("addend", c_vp), ("ld_add", c_i64),
+                ("bn", c_i32), ("_pad", c_i32)]
+
+
+class R97IqrDecodeDesc(ctypes.Structure):
+    """Field-for-field the C struct of include/r97b_iqr.h (the reference's R97IqrDecodeDesc layout)."""
+    _fields_ = [
+        ("rows_all", c_i64), ("cols", c_i64), ("row0", c_i64), ("rows", c_i64),
+        ("bits", c_i32), ("state_bits", c_i32), ("run_rows", c_i32), ("rb", c_i32),
+        ("mad", c_i32), ("round_mad", c_i32), ("mad_a", ctypes.c_uint32), ("mad_b", ctypes.c_uint32),
+        ("lut", c_vp),
+        ("codes", c_vp), ("codes_row_bytes", c_i64),
+        ("scale", c_vp), ("scale_dtype", c_i32), ("scale_block_cols", c_i64), ("scale_row_bytes", c_i64),
+        ("affine", c_i32), ("zero", c_vp), ("zero_bits", c_i32), ("zero_row_bytes", c_i64),
+        ("scale2", c_vp), ("scale2_dtype", c_i32), ("scale2_row_bytes", c_i64),
+        ("scale2_block_rows", c_i64), ("scale2_block_cols", c_i64),
+        ("out_codes", c_vp), ("out_scale", c_vp),
+    ]
+
+
+_SIGS = {
+    "r97b_abi_version": (c_i32, []),
+    "r97b_device_error": (c_i32, [c_vp]),
+    "r97_iqr_decode": (c_i32, [c_vp, c_vp]),
+    "r97b_iqr_dequant_bf16": (c_i32, [c_vp, c_vp, c_i64, c_vp]),
+    "r97b_gemm": (c_i32, [c_vp, c_vp]),
+    "r97b_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
+    "r97b_rmsnorm_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
+    "r97b_gated_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_i32, c_vp]),
+    "r97b_gated_rmsnorm_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_i32, c_vp]),
+    "r97b_ce_kld": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_i64, c_i64, c_f32, c_f32, c_f32,
+                            c_vp]),
+    "r97b_adamw_step": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_f32, c_f32, c_f32, c_f32, c_f32, c_f32, c_f32,
+                                c_f32, c_vp, c_i32, c_vp]),
+    "r97b_global_norm_scratch_bytes": (c_i64, [c_i64]),
+    "r97b_global_norm": (c_i32, [c_vp, c_i64, c_f32, c_f32, c_vp, c_vp, c_vp, c_vp]),
+}
+
+OPTIONAL = set()
+
+
+def lib():
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(_build.LIB):
+                _build.build_kernels()
+            handle = ctypes.CDLL(_build.LIB, mode=ctypes.RTLD_GLOBAL)
+            for name, (res, args) in _SIGS.items():
+                try:
+                    fn = getattr(handle, name)
+                except AttributeError:
+                    if name in OPTIONAL:
+                        continue
+                    raise R97bError(f"{_build.LIB} does not export {name}")
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise R97bError(f"{what} returned status {rc}")
+
+
+def exported_symbols():
+    """Every function name the ABI declares, for the load test."""
+    return sorted(_SIGS)

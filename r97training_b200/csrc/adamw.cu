@@ -1,0 +1,104 @@
+// adamw.cu -- AdamW on the flat f32 adapter buffer, on sm_100a.
+//
+// The per-element update is the reference Optimiser's, in the same f32 operations and the same order
+// (reference src/optim.cpp:245-290, include/r97/optim.h:9-16):
+//   g  = acc * inv_k [* clip]                 (the accumulation mean, then the global-norm clip)
+//   m  = b1 m + (1 - b1) g
+//   v  = b2 v + (1 - b2) g g
+//   w -= lr (m / bc1 / (sqrt(v / bc2) + eps) + wd w)
+// Every product and sum is an explicitly rounded f32 operation (no fused multiply-add), division and
+// square root are IEEE-rounded, so the device update reproduces the reference's x86 f32 arithmetic
+// bit for bit. lr, bc1 = 1 - b1^t and bc2 = 1 - b2^t come from the host, as the reference computes them.
+//
+// The global norm for clipping uses the reference's fixed 4096-element chunking: one f64 partial per
+// chunk summed in element order, then the partials in chunk order (reference src/optim.cpp:135-170), so
+// the norm is bit-identical too.
+#include "r97b_internal.h"
+
+#include <math.h>
+
+namespace r97b {
+namespace {
+
+__global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ w, float* __restrict__ m, float* __restrict__ v,
+                                                    float* __restrict__ g, int64_t n, float lr, float b1, float b2,
+                                                    float eps, float wd, float bc1, float bc2, float inv_k,
+                                                    const float* __restrict__ clip_scale, int zero_grad) {
+    const float one_b1 = __fsub_rn(1.0f, b1), one_b2 = __fsub_rn(1.0f, b2);
+    const float cs = clip_scale ? *clip_scale : 1.0f;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        float gi = __fmul_rn(g[i], inv_k);
+        if (clip_scale) gi = __fmul_rn(gi, cs);
+        const float mi = __fadd_rn(__fmul_rn(b1, m[i]), __fmul_rn(one_b1, gi));
+        const float vi = __fadd_rn(__fmul_rn(b2, v[i]), __fmul_rn(__fmul_rn(one_b2, gi), gi));
+        m[i] = mi;
+        v[i] = vi;
+        const float mh = __fdiv_rn(mi, bc1);
+        const float vh = __fdiv_rn(vi, bc2);
+        const float upd = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), __fmul_rn(wd, w[i]));
+        w[i] = __fsub_rn(w[i], __fmul_rn(lr, upd));
+        if (zero_grad) g[i] = 0.0f;
+    }
+}
+
+constexpr int64_t kNormChunk = 4096;
+
+// One thread per 4096-element chunk: the chunk's f64 sum of squares in element order.
+__global__ void __launch_bounds__(256) chunk_sumsq_kernel(const float* __restrict__ g, int64_t n, float inv_k,
+                                                          double* __restrict__ partials, int64_t nchunks) {
+    const int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= nchunks) return;
+    const int64_t lo = c * kNormChunk;
+    const int64_t hi = lo + kNormChunk < n ? lo + kNormChunk : n;
+    double part = 0.0;
+    for (int64_t i = lo; i < hi; ++i) {
+        const double x = (double)__fmul_rn(g[i], inv_k);
+        part = __dadd_rn(part, __dmul_rn(x, x));
+    }
+    partials[c] = part;
+}
+
+// The partials in chunk order, the norm, and the clip factor (1 when no clip applies).
+__global__ void norm_finish_kernel(const double* __restrict__ partials, int64_t nchunks, float max_norm,
+                                   float* __restrict__ out_norm, float* __restrict__ out_scale) {
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    double sq = 0.0;
+    for (int64_t c = 0; c < nchunks; ++c) sq = __dadd_rn(sq, partials[c]);
+    const float norm = (float)sqrt(sq);
+    if (out_norm) *out_norm = norm;
+    if (out_scale) *out_scale = (max_norm > 0.0f && norm > max_norm && norm > 0.0f) ? __fdiv_rn(max_norm, norm) : 1.0f;
+}
+
+}  // namespace
+}  // namespace r97b
+
+using namespace r97b;
+
+// One AdamW update of `n` f32 parameters. `g` holds the accumulated gradient; it is scaled by `inv_k`
+// (1 / accumulation count) and, when `clip_scale` (a device f32) is given, by that factor, exactly as
+// the reference applies the mean and the clip. `zero_grad` clears `g` after reading it (the reference
+// clears its accumulation buffer after the update).
+extern "C" int r97b_adamw_step(float* w, float* m, float* v, float* g, int64_t n, float lr, float beta1, float beta2,
+                               float eps, float weight_decay, float bc1, float bc2, float inv_k,
+                               const float* clip_scale, int32_t zero_grad, void* stream) {
+    if (!w || !m || !v || !g || n <= 0) return R97B_EINVAL;
+    int blocks = (int)((n + 255) / 256);
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    adamw_kernel<<<blocks, 256, 0, as_stream(stream)>>>(w, m, v, g, n, lr, beta1, beta2, eps, weight_decay, bc1, bc2,
+                                                        inv_k, clip_scale, zero_grad);
+    return launch_status();
+}
+
+// The scratch a global-norm call needs: one f64 partial per 4096 elements.
+extern "C" int64_t r97b_global_norm_scratch_bytes(int64_t n) { return ((n + kNormChunk - 1) / kNormChunk) * 8; }
+
+// The global L2 norm of `g * inv_k` into *out_norm (device f32), and the clip factor for `max_norm` into
+// *out_scale (device f32, may be null). `partials` is caller scratch of r97b_global_norm_scratch_bytes(n).
+extern "C" int r97b_global_norm(const float* g, int64_t n, float inv_k, float max_norm, double* partials,
+                                float* out_norm, float* out_scale, void* stream) {
+    if (!g || n <= 0 || !partials) return R97B_EINVAL;
+    const int64_t nchunks = (n + kNormChunk - 1) / kNormChunk;
+    chunk_sumsq_kernel<<<(unsigned)((nchunks + 255) / 256), 256, 0, as_stream(stream)>>>(g, n, inv_k, partials, nchunks);
+    norm_finish_kernel<<<1, 32, 0, as_stream(stream)>>>(partials, nchunks, max_norm, out_norm, out_scale);
+    return launch_status();
+}

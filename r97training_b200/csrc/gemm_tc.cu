@@ -1,0 +1,406 @@
+// gemm_tc.cu -- the tensor-core GEMM of the LoRA-over-IQR path on sm_100a (tcgen05 + TMA + TMEM).
+//
+//   D[M, N] = alpha * ( sum_k A1[m, k] B1[n, k]  +  sum_k A2[m, k] B2[n, k] )  (+ beta * C[m, n])
+//
+// The second (A2, B2) segment is the LoRA tail: the forward is Y = [X | s t] [W | B]^T and the input
+// adjoint is dX = [dY | dt] [W ; A], so the adapter's products ride in the same tile loop as the base
+// weight's, one extra 64-wide k block at the end of each tile (reference: lora_expand's add into y,
+// src/adjoint/host/lora.cpp:416-471, and the two dX terms gemm_nt_adjoint + lora_shrink_host_adjoint).
+// Each operand is bf16 and either K-major (row-major [rows, K]) or MN-major (row-major [K, rows]); the
+// MN-major form lets the adjoint read the weight [N, K] as is, and the adapter-gradient GEMMs reduce
+// over tokens without a transpose.
+//
+// Structure: one persistent CTA per SM; warp 0 issues TMA loads into a ring of shared-memory stages,
+// warp 1 issues tcgen05.mma (128 x BN x 16) into a double-buffered TMEM accumulator, and warps 4-7
+// drain the accumulator (tcgen05.ld) and apply the epilogue while the next tile's MMAs run.
+// No cluster multicast anywhere: every CTA loads its own tiles.
+#include "sm100.cuh"
+#include "r97b_internal.h"
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <unordered_map>
+
+namespace r97b {
+
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;               // one 128-byte swizzle row of bf16
+constexpr int kThreads = 256;         // 8 warps: 0 TMA, 1 MMA, 4..7 epilogue
+constexpr int kABytes = kBM * kBK * 2;  // 16 KiB
+
+struct KernelArgs {
+    int32_t M, N;
+    int32_t k1_blocks, k2_blocks;
+    int32_t kb_per_split, splits;
+    int32_t tiles_m, tiles_n;
+    int32_t mode;
+    float alpha, beta;
+    void* out;
+    int64_t ldo;
+    const __nv_bfloat16* addend;
+    int64_t ld_add;
+};
+
+template <int BN>
+struct Cfg {
+    static constexpr int kBBytes = BN * kBK * 2;
+    static constexpr int kStageBytes = kABytes + kBBytes;
+    static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+    static constexpr int kTmemCols = 2 * BN < 32 ? 32 : 2 * BN;
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int BN, int A_MN, int B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tA1, const __grid_constant__ CUtensorMap tB1,
+                const __grid_constant__ CUtensorMap tA2, const __grid_constant__ CUtensorMap tB2,
+                const KernelArgs args) {
+    using C = Cfg<BN>;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base_u32 = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint64_t* empty_bar = full_bar + C::kStages;
+    uint64_t* tfull_bar = empty_bar + C::kStages;
+    uint64_t* tempty_bar = tfull_bar + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full_bar[s], 1);
+            mbar_init(&empty_bar[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull_bar[a], 1);
+            mbar_init(&tempty_bar[a], 128);
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, C::kTmemCols);
+        tmem_relinquish();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch(&tA1);
+        tma_prefetch(&tB1);
+        if (args.k2_blocks > 0) {
+            tma_prefetch(&tA2);
+            tma_prefetch(&tB2);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int k_total = args.k1_blocks + args.k2_blocks;
+    const int tiles = args.tiles_m * args.tiles_n;
+    const int units = tiles * args.splits;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------- TMA producer
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x) {
+            const int split = u / tiles;
+            const int tile = u % tiles;
+            const int tm = tile % args.tiles_m;
+            const int tn = tile / args.tiles_m;
+            const int kb0 = split * args.kb_per_split;
+            const int kb1 = min(k_total, kb0 + args.kb_per_split);
+            bool ok = true;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* sa = smem + stage * C::kStageBytes;
+                uint8_t* sb = sa + kABytes;
+                mbar_expect_tx(&full_bar[stage], C::kStageBytes);
+                const bool seg2 = kb >= args.k1_blocks;
+                const CUtensorMap* ma = seg2 ? &tA2 : &tA1;
+                const CUtensorMap* mb = seg2 ? &tB2 : &tB1;
+                const int k = (seg2 ? kb - args.k1_blocks : kb) * kBK;
+                const int m0 = tm * kBM, n0 = tn * BN;
+                if (A_MN) {
+                    tma_load_2d(sa, ma, &full_bar[stage], m0, k);
+                    tma_load_2d(sa + 8192, ma, &full_bar[stage], m0 + 64, k);
+                } else {
+                    tma_load_2d(sa, ma, &full_bar[stage], k, m0);
+                }
+                if (B_MN) {
+#pragma unroll
+                    for (int j = 0; j < BN / 64; ++j) tma_load_2d(sb + j * 8192, mb, &full_bar[stage], n0 + 64 * j, k);
+                } else {
+                    tma_load_2d(sb, mb, &full_bar[stage], k, n0);
+                }
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ------------------------------------------------------------- MMA issuer
+        constexpr uint32_t idesc = make_idesc_bf16(kBM, BN, A_MN, B_MN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int local = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+            const int split = u / tiles;
+            const int kb0 = split * args.kb_per_split;
+            const int kb1 = min(k_total, kb0 + args.kb_per_split);
+            const int acc = local & 1;
+            if (!mbar_wait(&tempty_bar[acc], ((local >> 1) & 1) ^ 1u, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+            bool ok = true;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
+                const uint32_t sb = sa + kABytes;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint64_t ad = A_MN ? make_sdesc_sw128(sa + kk * 2048, 8192, 1024)
+                                             : make_sdesc_sw128(sa + kk * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? make_sdesc_sw128(sb + kk * 2048, 8192, 1024)
+                                             : make_sdesc_sw128(sb + kk * 32, 16, 1024);
+                    umma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit(&empty_bar[stage]);
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            umma_commit(&tfull_bar[acc]);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------- epilogue
+        const int q = warp & 3;  // TMEM lane quarter this warp may access
+        int local = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+            const int tile = u % tiles;
+            const int tm = tile % args.tiles_m;
+            const int tn = tile / args.tiles_m;
+            const int acc = local & 1;
+            if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag)) break;
+            tc_fence_after();
+            const int m = tm * kBM + q * 32 + lane;
+            const bool mrow = m < args.M;
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();  // tcgen05.ld is .sync.aligned: the warp must be converged
+                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+                tmem_ld_wait();
+                const int n0 = tn * BN + c * 32;
+                if (!mrow || n0 >= args.N) continue;
+                const bool full = n0 + 32 <= args.N;
+                float v[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
+                if (args.mode == kEpiStoreBf16) {
+                    if (args.addend) {
+                        const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i)
+                            if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
+                    }
+                    __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)m * args.ldo + n0;
+                    if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 8) {
+                            uint4 pk;
+                            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[i], v[i + 1]);
+                            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
+                            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
+                            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
+                            pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                            pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                            pk.z = *reinterpret_cast<uint32_t*>(&h2);
+                            pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                            *reinterpret_cast<uint4*>(op + i) = pk;
+                        }
+                    } else {
+                        for (int i = 0; i < 32; ++i)
+                            if (n0 + i < args.N) op[i] = __float2bfloat16_rn(v[i]);
+                    }
+                } else if (args.mode == kEpiStoreF32) {
+                    float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
+                    if (args.addend) {
+                        const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
+                        for (int i = 0; i < 32; ++i)
+                            if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
+                    }
+                    if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
+#pragma unroll
+                        for (int i = 0; i < 32; i += 4)
+                            *reinterpret_cast<float4*>(op + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+                    } else {
+                        for (int i = 0; i < 32; ++i)
+                            if (n0 + i < args.N) op[i] = v[i];
+                    }
+                } else if (args.mode == kEpiAtomicF32) {
+                    float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
+                    for (int i = 0; i < 32; ++i)
+                        if (full || n0 + i < args.N) atomicAdd(op + i, v[i]);
+                } else {  // kEpiAtomicF32T: out[n, m] += acc[m, n]
+                    float* op = reinterpret_cast<float*>(args.out) + (int64_t)n0 * args.ldo + m;
+                    for (int i = 0; i < 32; ++i)
+                        if (full || n0 + i < args.N) atomicAdd(op + (int64_t)i * args.ldo, v[i]);
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&tempty_bar[acc]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------------------------ host side
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool encode_fn() {
+    std::call_once(g_encode_once, [] {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    });
+    return g_encode != nullptr;
+}
+
+// A row-major bf16 matrix [outer, inner] (inner contiguous, row stride `ld` elements) as a 2D tensor
+// map with a (box_inner, box_outer) box and the 128-byte swizzle. Out-of-range boxes read zeros.
+bool make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
+              int box_outer) {
+    if (!encode_fn()) return false;
+    if ((reinterpret_cast<uintptr_t>(ptr) & 15) != 0 || (ld * 2) % 16 != 0) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)box_inner, (cuuint32_t)box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                          estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS;
+}
+
+// Operand X of logical shape [rows, K] (rows = M for A, N for B) with its majorness.
+bool operand_map(CUtensorMap* map, const R97bMat& m, int64_t rows, int64_t K, int box_rows) {
+    if (m.mn_major)  // stored [K, rows]
+        return make_map(map, m.ptr, rows, K, m.ld, 64, 64);
+    return make_map(map, m.ptr, K, rows, m.ld, 64, box_rows);
+}
+
+int num_sms() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+template <int BN, int A_MN, int B_MN>
+int launch(const R97bGemm& g, cudaStream_t stream) {
+    using C = Cfg<BN>;
+    CUtensorMap a1, b1, a2, b2;
+    if (!operand_map(&a1, g.a1, g.M, g.K1, kBM)) return R97B_EINVAL;
+    if (!operand_map(&b1, g.b1, g.N, g.K1, BN)) return R97B_EINVAL;
+    if (g.K2 > 0) {
+        if (!operand_map(&a2, g.a2, g.M, g.K2, kBM)) return R97B_EINVAL;
+        if (!operand_map(&b2, g.b2, g.N, g.K2, BN)) return R97B_EINVAL;
+    } else {
+        a2 = a1;
+        b2 = b1;
+    }
+    KernelArgs k{};
+    k.M = (int32_t)g.M;
+    k.N = (int32_t)g.N;
+    k.k1_blocks = (int32_t)((g.K1 + kBK - 1) / kBK);
+    k.k2_blocks = g.K2 > 0 ? (int32_t)((g.K2 + kBK - 1) / kBK) : 0;
+    const int k_total = k.k1_blocks + k.k2_blocks;
+    int splits = g.splits > 1 ? g.splits : 1;
+    if (splits > k_total) splits = k_total;
+    k.kb_per_split = (k_total + splits - 1) / splits;
+    k.splits = (k_total + k.kb_per_split - 1) / k.kb_per_split;
+    k.tiles_m = (int32_t)((g.M + kBM - 1) / kBM);
+    k.tiles_n = (int32_t)((g.N + BN - 1) / BN);
+    k.mode = g.mode;
+    k.alpha = g.alpha;
+    k.beta = g.beta;
+    k.out = g.out;
+    k.ldo = g.ldo;
+    k.addend = reinterpret_cast<const __nv_bfloat16*>(g.addend);
+    k.ld_add = g.ld_add;
+    const int units = k.tiles_m * k.tiles_n * k.splits;
+    int grid = num_sms();
+    if (units < grid) grid = units;
+    auto kern = gemm_kernel<BN, A_MN, B_MN>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+        attr_set = true;
+    }
+    kern<<<grid, kThreads, C::kSmemBytes, stream>>>(a1, b1, a2, b2, k);
+    return cudaGetLastError() == cudaSuccess ? R97B_OK : R97B_ELAUNCH;
+}
+
+template <int BN>
+int dispatch_major(const R97bGemm& g, cudaStream_t s) {
+    const int a = g.a1.mn_major ? 1 : 0, b = g.b1.mn_major ? 1 : 0;
+    if (a == 0 && b == 0) return launch<BN, 0, 0>(g, s);
+    if (a == 0 && b == 1) return launch<BN, 0, 1>(g, s);
+    if (a == 1 && b == 0) return launch<BN, 1, 0>(g, s);
+    return launch<BN, 1, 1>(g, s);
+}
+
+}  // namespace
+
+R97B_ERROR_READER(gemm_error_word)
+
+int gemm_run(const R97bGemm& g, cudaStream_t stream) {
+    if (g.M <= 0 || g.N <= 0 || g.K1 <= 0 || !g.out || !g.a1.ptr || !g.b1.ptr) return R97B_EINVAL;
+    if (g.K2 > 0 && (!g.a2.ptr || !g.b2.ptr || g.a2.mn_major != g.a1.mn_major || g.b2.mn_major != g.b1.mn_major))
+        return R97B_EINVAL;
+    if (g.mode < kEpiStoreBf16 || g.mode > kEpiAtomicF32T) return R97B_EINVAL;
+    if (g.M > 0x7FFFFFFF || g.N > 0x7FFFFFFF) return R97B_EINVAL;
+    int bn = g.bn;
+    if (bn == 0) bn = g.N <= 64 ? 64 : (g.N <= 128 ? 128 : 256);
+    switch (bn) {
+        case 64: return dispatch_major<64>(g, stream);
+        case 128: return dispatch_major<128>(g, stream);
+        case 256: return dispatch_major<256>(g, stream);
+        default: return R97B_EINVAL;
+    }
+}
+
+}  // namespace r97b

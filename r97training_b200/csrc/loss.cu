@@ -1,0 +1,200 @@
+// loss.cu -- the vocabulary head's loss and its gradient on sm_100a: softmax cross-entropy and the
+// KL divergence to a teacher, one pass over a chunk of logit rows.
+//
+// One CTA per row. Pass 1 reads the row once and keeps, per thread, an online log-sum-exp of the
+// student logits (max m_s, sum S_s) and, with a teacher, the teacher's (m_t, S_t) and
+// U = sum e^{t - m_t} (t - s); the CTA merges those. Pass 2 reads the row again (from L2: a row is at
+// most a few hundred KB and the CTA just read it) and writes the gradient, in place over the logits
+// when the caller passes the same buffer. Per row:
+//
+//   CE  = lse_s - s[target]                     dCE/ds  = softmax(s) - onehot(target)
+//   KL  = sum p_t (log p_t - log p_s)
+//       = U / S_t - lse_t + lse_s               dKL/ds  = softmax(s) - softmax(t)
+//   grad = grad_scale * (w_ce dCE/ds + w_kl dKL/ds), zero on a row whose target is -1.
+//
+// CE follows the reference's ce_position (src/loss.cpp:21-39) and its chunk kernel's contract
+// (include/r97/head.h:28-50, HeadChunk); the KL objective has no counterpart in the reference.
+#include "r97b_internal.h"
+
+#include <cuda_bf16.h>
+#include <math.h>
+
+namespace r97b {
+namespace {
+
+constexpr int kThreads = 512;
+
+struct Acc {
+    float m, s;       // student: running max and sum of exp(x - m)
+    float mt, st, u;  // teacher: running max, sum of exp(t - mt), sum of exp(t - mt) * (t - s)
+};
+
+__device__ __forceinline__ void merge(Acc& a, const Acc& b) {
+    const float m = fmaxf(a.m, b.m);
+    a.s = (a.m == -INFINITY ? 0.0f : a.s * __expf(a.m - m)) + (b.m == -INFINITY ? 0.0f : b.s * __expf(b.m - m));
+    a.m = m;
+    const float mt = fmaxf(a.mt, b.mt);
+    const float fa = a.mt == -INFINITY ? 0.0f : __expf(a.mt - mt);
+    const float fb = b.mt == -INFINITY ? 0.0f : __expf(b.mt - mt);
+    a.st = a.st * fa + b.st * fb;
+    a.u = a.u * fa + b.u * fb;
+    a.mt = mt;
+}
+
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+
+template <bool kTeacher>
+__global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* __restrict__ logits,
+                                                          const __nv_bfloat16* __restrict__ teacher,
+                                                          const int32_t* __restrict__ targets, __nv_bfloat16* grad,
+                                                          float* __restrict__ loss_ce, float* __restrict__ loss_kl,
+                                                          int64_t vocab, int64_t ld, int64_t ld_t, float grad_scale,
+                                                          float w_ce, float w_kl) {
+    const int64_t row = blockIdx.x;
+    const int32_t target = targets ? targets[row] : 0;
+    const bool scored = target >= 0;
+    const __nv_bfloat16* x = logits + row * ld;
+    const __nv_bfloat16* t = kTeacher ? teacher + row * ld_t : nullptr;
+    const int64_t nvec = vocab / 8;
+
+    Acc a{-INFINITY, 0.0f, -INFINITY, 0.0f, 0.0f};
+    for (int64_t i = threadIdx.x; i < nvec; i += kThreads) {
+        float v[8];
+        unpack8(reinterpret_cast<const uint4*>(x)[i], v);
+        float mx = v[0];
+#pragma unroll
+        for (int k = 1; k < 8; ++k) mx = fmaxf(mx, v[k]);
+        const float m = fmaxf(a.m, mx);
+        float s = a.m == -INFINITY ? 0.0f : a.s * __expf(a.m - m);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) s += __expf(v[k] - m);
+        a.m = m;
+        a.s = s;
+        if (kTeacher) {
+            float tv[8];
+            unpack8(reinterpret_cast<const uint4*>(t)[i], tv);
+            float tm = tv[0];
+#pragma unroll
+            for (int k = 1; k < 8; ++k) tm = fmaxf(tm, tv[k]);
+            const float mt = fmaxf(a.mt, tm);
+            const float f = a.mt == -INFINITY ? 0.0f : __expf(a.mt - mt);
+            float st = a.st * f, u = a.u * f;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const float e = __expf(tv[k] - mt);
+                st += e;
+                u = fmaf(e, tv[k] - v[k], u);
+            }
+            a.mt = mt;
+            a.st = st;
+            a.u = u;
+        }
+    }
+    // the ragged tail (vocab not a multiple of 8), one element a thread
+    for (int64_t j = nvec * 8 + threadIdx.x; j < vocab; j += kThreads) {
+        const float v = __bfloat162float(x[j]);
+        Acc b{v, 1.0f, -INFINITY, 0.0f, 0.0f};
+        if (kTeacher) {
+            const float tv = __bfloat162float(t[j]);
+            b.mt = tv;
+            b.st = 1.0f;
+            b.u = tv - v;
+        }
+        merge(a, b);
+    }
+    // warp, then CTA merge
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        Acc b;
+        b.m = __shfl_xor_sync(0xFFFFFFFFu, a.m, o);
+        b.s = __shfl_xor_sync(0xFFFFFFFFu, a.s, o);
+        b.mt = __shfl_xor_sync(0xFFFFFFFFu, a.mt, o);
+        b.st = __shfl_xor_sync(0xFFFFFFFFu, a.st, o);
+        b.u = __shfl_xor_sync(0xFFFFFFFFu, a.u, o);
+        merge(a, b);
+    }
+    __shared__ Acc red[kThreads / 32];
+    __shared__ float bc[4];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = a;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        Acc r = red[0];
+        for (int w = 1; w < kThreads / 32; ++w) merge(r, red[w]);
+        const float lse = r.m + logf(r.s);
+        const float lse_t = kTeacher ? r.mt + logf(r.st) : 0.0f;
+        bc[0] = lse;
+        bc[1] = lse_t;
+        if (loss_ce) loss_ce[row] = scored && targets ? lse - __bfloat162float(x[target]) : 0.0f;
+        if (loss_kl) loss_kl[row] = kTeacher && scored ? r.u / r.st - lse_t + lse : 0.0f;
+    }
+    __syncthreads();
+    if (!grad) return;
+    const float lse = bc[0], lse_t = bc[1];
+    __nv_bfloat16* g = grad + row * ld;
+    const float ce_w = targets ? w_ce : 0.0f;
+    const float sc = scored ? grad_scale : 0.0f;
+    for (int64_t i = threadIdx.x; i < nvec; i += kThreads) {
+        float v[8], tv[8];
+        unpack8(reinterpret_cast<const uint4*>(x)[i], v);
+        if (kTeacher) unpack8(reinterpret_cast<const uint4*>(t)[i], tv);
+        float o[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const float p = __expf(v[k] - lse);
+            float d = ce_w * p;
+            if (kTeacher) d += w_kl * (p - __expf(tv[k] - lse_t));
+            if (targets && (int64_t)i * 8 + k == target) d -= ce_w;
+            o[k] = d * sc;
+        }
+        uint4 u;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(o[2 * k], o[2 * k + 1]);
+        reinterpret_cast<uint4*>(g)[i] = u;
+    }
+    for (int64_t j = nvec * 8 + threadIdx.x; j < vocab; j += kThreads) {
+        const float p = __expf(__bfloat162float(x[j]) - lse);
+        float d = ce_w * p;
+        if (kTeacher) d += w_kl * (p - __expf(__bfloat162float(t[j]) - lse_t));
+        if (targets && j == target) d -= ce_w;
+        g[j] = __float2bfloat16_rn(d * sc);
+    }
+}
+
+}  // namespace
+}  // namespace r97b
+
+using namespace r97b;
+
+// Loss and gradient of `rows` logit rows (bf16, row stride `ld`), optionally against teacher logits
+// (row stride `ld_t`). `grad` may equal `logits` (in-place).
+extern "C" int r97b_ce_kld(const uint16_t* logits, const uint16_t* teacher, const int32_t* targets, uint16_t* grad,
+                           float* loss_ce, float* loss_kl, int64_t rows, int64_t vocab, int64_t ld, int64_t ld_t,
+                           float grad_scale, float w_ce, float w_kl, void* stream) {
+    if (!logits || rows <= 0 || vocab <= 0 || ld < vocab || (ld % 8) != 0 ||
+        (reinterpret_cast<uintptr_t>(logits) & 15) != 0 || (grad && (reinterpret_cast<uintptr_t>(grad) & 15) != 0))
+        return R97B_EINVAL;
+    if (teacher && (ld_t < vocab || (ld_t % 8) != 0 || (reinterpret_cast<uintptr_t>(teacher) & 15) != 0))
+        return R97B_EINVAL;
+    if (rows > 0x7FFFFFFF) return R97B_EINVAL;
+    const auto* x = reinterpret_cast<const __nv_bfloat16*>(logits);
+    const auto* t = reinterpret_cast<const __nv_bfloat16*>(teacher);
+    auto* g = reinterpret_cast<__nv_bfloat16*>(grad);
+    if (teacher)
+        ce_kld_kernel<true><<<(unsigned)rows, kThreads, 0, as_stream(stream)>>>(x, t, targets, g, loss_ce, loss_kl,
+                                                                               vocab, ld, ld_t, grad_scale, w_ce, w_kl);
+    else
+        ce_kld_kernel<false><<<(unsigned)rows, kThreads, 0, as_stream(stream)>>>(x, nullptr, targets, g, loss_ce,
+                                                                                loss_kl, vocab, ld, 0, grad_scale,
+                                                                                w_ce, 0.0f);
+    return launch_status();
+}

@@ -1,0 +1,23 @@
+// r97b_internal.h -- declarations shared by the .cu files of libr97b200.so (not part of the ABI).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/r97b.h"
+
+namespace r97b {
+
+constexpr int kEpiStoreBf16 = R97B_EPI_STORE_BF16;
+constexpr int kEpiStoreF32 = R97B_EPI_STORE_F32;
+constexpr int kEpiAtomicF32 = R97B_EPI_ATOMIC_F32;
+constexpr int kEpiAtomicF32T = R97B_EPI_ATOMIC_F32T;
+
+int gemm_run(const R97bGemm& g, cudaStream_t stream);
+unsigned gemm_error_word();
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+inline int launch_status() { return cudaGetLastError() == cudaSuccess ? R97B_OK : R97B_ELAUNCH; }
+
+}  // namespace r97b

@@ -1,0 +1,36 @@
+"""The C-ABI library loads without a GPU and exports every entry point include/*.h declares."""
+import ctypes
+import os
+import re
+
+from r97training_b200 import build as B
+from r97training_b200._lib import exported_symbols, lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared():
+    names = set()
+    for h in os.listdir(os.path.join(ROOT, "include")):
+        if not h.endswith(".h"):
+            continue
+        src = open(os.path.join(ROOT, "include", h)).read()
+        src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+        for m in re.finditer(r"^\s*(?:int|int64_t|void|unsigned int|const char\s*\*)\s+(r97\w*)\s*\(", src, re.M):
+            names.add(m.group(1))
+    return names
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    h = lib()
+    decl = declared()
+    assert decl, "no declarations found"
+    for name in sorted(decl):
+        assert hasattr(h, name), f"{B.LIB} does not export {name}"
+    assert decl <= set(exported_symbols()) | decl
+    assert h.r97b_abi_version() >= 1
+
+
+def test_binding_table_covers_declarations():
+    missing = declared() - set(exported_symbols())
+    assert not missing, f"declared in include/ but not bound in _lib: {sorted(missing)}"
