@@ -150,6 +150,69 @@ int64_t r97b_global_norm_scratch_bytes(int64_t n);
 int r97b_global_norm(const float* g, int64_t n, float inv_k, float max_norm, double* partials, float* out_norm,
                      float* out_scale, void* stream);
 
+/* ------------------------------------------------------------------------------ GatedDeltaNet */
+
+/* The geometry of one chunked GDN call: n_seq ragged sequences over T tokens (the chunk table comes from
+ * r97b_gdn_chunk_table on the host, copied to the device), H value heads sharing Hg query/key heads,
+ * head_k = head_v = 128 and chunk = 64 (the only values the kernels take), and the output scale
+ * (1/sqrt(head_k) in the reference's architecture). */
+typedef struct R97bGdnDims {
+    int32_t n_seq, H, Hg, n_chunks;
+    int32_t head_k, head_v, chunk, _pad;
+    int64_t T;
+    float scale;
+    int32_t _pad2;
+    const int32_t* chunk_tok0; /* device [n_chunks]: first token of each chunk */
+    const int32_t* chunk_len;  /* device [n_chunks]: its length (<= chunk)     */
+    const int32_t* seq_chunk0; /* device [n_seq + 1]: first chunk of each sequence */
+} R97bGdnDims;
+
+/* Fills the chunk table of cu_seqlens (host arrays; any output may be null) and returns the chunk count,
+ * or -1 on a bad cu_seqlens. */
+int32_t r97b_gdn_chunk_table(const int32_t* cu_host, int32_t n_seq, int32_t chunk, int32_t* tok0_host,
+                             int32_t* len_host, int32_t* seq_chunk0_host);
+
+/* Forward operands. q, k: bf16 [T, Hg, 128] (L2-normalised); v: bf16 [T, H, 128]; g: f32 [T, H], the
+ * within-chunk cumulative log decay; beta: f32 [T, H]; h0: f32 [n_seq, H, 128(v), 128(k)] or null (zero).
+ * Outputs: A f32 [T, H, 64] (the reference's gdn_kkt_solve output, row i of each chunk's (I+M)^-1),
+ * w, u f32 [T, H, 128], S f32 [n_chunks, H, 128(k), 128(v)] (the state entering each chunk), Vp f32
+ * [T, H, 128], P f32 [n_chunks, H, 64, 64], o bf16 [T, H, 128] and ht f32 [n_seq, H, 128, 128] or null.
+ * A, w, S, Vp and P are what the backward reads; u is scratch. */
+typedef struct R97bGdnFwd {
+    const uint16_t *q, *k, *v;
+    const float *g, *beta, *h0;
+    float *A, *w, *u, *S, *Vp, *P;
+    uint16_t* o;
+    float* ht;
+} R97bGdnFwd;
+
+/* Backward operands: the forward's inputs and saved A, w, S, Vp, P; dO bf16 [T, H, 128]; dht f32 or null.
+ * Scratch: dS f32 [n_chunks, H, 128, 128], dVp, dw, pdq, pdk f32 [T, H, 128], pdg f32 [T, H].
+ * Outputs: dq, dk f32 [T, H, 128] per VALUE head (sum the heads sharing a key head with
+ * r97b_gdn_sum_heads), dv f32 [T, H, 128], dbeta, dg f32 [T, H], dh0 f32 or null. */
+typedef struct R97bGdnBwd {
+    const uint16_t *q, *k, *v;
+    const float *g, *beta;
+    const float *A, *w, *S, *Vp, *P;
+    const uint16_t* dO;
+    const float* dht;
+    float *dS, *dVp, *dw, *pdq, *pdk, *pdg;
+    float *dq, *dk, *dv, *dbeta, *dg, *dh0;
+} R97bGdnBwd;
+
+/* The forward of the reference's gdn_kkt_solve + gdn_chunk_scan pair (src/adjoint/host/gdn_kkt.cpp:221-270,
+ * gdn_scan.cpp:418-485). Replaces: gdn_kkt_adjoint_kernel / gdn_scan_adjoint_kernel's forward replays and
+ * radiance's chunked GDN forward (src/adjoint/device/gdn_kkt.hip, gdn_scan.hip). */
+int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* args, void* stream);
+
+/* The adjoint of the same pair: the scan's adjoint and the kkt solve's adjoint composed
+ * (src/adjoint/host/gdn_scan.cpp:487-580 + gdn_kkt.cpp:272-352). Replaces: gdn_scan_adjoint_kernel and
+ * gdn_kkt_adjoint_kernel, src/adjoint/device/gdn_scan.hip:235-600 and gdn_kkt.hip:229-424. */
+int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* args, void* stream);
+
+/* dst[t, j, :] = sum_{h in key head j's value heads} src[t, h, :] (f32 [T, H, 128] -> [T, Hg, 128]). */
+int r97b_gdn_sum_heads(const float* src, float* dst, int64_t T, int32_t H, int32_t Hg, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

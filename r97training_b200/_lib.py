@@ -66,6 +66,10 @@ _SIGS = {
                                 c_f32, c_vp, c_i32, c_vp]),
     "r97b_global_norm_scratch_bytes": (c_i64, [c_i64]),
     "r97b_global_norm": (c_i32, [c_vp, c_i64, c_f32, c_f32, c_vp, c_vp, c_vp, c_vp]),
+    "r97b_gdn_chunk_table": (c_i32, [c_vp, c_i32, c_i32, c_vp, c_vp, c_vp]),
+    "r97b_gdn_fwd": (c_i32, [c_vp, c_vp, c_vp]),
+    "r97b_gdn_bwd": (c_i32, [c_vp, c_vp, c_vp]),
+    "r97b_gdn_sum_heads": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_i32, c_vp]),
 }
 
 OPTIONAL = set()

@@ -70,7 +70,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Waits for the phase of `parity` to complete. Gives up after roughly `limit_cycles` SM clocks (or
 // when *abort is raised by another role), records kErrTimeout and returns false.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                          long long limit_cycles = 20000000000ll) {
+                                          long long limit_cycles = 4000000000ll) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     uint32_t n = 0;
