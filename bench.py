@@ -1,0 +1,339 @@
+"""bench.py -- LoRA fwd+bwd+AdamW step throughput of the 9B-class synthetic hybrid model on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 5|4]
+
+One process per GPU (torchrun for N > 1, NCCL over NVLink). Each rank trains its own micro-batch of
+seq 4096 x 2 (config 5) on the same frozen IQR base and the same adapter; the adapter gradient is
+all-reduced (averaged) per layer bucket as the reverse walk finishes each layer, on a side stream, and
+every rank applies the same AdamW update (data parallel, weak scaling). Rank 0 prints one JSON line.
+
+`value` is the whole-job tokens/s with token ids already on the device; `e2e` is the same step driven
+through the public API from pinned host token ids, with the H2D copy of the ids and the D2H read of the
+loss inside the timed region. `roofline` is the dominant kernel -- the tcgen05 GEMM -- measured live:
+algorithmic FLOPs of every GEMM launch in the timed steps over their CUDA-event durations, against the
+measured sustained bf16 peak. `cpu_baseline` times the reference's own host rows (oracle/_ref) on a
+bounded sample and extrapolates tokens/s.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "LoRA fwd+bwd step tokens/sec at 1/2/4/8 B200; per-kernel roofline %"
+
+
+def _peaks():
+    try:
+        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        return None
+
+
+def _config(name):
+    from r97training_b200.model import CONFIG4, CONFIG5
+    return CONFIG5 if str(name) == "5" else CONFIG4
+
+
+def _cfg_dict(cfg, model_groups, base_weights, adapter_params):
+    return dict(hidden=cfg.hidden, ffn=cfg.ffn, rank=cfg.rank, alpha=cfg.alpha, vocab=cfg.vocab,
+                gdn_heads=cfg.gdn_heads, gdn_qk_heads=cfg.gdn_qk_heads, seq=cfg.seq, micro_batch=cfg.micro_batch,
+                kinds=cfg.kinds, groups=model_groups, base_weights=base_weights, adapter_params=adapter_params)
+
+
+def _static_sizes(cfg):
+    from r97training_b200.model import groups_of
+    groups = {k: groups_of(cfg, k) for k in ("gdn", "attn")}
+    base = cfg.vocab * cfg.hidden
+    adapter = 0
+    for kind in cfg.kinds:
+        for _, k, projs in groups[kind]:
+            for _, n in projs:
+                base += n * k
+                adapter += cfg.rank * (n + k)
+    return groups, base, adapter
+
+
+def cpu_reference(cfg, sample_tokens=None):
+    """tokens/s of the reference's own host rows on a bounded sample (rank 0, N = 1 only)."""
+    import oracle
+    from oracle import cpu_baseline as CB
+    if not oracle.ref_available():
+        return None, None
+    threads = CB.threads()
+    os.environ.setdefault("R97_THREADS", str(threads))
+    M = sample_tokens or max(16, min(64, 2 * threads))
+    groups, base, adapter = _static_sizes(cfg)
+    parts = CB.sample_step(_cfg_dict(cfg, groups, base, adapter), M)
+    return 1.0 / parts["seconds_per_token"], dict(parts=parts, M=M, threads=threads)
+
+
+def reference_arm(args):
+    """--impl reference: the reference's CPU implementation of the path (its own host rows, compiled
+    from its sources in oracle/_ref) on the host cores, K timed sample steps after W warm-ups."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    cfg = _config(args.config)
+    import oracle
+    if not oracle.ref_available():
+        print(json.dumps({"impl": "reference", "unavailable": "reference host library not built and reference tree absent"}))
+        return 0
+    from oracle import cpu_baseline as CB
+    threads = CB.threads()
+    os.environ.setdefault("R97_THREADS", str(threads))
+    groups, base, adapter = _static_sizes(cfg)
+    cd = _cfg_dict(cfg, groups, base, adapter)
+    M = 16
+    for _ in range(args.warmup):
+        CB.sample_step(cd, M, seed=1)
+    per_tok = []
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        per_tok.append(CB.sample_step(cd, M, seed=2 + i)["seconds_per_token"])
+    wall = time.perf_counter() - t0
+    sec = sum(per_tok) / len(per_tok)
+    value = 1.0 / sec
+    step_tokens = cfg.tokens
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * step_tokens * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": f"config {args.config}: hybrid LoRA step, reference host rows on a {M}-token sample",
+                   "model": "synthetic 9B-class hybrid (3 GDN : 1 gated attention)" if str(args.config) == "5" else
+                   "synthetic small hybrid", "global_batch": cfg.micro_batch, "seq_len": cfg.seq,
+                   "parallelism": "host threads"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                         "sample": f"{M} tokens of one GDN and one attention block, one 64-token GDN chunk, the "
+                                   "head, one 4096x4096 decode and a 16M AdamW, extrapolated per token"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "wall_s": wall,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sms, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sms.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        os.unlink(self.path)
+        if not sms:
+            return None
+        sms.sort()
+        return {"sm_mhz": sms[len(sms) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def b200_arm(args):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from r97training_b200 import ops
+    from r97training_b200.model import Adapter, HybridModel, TrainStep, flops_per_token
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+    cfg = _config(args.config)
+    model = HybridModel(cfg, dev)
+    adapter = Adapter(model, dev)
+    step = TrainStep(model, adapter)
+
+    comm = torch.cuda.Stream(device=dev) if world > 1 else None
+    pending = []
+
+    def hook(li):  # a layer's adapter gradient is final: all-reduce its bucket on the comm stream
+        lo, hi = adapter.layer_ranges[li]
+        ev = torch.cuda.Event()
+        ev.record()
+        comm.wait_event(ev)
+        with torch.cuda.stream(comm):
+            dist.all_reduce(adapter.g[lo:hi], op=dist.ReduceOp.AVG)
+        pending.append(li)
+
+    if world > 1:
+        step.grad_hook = hook
+
+    def one_step(ids):
+        loss = step.run(ids)
+        if world > 1:
+            torch.cuda.current_stream().wait_stream(comm)
+            pending.clear()
+        adapter.adamw()
+        return loss
+
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1000 + rank)
+    n_batches = args.warmup + args.steps
+    ids_dev = [torch.randint(0, cfg.vocab, (cfg.micro_batch, cfg.seq), device=dev, generator=gen, dtype=torch.int32)
+               for _ in range(min(n_batches, 4))]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(args.warmup):
+        one_step(ids_dev[i % len(ids_dev)])
+    barrier()
+    # ------------------------------------------------------------ timed: device-resident inputs
+    sampler = ClockSampler(local)
+    sampler.start()
+    prof = []
+    ops.GEMM_PROFILE = prof
+    from r97training_b200._lib import lib as _l
+    launches0 = int(_l().r97b_launch_count())
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.steps):
+        loss = one_step(ids_dev[i % len(ids_dev)])
+    e1.record()
+    barrier()
+    ops.GEMM_PROFILE = None
+    own_launches = int(_l().r97b_launch_count()) - launches0
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1)
+    launches, gemm_ms, gemm_flops = ops.gemm_profile_summary(prof)
+    t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    tokens = cfg.tokens * world * args.steps
+    value = tokens / (ms / 1e3)
+    # ------------------------------------------------------------ timed: e2e through the public API
+    host_ids = [torch.randint(0, cfg.vocab, (cfg.micro_batch, cfg.seq), generator=torch.Generator().manual_seed(7 + i),
+                              dtype=torch.int32).pin_memory() for i in range(2)]
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for i in range(args.steps):
+        ids = host_ids[i % 2].to(dev, non_blocking=True)
+        loss_host = float(one_step(ids).item())
+    f1.record()
+    barrier()
+    ms_e2e = f0.elapsed_time(f1)
+    t = torch.tensor([ms_e2e], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t.item())
+    e2e_value = tokens / (ms_e2e / 1e3)
+
+    peaks = _peaks()
+    if peaks:
+        peak, peak_src = float(peaks.get("bf16_tflops_sustained") or peaks["bf16_tflops"]), "measured sustained"
+    else:
+        peak, peak_src = 1400.0, "fallback"
+    gemm_tflops = gemm_flops / (gemm_ms / 1e3) / 1e12 if gemm_ms > 0 else 0.0
+    traffic = None
+    try:
+        tr = json.load(open(os.path.join(ROOT, "profiles", "gemm_traffic.json")))
+        traffic = tr.get("bytes_per_launch")
+    except Exception:
+        pass
+    gpu_launches = None
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform random token ids, seeded IQR base)",
+            "config": {"workload": f"config {args.config}: full LoRA fwd+bwd+AdamW step of the random-init "
+                                   f"{'9B-class' if str(args.config) == '5' else 'small'} hybrid",
+                       "model": f"hybrid {cfg.layers}L d{cfg.hidden} 3xGDN:1xattn, IQR u4 base, LoRA r{cfg.rank}",
+                       "global_batch": cfg.micro_batch * world, "seq_len": cfg.seq,
+                       "parallelism": f"dp{world}", "l2": "inputs larger than L2 (about 60 GB of activations a step)",
+                       "flops_per_token": flops_per_token(cfg)},
+            "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05)", "achieved": gemm_tflops, "peak": peak,
+                         "unit": "TFLOP/s", "frac": gemm_tflops / peak, "traffic": traffic,
+                         "peak_source": peak_src, "launches_per_step": launches / max(args.steps, 1),
+                         "gemm_ms_per_step": gemm_ms / max(args.steps, 1)},
+            "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": cfg.tokens * 4,
+                    "d2h_bytes_per_step": 4},
+            "clocks": clocks,
+            "loss": loss_host,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            try:
+                v, info = cpu_reference(cfg)
+                if v is not None:
+                    line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": info["threads"],
+                                            "kind": "reference",
+                                            "sample": f"{info['M']} tokens through one GDN and one attention block's "
+                                                      "reference host rows, one 64-token GDN chunk, the head, one "
+                                                      "4096x4096 decode and a 16M AdamW, extrapolated per token"}
+            except Exception as e:  # the baseline is reported, not required
+                line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
+        line["gpu_launches"] = own_launches
+        line["gpu_launches_per_step"] = own_launches / max(args.steps, 1)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="5")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return b200_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

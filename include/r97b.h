@@ -213,6 +213,87 @@ int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* args, void* stream);
 /* dst[t, j, :] = sum_{h in key head j's value heads} src[t, h, :] (f32 [T, H, 128] -> [T, Hg, 128]). */
 int r97b_gdn_sum_heads(const float* src, float* dst, int64_t T, int32_t H, int32_t Hg, void* stream);
 
+/* ------------------------------------------------------------------------------ block kernels */
+
+/* The GDN input prep: causal depthwise conv (width 4, weight f32 [conv_dim, 4], no bias) + silu over the first
+ * conv_dim = (2 Hg + H) * 128 columns of x (bf16 rows of ldx: q | k | v channels), then the L2 norm
+ * (eps 1e-6) of every q and k head. Out: q, k bf16 [T, Hg, 128], v bf16 [T, H, 128]. cu: device i32
+ * [n_seq + 1]; the conv window never crosses a sequence start (a cold prefill).
+ * Replaces: the conv / l2 phases of gdn_conv_prep, src/adjoint/host/gdn_prep.cpp:204-365 and
+ * src/adjoint/device/gdn_prep.hip:242-359. */
+int r97b_conv_prep_fwd(const uint16_t* x, int64_t ldx, const float* conv_w, const int32_t* cu, int32_t n_seq,
+                       int64_t T, int32_t Hg, int32_t H, uint16_t* q, uint16_t* k, uint16_t* v, void* stream);
+
+/* Its adjoint from the f32 cotangents of q, k ([T, Hg, 128]) and v ([T, H, 128]): dacc (f32 scratch
+ * [T, conv_dim]) then dx into the first conv_dim columns of bf16 rows of lddx.
+ * Replaces: gdn_conv_prep_host_adjoint's conv / l2 terms, src/adjoint/host/gdn_prep.cpp:367-455. */
+int r97b_conv_prep_bwd(const uint16_t* x, int64_t ldx, const float* conv_w, const int32_t* cu, int32_t n_seq,
+                       int64_t T, int32_t Hg, int32_t H, const float* dq, const float* dk, const float* dv,
+                       float* dacc, uint16_t* dx, int64_t lddx, void* stream);
+
+/* beta = sigmoid(b), g = within-chunk running sum of -exp(A_log) softplus(a + dt_bias) (threshold 20), from
+ * ba rows (bf16, ldba) holding b in columns [0, H) and a in [H, 2H); chunks from r97b_gdn_chunk_table.
+ * Replaces: the gate phase of gdn_conv_prep, src/adjoint/host/gdn_prep.cpp:320-336. */
+int r97b_gates_fwd(const uint16_t* ba, int64_t ldba, const float* a_log, const float* dt_bias,
+                   const int32_t* chunk_tok0, const int32_t* chunk_len, int32_t n_chunks, int32_t H, float* g,
+                   float* beta, void* stream);
+
+/* The adjoint of r97b_gates_fwd into dba (bf16 rows of lddba). Replaces:
+ * src/adjoint/host/gdn_prep.cpp:467-488. */
+int r97b_gates_bwd(const uint16_t* ba, int64_t ldba, const float* a_log, const float* dt_bias,
+                   const int32_t* chunk_tok0, const int32_t* chunk_len, int32_t n_chunks, int32_t H,
+                   const float* dg, const float* dbeta, uint16_t* dba, int64_t lddba, void* stream);
+
+/* y = silu(gate) * up over fused rows [gate (n) | up (n)]. Replaces: silu_mul's twin,
+ * src/adjoint/host/elementwise.cpp:278-293. */
+int r97b_swiglu_fwd(const uint16_t* gu, int64_t ldgu, int64_t rows, int64_t n, uint16_t* y, int64_t ldy,
+                    void* stream);
+
+/* Its adjoint into fused rows dgu. Replaces: silu_mul_host_adjoint, src/adjoint/host/elementwise.cpp:295-312. */
+int r97b_swiglu_bwd(const uint16_t* gu, int64_t ldgu, int64_t rows, int64_t n, const uint16_t* dy, int64_t lddy,
+                    uint16_t* dgu, int64_t lddgu, void* stream);
+
+/* Per (token, head) row of 256: RMSNorm (gain w f32 [256], eps) then NeoX RoPE on the first `rot` dims
+ * (cos / sin tables f32 [S, rot/2]), from rows of x (row_stride, head h at h * head_stride) into
+ * out[b, head, s, :] for a fixed-length batch (T = B * S). Replaces: the q/k norm + rope forward,
+ * src/adjoint/host/qk.cpp and rope.cpp. */
+int r97b_qk_norm_rope_fwd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
+                          const float* w, const float* cos_tab, const float* sin_tab, int32_t rot, int64_t T,
+                          int32_t S, float eps, uint16_t* out, void* stream);
+
+/* Its adjoint into dx (rows of dx_stride, the same head layout). Replaces: qk_adjoint_kernel,
+ * src/adjoint/device/qk.hip:254-488. */
+int r97b_qk_norm_rope_bwd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
+                          const float* w, const float* cos_tab, const float* sin_tab, int32_t rot, int64_t T,
+                          int32_t S, float eps, const uint16_t* dout, uint16_t* dx, int64_t dx_stride,
+                          void* stream);
+
+/* [T, heads, 256] rows -> [B, heads, S, 256] (reverse = 1: back into the rows). */
+int r97b_to_bhsd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads, int64_t T, int32_t S,
+                 uint16_t* out, int32_t reverse, void* stream);
+
+/* y[t, h * 256 + d] = attn[b, h, s, d] * sigmoid(gate[t, h * gate_hs + d]): the gated attention's output
+ * gate. Replaces: the gate half of attention.cpp's twin and gate_ste_kernel, attention.hip:562. */
+int r97b_gate_mul_fwd(const uint16_t* attn, const uint16_t* gate, int64_t gate_stride, int32_t gate_hs,
+                      int32_t heads, int64_t T, int32_t S, uint16_t* y, void* stream);
+
+/* Its adjoint: dattn [B, heads, S, 256] and dgate (rows of dgate_stride). */
+int r97b_gate_mul_bwd(const uint16_t* attn, const uint16_t* gate, int64_t gate_stride, int32_t gate_hs,
+                      int32_t heads, int64_t T, int32_t S, const uint16_t* dy, uint16_t* dattn, uint16_t* dgate,
+                      int64_t dgate_stride, void* stream);
+
+/* out[t, :] = table[ids[t], :] (bf16, zero for an id outside [0, vocab)). Replaces: embed_lookup's twin,
+ * src/adjoint/host/linear.cpp:388-418 (a stop: no adjoint). */
+int r97b_embed(const uint16_t* table, int64_t ld, int64_t vocab, const int32_t* ids, int64_t T, int64_t n,
+               uint16_t* out, void* stream);
+
+/* dst (bf16, ld_dst) = src (f32, ld_src), rows x cols: the adapter's bf16 mirrors after an update. */
+int r97b_cast_f32_bf16(const float* src, int64_t ld_src, uint16_t* dst, int64_t ld_dst, int64_t rows, int64_t cols,
+                       void* stream);
+
+/* How many kernels this library has launched in this process (a diagnostic for the bench). */
+uint64_t r97b_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

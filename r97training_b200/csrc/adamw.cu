@@ -100,5 +100,5 @@ extern "C" int r97b_global_norm(const float* g, int64_t n, float inv_k, float ma
     const int64_t nchunks = (n + kNormChunk - 1) / kNormChunk;
     chunk_sumsq_kernel<<<(unsigned)((nchunks + 255) / 256), 256, 0, as_stream(stream)>>>(g, n, inv_k, partials, nchunks);
     norm_finish_kernel<<<1, 32, 0, as_stream(stream)>>>(partials, nchunks, max_norm, out_norm, out_scale);
-    return launch_status();
+    return launch_status(2);
 }

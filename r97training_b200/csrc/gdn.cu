@@ -812,7 +812,7 @@ extern "C" int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* a, void* 
     if (dm.n_chunks > 0)
         gdn_fwd_out<<<dim3(dm.n_chunks, dm.H), 256, kSmemOut, s>>>(dm, q, k, a->g, a->S, a->Vp, a->P,
                                                                    reinterpret_cast<__nv_bfloat16*>(a->o));
-    return launch_status();
+    return launch_status(dm.n_chunks > 0 ? 3 : 1);
 }
 
 extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* stream) {
@@ -837,7 +837,7 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
                                                                 a->dw, a->pdq, a->pdk, a->pdg, a->dq, a->dk, a->dv,
                                                                 a->dbeta, a->dg);
     }
-    return launch_status();
+    return launch_status(dm.n_chunks > 0 ? 3 : 1);
 }
 
 extern "C" int r97b_gdn_sum_heads(const float* src, float* dst, int64_t T, int32_t H, int32_t Hg, void* stream) {

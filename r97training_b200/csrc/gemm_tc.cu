@@ -371,7 +371,7 @@ int launch(const R97bGemm& g, cudaStream_t stream) {
         attr_set = true;
     }
     kern<<<grid, kThreads, C::kSmemBytes, stream>>>(a1, b1, a2, b2, k);
-    return cudaGetLastError() == cudaSuccess ? R97B_OK : R97B_ELAUNCH;
+    return launch_status();
 }
 
 template <int BN>

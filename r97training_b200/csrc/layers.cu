@@ -1,0 +1,603 @@
+// layers.cu -- the elementwise and per-row kernels around the GEMMs and the recurrence of one hybrid
+// block, forward and backward, on sm_100a. All HBM-bound: 16-byte vector loads, f32 math, bf16 stores.
+//
+//   conv prep   causal depthwise conv (width 4) + silu over the q|k|v channels, L2 norm of q and k per
+//               head (eps 1e-6)             (reference src/adjoint/host/gdn_prep.cpp:204-365, 367-489)
+//   gates       g = chunk-local cumsum of -exp(A_log) softplus(a + dt_bias) (threshold 20), beta = sigmoid(b)
+//   swiglu      y = silu(gate) * up over a fused [rows, 2n] row (reference elementwise.cpp:278-312 silu_mul)
+//   attention   q/k RMSNorm per head + partial NeoX RoPE into the [B, H, S, D] layout the attention core
+//   prep        reads, and the sigmoid output gate (reference src/adjoint/host/qk.cpp, rope.cpp, attention.cpp)
+//   embedding   row gather of the tied head weight
+//   casts       f32 -> bf16 2-D strided copies (adapter mirrors)
+#include "r97b_internal.h"
+
+#include <cuda_bf16.h>
+#include <math.h>
+
+namespace r97b {
+namespace {
+
+__device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float silu(float x) { return x * sigm(x); }
+__device__ __forceinline__ float silu_grad(float x) {
+    const float s = sigm(x);
+    return s * (1.0f + x * (1.0f - s));
+}
+__device__ __forceinline__ float softplus(float x) { return x > 20.0f ? x : log1pf(expf(x)); }
+
+__device__ __forceinline__ void ld8(const __nv_bfloat16* p, float (&v)[8]) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float2 f = __bfloat1622float2(h[i]);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void st8(__nv_bfloat16* p, const float (&v)[8]) {
+    uint4 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+}
+__device__ __forceinline__ void st8f(float* p, const float (&v)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+__device__ __forceinline__ float sum16(float v) {
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+__device__ __forceinline__ float sum32(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+    return v;
+}
+
+// first token of the sequence holding token t
+__device__ __forceinline__ int seq_start(const int* cu, int n_seq, int t) {
+    int lo = 0, hi = n_seq;  // cu[lo] <= t < cu[hi]
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (cu[mid] <= t) lo = mid;
+        else hi = mid;
+    }
+    return cu[lo];
+}
+__device__ __forceinline__ int seq_end(const int* cu, int n_seq, int t) {
+    int lo = 0, hi = n_seq;
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (cu[mid] <= t) lo = mid;
+        else hi = mid;
+    }
+    return cu[lo + 1];
+}
+
+constexpr int kW = 4;  // conv width
+
+// ------------------------------------------------------------------------------------------- conv prep
+
+struct ConvArgs {
+    const __nv_bfloat16* x;
+    int64_t ldx;
+    const float* w;  // [conv_dim, 4]
+    const int* cu;
+    int n_seq, T, Hg, H, conv_dim;
+};
+
+// acc[c..c+7] of token t (pre-activation)
+__device__ __forceinline__ void conv8(const ConvArgs& a, int t, int t0, int c, float (&acc)[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kW; ++j) {
+        const int src = t - (kW - 1) + j;
+        if (src < t0) continue;
+        float xv[8];
+        ld8(a.x + (int64_t)src * a.ldx + c, xv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = fmaf(xv[i], a.w[(c + i) * kW + j], acc[i]);
+    }
+}
+
+__global__ void __launch_bounds__(256) conv_prep_fwd_kernel(ConvArgs a, __nv_bfloat16* __restrict__ q,
+                                                            __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v) {
+    const int groups = a.conv_dim / 8;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool valid = gid < (int64_t)a.T * groups;
+    const int t = valid ? (int)(gid / groups) : a.T - 1;
+    const int c = valid ? (int)(gid % groups) * 8 : 0;
+    const int t0 = seq_start(a.cu, a.n_seq, t);
+    float acc[8], u[8];
+    conv8(a, t, t0, c, acc);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        u[i] = silu(acc[i]);
+        ss = fmaf(u[i], u[i], ss);
+    }
+    const int qk = a.Hg * 128;
+    // 16 consecutive lanes cover one 128-wide head; the q|k|v boundaries are head aligned
+    ss = sum16(ss);
+    if (!valid) return;
+    if (c < 2 * qk) {
+        const float inv = rsqrtf(ss + 1e-6f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u[i] *= inv;
+        if (c < qk) st8(q + (int64_t)t * qk + c, u);
+        else st8(k + (int64_t)t * qk + (c - qk), u);
+    } else {
+        st8(v + (int64_t)t * a.H * 128 + (c - 2 * qk), u);
+    }
+}
+
+// dacc[t, c] from the cotangents of the normalised q, k (f32 [T, Hg, 128]) and of v (f32 [T, H, 128])
+__global__ void __launch_bounds__(256) conv_prep_dacc_kernel(ConvArgs a, const float* __restrict__ dq,
+                                                             const float* __restrict__ dk, const float* __restrict__ dv,
+                                                             float* __restrict__ dacc) {
+    const int groups = a.conv_dim / 8;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const bool valid = gid < (int64_t)a.T * groups;
+    const int t = valid ? (int)(gid / groups) : a.T - 1;
+    const int c = valid ? (int)(gid % groups) * 8 : 0;
+    const int t0 = seq_start(a.cu, a.n_seq, t);
+    const int qk = a.Hg * 128;
+    float acc[8], u[8], dout[8];
+    conv8(a, t, t0, c, acc);
+    if (c < qk) ld8f(dq + (int64_t)t * qk + c, dout);
+    else if (c < 2 * qk) ld8f(dk + (int64_t)t * qk + (c - qk), dout);
+    else ld8f(dv + (int64_t)t * a.H * 128 + (c - 2 * qk), dout);
+    float ss = 0.0f, dot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        u[i] = silu(acc[i]);
+        ss = fmaf(u[i], u[i], ss);
+        dot = fmaf(u[i], dout[i], dot);
+    }
+    ss = sum16(ss);
+    dot = sum16(dot);
+    if (!valid) return;
+    float o[8];
+    if (c < 2 * qk) {
+        const float inv = rsqrtf(ss + 1e-6f), inv3 = inv * inv * inv;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = (inv * dout[i] - inv3 * u[i] * dot) * silu_grad(acc[i]);
+    } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = dout[i] * silu_grad(acc[i]);
+    }
+    st8f(dacc + (int64_t)t * a.conv_dim + c, o);
+}
+
+// dx[t, c] = sum_{t' = t .. t+3, same sequence} dacc[t', c] w[c, t - t' + 3]
+__global__ void __launch_bounds__(256) conv_prep_dx_kernel(ConvArgs a, const float* __restrict__ dacc,
+                                                           __nv_bfloat16* __restrict__ dx, int64_t lddx) {
+    const int groups = a.conv_dim / 8;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)a.T * groups) return;
+    const int t = (int)(gid / groups);
+    const int c = (int)(gid % groups) * 8;
+    const int t1 = seq_end(a.cu, a.n_seq, t);
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+#pragma unroll
+    for (int s = 0; s < kW; ++s) {
+        const int tp = t + s;
+        if (tp >= t1) break;
+        float d[8];
+        ld8f(dacc + (int64_t)tp * a.conv_dim + c, d);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = fmaf(d[i], a.w[(c + i) * kW + (kW - 1 - s)], o[i]);
+    }
+    st8(dx + (int64_t)t * lddx + c, o);
+}
+
+// ------------------------------------------------------------------------------------------- gates
+
+// one thread per (chunk, head): beta = sigmoid(b), g = within-chunk running sum of the decay increment
+__global__ void gates_fwd_kernel(const __nv_bfloat16* __restrict__ ba, int64_t ldba, const float* __restrict__ a_log,
+                                 const float* __restrict__ dt_bias, const int* __restrict__ tok0,
+                                 const int* __restrict__ len, int n_chunks, int H, float* __restrict__ g,
+                                 float* __restrict__ beta) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n_chunks * H) return;
+    const int c = idx / H, h = idx % H;
+    const float decay = -expf(a_log[h]);
+    float run = 0.0f;
+    for (int i = 0; i < len[c]; ++i) {
+        const int64_t t = tok0[c] + i;
+        const float bv = __bfloat162float(ba[t * ldba + h]);
+        const float av = __bfloat162float(ba[t * ldba + H + h]);
+        run += decay * softplus(av + dt_bias[h]);
+        g[t * H + h] = run;
+        beta[t * H + h] = sigm(bv);
+    }
+}
+
+__global__ void gates_bwd_kernel(const __nv_bfloat16* __restrict__ ba, int64_t ldba, const float* __restrict__ a_log,
+                                 const float* __restrict__ dt_bias, const int* __restrict__ tok0,
+                                 const int* __restrict__ len, int n_chunks, int H, const float* __restrict__ dg,
+                                 const float* __restrict__ dbeta, __nv_bfloat16* __restrict__ dba, int64_t lddba) {
+    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= n_chunks * H) return;
+    const int c = idx / H, h = idx % H;
+    const float decay = -expf(a_log[h]);
+    float tail = 0.0f;
+    for (int i = len[c] - 1; i >= 0; --i) {
+        const int64_t t = tok0[c] + i;
+        tail += dg[t * H + h];
+        const float av = __bfloat162float(ba[t * ldba + H + h]) + dt_bias[h];
+        const float sp = av > 20.0f ? 1.0f : sigm(av);
+        dba[t * lddba + H + h] = __float2bfloat16_rn(tail * decay * sp);
+        const float s = sigm(__bfloat162float(ba[t * ldba + h]));
+        dba[t * lddba + h] = __float2bfloat16_rn(dbeta[t * H + h] * s * (1.0f - s));
+    }
+}
+
+// ------------------------------------------------------------------------------------------- swiglu
+
+__global__ void __launch_bounds__(256) swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, int64_t ldgu, int64_t rows,
+                                                         int n, __nv_bfloat16* __restrict__ y, int64_t ldy) {
+    const int groups = n / 8;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= rows * groups) return;
+    const int64_t r = gid / groups;
+    const int c = (int)(gid % groups) * 8;
+    float gv[8], uv[8];
+    ld8(gu + r * ldgu + c, gv);
+    ld8(gu + r * ldgu + n + c, uv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) gv[i] = silu(gv[i]) * uv[i];
+    st8(y + r * ldy + c, gv);
+}
+
+__global__ void __launch_bounds__(256) swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu, int64_t ldgu, int64_t rows,
+                                                         int n, const __nv_bfloat16* __restrict__ dy, int64_t lddy,
+                                                         __nv_bfloat16* __restrict__ dgu, int64_t lddgu) {
+    const int groups = n / 8;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= rows * groups) return;
+    const int64_t r = gid / groups;
+    const int c = (int)(gid % groups) * 8;
+    float gv[8], uv[8], d[8], og[8], ou[8];
+    ld8(gu + r * ldgu + c, gv);
+    ld8(gu + r * ldgu + n + c, uv);
+    ld8(dy + r * lddy + c, d);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        og[i] = d[i] * uv[i] * silu_grad(gv[i]);
+        ou[i] = d[i] * silu(gv[i]);
+    }
+    st8(dgu + r * lddgu + c, og);
+    st8(dgu + r * lddgu + n + c, ou);
+}
+
+// ------------------------------------------------------------------------------------------- attention prep
+
+// One warp per (token, head) row of 256: RMSNorm (eps) with gain w, then NeoX RoPE on the first
+// `rot` dims (lanes 0..rot/8-1), into out[b, head, s, :] with b, s from the token's sequence.
+struct QkArgs {
+    const __nv_bfloat16* x;  // rows of `row_stride`, head h at h * head_stride
+    int64_t row_stride;
+    int head_stride;
+    int heads;
+    const float* w;          // [256]
+    const float* cosb;       // [S, rot/2]
+    const float* sinb;
+    int rot;
+    int T, S;                // tokens, sequence length (fixed-length batch)
+    float eps;
+};
+
+__global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(QkArgs a, __nv_bfloat16* __restrict__ out) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row >= (int64_t)a.T * a.heads) return;
+    const int t = (int)(row / a.heads), h = (int)(row % a.heads);
+    const int b = t / a.S, s = t % a.S;
+    float v[8], w[8];
+    ld8(a.x + (int64_t)t * a.row_stride + h * a.head_stride + lane * 8, v);
+    ld8f(a.w + lane * 8, w);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+    ss = sum32(ss);
+    const float r = rsqrtf(ss / 256.0f + a.eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] *= r * w[i];
+    const int half = a.rot / 2;          // rotary pairs (i, i + half)
+    const int pl = half / 8;             // lanes holding the first half
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, v[i], pl);  // every lane joins
+    if (lane < 2 * pl) {
+        const bool first = lane < pl;
+        const int j0 = (first ? lane : lane - pl) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float cs = a.cosb[s * half + j0 + i], sn = a.sinb[s * half + j0 + i];
+            v[i] = first ? v[i] * cs - o[i] * sn : v[i] * cs + o[i] * sn;
+        }
+    }
+    st8(out + (((int64_t)b * a.heads + h) * a.S + s) * 256 + lane * 8, v);
+}
+
+// The adjoint: inverse rotation of dout, then the RMSNorm adjoint against the saved pre-norm row;
+// dx into rows of `dx_stride` (the projection's cotangent buffer).
+__global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(QkArgs a, const __nv_bfloat16* __restrict__ dout,
+                                                               __nv_bfloat16* __restrict__ dx, int64_t dx_stride) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    if (row >= (int64_t)a.T * a.heads) return;
+    const int t = (int)(row / a.heads), h = (int)(row % a.heads);
+    const int b = t / a.S, s = t % a.S;
+    float d[8], x[8], w[8];
+    ld8(dout + (((int64_t)b * a.heads + h) * a.S + s) * 256 + lane * 8, d);
+    ld8(a.x + (int64_t)t * a.row_stride + h * a.head_stride + lane * 8, x);
+    ld8f(a.w + lane * 8, w);
+    const int half = a.rot / 2, pl = half / 8;
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, d[i], pl);
+    if (lane < 2 * pl) {
+        const bool first = lane < pl;
+        const int j0 = (first ? lane : lane - pl) * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float cs = a.cosb[s * half + j0 + i], sn = a.sinb[s * half + j0 + i];
+            // y1 = x1 c - x2 s, y2 = x2 c + x1 s  =>  dx1 = dy1 c + dy2 s, dx2 = dy2 c - dy1 s
+            d[i] = first ? d[i] * cs + o[i] * sn : d[i] * cs - o[i] * sn;
+        }
+    }
+    float ss = 0.0f, tt = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        ss = fmaf(x[i], x[i], ss);
+        tt = fmaf(d[i] * x[i], w[i], tt);
+    }
+    ss = sum32(ss);
+    tt = sum32(tt);
+    const float r = rsqrtf(ss / 256.0f + a.eps);
+    const float kk = r * r * r * tt / 256.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) d[i] = r * w[i] * d[i] - kk * x[i];
+    st8(dx + (int64_t)t * dx_stride + h * a.head_stride + lane * 8, d);
+}
+
+// [T, heads, 256] rows (row stride) -> [B, heads, S, 256] and back
+__global__ void __launch_bounds__(256) to_bhsd_kernel(const __nv_bfloat16* __restrict__ x, int64_t row_stride,
+                                                      int head_stride, int heads, int T, int S,
+                                                      __nv_bfloat16* __restrict__ out, int reverse) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)T * heads * 32) return;
+    const int lane = (int)(gid & 31);
+    const int64_t row = gid >> 5;
+    const int t = (int)(row / heads), h = (int)(row % heads);
+    const int b = t / S, s = t % S;
+    const int64_t at_bhsd = (((int64_t)b * heads + h) * S + s) * 256 + lane * 8;
+    const int64_t at_row = (int64_t)t * row_stride + (int64_t)h * head_stride + lane * 8;
+    if (reverse)
+        *reinterpret_cast<uint4*>(const_cast<__nv_bfloat16*>(x) + at_row) = *reinterpret_cast<const uint4*>(out + at_bhsd);
+    else
+        *reinterpret_cast<uint4*>(out + at_bhsd) = *reinterpret_cast<const uint4*>(x + at_row);
+}
+
+// y[t, h*256 + d] = attn[b, h, s, d] * sigmoid(gate[t, h]) ; gate rows of `gate_stride`, head at h*gate_hs
+__global__ void __launch_bounds__(256) gate_mul_fwd_kernel(const __nv_bfloat16* __restrict__ attn,
+                                                           const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
+                                                           int gate_hs, int heads, int T, int S,
+                                                           __nv_bfloat16* __restrict__ y) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)T * heads * 32) return;
+    const int lane = (int)(gid & 31);
+    const int64_t row = gid >> 5;
+    const int t = (int)(row / heads), h = (int)(row % heads);
+    const int b = t / S, s = t % S;
+    float av[8], gv[8];
+    ld8(attn + (((int64_t)b * heads + h) * S + s) * 256 + lane * 8, av);
+    ld8(gate + (int64_t)t * gate_stride + (int64_t)h * gate_hs + lane * 8, gv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) av[i] *= sigm(gv[i]);
+    st8(y + ((int64_t)t * heads + h) * 256 + lane * 8, av);
+}
+
+__global__ void __launch_bounds__(256) gate_mul_bwd_kernel(const __nv_bfloat16* __restrict__ attn,
+                                                           const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
+                                                           int gate_hs, int heads, int T, int S,
+                                                           const __nv_bfloat16* __restrict__ dy,
+                                                           __nv_bfloat16* __restrict__ dattn,
+                                                           __nv_bfloat16* __restrict__ dgate, int64_t dgate_stride) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= (int64_t)T * heads * 32) return;
+    const int lane = (int)(gid & 31);
+    const int64_t row = gid >> 5;
+    const int t = (int)(row / heads), h = (int)(row % heads);
+    const int b = t / S, s = t % S;
+    const int64_t at = (((int64_t)b * heads + h) * S + s) * 256 + lane * 8;
+    float av[8], gv[8], d[8], da[8], dg[8];
+    ld8(attn + at, av);
+    ld8(gate + (int64_t)t * gate_stride + (int64_t)h * gate_hs + lane * 8, gv);
+    ld8(dy + ((int64_t)t * heads + h) * 256 + lane * 8, d);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float sg = sigm(gv[i]);
+        da[i] = d[i] * sg;
+        dg[i] = d[i] * av[i] * sg * (1.0f - sg);
+    }
+    st8(dattn + at, da);
+    st8(dgate + (int64_t)t * dgate_stride + (int64_t)h * gate_hs + lane * 8, dg);
+}
+
+// ------------------------------------------------------------------------------------------- misc
+
+__global__ void __launch_bounds__(256) embed_kernel(const __nv_bfloat16* __restrict__ table, int64_t ld, int64_t vocab,
+                                                    const int32_t* __restrict__ ids, int64_t T, int n,
+                                                    __nv_bfloat16* __restrict__ out) {
+    const int groups = n / 8;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= T * groups) return;
+    const int64_t t = gid / groups;
+    const int c = (int)(gid % groups) * 8;
+    const int id = ids[t];
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (id >= 0 && id < vocab) v = *reinterpret_cast<const uint4*>(table + (int64_t)id * ld + c);
+    *reinterpret_cast<uint4*>(out + t * n + c) = v;
+}
+
+__global__ void cast_2d_kernel(const float* __restrict__ src, int64_t ld_src, __nv_bfloat16* __restrict__ dst,
+                               int64_t ld_dst, int64_t rows, int64_t cols) {
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (gid >= rows * cols) return;
+    const int64_t r = gid / cols, c = gid % cols;
+    dst[r * ld_dst + c] = __float2bfloat16_rn(src[r * ld_src + c]);
+}
+
+unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256); }
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+}  // namespace
+}  // namespace r97b
+
+using namespace r97b;
+
+extern "C" int r97b_conv_prep_fwd(const uint16_t* x, int64_t ldx, const float* conv_w, const int32_t* cu, int32_t n_seq,
+                                  int64_t T, int32_t Hg, int32_t H, uint16_t* q, uint16_t* k, uint16_t* v,
+                                  void* stream) {
+    if (!x || !conv_w || !cu || !q || !k || !v || T <= 0 || Hg <= 0 || H <= 0 || (ldx % 8) || !al16(x)) return R97B_EINVAL;
+    ConvArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, conv_w, cu, n_seq, (int)T, Hg, H, (2 * Hg + H) * 128};
+    conv_prep_fwd_kernel<<<blocks_for(T * (a.conv_dim / 8)), 256, 0, as_stream(stream)>>>(
+        a, reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(k), reinterpret_cast<__nv_bfloat16*>(v));
+    return launch_status();
+}
+
+extern "C" int r97b_conv_prep_bwd(const uint16_t* x, int64_t ldx, const float* conv_w, const int32_t* cu,
+                                  int32_t n_seq, int64_t T, int32_t Hg, int32_t H, const float* dq, const float* dk,
+                                  const float* dv, float* dacc, uint16_t* dx, int64_t lddx, void* stream) {
+    if (!x || !conv_w || !cu || !dq || !dk || !dv || !dacc || !dx || T <= 0 || (ldx % 8) || (lddx % 8))
+        return R97B_EINVAL;
+    ConvArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, conv_w, cu, n_seq, (int)T, Hg, H, (2 * Hg + H) * 128};
+    const unsigned blocks = blocks_for(T * (a.conv_dim / 8));
+    conv_prep_dacc_kernel<<<blocks, 256, 0, as_stream(stream)>>>(a, dq, dk, dv, dacc);
+    conv_prep_dx_kernel<<<blocks, 256, 0, as_stream(stream)>>>(a, dacc, reinterpret_cast<__nv_bfloat16*>(dx), lddx);
+    return launch_status(2);
+}
+
+extern "C" int r97b_gates_fwd(const uint16_t* ba, int64_t ldba, const float* a_log, const float* dt_bias,
+                              const int32_t* chunk_tok0, const int32_t* chunk_len, int32_t n_chunks, int32_t H, float* g,
+                              float* beta, void* stream) {
+    if (!ba || !a_log || !dt_bias || !chunk_tok0 || !chunk_len || !g || !beta || H <= 0) return R97B_EINVAL;
+    if (n_chunks <= 0) return R97B_OK;
+    gates_fwd_kernel<<<blocks_for((int64_t)n_chunks * H), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(ba), ldba, a_log, dt_bias, chunk_tok0, chunk_len, n_chunks, H, g, beta);
+    return launch_status();
+}
+
+extern "C" int r97b_gates_bwd(const uint16_t* ba, int64_t ldba, const float* a_log, const float* dt_bias,
+                              const int32_t* chunk_tok0, const int32_t* chunk_len, int32_t n_chunks, int32_t H,
+                              const float* dg, const float* dbeta, uint16_t* dba, int64_t lddba, void* stream) {
+    if (!ba || !a_log || !dt_bias || !chunk_tok0 || !chunk_len || !dg || !dbeta || !dba || H <= 0) return R97B_EINVAL;
+    if (n_chunks <= 0) return R97B_OK;
+    gates_bwd_kernel<<<blocks_for((int64_t)n_chunks * H), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(ba), ldba, a_log, dt_bias, chunk_tok0, chunk_len, n_chunks, H, dg, dbeta,
+        reinterpret_cast<__nv_bfloat16*>(dba), lddba);
+    return launch_status();
+}
+
+extern "C" int r97b_swiglu_fwd(const uint16_t* gu, int64_t ldgu, int64_t rows, int64_t n, uint16_t* y, int64_t ldy,
+                               void* stream) {
+    if (!gu || !y || rows <= 0 || n <= 0 || n % 8 || ldgu % 8 || ldy % 8 || !al16(gu) || !al16(y)) return R97B_EINVAL;
+    swiglu_fwd_kernel<<<blocks_for(rows * (n / 8)), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gu), ldgu, rows, (int)n, reinterpret_cast<__nv_bfloat16*>(y), ldy);
+    return launch_status();
+}
+
+extern "C" int r97b_swiglu_bwd(const uint16_t* gu, int64_t ldgu, int64_t rows, int64_t n, const uint16_t* dy,
+                               int64_t lddy, uint16_t* dgu, int64_t lddgu, void* stream) {
+    if (!gu || !dy || !dgu || rows <= 0 || n <= 0 || n % 8 || ldgu % 8 || lddy % 8 || lddgu % 8) return R97B_EINVAL;
+    swiglu_bwd_kernel<<<blocks_for(rows * (n / 8)), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(gu), ldgu, rows, (int)n, reinterpret_cast<const __nv_bfloat16*>(dy), lddy,
+        reinterpret_cast<__nv_bfloat16*>(dgu), lddgu);
+    return launch_status();
+}
+
+extern "C" int r97b_qk_norm_rope_fwd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
+                                     const float* w, const float* cos_tab, const float* sin_tab, int32_t rot,
+                                     int64_t T, int32_t S, float eps, uint16_t* out, void* stream) {
+    if (!x || !w || !cos_tab || !sin_tab || !out || T <= 0 || S <= 0 || T % S || rot % 16 || rot > 256 ||
+        head_stride % 8 || row_stride % 8)
+        return R97B_EINVAL;
+    QkArgs a{reinterpret_cast<const __nv_bfloat16*>(x), row_stride, head_stride, heads, w, cos_tab, sin_tab, rot,
+             (int)T, S, eps};
+    qk_norm_rope_fwd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+        a, reinterpret_cast<__nv_bfloat16*>(out));
+    return launch_status();
+}
+
+extern "C" int r97b_qk_norm_rope_bwd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
+                                     const float* w, const float* cos_tab, const float* sin_tab, int32_t rot,
+                                     int64_t T, int32_t S, float eps, const uint16_t* dout, uint16_t* dx,
+                                     int64_t dx_stride, void* stream) {
+    if (!x || !w || !cos_tab || !sin_tab || !dout || !dx || T <= 0 || S <= 0 || T % S || rot % 16 || rot > 256)
+        return R97B_EINVAL;
+    QkArgs a{reinterpret_cast<const __nv_bfloat16*>(x), row_stride, head_stride, heads, w, cos_tab, sin_tab, rot,
+             (int)T, S, eps};
+    qk_norm_rope_bwd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+        a, reinterpret_cast<const __nv_bfloat16*>(dout), reinterpret_cast<__nv_bfloat16*>(dx), dx_stride);
+    return launch_status();
+}
+
+extern "C" int r97b_to_bhsd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads, int64_t T,
+                            int32_t S, uint16_t* out, int32_t reverse, void* stream) {
+    if (!x || !out || T <= 0 || S <= 0 || T % S || head_stride % 8 || row_stride % 8) return R97B_EINVAL;
+    to_bhsd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x), row_stride, head_stride, heads, (int)T, S,
+        reinterpret_cast<__nv_bfloat16*>(out), reverse);
+    return launch_status();
+}
+
+extern "C" int r97b_gate_mul_fwd(const uint16_t* attn, const uint16_t* gate, int64_t gate_stride, int32_t gate_hs,
+                                 int32_t heads, int64_t T, int32_t S, uint16_t* y, void* stream) {
+    if (!attn || !gate || !y || T <= 0 || S <= 0 || T % S) return R97B_EINVAL;
+    gate_mul_fwd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(attn), reinterpret_cast<const __nv_bfloat16*>(gate), gate_stride, gate_hs,
+        heads, (int)T, S, reinterpret_cast<__nv_bfloat16*>(y));
+    return launch_status();
+}
+
+extern "C" int r97b_gate_mul_bwd(const uint16_t* attn, const uint16_t* gate, int64_t gate_stride, int32_t gate_hs,
+                                 int32_t heads, int64_t T, int32_t S, const uint16_t* dy, uint16_t* dattn,
+                                 uint16_t* dgate, int64_t dgate_stride, void* stream) {
+    if (!attn || !gate || !dy || !dattn || !dgate || T <= 0 || S <= 0 || T % S) return R97B_EINVAL;
+    gate_mul_bwd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(attn), reinterpret_cast<const __nv_bfloat16*>(gate), gate_stride, gate_hs,
+        heads, (int)T, S, reinterpret_cast<const __nv_bfloat16*>(dy), reinterpret_cast<__nv_bfloat16*>(dattn),
+        reinterpret_cast<__nv_bfloat16*>(dgate), dgate_stride);
+    return launch_status();
+}
+
+extern "C" int r97b_embed(const uint16_t* table, int64_t ld, int64_t vocab, const int32_t* ids, int64_t T, int64_t n,
+                          uint16_t* out, void* stream) {
+    if (!table || !ids || !out || T <= 0 || n % 8 || ld % 8) return R97B_EINVAL;
+    embed_kernel<<<blocks_for(T * (n / 8)), 256, 0, as_stream(stream)>>>(
+        reinterpret_cast<const __nv_bfloat16*>(table), ld, vocab, ids, T, (int)n, reinterpret_cast<__nv_bfloat16*>(out));
+    return launch_status();
+}
+
+extern "C" int r97b_cast_f32_bf16(const float* src, int64_t ld_src, uint16_t* dst, int64_t ld_dst, int64_t rows,
+                                  int64_t cols, void* stream) {
+    if (!src || !dst || rows <= 0 || cols <= 0) return R97B_EINVAL;
+    cast_2d_kernel<<<blocks_for(rows * cols), 256, 0, as_stream(stream)>>>(src, ld_src,
+                                                                         reinterpret_cast<__nv_bfloat16*>(dst), ld_dst,
+                                                                         rows, cols);
+    return launch_status();
+}

@@ -18,6 +18,13 @@ unsigned gemm_error_word();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
-inline int launch_status() { return cudaGetLastError() == cudaSuccess ? R97B_OK : R97B_ELAUNCH; }
+// Counts this library's kernel launches (r97b_launch_count); `n` = the launches the caller just queued.
+void add_launches(int n);
+
+inline int launch_status(int n = 1) {
+    if (cudaGetLastError() != cudaSuccess) return R97B_ELAUNCH;
+    add_launches(n);
+    return R97B_OK;
+}
 
 }  // namespace r97b

@@ -75,8 +75,28 @@ def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STOR
     if addend is not None:
         _need(addend, torch.bfloat16, "addend")
         g.addend, g.ld_add = addend.data_ptr(), addend.stride(0)
+    prof = GEMM_PROFILE
+    if prof is not None:
+        s = stream if stream is not None else torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
     check(lib().r97b_gemm(ctypes.byref(g), _stream(stream)), "r97b_gemm")
+    if prof is not None:
+        e1.record(s)
+        prof.append((e0, e1, 2.0 * M * N * (K1 + (g.K2 if a2 is not None else 0))))
     return out
+
+
+# When a list, every gemm() appends (start event, end event, algorithmic FLOPs) recorded on its stream:
+# bench.py's live measurement of the tensor-core GEMM's launch durations.
+GEMM_PROFILE = None
+
+
+def gemm_profile_summary(prof):
+    """(launches, total device ms, total FLOPs) of a recorded profile (synchronises)."""
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b, _ in prof)
+    return len(prof), ms, sum(f for _, _, f in prof)
 
 
 # ------------------------------------------------------------------------------------------ norms
@@ -158,3 +178,85 @@ def global_norm(g, *, inv_k=1.0, max_norm=0.0, scratch=None, stream=None):
     check(lib().r97b_global_norm(_ptr(g), n, inv_k, max_norm, _ptr(scratch), ctypes.c_void_p(out.data_ptr()),
                                  ctypes.c_void_p(out.data_ptr() + 4), _stream(stream)), "r97b_global_norm")
     return out[0], out[1:2]
+
+
+# ------------------------------------------------------------------------------------------ layer kernels
+
+def conv_prep_fwd(x, conv_w, cu_dev, n_seq, Hg, H, q, k, v, stream=None):
+    """q, k (L2-normalised) and v of the causal conv + silu over the first (2 Hg + H) 128 columns of x."""
+    T = x.shape[0]
+    check(lib().r97b_conv_prep_fwd(_ptr(x), x.stride(0), _ptr(conv_w), _ptr(cu_dev), n_seq, T, Hg, H, _ptr(q),
+                                   _ptr(k), _ptr(v), _stream(stream)), "r97b_conv_prep_fwd")
+
+
+def conv_prep_bwd(x, conv_w, cu_dev, n_seq, Hg, H, dq, dk, dv, dacc, dx, stream=None):
+    T = x.shape[0]
+    check(lib().r97b_conv_prep_bwd(_ptr(x), x.stride(0), _ptr(conv_w), _ptr(cu_dev), n_seq, T, Hg, H, _ptr(dq),
+                                   _ptr(dk), _ptr(dv), _ptr(dacc), _ptr(dx), dx.stride(0), _stream(stream)),
+          "r97b_conv_prep_bwd")
+
+
+def gates_fwd(ba, a_log, dt_bias, plan, g, beta, stream=None):
+    check(lib().r97b_gates_fwd(_ptr(ba), ba.stride(0), _ptr(a_log), _ptr(dt_bias), _ptr(plan.tok0), _ptr(plan.len),
+                               plan.n_chunks, plan.H, _ptr(g), _ptr(beta), _stream(stream)), "r97b_gates_fwd")
+
+
+def gates_bwd(ba, a_log, dt_bias, plan, dg, dbeta, dba, stream=None):
+    check(lib().r97b_gates_bwd(_ptr(ba), ba.stride(0), _ptr(a_log), _ptr(dt_bias), _ptr(plan.tok0), _ptr(plan.len),
+                               plan.n_chunks, plan.H, _ptr(dg), _ptr(dbeta), _ptr(dba), dba.stride(0),
+                               _stream(stream)), "r97b_gates_bwd")
+
+
+def swiglu_fwd(gu, y, stream=None):
+    rows, n = y.shape
+    check(lib().r97b_swiglu_fwd(_ptr(gu), gu.stride(0), rows, n, _ptr(y), y.stride(0), _stream(stream)),
+          "r97b_swiglu_fwd")
+
+
+def swiglu_bwd(gu, dy, dgu, stream=None):
+    rows, n = dy.shape
+    check(lib().r97b_swiglu_bwd(_ptr(gu), gu.stride(0), rows, n, _ptr(dy), dy.stride(0), _ptr(dgu), dgu.stride(0),
+                                _stream(stream)), "r97b_swiglu_bwd")
+
+
+def qk_norm_rope_fwd(x, head_stride, heads, w, cos_t, sin_t, rot, S, eps, out, stream=None):
+    T = x.shape[0]
+    check(lib().r97b_qk_norm_rope_fwd(_ptr(x), x.stride(0), head_stride, heads, _ptr(w), _ptr(cos_t), _ptr(sin_t),
+                                      rot, T, S, eps, _ptr(out), _stream(stream)), "r97b_qk_norm_rope_fwd")
+
+
+def qk_norm_rope_bwd(x, head_stride, heads, w, cos_t, sin_t, rot, S, eps, dout, dx, stream=None):
+    T = x.shape[0]
+    check(lib().r97b_qk_norm_rope_bwd(_ptr(x), x.stride(0), head_stride, heads, _ptr(w), _ptr(cos_t), _ptr(sin_t),
+                                      rot, T, S, eps, _ptr(dout), _ptr(dx), dx.stride(0), _stream(stream)),
+          "r97b_qk_norm_rope_bwd")
+
+
+def to_bhsd(x, head_stride, heads, S, out, reverse=False, stream=None):
+    T = x.shape[0]
+    check(lib().r97b_to_bhsd(_ptr(x), x.stride(0), head_stride, heads, T, S, _ptr(out), int(reverse),
+                             _stream(stream)), "r97b_to_bhsd")
+
+
+def gate_mul_fwd(attn, gate, gate_hs, heads, S, y, stream=None):
+    T = y.shape[0]
+    check(lib().r97b_gate_mul_fwd(_ptr(attn), _ptr(gate), gate.stride(0), gate_hs, heads, T, S, _ptr(y),
+                                  _stream(stream)), "r97b_gate_mul_fwd")
+
+
+def gate_mul_bwd(attn, gate, gate_hs, heads, S, dy, dattn, dgate, stream=None):
+    T = dy.shape[0]
+    check(lib().r97b_gate_mul_bwd(_ptr(attn), _ptr(gate), gate.stride(0), gate_hs, heads, T, S, _ptr(dy),
+                                  _ptr(dattn), _ptr(dgate), dgate.stride(0), _stream(stream)), "r97b_gate_mul_bwd")
+
+
+def embed(table, ids, out, stream=None):
+    T, n = out.shape
+    check(lib().r97b_embed(_ptr(table), table.stride(0), table.shape[0], _ptr(ids), T, n, _ptr(out),
+                           _stream(stream)), "r97b_embed")
+
+
+def cast_f32_bf16(src, dst, stream=None):
+    rows, cols = src.shape
+    check(lib().r97b_cast_f32_bf16(_ptr(src), src.stride(0), _ptr(dst), dst.stride(0), rows, cols,
+                                   _stream(stream)), "r97b_cast_f32_bf16")

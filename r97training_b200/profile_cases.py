@@ -1,0 +1,69 @@
+"""Small, self-contained cases of the hot kernels, for profiling one launch under ncu:
+
+    python -m r97training_b200.profile_cases gemm      # the config-5 gate_up forward GEMM (8192 x 24576 x 4096)
+    python -m r97training_b200.profile_cases gemm_dx   # its input adjoint (B operand MN-major)
+    python -m r97training_b200.profile_cases gdn       # one config-5 GDN layer, forward + backward
+    python -m r97training_b200.profile_cases decode    # the IQR decode of a 24576 x 4096 weight
+    python -m r97training_b200.profile_cases norms     # rmsnorm fwd/bwd at 8192 x 4096
+
+Each case allocates a few hundred MB to a few GB (operands larger than the 126 MB L2), runs two warm-up
+launches and then the launches to capture, and exits.
+"""
+from __future__ import annotations
+
+import sys
+
+import torch
+
+
+def main(case: str) -> None:
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    if case in ("gemm", "gemm_dx"):
+        from . import ops
+        M, N, K = 8192, 24576, 4096
+        X = torch.randn(M, K, device=dev).bfloat16()
+        W = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+        if case == "gemm":
+            Y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            for _ in range(3):
+                ops.gemm(X, W, Y)
+        else:
+            dY = torch.randn(M, N, device=dev).bfloat16()
+            dX = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
+            for _ in range(3):
+                ops.gemm(dY, W, dX, b_mn=True, N=K)
+    elif case == "gdn":
+        from .gdn import GdnPlan
+        T, H, Hg = 8192, 32, 16
+        q = torch.nn.functional.normalize(torch.randn(T, Hg, 128, device=dev), dim=-1).bfloat16()
+        k = torch.nn.functional.normalize(torch.randn(T, Hg, 128, device=dev), dim=-1).bfloat16()
+        v = torch.randn(T, H, 128, device=dev).bfloat16()
+        g = (-torch.nn.functional.softplus(torch.randn(T, H, device=dev))).view(-1, 64, H).cumsum(1).view(T, H)
+        beta = torch.sigmoid(torch.randn(T, H, device=dev))
+        do = (torch.randn(T, H, 128, device=dev) * 1e-2).bfloat16()
+        plan = GdnPlan([0, 4096, 8192], H, Hg, dev)
+        for _ in range(2):
+            o, _, sv = plan.forward(q, k, v, g.contiguous(), beta)
+            plan.backward(sv, do)
+    elif case == "decode":
+        from . import iqr as IQ
+        w = IQ.synth_weight(24576, 4096, seed=1, device=dev)
+        out = torch.empty(24576, 4096, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            IQ.dequant_bf16(w, out=out)
+    elif case == "norms":
+        from . import ops
+        x = torch.randn(8192, 4096, device=dev).bfloat16()
+        dy = torch.randn(8192, 4096, device=dev).bfloat16()
+        w = torch.ones(4096, device=dev)
+        for _ in range(3):
+            ops.rmsnorm_fwd(x, w)
+            ops.rmsnorm_bwd(x, w, dy, addend=dy)
+    else:
+        raise SystemExit(f"unknown case {case}")
+    torch.cuda.synchronize()
+
+
+if __name__ == "__main__":
+    main(sys.argv[1] if len(sys.argv) > 1 else "gemm")

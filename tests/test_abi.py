@@ -16,7 +16,7 @@ def declared():
             continue
         src = open(os.path.join(ROOT, "include", h)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-        for m in re.finditer(r"^\s*(?:int|int64_t|void|unsigned int|const char\s*\*)\s+(r97\w*)\s*\(", src, re.M):
+        for m in re.finditer(r"^\s*(?:int|int32_t|int64_t|uint64_t|void|unsigned int|const char\s*\*)\s+(r97\w*)\s*\(", src, re.M):
             names.add(m.group(1))
     return names
 
