@@ -27,6 +27,7 @@ enum {
     R97B_EINVAL = 1,   /* arguments outside the kernel's rules (same meaning as the reference's 1) */
     R97B_ELAUNCH = 2,  /* a launch failed */
     R97B_EDEVICE = 3,  /* a device-side check fired (see r97b_device_error) */
+    R97B_ETOOLARGE = 4, /* the input exceeds the fixed capacity of an allocation-free entry point */
 };
 
 /* ------------------------------------------------------------------------------ library */
@@ -149,6 +150,23 @@ int64_t r97b_global_norm_scratch_bytes(int64_t n);
  * out_scale may be null). `partials` is caller scratch of r97b_global_norm_scratch_bytes(n). */
 int r97b_global_norm(const float* g, int64_t n, float inv_k, float max_norm, double* partials, float* out_norm,
                      float* out_scale, void* stream);
+
+/* The largest n r97b_global_norm_noalloc accepts: 65536 partials of 4096 elements. */
+#define R97B_GLOBAL_NORM_NOALLOC_MAX_ELEMS (65536LL * 4096LL)
+
+/* r97b_global_norm for callers that cannot allocate device memory -- a host framework whose allocator
+ * already owns the device's memory, or a loop that cannot afford cudaMalloc / cudaFree (cudaFree
+ * synchronises the whole device). It takes no scratch argument and allocates nothing: its f64 partials
+ * live in a fixed 512 KiB array inside the library, reserved on every GPU that loads the library until the
+ * process exits. Same results as r97b_global_norm (the same kernels, bit for bit).
+ *  - n > R97B_GLOBAL_NORM_NOALLOC_MAX_ELEMS (268,435,456) returns R97B_ETOOLARGE and launches nothing.
+ *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that
+ *    device current; make that first call before any stream capture.
+ *  - All calls share the one array, which keeps the last call's partials; calls whose kernels overlap on
+ *    the GPU (two streams, two host threads) race on it, so serialise them.
+ * No counterpart in the reference: its optimiser runs on the host. */
+int r97b_global_norm_noalloc(const float* g, int64_t n, float inv_k, float max_norm, float* out_norm,
+                             float* out_scale, void* stream);
 
 /* ------------------------------------------------------------------------------ GatedDeltaNet */
 

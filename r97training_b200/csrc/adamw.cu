@@ -17,6 +17,8 @@
 
 #include <math.h>
 
+#include <mutex>
+
 namespace r97b {
 namespace {
 
@@ -69,10 +71,58 @@ __global__ void norm_finish_kernel(const double* __restrict__ partials, int64_t 
     if (out_scale) *out_scale = (max_norm > 0.0f && norm > max_norm && norm > 0.0f) ? __fdiv_rn(max_norm, norm) : 1.0f;
 }
 
+// ---- the allocation-free global norm: its partials live in this file's own device array ----------------
+//
+// Some callers of this library cannot allocate device memory: a host framework whose allocator already
+// owns the whole device budget, or a loop that must not pay cudaMalloc / cudaFree (cudaFree synchronises
+// the device). r97b_global_norm_noalloc serves them with the scratch below, reserved when the library is
+// loaded: every GPU that loads the library holds these 512 KiB until the process exits.
+constexpr int64_t kNoAllocMaxChunks = R97B_GLOBAL_NORM_NOALLOC_MAX_ELEMS / kNormChunk;
+static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxChunks];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+double* g_noalloc_ptr[kMaxDevices] = {};
+
+// The array's device address on the current device, looked up once per device. Host code must not pass
+// `g_noalloc_partials` itself to a kernel: on the host that name is a stand-in, not a device address.
+int noalloc_partials(double** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return R97B_ELAUNCH;
+    if (dev < 0 || dev >= kMaxDevices) return R97B_EINVAL;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_partials);
+        if (e != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            return R97B_ELAUNCH;
+        }
+        g_noalloc_ptr[dev] = static_cast<double*>(p);
+    }
+    *out = g_noalloc_ptr[dev];
+    return R97B_OK;
+}
+
 }  // namespace
 }  // namespace r97b
 
 using namespace r97b;
+
+// See include/r97b.h. The same two kernels as r97b_global_norm, over the file's own partials array.
+extern "C" int r97b_global_norm_noalloc(const float* g, int64_t n, float inv_k, float max_norm, float* out_norm,
+                                        float* out_scale, void* stream) {
+    if (!g || n <= 0) return R97B_EINVAL;
+    if (n > R97B_GLOBAL_NORM_NOALLOC_MAX_ELEMS) return R97B_ETOOLARGE;
+    double* partials = nullptr;
+    const int rc = noalloc_partials(&partials);
+    if (rc != R97B_OK) return rc;
+    const int64_t nchunks = (n + kNormChunk - 1) / kNormChunk;
+    chunk_sumsq_kernel<<<(unsigned)((nchunks + 255) / 256), 256, 0, as_stream(stream)>>>(g, n, inv_k, partials,
+                                                                                          nchunks);
+    norm_finish_kernel<<<1, 32, 0, as_stream(stream)>>>(partials, nchunks, max_norm, out_norm, out_scale);
+    return launch_status(2);
+}
 
 // One AdamW update of `n` f32 parameters. `g` holds the accumulated gradient; it is scaled by `inv_k`
 // (1 / accumulation count) and, when `clip_scale` (a device f32) is given, by that factor, exactly as
