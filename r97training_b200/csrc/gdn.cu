@@ -1,4 +1,4 @@
-// gdn.cu -- the chunked GatedDeltaNet recurrence, forward and backward, on sm_100a.
+// gdn.cu -- the chunked GatedDeltaNet recurrence, forward and backward, on sm_100a tensor cores.
 //
 // It computes the reference's two ops as one path (reference src/adjoint/host/gdn_kkt.cpp and
 // gdn_scan.cpp; docs/adjoints/gdn-math.md s2.2, s3, s4):
@@ -6,7 +6,7 @@
 //   gdn_chunk_scan: W = beta (v - e^g k S), V' = A W, o = scale (e^g q S + causal(q k^T e^{g_i-g_j}) V'),
 //                   S_next = e^{g_L} S + sum_j e^{g_L - g_j} k_j (x) V'_j
 // with the state held as S[d][e] (key lane d, value lane e; the reference's transposed St) in f32 and
-// g the within-chunk cumulative log decay. Rewriting V' = u - w S with u = A diag(beta) v and
+// g the within-chunk cumulative log decay. Writing V' = u - w S with u = A diag(beta) v and
 // w = A diag(beta e^g) k moves every intra-chunk product into chunk-parallel kernels and leaves a short
 // sequential pass whose value lanes are independent:
 //
@@ -20,10 +20,16 @@
 //   B2b gdn_bwd_b    (chunk, head)        the intra-chunk terms: dP, dA = dw kb^T + dV' vb^T, A^T dw, A^T dV',
 //                                          and the solve's adjoint dM = -A^T dA A^T (the kkt adjoint)
 //
+// Every product runs on the tensor cores (wmma16.cuh: mma.sync m16n8k16, bf16 in, f32 accumulate).
+// q, k, v and dO are bf16 already and enter exactly; an f32 operand (a state, A, P, V', w, dV', ...) is
+// split into bf16 hi + lo tiles and its product takes two or three passes, which keeps ~16 bits of the
+// operand. The sequential passes keep their state in the f32 MMA accumulators. Only the 64-step forward
+// substitution of the solve runs on CUDA cores.
+//
 // Sequences are ragged (cu_seqlens); a sequence's last chunk may be short, and its padded rows are zero
 // so they add nothing. Head dims K = V = 128 and the chunk of 64 are fixed here.
-#include "blockmm.cuh"
 #include "r97b_internal.h"
+#include "wmma16.cuh"
 
 #include <cuda_bf16.h>
 #include <math.h>
@@ -31,12 +37,13 @@
 namespace r97b {
 namespace {
 
-constexpr int D = 128;       // key / value head dim
-constexpr int L = 64;        // chunk
-constexpr int P129 = D + 1;  // f32 pitch of a [*, 128] tile
-constexpr int P65 = L + 1;   // f32 pitch of a [64, 64] tile
-constexpr int P33 = 33;      // f32 pitch of a [*, 32] value slice
-constexpr int VS = 32;       // value lanes per sequential CTA
+using bf16 = __nv_bfloat16;
+
+constexpr int D = 128;   // key / value head dim
+constexpr int L = 64;    // chunk
+constexpr int VS = 32;   // value lanes per sequential CTA
+constexpr int P32 = 40;  // bf16 pitch of a [*, 32] tile
+constexpr int F65 = 65;  // f32 pitch of a [64, 64] tile
 
 struct Dims {
     int n_seq, H, Hg, grp, n_chunks;
@@ -46,32 +53,52 @@ struct Dims {
     const int* seq_c0;
 };
 
-__device__ __forceinline__ float bf(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+// ------------------------------------------------------------------------------------------ staging
 
-// rows [0, 64) x 128 of a token-major bf16 tensor [T, heads, 128] for one head; zero past `n` rows
-__device__ __forceinline__ void load_rows_bf16(float* dst, const __nv_bfloat16* src, int64_t tok0, int n, int heads,
-                                               int head, float scale = 1.0f) {
-    for (int idx = threadIdx.x; idx < L * D; idx += blockDim.x) {
-        const int i = idx >> 7, d = idx & 127;
-        dst[i * P129 + d] = i < n ? scale * bf(src + ((tok0 + i) * heads + head) * D + d) : 0.0f;
+// rows [0, 64) of one head of a token-major bf16 tensor [T, heads, 128] -> bf16 tile (pitch kP128);
+// rows >= n are zero
+__device__ __forceinline__ void stage_bf16(bf16* dst, const bf16* src, int64_t tok0, int n, int heads, int head) {
+    for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
+        const int i = idx >> 4, c = (idx & 15) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (i < n) v = *reinterpret_cast<const uint4*>(src + ((tok0 + i) * heads + head) * D + c);
+        *reinterpret_cast<uint4*>(dst + i * kP128 + c) = v;
     }
 }
 
-__device__ __forceinline__ void load_rows_f32(float* dst, const float* src, int64_t tok0, int n, int heads, int head,
-                                              float scale = 1.0f) {
-    for (int idx = threadIdx.x; idx < L * D; idx += blockDim.x) {
-        const int i = idx >> 7, d = idx & 127;
-        dst[i * P129 + d] = i < n ? scale * src[((tok0 + i) * heads + head) * D + d] : 0.0f;
+__device__ __forceinline__ void put_split(bf16* hi, bf16* lo, int at, float x) {
+    bf16 h, l;
+    split_bf16(x, h, l);
+    hi[at] = h;
+    lo[at] = l;
+}
+
+// f32 rows [0, 64) x 128 of [T, heads, 128] -> hi/lo tiles (pitch kP128), each row scaled by rs[i]
+// (null = 1); rows >= n zero
+__device__ __forceinline__ void stage_f32_split(bf16* hi, bf16* lo, const float* src, int64_t tok0, int n, int heads,
+                                                int head, const float* rs = nullptr) {
+    for (int idx = threadIdx.x; idx < L * 32; idx += blockDim.x) {
+        const int i = idx >> 5, c = (idx & 31) * 4;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < n) v = *reinterpret_cast<const float4*>(src + ((tok0 + i) * heads + head) * D + c);
+        const float s = rs ? rs[i] : 1.0f;
+        put_split(hi, lo, i * kP128 + c, v.x * s);
+        put_split(hi, lo, i * kP128 + c + 1, v.y * s);
+        put_split(hi, lo, i * kP128 + c + 2, v.z * s);
+        put_split(hi, lo, i * kP128 + c + 3, v.w * s);
     }
 }
 
-// the value slice [e0, e0 + 32) of rows [0, 64) of a [T, H, 128] tensor
-template <typename T>
-__device__ __forceinline__ void load_slice(float* dst, const T* src, int64_t tok0, int n, int H, int h, int e0,
-                                           float scale = 1.0f) {
-    for (int idx = threadIdx.x; idx < L * VS; idx += blockDim.x) {
-        const int i = idx >> 5, e = idx & 31;
-        dst[i * P33 + e] = i < n ? scale * ld_f32(src + ((tok0 + i) * H + h) * D + e0 + e) : 0.0f;
+// a dense f32 [rows][cols] matrix -> hi/lo tiles of pitch p
+template <int ROWS, int COLS>
+__device__ __forceinline__ void stage_mat_split(bf16* hi, bf16* lo, int p, const float* src) {
+    for (int idx = threadIdx.x; idx < ROWS * COLS / 4; idx += blockDim.x) {
+        const int e = idx * 4, r = e / COLS, c = e % COLS;
+        const float4 v = *reinterpret_cast<const float4*>(src + e);
+        put_split(hi, lo, r * p + c, v.x);
+        put_split(hi, lo, r * p + c + 1, v.y);
+        put_split(hi, lo, r * p + c + 2, v.z);
+        put_split(hi, lo, r * p + c + 3, v.w);
     }
 }
 
@@ -83,476 +110,476 @@ __device__ __forceinline__ void load_gb(float* gs, float* bs, const float* g, co
     }
 }
 
-// sum over the 16 threads of one row group (lanes sharing ty: a half warp)
-__device__ __forceinline__ float row16_sum(float v) {
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+// sum over the 4 lanes of an accumulator row quad (lanes sharing g = lane / 4)
+__device__ __forceinline__ float quad_sum(float v) {
+    v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
+    v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
     return v;
+}
+
+// two- / three-pass products of split operands
+template <int WM, int WN, int K, bool AT, bool BT>
+__device__ __forceinline__ void mma_split_a(float (&acc)[WM / 16][WN / 8][4], const bf16* Ah, const bf16* Al, int pa,
+                                            const bf16* B, int pb, int m0, int n0) {
+    warp_mma<WM, WN, K, AT, BT>(acc, Ah, pa, B, pb, m0, n0);
+    warp_mma<WM, WN, K, AT, BT>(acc, Al, pa, B, pb, m0, n0);
+}
+template <int WM, int WN, int K, bool AT, bool BT>
+__device__ __forceinline__ void mma_split_b(float (&acc)[WM / 16][WN / 8][4], const bf16* A, int pa, const bf16* Bh,
+                                            const bf16* Bl, int pb, int m0, int n0) {
+    warp_mma<WM, WN, K, AT, BT>(acc, A, pa, Bh, pb, m0, n0);
+    warp_mma<WM, WN, K, AT, BT>(acc, A, pa, Bl, pb, m0, n0);
+}
+template <int WM, int WN, int K, bool AT, bool BT>
+__device__ __forceinline__ void mma_split_ab(float (&acc)[WM / 16][WN / 8][4], const bf16* Ah, const bf16* Al, int pa,
+                                             const bf16* Bh, const bf16* Bl, int pb, int m0, int n0) {
+    warp_mma<WM, WN, K, AT, BT>(acc, Ah, pa, Bh, pb, m0, n0);
+    warp_mma<WM, WN, K, AT, BT>(acc, Al, pa, Bh, pb, m0, n0);
+    warp_mma<WM, WN, K, AT, BT>(acc, Ah, pa, Bl, pb, m0, n0);
 }
 
 // ============================================================================================ forward
 
-// F1: per (chunk, value head): A = (I + M)^-1, w = A diag(beta e^g) k, u = A diag(beta) v.
-__global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const __nv_bfloat16* __restrict__ q_unused,
-                                                    const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+// F1: per (chunk, value head): A = (I + M)^-1, w = (A diag(beta e^g)) k, u = (A diag(beta)) v.
+__global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restrict__ k, const bf16* __restrict__ v,
                                                     const float* __restrict__ g, const float* __restrict__ beta,
                                                     float* __restrict__ A, float* __restrict__ w, float* __restrict__ u) {
-    extern __shared__ float sm[];
-    float* ks = sm;                  // [64][129]
-    float* vs = ks + L * P129;       // [64][129]
-    float* Ms = vs + L * P129;       // [64][65]
-    float* As = Ms + L * P65;        // [64][65]
-    float* red = As + L * P65;       // [4][64]
-    float* gs = red + 4 * L;         // [64]
-    float* bs = gs + L;              // [64]
+    extern __shared__ __align__(16) unsigned char smraw[];
+    bf16* ks = reinterpret_cast<bf16*>(smraw);          // [64][136]
+    bf16* vs = ks + L * kP128;                           // [64][136]
+    bf16* a1h = vs + L * kP128;                          // [64][72]  A diag(beta e^g), hi/lo
+    bf16* a1l = a1h + L * kP64;
+    bf16* a2h = a1l + L * kP64;                          // A diag(beta), hi/lo
+    bf16* a2l = a2h + L * kP64;
+    float* Ms = reinterpret_cast<float*>(a2l + L * kP64);  // [64][65]
+    float* As = Ms + L * F65;                              // [64][65]
+    float* red = As + L * F65;                             // [4][64]
+    float* gs = red + 4 * L;
+    float* bs = gs + L;
     const int c = blockIdx.x, h = blockIdx.y, hk = h / dm.grp;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
-    load_rows_bf16(ks, k, tok0, n, dm.Hg, hk);
-    load_rows_bf16(vs, v, tok0, n, dm.H, h);
+    const int warp = threadIdx.x >> 5;
+    stage_bf16(ks, k, tok0, n, dm.Hg, hk);
+    stage_bf16(vs, v, tok0, n, dm.H, h);
     load_gb(gs, bs, g, beta, tok0, n, dm.H, h);
     __syncthreads();
     {
-        float acc[4][4];
-        zero_acc<64, 64>(acc);
-        bmm<64, 64, 128, false, true>(acc, ks, P129, ks, P129);
-        const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int r = ty + 16 * i, l = tx + 16 * j;
-                Ms[r * P65 + l] = l < r ? bs[r] * acc[i][j] * expf(gs[r] - gs[l]) : 0.0f;
-            }
+        // M = strict lower of beta_i (k_i . k_l) e^{g_i - g_l}
+        float acc[1][4][4];
+        acc_zero<16, 32>(acc);
+        const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
+        warp_mma<16, 32, 128, false, false>(acc, ks, kP128, ks, kP128, m0, n0);
+        acc_for<16, 32>(acc, m0, n0, [&](int r, int l, float& x) {
+            Ms[r * F65 + l] = l < r ? bs[r] * x * expf(gs[r] - gs[l]) : 0.0f;
+        });
     }
     __syncthreads();
-    // forward substitution, one row at a time: A[i][j] = delta_ij - sum_{l<i} M[i][l] A[l][j]
     {
+        // forward substitution, one row at a time: A[i][j] = delta_ij - sum_{l<i} M[i][l] A[l][j]
         const int j = threadIdx.x & 63, part = threadIdx.x >> 6;
         for (int i = 0; i < L; ++i) {
             float s = 0.0f;
             const int l0 = part * 16;
 #pragma unroll
             for (int l = l0; l < l0 + 16; ++l)
-                if (l < i) s = fmaf(Ms[i * P65 + l], As[l * P65 + j], s);
+                if (l < i) s = fmaf(Ms[i * F65 + l], As[l * F65 + j], s);
             red[part * L + j] = s;
             __syncthreads();
             if (part == 0) {
                 const float t = red[j] + red[L + j] + red[2 * L + j] + red[3 * L + j];
-                As[i * P65 + j] = j < i ? -t : (j == i ? 1.0f : 0.0f);
+                As[i * F65 + j] = j < i ? -t : (j == i ? 1.0f : 0.0f);
             }
             __syncthreads();
         }
     }
     for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
         const int i = idx >> 6, j = idx & 63;
-        if (i < n) A[((tok0 + i) * dm.H + h) * L + j] = As[i * P65 + j];
-    }
-    // kb = diag(beta e^g) k, vb = diag(beta) v, in place
-    for (int idx = threadIdx.x; idx < L * D; idx += blockDim.x) {
-        const int i = idx >> 7, d = idx & 127;
-        ks[i * P129 + d] *= bs[i] * expf(gs[i]);
-        vs[i * P129 + d] *= bs[i];
+        const float a = As[i * F65 + j];
+        if (i < n) A[((tok0 + i) * dm.H + h) * L + j] = a;
+        const float e = bs[j] * expf(gs[j]);
+        put_split(a1h, a1l, i * kP64 + j, a * e);
+        put_split(a2h, a2l, i * kP64 + j, a * bs[j]);
     }
     __syncthreads();
-    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-    float acc[4][8];
-    zero_acc<64, 128>(acc);
-    bmm<64, 128, 64, false, false>(acc, As, P65, ks, P129);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int r = ty + 16 * i;
-            if (r < n) w[((tok0 + r) * dm.H + h) * D + tx + 16 * j] = acc[i][j];
-        }
-    zero_acc<64, 128>(acc);
-    bmm<64, 128, 64, false, false>(acc, As, P65, vs, P129);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int r = ty + 16 * i;
-            if (r < n) u[((tok0 + r) * dm.H + h) * D + tx + 16 * j] = acc[i][j];
-        }
+    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
+    float acc[1][8][4];
+    acc_zero<16, 64>(acc);
+    mma_split_a<16, 64, 64, false, true>(acc, a1h, a1l, kP64, ks, kP128, m0, n0);
+    acc_for<16, 64>(acc, m0, n0, [&](int r, int d, float& x) {
+        if (r < n) w[((tok0 + r) * dm.H + h) * D + d] = x;
+    });
+    acc_zero<16, 64>(acc);
+    mma_split_a<16, 64, 64, false, true>(acc, a2h, a2l, kP64, vs, kP128, m0, n0);
+    acc_for<16, 64>(acc, m0, n0, [&](int r, int d, float& x) {
+        if (r < n) u[((tok0 + r) * dm.H + h) * D + d] = x;
+    });
 }
 
 // F2: per (sequence, value head, 32 value lanes): the state pass over the sequence's chunks.
-__global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const __nv_bfloat16* __restrict__ k,
-                                                     const float* __restrict__ g, const float* __restrict__ w,
-                                                     const float* __restrict__ u, const float* __restrict__ h0,
-                                                     float* __restrict__ S_all, float* __restrict__ Vp,
-                                                     float* __restrict__ ht) {
-    extern __shared__ float sm[];
-    float* Ss = sm;                  // [128][33]
-    float* ws = Ss + D * P33;        // [64][129]
-    float* ks = ws + L * P129;       // [64][129]
-    float* us = ks + L * P129;       // [64][33]
-    float* gs = us + L * P33;        // [64]
+// The state slice S[128][32] lives in the f32 accumulators of its own product (S += k^T V'').
+__global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __restrict__ k, const float* __restrict__ g,
+                                                     const float* __restrict__ w, const float* __restrict__ u,
+                                                     const float* __restrict__ h0, float* __restrict__ S_all,
+                                                     float* __restrict__ Vp, float* __restrict__ ht) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    bf16* sh = reinterpret_cast<bf16*>(smraw);   // S hi/lo [128][40]
+    bf16* sl = sh + D * P32;
+    bf16* wh = sl + D * P32;                     // w hi/lo [64][136]
+    bf16* wl = wh + L * kP128;
+    bf16* ks = wl + L * kP128;                   // k [64][136]
+    bf16* vh = ks + L * kP128;                   // V'' = e^{gL-g} V' hi/lo [64][40]
+    bf16* vl = vh + L * P32;
+    float* us = reinterpret_cast<float*>(vl + L * P32);  // u slice [64][33]
+    float* gs = us + L * 33;
     const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VS, hk = h / dm.grp;
-    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-    for (int idx = threadIdx.x; idx < D * VS; idx += blockDim.x) {
-        const int d = idx >> 5, e = idx & 31;
-        Ss[d * P33 + e] = h0 ? h0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
-    }
+    const int warp = threadIdx.x >> 5;
+    const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 16;  // this warp's S tile
+    const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 16;  // this warp's V' tile
+    float S[2][2][4];
+    acc_for<32, 16>(S, sm0, sn0, [&](int d, int e, float& x) {
+        x = h0 ? h0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
+    });
     const int c0 = dm.seq_c0[seq], c1 = dm.seq_c0[seq + 1];
     for (int c = c0; c < c1; ++c) {
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
-        __syncthreads();
         float* Sg = S_all + ((int64_t)c * dm.H + h) * D * D;
-        for (int idx = threadIdx.x; idx < D * VS; idx += blockDim.x) {
-            const int d = idx >> 5, e = idx & 31;
-            Sg[d * D + e0 + e] = Ss[d * P33 + e];
+        acc_for<32, 16>(S, sm0, sn0, [&](int d, int e, float& x) {
+            Sg[d * D + e0 + e] = x;
+            put_split(sh, sl, d * P32 + e, x);
+        });
+        stage_f32_split(wh, wl, w, tok0, n, dm.H, h);
+        stage_bf16(ks, k, tok0, n, dm.Hg, hk);
+        for (int idx = threadIdx.x; idx < L * VS; idx += blockDim.x) {
+            const int i = idx >> 5, e = idx & 31;
+            us[i * 33 + e] = i < n ? u[((tok0 + i) * dm.H + h) * D + e0 + e] : 0.0f;
         }
-        load_rows_f32(ws, w, tok0, n, dm.H, h);
-        load_rows_bf16(ks, k, tok0, n, dm.Hg, hk);
-        load_slice(us, u, tok0, n, dm.H, h, e0);
         load_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
         __syncthreads();
-        {
-            float acc[4][2];
-            zero_acc<64, 32>(acc);
-            bmm<64, 32, 128, false, false>(acc, ws, P129, Ss, P33);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int r = ty + 16 * i, e = tx + 16 * j;
-                    const float vp = us[r * P33 + e] - acc[i][j];
-                    us[r * P33 + e] = vp;
-                    if (r < n) Vp[((tok0 + r) * dm.H + h) * D + e0 + e] = vp;
-                }
-        }
         const float gl = gs[n - 1];
-        for (int idx = threadIdx.x; idx < L * D; idx += blockDim.x) {
-            const int i = idx >> 7, d = idx & 127;
-            ks[i * P129 + d] *= i < n ? expf(gl - gs[i]) : 0.0f;
+        {
+            float acc[1][2][4];
+            acc_zero<16, 16>(acc);
+            mma_split_ab<16, 16, 128, false, true>(acc, wh, wl, kP128, sh, sl, P32, vm0, vn0);
+            acc_for<16, 16>(acc, vm0, vn0, [&](int i, int e, float& x) {
+                const float vp = us[i * 33 + e] - x;
+                if (i < n) Vp[((tok0 + i) * dm.H + h) * D + e0 + e] = vp;
+                put_split(vh, vl, i * P32 + e, i < n ? vp * expf(gl - gs[i]) : 0.0f);
+            });
         }
         __syncthreads();
-        {
-            float acc[8][2];
-            zero_acc<128, 32>(acc);
-            bmm<128, 32, 64, true, false>(acc, ks, P129, us, P33);
-            const float el = expf(gl);
+        const float el = expf(gl);
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
+        for (int a = 0; a < 2; ++a)
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int d = ty + 16 * i, e = tx + 16 * j;
-                    Ss[d * P33 + e] = el * Ss[d * P33 + e] + acc[i][j];
-                }
-        }
+            for (int b = 0; b < 2; ++b)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) S[a][b][e] *= el;
+        mma_split_b<32, 16, 64, true, true>(S, ks, kP128, vh, vl, P32, sm0, sn0);
+        __syncthreads();
     }
-    __syncthreads();
     if (ht)
-        for (int idx = threadIdx.x; idx < D * VS; idx += blockDim.x) {
-            const int d = idx >> 5, e = idx & 31;
-            ht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] = Ss[d * P33 + e];
-        }
+        acc_for<32, 16>(S, sm0, sn0, [&](int d, int e, float& x) {
+            ht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] = x;
+        });
 }
 
 // F3: per (chunk, value head): P and the output rows.
-__global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const __nv_bfloat16* __restrict__ q,
-                                                   const __nv_bfloat16* __restrict__ k, const float* __restrict__ g,
-                                                   const float* __restrict__ S_all, const float* __restrict__ Vp,
-                                                   float* __restrict__ P_all, __nv_bfloat16* __restrict__ o) {
-    extern __shared__ float sm[];
-    float* qs = sm;                  // [64][129]
-    float* ks = qs + L * P129;       // [64][129]  k, then V'
-    float* Ps = ks + L * P129;       // [64][65]
-    float* Ss = Ps + L * P65;        // [128][129]
-    float* gs = Ss + D * P129;       // [64]
+__global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                   const float* __restrict__ g, const float* __restrict__ S_all,
+                                                   const float* __restrict__ Vp, float* __restrict__ P_all,
+                                                   bf16* __restrict__ o) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    bf16* qs = reinterpret_cast<bf16*>(smraw);   // [64][136]
+    bf16* ks = qs + L * kP128;                   // [64][136]
+    bf16* vh = ks + L * kP128;                   // V' hi/lo [64][136]
+    bf16* vl = vh + L * kP128;
+    bf16* sh = vl + L * kP128;                   // S hi/lo [128][136]
+    bf16* sl = sh + D * kP128;
+    bf16* ph = sl + D * kP128;                   // P hi/lo [64][72]
+    bf16* pl = ph + L * kP64;
+    float* gs = reinterpret_cast<float*>(pl + L * kP64);
     const int c = blockIdx.x, h = blockIdx.y, hk = h / dm.grp;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
-    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-    load_rows_bf16(qs, q, tok0, n, dm.Hg, hk);
-    load_rows_bf16(ks, k, tok0, n, dm.Hg, hk);
+    const int warp = threadIdx.x >> 5;
+    stage_bf16(qs, q, tok0, n, dm.Hg, hk);
+    stage_bf16(ks, k, tok0, n, dm.Hg, hk);
+    stage_f32_split(vh, vl, Vp, tok0, n, dm.H, h);
+    stage_mat_split<D, D>(sh, sl, kP128, S_all + ((int64_t)c * dm.H + h) * D * D);
     load_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
-    const float* Sg = S_all + ((int64_t)c * dm.H + h) * D * D;
-    for (int idx = threadIdx.x; idx < D * D; idx += blockDim.x) Ss[(idx >> 7) * P129 + (idx & 127)] = Sg[idx];
     __syncthreads();
     {
-        float acc[4][4];
-        zero_acc<64, 64>(acc);
-        bmm<64, 64, 128, false, true>(acc, qs, P129, ks, P129);
+        float acc[1][4][4];
+        acc_zero<16, 32>(acc);
+        const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
+        warp_mma<16, 32, 128, false, false>(acc, qs, kP128, ks, kP128, m0, n0);
         float* Pg = P_all + ((int64_t)c * dm.H + h) * L * L;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int r = ty + 16 * i, l = tx + 16 * j;
-                const float p = (l <= r && r < n) ? acc[i][j] * expf(gs[r] - gs[l]) : 0.0f;
-                Ps[r * P65 + l] = p;
-                Pg[r * L + l] = p;
-            }
+        acc_for<16, 32>(acc, m0, n0, [&](int r, int l, float& x) {
+            const float p = (l <= r && r < n) ? x * expf(gs[r] - gs[l]) : 0.0f;
+            Pg[r * L + l] = p;
+            put_split(ph, pl, r * kP64 + l, p);
+        });
     }
     __syncthreads();
-    load_rows_f32(ks, Vp, tok0, n, dm.H, h);
-    for (int idx = threadIdx.x; idx < L * D; idx += blockDim.x) {
-        const int i = idx >> 7, d = idx & 127;
-        qs[i * P129 + d] *= expf(gs[i]);
-    }
-    __syncthreads();
-    float acc[4][8];
-    zero_acc<64, 128>(acc);
-    bmm<64, 128, 128, false, false>(acc, qs, P129, Ss, P129);
-    bmm<64, 128, 64, false, false>(acc, Ps, P65, ks, P129);
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int r = ty + 16 * i;
-            if (r < n) o[((tok0 + r) * dm.H + h) * D + tx + 16 * j] = __float2bfloat16_rn(dm.scale * acc[i][j]);
-        }
+    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
+    float qsacc[1][8][4], pvacc[1][8][4];
+    acc_zero<16, 64>(qsacc);
+    acc_zero<16, 64>(pvacc);
+    mma_split_b<16, 64, 128, false, true>(qsacc, qs, kP128, sh, sl, kP128, m0, n0);
+    mma_split_ab<16, 64, 64, false, true>(pvacc, ph, pl, kP64, vh, vl, kP128, m0, n0);
+    const int lane = threadIdx.x & 31, gq = lane >> 2;
+    const float eg0 = expf(gs[m0 + gq]), eg1 = expf(gs[m0 + gq + 8]);
+    acc_walk<16, 64>(m0, n0, [&](int r, int e, int i, int j, int q) {
+        const float y = dm.scale * (qsacc[i][j][q] * ((q >> 1) ? eg1 : eg0) + pvacc[i][j][q]);
+        if (r < n) o[((tok0 + r) * dm.H + h) * D + e] = __float2bfloat16_rn(y);
+    });
 }
 
 // ============================================================================================ backward
 
-// B1: per (sequence, value head, 32 value lanes): the reverse state pass.
-__global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const __nv_bfloat16* __restrict__ q,
-                                                     const __nv_bfloat16* __restrict__ k, const float* __restrict__ g,
-                                                     const float* __restrict__ w, const float* __restrict__ P_all,
-                                                     const __nv_bfloat16* __restrict__ dO, const float* __restrict__ dht,
-                                                     float* __restrict__ dS_all, float* __restrict__ dVp,
-                                                     float* __restrict__ dh0) {
-    extern __shared__ float sm[];
-    float* dSs = sm;                 // [128][33]
-    float* Ps = dSs + D * P33;       // [64][65]
-    float* Kt = Ps + L * P65;        // [64][129]
-    float* Qt = Kt + L * P129;       // [64][129]
-    float* ws = Qt + L * P129;       // [64][129]
-    float* dOs = ws + L * P129;      // [64][33]
-    float* dVs = dOs + L * P33;      // [64][33]
-    float* gs = dVs + L * P33;       // [64]
+// B1: per (sequence, value head, 32 value lanes): the reverse state pass; dS lives in the accumulators.
+__global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                     const float* __restrict__ g, const float* __restrict__ w,
+                                                     const float* __restrict__ P_all, const bf16* __restrict__ dO,
+                                                     const float* __restrict__ dht, float* __restrict__ dS_all,
+                                                     float* __restrict__ dVp, float* __restrict__ dh0) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    bf16* dsh = reinterpret_cast<bf16*>(smraw);  // dS hi/lo [128][40]
+    bf16* dsl = dsh + D * P32;
+    bf16* ph = dsl + D * P32;                    // P hi/lo [64][72]
+    bf16* pl = ph + L * kP64;
+    bf16* ks = pl + L * kP64;                    // k [64][136]
+    bf16* qs = ks + L * kP128;                   // q [64][136]
+    bf16* wh = qs + L * kP128;                   // w hi/lo [64][136]
+    bf16* wl = wh + L * kP128;
+    bf16* dos = wl + L * kP128;                  // dO slice [64][40] (bf16, exact)
+    bf16* egh = dos + L * P32;                   // e^g dO hi/lo [64][40]
+    bf16* egl = egh + L * P32;
+    bf16* dvh = egl + L * P32;                   // dV' hi/lo [64][40]
+    bf16* dvl = dvh + L * P32;
+    float* gs = reinterpret_cast<float*>(dvl + L * P32);
     const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VS, hk = h / dm.grp;
-    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-    for (int idx = threadIdx.x; idx < D * VS; idx += blockDim.x) {
-        const int d = idx >> 5, e = idx & 31;
-        dSs[d * P33 + e] = dht ? dht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
-    }
+    const int warp = threadIdx.x >> 5;
+    const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 16;
+    const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 16;
+    float dS[2][2][4];
+    acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
+        x = dht ? dht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
+    });
     const int c0 = dm.seq_c0[seq], c1 = dm.seq_c0[seq + 1];
     for (int c = c1 - 1; c >= c0; --c) {
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
-        __syncthreads();
         float* dSg = dS_all + ((int64_t)c * dm.H + h) * D * D;
-        for (int idx = threadIdx.x; idx < D * VS; idx += blockDim.x) {
-            const int d = idx >> 5, e = idx & 31;
-            dSg[d * D + e0 + e] = dSs[d * P33 + e];
-        }
+        acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
+            dSg[d * D + e0 + e] = x;
+            put_split(dsh, dsl, d * P32 + e, x);
+        });
         load_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
-        const float* Pg = P_all + ((int64_t)c * dm.H + h) * L * L;
-        for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) Ps[(idx >> 6) * P65 + (idx & 63)] = Pg[idx];
-        load_rows_bf16(Kt, k, tok0, n, dm.Hg, hk);
-        load_rows_bf16(Qt, q, tok0, n, dm.Hg, hk);
-        load_rows_f32(ws, w, tok0, n, dm.H, h);
-        load_slice(dOs, dO, tok0, n, dm.H, h, e0, dm.scale);
+        stage_mat_split<L, L>(ph, pl, kP64, P_all + ((int64_t)c * dm.H + h) * L * L);
+        stage_bf16(ks, k, tok0, n, dm.Hg, hk);
+        stage_bf16(qs, q, tok0, n, dm.Hg, hk);
+        stage_f32_split(wh, wl, w, tok0, n, dm.H, h);
+        __syncthreads();
+        for (int idx = threadIdx.x; idx < L * VS; idx += blockDim.x) {
+            const int i = idx >> 5, e = idx & 31;
+            const bf16 x = i < n ? dO[((tok0 + i) * dm.H + h) * D + e0 + e] : __float2bfloat16_rn(0.0f);
+            dos[i * P32 + e] = x;
+            put_split(egh, egl, i * P32 + e, __bfloat162float(x) * expf(gs[i]));
+        }
         __syncthreads();
         const float gl = gs[n - 1];
-        for (int idx = threadIdx.x; idx < L * D; idx += blockDim.x) {
-            const int i = idx >> 7, d = idx & 127;
-            Kt[i * P129 + d] *= i < n ? expf(gl - gs[i]) : 0.0f;
-            Qt[i * P129 + d] *= expf(gs[i]);
+        {
+            // dV' = scale P^T dO + e^{gL - g} (k dS)
+            float a1[1][2][4], a2[1][2][4];
+            acc_zero<16, 16>(a1);
+            acc_zero<16, 16>(a2);
+            mma_split_a<16, 16, 64, true, true>(a1, ph, pl, kP64, dos, P32, vm0, vn0);
+            mma_split_b<16, 16, 128, false, true>(a2, ks, kP128, dsh, dsl, P32, vm0, vn0);
+            acc_walk<16, 16>(vm0, vn0, [&](int j, int e, int a, int b, int q) {
+                const float dv = j < n ? dm.scale * a1[a][b][q] + expf(gl - gs[j]) * a2[a][b][q] : 0.0f;
+                if (j < n) dVp[((tok0 + j) * dm.H + h) * D + e0 + e] = dv;
+                put_split(dvh, dvl, j * P32 + e, dv);
+            });
         }
         __syncthreads();
-        {
-            float acc[4][2];
-            zero_acc<64, 32>(acc);
-            bmm<64, 32, 64, true, false>(acc, Ps, P65, dOs, P33);
-            bmm<64, 32, 128, false, false>(acc, Kt, P129, dSs, P33);
+        // dS = e^{gL} dS + scale q^T (e^g dO) - w^T dV'
+        const float el = expf(gl);
+        float t1[2][2][4], t2[2][2][4];
+        acc_zero<32, 16>(t1);
+        acc_zero<32, 16>(t2);
+        mma_split_b<32, 16, 64, true, true>(t1, qs, kP128, egh, egl, P32, sm0, sn0);
+        mma_split_ab<32, 16, 64, true, true>(t2, wh, wl, kP128, dvh, dvl, P32, sm0, sn0);
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
+        for (int a = 0; a < 2; ++a)
 #pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int r = ty + 16 * i, e = tx + 16 * j;
-                    const float dv = r < n ? acc[i][j] : 0.0f;
-                    dVs[r * P33 + e] = dv;
-                    if (r < n) dVp[((tok0 + r) * dm.H + h) * D + e0 + e] = dv;
-                }
-        }
+            for (int b = 0; b < 2; ++b)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) dS[a][b][e] = el * dS[a][b][e] + dm.scale * t1[a][b][e] - t2[a][b][e];
         __syncthreads();
-        {
-            float acc[8][2], wt[8][2];
-            zero_acc<128, 32>(acc);
-            zero_acc<128, 32>(wt);
-            bmm<128, 32, 64, true, false>(acc, Qt, P129, dOs, P33);
-            bmm<128, 32, 64, true, false>(wt, ws, P129, dVs, P33);
-            const float el = expf(gl);
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const int d = ty + 16 * i, e = tx + 16 * j;
-                    dSs[d * P33 + e] = acc[i][j] + el * dSs[d * P33 + e] - wt[i][j];
-                }
-        }
     }
-    __syncthreads();
     if (dh0)
-        for (int idx = threadIdx.x; idx < D * VS; idx += blockDim.x) {
-            const int d = idx >> 5, e = idx & 31;
-            dh0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] = dSs[d * P33 + e];
-        }
+        acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
+            dh0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] = x;
+        });
 }
 
 // B2a: per (chunk, value head): the state-reading terms.
-__global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const __nv_bfloat16* __restrict__ q,
-                                                 const __nv_bfloat16* __restrict__ k, const float* __restrict__ g,
-                                                 const float* __restrict__ S_all, const float* __restrict__ Vp,
-                                                 const __nv_bfloat16* __restrict__ dO, const float* __restrict__ dS_all,
-                                                 const float* __restrict__ dVp, float* __restrict__ dw,
-                                                 float* __restrict__ pdq, float* __restrict__ pdk,
+__global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                 const float* __restrict__ g, const float* __restrict__ S_all,
+                                                 const float* __restrict__ Vp, const bf16* __restrict__ dO,
+                                                 const float* __restrict__ dS_all, const float* __restrict__ dVp,
+                                                 float* __restrict__ dw, float* __restrict__ pdq, float* __restrict__ pdk,
                                                  float* __restrict__ pdg) {
-    extern __shared__ float sm[];
-    float* Ss = sm;                  // [128][129]  S, then dS_next
-    float* X1 = Ss + D * P129;       // [64][129]   scale dO, then V'
-    float* X2 = X1 + L * P129;       // [64][129]   q, then k
-    float* X3 = X2 + L * P129;       // [64][129]   dV'
-    float* gs = X3 + L * P129;       // [64]
-    float* dgs = gs + L;             // [64]
-    float* red = dgs + L;            // [8]
+    extern __shared__ __align__(16) unsigned char smraw[];
+    bf16* sh = reinterpret_cast<bf16*>(smraw);   // S hi/lo [128][136], then dS_next
+    bf16* sl = sh + D * kP128;
+    bf16* xs = sl + D * kP128;                   // dO [64][136], then k
+    bf16* qs = xs + L * kP128;                   // q [64][136]
+    bf16* yh = qs + L * kP128;                   // dV' hi/lo [64][136], then V' hi/lo
+    bf16* yl = yh + L * kP128;
+    float* gs = reinterpret_cast<float*>(yl + L * kP128);
+    float* dgs = gs + L;
+    float* red = dgs + L;  // [8]
     const int c = blockIdx.x, h = blockIdx.y, hk = h / dm.grp;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
-    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-    const float* Sg = S_all + ((int64_t)c * dm.H + h) * D * D;
-    for (int idx = threadIdx.x; idx < D * D; idx += blockDim.x) Ss[(idx >> 7) * P129 + (idx & 127)] = Sg[idx];
-    load_rows_bf16(X1, dO, tok0, n, dm.H, h, dm.scale);
-    load_rows_bf16(X2, q, tok0, n, dm.Hg, hk);
-    load_rows_f32(X3, dVp, tok0, n, dm.H, h);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
+    stage_mat_split<D, D>(sh, sl, kP128, S_all + ((int64_t)c * dm.H + h) * D * D);
+    stage_bf16(xs, dO, tok0, n, dm.H, h);
+    stage_bf16(qs, q, tok0, n, dm.Hg, hk);
+    stage_f32_split(yh, yl, dVp, tok0, n, dm.H, h);
     load_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
     for (int i = threadIdx.x; i < L; i += blockDim.x) dgs[i] = 0.0f;
     __syncthreads();
-    float dq[4][8];
+    float dq[1][8][4];
     {
-        // dQ~ = (scale dO) S^T ; dq = e^g dQ~ ; dg_i += e^{g_i} q_i . dQ~_i
-        zero_acc<64, 128>(dq);
-        bmm<64, 128, 128, false, true>(dq, X1, P129, Ss, P129);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = ty + 16 * i;
-            const float eg = expf(gs[r]);
-            float part = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                dq[i][j] *= eg;
-                part = fmaf(X2[r * P129 + tx + 16 * j], dq[i][j], part);
-            }
-            part = row16_sum(part);
-            if (tx == 0) dgs[r] += part;
+        // dQ~ = scale dO S^T ; dq = e^g dQ~ ; dg_i += e^{g_i} q_i . dQ~_i
+        acc_zero<16, 64>(dq);
+        mma_split_b<16, 64, 128, false, false>(dq, xs, kP128, sh, sl, kP128, m0, n0);
+        float p0 = 0.0f, p1 = 0.0f;
+        acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
+            float& x = dq[i][j][q];
+            x *= dm.scale * expf(gs[r]);
+            const float t = __bfloat162float(qs[r * kP128 + d]) * x;
+            if (q >> 1) p1 += t; else p0 += t;
+        });
+        p0 = quad_sum(p0);
+        p1 = quad_sum(p1);
+        if ((lane & 3) == 0) {
+            atomicAdd(&dgs[m0 + (lane >> 2)], p0);
+            atomicAdd(&dgs[m0 + (lane >> 2) + 8], p1);
         }
     }
     {
         // dw = -dV' S^T
-        float acc[4][8];
-        zero_acc<64, 128>(acc);
-        bmm<64, 128, 128, false, true>(acc, X3, P129, Ss, P129);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                const int r = ty + 16 * i;
-                if (r < n) dw[((tok0 + r) * dm.H + h) * D + tx + 16 * j] = -acc[i][j];
-            }
+        float acc[1][8][4];
+        acc_zero<16, 64>(acc);
+        mma_split_ab<16, 64, 128, false, false>(acc, yh, yl, kP128, sh, sl, kP128, m0, n0);
+        acc_for<16, 64>(acc, m0, n0, [&](int r, int d, float& x) {
+            if (r < n) dw[((tok0 + r) * dm.H + h) * D + d] = -x;
+        });
     }
     __syncthreads();
-    // <S, dS_next>, replacing S by dS_next in place
+    // <S, dS_next> against the f32 state, then dS_next replaces S in the tiles
+    const float* Sg = S_all + ((int64_t)c * dm.H + h) * D * D;
     const float* dSg = dS_all + ((int64_t)c * dm.H + h) * D * D;
     float sdot = 0.0f;
-    for (int idx = threadIdx.x; idx < D * D; idx += blockDim.x) {
-        float* p = Ss + (idx >> 7) * P129 + (idx & 127);
-        const float ds = dSg[idx];
-        sdot = fmaf(*p, ds, sdot);
-        *p = ds;
+    for (int idx = threadIdx.x; idx < D * D / 4; idx += blockDim.x) {
+        const float4 s4 = *reinterpret_cast<const float4*>(Sg + idx * 4);
+        const float4 d4 = *reinterpret_cast<const float4*>(dSg + idx * 4);
+        sdot += s4.x * d4.x + s4.y * d4.y + s4.z * d4.z + s4.w * d4.w;
+        const int r = (idx * 4) >> 7, cc = (idx * 4) & 127;
+        put_split(sh, sl, r * kP128 + cc, d4.x);
+        put_split(sh, sl, r * kP128 + cc + 1, d4.y);
+        put_split(sh, sl, r * kP128 + cc + 2, d4.z);
+        put_split(sh, sl, r * kP128 + cc + 3, d4.w);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xFFFFFFFFu, sdot, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sdot;
-    load_rows_f32(X1, Vp, tok0, n, dm.H, h);
-    load_rows_bf16(X2, k, tok0, n, dm.Hg, hk);
+    if (lane == 0) red[warp] = sdot;
+    stage_f32_split(yh, yl, Vp, tok0, n, dm.H, h);
+    stage_bf16(xs, k, tok0, n, dm.Hg, hk);
     __syncthreads();
     const float gl = gs[n - 1];
-    float dk[4][8];
-    float tsum = 0.0f;
+    float dk[1][8][4];
     {
-        // dK~ = V' dS_next^T ; dk_j = e^{gL-gj} dK~_j ; dg_j -= K~_j . dK~_j ; dg_L += sum
-        zero_acc<64, 128>(dk);
-        bmm<64, 128, 128, false, true>(dk, X1, P129, Ss, P129);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = ty + 16 * i;
-            const float f = r < n ? expf(gl - gs[r]) : 0.0f;
-            float part = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                dk[i][j] *= f;
-                part = fmaf(X2[r * P129 + tx + 16 * j], dk[i][j], part);
-            }
-            part = row16_sum(part);
-            if (tx == 0) {
-                dgs[r] -= part;
-                tsum += part;
-            }
+        // dK~ = V' dS_next^T ; dk_j = e^{gL-gj} dK~_j ; dg_j -= K~_j . dK~_j ; dg_L += their sum
+        acc_zero<16, 64>(dk);
+        mma_split_ab<16, 64, 128, false, false>(dk, yh, yl, kP128, sh, sl, kP128, m0, n0);
+        float p0 = 0.0f, p1 = 0.0f;
+        acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
+            float& x = dk[i][j][q];
+            x *= r < n ? expf(gl - gs[r]) : 0.0f;
+            const float t = __bfloat162float(xs[r * kP128 + d]) * x;
+            if (q >> 1) p1 += t; else p0 += t;
+        });
+        p0 = quad_sum(p0);
+        p1 = quad_sum(p1);
+        if ((lane & 3) == 0) {
+            atomicAdd(&dgs[m0 + (lane >> 2)], -p0);
+            atomicAdd(&dgs[m0 + (lane >> 2) + 8], -p1);
+            atomicAdd(&dgs[n - 1], p0 + p1);
         }
     }
-    // tsum lives in the tx == 0 threads; gather it with the <S, dS_next> partials
-    __shared__ float tred[16];
-    if (tx == 0) tred[ty] = tsum;
     __syncthreads();
     if (threadIdx.x == 0) {
-        float s = 0.0f, t = 0.0f;
+        float s = 0.0f;
         for (int i = 0; i < 8; ++i) s += red[i];
-        for (int i = 0; i < 16; ++i) t += tred[i];
-        dgs[n - 1] += expf(gl) * s + t;
+        dgs[n - 1] += expf(gl) * s;
     }
     __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int r = ty + 16 * i;
-            if (r < n) {
-                const int64_t at = ((tok0 + r) * dm.H + h) * D + tx + 16 * j;
-                pdq[at] = dq[i][j];
-                pdk[at] = dk[i][j];
-            }
-        }
+    acc_for<16, 64>(dq, m0, n0, [&](int r, int d, float& x) {
+        if (r < n) pdq[((tok0 + r) * dm.H + h) * D + d] = x;
+    });
+    acc_for<16, 64>(dk, m0, n0, [&](int r, int d, float& x) {
+        if (r < n) pdk[((tok0 + r) * dm.H + h) * D + d] = x;
+    });
     for (int i = threadIdx.x; i < n; i += blockDim.x) pdg[(tok0 + i) * dm.H + h] = dgs[i];
 }
 
 // B2b: per (chunk, value head): the intra-chunk terms and the solve's adjoint; adds B2a's partials.
-__global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const __nv_bfloat16* __restrict__ q,
-                                                 const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
-                                                 const float* __restrict__ g, const float* __restrict__ beta,
-                                                 const float* __restrict__ A, const float* __restrict__ Vp,
-                                                 const __nv_bfloat16* __restrict__ dO, const float* __restrict__ dVp,
-                                                 const float* __restrict__ dw, const float* __restrict__ pdq,
-                                                 const float* __restrict__ pdk, const float* __restrict__ pdg,
-                                                 float* __restrict__ dq_out, float* __restrict__ dk_out,
-                                                 float* __restrict__ dv_out, float* __restrict__ dbeta_out,
-                                                 float* __restrict__ dg_out) {
-    extern __shared__ float sm[];
-    float* X1 = sm;                  // q, then v
-    float* X2 = X1 + L * P129;       // k
-    float* X3 = X2 + L * P129;       // scale dO, then dw, then Y = dA A^T (pitch 65)
-    float* X4 = X3 + L * P129;       // V', then dV'
-    float* T1 = X4 + L * P129;       // P^ (gated q k^T), then A
-    float* T2 = T1 + L * P65;        // K^ = (k k^T) e^{g_i-g_l}, strict lower
-    float* T3 = T2 + L * P65;        // gated dP, then dA, then E
-    float* gs = T3 + L * P65;
+__global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
+                                                 const bf16* __restrict__ v, const float* __restrict__ g,
+                                                 const float* __restrict__ beta, const float* __restrict__ A,
+                                                 const float* __restrict__ Vp, const bf16* __restrict__ dO,
+                                                 const float* __restrict__ dVp, const float* __restrict__ dw,
+                                                 const float* __restrict__ pdq, const float* __restrict__ pdk,
+                                                 const float* __restrict__ pdg, float* __restrict__ dq_out,
+                                                 float* __restrict__ dk_out, float* __restrict__ dv_out,
+                                                 float* __restrict__ dbeta_out, float* __restrict__ dg_out) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    bf16* ks = reinterpret_cast<bf16*>(smraw);   // k [64][136]
+    bf16* qv = ks + L * kP128;                   // q, then v [64][136]
+    bf16* dos = qv + L * kP128;                  // dO [64][136]
+    bf16* xh = dos + L * kP128;                  // V' hi/lo, then dw hi/lo [64][136]
+    bf16* xl = xh + L * kP128;
+    bf16* dvh = xl + L * kP128;                  // dV' hi/lo [64][136]
+    bf16* dvl = dvh + L * kP128;
+    bf16* ah = dvl + L * kP128;                  // A hi/lo [64][72]
+    bf16* al = ah + L * kP64;
+    bf16* th = al + L * kP64;                    // gated dP, then dA, then E (hi/lo) [64][72]
+    bf16* tl = th + L * kP64;
+    bf16* yh = tl + L * kP64;                    // Y = dA A^T hi/lo [64][72]
+    bf16* yl = yh + L * kP64;
+    float* Cs = reinterpret_cast<float*>(yl + L * kP64);  // (k k^T) e^{g_i-g_l}, strict lower [64][65]
+    float* gs = Cs + L * F65;
     float* bs = gs + L;
     float* dgs = bs + L;
     float* dbs = dgs + L;
     const int c = blockIdx.x, h = blockIdx.y, hk = h / dm.grp;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
-    const int ty = threadIdx.x >> 4, tx = threadIdx.x & 15;
-    load_rows_bf16(X1, q, tok0, n, dm.Hg, hk);
-    load_rows_bf16(X2, k, tok0, n, dm.Hg, hk);
-    load_rows_bf16(X3, dO, tok0, n, dm.H, h, dm.scale);
-    load_rows_f32(X4, Vp, tok0, n, dm.H, h);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pm0 = (warp & 3) * 16, pn0 = (warp >> 2) * 32;   // [64 x 64] warp tile
+    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;     // [64 x 128] warp tile
+    stage_bf16(ks, k, tok0, n, dm.Hg, hk);
+    stage_bf16(qv, q, tok0, n, dm.Hg, hk);
+    stage_bf16(dos, dO, tok0, n, dm.H, h);
+    stage_f32_split(xh, xl, Vp, tok0, n, dm.H, h);
     load_gb(gs, bs, g, beta, tok0, n, dm.H, h);
     for (int i = threadIdx.x; i < L; i += blockDim.x) {
         dgs[i] = 0.0f;
@@ -560,169 +587,144 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const __nv_bfloat16* _
     }
     __syncthreads();
     {
-        float acc[4][4];
-        zero_acc<64, 64>(acc);
-        bmm<64, 64, 128, false, true>(acc, X1, P129, X2, P129);  // q k^T
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int r = ty + 16 * i, l = tx + 16 * j;
-                T1[r * P65 + l] = (l <= r && r < n) ? acc[i][j] * expf(gs[r] - gs[l]) : 0.0f;
-            }
-        zero_acc<64, 64>(acc);
-        bmm<64, 64, 128, false, true>(acc, X2, P129, X2, P129);  // k k^T
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int r = ty + 16 * i, l = tx + 16 * j;
-                T2[r * P65 + l] = (l < r && r < n) ? acc[i][j] * expf(gs[r] - gs[l]) : 0.0f;
-            }
-        // dP = (scale dO) V'^T, causal; D = dP * P^ -> dg ; gated dP -> T3
-        zero_acc<64, 64>(acc);
-        bmm<64, 64, 128, false, true>(acc, X3, P129, X4, P129);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = ty + 16 * i;
-            float rowD = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int l = tx + 16 * j;
-                const bool on = l <= r && r < n;
-                const float dp = on ? acc[i][j] : 0.0f;
-                const float dd = dp * T1[r * P65 + l];
-                rowD += dd;
-                if (on) atomicAdd(&dgs[l], -dd);
-                T3[r * P65 + l] = on ? dp * expf(gs[r] - gs[l]) : 0.0f;
-            }
-            rowD = row16_sum(rowD);
-            if (tx == 0) atomicAdd(&dgs[r], rowD);
+        float qk[1][4][4], kk[1][4][4], dp[1][4][4];
+        acc_zero<16, 32>(qk);
+        acc_zero<16, 32>(kk);
+        acc_zero<16, 32>(dp);
+        warp_mma<16, 32, 128, false, false>(qk, qv, kP128, ks, kP128, pm0, pn0);
+        warp_mma<16, 32, 128, false, false>(kk, ks, kP128, ks, kP128, pm0, pn0);
+        mma_split_b<16, 32, 128, false, false>(dp, dos, kP128, xh, xl, kP128, pm0, pn0);
+        float r0 = 0.0f, r1 = 0.0f;
+        acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
+            const float phi = expf(gs[r] - gs[l]);
+            const bool on = l <= r && r < n;
+            const float dpv = on ? dm.scale * dp[i][j][q] : 0.0f;
+            const float dd = dpv * qk[i][j][q] * phi;
+            if (q >> 1) r1 += dd; else r0 += dd;
+            if (on) atomicAdd(&dgs[l], -dd);
+            put_split(th, tl, r * kP64 + l, on ? dpv * phi : 0.0f);
+            Cs[r * F65 + l] = (l < r && r < n) ? kk[i][j][q] * phi : 0.0f;
+        });
+        r0 = quad_sum(r0);
+        r1 = quad_sum(r1);
+        if ((lane & 3) == 0) {
+            atomicAdd(&dgs[pm0 + (lane >> 2)], r0);
+            atomicAdd(&dgs[pm0 + (lane >> 2) + 8], r1);
         }
     }
     __syncthreads();
-    float dqa[4][8], dka[4][8];
-    zero_acc<64, 128>(dqa);
-    zero_acc<64, 128>(dka);
-    bmm<64, 128, 64, false, false>(dqa, T3, P65, X2, P129);  // dq += gated dP k
-    bmm<64, 128, 64, true, false>(dka, T3, P65, X1, P129);   // dk += gated dP^T q
+    float dqa[1][8][4], dka[1][8][4];
+    acc_zero<16, 64>(dqa);
+    acc_zero<16, 64>(dka);
+    mma_split_a<16, 64, 64, false, true>(dqa, th, tl, kP64, ks, kP128, m0, n0);  // dq += gated dP k
+    mma_split_a<16, 64, 64, true, true>(dka, th, tl, kP64, qv, kP128, m0, n0);   // dk += gated dP^T q
     __syncthreads();
     // v, dw, dV', A
-    for (int idx = threadIdx.x; idx < L * D; idx += blockDim.x) {
-        const int i = idx >> 7, d = idx & 127;
-        const int64_t at = ((tok0 + i) * dm.H + h) * D + d;
-        X1[i * P129 + d] = i < n ? __bfloat162float(v[at]) : 0.0f;
-        X3[i * P129 + d] = i < n ? dw[at] : 0.0f;
-        X4[i * P129 + d] = i < n ? dVp[at] : 0.0f;
-    }
+    stage_bf16(qv, v, tok0, n, dm.H, h);
+    stage_f32_split(xh, xl, dw, tok0, n, dm.H, h);
+    stage_f32_split(dvh, dvl, dVp, tok0, n, dm.H, h);
     for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
         const int i = idx >> 6, j = idx & 63;
-        T1[i * P65 + j] = i < n ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f;
+        put_split(ah, al, i * kP64 + j, i < n ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f);
     }
     __syncthreads();
     {
         // dA = dw kb^T + dV' vb^T, strict lower ; kb_j = beta_j e^{g_j} k_j, vb_j = beta_j v_j
-        float a1[4][4], a2[4][4];
-        zero_acc<64, 64>(a1);
-        zero_acc<64, 64>(a2);
-        bmm<64, 64, 128, false, true>(a1, X3, P129, X2, P129);
-        bmm<64, 64, 128, false, true>(a2, X4, P129, X1, P129);
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int r = ty + 16 * i, l = tx + 16 * j;
-                T3[r * P65 + l] = l < r ? bs[l] * (expf(gs[l]) * a1[i][j] + a2[i][j]) : 0.0f;
-            }
+        float a1[1][4][4], a2[1][4][4];
+        acc_zero<16, 32>(a1);
+        acc_zero<16, 32>(a2);
+        mma_split_a<16, 32, 128, false, false>(a1, xh, xl, kP128, ks, kP128, pm0, pn0);
+        mma_split_a<16, 32, 128, false, false>(a2, dvh, dvl, kP128, qv, kP128, pm0, pn0);
+        acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
+            put_split(th, tl, r * kP64 + l, l < r ? bs[l] * (expf(gs[l]) * a1[i][j][q] + a2[i][j][q]) : 0.0f);
+        });
     }
     {
-        // dkb = A^T dw -> dk, dbeta, dg
-        float acc[4][8];
-        zero_acc<64, 128>(acc);
-        bmm<64, 128, 64, true, false>(acc, T1, P65, X3, P129);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = ty + 16 * i;
-            const float eg = expf(gs[r]), be = bs[r] * eg;
-            float part = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                part = fmaf(X2[r * P129 + tx + 16 * j], acc[i][j], part);
-                dka[i][j] = fmaf(be, acc[i][j], dka[i][j]);
-            }
-            part = row16_sum(part);
-            if (tx == 0) {
-                dbs[r] += eg * part;
-                dgs[r] += be * part;
-            }
+        // dkb = A^T dw -> dk, dbeta, dg ;  dvb = A^T dV' -> dv, dbeta
+        float acc[1][8][4];
+        acc_zero<16, 64>(acc);
+        mma_split_ab<16, 64, 64, true, true>(acc, ah, al, kP64, xh, xl, kP128, m0, n0);
+        float p0 = 0.0f, p1 = 0.0f;
+        acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
+            const float x = acc[i][j][q];
+            const float t = __bfloat162float(ks[r * kP128 + d]) * x;
+            if (q >> 1) p1 += t; else p0 += t;
+            dka[i][j][q] += bs[r] * expf(gs[r]) * x;
+        });
+        p0 = quad_sum(p0);
+        p1 = quad_sum(p1);
+        if ((lane & 3) == 0) {
+            const int ra = m0 + (lane >> 2), rb = ra + 8;
+            const float ea = expf(gs[ra]), eb = expf(gs[rb]);
+            atomicAdd(&dbs[ra], ea * p0);
+            atomicAdd(&dgs[ra], bs[ra] * ea * p0);
+            atomicAdd(&dbs[rb], eb * p1);
+            atomicAdd(&dgs[rb], bs[rb] * eb * p1);
         }
-        // dvb = A^T dV' -> dv, dbeta
-        zero_acc<64, 128>(acc);
-        bmm<64, 128, 64, true, false>(acc, T1, P65, X4, P129);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = ty + 16 * i;
-            float part = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                part = fmaf(X1[r * P129 + tx + 16 * j], acc[i][j], part);
-                if (r < n) dv_out[((tok0 + r) * dm.H + h) * D + tx + 16 * j] = bs[r] * acc[i][j];
-            }
-            part = row16_sum(part);
-            if (tx == 0) dbs[r] += part;
+        acc_zero<16, 64>(acc);
+        mma_split_ab<16, 64, 64, true, true>(acc, ah, al, kP64, dvh, dvl, kP128, m0, n0);
+        p0 = p1 = 0.0f;
+        acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
+            const float x = acc[i][j][q];
+            const float t = __bfloat162float(qv[r * kP128 + d]) * x;
+            if (q >> 1) p1 += t; else p0 += t;
+            if (r < n) dv_out[((tok0 + r) * dm.H + h) * D + d] = bs[r] * x;
+        });
+        p0 = quad_sum(p0);
+        p1 = quad_sum(p1);
+        if ((lane & 3) == 0) {
+            atomicAdd(&dbs[m0 + (lane >> 2)], p0);
+            atomicAdd(&dbs[m0 + (lane >> 2) + 8], p1);
         }
     }
     __syncthreads();
     {
-        // Y = dA A^T into X3 (pitch 65); dM = -A^T Y, strict lower
-        float acc[4][4];
-        zero_acc<64, 64>(acc);
-        bmm<64, 64, 64, false, true>(acc, T3, P65, T1, P65);
+        // Y = dA A^T ; dM = -A^T Y, strict lower
+        float acc[1][4][4];
+        acc_zero<16, 32>(acc);
+        mma_split_ab<16, 32, 64, false, false>(acc, th, tl, kP64, ah, al, kP64, pm0, pn0);
+        acc_for<16, 32>(acc, pm0, pn0, [&](int r, int l, float& x) { put_split(yh, yl, r * kP64 + l, x); });
         __syncthreads();
-        store_acc<64, 64>(acc, X3, P65);
-        __syncthreads();
-        zero_acc<64, 64>(acc);
-        bmm<64, 64, 64, true, false>(acc, T1, P65, X3, P65);
-        __syncthreads();
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int r = ty + 16 * i;
-            float rowB = 0.0f, rowG = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int l = tx + 16 * j;
-                const bool on = l < r && r < n;
-                const float dm_ = on ? -acc[i][j] : 0.0f;
-                const float kh = T2[r * P65 + l];
-                rowB = fmaf(dm_, kh, rowB);
-                const float gg = dm_ * bs[r] * kh;
-                rowG += gg;
-                if (on) atomicAdd(&dgs[l], -gg);
-                T3[r * P65 + l] = on ? dm_ * bs[r] * expf(gs[r] - gs[l]) : 0.0f;
-            }
-            rowB = row16_sum(rowB);
-            rowG = row16_sum(rowG);
-            if (tx == 0) {
-                dbs[r] += rowB;
-                atomicAdd(&dgs[r], rowG);  // other threads add column terms to the same entries
-            }
+        acc_zero<16, 32>(acc);
+        mma_split_ab<16, 32, 64, true, true>(acc, ah, al, kP64, yh, yl, kP64, pm0, pn0);
+        __syncthreads();  // every warp has read dA (th/tl) before E overwrites it
+        float b0 = 0.0f, b1 = 0.0f, g0 = 0.0f, g1 = 0.0f;
+        acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
+            const bool on = l < r && r < n;
+            const float dm_ = on ? -acc[i][j][q] : 0.0f;
+            const float kh = Cs[r * F65 + l];
+            const float gg = dm_ * bs[r] * kh;
+            if (q >> 1) { b1 += dm_ * kh; g1 += gg; } else { b0 += dm_ * kh; g0 += gg; }
+            if (on) atomicAdd(&dgs[l], -gg);
+            put_split(th, tl, r * kP64 + l, on ? dm_ * bs[r] * expf(gs[r] - gs[l]) : 0.0f);
+        });
+        b0 = quad_sum(b0);
+        b1 = quad_sum(b1);
+        g0 = quad_sum(g0);
+        g1 = quad_sum(g1);
+        if ((lane & 3) == 0) {
+            atomicAdd(&dbs[pm0 + (lane >> 2)], b0);
+            atomicAdd(&dgs[pm0 + (lane >> 2)], g0);
+            atomicAdd(&dbs[pm0 + (lane >> 2) + 8], b1);
+            atomicAdd(&dgs[pm0 + (lane >> 2) + 8], g1);
         }
     }
     __syncthreads();
-    bmm<64, 128, 64, false, false>(dka, T3, P65, X2, P129);  // dk_i += sum_l E_il k_l
-    bmm<64, 128, 64, true, false>(dka, T3, P65, X2, P129);   // dk_l += sum_i E_il k_i
+    mma_split_a<16, 64, 64, false, true>(dka, th, tl, kP64, ks, kP128, m0, n0);  // dk_i += sum_l E_il k_l
+    mma_split_a<16, 64, 64, true, true>(dka, th, tl, kP64, ks, kP128, m0, n0);   // dk_l += sum_i E_il k_i
     __syncthreads();
-#pragma unroll
-    for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const int r = ty + 16 * i;
-            if (r < n) {
-                const int64_t at = ((tok0 + r) * dm.H + h) * D + tx + 16 * j;
-                dq_out[at] = dqa[i][j] + pdq[at];
-                dk_out[at] = dka[i][j] + pdk[at];
-            }
+    acc_for<16, 64>(dqa, m0, n0, [&](int r, int d, float& x) {
+        if (r < n) {
+            const int64_t at = ((tok0 + r) * dm.H + h) * D + d;
+            dq_out[at] = x + pdq[at];
         }
+    });
+    acc_for<16, 64>(dka, m0, n0, [&](int r, int d, float& x) {
+        if (r < n) {
+            const int64_t at = ((tok0 + r) * dm.H + h) * D + d;
+            dk_out[at] = x + pdk[at];
+        }
+    });
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int64_t at = (tok0 + i) * dm.H + h;
         dg_out[at] = dgs[i] + pdg[at];
@@ -733,22 +735,25 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const __nv_bfloat16* _
 // dst[t, hk, :] = sum over the value heads hk * grp .. of src[t, h, :]
 __global__ void gdn_sum_heads_kernel(const float* __restrict__ src, float* __restrict__ dst, int64_t T, int H, int Hg) {
     const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= T * Hg * D) return;
-    const int d = idx % D;
-    const int hk = (idx / D) % Hg;
-    const int64_t t = idx / ((int64_t)D * Hg);
+    if (idx >= T * Hg * (D / 4)) return;
+    const int d4 = (int)(idx % (D / 4)) * 4;
+    const int hk = (int)((idx / (D / 4)) % Hg);
+    const int64_t t = idx / ((int64_t)(D / 4) * Hg);
     const int grp = H / Hg;
-    float s = 0.0f;
-    for (int j = 0; j < grp; ++j) s += src[(t * H + hk * grp + j) * D + d];
-    dst[idx] = s;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < grp; ++j) {
+        const float4 v = *reinterpret_cast<const float4*>(src + (t * H + hk * grp + j) * D + d4);
+        s.x += v.x, s.y += v.y, s.z += v.z, s.w += v.w;
+    }
+    *reinterpret_cast<float4*>(dst + (t * Hg + hk) * D + d4) = s;
 }
 
-constexpr size_t kSmemPrep = (2 * L * P129 + 2 * L * P65 + 4 * L + 2 * L) * 4;
-constexpr size_t kSmemState = (D * P33 + 2 * L * P129 + L * P33 + L) * 4;
-constexpr size_t kSmemOut = (2 * L * P129 + L * P65 + D * P129 + L) * 4;
-constexpr size_t kSmemBState = (D * P33 + L * P65 + 3 * L * P129 + 2 * L * P33 + L) * 4;
-constexpr size_t kSmemBA = (D * P129 + 3 * L * P129 + 2 * L + 8) * 4;
-constexpr size_t kSmemBB = (4 * L * P129 + 3 * L * P65 + 4 * L) * 4;
+constexpr size_t kSmemPrep = (2 * L * kP128 + 4 * L * kP64) * 2 + (2 * L * F65 + 4 * L + 2 * L) * 4;
+constexpr size_t kSmemState = (2 * D * P32 + 3 * L * kP128 + 2 * L * P32) * 2 + (L * 33 + L) * 4;
+constexpr size_t kSmemOut = (4 * L * kP128 + 2 * D * kP128 + 2 * L * kP64) * 2 + L * 4;
+constexpr size_t kSmemBState = (2 * D * P32 + 2 * L * kP64 + 4 * L * kP128 + 5 * L * P32) * 2 + L * 4;
+constexpr size_t kSmemBA = (2 * D * kP128 + 4 * L * kP128) * 2 + (2 * L + 8) * 4;
+constexpr size_t kSmemBB = (7 * L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 
 bool g_attr = false;
 
@@ -801,17 +806,16 @@ extern "C" int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* a, void* 
     set_attrs();
     const Dims dm = to_dims(*dims);
     cudaStream_t s = as_stream(stream);
-    const auto* q = reinterpret_cast<const __nv_bfloat16*>(a->q);
-    const auto* k = reinterpret_cast<const __nv_bfloat16*>(a->k);
-    const auto* v = reinterpret_cast<const __nv_bfloat16*>(a->v);
-    if (dm.n_chunks > 0) {
-        gdn_fwd_prep<<<dim3(dm.n_chunks, dm.H), 256, kSmemPrep, s>>>(dm, q, k, v, a->g, a->beta, a->A, a->w, a->u);
-    }
+    const auto* q = reinterpret_cast<const bf16*>(a->q);
+    const auto* k = reinterpret_cast<const bf16*>(a->k);
+    const auto* v = reinterpret_cast<const bf16*>(a->v);
+    if (dm.n_chunks > 0)
+        gdn_fwd_prep<<<dim3(dm.n_chunks, dm.H), 256, kSmemPrep, s>>>(dm, k, v, a->g, a->beta, a->A, a->w, a->u);
     gdn_fwd_state<<<dim3(dm.n_seq, dm.H, D / VS), 256, kSmemState, s>>>(dm, k, a->g, a->w, a->u, a->h0, a->S, a->Vp,
                                                                        a->ht);
     if (dm.n_chunks > 0)
         gdn_fwd_out<<<dim3(dm.n_chunks, dm.H), 256, kSmemOut, s>>>(dm, q, k, a->g, a->S, a->Vp, a->P,
-                                                                   reinterpret_cast<__nv_bfloat16*>(a->o));
+                                                                   reinterpret_cast<bf16*>(a->o));
     return launch_status(dm.n_chunks > 0 ? 3 : 1);
 }
 
@@ -824,10 +828,10 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
     set_attrs();
     const Dims dm = to_dims(*dims);
     cudaStream_t s = as_stream(stream);
-    const auto* q = reinterpret_cast<const __nv_bfloat16*>(a->q);
-    const auto* k = reinterpret_cast<const __nv_bfloat16*>(a->k);
-    const auto* v = reinterpret_cast<const __nv_bfloat16*>(a->v);
-    const auto* dO = reinterpret_cast<const __nv_bfloat16*>(a->dO);
+    const auto* q = reinterpret_cast<const bf16*>(a->q);
+    const auto* k = reinterpret_cast<const bf16*>(a->k);
+    const auto* v = reinterpret_cast<const bf16*>(a->v);
+    const auto* dO = reinterpret_cast<const bf16*>(a->dO);
     gdn_bwd_state<<<dim3(dm.n_seq, dm.H, D / VS), 256, kSmemBState, s>>>(dm, q, k, a->g, a->w, a->P, dO, a->dht,
                                                                         a->dS, a->dVp, a->dh0);
     if (dm.n_chunks > 0) {
@@ -842,7 +846,7 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
 
 extern "C" int r97b_gdn_sum_heads(const float* src, float* dst, int64_t T, int32_t H, int32_t Hg, void* stream) {
     if (!src || !dst || T < 0 || H <= 0 || Hg <= 0 || H % Hg) return R97B_EINVAL;
-    const int64_t total = T * Hg * 128;
+    const int64_t total = T * Hg * (128 / 4);
     if (total == 0) return R97B_OK;
     gdn_sum_heads_kernel<<<(unsigned)((total + 255) / 256), 256, 0, as_stream(stream)>>>(src, dst, T, H, Hg);
     return launch_status();
