@@ -258,3 +258,103 @@ def adamw_update(w, m, v, g, lr, b1, b2, eps, wd, t, inv_k=np.float32(1.0), clip
     vh = v / bc2
     w[:] = w - lr * (mh / (np.sqrt(vh) + eps) + wd * w)
     return bc1, bc2
+
+
+# ----------------------------------------------------------------------------- GDN conv prep + gates
+
+def _silu(x):
+    return x / (1.0 + np.exp(-x))
+
+
+def _silu_grad(x):
+    s = 1.0 / (1.0 + np.exp(-x))
+    return s * (1.0 + x * (1.0 - s))
+
+
+def _positions(cu, T):
+    pos = np.zeros(T, np.int64)
+    for s in range(len(cu) - 1):
+        pos[cu[s]:cu[s + 1]] = np.arange(cu[s + 1] - cu[s])
+    return pos
+
+
+def conv_acc(x, w, cu):
+    """Causal depthwise conv of width W over each sequence from a cold start (reference
+    src/adjoint/host/gdn_prep.cpp:204-229 conv_phase): acc[t, c] = sum_j x[t - W + 1 + j, c] w[c, j]."""
+    T, C = x.shape
+    W = w.shape[1]
+    pos = _positions(cu, T)
+    acc = np.zeros((T, C))
+    for j in range(W):
+        sh = W - 1 - j
+        src = np.zeros_like(x)
+        src[sh:] = x[:T - sh] if sh else x
+        acc += np.where((pos >= sh)[:, None], src, 0.0) * w[:, j][None, :]
+    return acc
+
+
+def conv_prep_fwd(x, w, cu, Hg, H, K=128, eps=1e-6):
+    """q, k (L2-normalised per head) and v (reference src/adjoint/host/gdn_prep.cpp:261-318)."""
+    T = x.shape[0]
+    qk = Hg * K
+    u = _silu(conv_acc(x[:, :2 * qk + H * K], w, cu))
+    q = u[:, :qk].reshape(T, Hg, K)
+    k = u[:, qk:2 * qk].reshape(T, Hg, K)
+    q = q / np.sqrt((q * q).sum(-1, keepdims=True) + eps)
+    k = k / np.sqrt((k * k).sum(-1, keepdims=True) + eps)
+    return q, k, u[:, 2 * qk:].reshape(T, H, K)
+
+
+def conv_prep_bwd(x, w, cu, Hg, H, dq, dk, dv, K=128, eps=1e-6):
+    """dx of conv_prep_fwd (reference src/adjoint/host/gdn_prep.cpp:367-455, without the carried state)."""
+    T = x.shape[0]
+    qk = Hg * K
+    C = 2 * qk + H * K
+    acc = conv_acc(x[:, :C], w, cu)
+    u = _silu(acc)
+    dacc = np.zeros((T, C))
+    for part, dout in ((slice(0, qk), dq), (slice(qk, 2 * qk), dk)):
+        uu = u[:, part].reshape(T, Hg, K)
+        ss = (uu * uu).sum(-1, keepdims=True)
+        inv = 1.0 / np.sqrt(ss + eps)
+        dot = (uu * dout).sum(-1, keepdims=True)
+        du = inv * dout - inv ** 3 * uu * dot
+        dacc[:, part] = du.reshape(T, qk) * _silu_grad(acc[:, part])
+    dacc[:, 2 * qk:] = dv.reshape(T, H * K) * _silu_grad(acc[:, 2 * qk:])
+    pos = _positions(cu, T)
+    W = w.shape[1]
+    dx = np.zeros((T, C))
+    for j in range(W):
+        sh = W - 1 - j  # output row t reads input row t - sh
+        contrib = np.where((pos >= sh)[:, None], dacc, 0.0) * w[:, j][None, :]
+        dx[:T - sh] += contrib[sh:] if sh else contrib
+    return dx
+
+
+def _softplus(x):
+    return np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0))))
+
+
+def gates_fwd(a, b, a_log, dt_bias, cu, chunk=64):
+    """g = within-chunk running sum of -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b)
+    (reference src/adjoint/host/gdn_prep.cpp:320-336)."""
+    inc = -np.exp(a_log)[None, :] * _softplus(a + dt_bias[None, :])
+    g = np.zeros_like(inc)
+    for s in range(len(cu) - 1):
+        for c0 in range(cu[s], cu[s + 1], chunk):
+            r = slice(c0, min(cu[s + 1], c0 + chunk))
+            g[r] = np.cumsum(inc[r], axis=0)
+    return g, 1.0 / (1.0 + np.exp(-b))
+
+
+def gates_bwd(a, b, a_log, dt_bias, cu, dg, dbeta, chunk=64):
+    """da, db of gates_fwd (reference src/adjoint/host/gdn_prep.cpp:467-488)."""
+    tail = np.zeros_like(dg)
+    for s in range(len(cu) - 1):
+        for c0 in range(cu[s], cu[s + 1], chunk):
+            r = slice(c0, min(cu[s + 1], c0 + chunk))
+            tail[r] = np.cumsum(dg[r][::-1], axis=0)[::-1]
+    av = a + dt_bias[None, :]
+    sp = np.where(av > 20.0, 1.0, 1.0 / (1.0 + np.exp(-av)))
+    sb = 1.0 / (1.0 + np.exp(-b))
+    return tail * (-np.exp(a_log))[None, :] * sp, dbeta * sb * (1.0 - sb)

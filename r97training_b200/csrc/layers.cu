@@ -94,112 +94,190 @@ struct ConvArgs {
     int n_seq, T, Hg, H, conv_dim;
 };
 
-// acc[c..c+7] of token t (pre-activation)
-__device__ __forceinline__ void conv8(const ConvArgs& a, int t, int t0, int c, float (&acc)[8]) {
+constexpr int kTB = 16;  // tokens a conv-prep thread walks
+
+// A conv-prep thread owns 8 channels [c, c + 8) of 16 consecutive tokens: it keeps the channels' 4-tap
+// weights (w is [conv_dim][4]) in registers and slides a window of input rows down the tokens, so each
+// row of x is read once per thread. The 16 threads of a half warp hold one 128-wide head's channels of
+// the same tokens, so a head's L2 norm is a half-warp shuffle sum.
+struct ConvThread {
+    int t_begin, c;
+    bool valid;
+};
+
+__device__ __forceinline__ ConvThread conv_thread(const ConvArgs& a) {
+    const int groups = a.conv_dim / 8;
+    const int tblocks = (a.T + kTB - 1) / kTB;
+    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    ConvThread ct;
+    ct.valid = gid < (int64_t)tblocks * groups;
+    const int64_t g = ct.valid ? gid : (int64_t)tblocks * groups - 1;
+    ct.t_begin = (int)(g / groups) * kTB;
+    ct.c = (int)(g % groups) * 8;
+    return ct;
+}
+
+__device__ __forceinline__ void load_w8(const ConvArgs& a, int c, float (&w)[8][kW]) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(a.w + (c + i) * kW);
+        w[i][0] = v.x, w[i][1] = v.y, w[i][2] = v.z, w[i][3] = v.w;
+    }
+}
+
+// Walks the thread's tokens and calls fn(t, acc) with the pre-activation conv output of channels c..c+7.
+template <typename F>
+__device__ __forceinline__ void conv_walk(const ConvArgs& a, const ConvThread& ct, const float (&w)[8][kW], F&& fn) {
+    float row[kW][8];
+    // the three rows before the first token (clipped at the sequence start per token below)
 #pragma unroll
-    for (int j = 0; j < kW; ++j) {
-        const int src = t - (kW - 1) + j;
-        if (src < t0) continue;
-        float xv[8];
-        ld8(a.x + (int64_t)src * a.ldx + c, xv);
+    for (int j = 0; j < kW - 1; ++j) {
+        const int src = ct.t_begin - (kW - 1) + j;
+        if (src >= 0 && src < a.T) ld8(a.x + (int64_t)src * a.ldx + ct.c, row[j]);
+        else
 #pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = fmaf(xv[i], a.w[(c + i) * kW + j], acc[i]);
+            for (int i = 0; i < 8; ++i) row[j][i] = 0.0f;
+    }
+    int s = 0;
+    while (s + 1 < a.n_seq && a.cu[s + 1] <= ct.t_begin) ++s;
+    int t0 = a.cu[s], t1 = a.cu[s + 1];
+#pragma unroll 1
+    for (int k = 0; k < kTB; ++k) {
+        const int t = ct.t_begin + k;
+        const int tc = t < a.T ? t : a.T - 1;
+        ld8(a.x + (int64_t)tc * a.ldx + ct.c, row[kW - 1]);
+        while (t >= t1 && s + 1 < a.n_seq) {
+            ++s;
+            t0 = a.cu[s];
+            t1 = a.cu[s + 1];
+        }
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kW; ++j) {
+            const bool on = t - (kW - 1) + j >= t0;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = fmaf(on ? row[j][i] : 0.0f, w[i][j], acc[i]);
+        }
+        fn(t, acc);
+#pragma unroll
+        for (int j = 0; j < kW - 1; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) row[j][i] = row[j + 1][i];
     }
 }
 
 __global__ void __launch_bounds__(256) conv_prep_fwd_kernel(ConvArgs a, __nv_bfloat16* __restrict__ q,
                                                             __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v) {
-    const int groups = a.conv_dim / 8;
-    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const bool valid = gid < (int64_t)a.T * groups;
-    const int t = valid ? (int)(gid / groups) : a.T - 1;
-    const int c = valid ? (int)(gid % groups) * 8 : 0;
-    const int t0 = seq_start(a.cu, a.n_seq, t);
-    float acc[8], u[8];
-    conv8(a, t, t0, c, acc);
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        u[i] = silu(acc[i]);
-        ss = fmaf(u[i], u[i], ss);
-    }
+    const ConvThread ct = conv_thread(a);
+    float w[8][kW];
+    load_w8(a, ct.c, w);
     const int qk = a.Hg * 128;
-    // 16 consecutive lanes cover one 128-wide head; the q|k|v boundaries are head aligned
-    ss = sum16(ss);
-    if (!valid) return;
-    if (c < 2 * qk) {
-        const float inv = rsqrtf(ss + 1e-6f);
+    conv_walk(a, ct, w, [&](int t, const float (&acc)[8]) {
+        float u[8], ss = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) u[i] *= inv;
-        if (c < qk) st8(q + (int64_t)t * qk + c, u);
-        else st8(k + (int64_t)t * qk + (c - qk), u);
-    } else {
-        st8(v + (int64_t)t * a.H * 128 + (c - 2 * qk), u);
-    }
+        for (int i = 0; i < 8; ++i) {
+            u[i] = silu(acc[i]);
+            ss = fmaf(u[i], u[i], ss);
+        }
+        ss = sum16(ss);  // every lane joins; the q|k|v boundaries are head aligned
+        if (!ct.valid || t >= a.T) return;
+        if (ct.c < 2 * qk) {
+            const float inv = rsqrtf(ss + 1e-6f);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) u[i] *= inv;
+            if (ct.c < qk) st8(q + (int64_t)t * qk + ct.c, u);
+            else st8(k + (int64_t)t * qk + (ct.c - qk), u);
+        } else {
+            st8(v + (int64_t)t * a.H * 128 + (ct.c - 2 * qk), u);
+        }
+    });
 }
 
 // dacc[t, c] from the cotangents of the normalised q, k (f32 [T, Hg, 128]) and of v (f32 [T, H, 128])
 __global__ void __launch_bounds__(256) conv_prep_dacc_kernel(ConvArgs a, const float* __restrict__ dq,
                                                              const float* __restrict__ dk, const float* __restrict__ dv,
                                                              float* __restrict__ dacc) {
-    const int groups = a.conv_dim / 8;
-    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const bool valid = gid < (int64_t)a.T * groups;
-    const int t = valid ? (int)(gid / groups) : a.T - 1;
-    const int c = valid ? (int)(gid % groups) * 8 : 0;
-    const int t0 = seq_start(a.cu, a.n_seq, t);
+    const ConvThread ct = conv_thread(a);
+    float w[8][kW];
+    load_w8(a, ct.c, w);
     const int qk = a.Hg * 128;
-    float acc[8], u[8], dout[8];
-    conv8(a, t, t0, c, acc);
-    if (c < qk) ld8f(dq + (int64_t)t * qk + c, dout);
-    else if (c < 2 * qk) ld8f(dk + (int64_t)t * qk + (c - qk), dout);
-    else ld8f(dv + (int64_t)t * a.H * 128 + (c - 2 * qk), dout);
-    float ss = 0.0f, dot = 0.0f;
+    const int c = ct.c;
+    conv_walk(a, ct, w, [&](int t, const float (&acc)[8]) {
+        const int tc = t < a.T ? t : a.T - 1;
+        float u[8], dout[8];
+        if (c < qk) ld8f(dq + (int64_t)tc * qk + c, dout);
+        else if (c < 2 * qk) ld8f(dk + (int64_t)tc * qk + (c - qk), dout);
+        else ld8f(dv + (int64_t)tc * a.H * 128 + (c - 2 * qk), dout);
+        float ss = 0.0f, dot = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        u[i] = silu(acc[i]);
-        ss = fmaf(u[i], u[i], ss);
-        dot = fmaf(u[i], dout[i], dot);
-    }
-    ss = sum16(ss);
-    dot = sum16(dot);
-    if (!valid) return;
-    float o[8];
-    if (c < 2 * qk) {
-        const float inv = rsqrtf(ss + 1e-6f), inv3 = inv * inv * inv;
+        for (int i = 0; i < 8; ++i) {
+            u[i] = silu(acc[i]);
+            ss = fmaf(u[i], u[i], ss);
+            dot = fmaf(u[i], dout[i], dot);
+        }
+        ss = sum16(ss);
+        dot = sum16(dot);
+        if (!ct.valid || t >= a.T) return;
+        float o[8];
+        if (c < 2 * qk) {
+            const float inv = rsqrtf(ss + 1e-6f), inv3 = inv * inv * inv;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = (inv * dout[i] - inv3 * u[i] * dot) * silu_grad(acc[i]);
-    } else {
+            for (int i = 0; i < 8; ++i) o[i] = (inv * dout[i] - inv3 * u[i] * dot) * silu_grad(acc[i]);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = dout[i] * silu_grad(acc[i]);
-    }
-    st8f(dacc + (int64_t)t * a.conv_dim + c, o);
+            for (int i = 0; i < 8; ++i) o[i] = dout[i] * silu_grad(acc[i]);
+        }
+        st8f(dacc + (int64_t)t * a.conv_dim + c, o);
+    });
 }
 
-// dx[t, c] = sum_{t' = t .. t+3, same sequence} dacc[t', c] w[c, t - t' + 3]
+// dx[t, c] = sum_{t' = t .. t+3, same sequence} dacc[t', c] w[c, t - t' + 3], walking the tokens with a
+// window of the next three dacc rows
 __global__ void __launch_bounds__(256) conv_prep_dx_kernel(ConvArgs a, const float* __restrict__ dacc,
                                                            __nv_bfloat16* __restrict__ dx, int64_t lddx) {
-    const int groups = a.conv_dim / 8;
-    const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (gid >= (int64_t)a.T * groups) return;
-    const int t = (int)(gid / groups);
-    const int c = (int)(gid % groups) * 8;
-    const int t1 = seq_end(a.cu, a.n_seq, t);
-    float o[8];
+    const ConvThread ct = conv_thread(a);
+    if (!ct.valid) return;
+    float w[8][kW];
+    load_w8(a, ct.c, w);
+    float row[kW][8];  // row[s] = dacc row t + s
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+    for (int s = 0; s < kW - 1; ++s) {
+        const int src = ct.t_begin + s;
+        if (src < a.T) ld8f(dacc + (int64_t)src * a.conv_dim + ct.c, row[s]);
+        else
 #pragma unroll
-    for (int s = 0; s < kW; ++s) {
-        const int tp = t + s;
-        if (tp >= t1) break;
-        float d[8];
-        ld8f(dacc + (int64_t)tp * a.conv_dim + c, d);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = fmaf(d[i], a.w[(c + i) * kW + (kW - 1 - s)], o[i]);
+            for (int i = 0; i < 8; ++i) row[s][i] = 0.0f;
     }
-    st8(dx + (int64_t)t * lddx + c, o);
+    int sq = 0;
+    while (sq + 1 < a.n_seq && a.cu[sq + 1] <= ct.t_begin) ++sq;
+    int t1 = a.cu[sq + 1];
+#pragma unroll 1
+    for (int k = 0; k < kTB; ++k) {
+        const int t = ct.t_begin + k;
+        if (t >= a.T) break;
+        const int src = t + kW - 1;
+        if (src < a.T) ld8f(dacc + (int64_t)src * a.conv_dim + ct.c, row[kW - 1]);
+        else
+#pragma unroll
+            for (int i = 0; i < 8; ++i) row[kW - 1][i] = 0.0f;
+        while (t >= t1 && sq + 1 < a.n_seq) t1 = a.cu[++sq + 1];
+        float o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+#pragma unroll
+        for (int s = 0; s < kW; ++s) {
+            const bool on = t + s < t1;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) o[i] = fmaf(on ? row[s][i] : 0.0f, w[i][kW - 1 - s], o[i]);
+        }
+        st8(dx + (int64_t)t * lddx + ct.c, o);
+#pragma unroll
+        for (int s = 0; s < kW - 1; ++s)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) row[s][i] = row[s + 1][i];
+    }
 }
 
 // ------------------------------------------------------------------------------------------- gates
@@ -475,7 +553,7 @@ extern "C" int r97b_conv_prep_fwd(const uint16_t* x, int64_t ldx, const float* c
                                   void* stream) {
     if (!x || !conv_w || !cu || !q || !k || !v || T <= 0 || Hg <= 0 || H <= 0 || (ldx % 8) || !al16(x)) return R97B_EINVAL;
     ConvArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, conv_w, cu, n_seq, (int)T, Hg, H, (2 * Hg + H) * 128};
-    conv_prep_fwd_kernel<<<blocks_for(T * (a.conv_dim / 8)), 256, 0, as_stream(stream)>>>(
+    conv_prep_fwd_kernel<<<blocks_for(((T + kTB - 1) / kTB) * (a.conv_dim / 8)), 256, 0, as_stream(stream)>>>(
         a, reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(k), reinterpret_cast<__nv_bfloat16*>(v));
     return launch_status();
 }
@@ -486,7 +564,7 @@ extern "C" int r97b_conv_prep_bwd(const uint16_t* x, int64_t ldx, const float* c
     if (!x || !conv_w || !cu || !dq || !dk || !dv || !dacc || !dx || T <= 0 || (ldx % 8) || (lddx % 8))
         return R97B_EINVAL;
     ConvArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, conv_w, cu, n_seq, (int)T, Hg, H, (2 * Hg + H) * 128};
-    const unsigned blocks = blocks_for(T * (a.conv_dim / 8));
+    const unsigned blocks = blocks_for(((T + kTB - 1) / kTB) * (a.conv_dim / 8));
     conv_prep_dacc_kernel<<<blocks, 256, 0, as_stream(stream)>>>(a, dq, dk, dv, dacc);
     conv_prep_dx_kernel<<<blocks, 256, 0, as_stream(stream)>>>(a, dacc, reinterpret_cast<__nv_bfloat16*>(dx), lddx);
     return launch_status(2);

@@ -167,3 +167,48 @@ def test_scheduled_lr_vs_reference():
         a = lib.ref_scheduled_lr(1e-3, 10, 100, 0.1, step)
         b = R.scheduled_lr(1e-3, 10, 100, 0.1, step)
         assert np.float32(a) == b
+
+
+def _conv_record(T, S, Hg, H, K, W=4):
+    C = 2 * Hg * K + H * K
+    ops = [Operand("x", "bf16", (T, C)), Operand("w", "bf16", (C, W)), Operand("b", "bf16", (C,)),
+           Operand("A_log", "f32", (H,)), Operand("dt_bias", "f32", (H,)),
+           Operand("conv_state", "bf16", (S, C, W - 1), written=True), Operand("cu", "i32", (S + 1,)),
+           Operand("a", "bf16", (T, H)), Operand("b_gate", "bf16", (T, H)), Operand("cache_idx", "i32", (S,)),
+           Operand("has_init", "i32", (S,)), Operand("q", "bf16", (T, Hg, K), written=True),
+           Operand("k", "bf16", (T, Hg, K), written=True), Operand("v", "bf16", (T, H, K), written=True),
+           Operand("g", "f32", (T, H), written=True), Operand("beta", "f32", (T, H), written=True)]
+    return ops, {"head_k": K, "head_v": K, "chunk": 64, "conv_width": W}
+
+
+def test_conv_prep_and_gates_vs_reference():
+    _ref()
+    rs = np.random.RandomState(21)
+    lens, Hg, H, K = (70, 5, 130), 2, 4, 16
+    T, S = sum(lens), len(lens)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int64)
+    C = 2 * Hg * K + H * K
+    x = rs.normal(size=(T, C))
+    w = rs.normal(size=(C, 4)) * 0.5
+    a, bg = rs.normal(size=(T, H)), rs.normal(size=(T, H))
+    a_log, dt_bias = np.log(rs.uniform(1, 16, size=H)), rs.normal(size=H) * 0.1
+    ops, params = _conv_record(T, S, Hg, H, K)
+    reads = {"x": x, "w": w, "b": np.zeros(C), "A_log": a_log, "dt_bias": dt_bias, "cu": cu, "a": a, "b_gate": bg,
+             "cache_idx": np.arange(S), "has_init": np.zeros(S)}
+    out = ref_twin("gdn_conv_prep", params, ops, reads)
+    q, k, v = R.conv_prep_fwd(x, w, cu, Hg, H, K)
+    g, beta = R.gates_fwd(a, bg, a_log, dt_bias, cu)
+    np.testing.assert_allclose(q, out["q"], rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(k, out["k"], rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(v, out["v"], rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(g, out["g"], rtol=1e-10, atol=1e-12)
+    np.testing.assert_allclose(beta, out["beta"], rtol=1e-10, atol=1e-12)
+    dq, dk, dv = rs.normal(size=q.shape), rs.normal(size=k.shape), rs.normal(size=v.shape)
+    dg, db = rs.normal(size=g.shape), rs.normal(size=beta.shape)
+    fwd = dict(reads, conv_state=out["conv_state"], q=out["q"], k=out["k"], v=out["v"], g=out["g"], beta=out["beta"])
+    cots = {"conv_state": np.zeros_like(out["conv_state"]), "q": dq, "k": dk, "v": dv, "g": dg, "beta": db}
+    dc, _ = ref_adjoint("gdn_conv_prep", params, ops, fwd, cots)
+    np.testing.assert_allclose(R.conv_prep_bwd(x, w, cu, Hg, H, dq, dk, dv, K), dc["x"], rtol=1e-9, atol=1e-11)
+    da, dbg = R.gates_bwd(a, bg, a_log, dt_bias, cu, dg, db)
+    np.testing.assert_allclose(da, dc["a"], rtol=1e-9, atol=1e-11)
+    np.testing.assert_allclose(dbg, dc["b_gate"], rtol=1e-9, atol=1e-11)
