@@ -112,14 +112,17 @@ int r97b_rmsnorm_bwd(const uint16_t* x, const float* w, const uint16_t* dy, cons
                      int64_t rows, int64_t n, float eps, float wadd, float mult, void* stream);
 
 /* o = x * rsqrt(mean(x^2) + eps) * w * act(z), act = silu (act_sigmoid = 0) or sigmoid; per row of n.
- * Replaces: the gdn_gated_rmsnorm forward, src/adjoint/host/gdn_prep.cpp:501-531. */
-int r97b_gated_rmsnorm_fwd(const uint16_t* x, const uint16_t* z, const float* w, uint16_t* o, int64_t rows, int64_t n,
-                           float eps, int32_t act_sigmoid, void* stream);
+ * x and o are dense [rows, n]; z (and dz below) may sit inside wider token rows: with z_heads > 0, row r of z
+ * is at (r / z_heads) * z_tok_stride + (r % z_heads) * n (the z columns of a fused projection); z_heads = 0
+ * means dense. Replaces: the gdn_gated_rmsnorm forward, src/adjoint/host/gdn_prep.cpp:501-531. */
+int r97b_gated_rmsnorm_fwd(const uint16_t* x, const uint16_t* z, int64_t z_tok_stride, int32_t z_heads, const float* w,
+                           uint16_t* o, int64_t rows, int64_t n, float eps, int32_t act_sigmoid, void* stream);
 
-/* dx, dz of the gated norm for the cotangent dout. Replaces: gated_rmsnorm_adjoint_kernel,
+/* dx, dz of the gated norm for the cotangent dout (dz laid out like z). Replaces: gated_rmsnorm_adjoint_kernel,
  * src/adjoint/device/gdn_prep.hip:643-731 (host row src/adjoint/host/gdn_prep.cpp:541-592). */
-int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, const float* w, const uint16_t* dout, uint16_t* dx,
-                           uint16_t* dz, int64_t rows, int64_t n, float eps, int32_t act_sigmoid, void* stream);
+int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, int64_t z_tok_stride, int32_t z_heads, const float* w,
+                           const uint16_t* dout, uint16_t* dx, uint16_t* dz, int64_t rows, int64_t n, float eps,
+                           int32_t act_sigmoid, void* stream);
 
 /* ------------------------------------------------------------------------------ loss */
 
@@ -195,7 +198,9 @@ int32_t r97b_gdn_chunk_table(const int32_t* cu_host, int32_t n_seq, int32_t chun
  * Outputs: A f32 [T, H, 64] (the reference's gdn_kkt_solve output, row i of each chunk's (I+M)^-1),
  * w, u f32 [T, H, 128], S f32 [n_chunks, H, 128(k), 128(v)] (the state entering each chunk), Vp f32
  * [T, H, 128], P f32 [n_chunks, H, 64, 64], o bf16 [T, H, 128] and ht f32 [n_seq, H, 128, 128] or null.
- * A, w, S, Vp and P are what the backward reads; u is scratch. */
+ * A, w, S, Vp and P are what the backward reads; u is scratch. w and P are opaque to the caller: they
+ * are kept as bf16 (hi, lo) pairs -- hi = bf16(x), lo = bf16(x - hi), the hi plane first -- in the bytes
+ * of the f32 buffers described here, which are what the tensor-core passes stream. */
 typedef struct R97bGdnFwd {
     const uint16_t *q, *k, *v;
     const float *g, *beta, *h0;

@@ -12,6 +12,14 @@ from __future__ import annotations
 import numpy as np
 
 
+def _decay(gc, k=0):
+    """e^{g_i - g_j} on the lower triangle (j <= i + k), zero above it, without forming the overflowing
+    upper entries."""
+    L = len(gc)
+    low = np.tri(L, k=k, dtype=bool)
+    return np.where(low, np.exp(np.where(low, gc[:, None] - gc[None, :], 0.0)), 0.0)
+
+
 def _chunks(cu, chunk):
     for s in range(len(cu) - 1):
         bos, slen = int(cu[s]), int(cu[s + 1]) - int(cu[s])
@@ -30,7 +38,7 @@ def kkt_fwd(k, beta, g, cu, chunk=64):
             for c0, L in cs:
                 rows = slice(bos + c0, bos + c0 + L)
                 kc, bc, gc = k[rows, h // grp], beta[rows, h], g[rows, h]
-                M = np.tril(bc[:, None] * (kc @ kc.T) * np.exp(gc[:, None] - gc[None, :]), -1)
+                M = bc[:, None] * (kc @ kc.T) * _decay(gc, -1)
                 Ainv = np.linalg.solve(np.eye(L) + M, np.eye(L))
                 A[rows, h, :L] = np.tril(Ainv)
     return A
@@ -53,7 +61,9 @@ def kkt_bwd(k, beta, g, cu, A, dA, chunk=64):
                 Ac = np.tril(dA[rows, h, :L])
                 Y = np.tril(Ac @ Al.T)
                 Et = np.tril(-(Al.T @ Y), -1)
-                phi = np.exp(gc[:, None] - gc[None, :])
+                # e^{g_i - g_l} on the strict lower block only (the reference forms it only there; above the
+                # diagonal it can overflow)
+                phi = _decay(gc, -1)
                 C = (kc @ kc.T) * phi
                 Mm = bc[:, None] * C
                 dbeta[rows, h] += (Et * C).sum(1)
@@ -87,7 +97,7 @@ def scan_fwd(q, k, v, A, g, beta, cu, h0=None, scale=None, chunk=64):
                 ge = np.exp(gc)
                 W = bc[:, None] * (vc - ge[:, None] * (kc @ S))
                 Vp = Ac @ W
-                P = np.tril((qc @ kc.T) * np.exp(gc[:, None] - gc[None, :]))
+                P = (qc @ kc.T) * _decay(gc)
                 o[rows, h] = scale * (ge[:, None] * (qc @ S) + P @ Vp)
                 gl = gc[L - 1]
                 S = np.exp(gl) * S + (kc * np.exp(gl - gc)[:, None]).T @ Vp
@@ -153,7 +163,7 @@ def scan_bwd(q, k, v, A, g, beta, cu, do, dht=None, h0=None, scale=None, chunk=6
                 dqc += E[:, None] * S0oc
                 dgc += E * (qc * S0oc).sum(1)
                 dS0 += (qc * E[:, None]).T @ oc
-                Phi = np.tril(scale * np.exp(gc[:, None] - gc[None, :]))
+                Phi = scale * _decay(gc)
                 QK, VO = qc @ kc.T, oc @ Vp.T
                 dqc += (Phi * VO) @ kc
                 dkc += (Phi * VO).T @ qc

@@ -11,7 +11,7 @@
 // sequential pass whose value lanes are independent:
 //
 //   F1 gdn_fwd_prep  (chunk, head)        M, A by forward substitution, w, u
-//   F2 gdn_fwd_state (seq, head, V/32)    S_c entering each chunk, V'_c = u_c - w_c S_c, S_{c+1}
+//   F2 gdn_fwd_state (seq, head, V/64)    S_c entering each chunk, V'_c = u_c - w_c S_c, S_{c+1}
 //   F3 gdn_fwd_out   (chunk, head)        P = causal(q k^T e^{g_i-g_j}), o = scale (e^g q S_c + P V'_c)
 //   B1 gdn_bwd_state (seq, head, V/32)    reverse pass: dV' = scale P^T dO + K~ dS_next,
 //                                          dS = scale Q~^T dO + e^{g_L} dS_next - w^T dV'
@@ -47,6 +47,7 @@ constexpr int F65 = 65;  // f32 pitch of a [64, 64] tile
 
 struct Dims {
     int n_seq, H, Hg, grp, n_chunks;
+    int64_t T;
     float scale;
     const int* tok0;
     const int* len;
@@ -66,7 +67,7 @@ __device__ __forceinline__ void stage_bf16(bf16* dst, const bf16* src, int64_t t
     }
 }
 
-__device__ __forceinline__ void put_split(bf16* hi, bf16* lo, int at, float x) {
+__device__ __forceinline__ void put_split(bf16* hi, bf16* lo, int64_t at, float x) {
     bf16 h, l;
     split_bf16(x, h, l);
     hi[at] = h;
@@ -206,8 +207,10 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
     float acc[1][8][4];
     acc_zero<16, 64>(acc);
     mma_split_a<16, 64, 64, false, true>(acc, a1h, a1l, kP64, ks, kP128, m0, n0);
+    bf16* w_hi = reinterpret_cast<bf16*>(w);             // w is kept as a bf16 (hi, lo) pair in the
+    bf16* w_lo = w_hi + (int64_t)dm.T * dm.H * D;         // bytes of an f32 [T, H, 128] buffer
     acc_for<16, 64>(acc, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) w[((tok0 + r) * dm.H + h) * D + d] = x;
+        if (r < n) put_split(w_hi, w_lo, ((tok0 + r) * dm.H + h) * D + d, x);
     });
     acc_zero<16, 64>(acc);
     mma_split_a<16, 64, 64, false, true>(acc, a2h, a2l, kP64, vs, kP128, m0, n0);
@@ -216,56 +219,81 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
     });
 }
 
-// F2: per (sequence, value head, 32 value lanes): the state pass over the sequence's chunks.
-// The state slice S[128][32] lives in the f32 accumulators of its own product (S += k^T V'').
+// F2: per (sequence, value head, 64 value lanes): the state pass over the sequence's chunks. The state
+// slice S[128][64] lives in the f32 accumulators of its own product (S += k^T V''); each chunk's operands
+// (w as a bf16 hi/lo pair, k, the u slice, g) stream into a double-buffered stage with cp.async while the
+// previous chunk computes.
+constexpr int VS2 = 64;   // value lanes per forward-state CTA
+constexpr int P64 = 72;   // bf16 pitch of a [*, 64] tile (== kP64)
+constexpr int U68 = 68;   // f32 pitch of the u slice
+
+struct F2Stage {
+    bf16 wh[L * kP128], wl[L * kP128], ks[L * kP128];
+    float us[L * U68];
+    float gs[L];
+};
+
+__device__ __forceinline__ void f2_issue(F2Stage& st, const Dims& dm, const bf16* w_hi, const bf16* w_lo,
+                                         const bf16* k, const float* u, const float* g, int c, int h, int hk, int e0) {
+    const int64_t tok0 = dm.tok0[c];
+    const int n = dm.len[c];
+    for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
+        const int i = idx >> 4, q = (idx & 15) * 8;
+        const bool on = i < n;
+        const int64_t row = on ? tok0 + i : tok0;
+        cp_async16(&st.wh[i * kP128 + q], w_hi + (row * dm.H + h) * D + q, on);
+        cp_async16(&st.wl[i * kP128 + q], w_lo + (row * dm.H + h) * D + q, on);
+        cp_async16(&st.ks[i * kP128 + q], k + (row * dm.Hg + hk) * D + q, on);
+        cp_async16(&st.us[i * U68 + (q >> 1)], u + (row * dm.H + h) * D + e0 + (q >> 1), on);
+    }
+    for (int i = threadIdx.x; i < L; i += blockDim.x) {
+        const bool on = i < n;
+        cp_async4(&st.gs[i], g + ((on ? tok0 + i : tok0) * dm.H + h), on);
+    }
+    cp_async_commit();
+}
+
 __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __restrict__ k, const float* __restrict__ g,
                                                      const float* __restrict__ w, const float* __restrict__ u,
                                                      const float* __restrict__ h0, float* __restrict__ S_all,
                                                      float* __restrict__ Vp, float* __restrict__ ht) {
     extern __shared__ __align__(16) unsigned char smraw[];
-    bf16* sh = reinterpret_cast<bf16*>(smraw);   // S hi/lo [128][40]
-    bf16* sl = sh + D * P32;
-    bf16* wh = sl + D * P32;                     // w hi/lo [64][136]
-    bf16* wl = wh + L * kP128;
-    bf16* ks = wl + L * kP128;                   // k [64][136]
-    bf16* vh = ks + L * kP128;                   // V'' = e^{gL-g} V' hi/lo [64][40]
-    bf16* vl = vh + L * P32;
-    float* us = reinterpret_cast<float*>(vl + L * P32);  // u slice [64][33]
-    float* gs = us + L * 33;
-    const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VS, hk = h / dm.grp;
+    F2Stage* stage = reinterpret_cast<F2Stage*>(smraw);           // [2]
+    bf16* sh = reinterpret_cast<bf16*>(smraw + 2 * sizeof(F2Stage));  // S hi/lo [128][72]
+    bf16* sl = sh + D * P64;
+    bf16* vh = sl + D * P64;                                       // V'' = e^{gL-g} V' hi/lo [64][72]
+    bf16* vl = vh + L * P64;
+    const bf16* w_hi = reinterpret_cast<const bf16*>(w);
+    const bf16* w_lo = w_hi + dm.T * dm.H * D;
+    const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VS2, hk = h / dm.grp;
     const int warp = threadIdx.x >> 5;
-    const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 16;  // this warp's S tile
-    const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 16;  // this warp's V' tile
-    float S[2][2][4];
-    acc_for<32, 16>(S, sm0, sn0, [&](int d, int e, float& x) {
-        x = h0 ? h0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
-    });
+    const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 32;  // this warp's S tile (32 x 32)
+    const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 32;  // this warp's V' tile (16 x 32)
     const int c0 = dm.seq_c0[seq], c1 = dm.seq_c0[seq + 1];
+    if (c0 < c1) f2_issue(stage[0], dm, w_hi, w_lo, k, u, g, c0, h, hk, e0);
+    float S[2][4][4];
+    acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) {
+        x = h0 ? h0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
+        put_split(sh, sl, d * P64 + e, x);
+    });
     for (int c = c0; c < c1; ++c) {
+        F2Stage& st = stage[(c - c0) & 1];
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
         float* Sg = S_all + ((int64_t)c * dm.H + h) * D * D;
-        acc_for<32, 16>(S, sm0, sn0, [&](int d, int e, float& x) {
-            Sg[d * D + e0 + e] = x;
-            put_split(sh, sl, d * P32 + e, x);
-        });
-        stage_f32_split(wh, wl, w, tok0, n, dm.H, h);
-        stage_bf16(ks, k, tok0, n, dm.Hg, hk);
-        for (int idx = threadIdx.x; idx < L * VS; idx += blockDim.x) {
-            const int i = idx >> 5, e = idx & 31;
-            us[i * 33 + e] = i < n ? u[((tok0 + i) * dm.H + h) * D + e0 + e] : 0.0f;
-        }
-        load_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
-        __syncthreads();
-        const float gl = gs[n - 1];
+        acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) { Sg[d * D + e0 + e] = x; });
+        cp_async_wait_all();
+        __syncthreads();  // stage c landed; S split written; every warp is past chunk c-1's products
+        if (c + 1 < c1) f2_issue(stage[(c + 1 - c0) & 1], dm, w_hi, w_lo, k, u, g, c + 1, h, hk, e0);
+        const float gl = st.gs[n - 1];
         {
-            float acc[1][2][4];
-            acc_zero<16, 16>(acc);
-            mma_split_ab<16, 16, 128, false, true>(acc, wh, wl, kP128, sh, sl, P32, vm0, vn0);
-            acc_for<16, 16>(acc, vm0, vn0, [&](int i, int e, float& x) {
-                const float vp = us[i * 33 + e] - x;
+            float acc[1][4][4];
+            acc_zero<16, 32>(acc);
+            mma_split_ab<16, 32, 128, false, true>(acc, st.wh, st.wl, kP128, sh, sl, P64, vm0, vn0);
+            acc_for<16, 32>(acc, vm0, vn0, [&](int i, int e, float& x) {
+                const float vp = st.us[i * U68 + e] - x;
                 if (i < n) Vp[((tok0 + i) * dm.H + h) * D + e0 + e] = vp;
-                put_split(vh, vl, i * P32 + e, i < n ? vp * expf(gl - gs[i]) : 0.0f);
+                put_split(vh, vl, i * P64 + e, i < n ? vp * expf(gl - st.gs[i]) : 0.0f);
             });
         }
         __syncthreads();
@@ -273,14 +301,15 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
 #pragma unroll
         for (int a = 0; a < 2; ++a)
 #pragma unroll
-            for (int b = 0; b < 2; ++b)
+            for (int b = 0; b < 4; ++b)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) S[a][b][e] *= el;
-        mma_split_b<32, 16, 64, true, true>(S, ks, kP128, vh, vl, P32, sm0, sn0);
-        __syncthreads();
+        mma_split_b<32, 32, 64, true, true>(S, st.ks, kP128, vh, vl, P64, sm0, sn0);
+        // the next chunk's S operand (sh/sl were last read before the sync above)
+        acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) { put_split(sh, sl, d * P64 + e, x); });
     }
     if (ht)
-        acc_for<32, 16>(S, sm0, sn0, [&](int d, int e, float& x) {
+        acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) {
             ht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] = x;
         });
 }
@@ -315,10 +344,13 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
         acc_zero<16, 32>(acc);
         const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
         warp_mma<16, 32, 128, false, false>(acc, qs, kP128, ks, kP128, m0, n0);
-        float* Pg = P_all + ((int64_t)c * dm.H + h) * L * L;
+        // P is kept as a bf16 (hi, lo) pair in the bytes of an f32 [chunks, H, 64, 64] buffer
+        bf16* P_hi = reinterpret_cast<bf16*>(P_all);
+        bf16* P_lo = P_hi + (int64_t)dm.n_chunks * dm.H * L * L;
+        const int64_t pbase = ((int64_t)c * dm.H + h) * L * L;
         acc_for<16, 32>(acc, m0, n0, [&](int r, int l, float& x) {
             const float p = (l <= r && r < n) ? x * expf(gs[r] - gs[l]) : 0.0f;
-            Pg[r * L + l] = p;
+            put_split(P_hi, P_lo, pbase + r * L + l, p);
             put_split(ph, pl, r * kP64 + l, p);
         });
     }
@@ -340,66 +372,96 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
 // ============================================================================================ backward
 
 // B1: per (sequence, value head, 32 value lanes): the reverse state pass; dS lives in the accumulators.
+// Each chunk's operands (P and w as bf16 hi/lo pairs, q, k, the dO slice, g) stream into a double-buffered
+// stage with cp.async while the following chunk computes.
+struct B1Stage {
+    bf16 ph[L * kP64], pl[L * kP64];
+    bf16 ks[L * kP128], qs[L * kP128], wh[L * kP128], wl[L * kP128];
+    bf16 dos[L * P32];
+    float gs[L];
+};
+
+__device__ __forceinline__ void b1_issue(B1Stage& st, const Dims& dm, const bf16* q, const bf16* k, const bf16* w_hi,
+                                         const bf16* w_lo, const bf16* P_hi, const bf16* P_lo, const bf16* dO,
+                                         const float* g, int c, int h, int hk, int e0) {
+    const int64_t tok0 = dm.tok0[c];
+    const int n = dm.len[c];
+    const int64_t pbase = ((int64_t)c * dm.H + h) * L * L;
+    for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
+        const int i = idx >> 4, x = (idx & 15) * 8;
+        const bool on = i < n;
+        const int64_t row = on ? tok0 + i : tok0;
+        cp_async16(&st.ks[i * kP128 + x], k + (row * dm.Hg + hk) * D + x, on);
+        cp_async16(&st.qs[i * kP128 + x], q + (row * dm.Hg + hk) * D + x, on);
+        cp_async16(&st.wh[i * kP128 + x], w_hi + (row * dm.H + h) * D + x, on);
+        cp_async16(&st.wl[i * kP128 + x], w_lo + (row * dm.H + h) * D + x, on);
+        if (x < L) {
+            cp_async16(&st.ph[i * kP64 + x], P_hi + pbase + i * L + x, true);
+            cp_async16(&st.pl[i * kP64 + x], P_lo + pbase + i * L + x, true);
+        }
+        if (x < VS) cp_async16(&st.dos[i * P32 + x], dO + (row * dm.H + h) * D + e0 + x, on);
+    }
+    for (int i = threadIdx.x; i < L; i += blockDim.x) {
+        const bool on = i < n;
+        cp_async4(&st.gs[i], g + ((on ? tok0 + i : tok0) * dm.H + h), on);
+    }
+    cp_async_commit();
+}
+
 __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                      const float* __restrict__ g, const float* __restrict__ w,
                                                      const float* __restrict__ P_all, const bf16* __restrict__ dO,
                                                      const float* __restrict__ dht, float* __restrict__ dS_all,
                                                      float* __restrict__ dVp, float* __restrict__ dh0) {
     extern __shared__ __align__(16) unsigned char smraw[];
-    bf16* dsh = reinterpret_cast<bf16*>(smraw);  // dS hi/lo [128][40]
+    B1Stage* stage = reinterpret_cast<B1Stage*>(smraw);              // [2]
+    bf16* dsh = reinterpret_cast<bf16*>(smraw + 2 * sizeof(B1Stage));  // dS hi/lo [128][40]
     bf16* dsl = dsh + D * P32;
-    bf16* ph = dsl + D * P32;                    // P hi/lo [64][72]
-    bf16* pl = ph + L * kP64;
-    bf16* ks = pl + L * kP64;                    // k [64][136]
-    bf16* qs = ks + L * kP128;                   // q [64][136]
-    bf16* wh = qs + L * kP128;                   // w hi/lo [64][136]
-    bf16* wl = wh + L * kP128;
-    bf16* dos = wl + L * kP128;                  // dO slice [64][40] (bf16, exact)
-    bf16* egh = dos + L * P32;                   // e^g dO hi/lo [64][40]
+    bf16* egh = dsl + D * P32;                                         // e^g dO hi/lo [64][40]
     bf16* egl = egh + L * P32;
-    bf16* dvh = egl + L * P32;                   // dV' hi/lo [64][40]
+    bf16* dvh = egl + L * P32;                                         // dV' hi/lo [64][40]
     bf16* dvl = dvh + L * P32;
-    float* gs = reinterpret_cast<float*>(dvl + L * P32);
+    const bf16* w_hi = reinterpret_cast<const bf16*>(w);
+    const bf16* w_lo = w_hi + dm.T * dm.H * D;
+    const bf16* P_hi = reinterpret_cast<const bf16*>(P_all);
+    const bf16* P_lo = P_hi + (int64_t)dm.n_chunks * dm.H * L * L;
     const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VS, hk = h / dm.grp;
     const int warp = threadIdx.x >> 5;
     const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 16;
     const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 16;
+    const int c0 = dm.seq_c0[seq], c1 = dm.seq_c0[seq + 1];
+    if (c0 < c1) b1_issue(stage[0], dm, q, k, w_hi, w_lo, P_hi, P_lo, dO, g, c1 - 1, h, hk, e0);
     float dS[2][2][4];
     acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
         x = dht ? dht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
     });
-    const int c0 = dm.seq_c0[seq], c1 = dm.seq_c0[seq + 1];
     for (int c = c1 - 1; c >= c0; --c) {
+        B1Stage& st = stage[(c1 - 1 - c) & 1];
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
         float* dSg = dS_all + ((int64_t)c * dm.H + h) * D * D;
+        // dsh/dsl were last read by the previous chunk's dV' products, which precede its middle barrier
         acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
             dSg[d * D + e0 + e] = x;
             put_split(dsh, dsl, d * P32 + e, x);
         });
-        load_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
-        stage_mat_split<L, L>(ph, pl, kP64, P_all + ((int64_t)c * dm.H + h) * L * L);
-        stage_bf16(ks, k, tok0, n, dm.Hg, hk);
-        stage_bf16(qs, q, tok0, n, dm.Hg, hk);
-        stage_f32_split(wh, wl, w, tok0, n, dm.H, h);
-        __syncthreads();
+        cp_async_wait_all();
+        __syncthreads();  // stage c landed; dS split written; every warp is past chunk c+1's products
+        if (c > c0) b1_issue(stage[(c1 - c) & 1], dm, q, k, w_hi, w_lo, P_hi, P_lo, dO, g, c - 1, h, hk, e0);
+        const float gl = st.gs[n - 1];
         for (int idx = threadIdx.x; idx < L * VS; idx += blockDim.x) {
             const int i = idx >> 5, e = idx & 31;
-            const bf16 x = i < n ? dO[((tok0 + i) * dm.H + h) * D + e0 + e] : __float2bfloat16_rn(0.0f);
-            dos[i * P32 + e] = x;
-            put_split(egh, egl, i * P32 + e, __bfloat162float(x) * expf(gs[i]));
+            put_split(egh, egl, i * P32 + e, __bfloat162float(st.dos[i * P32 + e]) * expf(st.gs[i]));
         }
-        __syncthreads();
-        const float gl = gs[n - 1];
         {
             // dV' = scale P^T dO + e^{gL - g} (k dS)
             float a1[1][2][4], a2[1][2][4];
             acc_zero<16, 16>(a1);
             acc_zero<16, 16>(a2);
-            mma_split_a<16, 16, 64, true, true>(a1, ph, pl, kP64, dos, P32, vm0, vn0);
-            mma_split_b<16, 16, 128, false, true>(a2, ks, kP128, dsh, dsl, P32, vm0, vn0);
-            acc_walk<16, 16>(vm0, vn0, [&](int j, int e, int a, int b, int q) {
-                const float dv = j < n ? dm.scale * a1[a][b][q] + expf(gl - gs[j]) * a2[a][b][q] : 0.0f;
+            mma_split_a<16, 16, 64, true, true>(a1, st.ph, st.pl, kP64, st.dos, P32, vm0, vn0);
+            mma_split_b<16, 16, 128, false, true>(a2, st.ks, kP128, dsh, dsl, P32, vm0, vn0);
+            acc_walk<16, 16>(vm0, vn0, [&](int j, int e, int a, int b, int x) {
+                const float dv = j < n ? dm.scale * a1[a][b][x] + expf(gl - st.gs[j]) * a2[a][b][x] : 0.0f;
                 if (j < n) dVp[((tok0 + j) * dm.H + h) * D + e0 + e] = dv;
                 put_split(dvh, dvl, j * P32 + e, dv);
             });
@@ -410,15 +472,14 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
         float t1[2][2][4], t2[2][2][4];
         acc_zero<32, 16>(t1);
         acc_zero<32, 16>(t2);
-        mma_split_b<32, 16, 64, true, true>(t1, qs, kP128, egh, egl, P32, sm0, sn0);
-        mma_split_ab<32, 16, 64, true, true>(t2, wh, wl, kP128, dvh, dvl, P32, sm0, sn0);
+        mma_split_b<32, 16, 64, true, true>(t1, st.qs, kP128, egh, egl, P32, sm0, sn0);
+        mma_split_ab<32, 16, 64, true, true>(t2, st.wh, st.wl, kP128, dvh, dvl, P32, sm0, sn0);
 #pragma unroll
         for (int a = 0; a < 2; ++a)
 #pragma unroll
             for (int b = 0; b < 2; ++b)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) dS[a][b][e] = el * dS[a][b][e] + dm.scale * t1[a][b][e] - t2[a][b][e];
-        __syncthreads();
     }
     if (dh0)
         acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
@@ -596,8 +657,10 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
         mma_split_b<16, 32, 128, false, false>(dp, dos, kP128, xh, xl, kP128, pm0, pn0);
         float r0 = 0.0f, r1 = 0.0f;
         acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
-            const float phi = expf(gs[r] - gs[l]);
             const bool on = l <= r && r < n;
+            // e^{g_r - g_l} only where l <= r: above the diagonal it can overflow (g decreases within a
+            // chunk), and 0 * inf would poison the sums
+            const float phi = on ? expf(gs[r] - gs[l]) : 0.0f;
             const float dpv = on ? dm.scale * dp[i][j][q] : 0.0f;
             const float dd = dpv * qk[i][j][q] * phi;
             if (q >> 1) r1 += dd; else r0 += dd;
@@ -749,9 +812,9 @@ __global__ void gdn_sum_heads_kernel(const float* __restrict__ src, float* __res
 }
 
 constexpr size_t kSmemPrep = (2 * L * kP128 + 4 * L * kP64) * 2 + (2 * L * F65 + 4 * L + 2 * L) * 4;
-constexpr size_t kSmemState = (2 * D * P32 + 3 * L * kP128 + 2 * L * P32) * 2 + (L * 33 + L) * 4;
+constexpr size_t kSmemState = 2 * sizeof(F2Stage) + (2 * D * P64 + 2 * L * P64) * 2;
 constexpr size_t kSmemOut = (4 * L * kP128 + 2 * D * kP128 + 2 * L * kP64) * 2 + L * 4;
-constexpr size_t kSmemBState = (2 * D * P32 + 2 * L * kP64 + 4 * L * kP128 + 5 * L * P32) * 2 + L * 4;
+constexpr size_t kSmemBState = 2 * sizeof(B1Stage) + (2 * D * P32 + 4 * L * P32) * 2;
 constexpr size_t kSmemBA = (2 * D * kP128 + 4 * L * kP128) * 2 + (2 * L + 8) * 4;
 constexpr size_t kSmemBB = (7 * L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 
@@ -774,7 +837,7 @@ bool dims_ok(const R97bGdnDims& d) {
 }
 
 Dims to_dims(const R97bGdnDims& d) {
-    return Dims{d.n_seq, d.H, d.Hg, d.H / d.Hg, d.n_chunks, d.scale, d.chunk_tok0, d.chunk_len, d.seq_chunk0};
+    return Dims{d.n_seq, d.H, d.Hg, d.H / d.Hg, d.n_chunks, d.T, d.scale, d.chunk_tok0, d.chunk_len, d.seq_chunk0};
 }
 
 }  // namespace
@@ -811,7 +874,7 @@ extern "C" int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* a, void* 
     const auto* v = reinterpret_cast<const bf16*>(a->v);
     if (dm.n_chunks > 0)
         gdn_fwd_prep<<<dim3(dm.n_chunks, dm.H), 256, kSmemPrep, s>>>(dm, k, v, a->g, a->beta, a->A, a->w, a->u);
-    gdn_fwd_state<<<dim3(dm.n_seq, dm.H, D / VS), 256, kSmemState, s>>>(dm, k, a->g, a->w, a->u, a->h0, a->S, a->Vp,
+    gdn_fwd_state<<<dim3(dm.n_seq, dm.H, D / VS2), 256, kSmemState, s>>>(dm, k, a->g, a->w, a->u, a->h0, a->S, a->Vp,
                                                                        a->ht);
     if (dm.n_chunks > 0)
         gdn_fwd_out<<<dim3(dm.n_chunks, dm.H), 256, kSmemOut, s>>>(dm, q, k, a->g, a->S, a->Vp, a->P,

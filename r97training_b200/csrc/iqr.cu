@@ -224,12 +224,31 @@ __global__ void __launch_bounds__(256) iqr_decode_u4(const R97IqrDecodeDesc d, c
     }
     const uint32_t A = d.mad_a, B = d.mad_b;
     const int64_t kb = j0 >> 7;
+    // rows in batches of 8: the batch's code words and scales are all requested before the first row's
+    // arithmetic, so eight loads are in flight per thread instead of one
+    constexpr int kBatch = 8;
+    uint32_t wb[kBatch];
+    float sb8[kBatch];
     for (int64_t r = sr0; r < sr1; ++r) {
-        const uint32_t w = word(r);
-        const float sc = d.scale_dtype == R97_IQR_F32
-                             ? reinterpret_cast<const float*>(d.scale + (r - d.row0) * d.scale_row_bytes)[kb]
-                             : bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(
-                                   d.scale + (r - d.row0) * d.scale_row_bytes)[kb]);
+        const int bi = (int)((r - sr0) & (kBatch - 1));
+        if (bi == 0) {
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) {
+                const int64_t rr = r + b < sr1 ? r + b : sr1 - 1;
+                wb[b] = word(rr);
+                const uint8_t* srow = d.scale + (rr - d.row0) * d.scale_row_bytes;
+                sb8[b] = d.scale_dtype == R97_IQR_F32 ? reinterpret_cast<const float*>(srow)[kb]
+                                                      : bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(srow)[kb]);
+            }
+        }
+        uint32_t w = wb[0];
+        float sc = sb8[0];
+#pragma unroll
+        for (int b = 1; b < kBatch; ++b)
+            if (bi == b) {
+                w = wb[b];
+                sc = sb8[b];
+            }
         int32_t v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {

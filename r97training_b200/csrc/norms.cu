@@ -126,11 +126,17 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
     }
 }
 
+// z rows may live inside a wider token row: row r of z is at (r / zh) * zts + (r % zh) * n when zh > 0
+__device__ __forceinline__ int64_t zrow(int64_t r, int n, int64_t zts, int zh) {
+    return zh > 0 ? (r / zh) * zts + (r % zh) * (int64_t)n : r * (int64_t)n;
+}
+
 template <int W>
 __global__ void __launch_bounds__(256) gated_rmsnorm_fwd_kernel(const __nv_bfloat16* __restrict__ x,
                                                                 const __nv_bfloat16* __restrict__ z,
                                                                 const float* __restrict__ w, __nv_bfloat16* __restrict__ o,
-                                                                int64_t rows, int n, float eps, int sig) {
+                                                                int64_t rows, int n, float eps, int sig, int64_t zts,
+                                                                int zh) {
     const int lane = threadIdx.x & (W - 1);
     const int64_t grow = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / W;
     // lanes past the last row still join the shuffles, on a clamped row, and store nothing
@@ -148,7 +154,7 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_fwd_kernel(const __nv_bfloa
     for (int c = lane * 8; c < n; c += W * 8) {
         float v[8], zz[8], g[8];
         load8(x + row * n + c, v);
-        load8(z + row * n + c, zz);
+        load8(z + zrow(row, n, zts, zh) + c, zz);
         loadw8(w + c, g);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -165,7 +171,8 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_bwd_kernel(const __nv_bfloa
                                                                 const float* __restrict__ w,
                                                                 const __nv_bfloat16* __restrict__ dout,
                                                                 __nv_bfloat16* __restrict__ dx, __nv_bfloat16* __restrict__ dz,
-                                                                int64_t rows, int n, float eps, int sig) {
+                                                                int64_t rows, int n, float eps, int sig, int64_t zts,
+                                                                int zh) {
     const int lane = threadIdx.x & (W - 1);
     const int64_t grow = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / W;
     // lanes past the last row still join the shuffles, on a clamped row, and store nothing
@@ -175,7 +182,7 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_bwd_kernel(const __nv_bfloa
     for (int c = lane * 8; c < n; c += W * 8) {
         float v[8], zz[8], g[8], d[8];
         load8(x + row * n + c, v);
-        load8(z + row * n + c, zz);
+        load8(z + zrow(row, n, zts, zh) + c, zz);
         load8(dout + row * n + c, d);
         loadw8(w + c, g);
 #pragma unroll
@@ -193,7 +200,7 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_bwd_kernel(const __nv_bfloa
     for (int c = lane * 8; c < n; c += W * 8) {
         float v[8], zz[8], g[8], d[8], ox[8], oz[8];
         load8(x + row * n + c, v);
-        load8(z + row * n + c, zz);
+        load8(z + zrow(row, n, zts, zh) + c, zz);
         load8(dout + row * n + c, d);
         loadw8(w + c, g);
 #pragma unroll
@@ -206,7 +213,7 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_bwd_kernel(const __nv_bfloa
         }
         if (valid) {
             store8(dx + row * n + c, ox);
-            store8(dz + row * n + c, oz);
+            store8(dz + zrow(row, n, zts, zh) + c, oz);
         }
     }
 }
@@ -265,8 +272,10 @@ extern "C" int r97b_rmsnorm_bwd(const uint16_t* x, const float* w, const uint16_
     return launch_status();
 }
 
-extern "C" int r97b_gated_rmsnorm_fwd(const uint16_t* x, const uint16_t* z, const float* w, uint16_t* o, int64_t rows,
-                                      int64_t n, float eps, int32_t act_sigmoid, void* stream) {
+extern "C" int r97b_gated_rmsnorm_fwd(const uint16_t* x, const uint16_t* z, int64_t z_tok_stride, int32_t z_heads,
+                                      const float* w, uint16_t* o, int64_t rows, int64_t n, float eps,
+                                      int32_t act_sigmoid, void* stream) {
+    if (z_heads < 0 || (z_heads > 0 && (rows % z_heads || z_tok_stride % 8))) return R97B_EINVAL;
     if (!x || !z || !w || !o || rows <= 0 || n <= 0 || n % 8 || !aligned16(x) || !aligned16(z) || !aligned16(w) ||
         !aligned16(o))
         return R97B_EINVAL;
@@ -275,13 +284,15 @@ extern "C" int r97b_gated_rmsnorm_fwd(const uint16_t* x, const uint16_t* z, cons
     const unsigned blocks = (unsigned)((threads + 255) / 256);
     R97B_DISPATCH_W(W, (gated_rmsnorm_fwd_kernel<kW><<<blocks, 256, 0, as_stream(stream)>>>(
                             reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(z), w,
-                            reinterpret_cast<__nv_bfloat16*>(o), rows, (int)n, eps, act_sigmoid)));
+                            reinterpret_cast<__nv_bfloat16*>(o), rows, (int)n, eps, act_sigmoid, z_tok_stride,
+                            z_heads)));
     return launch_status();
 }
 
-extern "C" int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, const float* w, const uint16_t* dout,
-                                      uint16_t* dx, uint16_t* dz, int64_t rows, int64_t n, float eps,
-                                      int32_t act_sigmoid, void* stream) {
+extern "C" int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, int64_t z_tok_stride, int32_t z_heads,
+                                      const float* w, const uint16_t* dout, uint16_t* dx, uint16_t* dz, int64_t rows,
+                                      int64_t n, float eps, int32_t act_sigmoid, void* stream) {
+    if (z_heads < 0 || (z_heads > 0 && (rows % z_heads || z_tok_stride % 8))) return R97B_EINVAL;
     if (!x || !z || !w || !dout || !dx || !dz || rows <= 0 || n <= 0 || n % 8 || !aligned16(x) || !aligned16(z) ||
         !aligned16(w) || !aligned16(dout) || !aligned16(dx) || !aligned16(dz))
         return R97B_EINVAL;
@@ -291,6 +302,7 @@ extern "C" int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, cons
     R97B_DISPATCH_W(W, (gated_rmsnorm_bwd_kernel<kW><<<blocks, 256, 0, as_stream(stream)>>>(
                             reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(z), w,
                             reinterpret_cast<const __nv_bfloat16*>(dout), reinterpret_cast<__nv_bfloat16*>(dx),
-                            reinterpret_cast<__nv_bfloat16*>(dz), rows, (int)n, eps, act_sigmoid)));
+                            reinterpret_cast<__nv_bfloat16*>(dz), rows, (int)n, eps, act_sigmoid, z_tok_stride,
+                            z_heads)));
     return launch_status();
 }

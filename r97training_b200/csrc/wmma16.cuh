@@ -125,6 +125,20 @@ __device__ __forceinline__ void acc_walk(int m0, int n0, F&& fn) {
             for (int e = 0; e < 4; ++e) fn(m0 + 16 * i + g + ((e >> 1) << 3), n0 + 8 * j + 2 * t + (e & 1), i, j, e);
 }
 
+// ------------------------------------------------------------------- asynchronous global -> shared copies
+// cp.async with a source size of 0 writes zeros (rows past a chunk's end); `src` must still be a valid
+// address, so callers clamp it.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool pred) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s_addr(dst)), "l"(src), "r"(pred ? 16 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async4(void* dst, const void* src, bool pred) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"(s_addr(dst)), "l"(src), "r"(pred ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+
 // x -> (hi, lo) bf16 pair with hi + lo ~ x to about 16 bits
 __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
     hi = __float2bfloat16_rn(x);

@@ -341,9 +341,8 @@ class TrainStep:
         ba = y_in[:, 2 * qk + 2 * H * K:]
         ops.gates_fwd(ba, blk["a_log"], blk["dt_bias"], self.plan, gg, beta)
         o, _, gsv = self.plan.forward(q, k, v, gg, beta)
-        z = y_in[:, 2 * qk + H * K:2 * qk + 2 * H * K]
-        on = ops.gated_rmsnorm_fwd(o.view(T * H, K), z.reshape(T * H, K) if z.is_contiguous() else
-                                   z.contiguous().view(T * H, K), blk["gnorm_w"], eps=cfg.eps).view(T, H * K)
+        z = y_in[:, 2 * qk + H * K:2 * qk + 2 * H * K]  # read in place (strided), no copy
+        on = ops.gated_rmsnorm_fwd(o.view(T * H, K), z, blk["gnorm_w"], eps=cfg.eps).view(T, H * K)
         W = decode_group(g_out, self.ws.w_scratch)
         h1 = torch.empty_like(x)
         t_out = self._lin_fwd(li, g_out, on, W, h1, addend=x)
@@ -359,13 +358,12 @@ class TrainStep:
         don = torch.empty((T, H * K), dtype=torch.bfloat16, device=x.device)
         self._lin_bwd(li, g_out, sv["on"], sv["t_out"], W, dh1, don)
         y_in = sv["y_in"]
-        z = y_in[:, 2 * qk + H * K:2 * qk + 2 * H * K].contiguous()
+        zsl = slice(2 * qk + H * K, 2 * qk + 2 * H * K)
         d_yin = torch.empty_like(y_in)
         do = torch.empty((T, H, K), dtype=torch.bfloat16, device=x.device)
-        dz = torch.empty((T * H, K), dtype=torch.bfloat16, device=x.device)
-        ops.gated_rmsnorm_bwd(sv["o"].view(T * H, K), z.view(T * H, K), blk["gnorm_w"], don.view(T * H, K),
-                              eps=cfg.eps, dx=do.view(T * H, K), dz=dz)
-        d_yin[:, 2 * qk + H * K:2 * qk + 2 * H * K].copy_(dz.view(T, H * K))
+        # dz lands straight in its columns of the projection's cotangent
+        ops.gated_rmsnorm_bwd(sv["o"].view(T * H, K), y_in[:, zsl], blk["gnorm_w"], don.view(T * H, K),
+                              eps=cfg.eps, dx=do.view(T * H, K), dz=d_yin[:, zsl])
         gr = self.plan.backward(sv["gsv"], do)
         dacc = torch.empty((T, 2 * qk + H * K), dtype=torch.float32, device=x.device)
         ops.conv_prep_bwd(y_in, blk["conv_w"], self.cu_dev, self.plan.n_seq, Hg, H, gr["dq"], gr["dk"], gr["dv"],

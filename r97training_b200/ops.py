@@ -122,22 +122,36 @@ def rmsnorm_bwd(x, w, dy, *, addend=None, eps=1e-6, wadd=0.0, mult=1.0, out=None
     return out
 
 
+def _z_layout(z, n, rows):
+    """(token stride, heads per token) of z: dense rows of n, or a [T, heads * n] column slice of a wider row."""
+    if z.dim() == 2 and z.shape[1] != n and z.stride(1) == 1:
+        heads = z.shape[1] // n
+        return z.stride(0), heads
+    return 0, 0
+
+
 def gated_rmsnorm_fwd(x, z, w, *, eps=1e-6, sigmoid=False, out=None, stream=None):
+    """x dense [rows, n]; z either dense like x or a [T, heads * n] view (row r = token r // heads)."""
     n = x.shape[-1]
     rows = x.numel() // n
+    zts, zh = _z_layout(z, n, rows)
     out = torch.empty_like(x) if out is None else out
-    check(lib().r97b_gated_rmsnorm_fwd(_ptr(x), _ptr(z), _ptr(w), _ptr(out), rows, n, eps, int(sigmoid),
+    check(lib().r97b_gated_rmsnorm_fwd(_ptr(x), _ptr(z), zts, zh, _ptr(w), _ptr(out), rows, n, eps, int(sigmoid),
                                        _stream(stream)), "r97b_gated_rmsnorm_fwd")
     return out
 
 
 def gated_rmsnorm_bwd(x, z, w, dout, *, eps=1e-6, sigmoid=False, dx=None, dz=None, stream=None):
+    """dz has z's layout (dense, or the same column slice of a wider buffer)."""
     n = x.shape[-1]
     rows = x.numel() // n
+    zts, zh = _z_layout(z, n, rows)
     dx = torch.empty_like(x) if dx is None else dx
     dz = torch.empty_like(z) if dz is None else dz
-    check(lib().r97b_gated_rmsnorm_bwd(_ptr(x), _ptr(z), _ptr(w), _ptr(dout), _ptr(dx), _ptr(dz), rows, n, eps,
-                                       int(sigmoid), _stream(stream)), "r97b_gated_rmsnorm_bwd")
+    if zh and (dz.stride(0) != zts):
+        raise R97bError("dz must share z's token stride")
+    check(lib().r97b_gated_rmsnorm_bwd(_ptr(x), _ptr(z), zts, zh, _ptr(w), _ptr(dout), _ptr(dx), _ptr(dz), rows, n,
+                                       eps, int(sigmoid), _stream(stream)), "r97b_gated_rmsnorm_bwd")
     return dx, dz
 
 

@@ -17,10 +17,13 @@ def _bf16(x):
     return torch.from_numpy(np.asarray(x, np.float32)).to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("lens,H,Hg,states", [((64,), 2, 2, False), ((200, 64, 1, 130), 4, 2, True),
-                                              ((512,), 4, 4, False)])
-def test_gdn_fwd_bwd_vs_oracle(cuda, lens, H, Hg, states):
+@pytest.mark.parametrize("lens,H,Hg,states,decay", [((64,), 2, 2, False, 1.0), ((200, 64, 1, 130), 4, 2, True, 1.0),
+                                                    ((512,), 4, 4, False, 1.0), ((300, 64), 4, 2, True, 40.0)])
+def test_gdn_fwd_bwd_vs_oracle(cuda, lens, H, Hg, states, decay):
+    """decay scales the per-token log decay: 40 drives e^{g_i - g_j} far past f32's range above the
+    diagonal (where it must never be formed) and to zero below it."""
     d = G.synth_inputs(list(lens), H, Hg, seed=sum(lens) + H)
+    d["g"] = d["g"] * decay
     q, k, v, do = (_bf16(d[n]) for n in ("q", "k", "v", "do"))
     # the oracle sees exactly the bf16 values the kernels read
     qn, kn, vn, don = (t.double().numpy() for t in (q, k, v, do))

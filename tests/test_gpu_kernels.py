@@ -234,3 +234,26 @@ def test_global_norm_and_clip(cuda):
     want = np.float32(np.sqrt(np.sum(parts)))
     assert abs(float(norm) - float(want)) <= 1e-6 * float(want)
     assert abs(float(scale) - min(1.0, 0.5 / float(want))) < 1e-6
+
+
+def test_gated_rmsnorm_strided_z(cuda):
+    """z read from (and dz written into) the z columns of a wider fused projection row."""
+    rs = np.random.RandomState(10)
+    T, H, n, pad = 257, 4, 128, 96
+    x, do = _bf(rs, (T * H, n)), _bf(rs, (T * H, n), 1e-2)
+    wide = _bf(rs, (T, pad + H * n + 64))
+    w = torch.from_numpy(rs.normal(size=n).astype(np.float32))
+    wd = wide.to(cuda)
+    zs = wd[:, pad:pad + H * n]
+    o = ops.gated_rmsnorm_fwd(x.to(cuda), zs, w.to(cuda))
+    dwide = torch.zeros_like(wd)
+    dx, _ = ops.gated_rmsnorm_bwd(x.to(cuda), zs, w.to(cuda), do.to(cuda), dz=dwide[:, pad:pad + H * n])
+    torch.cuda.synchronize()
+    zn = wide.double().numpy()[:, pad:pad + H * n].reshape(T * H, n)
+    xn, wn, don = x.double().numpy(), w.double().numpy(), do.double().numpy()
+    assert_close_bf16(to_np(o), R.gated_rmsnorm_fwd(xn, zn, wn), rel=5e-3, what="o")
+    rdx, rdz = R.gated_rmsnorm_bwd(xn, zn, wn, don)
+    assert_close_bf16(to_np(dx), rdx, rel=5e-3, what="dx")
+    got = to_np(dwide)
+    assert_close_bf16(got[:, pad:pad + H * n].reshape(T * H, n), rdz, rel=5e-3, what="dz")
+    assert not got[:, :pad].any() and not got[:, pad + H * n:].any()
