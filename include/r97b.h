@@ -39,6 +39,24 @@ int r97b_abi_version(void);
  * arguments) -- read and cleared. Synchronises the current device. */
 int r97b_device_error(unsigned int* out_bits);
 
+/* ------------------------------------------------------------------------------ plumbing */
+/* Device memory and streams for a C++ host that drives the kernels (the adjoint-row plugin,
+ * libr97host.so), so that it needs no CUDA headers of its own. Replace: the reference's rad_dev_alloc /
+ * rad_dev_free / rad_memcpy / rad_stream_create device layer as its device rows use it
+ * (src/adjoint/device/scratch.cpp, linear.hip:423-430). */
+
+/* Device allocation (cudaMalloc: 256-byte aligned); bytes == 0 gives null and R97B_OK. */
+int r97b_mem_alloc(void** out, int64_t bytes);
+int r97b_mem_free(void* p);
+/* Asynchronous copy on `stream`: kind 0 host->device, 1 device->host, 2 device->device. */
+int r97b_memcpy(void* dst, const void* src, int64_t bytes, int32_t kind, void* stream);
+int r97b_memset(void* dst, int32_t byte, int64_t bytes, void* stream);
+/* A non-blocking stream on the current device, and a wait for everything queued on one. */
+int r97b_stream_create(void** out);
+int r97b_stream_sync(void* stream);
+/* The CUDA runtime's text for the last error (not cleared). */
+const char* r97b_last_cuda_error(void);
+
 /* ------------------------------------------------------------------------------ IQR decode */
 
 /* Reference-compatible decode: stored trellis/affine IQR codes -> int8 grid [rows, cols] plus bf16 scale
@@ -55,6 +73,13 @@ int r97_iqr_decode(const R97IqrDecodeDesc* desc, R97IqrStream stream);
  * pair the reference's kernels read (reference src/adjoint/host/linear.cpp:132-163 value_at).
  * Replaces: the decode half of the reference's stored-weight dX path, linear.hip:601-622. */
 int r97b_iqr_dequant_bf16(const R97IqrDecodeDesc* desc, uint16_t* out_w, int64_t ld_w, void* stream);
+
+/* The stored pair of a decoded weight -- int8 codes [rows, cols] and bf16 scale bits [rows, ceil(cols/group)]
+ * (reference src/stored_weight.h StoredWeight) -- as the GEMM operand: W[r, k] = bf16(code * scale), the
+ * product and rounding r97b_iqr_dequant_bf16 uses, into `out_w` (row stride `ld_w`).
+ * Replaces: the int8-pair reader of the reference's stored-weight dX path (linear.hip:520-600). */
+int r97b_codes_dequant_bf16(const int8_t* codes, const uint16_t* scale, int64_t rows, int64_t cols, int64_t group,
+                            uint16_t* out_w, int64_t ld_w, void* stream);
 
 /* ------------------------------------------------------------------------------ GEMM */
 
@@ -126,7 +151,8 @@ int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, int64_t z_tok_s
 
 /* ------------------------------------------------------------------------------ loss */
 
-/* Per logit row (bf16, row stride ld): CE = lse - x[target] into loss_ce[row] (target -1: not scored,
+/* Per logit row (bf16, row stride ld; 16-byte aligned rows are read 8 values a load, others one at a
+ * time): CE = lse - x[target] into loss_ce[row] (a target of -1, or one outside [0, vocab): not scored,
  * loss 0, gradient 0), KL(softmax(teacher) || softmax(x)) into loss_kl[row] when teacher is given, and
  * grad = grad_scale * (w_ce (softmax - onehot) + w_kl (softmax(x) - softmax(teacher))) as bf16; grad may
  * equal logits (in place), targets may be null (KL only). loss_ce / loss_kl / grad may be null.
@@ -179,7 +205,7 @@ int r97b_global_norm_noalloc(const float* g, int64_t n, float inv_k, float max_n
  * (1/sqrt(head_k) in the reference's architecture). */
 typedef struct R97bGdnDims {
     int32_t n_seq, H, Hg, n_chunks;
-    int32_t head_k, head_v, chunk, _pad;
+    int32_t head_k, head_v, chunk, flags; /* flags: R97B_GDN_* below, 0 for the fused layer */
     int64_t T;
     float scale;
     int32_t _pad2;
@@ -187,6 +213,15 @@ typedef struct R97bGdnDims {
     const int32_t* chunk_len;  /* device [n_chunks]: its length (<= chunk)     */
     const int32_t* seq_chunk0; /* device [n_seq + 1]: first chunk of each sequence */
 } R97bGdnDims;
+
+/* The forward reads A (f32 [T, H, 64]: row i of each chunk's (I+M)^-1, its lower triangle with the
+ * diagonal; the rest is ignored) instead of solving for it: the reference's gdn_chunk_scan, which takes
+ * the gdn_kkt_solve output as an operand. */
+#define R97B_GDN_A_GIVEN 1
+/* The backward writes the scan's own cotangent of A into R97bGdnBwd.dA (f32 [T, H, 64], lower triangle
+ * with the diagonal, zeros above) and leaves the solve's adjoint out of dk, dbeta and dg; the caller
+ * applies it with r97b_gdn_kkt_bwd (the reference's gdn_kkt_solve adjoint). */
+#define R97B_GDN_SPLIT_KKT 2
 
 /* Fills the chunk table of cu_seqlens (host arrays; any output may be null) and returns the chunk count,
  * or -1 on a bad cu_seqlens. */
@@ -221,6 +256,7 @@ typedef struct R97bGdnBwd {
     const float* dht;
     float *dS, *dVp, *dw, *pdq, *pdk, *pdg;
     float *dq, *dk, *dv, *dbeta, *dg, *dh0;
+    float* dA; /* R97B_GDN_SPLIT_KKT only: the scan's cotangent of A, f32 [T, H, 64]; else unused */
 } R97bGdnBwd;
 
 /* The forward of the reference's gdn_kkt_solve + gdn_chunk_scan pair (src/adjoint/host/gdn_kkt.cpp:221-270,
@@ -232,6 +268,13 @@ int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* args, void* stream);
  * (src/adjoint/host/gdn_scan.cpp:487-580 + gdn_kkt.cpp:272-352). Replaces: gdn_scan_adjoint_kernel and
  * gdn_kkt_adjoint_kernel, src/adjoint/device/gdn_scan.hip:235-600 and gdn_kkt.hip:229-424. */
 int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* args, void* stream);
+
+/* The kkt solve's adjoint alone (reference src/adjoint/host/gdn_kkt.cpp:272-352), for the split form:
+ * from k bf16 [T, Hg, 128], g, beta f32 [T, H], the solve's output A and its cotangent dA (f32 [T, H, 64],
+ * lower triangles) it WRITES dk f32 [T, H, 128] per value head, dbeta and dg f32 [T, H].
+ * Replaces: gdn_kkt_adjoint_kernel, src/adjoint/device/gdn_kkt.hip:229-424. */
+int r97b_gdn_kkt_bwd(const R97bGdnDims* dims, const uint16_t* k, const float* g, const float* beta, const float* A,
+                     const float* dA, float* dk, float* dbeta, float* dg, void* stream);
 
 /* dst[t, j, :] = sum_{h in key head j's value heads} src[t, h, :] (f32 [T, H, 128] -> [T, Hg, 128]). */
 int r97b_gdn_sum_heads(const float* src, float* dst, int64_t T, int32_t H, int32_t Hg, void* stream);

@@ -62,11 +62,15 @@ def ref_lib():
             if not os.path.isdir(os.path.join(REF_TREE, "src")):
                 raise FileNotFoundError("oracle/_ref/libr97ref.so is not built and the reference tree is absent")
             build(ref=True)
-        lib = ctypes.CDLL(path)
+        # global: a device-row plugin loaded after it binds to this registry by name
+        lib = ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
         lib.ref_last_error.restype = ctypes.c_char_p
         lib.ref_iqr_decode.restype = ctypes.c_int
         lib.ref_twin.restype = ctypes.c_int
         lib.ref_adjoint.restype = ctypes.c_int
+        lib.ref_adjoint_on.restype = ctypes.c_int
+        lib.ref_op_rows.restype = ctypes.c_int
+        lib.ref_paramset.restype = ctypes.c_void_p
         lib.ref_grad_count.restype = ctypes.c_int
         lib.ref_grad_name.restype = ctypes.c_char_p
         lib.ref_grad_numel.restype = ctypes.c_int64
@@ -174,9 +178,23 @@ def ref_twin(op, params, operands, reads):
     return res
 
 
-def ref_adjoint(op, params, operands, fwd, cots, prefix="m", fused_slots=False):
-    """Runs the reference host adjoint. ``fwd`` maps buffer -> forward value (None for stored),
-    ``cots`` maps each written buffer -> its cotangent. Returns (dc dict, grads dict)."""
+def op_rows(op):
+    """What the reference registry holds for ``op``: {"twin", "host", "device": bool, "host_frozen",
+    "device_frozen": lists}."""
+    lib = ref_lib()
+    hf, df = (ctypes.c_int * 16)(), (ctypes.c_int * 16)()
+    nh, nd = ctypes.c_int(), ctypes.c_int()
+    bits = lib.ref_op_rows(op.encode(), hf, ctypes.byref(nh), df, ctypes.byref(nd))
+    return {"twin": bool(bits & 1), "host": bool(bits & 2), "device": bool(bits & 4),
+            "host_frozen": list(hf[:nh.value]), "device_frozen": list(df[:nd.value])}
+
+
+def ref_adjoint(op, params, operands, fwd, cots, prefix="m", fused_slots=False, side="host", flush=None):
+    """Runs the adjoint row the reference registry serves for ``op`` on ``side`` ("host": the reference's
+    own f64 row; "device": whatever device row a loaded plugin registered). ``fwd`` maps buffer -> forward
+    value (None for stored), ``cots`` maps each written buffer -> its cotangent. ``flush``, when given, is
+    called with the call's ParamSet pointer before the gradients are read (a device row's gradients wait
+    in its stage until flushed). Returns (dc dict, grads dict)."""
     lib = ref_lib()
     ps, os_, keep = _pack(op, params, operands)
     flist = [None if fwd.get(o.buffer) is None else np.ascontiguousarray(fwd[o.buffer], np.float64).reshape(-1)
@@ -184,10 +202,12 @@ def ref_adjoint(op, params, operands, fwd, cots, prefix="m", fused_slots=False):
     clist = [np.ascontiguousarray(cots[o.buffer], np.float64).reshape(-1) for o in operands if o.written]
     dcs = [np.zeros(o.numel, np.float64) for o in operands]
     pb = prefix.encode()
-    rc = lib.ref_adjoint(op.encode(), ps, len(params), os_, len(operands), _dptrs(flist, keep),
-                         _dptrs(clist, keep), _dptrs(dcs, keep), pb, int(fused_slots))
+    rc = lib.ref_adjoint_on(op.encode(), ps, len(params), os_, len(operands), _dptrs(flist, keep),
+                            _dptrs(clist, keep), _dptrs(dcs, keep), pb, int(fused_slots), int(side == "device"))
     if rc != 0:
-        raise RuntimeError(f"ref_adjoint({op}) rc={rc}: {lib.ref_last_error().decode()}")
+        raise RuntimeError(f"ref_adjoint({op}, {side}) rc={rc}: {lib.ref_last_error().decode()}")
+    if flush is not None:
+        flush(lib.ref_paramset())
     dc = {o.buffer: dcs[i].reshape(o.shape) for i, o in enumerate(operands)}
     grads = {}
     for i in range(lib.ref_grad_count()):

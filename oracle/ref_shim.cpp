@@ -16,6 +16,7 @@
 #include "iqr_decode.h"
 #include "stored_weight.h"
 
+#include <algorithm>
 #include <cstdint>
 #include <cstring>
 #include <exception>
@@ -165,15 +166,16 @@ int ref_twin(const char* op, const RefParam* params, int nparams, const RefOpera
 // order (null for a stored one), `cots` the cotangent of each written operand in write order, and
 // `dc` one array per operand (schema order, sized by its shape) that the row adds into. Gradients
 // of trainable leaves land in a ParamSet read back with ref_grad_*.
-int ref_adjoint(const char* op, const RefParam* params, int nparams, const RefOperand* ops, int nops,
-                const double* const* fwd, const double* const* cots, double* const* dc,
-                const char* prefix, int fused_slots) {
+int ref_adjoint_on(const char* op, const RefParam* params, int nparams, const RefOperand* ops, int nops,
+                   const double* const* fwd, const double* const* cots, double* const* dc,
+                   const char* prefix, int fused_slots, int side) {
     try {
         g_error.clear();
         g_grads.clear();
         r97::OpRecord rec = make_record(op, params, nparams, ops, nops);
         std::string err;
-        r97::AdjointFn fn = r97::adjoint_find(rec.op, r97::Side::host, rec.params, &err);
+        r97::AdjointFn fn =
+            r97::adjoint_find(rec.op, side ? r97::Side::device : r97::Side::host, rec.params, &err);
         if (!fn) {
             g_error = err.empty() ? "no adjoint" : err;
             return 1;
@@ -208,6 +210,29 @@ int ref_adjoint(const char* op, const RefParam* params, int nparams, const RefOp
         return 4;
     }
 }
+
+// The host rows (side 0): the reference's own f64 adjoints.
+int ref_adjoint(const char* op, const RefParam* params, int nparams, const RefOperand* ops, int nops,
+                const double* const* fwd, const double* const* cots, double* const* dc,
+                const char* prefix, int fused_slots) {
+    return ref_adjoint_on(op, params, nparams, ops, nops, fwd, cots, dc, prefix, fused_slots, 0);
+}
+
+// What the registry holds for `op` (op_rows): bit 0 twin, bit 1 host adjoint, bit 2 device adjoint; the
+// frozen positions of each side into the caller's arrays (up to 16 each), their counts into *n_host /
+// *n_dev.
+int ref_op_rows(const char* op, int* host_frozen, int* n_host, int* dev_frozen, int* n_dev) {
+    const r97::OpRows r = r97::op_rows(op);
+    *n_host = (int)std::min<size_t>(16, r.host_frozen.size());
+    *n_dev = (int)std::min<size_t>(16, r.device_frozen.size());
+    for (int i = 0; i < *n_host; ++i) host_frozen[i] = r.host_frozen[(size_t)i];
+    for (int i = 0; i < *n_dev; ++i) dev_frozen[i] = r.device_frozen[(size_t)i];
+    return (r.twin ? 1 : 0) | (r.host_adjoint ? 2 : 0) | (r.device_adjoint ? 4 : 0);
+}
+
+// The ParamSet the last ref_adjoint_on call's rows added to (a device row's gradients arrive there when
+// the caller flushes its device stage into it).
+void* ref_paramset() { return &g_grads; }
 
 int ref_grad_count() { return (int)g_grads.size(); }
 const char* ref_grad_name(int i) { return g_grads[(size_t)i].name.c_str(); }

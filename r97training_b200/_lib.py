@@ -71,6 +71,15 @@ _SIGS = {
     "r97b_gdn_fwd": (c_i32, [c_vp, c_vp, c_vp]),
     "r97b_gdn_bwd": (c_i32, [c_vp, c_vp, c_vp]),
     "r97b_gdn_sum_heads": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_i32, c_vp]),
+    "r97b_codes_dequant_bf16": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
+    "r97b_mem_alloc": (c_i32, [c_vp, c_i64]),
+    "r97b_mem_free": (c_i32, [c_vp]),
+    "r97b_memcpy": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp]),
+    "r97b_memset": (c_i32, [c_vp, c_i32, c_i64, c_vp]),
+    "r97b_stream_create": (c_i32, [c_vp]),
+    "r97b_stream_sync": (c_i32, [c_vp]),
+    "r97b_last_cuda_error": (ctypes.c_char_p, []),
+    "r97b_gdn_kkt_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "r97b_conv_prep_fwd": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp]),
     "r97b_conv_prep_bwd": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_i32, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp,
                                    c_vp, c_i64, c_vp]),

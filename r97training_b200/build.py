@@ -50,7 +50,7 @@ def build_kernels(verbose: bool = False) -> str:
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         objs = list(ex.map(lambda s: _compile(s, headers), srcs))
     if not _newer(LIB, objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda" if False else "-lrt"]
+        cmd = [NVCC] + ARCH + ["-shared", "-Xlinker", "-soname=libr97b200.so", "-o", LIB] + objs + ["-lrt"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
@@ -63,12 +63,13 @@ def build_host(verbose: bool = False) -> str:
     srcs = sorted(glob.glob(os.path.join(HOST, "*.cpp")))
     if not srcs:
         return ""
-    headers = sorted(glob.glob(os.path.join(HOST, "*.h")) + glob.glob(os.path.join(ROOT, "include", "r97", "*.h")) +
-                     glob.glob(os.path.join(ROOT, "include", "*.h")))
-    if _newer(HOSTLIB, srcs + headers):
+    headers = sorted(glob.glob(os.path.join(HOST, "*.h")) + glob.glob(os.path.join(ROOT, "include", "*.h")))
+    if _newer(HOSTLIB, srcs + headers + [LIB]):
         return HOSTLIB
+    # links the kernel library by name, found beside it at run time ($ORIGIN); the reference's registry
+    # symbols stay weak and unresolved until a process that holds them loads the plugin
     cmd = ["g++", "-O2", "-std=c++20", "-fPIC", "-shared", "-pthread", "-I", os.path.join(ROOT, "include"),
-           "-o", HOSTLIB] + srcs + ["-ldl"]
+           "-Wl,-soname,libr97host.so", "-o", HOSTLIB] + srcs + ["-L", PKG, "-lr97b200", "-Wl,-rpath,$ORIGIN"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"g++ failed:\n{r.stdout}\n{r.stderr}")

@@ -1,5 +1,5 @@
-// capi.cu -- library-level entry points of libr97b200.so: the ABI version, the device error word and
-// the GEMM.
+// capi.cu -- library-level entry points of libr97b200.so: the ABI version, the device error word, the
+// GEMM, and the device memory / stream plumbing a C++ host (the adjoint-row plugin) drives kernels with.
 #include "r97b_internal.h"
 
 #include <atomic>
@@ -13,7 +13,7 @@ void add_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memo
 
 extern "C" uint64_t r97b_launch_count(void) { return r97b::g_launches.load(std::memory_order_relaxed); }
 
-extern "C" int r97b_abi_version(void) { return 1; }
+extern "C" int r97b_abi_version(void) { return 2; }
 
 extern "C" int r97b_device_error(unsigned int* out_bits) {
     unsigned bits = r97b::gemm_error_word();
@@ -25,3 +25,45 @@ extern "C" int r97b_gemm(const R97bGemm* g, void* stream) {
     if (!g) return R97B_EINVAL;
     return r97b::gemm_run(*g, r97b::as_stream(stream));  // gemm_run counts its launch
 }
+
+extern "C" int r97b_mem_alloc(void** out, int64_t bytes) {
+    if (!out || bytes < 0) return R97B_EINVAL;
+    *out = nullptr;
+    if (bytes == 0) return R97B_OK;
+    return cudaMalloc(out, (size_t)bytes) == cudaSuccess ? R97B_OK : R97B_EDEVICE;
+}
+
+extern "C" int r97b_mem_free(void* p) {
+    if (!p) return R97B_OK;
+    return cudaFree(p) == cudaSuccess ? R97B_OK : R97B_EDEVICE;
+}
+
+extern "C" int r97b_memcpy(void* dst, const void* src, int64_t bytes, int32_t kind, void* stream) {
+    if (bytes < 0 || kind < 0 || kind > 2) return R97B_EINVAL;
+    if (bytes == 0) return R97B_OK;
+    if (!dst || !src) return R97B_EINVAL;
+    static const cudaMemcpyKind kinds[3] = {cudaMemcpyHostToDevice, cudaMemcpyDeviceToHost, cudaMemcpyDeviceToDevice};
+    return cudaMemcpyAsync(dst, src, (size_t)bytes, kinds[kind], r97b::as_stream(stream)) == cudaSuccess ? R97B_OK
+                                                                                                         : R97B_ELAUNCH;
+}
+
+extern "C" int r97b_memset(void* dst, int32_t byte, int64_t bytes, void* stream) {
+    if (bytes < 0) return R97B_EINVAL;
+    if (bytes == 0) return R97B_OK;
+    if (!dst) return R97B_EINVAL;
+    return cudaMemsetAsync(dst, byte, (size_t)bytes, r97b::as_stream(stream)) == cudaSuccess ? R97B_OK : R97B_ELAUNCH;
+}
+
+extern "C" int r97b_stream_create(void** out) {
+    if (!out) return R97B_EINVAL;
+    cudaStream_t s = nullptr;
+    if (cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking) != cudaSuccess) return R97B_EDEVICE;
+    *out = s;
+    return R97B_OK;
+}
+
+extern "C" int r97b_stream_sync(void* stream) {
+    return cudaStreamSynchronize(r97b::as_stream(stream)) == cudaSuccess ? R97B_OK : R97B_EDEVICE;
+}
+
+extern "C" const char* r97b_last_cuda_error(void) { return cudaGetErrorString(cudaPeekAtLastError()); }

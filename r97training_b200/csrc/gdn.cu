@@ -46,7 +46,7 @@ constexpr int P32 = 40;  // bf16 pitch of a [*, 32] tile
 constexpr int F65 = 65;  // f32 pitch of a [64, 64] tile
 
 struct Dims {
-    int n_seq, H, Hg, grp, n_chunks;
+    int n_seq, H, Hg, grp, n_chunks, flags;
     int64_t T;
     float scale;
     const int* tok0;
@@ -161,11 +161,17 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
     const int warp = threadIdx.x >> 5;
+    const bool given = (dm.flags & R97B_GDN_A_GIVEN) != 0;
     stage_bf16(ks, k, tok0, n, dm.Hg, hk);
     stage_bf16(vs, v, tok0, n, dm.H, h);
     load_gb(gs, bs, g, beta, tok0, n, dm.H, h);
+    if (given)  // the caller's solve: its lower triangle, diagonal included, for the chunk's rows
+        for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
+            const int i = idx >> 6, j = idx & 63;
+            As[i * F65 + j] = (i < n && j <= i) ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f;
+        }
     __syncthreads();
-    {
+    if (!given) {
         // M = strict lower of beta_i (k_i . k_l) e^{g_i - g_l}
         float acc[1][4][4];
         acc_zero<16, 32>(acc);
@@ -174,9 +180,7 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
         acc_for<16, 32>(acc, m0, n0, [&](int r, int l, float& x) {
             Ms[r * F65 + l] = l < r ? bs[r] * x * expf(gs[r] - gs[l]) : 0.0f;
         });
-    }
-    __syncthreads();
-    {
+        __syncthreads();
         // forward substitution, one row at a time: A[i][j] = delta_ij - sum_{l<i} M[i][l] A[l][j]
         const int j = threadIdx.x & 63, part = threadIdx.x >> 6;
         for (int i = 0; i < L; ++i) {
@@ -197,7 +201,7 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
     for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
         const int i = idx >> 6, j = idx & 63;
         const float a = As[i * F65 + j];
-        if (i < n) A[((tok0 + i) * dm.H + h) * L + j] = a;
+        if (i < n && !given) A[((tok0 + i) * dm.H + h) * L + j] = a;
         const float e = bs[j] * expf(gs[j]);
         put_split(a1h, a1l, i * kP64 + j, a * e);
         put_split(a2h, a2l, i * kP64 + j, a * bs[j]);
@@ -602,6 +606,52 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
     for (int i = threadIdx.x; i < n; i += blockDim.x) pdg[(tok0 + i) * dm.H + h] = dgs[i];
 }
 
+// The solve's adjoint for one (chunk, head), shared by B2b and B3 (reference gdn_kkt.cpp:272-352): with
+// dA in th/tl (its strict lower triangle is what counts), Y = dA A^T, dM = -A^T Y on the strict lower
+// block, then dbeta_i += sum_l dM_il C_il, dg_i += sum_l dM_il M_il, dg_l -= the same, and
+// dk += E k + E^T k with E_il = dM_il beta_i e^{g_i - g_l}. C = (k k^T) e^{g_i - g_l} (strict lower, Cs).
+// th/tl are overwritten with E; yh/yl are scratch. Every thread of the CTA calls it.
+__device__ __forceinline__ void kkt_adjoint(const bf16* ah, const bf16* al, bf16* th, bf16* tl, bf16* yh, bf16* yl,
+                                            const bf16* ks, const float* Cs, const float* gs, const float* bs,
+                                            float* dgs, float* dbs, int n, float (&dka)[1][8][4]) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pm0 = (warp & 3) * 16, pn0 = (warp >> 2) * 32;
+    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
+    {
+        float acc[1][4][4];
+        acc_zero<16, 32>(acc);
+        mma_split_ab<16, 32, 64, false, false>(acc, th, tl, kP64, ah, al, kP64, pm0, pn0);
+        acc_for<16, 32>(acc, pm0, pn0, [&](int r, int l, float& x) { put_split(yh, yl, r * kP64 + l, x); });
+        __syncthreads();
+        acc_zero<16, 32>(acc);
+        mma_split_ab<16, 32, 64, true, true>(acc, ah, al, kP64, yh, yl, kP64, pm0, pn0);
+        __syncthreads();  // every warp has read dA (th/tl) before E overwrites it
+        float b0 = 0.0f, b1 = 0.0f, g0 = 0.0f, g1 = 0.0f;
+        acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
+            const bool on = l < r && r < n;
+            const float dm_ = on ? -acc[i][j][q] : 0.0f;
+            const float kh = Cs[r * F65 + l];
+            const float gg = dm_ * bs[r] * kh;
+            if (q >> 1) { b1 += dm_ * kh; g1 += gg; } else { b0 += dm_ * kh; g0 += gg; }
+            if (on) atomicAdd(&dgs[l], -gg);
+            put_split(th, tl, r * kP64 + l, on ? dm_ * bs[r] * expf(gs[r] - gs[l]) : 0.0f);
+        });
+        b0 = quad_sum(b0);
+        b1 = quad_sum(b1);
+        g0 = quad_sum(g0);
+        g1 = quad_sum(g1);
+        if ((lane & 3) == 0) {
+            atomicAdd(&dbs[pm0 + (lane >> 2)], b0);
+            atomicAdd(&dgs[pm0 + (lane >> 2)], g0);
+            atomicAdd(&dbs[pm0 + (lane >> 2) + 8], b1);
+            atomicAdd(&dgs[pm0 + (lane >> 2) + 8], g1);
+        }
+    }
+    __syncthreads();
+    mma_split_a<16, 64, 64, false, true>(dka, th, tl, kP64, ks, kP128, m0, n0);  // dk_i += sum_l E_il k_l
+    mma_split_a<16, 64, 64, true, true>(dka, th, tl, kP64, ks, kP128, m0, n0);   // dk_l += sum_i E_il k_i
+}
+
 // B2b: per (chunk, value head): the intra-chunk terms and the solve's adjoint; adds B2a's partials.
 __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                  const bf16* __restrict__ v, const float* __restrict__ g,
@@ -611,7 +661,8 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
                                                  const float* __restrict__ pdq, const float* __restrict__ pdk,
                                                  const float* __restrict__ pdg, float* __restrict__ dq_out,
                                                  float* __restrict__ dk_out, float* __restrict__ dv_out,
-                                                 float* __restrict__ dbeta_out, float* __restrict__ dg_out) {
+                                                 float* __restrict__ dbeta_out, float* __restrict__ dg_out,
+                                                 float* __restrict__ dA_out) {
     extern __shared__ __align__(16) unsigned char smraw[];
     bf16* ks = reinterpret_cast<bf16*>(smraw);   // k [64][136]
     bf16* qv = ks + L * kP128;                   // q, then v [64][136]
@@ -637,6 +688,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pm0 = (warp & 3) * 16, pn0 = (warp >> 2) * 32;   // [64 x 64] warp tile
     const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;     // [64 x 128] warp tile
+    const bool split = (dm.flags & R97B_GDN_SPLIT_KKT) != 0;
     stage_bf16(ks, k, tok0, n, dm.Hg, hk);
     stage_bf16(qv, q, tok0, n, dm.Hg, hk);
     stage_bf16(dos, dO, tok0, n, dm.H, h);
@@ -699,7 +751,12 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
         mma_split_a<16, 32, 128, false, false>(a1, xh, xl, kP128, ks, kP128, pm0, pn0);
         mma_split_a<16, 32, 128, false, false>(a2, dvh, dvl, kP128, qv, kP128, pm0, pn0);
         acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
-            put_split(th, tl, r * kP64 + l, l < r ? bs[l] * (expf(gs[l]) * a1[i][j][q] + a2[i][j][q]) : 0.0f);
+            const float da = bs[l] * (expf(gs[l]) * a1[i][j][q] + a2[i][j][q]);
+            if (split) {  // the scan's own cotangent of A, its lower triangle with the diagonal
+                if (r < n) dA_out[((tok0 + r) * dm.H + h) * L + l] = l <= r ? da : 0.0f;
+            } else {
+                put_split(th, tl, r * kP64 + l, l < r ? da : 0.0f);
+            }
         });
     }
     {
@@ -741,40 +798,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
         }
     }
     __syncthreads();
-    {
-        // Y = dA A^T ; dM = -A^T Y, strict lower
-        float acc[1][4][4];
-        acc_zero<16, 32>(acc);
-        mma_split_ab<16, 32, 64, false, false>(acc, th, tl, kP64, ah, al, kP64, pm0, pn0);
-        acc_for<16, 32>(acc, pm0, pn0, [&](int r, int l, float& x) { put_split(yh, yl, r * kP64 + l, x); });
-        __syncthreads();
-        acc_zero<16, 32>(acc);
-        mma_split_ab<16, 32, 64, true, true>(acc, ah, al, kP64, yh, yl, kP64, pm0, pn0);
-        __syncthreads();  // every warp has read dA (th/tl) before E overwrites it
-        float b0 = 0.0f, b1 = 0.0f, g0 = 0.0f, g1 = 0.0f;
-        acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
-            const bool on = l < r && r < n;
-            const float dm_ = on ? -acc[i][j][q] : 0.0f;
-            const float kh = Cs[r * F65 + l];
-            const float gg = dm_ * bs[r] * kh;
-            if (q >> 1) { b1 += dm_ * kh; g1 += gg; } else { b0 += dm_ * kh; g0 += gg; }
-            if (on) atomicAdd(&dgs[l], -gg);
-            put_split(th, tl, r * kP64 + l, on ? dm_ * bs[r] * expf(gs[r] - gs[l]) : 0.0f);
-        });
-        b0 = quad_sum(b0);
-        b1 = quad_sum(b1);
-        g0 = quad_sum(g0);
-        g1 = quad_sum(g1);
-        if ((lane & 3) == 0) {
-            atomicAdd(&dbs[pm0 + (lane >> 2)], b0);
-            atomicAdd(&dgs[pm0 + (lane >> 2)], g0);
-            atomicAdd(&dbs[pm0 + (lane >> 2) + 8], b1);
-            atomicAdd(&dgs[pm0 + (lane >> 2) + 8], g1);
-        }
-    }
-    __syncthreads();
-    mma_split_a<16, 64, 64, false, true>(dka, th, tl, kP64, ks, kP128, m0, n0);  // dk_i += sum_l E_il k_l
-    mma_split_a<16, 64, 64, true, true>(dka, th, tl, kP64, ks, kP128, m0, n0);   // dk_l += sum_i E_il k_i
+    if (!split) kkt_adjoint(ah, al, th, tl, yh, yl, ks, Cs, gs, bs, dgs, dbs, n, dka);
     __syncthreads();
     acc_for<16, 64>(dqa, m0, n0, [&](int r, int d, float& x) {
         if (r < n) {
@@ -791,6 +815,69 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int64_t at = (tok0 + i) * dm.H + h;
         dg_out[at] = dgs[i] + pdg[at];
+        dbeta_out[at] = dbs[i];
+    }
+}
+
+// B3: per (chunk, value head): the solve's adjoint alone, for a caller that keeps gdn_kkt_solve and
+// gdn_chunk_scan as two ops (the backward's R97B_GDN_SPLIT_KKT mode hands it the scan's dA).
+// dk is per value head [T, H, 128]; dbeta and dg [T, H] are written, not added.
+__global__ void __launch_bounds__(256) gdn_kkt_bwd(Dims dm, const bf16* __restrict__ k, const float* __restrict__ g,
+                                                   const float* __restrict__ beta, const float* __restrict__ A,
+                                                   const float* __restrict__ dA, float* __restrict__ dk_out,
+                                                   float* __restrict__ dbeta_out, float* __restrict__ dg_out) {
+    extern __shared__ __align__(16) unsigned char smraw[];
+    bf16* ks = reinterpret_cast<bf16*>(smraw);   // k [64][136]
+    bf16* ah = ks + L * kP128;                   // A hi/lo [64][72]
+    bf16* al = ah + L * kP64;
+    bf16* th = al + L * kP64;                    // dA, then E hi/lo [64][72]
+    bf16* tl = th + L * kP64;
+    bf16* yh = tl + L * kP64;                    // Y = dA A^T hi/lo [64][72]
+    bf16* yl = yh + L * kP64;
+    float* Cs = reinterpret_cast<float*>(yl + L * kP64);  // (k k^T) e^{g_i-g_l}, strict lower [64][65]
+    float* gs = Cs + L * F65;
+    float* bs = gs + L;
+    float* dgs = bs + L;
+    float* dbs = dgs + L;
+    const int c = blockIdx.x, h = blockIdx.y, hk = h / dm.grp;
+    const int64_t tok0 = dm.tok0[c];
+    const int n = dm.len[c];
+    const int warp = threadIdx.x >> 5;
+    stage_bf16(ks, k, tok0, n, dm.Hg, hk);
+    load_gb(gs, bs, g, beta, tok0, n, dm.H, h);
+    for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
+        const int i = idx >> 6, j = idx & 63;
+        const bool on = i < n && j <= i;
+        const int64_t at = ((tok0 + i) * dm.H + h) * L + j;
+        put_split(ah, al, i * kP64 + j, on ? A[at] : 0.0f);
+        put_split(th, tl, i * kP64 + j, on ? dA[at] : 0.0f);
+    }
+    for (int i = threadIdx.x; i < L; i += blockDim.x) {
+        dgs[i] = 0.0f;
+        dbs[i] = 0.0f;
+    }
+    __syncthreads();
+    {
+        float kk[1][4][4];
+        acc_zero<16, 32>(kk);
+        const int pm0 = (warp & 3) * 16, pn0 = (warp >> 2) * 32;
+        warp_mma<16, 32, 128, false, false>(kk, ks, kP128, ks, kP128, pm0, pn0);
+        acc_for<16, 32>(kk, pm0, pn0, [&](int r, int l, float& x) {
+            Cs[r * F65 + l] = (l < r && r < n) ? x * expf(gs[r] - gs[l]) : 0.0f;
+        });
+    }
+    __syncthreads();
+    float dka[1][8][4];
+    acc_zero<16, 64>(dka);
+    kkt_adjoint(ah, al, th, tl, yh, yl, ks, Cs, gs, bs, dgs, dbs, n, dka);
+    __syncthreads();
+    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
+    acc_for<16, 64>(dka, m0, n0, [&](int r, int d, float& x) {
+        if (r < n) dk_out[((tok0 + r) * dm.H + h) * D + d] = x;
+    });
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int64_t at = (tok0 + i) * dm.H + h;
+        dg_out[at] = dgs[i];
         dbeta_out[at] = dbs[i];
     }
 }
@@ -817,6 +904,7 @@ constexpr size_t kSmemOut = (4 * L * kP128 + 2 * D * kP128 + 2 * L * kP64) * 2 +
 constexpr size_t kSmemBState = 2 * sizeof(B1Stage) + (2 * D * P32 + 4 * L * P32) * 2;
 constexpr size_t kSmemBA = (2 * D * kP128 + 4 * L * kP128) * 2 + (2 * L + 8) * 4;
 constexpr size_t kSmemBB = (7 * L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
+constexpr size_t kSmemKB = (L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 
 bool g_attr = false;
 
@@ -828,16 +916,18 @@ void set_attrs() {
     cudaFuncSetAttribute(gdn_bwd_state, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBState);
     cudaFuncSetAttribute(gdn_bwd_a, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBA);
     cudaFuncSetAttribute(gdn_bwd_b, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBB);
+    cudaFuncSetAttribute(gdn_kkt_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemKB);
     g_attr = true;
 }
 
 bool dims_ok(const R97bGdnDims& d) {
     return d.n_seq > 0 && d.H > 0 && d.Hg > 0 && d.H % d.Hg == 0 && d.n_chunks >= 0 && d.T >= 0 && d.chunk_tok0 &&
-           d.chunk_len && d.seq_chunk0 && d.head_k == D && d.head_v == D && d.chunk == L;
+           d.chunk_len && d.seq_chunk0 && d.head_k == D && d.head_v == D && d.chunk == L &&
+           (d.flags & ~(R97B_GDN_A_GIVEN | R97B_GDN_SPLIT_KKT)) == 0;
 }
 
 Dims to_dims(const R97bGdnDims& d) {
-    return Dims{d.n_seq, d.H, d.Hg, d.H / d.Hg, d.n_chunks, d.T, d.scale, d.chunk_tok0, d.chunk_len, d.seq_chunk0};
+    return Dims{d.n_seq, d.H, d.Hg, d.H / d.Hg, d.n_chunks, d.flags, d.T, d.scale, d.chunk_tok0, d.chunk_len, d.seq_chunk0};
 }
 
 }  // namespace
@@ -888,6 +978,7 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
         !a->dS || !a->dVp || !a->dw || !a->pdq || !a->pdk || !a->pdg || !a->dq || !a->dk || !a->dv || !a->dbeta ||
         !a->dg)
         return R97B_EINVAL;
+    if ((dims->flags & R97B_GDN_SPLIT_KKT) && !a->dA) return R97B_EINVAL;
     set_attrs();
     const Dims dm = to_dims(*dims);
     cudaStream_t s = as_stream(stream);
@@ -902,9 +993,20 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
                                                                 a->pdq, a->pdk, a->pdg);
         gdn_bwd_b<<<dim3(dm.n_chunks, dm.H), 256, kSmemBB, s>>>(dm, q, k, v, a->g, a->beta, a->A, a->Vp, dO, a->dVp,
                                                                 a->dw, a->pdq, a->pdk, a->pdg, a->dq, a->dk, a->dv,
-                                                                a->dbeta, a->dg);
+                                                                a->dbeta, a->dg, a->dA);
     }
     return launch_status(dm.n_chunks > 0 ? 3 : 1);
+}
+
+extern "C" int r97b_gdn_kkt_bwd(const R97bGdnDims* dims, const uint16_t* k, const float* g, const float* beta,
+                                const float* A, const float* dA, float* dk, float* dbeta, float* dg, void* stream) {
+    if (!dims || !dims_ok(*dims) || !k || !g || !beta || !A || !dA || !dk || !dbeta || !dg) return R97B_EINVAL;
+    if (dims->n_chunks == 0) return R97B_OK;
+    set_attrs();
+    const Dims dm = to_dims(*dims);
+    gdn_kkt_bwd<<<dim3(dm.n_chunks, dm.H), 256, kSmemKB, as_stream(stream)>>>(
+        dm, reinterpret_cast<const bf16*>(k), g, beta, A, dA, dk, dbeta, dg);
+    return launch_status();
 }
 
 extern "C" int r97b_gdn_sum_heads(const float* src, float* dst, int64_t T, int32_t H, int32_t Hg, void* stream) {

@@ -345,6 +345,37 @@ general : {
 
 }  // namespace r97b
 
+
+namespace r97b {
+namespace {
+// W[r, k] = bf16(code[r, k] * scale[r, k / group]): the stored (codes, scale) pair of a decoded weight as
+// the GEMM operand, with the same product and rounding the fused decode uses. 8 columns a thread.
+__global__ void codes_dequant_kernel(const int8_t* __restrict__ codes, const uint16_t* __restrict__ scale,
+                                     int64_t rows, int64_t cols, int64_t group, int64_t groups,
+                                     uint16_t* __restrict__ out, int64_t ld) {
+    const int64_t per_row = (cols + 7) / 8;
+    const int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= rows * per_row) return;
+    const int64_t r = t / per_row, c0 = (t % per_row) * 8;
+    for (int64_t c = c0; c < c0 + 8 && c < cols; ++c) {
+        const float sb = bf16_bits_to_f32(scale[r * groups + c / group]);
+        out[r * ld + c] = f32_to_bf16_bits((float)codes[r * cols + c] * sb);
+    }
+}
+}  // namespace
+}  // namespace r97b
+
+extern "C" int r97b_codes_dequant_bf16(const int8_t* codes, const uint16_t* scale, int64_t rows, int64_t cols,
+                                       int64_t group, uint16_t* out_w, int64_t ld_w, void* stream) {
+    if (!codes || !scale || !out_w || rows <= 0 || cols <= 0 || group <= 0 || ld_w < cols) return R97B_EINVAL;
+    const int64_t groups = (cols + group - 1) / group;
+    const int64_t threads = rows * ((cols + 7) / 8);
+    if (threads / 256 + 1 > 0x7FFFFFFF) return R97B_EINVAL;
+    r97b::codes_dequant_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, r97b::as_stream(stream)>>>(
+        codes, scale, rows, cols, group, groups, out_w, ld_w);
+    return r97b::launch_status();
+}
+
 extern "C" int r97_iqr_decode(const R97IqrDecodeDesc* desc, R97IqrStream stream) {
     if (!desc || r97b::validate(*desc, true)) return 1;
     r97b::Sink s{desc->out_codes, desc->out_scale, nullptr, 0};

@@ -57,13 +57,15 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
                                                           const int32_t* __restrict__ targets, __nv_bfloat16* grad,
                                                           float* __restrict__ loss_ce, float* __restrict__ loss_kl,
                                                           int64_t vocab, int64_t ld, int64_t ld_t, float grad_scale,
-                                                          float w_ce, float w_kl) {
+                                                          float w_ce, float w_kl, int vec) {
     const int64_t row = blockIdx.x;
     const int32_t target = targets ? targets[row] : 0;
-    const bool scored = target >= 0;
+    // a target outside the vocabulary scores nothing, like -1, rather than reading past the row
+    const bool scored = target >= 0 && target < vocab;
     const __nv_bfloat16* x = logits + row * ld;
     const __nv_bfloat16* t = kTeacher ? teacher + row * ld_t : nullptr;
-    const int64_t nvec = vocab / 8;
+    // rows 16-byte aligned (every stride a multiple of 8 elements): 8 values a load; else one at a time
+    const int64_t nvec = vec ? vocab / 8 : 0;
 
     Acc a{-INFINITY, 0.0f, -INFINITY, 0.0f, 0.0f};
     for (int64_t i = threadIdx.x; i < nvec; i += kThreads) {
@@ -180,21 +182,23 @@ using namespace r97b;
 extern "C" int r97b_ce_kld(const uint16_t* logits, const uint16_t* teacher, const int32_t* targets, uint16_t* grad,
                            float* loss_ce, float* loss_kl, int64_t rows, int64_t vocab, int64_t ld, int64_t ld_t,
                            float grad_scale, float w_ce, float w_kl, void* stream) {
-    if (!logits || rows <= 0 || vocab <= 0 || ld < vocab || (ld % 8) != 0 ||
-        (reinterpret_cast<uintptr_t>(logits) & 15) != 0 || (grad && (reinterpret_cast<uintptr_t>(grad) & 15) != 0))
+    if (!logits || rows <= 0 || vocab <= 0 || ld < vocab || (teacher && ld_t < vocab)) return R97B_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(logits) & 1) || (grad && (reinterpret_cast<uintptr_t>(grad) & 1)) ||
+        (teacher && (reinterpret_cast<uintptr_t>(teacher) & 1)))
         return R97B_EINVAL;
-    if (teacher && (ld_t < vocab || (ld_t % 8) != 0 || (reinterpret_cast<uintptr_t>(teacher) & 15) != 0))
-        return R97B_EINVAL;
+    const auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const int vec = (ld % 8) == 0 && a16(logits) && (!grad || a16(grad)) &&
+                    (!teacher || ((ld_t % 8) == 0 && a16(teacher)));
     if (rows > 0x7FFFFFFF) return R97B_EINVAL;
     const auto* x = reinterpret_cast<const __nv_bfloat16*>(logits);
     const auto* t = reinterpret_cast<const __nv_bfloat16*>(teacher);
     auto* g = reinterpret_cast<__nv_bfloat16*>(grad);
     if (teacher)
         ce_kld_kernel<true><<<(unsigned)rows, kThreads, 0, as_stream(stream)>>>(x, t, targets, g, loss_ce, loss_kl,
-                                                                               vocab, ld, ld_t, grad_scale, w_ce, w_kl);
+                                                                               vocab, ld, ld_t, grad_scale, w_ce, w_kl, vec);
     else
         ce_kld_kernel<false><<<(unsigned)rows, kThreads, 0, as_stream(stream)>>>(x, nullptr, targets, g, loss_ce,
                                                                                 loss_kl, vocab, ld, 0, grad_scale,
-                                                                                w_ce, 0.0f);
+                                                                                w_ce, 0.0f, vec);
     return launch_status();
 }

@@ -22,7 +22,7 @@ c_vp = ctypes.c_void_p
 class R97bGdnDims(ctypes.Structure):
     _fields_ = [("n_seq", ctypes.c_int32), ("H", ctypes.c_int32), ("Hg", ctypes.c_int32),
                 ("n_chunks", ctypes.c_int32), ("head_k", ctypes.c_int32), ("head_v", ctypes.c_int32),
-                ("chunk", ctypes.c_int32), ("_pad", ctypes.c_int32), ("T", ctypes.c_int64),
+                ("chunk", ctypes.c_int32), ("flags", ctypes.c_int32), ("T", ctypes.c_int64),
                 ("scale", ctypes.c_float), ("_pad2", ctypes.c_int32), ("chunk_tok0", c_vp),
                 ("chunk_len", c_vp), ("seq_chunk0", c_vp)]
 
@@ -33,7 +33,7 @@ class R97bGdnFwd(ctypes.Structure):
 
 class R97bGdnBwd(ctypes.Structure):
     _fields_ = [(n, c_vp) for n in ("q", "k", "v", "g", "beta", "A", "w", "S", "Vp", "P", "dO", "dht", "dS", "dVp",
-                                     "dw", "pdq", "pdk", "pdg", "dq", "dk", "dv", "dbeta", "dg", "dh0")]
+                                     "dw", "pdq", "pdk", "pdg", "dq", "dk", "dv", "dbeta", "dg", "dh0", "dA")]
 
 
 def _p(t):

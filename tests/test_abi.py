@@ -12,7 +12,7 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def declared():
     names = set()
     for h in os.listdir(os.path.join(ROOT, "include")):
-        if not h.endswith(".h"):
+        if not h.endswith(".h") or h == "r97host.h":  # the plugin's own entry points (test_host_plugin.py)
             continue
         src = open(os.path.join(ROOT, "include", h)).read()
         src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
