@@ -183,32 +183,22 @@ def b200_arm(args):
     dev = torch.device("cuda", local)
     if world > 1:
         import datetime
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     cfg = _config(args.config)
     model = HybridModel(cfg, dev)
     adapter = Adapter(model, dev)
     step = TrainStep(model, adapter)
 
-    comm = torch.cuda.Stream(device=dev) if world > 1 else None
-    pending = []
-
-    def hook(li):  # a layer's adapter gradient is final: all-reduce its bucket on the comm stream
-        lo, hi = adapter.layer_ranges[li]
-        ev = torch.cuda.Event()
-        ev.record()
-        comm.wait_event(ev)
-        with torch.cuda.stream(comm):
-            dist.all_reduce(adapter.g[lo:hi], op=dist.ReduceOp.AVG)
-        pending.append(li)
-
-    if world > 1:
-        step.grad_hook = hook
+    buckets = None
+    if world > 1:  # a layer's adapter gradient is final: all-reduce its bucket while the walk goes on
+        from r97training_b200.dp import GradBuckets
+        buckets = GradBuckets(adapter.g, adapter.layer_ranges)
+        step.grad_hook = buckets.ready
 
     def one_step(ids):
         loss = step.run(ids)
-        if world > 1:
-            torch.cuda.current_stream().wait_stream(comm)
-            pending.clear()
+        if buckets is not None:
+            buckets.join()
         adapter.adamw()
         return loss
 
