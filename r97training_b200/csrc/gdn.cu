@@ -141,6 +141,78 @@ __device__ __forceinline__ void mma_split_ab(float (&acc)[WM / 16][WN / 8][4], c
 
 // ============================================================================================ forward
 
+// ------------------------------------------------------------------------------ the chunk's solve
+
+// dst[i][j] = sign * sum_l X[i][l] Y[l][j] for N x N blocks (pitches px, py, pd), by the whole CTA.
+template <int N>
+__device__ __forceinline__ void block_product(const float* X, int px, const float* Y, int py, float* dst, int pd,
+                                              float sign) {
+    for (int e = threadIdx.x; e < N * N; e += blockDim.x) {
+        const int i = e / N, j = e % N;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int l = 0; l < N; ++l) acc = fmaf(X[i * px + l], Y[l * py + j], acc);
+        dst[i * pd + j] = sign * acc;
+    }
+}
+
+// As = (I + Ms)^-1 for a strictly lower-triangular 64x64 Ms (pitch F65); `scratch` holds 2 x 32 x 33 f32.
+// Every thread of the 256-thread CTA calls it; it ends with the CTA synchronised.
+__device__ __forceinline__ void invert_unit_lower(const float* Ms, float* As, float* scratch) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp < 4) {
+        // diagonal block b: lane j < 16 holds column j in registers; rows in order, no barrier needed
+        const int b0 = warp * 16;
+        if (lane < 16) {
+            const int j = lane;
+            float a[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int l = 0; l < i; ++l) acc = fmaf(Ms[(b0 + i) * F65 + b0 + l], a[l], acc);
+                a[i] = i == j ? 1.0f : (j < i ? -acc : 0.0f);
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) As[(b0 + i) * F65 + b0 + j] = a[i];
+        }
+    } else {
+        // the strictly upper blocks are zero
+        for (int e = threadIdx.x - 128; e < 64 * 64; e += 128) {
+            const int i = e >> 6, j = e & 63;
+            if ((j >> 4) > (i >> 4)) As[i * F65 + j] = 0.0f;
+        }
+    }
+    __syncthreads();
+    // 16 -> 32: blocks (1,0) and (3,2) (pair p: rows r0 = 16 or 48, columns c0 = 0 or 32);
+    // T = M21 A11 into scratch, then X21 = -A22 T
+    for (int e = threadIdx.x; e < 512; e += blockDim.x) {
+        const int p = e >> 8, i = (e >> 4) & 15, j = e & 15;
+        const int r0 = p ? 48 : 16, c0 = p ? 32 : 0;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int l = 0; l < 16; ++l) acc = fmaf(Ms[(r0 + i) * F65 + c0 + l], As[(c0 + l) * F65 + c0 + j], acc);
+        scratch[p * 16 * 17 + i * 17 + j] = acc;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < 512; e += blockDim.x) {
+        const int p = e >> 8, i = (e >> 4) & 15, j = e & 15;
+        const int r0 = p ? 48 : 16, c0 = p ? 32 : 0;
+        const float* t = scratch + p * 16 * 17;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int l = 0; l < 16; ++l) acc = fmaf(As[(r0 + i) * F65 + r0 + l], t[l * 17 + j], acc);
+        As[(r0 + i) * F65 + c0 + j] = -acc;
+    }
+    __syncthreads();
+    // 32 -> 64: block (1,0) of 32x32 blocks; T = M[32:64][0:32] A[0:32][0:32], X = -A[32:64][32:64] T
+    float* t = scratch;  // [32][33]
+    block_product<32>(Ms + 32 * F65, F65, As, F65, t, 33, 1.0f);
+    __syncthreads();
+    block_product<32>(As + 32 * F65 + 32, F65, t, 33, As + 32 * F65, F65, -1.0f);
+    __syncthreads();
+}
+
 // F1: per (chunk, value head): A = (I + M)^-1, w = (A diag(beta e^g)) k, u = (A diag(beta)) v.
 __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restrict__ k, const bf16* __restrict__ v,
                                                     const float* __restrict__ g, const float* __restrict__ beta,
@@ -178,25 +250,14 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
         const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
         warp_mma<16, 32, 128, false, false>(acc, ks, kP128, ks, kP128, m0, n0);
         acc_for<16, 32>(acc, m0, n0, [&](int r, int l, float& x) {
-            Ms[r * F65 + l] = l < r ? bs[r] * x * expf(gs[r] - gs[l]) : 0.0f;
+            // only the chunk's own rows: a padded row's g is 0, and e^{0 - g_l} can overflow to inf, whose
+            // 0 * inf the blocked inverse would carry into every row
+            Ms[r * F65 + l] = (l < r && r < n) ? bs[r] * x * expf(gs[r] - gs[l]) : 0.0f;
         });
         __syncthreads();
-        // forward substitution, one row at a time: A[i][j] = delta_ij - sum_{l<i} M[i][l] A[l][j]
-        const int j = threadIdx.x & 63, part = threadIdx.x >> 6;
-        for (int i = 0; i < L; ++i) {
-            float s = 0.0f;
-            const int l0 = part * 16;
-#pragma unroll
-            for (int l = l0; l < l0 + 16; ++l)
-                if (l < i) s = fmaf(Ms[i * F65 + l], As[l * F65 + j], s);
-            red[part * L + j] = s;
-            __syncthreads();
-            if (part == 0) {
-                const float t = red[j] + red[L + j] + red[2 * L + j] + red[3 * L + j];
-                As[i * F65 + j] = j < i ? -t : (j == i ? 1.0f : 0.0f);
-            }
-            __syncthreads();
-        }
+        // A = (I + M)^-1 by blocks: the four 16x16 diagonal blocks by forward substitution (a warp each),
+        // then 16 -> 32 -> 64 with X21 = -A22 (M21 A11) (the inverse of a block lower-triangular matrix)
+        invert_unit_lower(Ms, As, reinterpret_cast<float*>(a1h));
     }
     for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
         const int i = idx >> 6, j = idx & 63;

@@ -284,9 +284,14 @@ class TrainStep:
     scalar) and leaves the adapter gradient in ``adapter.g``. ``grad_hook(layer)`` is called as each
     layer's adapter gradient becomes final in the reverse walk (the data-parallel all-reduce hook)."""
 
-    def __init__(self, model: HybridModel, adapter: Adapter, head_chunk: int = 2048):
+    def __init__(self, model: HybridModel, adapter: Adapter, head_chunk: int = 2048, keep_decoded: bool = True):
         self.model, self.adapter, self.cfg = model, adapter, model.cfg
         self.ws = Workspace(model, head_chunk)
+        # keep_decoded: each projection group is decoded once a step, in the forward, into a buffer of its
+        # own that the same layer's backward reads again (13.8 GB bf16 at config 5, against a second
+        # decode of every weight); False decodes into one shared scratch in both passes.
+        self.keep_decoded = keep_decoded
+        self.w_keep = {}
         cfg = self.cfg
         self.T = cfg.tokens
         cu = np.arange(0, self.T + 1, cfg.seq, dtype=np.int32)
@@ -294,6 +299,23 @@ class TrainStep:
         self.plan = GdnPlan(cu, cfg.gdn_heads, cfg.gdn_qk_heads, model.device)
         self.grad_hook = None
         self.launches = 0
+
+    # ------------------------------------------------------------------ decoded base weights
+    def _w_fwd(self, li, g: Group) -> torch.Tensor:
+        """The group's base weight for the forward: decoded now."""
+        if not self.keep_decoded:
+            return decode_group(g, self.ws.w_scratch)
+        buf = self.w_keep.get((li, g.name))
+        if buf is None:
+            buf = torch.empty(g.n * g.k, dtype=torch.bfloat16, device=self.model.device)
+            self.w_keep[(li, g.name)] = buf
+        return decode_group(g, buf)
+
+    def _w_bwd(self, li, g: Group) -> torch.Tensor:
+        """The group's base weight for the backward: this step's forward decode, or decoded again."""
+        if not self.keep_decoded:
+            return decode_group(g, self.ws.w_scratch)
+        return self.w_keep[(li, g.name)][:g.n * g.k].view(g.n, g.k)
 
     # ------------------------------------------------------------------ fused LoRA linear
     def _lin_fwd(self, li, g: Group, x: torch.Tensor, W: torch.Tensor, out: torch.Tensor, addend=None):
@@ -328,7 +350,7 @@ class TrainStep:
         H, Hg, K = cfg.gdn_heads, cfg.gdn_qk_heads, cfg.head_k
         g_in, g_out = blk["groups"][0], blk["groups"][1]
         n1 = ops.rmsnorm_fwd(x, blk["w_in"], eps=cfg.eps)
-        W = decode_group(g_in, self.ws.w_scratch)
+        W = self._w_fwd(li, g_in)
         y_in = torch.empty((T, g_in.n), dtype=torch.bfloat16, device=x.device)
         t_in = self._lin_fwd(li, g_in, n1, W, y_in)
         qk = Hg * K
@@ -343,7 +365,7 @@ class TrainStep:
         o, _, gsv = self.plan.forward(q, k, v, gg, beta)
         z = y_in[:, 2 * qk + H * K:2 * qk + 2 * H * K]  # read in place (strided), no copy
         on = ops.gated_rmsnorm_fwd(o.view(T * H, K), z, blk["gnorm_w"], eps=cfg.eps).view(T, H * K)
-        W = decode_group(g_out, self.ws.w_scratch)
+        W = self._w_fwd(li, g_out)
         h1 = torch.empty_like(x)
         t_out = self._lin_fwd(li, g_out, on, W, h1, addend=x)
         sv.update(n1=n1, y_in=y_in, t_in=t_in, gsv=gsv, o=o, on=on, t_out=t_out)
@@ -354,7 +376,7 @@ class TrainStep:
         H, Hg, K = cfg.gdn_heads, cfg.gdn_qk_heads, cfg.head_k
         g_in, g_out = blk["groups"][0], blk["groups"][1]
         qk = Hg * K
-        W = decode_group(g_out, self.ws.w_scratch)
+        W = self._w_bwd(li, g_out)
         don = torch.empty((T, H * K), dtype=torch.bfloat16, device=x.device)
         self._lin_bwd(li, g_out, sv["on"], sv["t_out"], W, dh1, don)
         y_in = sv["y_in"]
@@ -371,7 +393,7 @@ class TrainStep:
         ba = y_in[:, 2 * qk + 2 * H * K:]
         ops.gates_bwd(ba, blk["a_log"], blk["dt_bias"], self.plan, gr["dg"], gr["dbeta"],
                       d_yin[:, 2 * qk + 2 * H * K:])
-        W = decode_group(g_in, self.ws.w_scratch)
+        W = self._w_bwd(li, g_in)
         dn1 = torch.empty_like(x)
         self._lin_bwd(li, g_in, sv["n1"], sv["t_in"], W, d_yin, dn1)
         return ops.rmsnorm_bwd(x, blk["w_in"], dn1, addend=dh1, eps=cfg.eps)
@@ -381,7 +403,7 @@ class TrainStep:
         Hq, Hkv, Dh, B = cfg.attn_heads, cfg.attn_kv_heads, cfg.attn_head_dim, cfg.micro_batch
         g_qkv, g_o = blk["groups"][0], blk["groups"][1]
         n1 = ops.rmsnorm_fwd(x, blk["w_in"], eps=cfg.eps)
-        W = decode_group(g_qkv, self.ws.w_scratch)
+        W = self._w_fwd(li, g_qkv)
         y = torch.empty((T, g_qkv.n), dtype=torch.bfloat16, device=x.device)
         t_qkv = self._lin_fwd(li, g_qkv, n1, W, y)
         qn = 2 * Hq * Dh
@@ -398,7 +420,7 @@ class TrainStep:
             attn = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True, enable_gqa=True)
         ga = torch.empty((T, Hq * Dh), dtype=torch.bfloat16, device=x.device)
         ops.gate_mul_fwd(attn.detach(), y[:, Dh:], 2 * Dh, Hq, S, ga)
-        W = decode_group(g_o, self.ws.w_scratch)
+        W = self._w_fwd(li, g_o)
         h1 = torch.empty_like(x)
         t_o = self._lin_fwd(li, g_o, ga, W, h1, addend=x)
         sv.update(n1=n1, y=y, t_qkv=t_qkv, qkv=(qg, kg, vg), attn=attn, ga=ga, t_o=t_o)
@@ -409,7 +431,7 @@ class TrainStep:
         Hq, Hkv, Dh, B = cfg.attn_heads, cfg.attn_kv_heads, cfg.attn_head_dim, cfg.micro_batch
         g_qkv, g_o = blk["groups"][0], blk["groups"][1]
         qn = 2 * Hq * Dh
-        W = decode_group(g_o, self.ws.w_scratch)
+        W = self._w_bwd(li, g_o)
         dga = torch.empty((T, Hq * Dh), dtype=torch.bfloat16, device=x.device)
         self._lin_bwd(li, g_o, sv["ga"], sv["t_o"], W, dh1, dga)
         y = sv["y"]
@@ -423,7 +445,7 @@ class TrainStep:
         ops.qk_norm_rope_bwd(y[:, qn:], Dh, Hkv, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
                              cfg.rotary_dim, S, cfg.eps, dk.contiguous(), dy[:, qn:])
         ops.to_bhsd(dy[:, qn + Hkv * Dh:], Dh, Hkv, S, dv.contiguous(), reverse=True)
-        W = decode_group(g_qkv, self.ws.w_scratch)
+        W = self._w_bwd(li, g_qkv)
         dn1 = torch.empty_like(x)
         self._lin_bwd(li, g_qkv, sv["n1"], sv["t_qkv"], W, dy, dn1)
         return ops.rmsnorm_bwd(x, blk["w_in"], dn1, addend=dh1, eps=cfg.eps)
@@ -432,12 +454,12 @@ class TrainStep:
         cfg, T = self.cfg, self.T
         g_gu, g_d = blk["groups"][2], blk["groups"][3]
         n2 = ops.rmsnorm_fwd(h1, blk["w_post"], eps=cfg.eps)
-        W = decode_group(g_gu, self.ws.w_scratch)
+        W = self._w_fwd(li, g_gu)
         y_gu = torch.empty((T, 2 * cfg.ffn), dtype=torch.bfloat16, device=h1.device)
         t_gu = self._lin_fwd(li, g_gu, n2, W, y_gu)
         a = torch.empty((T, cfg.ffn), dtype=torch.bfloat16, device=h1.device)
         ops.swiglu_fwd(y_gu, a)
-        W = decode_group(g_d, self.ws.w_scratch)
+        W = self._w_fwd(li, g_d)
         xn = torch.empty_like(h1)
         t_d = self._lin_fwd(li, g_d, a, W, xn, addend=h1)
         sv.update(n2=n2, y_gu=y_gu, t_gu=t_gu, a=a, t_d=t_d)
@@ -446,12 +468,12 @@ class TrainStep:
     def _mlp_bwd(self, li, blk, h1, sv, dxn):
         cfg, T = self.cfg, self.T
         g_gu, g_d = blk["groups"][2], blk["groups"][3]
-        W = decode_group(g_d, self.ws.w_scratch)
+        W = self._w_bwd(li, g_d)
         da = torch.empty((T, cfg.ffn), dtype=torch.bfloat16, device=h1.device)
         self._lin_bwd(li, g_d, sv["a"], sv["t_d"], W, dxn, da)
         dgu = torch.empty_like(sv["y_gu"])
         ops.swiglu_bwd(sv["y_gu"], da, dgu)
-        W = decode_group(g_gu, self.ws.w_scratch)
+        W = self._w_bwd(li, g_gu)
         dn2 = torch.empty_like(h1)
         self._lin_bwd(li, g_gu, sv["n2"], sv["t_gu"], W, dgu, dn2)
         return ops.rmsnorm_bwd(h1, blk["w_post"], dn2, addend=dxn, eps=cfg.eps)

@@ -5,6 +5,8 @@
     python -m r97training_b200.profile_cases gdn       # one config-5 GDN layer, forward + backward
     python -m r97training_b200.profile_cases decode    # the IQR decode of a 24576 x 4096 weight
     python -m r97training_b200.profile_cases norms     # rmsnorm fwd/bwd at 8192 x 4096
+    python -m r97training_b200.profile_cases step      # one config-5 training step after one warm-up step,
+                                                       # inside an NVTX range "step" (ncu --nvtx-include step/)
 
 Each case allocates a few hundred MB to a few GB (operands larger than the 126 MB L2), runs two warm-up
 launches and then the launches to capture, and exits.
@@ -60,6 +62,22 @@ def main(case: str) -> None:
         for _ in range(3):
             ops.rmsnorm_fwd(x, w)
             ops.rmsnorm_bwd(x, w, dy, addend=dy)
+    elif case == "step":
+        from .model import CONFIG5, Adapter, HybridModel, TrainStep
+        model = HybridModel(CONFIG5, dev)
+        adapter = Adapter(model, dev)
+        step = TrainStep(model, adapter)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        ids = torch.randint(0, CONFIG5.vocab, (CONFIG5.micro_batch, CONFIG5.seq), device=dev, generator=gen,
+                            dtype=torch.int32)
+        step.run(ids)
+        adapter.adamw()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("step")
+        step.run(ids)
+        adapter.adamw()
+        torch.cuda.nvtx.range_pop()
     else:
         raise SystemExit(f"unknown case {case}")
     torch.cuda.synchronize()
