@@ -13,7 +13,7 @@
 //   F1 gdn_fwd_prep  (chunk, head)        M, A by forward substitution, w, u
 //   F2 gdn_fwd_state (seq, head, V/64)    S_c entering each chunk, V'_c = u_c - w_c S_c, S_{c+1}
 //   F3 gdn_fwd_out   (chunk, head)        P = causal(q k^T e^{g_i-g_j}), o = scale (e^g q S_c + P V'_c)
-//   B1 gdn_bwd_state (seq, head, V/32)    reverse pass: dV' = scale P^T dO + K~ dS_next,
+//   B1 gdn_bwd_state (seq, head, V/64)    reverse pass: dV' = scale P^T dO + K~ dS_next,
 //                                          dS = scale Q~^T dO + e^{g_L} dS_next - w^T dV'
 //   B2a gdn_bwd_a    (chunk, head)        the terms that read the states: dQ~ = scale dO S^T, dw = -dV' S^T,
 //                                          dK~ = V' dS_next^T, and dg_L's e^{g_L} <S, dS_next>
@@ -41,8 +41,6 @@ using bf16 = __nv_bfloat16;
 
 constexpr int D = 128;   // key / value head dim
 constexpr int L = 64;    // chunk
-constexpr int VS = 32;   // value lanes per sequential CTA
-constexpr int P32 = 40;  // bf16 pitch of a [*, 32] tile
 constexpr int F65 = 65;  // f32 pitch of a [64, 64] tile
 
 struct Dims {
@@ -74,35 +72,6 @@ __device__ __forceinline__ void put_split(bf16* hi, bf16* lo, int64_t at, float 
     lo[at] = l;
 }
 
-// f32 rows [0, 64) x 128 of [T, heads, 128] -> hi/lo tiles (pitch kP128), each row scaled by rs[i]
-// (null = 1); rows >= n zero
-__device__ __forceinline__ void stage_f32_split(bf16* hi, bf16* lo, const float* src, int64_t tok0, int n, int heads,
-                                                int head, const float* rs = nullptr) {
-    for (int idx = threadIdx.x; idx < L * 32; idx += blockDim.x) {
-        const int i = idx >> 5, c = (idx & 31) * 4;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < n) v = *reinterpret_cast<const float4*>(src + ((tok0 + i) * heads + head) * D + c);
-        const float s = rs ? rs[i] : 1.0f;
-        put_split(hi, lo, i * kP128 + c, v.x * s);
-        put_split(hi, lo, i * kP128 + c + 1, v.y * s);
-        put_split(hi, lo, i * kP128 + c + 2, v.z * s);
-        put_split(hi, lo, i * kP128 + c + 3, v.w * s);
-    }
-}
-
-// a dense f32 [rows][cols] matrix -> hi/lo tiles of pitch p
-template <int ROWS, int COLS>
-__device__ __forceinline__ void stage_mat_split(bf16* hi, bf16* lo, int p, const float* src) {
-    for (int idx = threadIdx.x; idx < ROWS * COLS / 4; idx += blockDim.x) {
-        const int e = idx * 4, r = e / COLS, c = e % COLS;
-        const float4 v = *reinterpret_cast<const float4*>(src + e);
-        put_split(hi, lo, r * p + c, v.x);
-        put_split(hi, lo, r * p + c + 1, v.y);
-        put_split(hi, lo, r * p + c + 2, v.z);
-        put_split(hi, lo, r * p + c + 3, v.w);
-    }
-}
-
 __device__ __forceinline__ void load_gb(float* gs, float* bs, const float* g, const float* beta, int64_t tok0, int n,
                                         int H, int h) {
     for (int i = threadIdx.x; i < L; i += blockDim.x) {
@@ -111,11 +80,80 @@ __device__ __forceinline__ void load_gb(float* gs, float* bs, const float* g, co
     }
 }
 
+// ---- asynchronous staging (cp.async): every f32 intermediate the kernels hand each other (V', S, dV', dS,
+// dw, w, P) is kept as a bf16 (hi, lo) pair -- hi plane then lo plane, in the bytes of its f32 buffer --
+// so a consumer copies it into its split tiles without converting. Rows past a chunk's end land as zeros.
+
+// The (hi, lo) planes of an f32 buffer of `count` values.
+struct Pair {
+    bf16* hi;
+    bf16* lo;
+};
+__device__ __forceinline__ Pair pair_of(const float* buf, int64_t count) {
+    bf16* h = const_cast<bf16*>(reinterpret_cast<const bf16*>(buf));
+    return Pair{h, h + count};
+}
+
+// rows [0, 64) of one head of a token-major [T, heads, 128] bf16 tensor -> a [64][kP128] tile
+__device__ __forceinline__ void async_rows(bf16* dst, const bf16* src, int64_t tok0, int n, int heads, int head) {
+    for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
+        const int i = idx >> 4, x = (idx & 15) * 8;
+        const bool on = i < n;
+        cp_async16(dst + i * kP128 + x, src + ((on ? tok0 + i : tok0) * heads + head) * D + x, on);
+    }
+}
+
+// the same rows of a pair buffer -> hi and lo tiles
+__device__ __forceinline__ void async_rows_pair(bf16* dh, bf16* dl, Pair src, int64_t tok0, int n, int heads,
+                                                int head) {
+    async_rows(dh, src.hi, tok0, n, heads, head);
+    async_rows(dl, src.lo, tok0, n, heads, head);
+}
+
+// one (chunk, head)'s [128][128] block of a pair buffer [chunks, H, 128, 128] -> [128][kP128] tiles
+__device__ __forceinline__ void async_block_pair(bf16* dh, bf16* dl, Pair src, int64_t block) {
+    const bf16* h = src.hi + block * D * D;
+    const bf16* l = src.lo + block * D * D;
+    for (int idx = threadIdx.x; idx < D * 16; idx += blockDim.x) {
+        const int r = idx >> 4, x = (idx & 15) * 8;
+        cp_async16(dh + r * kP128 + x, h + r * D + x, true);
+        cp_async16(dl + r * kP128 + x, l + r * D + x, true);
+    }
+}
+
+// g (and beta) of the chunk's rows; zero past its end
+__device__ __forceinline__ void async_gb(float* gs, float* bs, const float* g, const float* beta, int64_t tok0, int n,
+                                         int H, int h) {
+    for (int i = threadIdx.x; i < L; i += blockDim.x) {
+        const bool on = i < n;
+        const int64_t at = (on ? tok0 + i : tok0) * H + h;
+        cp_async4(gs + i, g + at, on);
+        if (bs) cp_async4(bs + i, beta + at, on);
+    }
+}
+
 // sum over the 4 lanes of an accumulator row quad (lanes sharing g = lane / 4)
 __device__ __forceinline__ float quad_sum(float v) {
     v += __shfl_xor_sync(0xFFFFFFFFu, v, 1);
     v += __shfl_xor_sync(0xFFFFFFFFu, v, 2);
     return v;
+}
+
+// Adds the column sums of a warp's 16 x 32 accumulator tile -- cs[j][b] holds this lane's partial for
+// column n0 + 8j + 2t + b (t = lane % 4) over its two rows -- into dst[col]: a reduction over the eight
+// lanes sharing t, then one shared-memory atomic per column instead of one per element.
+__device__ __forceinline__ void colsum_add(float (&cs)[4][2], int n0, float* dst) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int b = 0; b < 2; ++b) {
+            float v = cs[j][b];
+            v += __shfl_xor_sync(0xFFFFFFFFu, v, 4);
+            v += __shfl_xor_sync(0xFFFFFFFFu, v, 8);
+            v += __shfl_xor_sync(0xFFFFFFFFu, v, 16);
+            if (lane < 4) atomicAdd(&dst[n0 + 8 * j + 2 * lane + b], v);
+        }
 }
 
 // two- / three-pass products of split operands
@@ -274,8 +312,8 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
     mma_split_a<16, 64, 64, false, true>(acc, a1h, a1l, kP64, ks, kP128, m0, n0);
     bf16* w_hi = reinterpret_cast<bf16*>(w);             // w is kept as a bf16 (hi, lo) pair in the
     bf16* w_lo = w_hi + (int64_t)dm.T * dm.H * D;         // bytes of an f32 [T, H, 128] buffer
-    acc_for<16, 64>(acc, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) put_split(w_hi, w_lo, ((tok0 + r) * dm.H + h) * D + d, x);
+    acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {
+        if (r < n) put_split2(w_hi, w_lo, ((tok0 + r) * dm.H + h) * D + d, acc[i][j][2 * hh], acc[i][j][2 * hh + 1]);
     });
     acc_zero<16, 64>(acc);
     mma_split_a<16, 64, 64, false, true>(acc, a2h, a2l, kP64, vs, kP128, m0, n0);
@@ -339,14 +377,20 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
     float S[2][4][4];
     acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) {
         x = h0 ? h0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
-        put_split(sh, sl, d * P64 + e, x);
     });
+    acc_pairs<32, 32>(sm0, sn0, [&](int d, int e, int i, int j, int hh) {
+        put_split2(sh, sl, d * P64 + e, S[i][j][2 * hh], S[i][j][2 * hh + 1]);
+    });
+    const Pair Sp = pair_of(S_all, (int64_t)dm.n_chunks * dm.H * D * D);
+    const Pair Vpp = pair_of(Vp, dm.T * dm.H * D);
     for (int c = c0; c < c1; ++c) {
         F2Stage& st = stage[(c - c0) & 1];
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
-        float* Sg = S_all + ((int64_t)c * dm.H + h) * D * D;
-        acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) { Sg[d * D + e0 + e] = x; });
+        const int64_t sb = ((int64_t)c * dm.H + h) * D * D;
+        acc_pairs<32, 32>(sm0, sn0, [&](int d, int e, int i, int j, int hh) {
+            put_split2(Sp.hi, Sp.lo, sb + d * D + e0 + e, S[i][j][2 * hh], S[i][j][2 * hh + 1]);
+        });
         cp_async_wait_all();
         __syncthreads();  // stage c landed; S split written; every warp is past chunk c-1's products
         if (c + 1 < c1) f2_issue(stage[(c + 1 - c0) & 1], dm, w_hi, w_lo, k, u, g, c + 1, h, hk, e0);
@@ -355,10 +399,12 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
             float acc[1][4][4];
             acc_zero<16, 32>(acc);
             mma_split_ab<16, 32, 128, false, true>(acc, st.wh, st.wl, kP128, sh, sl, P64, vm0, vn0);
-            acc_for<16, 32>(acc, vm0, vn0, [&](int i, int e, float& x) {
-                const float vp = st.us[i * U68 + e] - x;
-                if (i < n) Vp[((tok0 + i) * dm.H + h) * D + e0 + e] = vp;
-                put_split(vh, vl, i * P64 + e, i < n ? vp * expf(gl - st.gs[i]) : 0.0f);
+            acc_pairs<16, 32>(vm0, vn0, [&](int i, int e, int a, int b, int hh) {
+                const float v0 = st.us[i * U68 + e] - acc[a][b][2 * hh];
+                const float v1 = st.us[i * U68 + e + 1] - acc[a][b][2 * hh + 1];
+                const float sc = i < n ? expf(gl - st.gs[i]) : 0.0f;
+                if (i < n) put_split2(Vpp.hi, Vpp.lo, ((tok0 + i) * dm.H + h) * D + e0 + e, v0, v1);
+                put_split2(vh, vl, i * P64 + e, v0 * sc, v1 * sc);
             });
         }
         __syncthreads();
@@ -371,7 +417,9 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
                 for (int e = 0; e < 4; ++e) S[a][b][e] *= el;
         mma_split_b<32, 32, 64, true, true>(S, st.ks, kP128, vh, vl, P64, sm0, sn0);
         // the next chunk's S operand (sh/sl were last read before the sync above)
-        acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) { put_split(sh, sl, d * P64 + e, x); });
+        acc_pairs<32, 32>(sm0, sn0, [&](int d, int e, int i, int j, int hh) {
+            put_split2(sh, sl, d * P64 + e, S[i][j][2 * hh], S[i][j][2 * hh + 1]);
+        });
     }
     if (ht)
         acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) {
@@ -398,11 +446,13 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
     const int warp = threadIdx.x >> 5;
-    stage_bf16(qs, q, tok0, n, dm.Hg, hk);
-    stage_bf16(ks, k, tok0, n, dm.Hg, hk);
-    stage_f32_split(vh, vl, Vp, tok0, n, dm.H, h);
-    stage_mat_split<D, D>(sh, sl, kP128, S_all + ((int64_t)c * dm.H + h) * D * D);
-    load_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
+    async_rows(qs, q, tok0, n, dm.Hg, hk);
+    async_rows(ks, k, tok0, n, dm.Hg, hk);
+    async_rows_pair(vh, vl, pair_of(Vp, dm.T * dm.H * D), tok0, n, dm.H, h);
+    async_block_pair(sh, sl, pair_of(S_all, (int64_t)dm.n_chunks * dm.H * D * D), (int64_t)c * dm.H + h);
+    async_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
+    cp_async_commit();
+    cp_async_wait_all();
     __syncthreads();
     {
         float acc[1][4][4];
@@ -413,10 +463,11 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
         bf16* P_hi = reinterpret_cast<bf16*>(P_all);
         bf16* P_lo = P_hi + (int64_t)dm.n_chunks * dm.H * L * L;
         const int64_t pbase = ((int64_t)c * dm.H + h) * L * L;
-        acc_for<16, 32>(acc, m0, n0, [&](int r, int l, float& x) {
-            const float p = (l <= r && r < n) ? x * expf(gs[r] - gs[l]) : 0.0f;
-            put_split(P_hi, P_lo, pbase + r * L + l, p);
-            put_split(ph, pl, r * kP64 + l, p);
+        acc_pairs<16, 32>(m0, n0, [&](int r, int l, int i, int j, int hh) {
+            const float p0 = (l <= r && r < n) ? acc[i][j][2 * hh] * expf(gs[r] - gs[l]) : 0.0f;
+            const float p1 = (l + 1 <= r && r < n) ? acc[i][j][2 * hh + 1] * expf(gs[r] - gs[l + 1]) : 0.0f;
+            put_split2(P_hi, P_lo, pbase + r * L + l, p0, p1);
+            put_split2(ph, pl, r * kP64 + l, p0, p1);
         });
     }
     __syncthreads();
@@ -436,19 +487,40 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
 
 // ============================================================================================ backward
 
-// B1: per (sequence, value head, 32 value lanes): the reverse state pass; dS lives in the accumulators.
-// Each chunk's operands (P and w as bf16 hi/lo pairs, q, k, the dO slice, g) stream into a double-buffered
-// stage with cp.async while the following chunk computes.
-struct B1Stage {
+// B1: per (sequence, value head, 64 value lanes): the reverse state pass; dS lives in the accumulators.
+// Each chunk's operands stream in with cp.async: the ones read late in a chunk (w as a bf16 hi/lo pair, q)
+// are double-buffered and fetched a whole chunk ahead; the ones only the dV' products read (P as a pair,
+// k, the dO slice, g) have one buffer, refilled for the next chunk as soon as those products are done.
+constexpr int VSB = 64;  // value lanes per backward-state CTA
+
+struct B1Late {
+    bf16 wh[L * kP128], wl[L * kP128], qs[L * kP128];
+};
+struct B1Early {
     bf16 ph[L * kP64], pl[L * kP64];
-    bf16 ks[L * kP128], qs[L * kP128], wh[L * kP128], wl[L * kP128];
-    bf16 dos[L * P32];
+    bf16 ks[L * kP128];
+    bf16 dos[L * kP64];
     float gs[L];
 };
 
-__device__ __forceinline__ void b1_issue(B1Stage& st, const Dims& dm, const bf16* q, const bf16* k, const bf16* w_hi,
-                                         const bf16* w_lo, const bf16* P_hi, const bf16* P_lo, const bf16* dO,
-                                         const float* g, int c, int h, int hk, int e0) {
+__device__ __forceinline__ void b1_issue_late(B1Late& st, const Dims& dm, const bf16* q, const bf16* w_hi,
+                                              const bf16* w_lo, int c, int h, int hk) {
+    const int64_t tok0 = dm.tok0[c];
+    const int n = dm.len[c];
+    for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
+        const int i = idx >> 4, x = (idx & 15) * 8;
+        const bool on = i < n;
+        const int64_t row = on ? tok0 + i : tok0;
+        cp_async16(&st.wh[i * kP128 + x], w_hi + (row * dm.H + h) * D + x, on);
+        cp_async16(&st.wl[i * kP128 + x], w_lo + (row * dm.H + h) * D + x, on);
+        cp_async16(&st.qs[i * kP128 + x], q + (row * dm.Hg + hk) * D + x, on);
+    }
+    cp_async_commit();
+}
+
+__device__ __forceinline__ void b1_issue_early(B1Early& st, const Dims& dm, const bf16* k, const bf16* P_hi,
+                                               const bf16* P_lo, const bf16* dO, const float* g, int c, int h,
+                                               int hk, int e0) {
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
     const int64_t pbase = ((int64_t)c * dm.H + h) * L * L;
@@ -457,14 +529,11 @@ __device__ __forceinline__ void b1_issue(B1Stage& st, const Dims& dm, const bf16
         const bool on = i < n;
         const int64_t row = on ? tok0 + i : tok0;
         cp_async16(&st.ks[i * kP128 + x], k + (row * dm.Hg + hk) * D + x, on);
-        cp_async16(&st.qs[i * kP128 + x], q + (row * dm.Hg + hk) * D + x, on);
-        cp_async16(&st.wh[i * kP128 + x], w_hi + (row * dm.H + h) * D + x, on);
-        cp_async16(&st.wl[i * kP128 + x], w_lo + (row * dm.H + h) * D + x, on);
         if (x < L) {
             cp_async16(&st.ph[i * kP64 + x], P_hi + pbase + i * L + x, true);
             cp_async16(&st.pl[i * kP64 + x], P_lo + pbase + i * L + x, true);
+            cp_async16(&st.dos[i * kP64 + x], dO + (row * dm.H + h) * D + e0 + x, on);
         }
-        if (x < VS) cp_async16(&st.dos[i * P32 + x], dO + (row * dm.H + h) * D + e0 + x, on);
     }
     for (int i = threadIdx.x; i < L; i += blockDim.x) {
         const bool on = i < n;
@@ -479,80 +548,94 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
                                                      const float* __restrict__ dht, float* __restrict__ dS_all,
                                                      float* __restrict__ dVp, float* __restrict__ dh0) {
     extern __shared__ __align__(16) unsigned char smraw[];
-    B1Stage* stage = reinterpret_cast<B1Stage*>(smraw);              // [2]
-    bf16* dsh = reinterpret_cast<bf16*>(smraw + 2 * sizeof(B1Stage));  // dS hi/lo [128][40]
-    bf16* dsl = dsh + D * P32;
-    bf16* egh = dsl + D * P32;                                         // e^g dO hi/lo [64][40]
-    bf16* egl = egh + L * P32;
-    bf16* dvh = egl + L * P32;                                         // dV' hi/lo [64][40]
-    bf16* dvl = dvh + L * P32;
+    B1Late* late = reinterpret_cast<B1Late*>(smraw);                          // [2]
+    B1Early* early = reinterpret_cast<B1Early*>(smraw + 2 * sizeof(B1Late));  // [1]
+    bf16* dsh = reinterpret_cast<bf16*>(smraw + 2 * sizeof(B1Late) + sizeof(B1Early));  // dS hi/lo [128][72]
+    bf16* dsl = dsh + D * kP64;
+    bf16* egh = dsl + D * kP64;  // e^g dO hi/lo [64][72]
+    bf16* egl = egh + L * kP64;
+    bf16* dvh = egl + L * kP64;  // dV' hi/lo [64][72]
+    bf16* dvl = dvh + L * kP64;
     const bf16* w_hi = reinterpret_cast<const bf16*>(w);
     const bf16* w_lo = w_hi + dm.T * dm.H * D;
     const bf16* P_hi = reinterpret_cast<const bf16*>(P_all);
     const bf16* P_lo = P_hi + (int64_t)dm.n_chunks * dm.H * L * L;
-    const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VS, hk = h / dm.grp;
+    const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VSB, hk = h / dm.grp;
     const int warp = threadIdx.x >> 5;
-    const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 16;
-    const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 16;
+    const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 32;  // this warp's dS tile (32 x 32)
+    const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 32;  // this warp's dV' tile (16 x 32)
+    const Pair dSp = pair_of(dS_all, (int64_t)dm.n_chunks * dm.H * D * D);
+    const Pair dVpp = pair_of(dVp, dm.T * dm.H * D);
     const int c0 = dm.seq_c0[seq], c1 = dm.seq_c0[seq + 1];
-    if (c0 < c1) b1_issue(stage[0], dm, q, k, w_hi, w_lo, P_hi, P_lo, dO, g, c1 - 1, h, hk, e0);
-    float dS[2][2][4];
-    acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
+    if (c0 < c1) {
+        b1_issue_late(late[0], dm, q, w_hi, w_lo, c1 - 1, h, hk);
+        b1_issue_early(*early, dm, k, P_hi, P_lo, dO, g, c1 - 1, h, hk, e0);
+    }
+    float dS[2][4][4];
+    acc_for<32, 32>(dS, sm0, sn0, [&](int d, int e, float& x) {
         x = dht ? dht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
     });
     for (int c = c1 - 1; c >= c0; --c) {
-        B1Stage& st = stage[(c1 - 1 - c) & 1];
+        B1Late& lt = late[(c1 - 1 - c) & 1];
+        B1Early& et = *early;
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
-        float* dSg = dS_all + ((int64_t)c * dm.H + h) * D * D;
-        // dsh/dsl were last read by the previous chunk's dV' products, which precede its middle barrier
-        acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
-            dSg[d * D + e0 + e] = x;
-            put_split(dsh, dsl, d * P32 + e, x);
+        const int64_t sb = ((int64_t)c * dm.H + h) * D * D;
+        // dsh/dsl were last read by the previous chunk's dV' products, before its middle barrier
+        acc_pairs<32, 32>(sm0, sn0, [&](int d, int e, int i, int j, int hh) {
+            const float x0 = dS[i][j][2 * hh], x1 = dS[i][j][2 * hh + 1];
+            put_split2(dSp.hi, dSp.lo, sb + d * D + e0 + e, x0, x1);
+            put_split2(dsh, dsl, d * kP64 + e, x0, x1);
         });
         cp_async_wait_all();
-        __syncthreads();  // stage c landed; dS split written; every warp is past chunk c+1's products
-        if (c > c0) b1_issue(stage[(c1 - c) & 1], dm, q, k, w_hi, w_lo, P_hi, P_lo, dO, g, c - 1, h, hk, e0);
-        const float gl = st.gs[n - 1];
-        for (int idx = threadIdx.x; idx < L * VS; idx += blockDim.x) {
-            const int i = idx >> 5, e = idx & 31;
-            put_split(egh, egl, i * P32 + e, __bfloat162float(st.dos[i * P32 + e]) * expf(st.gs[i]));
+        __syncthreads();  // chunk c's operands landed; dS split written; chunk c+1's products are done
+        if (c > c0) b1_issue_late(late[(c1 - c) & 1], dm, q, w_hi, w_lo, c - 1, h, hk);
+        const float gl = et.gs[n - 1];
+        for (int idx = threadIdx.x; idx < L * VSB / 2; idx += blockDim.x) {
+            const int i = idx >> 5, e = (idx & 31) * 2;
+            const float eg = expf(et.gs[i]);
+            const float2 d2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(et.dos + i * kP64 + e));
+            put_split2(egh, egl, i * kP64 + e, d2.x * eg, d2.y * eg);
         }
         {
             // dV' = scale P^T dO + e^{gL - g} (k dS)
-            float a1[1][2][4], a2[1][2][4];
-            acc_zero<16, 16>(a1);
-            acc_zero<16, 16>(a2);
-            mma_split_a<16, 16, 64, true, true>(a1, st.ph, st.pl, kP64, st.dos, P32, vm0, vn0);
-            mma_split_b<16, 16, 128, false, true>(a2, st.ks, kP128, dsh, dsl, P32, vm0, vn0);
-            acc_walk<16, 16>(vm0, vn0, [&](int j, int e, int a, int b, int x) {
-                const float dv = j < n ? dm.scale * a1[a][b][x] + expf(gl - st.gs[j]) * a2[a][b][x] : 0.0f;
-                if (j < n) dVp[((tok0 + j) * dm.H + h) * D + e0 + e] = dv;
-                put_split(dvh, dvl, j * P32 + e, dv);
+            float a1[1][4][4], a2[1][4][4];
+            acc_zero<16, 32>(a1);
+            acc_zero<16, 32>(a2);
+            mma_split_a<16, 32, 64, true, true>(a1, et.ph, et.pl, kP64, et.dos, kP64, vm0, vn0);
+            mma_split_b<16, 32, 128, false, true>(a2, et.ks, kP128, dsh, dsl, kP64, vm0, vn0);
+            acc_pairs<16, 32>(vm0, vn0, [&](int j, int e, int a, int b, int hh) {
+                const float sc = j < n ? expf(gl - et.gs[j]) : 0.0f;
+                const float d0 = j < n ? dm.scale * a1[a][b][2 * hh] + sc * a2[a][b][2 * hh] : 0.0f;
+                const float d1 = j < n ? dm.scale * a1[a][b][2 * hh + 1] + sc * a2[a][b][2 * hh + 1] : 0.0f;
+                if (j < n) put_split2(dVpp.hi, dVpp.lo, ((tok0 + j) * dm.H + h) * D + e0 + e, d0, d1);
+                put_split2(dvh, dvl, j * kP64 + e, d0, d1);
             });
         }
-        __syncthreads();
+        __syncthreads();  // dV' written; chunk c's P, k, dO and g are no longer read
+        if (c > c0) b1_issue_early(*early, dm, k, P_hi, P_lo, dO, g, c - 1, h, hk, e0);
         // dS = e^{gL} dS + scale q^T (e^g dO) - w^T dV'
         const float el = expf(gl);
-        float t1[2][2][4], t2[2][2][4];
-        acc_zero<32, 16>(t1);
-        acc_zero<32, 16>(t2);
-        mma_split_b<32, 16, 64, true, true>(t1, st.qs, kP128, egh, egl, P32, sm0, sn0);
-        mma_split_ab<32, 16, 64, true, true>(t2, st.wh, st.wl, kP128, dvh, dvl, P32, sm0, sn0);
+        float t1[2][4][4], t2[2][4][4];
+        acc_zero<32, 32>(t1);
+        acc_zero<32, 32>(t2);
+        mma_split_b<32, 32, 64, true, true>(t1, lt.qs, kP128, egh, egl, kP64, sm0, sn0);
+        mma_split_ab<32, 32, 64, true, true>(t2, lt.wh, lt.wl, kP128, dvh, dvl, kP64, sm0, sn0);
 #pragma unroll
         for (int a = 0; a < 2; ++a)
 #pragma unroll
-            for (int b = 0; b < 2; ++b)
+            for (int b = 0; b < 4; ++b)
 #pragma unroll
                 for (int e = 0; e < 4; ++e) dS[a][b][e] = el * dS[a][b][e] + dm.scale * t1[a][b][e] - t2[a][b][e];
     }
     if (dh0)
-        acc_for<32, 16>(dS, sm0, sn0, [&](int d, int e, float& x) {
+        acc_for<32, 32>(dS, sm0, sn0, [&](int d, int e, float& x) {
             dh0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] = x;
         });
 }
 
-// B2a: per (chunk, value head): the state-reading terms.
+// B2a: per (chunk, value head): the state-reading terms. Its operands arrive in three cp.async groups:
+// what dQ~ and dw read (S, dO, q, dV', g), then dS_next, then (into the tiles dQ~ and dw free) V' and k.
 __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                  const float* __restrict__ g, const float* __restrict__ S_all,
                                                  const float* __restrict__ Vp, const bf16* __restrict__ dO,
@@ -560,9 +643,11 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
                                                  float* __restrict__ dw, float* __restrict__ pdq, float* __restrict__ pdk,
                                                  float* __restrict__ pdg) {
     extern __shared__ __align__(16) unsigned char smraw[];
-    bf16* sh = reinterpret_cast<bf16*>(smraw);   // S hi/lo [128][136], then dS_next
+    bf16* sh = reinterpret_cast<bf16*>(smraw);   // S hi/lo [128][136]
     bf16* sl = sh + D * kP128;
-    bf16* xs = sl + D * kP128;                   // dO [64][136], then k
+    bf16* th = sl + D * kP128;                   // dS_next hi/lo [128][136]
+    bf16* tl = th + D * kP128;
+    bf16* xs = tl + D * kP128;                   // dO [64][136], then k
     bf16* qs = xs + L * kP128;                   // q [64][136]
     bf16* yh = qs + L * kP128;                   // dV' hi/lo [64][136], then V' hi/lo
     bf16* yl = yh + L * kP128;
@@ -574,12 +659,18 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
     const int n = dm.len[c];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
-    stage_mat_split<D, D>(sh, sl, kP128, S_all + ((int64_t)c * dm.H + h) * D * D);
-    stage_bf16(xs, dO, tok0, n, dm.H, h);
-    stage_bf16(qs, q, tok0, n, dm.Hg, hk);
-    stage_f32_split(yh, yl, dVp, tok0, n, dm.H, h);
-    load_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
+    const int64_t nb = (int64_t)dm.n_chunks * dm.H * D * D, nt = dm.T * dm.H * D;
+    const int64_t blk = (int64_t)c * dm.H + h;
+    async_block_pair(sh, sl, pair_of(S_all, nb), blk);
+    async_rows(xs, dO, tok0, n, dm.H, h);
+    async_rows(qs, q, tok0, n, dm.Hg, hk);
+    async_rows_pair(yh, yl, pair_of(dVp, nt), tok0, n, dm.H, h);
+    async_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
+    cp_async_commit();
+    async_block_pair(th, tl, pair_of(dS_all, nb), blk);
+    cp_async_commit();
     for (int i = threadIdx.x; i < L; i += blockDim.x) dgs[i] = 0.0f;
+    cp_async_wait_but_one();
     __syncthreads();
     float dq[1][8][4];
     {
@@ -602,40 +693,41 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
     }
     {
         // dw = -dV' S^T
+        const Pair dwp = pair_of(dw, nt);
         float acc[1][8][4];
         acc_zero<16, 64>(acc);
         mma_split_ab<16, 64, 128, false, false>(acc, yh, yl, kP128, sh, sl, kP128, m0, n0);
-        acc_for<16, 64>(acc, m0, n0, [&](int r, int d, float& x) {
-            if (r < n) dw[((tok0 + r) * dm.H + h) * D + d] = -x;
+        acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {
+            if (r < n) put_split2(dwp.hi, dwp.lo, ((tok0 + r) * dm.H + h) * D + d, -acc[i][j][2 * hh], -acc[i][j][2 * hh + 1]);
         });
     }
+    __syncthreads();  // dO and dV' are no longer read
+    async_rows_pair(yh, yl, pair_of(Vp, nt), tok0, n, dm.H, h);
+    async_rows(xs, k, tok0, n, dm.Hg, hk);
+    cp_async_commit();
+    cp_async_wait_but_one();  // dS_next landed
     __syncthreads();
-    // <S, dS_next> against the f32 state, then dS_next replaces S in the tiles
-    const float* Sg = S_all + ((int64_t)c * dm.H + h) * D * D;
-    const float* dSg = dS_all + ((int64_t)c * dm.H + h) * D * D;
+    // <S, dS_next> from the pairs, while V' and k land
     float sdot = 0.0f;
-    for (int idx = threadIdx.x; idx < D * D / 4; idx += blockDim.x) {
-        const float4 s4 = *reinterpret_cast<const float4*>(Sg + idx * 4);
-        const float4 d4 = *reinterpret_cast<const float4*>(dSg + idx * 4);
-        sdot += s4.x * d4.x + s4.y * d4.y + s4.z * d4.z + s4.w * d4.w;
-        const int r = (idx * 4) >> 7, cc = (idx * 4) & 127;
-        put_split(sh, sl, r * kP128 + cc, d4.x);
-        put_split(sh, sl, r * kP128 + cc + 1, d4.y);
-        put_split(sh, sl, r * kP128 + cc + 2, d4.z);
-        put_split(sh, sl, r * kP128 + cc + 3, d4.w);
+    for (int idx = threadIdx.x; idx < D * D / 2; idx += blockDim.x) {
+        const int r = (idx * 2) >> 7, cc = (idx * 2) & 127;
+        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sh + r * kP128 + cc));
+        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sl + r * kP128 + cc));
+        const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(th + r * kP128 + cc));
+        const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(tl + r * kP128 + cc));
+        sdot += (a.x + b.x) * (x.x + y.x) + (a.y + b.y) * (x.y + y.y);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xFFFFFFFFu, sdot, o);
     if (lane == 0) red[warp] = sdot;
-    stage_f32_split(yh, yl, Vp, tok0, n, dm.H, h);
-    stage_bf16(xs, k, tok0, n, dm.Hg, hk);
+    cp_async_wait_all();
     __syncthreads();
     const float gl = gs[n - 1];
     float dk[1][8][4];
     {
         // dK~ = V' dS_next^T ; dk_j = e^{gL-gj} dK~_j ; dg_j -= K~_j . dK~_j ; dg_L += their sum
         acc_zero<16, 64>(dk);
-        mma_split_ab<16, 64, 128, false, false>(dk, yh, yl, kP128, sh, sl, kP128, m0, n0);
+        mma_split_ab<16, 64, 128, false, false>(dk, yh, yl, kP128, th, tl, kP128, m0, n0);
         float p0 = 0.0f, p1 = 0.0f;
         acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
             float& x = dk[i][j][q];
@@ -688,15 +780,17 @@ __device__ __forceinline__ void kkt_adjoint(const bf16* ah, const bf16* al, bf16
         mma_split_ab<16, 32, 64, true, true>(acc, ah, al, kP64, yh, yl, kP64, pm0, pn0);
         __syncthreads();  // every warp has read dA (th/tl) before E overwrites it
         float b0 = 0.0f, b1 = 0.0f, g0 = 0.0f, g1 = 0.0f;
+        float cs[4][2] = {};
         acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
             const bool on = l < r && r < n;
             const float dm_ = on ? -acc[i][j][q] : 0.0f;
             const float kh = Cs[r * F65 + l];
             const float gg = dm_ * bs[r] * kh;
             if (q >> 1) { b1 += dm_ * kh; g1 += gg; } else { b0 += dm_ * kh; g0 += gg; }
-            if (on) atomicAdd(&dgs[l], -gg);
+            cs[j][q & 1] -= gg;  // zero off the strict lower block
             put_split(th, tl, r * kP64 + l, on ? dm_ * bs[r] * expf(gs[r] - gs[l]) : 0.0f);
         });
+        colsum_add(cs, pn0, dgs);
         b0 = quad_sum(b0);
         b1 = quad_sum(b1);
         g0 = quad_sum(g0);
@@ -750,15 +844,24 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
     const int pm0 = (warp & 3) * 16, pn0 = (warp >> 2) * 32;   // [64 x 64] warp tile
     const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;     // [64 x 128] warp tile
     const bool split = (dm.flags & R97B_GDN_SPLIT_KKT) != 0;
-    stage_bf16(ks, k, tok0, n, dm.Hg, hk);
-    stage_bf16(qv, q, tok0, n, dm.Hg, hk);
-    stage_bf16(dos, dO, tok0, n, dm.H, h);
-    stage_f32_split(xh, xl, Vp, tok0, n, dm.H, h);
-    load_gb(gs, bs, g, beta, tok0, n, dm.H, h);
+    const int64_t nt = dm.T * dm.H * D;
+    async_rows(ks, k, tok0, n, dm.Hg, hk);
+    async_rows(qv, q, tok0, n, dm.Hg, hk);
+    async_rows(dos, dO, tok0, n, dm.H, h);
+    async_rows_pair(xh, xl, pair_of(Vp, nt), tok0, n, dm.H, h);
+    async_rows_pair(dvh, dvl, pair_of(dVp, nt), tok0, n, dm.H, h);
+    async_gb(gs, bs, g, beta, tok0, n, dm.H, h);
+    cp_async_commit();
+    // A (the caller's f32) is split by hand while the copies fly
+    for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
+        const int i = idx >> 6, j = idx & 63;
+        put_split(ah, al, i * kP64 + j, i < n ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f);
+    }
     for (int i = threadIdx.x; i < L; i += blockDim.x) {
         dgs[i] = 0.0f;
         dbs[i] = 0.0f;
     }
+    cp_async_wait_all();
     __syncthreads();
     {
         float qk[1][4][4], kk[1][4][4], dp[1][4][4];
@@ -769,6 +872,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
         warp_mma<16, 32, 128, false, false>(kk, ks, kP128, ks, kP128, pm0, pn0);
         mma_split_b<16, 32, 128, false, false>(dp, dos, kP128, xh, xl, kP128, pm0, pn0);
         float r0 = 0.0f, r1 = 0.0f;
+        float cs[4][2] = {};
         acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
             const bool on = l <= r && r < n;
             // e^{g_r - g_l} only where l <= r: above the diagonal it can overflow (g decreases within a
@@ -777,10 +881,11 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
             const float dpv = on ? dm.scale * dp[i][j][q] : 0.0f;
             const float dd = dpv * qk[i][j][q] * phi;
             if (q >> 1) r1 += dd; else r0 += dd;
-            if (on) atomicAdd(&dgs[l], -dd);
+            cs[j][q & 1] -= dd;  // dd is zero off the lower triangle
             put_split(th, tl, r * kP64 + l, on ? dpv * phi : 0.0f);
             Cs[r * F65 + l] = (l < r && r < n) ? kk[i][j][q] * phi : 0.0f;
         });
+        colsum_add(cs, pn0, dgs);
         r0 = quad_sum(r0);
         r1 = quad_sum(r1);
         if ((lane & 3) == 0) {
@@ -794,15 +899,11 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
     acc_zero<16, 64>(dka);
     mma_split_a<16, 64, 64, false, true>(dqa, th, tl, kP64, ks, kP128, m0, n0);  // dq += gated dP k
     mma_split_a<16, 64, 64, true, true>(dka, th, tl, kP64, qv, kP128, m0, n0);   // dk += gated dP^T q
-    __syncthreads();
-    // v, dw, dV', A
-    stage_bf16(qv, v, tok0, n, dm.H, h);
-    stage_f32_split(xh, xl, dw, tok0, n, dm.H, h);
-    stage_f32_split(dvh, dvl, dVp, tok0, n, dm.H, h);
-    for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
-        const int i = idx >> 6, j = idx & 63;
-        put_split(ah, al, i * kP64 + j, i < n ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f);
-    }
+    __syncthreads();  // q and V' are no longer read
+    async_rows(qv, v, tok0, n, dm.H, h);
+    async_rows_pair(xh, xl, pair_of(dw, nt), tok0, n, dm.H, h);
+    cp_async_commit();
+    cp_async_wait_all();
     __syncthreads();
     {
         // dA = dw kb^T + dV' vb^T, strict lower ; kb_j = beta_j e^{g_j} k_j, vb_j = beta_j v_j
@@ -962,8 +1063,8 @@ __global__ void gdn_sum_heads_kernel(const float* __restrict__ src, float* __res
 constexpr size_t kSmemPrep = (2 * L * kP128 + 4 * L * kP64) * 2 + (2 * L * F65 + 4 * L + 2 * L) * 4;
 constexpr size_t kSmemState = 2 * sizeof(F2Stage) + (2 * D * P64 + 2 * L * P64) * 2;
 constexpr size_t kSmemOut = (4 * L * kP128 + 2 * D * kP128 + 2 * L * kP64) * 2 + L * 4;
-constexpr size_t kSmemBState = 2 * sizeof(B1Stage) + (2 * D * P32 + 4 * L * P32) * 2;
-constexpr size_t kSmemBA = (2 * D * kP128 + 4 * L * kP128) * 2 + (2 * L + 8) * 4;
+constexpr size_t kSmemBState = 2 * sizeof(B1Late) + sizeof(B1Early) + (2 * D * kP64 + 4 * L * kP64) * 2;
+constexpr size_t kSmemBA = (4 * D * kP128 + 4 * L * kP128) * 2 + (2 * L + 8) * 4;
 constexpr size_t kSmemBB = (7 * L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 constexpr size_t kSmemKB = (L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 
@@ -1047,7 +1148,7 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
     const auto* k = reinterpret_cast<const bf16*>(a->k);
     const auto* v = reinterpret_cast<const bf16*>(a->v);
     const auto* dO = reinterpret_cast<const bf16*>(a->dO);
-    gdn_bwd_state<<<dim3(dm.n_seq, dm.H, D / VS), 256, kSmemBState, s>>>(dm, q, k, a->g, a->w, a->P, dO, a->dht,
+    gdn_bwd_state<<<dim3(dm.n_seq, dm.H, D / VSB), 256, kSmemBState, s>>>(dm, q, k, a->g, a->w, a->P, dO, a->dht,
                                                                         a->dS, a->dVp, a->dh0);
     if (dm.n_chunks > 0) {
         gdn_bwd_a<<<dim3(dm.n_chunks, dm.H), 256, kSmemBA, s>>>(dm, q, k, a->g, a->S, a->Vp, dO, a->dS, a->dVp, a->dw,

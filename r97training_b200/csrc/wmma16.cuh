@@ -125,6 +125,28 @@ __device__ __forceinline__ void acc_walk(int m0, int n0, F&& fn) {
             for (int e = 0; e < 4; ++e) fn(m0 + 16 * i + g + ((e >> 1) << 3), n0 + 8 * j + 2 * t + (e & 1), i, j, e);
 }
 
+// The walk by column pairs: each lane's accumulator holds two adjacent columns (2t, 2t+1) of a row, so a
+// store of both is one 4-byte access. fn(row, col, i, j, h) with the pair acc[i][j][2h], acc[i][j][2h + 1]
+// at (row, col) and (row, col + 1).
+template <int WM, int WN, typename F>
+__device__ __forceinline__ void acc_pairs(int m0, int n0, F&& fn) {
+    const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int i = 0; i < WM / 16; ++i)
+#pragma unroll
+        for (int j = 0; j < WN / 8; ++j)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) fn(m0 + 16 * i + g + 8 * h, n0 + 8 * j + 2 * t, i, j, h);
+}
+
+// x0, x1 -> their (hi, lo) bf16 pairs at hi[at], hi[at + 1] and lo[at], lo[at + 1] (at even)
+__device__ __forceinline__ void put_split2(__nv_bfloat16* hi, __nv_bfloat16* lo, int64_t at, float x0, float x1) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+    const float2 hf = __bfloat1622float2(h);
+    *reinterpret_cast<__nv_bfloat162*>(hi + at) = h;
+    *reinterpret_cast<__nv_bfloat162*>(lo + at) = __floats2bfloat162_rn(x0 - hf.x, x1 - hf.y);
+}
+
 // ------------------------------------------------------------------- asynchronous global -> shared copies
 // cp.async with a source size of 0 writes zeros (rows past a chunk's end); `src` must still be a valid
 // address, so callers clamp it.
@@ -138,6 +160,8 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src, bool pred)
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// every committed group but the most recent one has landed
+__device__ __forceinline__ void cp_async_wait_but_one() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 
 // x -> (hi, lo) bf16 pair with hi + lo ~ x to about 16 bits
 __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16& hi, __nv_bfloat16& lo) {
