@@ -102,7 +102,9 @@ enum {
 /* D[M, N] = alpha * (A1[M, K1] B1[N, K1]^T + A2[M, K2] B2[N, K2]^T) (+ beta * addend), on tcgen05 tensor
  * cores with f32 accumulation in TMEM. K2 = 0 drops the second segment; when present, a2/b2 have the
  * same majorness as a1/b1. `splits` > 1 splits the reduction (atomic epilogues only). `bn` picks the
- * tile width (64, 128, 256; 0 = by N).
+ * tile: 64, 128 or 256 wide on one SM (128 rows), 512 for a 256 x 256 tile computed by a pair of SMs
+ * (tcgen05 cta_group::2, half the operand bytes per multiply-add); 0 picks by shape (the pair for
+ * M, N > 128).
  * Replaces: the reference's linear_dx_kernel (src/adjoint/device/linear.hip:172-285) and the LoRA
  * kernels shrink_dx / shrink_da / expand_dt / expand_db (src/adjoint/device/lora.hip:268-399). */
 typedef struct R97bGemm {

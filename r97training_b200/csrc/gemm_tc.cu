@@ -54,6 +54,64 @@ struct Cfg {
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// The epilogue of 32 accumulator columns [n0, n0 + 32) of row m (r = the raw f32 bits), per args.mode.
+__device__ __forceinline__ void epilogue32(const KernelArgs& args, int m, int n0, const uint32_t (&r)[32]) {
+    const bool full = n0 + 32 <= args.N;
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
+    if (args.mode == kEpiStoreBf16) {
+        if (args.addend) {
+            const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+                if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
+        }
+        __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)m * args.ldo + n0;
+        if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+                uint4 pk;
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(v[i], v[i + 1]);
+                __nv_bfloat162 h1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
+                __nv_bfloat162 h3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
+                pk.x = *reinterpret_cast<uint32_t*>(&h0);
+                pk.y = *reinterpret_cast<uint32_t*>(&h1);
+                pk.z = *reinterpret_cast<uint32_t*>(&h2);
+                pk.w = *reinterpret_cast<uint32_t*>(&h3);
+                *reinterpret_cast<uint4*>(op + i) = pk;
+            }
+        } else {
+            for (int i = 0; i < 32; ++i)
+                if (n0 + i < args.N) op[i] = __float2bfloat16_rn(v[i]);
+        }
+    } else if (args.mode == kEpiStoreF32) {
+        float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
+        if (args.addend) {
+            const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
+            for (int i = 0; i < 32; ++i)
+                if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
+        }
+        if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(op + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+        } else {
+            for (int i = 0; i < 32; ++i)
+                if (n0 + i < args.N) op[i] = v[i];
+        }
+    } else if (args.mode == kEpiAtomicF32) {
+        float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
+        for (int i = 0; i < 32; ++i)
+            if (full || n0 + i < args.N) atomicAdd(op + i, v[i]);
+    } else {  // kEpiAtomicF32T: out[n, m] += acc[m, n]
+        float* op = reinterpret_cast<float*>(args.out) + (int64_t)n0 * args.ldo + m;
+        for (int i = 0; i < 32; ++i)
+            if (full || n0 + i < args.N) atomicAdd(op + (int64_t)i * args.ldo, v[i]);
+    }
+}
+
 template <int BN, int A_MN, int B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tA1, const __grid_constant__ CUtensorMap tB1,
@@ -211,60 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_wait();
                 const int n0 = tn * BN + c * 32;
                 if (!mrow || n0 >= args.N) continue;
-                const bool full = n0 + 32 <= args.N;
-                float v[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
-                if (args.mode == kEpiStoreBf16) {
-                    if (args.addend) {
-                        const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
-#pragma unroll
-                        for (int i = 0; i < 32; ++i)
-                            if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
-                    }
-                    __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)m * args.ldo + n0;
-                    if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 8) {
-                            uint4 pk;
-                            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[i], v[i + 1]);
-                            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
-                            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
-                            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
-                            pk.x = *reinterpret_cast<uint32_t*>(&h0);
-                            pk.y = *reinterpret_cast<uint32_t*>(&h1);
-                            pk.z = *reinterpret_cast<uint32_t*>(&h2);
-                            pk.w = *reinterpret_cast<uint32_t*>(&h3);
-                            *reinterpret_cast<uint4*>(op + i) = pk;
-                        }
-                    } else {
-                        for (int i = 0; i < 32; ++i)
-                            if (n0 + i < args.N) op[i] = __float2bfloat16_rn(v[i]);
-                    }
-                } else if (args.mode == kEpiStoreF32) {
-                    float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
-                    if (args.addend) {
-                        const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
-                        for (int i = 0; i < 32; ++i)
-                            if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
-                    }
-                    if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
-#pragma unroll
-                        for (int i = 0; i < 32; i += 4)
-                            *reinterpret_cast<float4*>(op + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-                    } else {
-                        for (int i = 0; i < 32; ++i)
-                            if (n0 + i < args.N) op[i] = v[i];
-                    }
-                } else if (args.mode == kEpiAtomicF32) {
-                    float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
-                    for (int i = 0; i < 32; ++i)
-                        if (full || n0 + i < args.N) atomicAdd(op + i, v[i]);
-                } else {  // kEpiAtomicF32T: out[n, m] += acc[m, n]
-                    float* op = reinterpret_cast<float*>(args.out) + (int64_t)n0 * args.ldo + m;
-                    for (int i = 0; i < 32; ++i)
-                        if (full || n0 + i < args.N) atomicAdd(op + (int64_t)i * args.ldo, v[i]);
-                }
+                epilogue32(args, m, n0, r);
             }
             tc_fence_before();
             mbar_arrive(&tempty_bar[acc]);
@@ -276,6 +281,201 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, C::kTmemCols);
+    }
+}
+
+
+// ---------------------------------------------------------------------------- the CTA-pair kernel
+// A cluster of two CTAs on two SMs computes 256 x 256 tiles with tcgen05.mma.cta_group::2: CTA rank r
+// loads rows [128 r, 128 r + 128) of the tile's A and of its B into its own shared memory (same offsets
+// in both), the leader (rank 0) issues M = 256, N = 256 MMAs that read both CTAs' halves, and each CTA
+// drains its own 128 rows of the accumulator from its own tensor memory. Per SM that is half the operand
+// bytes per multiply-add of the single-CTA 128 x 256 tile. The peer's TMA loads complete on the leader's
+// "full" barrier; the leader's commits arrive on both CTAs' "empty" and "accumulator full" barriers; both
+// CTAs' epilogues arrive on the leader's "accumulator empty" barrier. Every wait is bounded.
+struct CfgPair {
+    static constexpr int kHalfBytes = 128 * kBK * 2;           // one CTA's 128 x 64 slice of A or B: 16 KiB
+    static constexpr int kStageBytes = 2 * kHalfBytes;         // its A and B slices
+    static constexpr int kStages = 6;
+    static constexpr int kTmemCols = 512;                      // two 256-column accumulators
+    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+};
+
+template <int A_MN, int B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tA1, const __grid_constant__ CUtensorMap tB1,
+                     const __grid_constant__ CUtensorMap tA2, const __grid_constant__ CUtensorMap tB2,
+                     const KernelArgs args) {
+    using C = CfgPair;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t base_u32 = smem_u32(smem_raw);
+    uint8_t* smem = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u);
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint64_t* empty_bar = full_bar + C::kStages;
+    uint64_t* tfull_bar = empty_bar + C::kStages;
+    uint64_t* tempty_bar = tfull_bar + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();  // 0: the leader, 1: its peer
+    const bool leader = rank == 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < C::kStages; ++s) {
+            mbar_init(&full_bar[s], 1);   // the leader's expect_tx; both CTAs' bytes
+            mbar_init(&empty_bar[s], 1);  // the leader's commit
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&tfull_bar[a], 1);
+            mbar_init(&tempty_bar[a], 256);  // both CTAs' 128 epilogue threads (used on the leader)
+        }
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair(tmem_slot, C::kTmemCols);
+        tmem_relinquish_pair();
+    }
+    if (warp == 0 && lane == 0) {
+        tma_prefetch(&tA1);
+        tma_prefetch(&tB1);
+        if (args.k2_blocks > 0) {
+            tma_prefetch(&tA2);
+            tma_prefetch(&tB2);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers are initialised before either signals the other's
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    const int k_total = args.k1_blocks + args.k2_blocks;
+    const int tiles = args.tiles_m * args.tiles_n;  // 256 x 256 tiles
+    const int units = tiles * args.splits;
+    const int pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+
+    if (warp == 0 && lane == 0) {
+        // ------------------------------------------------------------- TMA producer (both CTAs)
+        int stage = 0;
+        uint32_t phase = 0;
+        for (int u = pair; u < units; u += pairs) {
+            const int split = u / tiles;
+            const int tile = u % tiles;
+            const int tm = tile % args.tiles_m;
+            const int tn = tile / args.tiles_m;
+            const int kb0 = split * args.kb_per_split;
+            const int kb1 = min(k_total, kb0 + args.kb_per_split);
+            bool ok = true;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t* sa = smem + stage * C::kStageBytes;
+                uint8_t* sb = sa + C::kHalfBytes;
+                const uint32_t bar = cluster_addr(&full_bar[stage], 0);  // the leader's
+                if (leader) mbar_expect_tx(&full_bar[stage], 2 * C::kStageBytes);
+                const bool seg2 = kb >= args.k1_blocks;
+                const CUtensorMap* ma = seg2 ? &tA2 : &tA1;
+                const CUtensorMap* mb = seg2 ? &tB2 : &tB1;
+                const int k = (seg2 ? kb - args.k1_blocks : kb) * kBK;
+                const int m0 = tm * 256 + 128 * (int)rank, n0 = tn * 256 + 128 * (int)rank;
+                if (A_MN) {
+                    tma_load_2d_pair(sa, ma, bar, m0, k);
+                    tma_load_2d_pair(sa + 8192, ma, bar, m0 + 64, k);
+                } else {
+                    tma_load_2d_pair(sa, ma, bar, k, m0);
+                }
+                if (B_MN) {
+                    tma_load_2d_pair(sb, mb, bar, n0, k);
+                    tma_load_2d_pair(sb + 8192, mb, bar, n0 + 64, k);
+                } else {
+                    tma_load_2d_pair(sb, mb, bar, k, n0);
+                }
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+        }
+    } else if (warp == 1 && lane == 0 && leader) {
+        // ------------------------------------------------------------- MMA issuer (the leader)
+        constexpr uint32_t idesc = make_idesc_bf16(256, 256, A_MN, B_MN);
+        int stage = 0;
+        uint32_t phase = 0;
+        int local = 0;
+        for (int u = pair; u < units; u += pairs, ++local) {
+            const int split = u / tiles;
+            const int kb0 = split * args.kb_per_split;
+            const int kb1 = min(k_total, kb0 + args.kb_per_split);
+            const int acc = local & 1;
+            if (!mbar_wait(&tempty_bar[acc], ((local >> 1) & 1) ^ 1u, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
+            bool ok = true;
+            for (int kb = kb0; kb < kb1; ++kb) {
+                if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
+                const uint32_t sb = sa + C::kHalfBytes;
+#pragma unroll
+                for (int kk = 0; kk < kBK / 16; ++kk) {
+                    const uint64_t ad = A_MN ? make_sdesc_sw128(sa + kk * 2048, 8192, 1024)
+                                             : make_sdesc_sw128(sa + kk * 32, 16, 1024);
+                    const uint64_t bd = B_MN ? make_sdesc_sw128(sb + kk * 2048, 8192, 1024)
+                                             : make_sdesc_sw128(sb + kk * 32, 16, 1024);
+                    umma_f16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+                }
+                umma_commit_pair(&empty_bar[stage], 0x3);
+                if (++stage == C::kStages) {
+                    stage = 0;
+                    phase ^= 1u;
+                }
+            }
+            if (!ok) break;
+            umma_commit_pair(&tfull_bar[acc], 0x3);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------- epilogue (both CTAs)
+        const int q = warp & 3;
+        int local = 0;
+        for (int u = pair; u < units; u += pairs, ++local) {
+            const int tile = u % tiles;
+            const int tm = tile % args.tiles_m;
+            const int tn = tile / args.tiles_m;
+            const int acc = local & 1;
+            if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag)) break;
+            tc_fence_after();
+            const int m = tm * 256 + 128 * (int)rank + q * 32 + lane;
+            const bool mrow = m < args.M;
+#pragma unroll 1
+            for (int c = 0; c < 256 / 32; ++c) {
+                uint32_t r[32];
+                __syncwarp();
+                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256 + c * 32), r);
+                tmem_ld_wait();
+                const int n0 = tn * 256 + c * 32;
+                if (!mrow || n0 >= args.N) continue;
+                epilogue32(args, m, n0, r);
+            }
+            tc_fence_before();
+            mbar_arrive_cluster(cluster_addr(&tempty_bar[acc], 0));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // neither CTA leaves while the other may still signal its barriers or use its TMEM
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, C::kTmemCols);
     }
 }
 
@@ -374,6 +574,51 @@ int launch(const R97bGemm& g, cudaStream_t stream) {
     return launch_status();
 }
 
+template <int A_MN, int B_MN>
+int launch_pair(const R97bGemm& g, cudaStream_t stream) {
+    using C = CfgPair;
+    CUtensorMap a1, b1, a2, b2;
+    if (!operand_map(&a1, g.a1, g.M, g.K1, 128)) return R97B_EINVAL;
+    if (!operand_map(&b1, g.b1, g.N, g.K1, 128)) return R97B_EINVAL;
+    if (g.K2 > 0) {
+        if (!operand_map(&a2, g.a2, g.M, g.K2, 128)) return R97B_EINVAL;
+        if (!operand_map(&b2, g.b2, g.N, g.K2, 128)) return R97B_EINVAL;
+    } else {
+        a2 = a1;
+        b2 = b1;
+    }
+    KernelArgs k{};
+    k.M = (int32_t)g.M;
+    k.N = (int32_t)g.N;
+    k.k1_blocks = (int32_t)((g.K1 + kBK - 1) / kBK);
+    k.k2_blocks = g.K2 > 0 ? (int32_t)((g.K2 + kBK - 1) / kBK) : 0;
+    const int k_total = k.k1_blocks + k.k2_blocks;
+    int splits = g.splits > 1 ? g.splits : 1;
+    if (splits > k_total) splits = k_total;
+    k.kb_per_split = (k_total + splits - 1) / splits;
+    k.splits = (k_total + k.kb_per_split - 1) / k.kb_per_split;
+    k.tiles_m = (int32_t)((g.M + 255) / 256);
+    k.tiles_n = (int32_t)((g.N + 255) / 256);
+    k.mode = g.mode;
+    k.alpha = g.alpha;
+    k.beta = g.beta;
+    k.out = g.out;
+    k.ldo = g.ldo;
+    k.addend = reinterpret_cast<const __nv_bfloat16*>(g.addend);
+    k.ld_add = g.ld_add;
+    const int units = k.tiles_m * k.tiles_n * k.splits;
+    int pairs = num_sms() / 2;
+    if (units < pairs) pairs = units;
+    auto kern = gemm_pair_kernel<A_MN, B_MN>;
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+        attr_set = true;
+    }
+    kern<<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(a1, b1, a2, b2, k);
+    return launch_status();
+}
+
 template <int BN>
 int dispatch_major(const R97bGemm& g, cudaStream_t s) {
     const int a = g.a1.mn_major ? 1 : 0, b = g.b1.mn_major ? 1 : 0;
@@ -394,7 +639,14 @@ int gemm_run(const R97bGemm& g, cudaStream_t stream) {
     if (g.mode < kEpiStoreBf16 || g.mode > kEpiAtomicF32T) return R97B_EINVAL;
     if (g.M > 0x7FFFFFFF || g.N > 0x7FFFFFFF) return R97B_EINVAL;
     int bn = g.bn;
-    if (bn == 0) bn = g.N <= 64 ? 64 : (g.N <= 128 ? 128 : 256);
+    if (bn == 0) bn = g.N <= 64 ? 64 : (g.N <= 128 ? 128 : (g.M <= 128 ? 256 : 512));
+    if (bn == 512) {  // the CTA-pair kernel: 256 x 256 tiles over two SMs
+        const int a = g.a1.mn_major ? 1 : 0, b = g.b1.mn_major ? 1 : 0;
+        if (a == 0 && b == 0) return launch_pair<0, 0>(g, stream);
+        if (a == 0 && b == 1) return launch_pair<0, 1>(g, stream);
+        if (a == 1 && b == 0) return launch_pair<1, 0>(g, stream);
+        return launch_pair<1, 1>(g, stream);
+    }
     switch (bn) {
         case 64: return dispatch_major<64>(g, stream);
         case 128: return dispatch_major<128>(g, stream);

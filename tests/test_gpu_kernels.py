@@ -67,8 +67,10 @@ def _bf(rs, shape, std=1.0):
 
 @pytest.mark.parametrize("a_mn", [False, True])
 @pytest.mark.parametrize("b_mn", [False, True])
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn", [64, 128, 256, 512])
 def test_gemm_layouts(cuda, a_mn, b_mn, bn):
+    """bn 512 is the CTA-pair kernel (256 x 256 tiles over two SMs); the shapes are ragged in M, N and K
+    against every tile."""
     rs = np.random.RandomState(100 + 4 * a_mn + 2 * b_mn + bn)
     M, N, K = 384, 320, 448
     A = _bf(rs, (M, K))
@@ -77,6 +79,21 @@ def test_gemm_layouts(cuda, a_mn, b_mn, bn):
     b_dev = (B.t().contiguous() if b_mn else B).to(cuda)
     out = torch.zeros((M, N), dtype=torch.float32, device=cuda)
     ops.gemm(a_dev, b_dev, out, a_mn=a_mn, b_mn=b_mn, mode=ops.EPI_STORE_F32, bn=bn)
+    torch.cuda.synchronize()
+    want = A.double().numpy() @ B.double().numpy().T
+    assert rel_l2(to_np(out), want) < 1e-5
+
+
+@pytest.mark.parametrize("splits", [1, 3])
+def test_gemm_pair_kernel_many_tiles(cuda, splits):
+    """The CTA-pair kernel over more 256 x 256 tiles than pairs of SMs (every pair runs several tiles, so
+    both accumulators and the stage ring wrap), with split-K atomics."""
+    rs = np.random.RandomState(7 + splits)
+    M, N, K = 2304, 4352, 640
+    A, B = _bf(rs, (M, K)), _bf(rs, (N, K))
+    out = torch.zeros((M, N), dtype=torch.float32, device=cuda)
+    mode = ops.EPI_ATOMIC_F32 if splits > 1 else ops.EPI_STORE_F32
+    ops.gemm(A.to(cuda), B.to(cuda), out, mode=mode, splits=splits, bn=512)
     torch.cuda.synchronize()
     want = A.double().numpy() @ B.double().numpy().T
     assert rel_l2(to_np(out), want) < 1e-5
