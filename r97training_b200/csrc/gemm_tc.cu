@@ -54,6 +54,19 @@ struct Cfg {
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// The tile order: bands of up to 16 M-tiles, N-tiles walked inside a band with M fastest, so one wave of
+// persistent CTAs works on a band's A rows (which stay in L2 across the band's waves) against a few
+// N-tiles of B, instead of all of A against two or three N-tiles.
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+    constexpr int kBand = 16;
+    const int band = tile / (kBand * tiles_n);
+    const int m_base = band * kBand;
+    const int gm = min(kBand, tiles_m - m_base);
+    const int r = tile - band * kBand * tiles_n;
+    tm = m_base + r % gm;
+    tn = r / gm;
+}
+
 // The epilogue of 32 accumulator columns [n0, n0 + 32) of row m (r = the raw f32 bits), per args.mode.
 __device__ __forceinline__ void epilogue32(const KernelArgs& args, int m, int n0, const uint32_t (&r)[32]) {
     const bool full = n0 + 32 <= args.N;
@@ -171,8 +184,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = blockIdx.x; u < units; u += gridDim.x) {
             const int split = u / tiles;
             const int tile = u % tiles;
-            const int tm = tile % args.tiles_m;
-            const int tn = tile / args.tiles_m;
+            int tm, tn;
+            tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
             const int kb0 = split * args.kb_per_split;
             const int kb1 = min(k_total, kb0 + args.kb_per_split);
             bool ok = true;
@@ -254,8 +267,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int local = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
             const int tile = u % tiles;
-            const int tm = tile % args.tiles_m;
-            const int tn = tile / args.tiles_m;
+            int tm, tn;
+            tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
             const int acc = local & 1;
             if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag)) break;
             tc_fence_after();
@@ -364,8 +377,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int u = pair; u < units; u += pairs) {
             const int split = u / tiles;
             const int tile = u % tiles;
-            const int tm = tile % args.tiles_m;
-            const int tn = tile / args.tiles_m;
+            int tm, tn;
+            tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
             const int kb0 = split * args.kb_per_split;
             const int kb1 = min(k_total, kb0 + args.kb_per_split);
             bool ok = true;
@@ -448,8 +461,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         int local = 0;
         for (int u = pair; u < units; u += pairs, ++local) {
             const int tile = u % tiles;
-            const int tm = tile % args.tiles_m;
-            const int tn = tile / args.tiles_m;
+            int tm, tn;
+            tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
             const int acc = local & 1;
             if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag)) break;
             tc_fence_after();
