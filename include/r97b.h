@@ -292,12 +292,13 @@ int r97b_gdn_sum_heads(const float* src, float* dst, int64_t T, int32_t H, int32
 int r97b_conv_prep_fwd(const uint16_t* x, int64_t ldx, const float* conv_w, const int32_t* cu, int32_t n_seq,
                        int64_t T, int32_t Hg, int32_t H, uint16_t* q, uint16_t* k, uint16_t* v, void* stream);
 
-/* Its adjoint from the f32 cotangents of q, k ([T, Hg, 128]) and v ([T, H, 128]): dacc (f32 scratch
- * [T, conv_dim]) then dx into the first conv_dim columns of bf16 rows of lddx.
+/* Its adjoint from the f32 cotangents of q, k ([T, dqk_heads, 128]: dqk_heads = Hg, or H when they are still
+ * per value head -- the heads sharing a key head are summed as they are read) and v ([T, H, 128]), into dx
+ * (the first conv_dim columns of bf16 rows of lddx), in one pass with no scratch.
  * Replaces: gdn_conv_prep_host_adjoint's conv / l2 terms, src/adjoint/host/gdn_prep.cpp:367-455. */
 int r97b_conv_prep_bwd(const uint16_t* x, int64_t ldx, const float* conv_w, const int32_t* cu, int32_t n_seq,
                        int64_t T, int32_t Hg, int32_t H, const float* dq, const float* dk, const float* dv,
-                       float* dacc, uint16_t* dx, int64_t lddx, void* stream);
+                       int32_t dqk_heads, uint16_t* dx, int64_t lddx, void* stream);
 
 /* beta = sigmoid(b), g = within-chunk running sum of -exp(A_log) softplus(a + dt_bias) (threshold 20), from
  * ba rows (bf16, ldba) holding b in columns [0, H) and a in [H, 2H); chunks from r97b_gdn_chunk_table.

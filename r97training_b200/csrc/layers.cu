@@ -46,40 +46,11 @@ __device__ __forceinline__ void ld8f(const float* p, float (&v)[8]) {
     const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
     v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
 }
-__device__ __forceinline__ void st8f(float* p, const float (&v)[8]) {
-    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
-    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
-}
 
-__device__ __forceinline__ float sum16(float v) {
-#pragma unroll
-    for (int o = 8; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
-    return v;
-}
 __device__ __forceinline__ float sum32(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
     return v;
-}
-
-// first token of the sequence holding token t
-__device__ __forceinline__ int seq_start(const int* cu, int n_seq, int t) {
-    int lo = 0, hi = n_seq;  // cu[lo] <= t < cu[hi]
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (cu[mid] <= t) lo = mid;
-        else hi = mid;
-    }
-    return cu[lo];
-}
-__device__ __forceinline__ int seq_end(const int* cu, int n_seq, int t) {
-    int lo = 0, hi = n_seq;
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (cu[mid] <= t) lo = mid;
-        else hi = mid;
-    }
-    return cu[lo + 1];
 }
 
 constexpr int kW = 4;  // conv width
@@ -94,189 +65,255 @@ struct ConvArgs {
     int n_seq, T, Hg, H, conv_dim;
 };
 
-constexpr int kTB = 16;  // tokens a conv-prep thread walks
+__device__ __forceinline__ void ld4(const __nv_bfloat16* p, float (&v)[4]) {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const float2 f0 = __bfloat1622float2(h[0]), f1 = __bfloat1622float2(h[1]);
+    v[0] = f0.x, v[1] = f0.y, v[2] = f1.x, v[3] = f1.y;
+}
+__device__ __forceinline__ void st4(__nv_bfloat16* p, const float (&v)[4]) {
+    uint2 u;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+    h[0] = __floats2bfloat162_rn(v[0], v[1]);
+    h[1] = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(p) = u;
+}
+// The conv prep, forward and adjoint. A thread owns 4 channels [c, c + 4) of a run of consecutive tokens;
+// a warp is one 128-wide head, so a head's L2-norm sums are warp reductions. Tokens go in groups of four:
+// the group's rows are loaded together, its four tokens' conv outputs and partial sums formed, and the
+// eight warp reductions of a group interleaved, so the shuffles' latency overlaps.
+constexpr int kG = 4;
+constexpr int kRunF = 32;                // tokens a forward thread emits (8 groups)
+constexpr int kRunB = 29;                // tokens a backward thread emits: 29 + 3 = 32 dacc rows = 8 groups
 
-// A conv-prep thread owns 8 channels [c, c + 8) of 16 consecutive tokens: it keeps the channels' 4-tap
-// weights (w is [conv_dim][4]) in registers and slides a window of input rows down the tokens, so each
-// row of x is read once per thread. The 16 threads of a half warp hold one 128-wide head's channels of
-// the same tokens, so a head's L2 norm is a half-warp shuffle sum.
-struct ConvThread {
+// sigmoid by the fast exponential; silu(x) = x s, silu'(x) = s (1 + x (1 - s))
+__device__ __forceinline__ float sigm_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+
+struct ConvRun {
     int t_begin, c;
     bool valid;
 };
 
-__device__ __forceinline__ ConvThread conv_thread(const ConvArgs& a) {
-    const int groups = a.conv_dim / 8;
-    const int tblocks = (a.T + kTB - 1) / kTB;
+// The thread's channels and token run; whole warps are valid or not (the channel groups are a multiple
+// of 32, so a warp never straddles the end).
+__device__ __forceinline__ ConvRun conv_run(const ConvArgs& a, int run) {
+    const int groups = a.conv_dim / 4;
+    const int runs = (a.T + run - 1) / run;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    ConvThread ct;
-    ct.valid = gid < (int64_t)tblocks * groups;
-    const int64_t g = ct.valid ? gid : (int64_t)tblocks * groups - 1;
-    ct.t_begin = (int)(g / groups) * kTB;
-    ct.c = (int)(g % groups) * 8;
-    return ct;
+    ConvRun r;
+    r.valid = gid < (int64_t)runs * groups;
+    const int64_t gi = r.valid ? gid : (int64_t)runs * groups - 1;
+    r.t_begin = (int)(gi / groups) * run;
+    r.c = (int)(gi % groups) * 4;
+    return r;
 }
 
-__device__ __forceinline__ void load_w8(const ConvArgs& a, int c, float (&w)[8][kW]) {
+__device__ __forceinline__ void load_w4(const ConvArgs& a, int c, float (&w)[4][kW]) {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < 4; ++i) {
         const float4 v = *reinterpret_cast<const float4*>(a.w + (c + i) * kW);
         w[i][0] = v.x, w[i][1] = v.y, w[i][2] = v.z, w[i][3] = v.w;
     }
 }
 
-// Walks the thread's tokens and calls fn(t, acc) with the pre-activation conv output of channels c..c+7.
-template <typename F>
-__device__ __forceinline__ void conv_walk(const ConvArgs& a, const ConvThread& ct, const float (&w)[8][kW], F&& fn) {
-    float row[kW][8];
-    // the three rows before the first token (clipped at the sequence start per token below)
-#pragma unroll
-    for (int j = 0; j < kW - 1; ++j) {
-        const int src = ct.t_begin - (kW - 1) + j;
-        if (src >= 0 && src < a.T) ld8(a.x + (int64_t)src * a.ldx + ct.c, row[j]);
-        else
-#pragma unroll
-            for (int i = 0; i < 8; ++i) row[j][i] = 0.0f;
-    }
-    int s = 0;
-    while (s + 1 < a.n_seq && a.cu[s + 1] <= ct.t_begin) ++s;
-    int t0 = a.cu[s], t1 = a.cu[s + 1];
-#pragma unroll 1
-    for (int k = 0; k < kTB; ++k) {
-        const int t = ct.t_begin + k;
-        const int tc = t < a.T ? t : a.T - 1;
-        ld8(a.x + (int64_t)tc * a.ldx + ct.c, row[kW - 1]);
-        while (t >= t1 && s + 1 < a.n_seq) {
-            ++s;
-            t0 = a.cu[s];
-            t1 = a.cu[s + 1];
-        }
-        float acc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < kW; ++j) {
-            const bool on = t - (kW - 1) + j >= t0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) acc[i] = fmaf(on ? row[j][i] : 0.0f, w[i][j], acc[i]);
-        }
-        fn(t, acc);
-#pragma unroll
-        for (int j = 0; j < kW - 1; ++j)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) row[j][i] = row[j + 1][i];
-    }
+__device__ __forceinline__ void load_x4(const ConvArgs& a, int c, int t, float (&v)[4]) {
+    if (t >= 0 && t < a.T) ld4(a.x + (int64_t)t * a.ldx + c, v);
+    else v[0] = v[1] = v[2] = v[3] = 0.0f;
 }
+
+// Tracks the sequence holding a token as tokens advance: start/end of it.
+struct SeqCursor {
+    int s, start, end;
+    __device__ __forceinline__ void init(const ConvArgs& a, int t) {
+        s = 0;
+        while (s + 1 < a.n_seq && a.cu[s + 1] <= t) ++s;
+        start = a.cu[s];
+        end = a.cu[s + 1];
+    }
+    __device__ __forceinline__ void advance(const ConvArgs& a, int t) {
+        while (t >= end && s + 1 < a.n_seq) {
+            ++s;
+            start = a.cu[s];
+            end = a.cu[s + 1];
+        }
+    }
+};
 
 __global__ void __launch_bounds__(256) conv_prep_fwd_kernel(ConvArgs a, __nv_bfloat16* __restrict__ q,
                                                             __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v) {
-    const ConvThread ct = conv_thread(a);
-    float w[8][kW];
-    load_w8(a, ct.c, w);
+    const ConvRun cr = conv_run(a, kRunF);
+    const int c = cr.c;
+    float w[4][kW];
+    load_w4(a, c, w);
     const int qk = a.Hg * 128;
-    conv_walk(a, ct, w, [&](int t, const float (&acc)[8]) {
-        float u[8], ss = 0.0f;
+    const bool normed = c < 2 * qk;
+    __nv_bfloat16* dst;
+    int64_t stride;
+    if (c < qk) dst = q + c, stride = qk;
+    else if (c < 2 * qk) dst = k + (c - qk), stride = qk;
+    else dst = v + (c - 2 * qk), stride = (int64_t)a.H * 128;
+    float xr[kW - 1 + kG][4];  // rows t0 - 3 .. t0 + 3 of the current group at t0
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            u[i] = silu(acc[i]);
-            ss = fmaf(u[i], u[i], ss);
-        }
-        ss = sum16(ss);  // every lane joins; the q|k|v boundaries are head aligned
-        if (!ct.valid || t >= a.T) return;
-        if (ct.c < 2 * qk) {
-            const float inv = rsqrtf(ss + 1e-6f);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) u[i] *= inv;
-            if (ct.c < qk) st8(q + (int64_t)t * qk + ct.c, u);
-            else st8(k + (int64_t)t * qk + (ct.c - qk), u);
-        } else {
-            st8(v + (int64_t)t * a.H * 128 + (ct.c - 2 * qk), u);
-        }
-    });
-}
-
-// dacc[t, c] from the cotangents of the normalised q, k (f32 [T, Hg, 128]) and of v (f32 [T, H, 128])
-__global__ void __launch_bounds__(256) conv_prep_dacc_kernel(ConvArgs a, const float* __restrict__ dq,
-                                                             const float* __restrict__ dk, const float* __restrict__ dv,
-                                                             float* __restrict__ dacc) {
-    const ConvThread ct = conv_thread(a);
-    float w[8][kW];
-    load_w8(a, ct.c, w);
-    const int qk = a.Hg * 128;
-    const int c = ct.c;
-    conv_walk(a, ct, w, [&](int t, const float (&acc)[8]) {
-        const int tc = t < a.T ? t : a.T - 1;
-        float u[8], dout[8];
-        if (c < qk) ld8f(dq + (int64_t)tc * qk + c, dout);
-        else if (c < 2 * qk) ld8f(dk + (int64_t)tc * qk + (c - qk), dout);
-        else ld8f(dv + (int64_t)tc * a.H * 128 + (c - 2 * qk), dout);
-        float ss = 0.0f, dot = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            u[i] = silu(acc[i]);
-            ss = fmaf(u[i], u[i], ss);
-            dot = fmaf(u[i], dout[i], dot);
-        }
-        ss = sum16(ss);
-        dot = sum16(dot);
-        if (!ct.valid || t >= a.T) return;
-        float o[8];
-        if (c < 2 * qk) {
-            const float inv = rsqrtf(ss + 1e-6f), inv3 = inv * inv * inv;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = (inv * dout[i] - inv3 * u[i] * dot) * silu_grad(acc[i]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = dout[i] * silu_grad(acc[i]);
-        }
-        st8f(dacc + (int64_t)t * a.conv_dim + c, o);
-    });
-}
-
-// dx[t, c] = sum_{t' = t .. t+3, same sequence} dacc[t', c] w[c, t - t' + 3], walking the tokens with a
-// window of the next three dacc rows
-__global__ void __launch_bounds__(256) conv_prep_dx_kernel(ConvArgs a, const float* __restrict__ dacc,
-                                                           __nv_bfloat16* __restrict__ dx, int64_t lddx) {
-    const ConvThread ct = conv_thread(a);
-    if (!ct.valid) return;
-    float w[8][kW];
-    load_w8(a, ct.c, w);
-    float row[kW][8];  // row[s] = dacc row t + s
-#pragma unroll
-    for (int s = 0; s < kW - 1; ++s) {
-        const int src = ct.t_begin + s;
-        if (src < a.T) ld8f(dacc + (int64_t)src * a.conv_dim + ct.c, row[s]);
-        else
-#pragma unroll
-            for (int i = 0; i < 8; ++i) row[s][i] = 0.0f;
-    }
-    int sq = 0;
-    while (sq + 1 < a.n_seq && a.cu[sq + 1] <= ct.t_begin) ++sq;
-    int t1 = a.cu[sq + 1];
+    for (int j = 0; j < kW - 1; ++j) load_x4(a, c, cr.t_begin - (kW - 1) + j, xr[j]);
+    SeqCursor sq;
+    sq.init(a, cr.t_begin);
 #pragma unroll 1
-    for (int k = 0; k < kTB; ++k) {
-        const int t = ct.t_begin + k;
-        if (t >= a.T) break;
-        const int src = t + kW - 1;
-        if (src < a.T) ld8f(dacc + (int64_t)src * a.conv_dim + ct.c, row[kW - 1]);
-        else
+    for (int g0 = 0; g0 < kRunF; g0 += kG) {
+        const int tg = cr.t_begin + g0;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) row[kW - 1][i] = 0.0f;
-        while (t >= t1 && sq + 1 < a.n_seq) t1 = a.cu[++sq + 1];
-        float o[8];
+        for (int j = 0; j < kG; ++j) load_x4(a, c, tg + j, xr[kW - 1 + j]);
+        float u[kG][4], ss[kG];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+        for (int j = 0; j < kG; ++j) {
+            sq.advance(a, tg + j);
+            ss[j] = 0.0f;
 #pragma unroll
-        for (int s = 0; s < kW; ++s) {
-            const bool on = t + s < t1;
+            for (int i = 0; i < 4; ++i) {
+                float acc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 8; ++i) o[i] = fmaf(on ? row[s][i] : 0.0f, w[i][kW - 1 - s], o[i]);
+                for (int tap = 0; tap < kW; ++tap)
+                    acc = fmaf(tg + j - (kW - 1) + tap >= sq.start ? xr[j + tap][i] : 0.0f, w[i][tap], acc);
+                u[j][i] = acc * sigm_fast(acc);
+                ss[j] = fmaf(u[j][i], u[j][i], ss[j]);
+            }
         }
-        st8(dx + (int64_t)t * lddx + ct.c, o);
 #pragma unroll
-        for (int s = 0; s < kW - 1; ++s)
+        for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) row[s][i] = row[s + 1][i];
+            for (int j = 0; j < kG; ++j) ss[j] += __shfl_xor_sync(0xFFFFFFFFu, ss[j], o);
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+            const int t = tg + j;
+            if (normed) {
+                const float inv = rsqrtf(ss[j] + 1e-6f);
+#pragma unroll
+                for (int i = 0; i < 4; ++i) u[j][i] *= inv;
+            }
+            if (cr.valid && t < a.T) st4(dst + (int64_t)t * stride, u[j]);
+        }
+#pragma unroll
+        for (int j = 0; j < kW - 1; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) xr[j][i] = xr[kG + j][i];
+    }
+}
+
+// The adjoint in one pass: for the dacc rows t' = t_begin .. t_begin + kRunB + 2 (the run plus the three
+// rows dx's taps reach past it) the thread rebuilds the conv output from x, forms dacc(t') (silu's and,
+// for q/k, the L2 norm's backward), and emits dx(t) = sum_{s = 0..3, same sequence} dacc(t + s) w[c, 3 - s]
+// as soon as its four dacc rows are known. dq/dk may still be per value head (grp value heads a key
+// head): the thread sums them as it reads.
+__global__ void __launch_bounds__(256) conv_prep_bwd_kernel(ConvArgs a, const float* __restrict__ dq,
+                                                            const float* __restrict__ dk, const float* __restrict__ dv,
+                                                            int grp, __nv_bfloat16* __restrict__ dx, int64_t lddx) {
+    const ConvRun cr = conv_run(a, kRunB);
+    const int c = cr.c;
+    float w[4][kW];
+    load_w4(a, c, w);
+    const int qk = a.Hg * 128;
+    const bool normed = c < 2 * qk;
+    const float* dsrc;
+    int64_t dstride;
+    int nsum;
+    if (c < qk) {
+        dsrc = dq + (int64_t)(c >> 7) * grp * 128 + (c & 127);
+        dstride = (int64_t)a.Hg * grp * 128;
+        nsum = grp;
+    } else if (c < 2 * qk) {
+        dsrc = dk + (int64_t)((c - qk) >> 7) * grp * 128 + ((c - qk) & 127);
+        dstride = (int64_t)a.Hg * grp * 128;
+        nsum = grp;
+    } else {
+        dsrc = dv + (c - 2 * qk);
+        dstride = (int64_t)a.H * 128;
+        nsum = 1;
+    }
+    float xr[kW - 1 + kG][4];  // x rows t0 - 3 .. t0 + 3 of the group at t0
+    float dw[kW - 1 + kG][4];  // dacc rows t0 - 3 .. t0 + 3
+#pragma unroll
+    for (int j = 0; j < kW - 1; ++j) {
+        load_x4(a, c, cr.t_begin - (kW - 1) + j, xr[j]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dw[j][i] = 0.0f;
+    }
+    SeqCursor sa, sb;  // the sequence of t' (conv taps) and of t' - 3 (dx's taps)
+    sa.init(a, cr.t_begin);
+    sb = sa;
+#pragma unroll 1
+    for (int g0 = 0; g0 < kRunB + kW - 1; g0 += kG) {
+        const int tg = cr.t_begin + g0;
+        float d[kG][4];
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+            load_x4(a, c, tg + j, xr[kW - 1 + j]);
+            const int tc = tg + j < a.T ? tg + j : a.T - 1;
+            float4 s4 = *reinterpret_cast<const float4*>(dsrc + (int64_t)tc * dstride);
+            for (int e = 1; e < nsum; ++e) {
+                const float4 x4 = *reinterpret_cast<const float4*>(dsrc + (int64_t)tc * dstride + e * 128);
+                s4.x += x4.x, s4.y += x4.y, s4.z += x4.z, s4.w += x4.w;
+            }
+            d[j][0] = s4.x, d[j][1] = s4.y, d[j][2] = s4.z, d[j][3] = s4.w;
+        }
+        float acc[kG][4], sg[kG][4], ss[kG], dot[kG];
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+            sa.advance(a, tg + j);
+            ss[j] = 0.0f;
+            dot[j] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float x = 0.0f;
+#pragma unroll
+                for (int tap = 0; tap < kW; ++tap)
+                    x = fmaf(tg + j - (kW - 1) + tap >= sa.start ? xr[j + tap][i] : 0.0f, w[i][tap], x);
+                acc[j][i] = x;
+                sg[j][i] = sigm_fast(x);
+                const float u = x * sg[j][i];
+                ss[j] = fmaf(u, u, ss[j]);
+                dot[j] = fmaf(u, d[j][i], dot[j]);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+            for (int j = 0; j < kG; ++j) {
+                ss[j] += __shfl_xor_sync(0xFFFFFFFFu, ss[j], o);
+                dot[j] += __shfl_xor_sync(0xFFFFFFFFu, dot[j], o);
+            }
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+            const bool live = tg + j < a.T;
+            const float inv = rsqrtf(ss[j] + 1e-6f), inv3 = inv * inv * inv;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const float s = sg[j][i], x = acc[j][i];
+                const float sgrad = s * (1.0f + x * (1.0f - s));
+                const float g = normed ? inv * d[j][i] - inv3 * (x * s) * dot[j] : d[j][i];
+                dw[kW - 1 + j][i] = live ? g * sgrad : 0.0f;
+            }
+        }
+        // dx of tokens tg + j - 3 (j = 0..3) from dacc rows tg + j - 3 .. tg + j
+#pragma unroll
+        for (int j = 0; j < kG; ++j) {
+            const int t = tg + j - (kW - 1);
+            if (t < cr.t_begin) continue;  // the first group's first three: rows before the run
+            sb.advance(a, t);
+            float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+            for (int s = 0; s < kW; ++s) {
+                const bool on = t + s < sb.end;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) o[i] = fmaf(on ? dw[j + s][i] : 0.0f, w[i][kW - 1 - s], o[i]);
+            }
+            if (cr.valid && t < a.T) st4(dx + (int64_t)t * lddx + c, o);
+        }
+#pragma unroll
+        for (int j = 0; j < kW - 1; ++j)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                xr[j][i] = xr[kG + j][i];
+                dw[j][i] = dw[kG + j][i];
+            }
     }
 }
 
@@ -553,21 +590,21 @@ extern "C" int r97b_conv_prep_fwd(const uint16_t* x, int64_t ldx, const float* c
                                   void* stream) {
     if (!x || !conv_w || !cu || !q || !k || !v || T <= 0 || Hg <= 0 || H <= 0 || (ldx % 8) || !al16(x)) return R97B_EINVAL;
     ConvArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, conv_w, cu, n_seq, (int)T, Hg, H, (2 * Hg + H) * 128};
-    conv_prep_fwd_kernel<<<blocks_for(((T + kTB - 1) / kTB) * (a.conv_dim / 8)), 256, 0, as_stream(stream)>>>(
+    conv_prep_fwd_kernel<<<blocks_for(((T + kRunF - 1) / kRunF) * (a.conv_dim / 4)), 256, 0, as_stream(stream)>>>(
         a, reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(k), reinterpret_cast<__nv_bfloat16*>(v));
     return launch_status();
 }
 
 extern "C" int r97b_conv_prep_bwd(const uint16_t* x, int64_t ldx, const float* conv_w, const int32_t* cu,
                                   int32_t n_seq, int64_t T, int32_t Hg, int32_t H, const float* dq, const float* dk,
-                                  const float* dv, float* dacc, uint16_t* dx, int64_t lddx, void* stream) {
-    if (!x || !conv_w || !cu || !dq || !dk || !dv || !dacc || !dx || T <= 0 || (ldx % 8) || (lddx % 8))
-        return R97B_EINVAL;
+                                  const float* dv, int32_t dqk_heads, uint16_t* dx, int64_t lddx, void* stream) {
+    if (!x || !conv_w || !cu || !dq || !dk || !dv || !dx || T <= 0 || (ldx % 4) || (lddx % 4)) return R97B_EINVAL;
+    if (Hg <= 0 || H <= 0 || dqk_heads < Hg || dqk_heads % Hg) return R97B_EINVAL;
     ConvArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, conv_w, cu, n_seq, (int)T, Hg, H, (2 * Hg + H) * 128};
-    const unsigned blocks = blocks_for(((T + kTB - 1) / kTB) * (a.conv_dim / 8));
-    conv_prep_dacc_kernel<<<blocks, 256, 0, as_stream(stream)>>>(a, dq, dk, dv, dacc);
-    conv_prep_dx_kernel<<<blocks, 256, 0, as_stream(stream)>>>(a, dacc, reinterpret_cast<__nv_bfloat16*>(dx), lddx);
-    return launch_status(2);
+    const unsigned blocks = blocks_for(((T + kRunB - 1) / kRunB) * (a.conv_dim / 4));
+    conv_prep_bwd_kernel<<<blocks, 256, 0, as_stream(stream)>>>(a, dq, dk, dv, dqk_heads / Hg,
+                                                                reinterpret_cast<__nv_bfloat16*>(dx), lddx);
+    return launch_status();
 }
 
 extern "C" int r97b_gates_fwd(const uint16_t* ba, int64_t ldba, const float* a_log, const float* dt_bias,

@@ -386,10 +386,10 @@ class TrainStep:
         # dz lands straight in its columns of the projection's cotangent
         ops.gated_rmsnorm_bwd(sv["o"].view(T * H, K), y_in[:, zsl], blk["gnorm_w"], don.view(T * H, K),
                               eps=cfg.eps, dx=do.view(T * H, K), dz=d_yin[:, zsl])
-        gr = self.plan.backward(sv["gsv"], do)
-        dacc = torch.empty((T, 2 * qk + H * K), dtype=torch.float32, device=x.device)
+        # dq, dk stay per value head: the conv adjoint sums each key head's value heads as it reads them
+        gr = self.plan.backward(sv["gsv"], do, sum_heads=False)
         ops.conv_prep_bwd(y_in, blk["conv_w"], self.cu_dev, self.plan.n_seq, Hg, H, gr["dq"], gr["dk"], gr["dv"],
-                          dacc, d_yin)
+                          d_yin)
         ba = y_in[:, 2 * qk + 2 * H * K:]
         ops.gates_bwd(ba, blk["a_log"], blk["dt_bias"], self.plan, gr["dg"], gr["dbeta"],
                       d_yin[:, 2 * qk + 2 * H * K:])

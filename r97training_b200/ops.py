@@ -203,10 +203,11 @@ def conv_prep_fwd(x, conv_w, cu_dev, n_seq, Hg, H, q, k, v, stream=None):
                                    _ptr(k), _ptr(v), _stream(stream)), "r97b_conv_prep_fwd")
 
 
-def conv_prep_bwd(x, conv_w, cu_dev, n_seq, Hg, H, dq, dk, dv, dacc, dx, stream=None):
+def conv_prep_bwd(x, conv_w, cu_dev, n_seq, Hg, H, dq, dk, dv, dx, stream=None):
+    """dq, dk: f32 [T, Hg, 128], or [T, H, 128] per value head (summed over the heads of a key head as read)."""
     T = x.shape[0]
     check(lib().r97b_conv_prep_bwd(_ptr(x), x.stride(0), _ptr(conv_w), _ptr(cu_dev), n_seq, T, Hg, H, _ptr(dq),
-                                   _ptr(dk), _ptr(dv), _ptr(dacc), _ptr(dx), dx.stride(0), _stream(stream)),
+                                   _ptr(dk), _ptr(dv), dq.shape[1], _ptr(dx), dx.stride(0), _stream(stream)),
           "r97b_conv_prep_bwd")
 
 

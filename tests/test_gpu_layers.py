@@ -35,18 +35,25 @@ def test_conv_prep_fwd_bwd(cuda, lens, Hg, H):
     qd = torch.empty((T, Hg, K), dtype=torch.bfloat16, device=cuda)
     kd, vd = torch.empty_like(qd), torch.empty((T, H, K), dtype=torch.bfloat16, device=cuda)
     ops.conv_prep_fwd(xd, wd, cud, len(lens), Hg, H, qd, kd, vd)
-    dq, dk, dv = (rs.normal(size=s).astype(np.float32) for s in ((T, Hg, K), (T, Hg, K), (T, H, K)))
-    dacc = torch.empty((T, C), dtype=torch.float32, device=cuda)
-    dx = torch.zeros((T, C + extra), dtype=torch.bfloat16, device=cuda)
-    ops.conv_prep_bwd(xd, wd, cud, len(lens), Hg, H, torch.from_numpy(dq).to(cuda), torch.from_numpy(dk).to(cuda),
-                      torch.from_numpy(dv).to(cuda), dacc, dx)
+    # dq, dk per value head (as the GDN backward leaves them); the adjoint sums each key head's value heads
+    grp = H // Hg
+    dqh, dkh = (rs.normal(size=(T, H, K)).astype(np.float32) for _ in range(2))
+    dv = rs.normal(size=(T, H, K)).astype(np.float32)
+    dq = dqh.reshape(T, Hg, grp, K).sum(2)
+    dk = dkh.reshape(T, Hg, grp, K).sum(2)
     torch.cuda.synchronize()
     assert_close_bf16(to_np(qd), q, rel=5e-3, what="q")
     assert_close_bf16(to_np(kd), k, rel=5e-3, what="k")
     assert_close_bf16(to_np(vd), v, rel=5e-3, what="v")
     want = R.conv_prep_bwd(xn, w.astype(np.float64), cu, Hg, H, dq, dk, dv, K)
-    assert_close_bf16(to_np(dx)[:, :C], want, rel=5e-3, what="dx")
-    assert not to_np(dx)[:, C:].any()  # columns past the conv channels are not written
+    for per_value_head in (False, True):
+        dx = torch.zeros((T, C + extra), dtype=torch.bfloat16, device=cuda)
+        a, b = (dqh, dkh) if per_value_head else (dq, dk)
+        ops.conv_prep_bwd(xd, wd, cud, len(lens), Hg, H, torch.from_numpy(np.ascontiguousarray(a)).to(cuda),
+                          torch.from_numpy(np.ascontiguousarray(b)).to(cuda), torch.from_numpy(dv).to(cuda), dx)
+        torch.cuda.synchronize()
+        assert_close_bf16(to_np(dx)[:, :C], want, rel=5e-3, what=f"dx (per value head: {per_value_head})")
+        assert not to_np(dx)[:, C:].any()  # columns past the conv channels are not written
 
 
 def test_gates_fwd_bwd(cuda):
