@@ -213,14 +213,41 @@ def b200_arm(args):
             dist.barrier()
         torch.cuda.synchronize()
 
-    for i in range(args.warmup):
+    # warm-up: eager steps first (kernel attributes, encoders and buffers are set up on first use), then the
+    # step is captured as one CUDA graph and the rest of the warm-up and every timed step replay it
+    eager_warm = 1 if args.eager else min(2, max(1, args.warmup - 1))
+    for i in range(eager_warm if not args.eager else args.warmup):
         one_step(ids_dev[i % len(ids_dev)])
+    graph = None
+    graph_launches = 0
+    prof = []
+    if not args.eager:
+        from r97training_b200.model import GraphStep
+        from r97training_b200._lib import lib as _lc
+        barrier()
+        ops.GEMM_PROFILE = prof  # the GEMMs' timing events become nodes of the graph
+        c0 = int(_lc().r97b_launch_count())
+        graph = GraphStep(step, ids_dev[0], update=(world == 1))
+        graph_launches = int(_lc().r97b_launch_count()) - c0  # this library's kernels in the captured step
+        ops.GEMM_PROFILE = None
+
+        def one_step(ids):  # noqa: F811 -- the replayed step
+            loss = graph.replay(ids)
+            if world > 1:  # the exchange and the update run eagerly after the captured backward
+                for li in range(len(adapter.layer_ranges) - 1, -1, -1):
+                    buckets.ready(li)
+                buckets.join()
+                adapter.adamw()
+            return loss
+
+        for i in range(eager_warm, args.warmup):
+            one_step(ids_dev[i % len(ids_dev)])
     barrier()
     # ------------------------------------------------------------ timed: device-resident inputs
     sampler = ClockSampler(local)
     sampler.start()
-    prof = []
-    ops.GEMM_PROFILE = prof
+    if graph is None:
+        ops.GEMM_PROFILE = prof
     from r97training_b200._lib import lib as _l
     launches0 = int(_l().r97b_launch_count())
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -230,10 +257,14 @@ def b200_arm(args):
     e1.record()
     barrier()
     ops.GEMM_PROFILE = None
-    own_launches = int(_l().r97b_launch_count()) - launches0
+    # this library's kernels launched in the timed region: counted at launch from the host, or, when the
+    # step is a replayed graph, the kernels captured in it times the replays
+    own_launches = int(_l().r97b_launch_count()) - launches0 + graph_launches * (args.steps if graph else 0)
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
     launches, gemm_ms, gemm_flops = ops.gemm_profile_summary(prof)
+    if graph is not None:  # the graph's events hold the last timed replay: one step's GEMMs
+        launches, gemm_ms, gemm_flops = launches * args.steps, gemm_ms * args.steps, gemm_flops * args.steps
     t = torch.tensor([ms], device=dev)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -281,6 +312,9 @@ def b200_arm(args):
                        "model": f"hybrid {cfg.layers}L d{cfg.hidden} 3xGDN:1xattn, IQR u4 base, LoRA r{cfg.rank}",
                        "global_batch": cfg.micro_batch * world, "seq_len": cfg.seq,
                        "parallelism": f"dp{world}", "l2": "inputs larger than L2 (about 60 GB of activations a step)",
+                       "launch": "eager" if graph is None else
+                       ("CUDA graph of the whole step" if world == 1 else
+                        "CUDA graph of forward+backward; gradient all-reduce and AdamW eager"),
                        "flops_per_token": flops_per_token(cfg)},
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05)", "achieved": gemm_tflops, "peak": peak,
                          "unit": "TFLOP/s", "frac": gemm_tflops / peak, "traffic": traffic,
@@ -319,6 +353,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--eager", action="store_true", help="launch every kernel from the host each step "
+                    "instead of replaying the step captured as a CUDA graph")
     args = ap.parse_args()
     if args.impl == "reference":
         return reference_arm(args)

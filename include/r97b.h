@@ -173,6 +173,13 @@ int r97b_adamw_step(float* w, float* m, float* v, float* g, int64_t n, float lr,
                     float weight_decay, float bc1, float bc2, float inv_k, const float* clip_scale,
                     int32_t zero_grad, void* stream);
 
+/* The same update with lr, bc1 and bc2 read from device memory when the kernel runs (sched[0] = lr,
+ * sched[1] = bc1, sched[2] = bc2, f32), so that a CUDA graph holding the update advances the schedule by a
+ * write to sched before each replay instead of being captured again. Same arithmetic, bit for bit. */
+int r97b_adamw_step_dev(float* w, float* m, float* v, float* g, int64_t n, const float* sched, float beta1,
+                        float beta2, float eps, float weight_decay, float inv_k, const float* clip_scale,
+                        int32_t zero_grad, void* stream);
+
 /* Bytes of scratch r97b_global_norm needs for n elements (one f64 per 4096). */
 int64_t r97b_global_norm_scratch_bytes(int64_t n);
 

@@ -97,6 +97,8 @@ _SIGS = {
     "r97b_embed": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp]),
     "r97b_cast_f32_bf16": (c_i32, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "r97b_launch_count": (ctypes.c_uint64, []),
+    "r97b_adamw_step_dev": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_vp, c_f32, c_f32, c_f32, c_f32, c_f32, c_vp,
+                                    c_i32, c_vp]),
     "r97b_global_norm_noalloc": (c_i32, [c_vp, c_i64, c_f32, c_f32, c_vp, c_vp, c_vp]),
 }
 

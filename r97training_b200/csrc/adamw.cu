@@ -22,23 +22,62 @@
 namespace r97b {
 namespace {
 
+// One element's update in the reference's f32 operation order (every step rounded as the reference rounds).
+struct AdamWConst {
+    float lr, b1, b2, one_b1, one_b2, eps, wd, bc1, bc2, inv_k, cs;
+    bool clip;
+};
+
+__device__ __forceinline__ void adamw_one(const AdamWConst& k, float& w, float& m, float& v, float g) {
+    float gi = __fmul_rn(g, k.inv_k);
+    if (k.clip) gi = __fmul_rn(gi, k.cs);
+    const float mi = __fadd_rn(__fmul_rn(k.b1, m), __fmul_rn(k.one_b1, gi));
+    const float vi = __fadd_rn(__fmul_rn(k.b2, v), __fmul_rn(__fmul_rn(k.one_b2, gi), gi));
+    m = mi;
+    v = vi;
+    const float mh = __fdiv_rn(mi, k.bc1);
+    const float vh = __fdiv_rn(vi, k.bc2);
+    const float upd = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), k.eps)), __fmul_rn(k.wd, w));
+    w = __fsub_rn(w, __fmul_rn(k.lr, upd));
+}
+
+// Four elements a thread per step (16-byte loads and stores) over the aligned body, one at a time over the
+// ragged tail.
 __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ w, float* __restrict__ m, float* __restrict__ v,
                                                     float* __restrict__ g, int64_t n, float lr, float b1, float b2,
                                                     float eps, float wd, float bc1, float bc2, float inv_k,
-                                                    const float* __restrict__ clip_scale, int zero_grad) {
-    const float one_b1 = __fsub_rn(1.0f, b1), one_b2 = __fsub_rn(1.0f, b2);
-    const float cs = clip_scale ? *clip_scale : 1.0f;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        float gi = __fmul_rn(g[i], inv_k);
-        if (clip_scale) gi = __fmul_rn(gi, cs);
-        const float mi = __fadd_rn(__fmul_rn(b1, m[i]), __fmul_rn(one_b1, gi));
-        const float vi = __fadd_rn(__fmul_rn(b2, v[i]), __fmul_rn(__fmul_rn(one_b2, gi), gi));
+                                                    const float* __restrict__ clip_scale, int zero_grad,
+                                                    const float* __restrict__ sched) {
+    if (sched) {  // lr, bc1, bc2 from device memory (a captured graph's replays advance them)
+        lr = sched[0];
+        bc1 = sched[1];
+        bc2 = sched[2];
+    }
+    const AdamWConst k{lr, b1, b2, __fsub_rn(1.0f, b1), __fsub_rn(1.0f, b2), eps, wd, bc1, bc2, inv_k,
+                       clip_scale ? *clip_scale : 1.0f, clip_scale != nullptr};
+    const bool vec = ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(m) | reinterpret_cast<uintptr_t>(v) |
+                       reinterpret_cast<uintptr_t>(g)) & 15) == 0;
+    const int64_t n4 = vec ? n / 4 : 0;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        float4 wv = reinterpret_cast<float4*>(w)[i], mv = reinterpret_cast<float4*>(m)[i];
+        float4 vv = reinterpret_cast<float4*>(v)[i];
+        const float4 gv = reinterpret_cast<const float4*>(g)[i];
+        adamw_one(k, wv.x, mv.x, vv.x, gv.x);
+        adamw_one(k, wv.y, mv.y, vv.y, gv.y);
+        adamw_one(k, wv.z, mv.z, vv.z, gv.z);
+        adamw_one(k, wv.w, mv.w, vv.w, gv.w);
+        reinterpret_cast<float4*>(w)[i] = wv;
+        reinterpret_cast<float4*>(m)[i] = mv;
+        reinterpret_cast<float4*>(v)[i] = vv;
+        if (zero_grad) reinterpret_cast<float4*>(g)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    for (int64_t i = n4 * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+        float wi = w[i], mi = m[i], vi = v[i];
+        adamw_one(k, wi, mi, vi, g[i]);
+        w[i] = wi;
         m[i] = mi;
         v[i] = vi;
-        const float mh = __fdiv_rn(mi, bc1);
-        const float vh = __fdiv_rn(vi, bc2);
-        const float upd = __fadd_rn(__fdiv_rn(mh, __fadd_rn(__fsqrt_rn(vh), eps)), __fmul_rn(wd, w[i]));
-        w[i] = __fsub_rn(w[i], __fmul_rn(lr, upd));
         if (zero_grad) g[i] = 0.0f;
     }
 }
@@ -135,7 +174,19 @@ extern "C" int r97b_adamw_step(float* w, float* m, float* v, float* g, int64_t n
     int blocks = (int)((n + 255) / 256);
     if (blocks > 148 * 16) blocks = 148 * 16;
     adamw_kernel<<<blocks, 256, 0, as_stream(stream)>>>(w, m, v, g, n, lr, beta1, beta2, eps, weight_decay, bc1, bc2,
-                                                        inv_k, clip_scale, zero_grad);
+                                                        inv_k, clip_scale, zero_grad, nullptr);
+    return launch_status();
+}
+
+// The same update with lr, bc1, bc2 read from sched[0..2] (device f32) when the kernel runs.
+extern "C" int r97b_adamw_step_dev(float* w, float* m, float* v, float* g, int64_t n, const float* sched, float beta1,
+                                   float beta2, float eps, float weight_decay, float inv_k, const float* clip_scale,
+                                   int32_t zero_grad, void* stream) {
+    if (!w || !m || !v || !g || !sched || n <= 0) return R97B_EINVAL;
+    const int64_t want = (n + 255) / 256;
+    const unsigned blocks = (unsigned)(want < 148 * 16 ? want : 148 * 16);
+    adamw_kernel<<<blocks, 256, 0, as_stream(stream)>>>(w, m, v, g, n, 0.0f, beta1, beta2, eps, weight_decay, 1.0f,
+                                                        1.0f, inv_k, clip_scale, zero_grad, sched);
     return launch_status();
 }
 

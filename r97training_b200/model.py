@@ -25,7 +25,6 @@ from dataclasses import dataclass, field
 
 import numpy as np
 import torch
-import torch.nn.functional as F
 
 from . import iqr as IQ
 from . import ops
@@ -205,6 +204,7 @@ class Adapter:
         self.m = torch.zeros_like(self.w)
         self.v = torch.zeros_like(self.w)
         self.step = 0
+        self.sched = torch.zeros(3, dtype=torch.float32, device=device)  # lr, bc1, bc2 of the current step
         # bf16 mirrors
         self.a_bf, self.b_blk = {}, {}
         for li, blk in enumerate(model.blocks):
@@ -233,9 +233,10 @@ class Adapter:
                     ops.cast_f32_bf16(self.b_view(self.w, g, i), dst, stream=stream)
                     row += n
 
-    def adamw(self, lr=None, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0, stream=None):
-        """One AdamW update of the whole adapter (bit-identical to the reference Optimiser's f32 update),
-        then the gradient is cleared and the bf16 mirrors refreshed."""
+    def advance_schedule(self, lr=None, beta1=0.9, beta2=0.999, stream=None):
+        """Counts one more step and writes its lr and bias corrections bc1 = 1 - beta1^t, bc2 = 1 - beta2^t
+        (f32 powf, as the reference's optimiser forms them) into the device schedule `sched` the update
+        reads; stream-ordered before whatever is queued after it."""
         import ctypes
         self.step += 1
         t = self.step
@@ -244,10 +245,22 @@ class Adapter:
         libm.powf.argtypes = [ctypes.c_float, ctypes.c_float]
         bc1 = float(np.float32(1.0) - np.float32(libm.powf(beta1, float(t))))
         bc2 = float(np.float32(1.0) - np.float32(libm.powf(beta2, float(t))))
-        ops.adamw_step(self.w, self.m, self.v, self.g, lr=self.cfg.lr if lr is None else lr, beta1=beta1,
-                       beta2=beta2, eps=eps, weight_decay=weight_decay, bc1=bc1, bc2=bc2, zero_grad=True,
-                       stream=stream)
+        vals = torch.tensor([self.cfg.lr if lr is None else lr, bc1, bc2], dtype=torch.float32)
+        with torch.cuda.stream(stream or torch.cuda.current_stream()):
+            self.sched.copy_(vals)  # pageable source: staged before the call returns
+
+    def update(self, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0, stream=None):
+        """The AdamW update at the schedule's current step, then the gradient is cleared and the bf16
+        mirrors refreshed; reads its step-dependent scalars from `sched`, so it can live in a CUDA graph."""
+        ops.adamw_step_dev(self.w, self.m, self.v, self.g, self.sched, beta1=beta1, beta2=beta2, eps=eps,
+                           weight_decay=weight_decay, zero_grad=True, stream=stream)
         self.refresh_mirrors(stream=stream)
+
+    def adamw(self, lr=None, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0, stream=None):
+        """One AdamW update of the whole adapter (bit-identical to the reference Optimiser's f32 update),
+        then the gradient is cleared and the bf16 mirrors refreshed."""
+        self.advance_schedule(lr, beta1, beta2, stream=stream)
+        self.update(beta1, beta2, eps, weight_decay, stream=stream)
 
 
 # ============================================================================================ the step
@@ -415,15 +428,16 @@ class TrainStep:
         ops.qk_norm_rope_fwd(y[:, qn:], Dh, Hkv, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
                              cfg.rotary_dim, S, cfg.eps, kr)
         ops.to_bhsd(y[:, qn + Hkv * Dh:], Dh, Hkv, S, vt)
-        qg, kg, vg = (t.detach().requires_grad_(True) for t in (qr, kr, vt))
-        with torch.enable_grad():
-            attn = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True, enable_gqa=True)
+        # the attention core is the flash kernel's forward (GQA native), called without autograd so the
+        # step stays on this stream and capturable; its saved state feeds the matching backward below
+        fa = torch.ops.aten._scaled_dot_product_flash_attention(qr, kr, vt, 0.0, True, False)
+        attn = fa[0]
         ga = torch.empty((T, Hq * Dh), dtype=torch.bfloat16, device=x.device)
-        ops.gate_mul_fwd(attn.detach(), y[:, Dh:], 2 * Dh, Hq, S, ga)
+        ops.gate_mul_fwd(attn, y[:, Dh:], 2 * Dh, Hq, S, ga)
         W = self._w_fwd(li, g_o)
         h1 = torch.empty_like(x)
         t_o = self._lin_fwd(li, g_o, ga, W, h1, addend=x)
-        sv.update(n1=n1, y=y, t_qkv=t_qkv, qkv=(qg, kg, vg), attn=attn, ga=ga, t_o=t_o)
+        sv.update(n1=n1, y=y, t_qkv=t_qkv, qkv=(qr, kr, vt), fa=fa, attn=attn, ga=ga, t_o=t_o)
         return h1
 
     def _attn_bwd(self, li, blk, x, sv, dh1):
@@ -437,9 +451,11 @@ class TrainStep:
         y = sv["y"]
         dy = torch.empty_like(y)
         dattn = torch.empty((B, Hq, S, Dh), dtype=torch.bfloat16, device=x.device)
-        ops.gate_mul_bwd(sv["attn"].detach(), y[:, Dh:], 2 * Dh, Hq, S, dga, dattn, dy[:, Dh:])
+        ops.gate_mul_bwd(sv["attn"], y[:, Dh:], 2 * Dh, Hq, S, dga, dattn, dy[:, Dh:])
         qg, kg, vg = sv["qkv"]
-        dq, dk, dv = torch.autograd.grad(sv["attn"], (qg, kg, vg), dattn)
+        fa = sv["fa"]
+        dq, dk, dv = torch.ops.aten._scaled_dot_product_flash_attention_backward(
+            dattn, qg, kg, vg, fa[0], fa[1], fa[2], fa[3], fa[4], fa[5], 0.0, True, fa[6], fa[7])
         ops.qk_norm_rope_bwd(y, 2 * Dh, Hq, blk["q_norm"], self.model.rope_cos, self.model.rope_sin, cfg.rotary_dim,
                              S, cfg.eps, dq.contiguous(), dy)
         ops.qk_norm_rope_bwd(y[:, qn:], Dh, Hkv, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
@@ -479,18 +495,20 @@ class TrainStep:
         return ops.rmsnorm_bwd(h1, blk["w_post"], dn2, addend=dxn, eps=cfg.eps)
 
     # ------------------------------------------------------------------ the whole step
-    def run(self, ids: torch.Tensor, targets: torch.Tensor | None = None):
+    def run(self, ids: torch.Tensor, targets: torch.Tensor | None = None, n_scored: int | None = None):
         """ids: int32 [micro_batch, seq] (device). targets: int32 [micro_batch * seq] with -1 where a row
         is not scored; default: next-token targets, the last position of each sequence unscored.
+        n_scored: how many rows targets scores, when the caller knows it (default targets: from the shape;
+        explicit targets without it: counted on the device, which synchronises the host once).
         Returns the mean CE over scored rows (device f32 scalar)."""
         cfg, model, T = self.cfg, self.model, self.T
         ids = ids.reshape(-1).to(torch.int32).contiguous()
         if targets is None:
+            n_scored = int(cfg.micro_batch * (cfg.seq - 1))
             targets = torch.empty_like(ids)
             tv = targets.view(cfg.micro_batch, cfg.seq)
             tv[:, :-1] = ids.view(cfg.micro_batch, cfg.seq)[:, 1:]
             tv[:, -1] = -1
-        n_scored = int(cfg.micro_batch * (cfg.seq - 1)) if targets is None else None
         # the tied head, decoded once for the embedding and both head products
         IQ.dequant_bf16(model.head, out=self.ws.head_w)
         x = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=model.device)
@@ -528,6 +546,41 @@ class TrainStep:
             if self.grad_hook is not None:
                 self.grad_hook(li)
         return loss_rows.sum() * scale
+
+
+class GraphStep:
+    """One whole training step captured as a CUDA graph and replayed: forward, loss, backward and (with
+    `update`) the AdamW update, over static input and output buffers. The host's share of a step becomes
+    a copy of the token ids, the schedule write and one graph launch, instead of ~2000 kernel launches.
+
+    The step must have run eagerly at least once first (kernel attributes, tensor-map encoders and the
+    decoded-weight buffers are set up on first use, outside any capture). `grad_hook` is not captured: a
+    data-parallel caller captures without the update and exchanges the gradient after each replay."""
+
+    def __init__(self, step: "TrainStep", ids: torch.Tensor, update: bool = True):
+        self.step, self.update = step, update
+        dev = step.model.device
+        self.ids = ids.reshape(-1).to(torch.int32).clone()
+        hook, step.grad_hook = step.grad_hook, None
+        torch.cuda.synchronize(dev)
+        self.graph = torch.cuda.CUDAGraph()
+        try:
+            with torch.cuda.graph(self.graph):
+                self.loss = step.run(self.ids)
+                if update:
+                    step.adapter.update()
+        finally:
+            step.grad_hook = hook
+
+    def replay(self, ids: torch.Tensor | None = None, lr=None) -> torch.Tensor:
+        """Runs one step on `ids` (copied into the captured input; None reuses the last ids) and returns the
+        captured loss tensor (valid until the next replay)."""
+        if ids is not None:
+            self.ids.copy_(ids.reshape(-1), non_blocking=True)
+        if self.update:
+            self.step.adapter.advance_schedule(lr)
+        self.graph.replay()
+        return self.loss
 
 
 def flops_per_token(cfg: HybridConfig) -> float:

@@ -78,7 +78,10 @@ def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STOR
     prof = GEMM_PROFILE
     if prof is not None:
         s = stream if stream is not None else torch.cuda.current_stream()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        # inside a graph capture the events become record nodes of the graph, re-recorded at every replay
+        ext = torch.cuda.is_current_stream_capturing()
+        e0 = torch.cuda.Event(enable_timing=True, external=ext)
+        e1 = torch.cuda.Event(enable_timing=True, external=ext)
         e0.record(s)
     check(lib().r97b_gemm(ctypes.byref(g), _stream(stream)), "r97b_gemm")
     if prof is not None:
@@ -87,7 +90,8 @@ def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STOR
     return out
 
 
-# When a list, every gemm() appends (start event, end event, algorithmic FLOPs) recorded on its stream:
+# When a list, every gemm() appends (start event, end event, algorithmic FLOPs) recorded on its stream (in a
+# captured graph: recorded again by every replay, so a summary after replays reads the last one):
 # bench.py's live measurement of the tensor-core GEMM's launch durations.
 GEMM_PROFILE = None
 
@@ -181,6 +185,16 @@ def adamw_step(w, m, v, g, *, lr, beta1, beta2, eps, weight_decay, bc1, bc2, inv
     check(lib().r97b_adamw_step(_ptr(w), _ptr(m), _ptr(v), _ptr(g), w.numel(), lr, beta1, beta2, eps, weight_decay,
                                 bc1, bc2, inv_k, _ptr(clip_scale), int(zero_grad), _stream(stream)),
           "r97b_adamw_step")
+
+
+def adamw_step_dev(w, m, v, g, sched, *, beta1, beta2, eps, weight_decay, inv_k=1.0, clip_scale=None,
+                   zero_grad=False, stream=None):
+    """AdamW with lr, bc1, bc2 read from the device tensor sched[0:3] when the kernel runs."""
+    for t, nm in ((w, "w"), (m, "m"), (v, "v"), (g, "g"), (sched, "sched")):
+        _need(t, torch.float32, nm)
+    check(lib().r97b_adamw_step_dev(_ptr(w), _ptr(m), _ptr(v), _ptr(g), w.numel(), _ptr(sched), beta1, beta2, eps,
+                                    weight_decay, inv_k, _ptr(clip_scale), int(zero_grad), _stream(stream)),
+          "r97b_adamw_step_dev")
 
 
 def global_norm(g, *, inv_k=1.0, max_norm=0.0, scratch=None, stream=None):

@@ -5,6 +5,9 @@
     python -m r97training_b200.profile_cases gdn       # one config-5 GDN layer, forward + backward
     python -m r97training_b200.profile_cases decode    # the IQR decode of a 24576 x 4096 weight
     python -m r97training_b200.profile_cases norms     # rmsnorm fwd/bwd at 8192 x 4096
+    python -m r97training_b200.profile_cases loss      # CE over 2048 x 151936 bf16 logits (one head chunk)
+    python -m r97training_b200.profile_cases adamw     # AdamW over the config-5 adapter (160.4 M f32 params)
+    python -m r97training_b200.profile_cases conv      # GDN conv prep fwd + bwd at 8192 tokens, 8192 channels
     python -m r97training_b200.profile_cases step      # one config-5 training step after one warm-up step,
                                                        # inside an NVTX range "step" (ncu --nvtx-include step/)
 
@@ -62,6 +65,37 @@ def main(case: str) -> None:
         for _ in range(3):
             ops.rmsnorm_fwd(x, w)
             ops.rmsnorm_bwd(x, w, dy, addend=dy)
+    elif case == "loss":
+        from . import ops
+        rows, vocab = 2048, 151936
+        logits = (torch.randn(rows, vocab, device=dev) * 2).bfloat16()
+        tgt = torch.randint(0, vocab, (rows,), device=dev, dtype=torch.int32)
+        loss = torch.empty(rows, device=dev)
+        grad = torch.empty_like(logits)
+        for _ in range(3):
+            ops.ce_kld(logits, tgt, loss_ce=loss, grad=grad, grad_scale=1.0 / rows)
+    elif case == "adamw":
+        from . import ops
+        n = 160_432_128
+        w = torch.randn(n, device=dev) * 0.01
+        m, v, g = torch.zeros_like(w), torch.zeros_like(w), torch.randn(n, device=dev) * 1e-3
+        for i in range(3):
+            ops.adamw_step(w, m, v, g, lr=1e-4, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0,
+                           bc1=1.0 - 0.9 ** (i + 1), bc2=1.0 - 0.999 ** (i + 1))
+    elif case == "conv":
+        from . import ops
+        T, Hg, H = 8192, 16, 32
+        C = (2 * Hg + H) * 128
+        x = torch.randn(T, C + 8256, device=dev).bfloat16()
+        cw = torch.randn(C, 4, device=dev) * 0.5
+        cu = torch.tensor([0, 4096, 8192], dtype=torch.int32, device=dev)
+        q = torch.empty(T, Hg, 128, device=dev, dtype=torch.bfloat16)
+        k, v = torch.empty_like(q), torch.empty(T, H, 128, device=dev, dtype=torch.bfloat16)
+        dq, dk, dv = (torch.randn(T, H, 128, device=dev) for _ in range(3))
+        dx = torch.zeros_like(x)
+        for _ in range(3):
+            ops.conv_prep_fwd(x, cw, cu, 2, Hg, H, q, k, v)
+            ops.conv_prep_bwd(x, cw, cu, 2, Hg, H, dq, dk, dv, dx)
     elif case == "step":
         from .model import CONFIG5, Adapter, HybridModel, TrainStep
         model = HybridModel(CONFIG5, dev)

@@ -29,3 +29,44 @@ def test_small_hybrid_steps_are_finite_and_learn(cuda):
         losses.append(float(loss))
     assert all(torch.isfinite(torch.tensor(losses))), losses
     assert losses[-1] < losses[0], losses
+
+
+def test_graph_replay_matches_eager_steps(cuda):
+    """The step captured as one CUDA graph (forward, backward, AdamW) and replayed gives the eager steps'
+    losses and the same adapter updates from the same start. The GDN adjoint sums some per-row terms
+    with shared-memory float atomics, so two eager runs differ in the last bits too, and early AdamW
+    steps move every weight by about lr whatever the gradient's size: the updates are compared by
+    direction and size, against the spread of two eager runs."""
+    from r97training_b200.model import GraphStep
+    cfg = HybridConfig(hidden=512, layers=4, gdn_heads=4, gdn_qk_heads=2, attn_heads=2, attn_kv_heads=1, ffn=1024,
+                       vocab=4096, rank=16, alpha=32, seq=256, micro_batch=2, lr=1e-3)
+    gen = torch.Generator(device=cuda)
+    gen.manual_seed(7)
+    batches = [torch.randint(0, cfg.vocab, (cfg.micro_batch, cfg.seq), device=cuda, generator=gen,
+                             dtype=torch.int32) for _ in range(4)]
+    runs = []
+    for graph in (False, False, True):
+        model = HybridModel(cfg, cuda)
+        ad = Adapter(model, cuda)
+        step = TrainStep(model, ad, head_chunk=256)
+        w0 = ad.w.clone()
+        losses = [float(step.run(batches[0]))]
+        ad.adamw()
+        if graph:
+            gs = GraphStep(step, batches[1])
+            for b in batches[1:]:
+                losses.append(float(gs.replay(b)))
+        else:
+            for b in batches[1:]:
+                losses.append(float(step.run(b)))
+                ad.adamw()
+        torch.cuda.synchronize()
+        runs.append((losses, (ad.w - w0).double(), ad.step))
+    (le, de, se), (l2, d2, s2), (lg, dg, sg) = runs
+    assert se == s2 == sg == 4
+    for a, b in zip(le, lg):
+        assert abs(a - b) <= 1e-3 * abs(a), (le, lg)
+    cos = float((de * dg).sum() / (de.norm() * dg.norm()))
+    spread = float((de - d2).norm() / de.norm())  # two eager runs
+    assert cos > 0.99, cos
+    assert float((de - dg).norm() / de.norm()) <= max(3 * spread, 0.05), (spread, cos)
