@@ -185,11 +185,13 @@ __global__ void iqr_decode_general(const R97IqrDecodeDesc d, const Sink s) {
     }
 }
 
-constexpr int kSegRows = 32;
+constexpr int kSegRows = 16;
 
 // The trunk form: u4 codes, 16 state bits, mad codebook, per-(row, 128 col) f32/bf16 scale, rb = 1.
+// A thread requests every code word and scale of its segment (and the 3 words above it) before the first
+// row's arithmetic: 19 loads in flight per thread, 3 CTAs of 256 threads per SM.
 template <bool kBf16Out>
-__global__ void __launch_bounds__(256) iqr_decode_u4(const R97IqrDecodeDesc d, const Sink s, int64_t nseg_per_run) {
+__global__ void __launch_bounds__(256, 3) iqr_decode_u4(const R97IqrDecodeDesc d, const Sink s, int64_t nseg_per_run) {
     const int64_t groups = d.cols >> 3;  // 8-column groups
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int64_t nruns = (d.rows + d.run_rows - 1) / d.run_rows;
@@ -210,61 +212,71 @@ __global__ void __launch_bounds__(256) iqr_decode_u4(const R97IqrDecodeDesc d, c
     auto word = [&](int64_t r) -> uint32_t {
         return *reinterpret_cast<const uint32_t*>(cbase + (r - d.row0) * d.codes_row_bytes);
     };
-    // The 3 codes above the segment's first row, wrapping to the run's tail (the seam).
-    uint32_t st[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) st[i] = 0;
+    const int64_t kb = j0 >> 7;
+    const int nrow = (int)(sr1 - sr0);
+    // the 3 words above the segment's first row, wrapping to the run's tail (the seam)
+    uint32_t halo[3];
 #pragma unroll
     for (int q = 3; q >= 1; --q) {
         int64_t t = sr0 - q;
         if (t < r0) t += len;
-        const uint32_t w = word(t);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) st[i] = (st[i] << 4) | ((w >> (4 * i)) & 15u);
+        halo[3 - q] = word(t);
     }
-    const uint32_t A = d.mad_a, B = d.mad_b;
-    const int64_t kb = j0 >> 7;
-    // rows in batches of 8: the batch's code words and scales are all requested before the first row's
-    // arithmetic, so eight loads are in flight per thread instead of one
-    constexpr int kBatch = 8;
-    uint32_t wb[kBatch];
-    float sb8[kBatch];
-    for (int64_t r = sr0; r < sr1; ++r) {
-        const int bi = (int)((r - sr0) & (kBatch - 1));
-        if (bi == 0) {
+    uint32_t wb[kSegRows];
+    float sb[kSegRows];
+    {
+        const uint8_t* cp = cbase + (sr0 - d.row0) * d.codes_row_bytes;
+        const int crb = (int)d.codes_row_bytes, srb = (int)d.scale_row_bytes;
+        const bool f32s = d.scale_dtype == R97_IQR_F32;
+        const uint8_t* sp = d.scale + (sr0 - d.row0) * d.scale_row_bytes + kb * (f32s ? 4 : 2);
 #pragma unroll
-            for (int b = 0; b < kBatch; ++b) {
-                const int64_t rr = r + b < sr1 ? r + b : sr1 - 1;
-                wb[b] = word(rr);
-                const uint8_t* srow = d.scale + (rr - d.row0) * d.scale_row_bytes;
-                sb8[b] = d.scale_dtype == R97_IQR_F32 ? reinterpret_cast<const float*>(srow)[kb]
-                                                      : bf16_bits_to_f32(reinterpret_cast<const uint16_t*>(srow)[kb]);
-            }
+        for (int b = 0; b < kSegRows; ++b) {
+            const int rb = b < nrow ? b : nrow - 1;
+            wb[b] = *reinterpret_cast<const uint32_t*>(cp + rb * crb);
+            sb[b] = f32s ? *reinterpret_cast<const float*>(sp + rb * srb)
+                         : bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sp + rb * srb));
         }
-        uint32_t w = wb[0];
-        float sc = sb8[0];
+    }
+    uint32_t st[8];
 #pragma unroll
-        for (int b = 1; b < kBatch; ++b)
-            if (bi == b) {
-                w = wb[b];
-                sc = sb8[b];
-            }
-        int32_t v[8];
+    for (int i = 0; i < 8; ++i)
+        st[i] = (((halo[0] >> (4 * i)) & 15u) << 8) | (((halo[1] >> (4 * i)) & 15u) << 4) |
+                ((halo[2] >> (4 * i)) & 15u);
+    const uint32_t A = d.mad_a & 0xFFFFFFu, B = d.mad_b;
+    uint16_t* wrow = kBf16Out ? s.w + (sr0 - d.row0) * s.ld_w + j0 : nullptr;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            st[i] = ((st[i] << 4) | ((w >> (4 * i)) & 15u)) & 0xFFFFu;
-            v[i] = mad_value(st[i], A, B);
-        }
-        const int64_t lr = r - d.row0;
+    for (int b = 0; b < kSegRows; ++b) {
+        if (b >= nrow) break;
+        const uint32_t w = wb[b];
+        const int64_t lr = sr0 + b - d.row0;
         if (kBf16Out) {
-            const float sb = bf16_bits_to_f32(f32_to_bf16_bits(sc));
+            // value = (byte sum of the hash) - 126, formed exactly as a float: the dot product's
+            // accumulator starts at 2^23's bit pattern, so the sum lands in the mantissa
+            const float sc = bf16_bits_to_f32(f32_to_bf16_bits(sb[b]));
+            float vf[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                st[i] = ((st[i] << 4) | ((w >> (4 * i)) & 15u)) & 0xFFFFu;
+                const uint32_t h = (st[i] * A + B) & 0x3F3F3F3Fu;
+                vf[i] = __uint_as_float(__dp4a(h, 0x01010101u, 0x4B000000u)) - 8388734.0f;
+            }
+            // code * scale rounded to nearest-even bf16 by the hardware conversion (finite and infinite
+            // products round exactly as f32_to_bf16_bits does)
             uint32_t pk[4];
 #pragma unroll
-            for (int i = 0; i < 4; ++i)
-                pk[i] = (uint32_t)f32_to_bf16_bits((float)v[2 * i] * sb) |
-                        ((uint32_t)f32_to_bf16_bits((float)v[2 * i + 1] * sb) << 16);
-            *reinterpret_cast<uint4*>(s.w + lr * s.ld_w + j0) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            for (int i = 0; i < 4; ++i) {
+                const __nv_bfloat162 p2 = __floats2bfloat162_rn(vf[2 * i] * sc, vf[2 * i + 1] * sc);
+                pk[i] = *reinterpret_cast<const uint32_t*>(&p2);
+            }
+            *reinterpret_cast<uint4*>(wrow) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            wrow += s.ld_w;
         } else {
+            int32_t v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                st[i] = ((st[i] << 4) | ((w >> (4 * i)) & 15u)) & 0xFFFFu;
+                v[i] = mad_value(st[i], A, B);
+            }
             uint32_t lo = 0, hi = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
@@ -272,7 +284,7 @@ __global__ void __launch_bounds__(256) iqr_decode_u4(const R97IqrDecodeDesc d, c
                 hi |= ((uint32_t)(uint8_t)(int8_t)v[4 + i]) << (8 * i);
             }
             *reinterpret_cast<uint2*>(s.codes + lr * d.cols + j0) = make_uint2(lo, hi);
-            if ((j0 & 127) == 0) s.scale[lr * (d.cols >> 7) + kb] = f32_to_bf16_bits(sc);
+            if ((j0 & 127) == 0) s.scale[lr * (d.cols >> 7) + kb] = f32_to_bf16_bits(sb[b]);
         }
     }
 }
