@@ -5,6 +5,8 @@
     python -m r97training_b200.profile_cases gdn       # one config-5 GDN layer, forward + backward
     python -m r97training_b200.profile_cases decode    # the IQR decode of a 24576 x 4096 weight
     python -m r97training_b200.profile_cases norms     # rmsnorm fwd/bwd at 8192 x 4096
+    python -m r97training_b200.profile_cases gnorm     # gated rmsnorm fwd/bwd at 8192 tokens x 32 heads x 128
+    python -m r97training_b200.profile_cases swiglu    # SwiGLU fwd/bwd at 8192 x 12288
     python -m r97training_b200.profile_cases loss      # CE over 2048 x 151936 bf16 logits (one head chunk)
     python -m r97training_b200.profile_cases adamw     # AdamW over the config-5 adapter (160.4 M f32 params)
     python -m r97training_b200.profile_cases conv      # GDN conv prep fwd + bwd at 8192 tokens, 8192 channels
@@ -65,6 +67,27 @@ def main(case: str) -> None:
         for _ in range(3):
             ops.rmsnorm_fwd(x, w)
             ops.rmsnorm_bwd(x, w, dy, addend=dy)
+    elif case == "gnorm":
+        from . import ops
+        T, H = 8192, 32
+        x = torch.randn(T * H, 128, device=dev).bfloat16()
+        z = torch.randn(T, H * 128, device=dev).bfloat16()
+        do = torch.randn(T * H, 128, device=dev).bfloat16()
+        w = torch.ones(128, device=dev)
+        dx, dz = torch.empty_like(x), torch.empty_like(z)
+        for _ in range(3):
+            ops.gated_rmsnorm_fwd(x, z, w)
+            ops.gated_rmsnorm_bwd(x, z, w, do, dx=dx, dz=dz)
+    elif case == "swiglu":
+        from . import ops
+        T, F = 8192, 12288
+        gu = torch.randn(T, 2 * F, device=dev).bfloat16()
+        y = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
+        dy = torch.randn(T, F, device=dev).bfloat16()
+        dgu = torch.empty_like(gu)
+        for _ in range(3):
+            ops.swiglu_fwd(gu, y)
+            ops.swiglu_bwd(gu, dy, dgu)
     elif case == "loss":
         from . import ops
         rows, vocab = 2048, 151936
