@@ -97,11 +97,18 @@ enum {
     R97B_EPI_STORE_F32 = 1,   /* out[m, n] = alpha * acc + beta * addend[m, n]      */
     R97B_EPI_ATOMIC_F32 = 2,  /* out[m, n] += alpha * acc  (f32, split-K allowed)   */
     R97B_EPI_ATOMIC_F32T = 3, /* out[n, m] += alpha * acc  (f32, split-K allowed)   */
+    R97B_EPI_SPLIT_BF16 = 4,  /* out[m, n] = bf16(alpha * acc + beta * addend[m, n]) with the reduction
+                               * split `splits` ways: each split stores its f32 partial tile in `ws`, and
+                               * the last split of a tile to finish sums the partials in split order
+                               * (deterministic) and stores the result */
 };
 
 /* D[M, N] = alpha * (A1[M, K1] B1[N, K1]^T + A2[M, K2] B2[N, K2]^T) (+ beta * addend), on tcgen05 tensor
  * cores with f32 accumulation in TMEM. K2 = 0 drops the second segment; when present, a2/b2 have the
- * same majorness as a1/b1. `splits` > 1 splits the reduction (atomic epilogues only). `bn` picks the
+ * same majorness as a1/b1. `splits` > 1 splits the reduction (atomic epilogues, and R97B_EPI_SPLIT_BF16
+ * with a workspace `ws` of at least r97b_gemm_workspace_bytes(g) bytes, 256-byte aligned, zeroed once
+ * before its first use: its tile counters return to zero at the end of every call, so it stays reusable,
+ * but calls that share one workspace must not overlap on the GPU). `bn` picks the
  * tile: 64, 128 or 256 wide on one SM (128 rows), 512 for a 256 x 256 tile computed by a pair of SMs
  * (tcgen05 cta_group::2, half the operand bytes per multiply-add); 0 picks by shape (the pair for
  * M, N > 128).
@@ -120,9 +127,15 @@ typedef struct R97bGemm {
     int64_t ld_add;
     int32_t bn;
     int32_t _pad;
+    void* ws;          /* R97B_EPI_SPLIT_BF16 with splits > 1: the split-K workspace */
+    int64_t ws_bytes;
 } R97bGemm;
 
 int r97b_gemm(const R97bGemm* g, void* stream);
+
+/* Bytes of workspace r97b_gemm needs for `g` (0 unless g->mode is R97B_EPI_SPLIT_BF16 with splits > 1);
+ * -1 for a description r97b_gemm would reject. */
+int64_t r97b_gemm_workspace_bytes(const R97bGemm* g);
 
 /* ------------------------------------------------------------------------------ norms */
 

@@ -31,7 +31,7 @@ class R97bGemm(ctypes.Structure):
                 ("a1", R97bMat), ("b1", R97bMat), ("a2", R97bMat), ("b2", R97bMat),
                 ("mode", c_i32), ("splits", c_i32), ("alpha", c_f32), ("beta", c_f32),
                 ("out", c_vp), ("ldo", c_i64), ("addend", c_vp), ("ld_add", c_i64),
-                ("bn", c_i32), ("_pad", c_i32)]
+                ("bn", c_i32), ("_pad", c_i32), ("ws", c_vp), ("ws_bytes", c_i64)]
 
 
 class R97IqrDecodeDesc(ctypes.Structure):
@@ -56,6 +56,7 @@ _SIGS = {
     "r97_iqr_decode": (c_i32, [c_vp, c_vp]),
     "r97b_iqr_dequant_bf16": (c_i32, [c_vp, c_vp, c_i64, c_vp]),
     "r97b_gemm": (c_i32, [c_vp, c_vp]),
+    "r97b_gemm_workspace_bytes": (c_i64, [c_vp]),
     "r97b_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
     "r97b_rmsnorm_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
     "r97b_gated_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp, c_vp, c_i64, c_i64, c_f32, c_i32, c_vp]),

@@ -13,7 +13,7 @@ void add_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memo
 
 extern "C" uint64_t r97b_launch_count(void) { return r97b::g_launches.load(std::memory_order_relaxed); }
 
-extern "C" int r97b_abi_version(void) { return 2; }
+extern "C" int r97b_abi_version(void) { return 3; }
 
 extern "C" int r97b_device_error(unsigned int* out_bits) {
     unsigned bits = r97b::gemm_error_word();
@@ -24,6 +24,11 @@ extern "C" int r97b_device_error(unsigned int* out_bits) {
 extern "C" int r97b_gemm(const R97bGemm* g, void* stream) {
     if (!g) return R97B_EINVAL;
     return r97b::gemm_run(*g, r97b::as_stream(stream));  // gemm_run counts its launch
+}
+
+extern "C" int64_t r97b_gemm_workspace_bytes(const R97bGemm* g) {
+    if (!g) return -1;
+    return r97b::gemm_workspace_bytes(*g);
 }
 
 extern "C" int r97b_mem_alloc(void** out, int64_t bytes) {

@@ -43,7 +43,23 @@ struct KernelArgs {
     int64_t ldo;
     const __nv_bfloat16* addend;
     int64_t ld_add;
+    float* ws_part;  // kEpiSplitBf16: f32 partial tiles [splits][tiles][kBM][BN]
+    int* ws_cnt;     // kEpiSplitBf16: per-tile count of finished splits (back to 0 after the tile's fix-up)
 };
+
+// The 128 epilogue threads (warps 4-7) synchronise among themselves on named barrier 1.
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// ... and agree on a flag: true only if it is true in every epilogue thread.
+__device__ __forceinline__ bool epi_all(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, 1, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v)
+        : "memory");
+    return r != 0;
+}
 
 template <int BN>
 struct Cfg {
@@ -67,13 +83,13 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
     tn = r / gm;
 }
 
-// The epilogue of 32 accumulator columns [n0, n0 + 32) of row m (r = the raw f32 bits), per args.mode.
-__device__ __forceinline__ void epilogue32(const KernelArgs& args, int m, int n0, const uint32_t (&r)[32]) {
+// The epilogue of 32 accumulator columns [n0, n0 + 32) of row m (r = the raw f32 bits), per `mode`.
+__device__ __forceinline__ void epilogue32(const KernelArgs& args, int mode, int m, int n0, const uint32_t (&r)[32]) {
     const bool full = n0 + 32 <= args.N;
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
-    if (args.mode == kEpiStoreBf16) {
+    if (mode == kEpiStoreBf16) {
         if (args.addend) {
             const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
 #pragma unroll
@@ -99,7 +115,7 @@ __device__ __forceinline__ void epilogue32(const KernelArgs& args, int m, int n0
             for (int i = 0; i < 32; ++i)
                 if (n0 + i < args.N) op[i] = __float2bfloat16_rn(v[i]);
         }
-    } else if (args.mode == kEpiStoreF32) {
+    } else if (mode == kEpiStoreF32) {
         float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
         if (args.addend) {
             const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
@@ -114,7 +130,7 @@ __device__ __forceinline__ void epilogue32(const KernelArgs& args, int m, int n0
             for (int i = 0; i < 32; ++i)
                 if (n0 + i < args.N) op[i] = v[i];
         }
-    } else if (args.mode == kEpiAtomicF32) {
+    } else if (mode == kEpiAtomicF32) {
         float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
         for (int i = 0; i < 32; ++i)
             if (full || n0 + i < args.N) atomicAdd(op + i, v[i]);
@@ -140,6 +156,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* tempty_bar = tfull_bar + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+    volatile int* split_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -264,16 +281,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp >= 4) {
         // ------------------------------------------------------------- epilogue
         const int q = warp & 3;  // TMEM lane quarter this warp may access
+        const bool split_mode = args.mode == kEpiSplitBf16;
         int local = 0;
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
             const int tile = u % tiles;
             int tm, tn;
             tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
             const int acc = local & 1;
-            if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag)) break;
+            bool ok = mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag);
+            if (split_mode) ok = epi_all(ok);  // the fix-up below syncs the four warps: they leave together
+            if (!ok) break;
             tc_fence_after();
             const int m = tm * kBM + q * 32 + lane;
             const bool mrow = m < args.M;
+            if (split_mode) {
+                // store this split's partial tile, release the accumulator, count the split in; the tile's
+                // last split sums every split's partial in split order and stores the bf16 result
+                const int split = u / tiles;
+                const int row = q * 32 + lane;
+                float* part = args.ws_part + (((int64_t)split * tiles + tile) * kBM + row) * BN;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    __syncwarp();
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+                    tmem_ld_wait();
+                    float4* dst = reinterpret_cast<float4*>(part + c * 32);
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        dst[i] = make_float4(__uint_as_float(r[4 * i]), __uint_as_float(r[4 * i + 1]),
+                                             __uint_as_float(r[4 * i + 2]), __uint_as_float(r[4 * i + 3]));
+                }
+                tc_fence_before();
+                mbar_arrive(&tempty_bar[acc]);
+                __threadfence();
+                epi_sync();
+                if (threadIdx.x == 128) {
+                    const int done = atomicAdd(args.ws_cnt + tile, 1) + 1;
+                    const int last = done == args.splits;
+                    if (last) atomicExch(args.ws_cnt + tile, 0);
+                    *split_flag = last;
+                }
+                epi_sync();
+                if (*split_flag) {
+                    __threadfence();
+                    const float* p0 = args.ws_part + ((int64_t)tile * kBM + row) * BN;
+                    const int64_t split_stride = (int64_t)tiles * kBM * BN;
+#pragma unroll 1
+                    for (int c = 0; c < BN / 32; ++c) {
+                        const int n0 = tn * BN + c * 32;
+                        if (!mrow || n0 >= args.N) continue;
+                        float v[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+                        for (int sp = 0; sp < args.splits; ++sp) {
+                            const float4* src = reinterpret_cast<const float4*>(p0 + sp * split_stride + c * 32);
+#pragma unroll
+                            for (int i = 0; i < 8; ++i) {
+                                const float4 x = __ldcg(src + i);
+                                v[4 * i] += x.x;
+                                v[4 * i + 1] += x.y;
+                                v[4 * i + 2] += x.z;
+                                v[4 * i + 3] += x.w;
+                            }
+                        }
+                        uint32_t r[32];
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
+                        epilogue32(args, kEpiStoreBf16, m, n0, r);
+                    }
+                }
+                continue;
+            }
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
@@ -282,7 +361,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 tmem_ld_wait();
                 const int n0 = tn * BN + c * 32;
                 if (!mrow || n0 >= args.N) continue;
-                epilogue32(args, m, n0, r);
+                epilogue32(args, args.mode, m, n0, r);
             }
             tc_fence_before();
             mbar_arrive(&tempty_bar[acc]);
@@ -476,7 +555,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 tmem_ld_wait();
                 const int n0 = tn * 256 + c * 32;
                 if (!mrow || n0 >= args.N) continue;
-                epilogue32(args, m, n0, r);
+                epilogue32(args, args.mode, m, n0, r);
             }
             tc_fence_before();
             mbar_arrive_cluster(cluster_addr(&tempty_bar[acc], 0));
@@ -542,6 +621,36 @@ int num_sms() {
     return n;
 }
 
+// How launch() splits the reduction: k blocks per split and the resulting number of splits.
+void split_geometry(const R97bGemm& g, int& kb_per_split, int& splits) {
+    const int k_total = (int)((g.K1 + kBK - 1) / kBK) + (g.K2 > 0 ? (int)((g.K2 + kBK - 1) / kBK) : 0);
+    int sp = g.splits > 1 ? g.splits : 1;
+    if (sp > k_total) sp = k_total;
+    kb_per_split = (k_total + sp - 1) / sp;
+    splits = (k_total + kb_per_split - 1) / kb_per_split;
+}
+
+int pick_bn(const R97bGemm& g) {
+    int bn = g.bn;
+    if (bn == 0) bn = g.N <= 64 ? 64 : (g.N <= 128 ? 128 : (g.M <= 128 ? 256 : 512));
+    if (bn == 512 && g.mode == kEpiSplitBf16) bn = 256;  // the split fix-up runs in the single-SM kernel
+    return bn;
+}
+
+// The split-K workspace of kEpiSplitBf16: per-tile counters (rounded up to 256 bytes), then the f32
+// partial tiles [splits][tiles][kBM][bn]. 0 when the call does not split.
+int64_t split_ws_bytes(const R97bGemm& g, int64_t* cnt_bytes) {
+    if (g.mode != kEpiSplitBf16) return 0;
+    const int bn = pick_bn(g);
+    int kbs, splits;
+    split_geometry(g, kbs, splits);
+    if (splits <= 1) return 0;
+    const int64_t tiles = ((g.M + kBM - 1) / kBM) * ((g.N + bn - 1) / bn);
+    const int64_t cb = (tiles * 4 + 255) / 256 * 256;
+    if (cnt_bytes) *cnt_bytes = cb;
+    return cb + (int64_t)splits * tiles * kBM * bn * 4;
+}
+
 template <int BN, int A_MN, int B_MN>
 int launch(const R97bGemm& g, cudaStream_t stream) {
     using C = Cfg<BN>;
@@ -560,14 +669,24 @@ int launch(const R97bGemm& g, cudaStream_t stream) {
     k.N = (int32_t)g.N;
     k.k1_blocks = (int32_t)((g.K1 + kBK - 1) / kBK);
     k.k2_blocks = g.K2 > 0 ? (int32_t)((g.K2 + kBK - 1) / kBK) : 0;
-    const int k_total = k.k1_blocks + k.k2_blocks;
-    int splits = g.splits > 1 ? g.splits : 1;
-    if (splits > k_total) splits = k_total;
-    k.kb_per_split = (k_total + splits - 1) / splits;
-    k.splits = (k_total + k.kb_per_split - 1) / k.kb_per_split;
+    int kbs, splits;
+    split_geometry(g, kbs, splits);
+    k.kb_per_split = kbs;
+    k.splits = splits;
     k.tiles_m = (int32_t)((g.M + kBM - 1) / kBM);
     k.tiles_n = (int32_t)((g.N + BN - 1) / BN);
     k.mode = g.mode;
+    if (g.mode == kEpiSplitBf16) {
+        if (splits <= 1) {
+            k.mode = kEpiStoreBf16;
+        } else {
+            int64_t cb = 0;
+            const int64_t need = split_ws_bytes(g, &cb);
+            if (!g.ws || (reinterpret_cast<uintptr_t>(g.ws) & 255) != 0 || g.ws_bytes < need) return R97B_EINVAL;
+            k.ws_cnt = reinterpret_cast<int*>(g.ws);
+            k.ws_part = reinterpret_cast<float*>(reinterpret_cast<char*>(g.ws) + cb);
+        }
+    }
     k.alpha = g.alpha;
     k.beta = g.beta;
     k.out = g.out;
@@ -605,11 +724,10 @@ int launch_pair(const R97bGemm& g, cudaStream_t stream) {
     k.N = (int32_t)g.N;
     k.k1_blocks = (int32_t)((g.K1 + kBK - 1) / kBK);
     k.k2_blocks = g.K2 > 0 ? (int32_t)((g.K2 + kBK - 1) / kBK) : 0;
-    const int k_total = k.k1_blocks + k.k2_blocks;
-    int splits = g.splits > 1 ? g.splits : 1;
-    if (splits > k_total) splits = k_total;
-    k.kb_per_split = (k_total + splits - 1) / splits;
-    k.splits = (k_total + k.kb_per_split - 1) / k.kb_per_split;
+    int kbs, splits;
+    split_geometry(g, kbs, splits);
+    k.kb_per_split = kbs;
+    k.splits = splits;
     k.tiles_m = (int32_t)((g.M + 255) / 256);
     k.tiles_n = (int32_t)((g.N + 255) / 256);
     k.mode = g.mode;
@@ -645,14 +763,20 @@ int dispatch_major(const R97bGemm& g, cudaStream_t s) {
 
 R97B_ERROR_READER(gemm_error_word)
 
+int64_t gemm_workspace_bytes(const R97bGemm& g) {
+    if (g.M <= 0 || g.N <= 0 || g.K1 <= 0 || g.mode < kEpiStoreBf16 || g.mode > kEpiSplitBf16) return -1;
+    const int bn = pick_bn(g);
+    if (bn != 64 && bn != 128 && bn != 256 && bn != 512) return -1;
+    return split_ws_bytes(g, nullptr);
+}
+
 int gemm_run(const R97bGemm& g, cudaStream_t stream) {
     if (g.M <= 0 || g.N <= 0 || g.K1 <= 0 || !g.out || !g.a1.ptr || !g.b1.ptr) return R97B_EINVAL;
     if (g.K2 > 0 && (!g.a2.ptr || !g.b2.ptr || g.a2.mn_major != g.a1.mn_major || g.b2.mn_major != g.b1.mn_major))
         return R97B_EINVAL;
-    if (g.mode < kEpiStoreBf16 || g.mode > kEpiAtomicF32T) return R97B_EINVAL;
+    if (g.mode < kEpiStoreBf16 || g.mode > kEpiSplitBf16) return R97B_EINVAL;
     if (g.M > 0x7FFFFFFF || g.N > 0x7FFFFFFF) return R97B_EINVAL;
-    int bn = g.bn;
-    if (bn == 0) bn = g.N <= 64 ? 64 : (g.N <= 128 ? 128 : (g.M <= 128 ? 256 : 512));
+    const int bn = pick_bn(g);
     if (bn == 512) {  // the CTA-pair kernel: 256 x 256 tiles over two SMs
         const int a = g.a1.mn_major ? 1 : 0, b = g.b1.mn_major ? 1 : 0;
         if (a == 0 && b == 0) return launch_pair<0, 0>(g, stream);

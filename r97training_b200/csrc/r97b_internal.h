@@ -12,8 +12,10 @@ constexpr int kEpiStoreBf16 = R97B_EPI_STORE_BF16;
 constexpr int kEpiStoreF32 = R97B_EPI_STORE_F32;
 constexpr int kEpiAtomicF32 = R97B_EPI_ATOMIC_F32;
 constexpr int kEpiAtomicF32T = R97B_EPI_ATOMIC_F32T;
+constexpr int kEpiSplitBf16 = R97B_EPI_SPLIT_BF16;
 
 int gemm_run(const R97bGemm& g, cudaStream_t stream);
+int64_t gemm_workspace_bytes(const R97bGemm& g);
 unsigned gemm_error_word();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }

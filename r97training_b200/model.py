@@ -312,6 +312,7 @@ class TrainStep:
         self.plan = GdnPlan(cu, cfg.gdn_heads, cfg.gdn_qk_heads, model.device)
         self.grad_hook = None
         self.launches = 0
+        self.split_ws = ops.SplitWorkspace(model.device)
 
     # ------------------------------------------------------------------ decoded base weights
     def _w_fwd(self, li, g: Group) -> torch.Tensor:
@@ -335,9 +336,17 @@ class TrainStep:
         """t = s x A_all^T ; out = x W^T + t B_blk^T (+ addend). Returns t (saved for dB)."""
         cfg, ad = self.cfg, self.adapter
         t = torch.empty((x.shape[0], g.r_all * cfg.rank), dtype=torch.bfloat16, device=x.device)
-        ops.gemm(x, ad.a_bf[(li, g.name)], t, alpha=cfg.lora_scale)
+        self._skinny(x, ad.a_bf[(li, g.name)], t, g.k, False)
         ops.gemm(x, W, out, a2=t, b2=ad.b_blk[(li, g.name)], addend=addend, beta=1.0)
         return t
+
+    def _skinny(self, a, b, out, K, b_mn):
+        """out = s a b^T for the adapter's narrow products (t = s x A_all^T, dt = s dY B_blk): tiled and
+        split so that ~all SMs share the read of `a` (ops.skinny_tiling)."""
+        M, N = out.shape
+        bn, splits = ops.skinny_tiling(M, N, K)
+        ops.gemm(a, b, out, b_mn=b_mn, alpha=self.cfg.lora_scale, N=N, bn=bn, splits=splits,
+                 mode=ops.EPI_SPLIT_BF16 if splits > 1 else ops.EPI_STORE_BF16, ws=self.split_ws.buf)
 
     def _lin_bwd(self, li, g: Group, x: torch.Tensor, t: torch.Tensor, W: torch.Tensor, dy: torch.Tensor,
                  dx_out: torch.Tensor):
@@ -345,16 +354,16 @@ class TrainStep:
         cfg, ad = self.cfg, self.adapter
         r = cfg.rank
         dt = torch.empty((dy.shape[0], g.r_all * r), dtype=torch.bfloat16, device=dy.device)
-        ops.gemm(dy, ad.b_blk[(li, g.name)], dt, b_mn=True, alpha=cfg.lora_scale, N=g.r_all * r)
+        self._skinny(dy, ad.b_blk[(li, g.name)], dt, g.n, True)
         ops.gemm(dy, W, dx_out, b_mn=True, a2=dt, b2=ad.a_bf[(li, g.name)], N=g.k)
-        M = x.shape[0]
-        splits = max(1, M // 1024)
+        bn, splits = ops.grad_tiling(g.k, g.r_all * r)
         ops.gemm(x, dt, ad.a_view(ad.g, g), a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32T, splits=splits,
-                 M=g.k, N=g.r_all * r)
+                 bn=bn, M=g.k, N=g.r_all * r)
         col = 0
         for i, (_, n) in enumerate(g.projs):
+            bn, splits = ops.grad_tiling(n, r)
             ops.gemm(dy[:, col:col + n], t[:, i * r:(i + 1) * r], ad.b_view(ad.g, g, i), a_mn=True, b_mn=True,
-                     mode=ops.EPI_ATOMIC_F32, splits=splits, M=n, N=r)
+                     mode=ops.EPI_ATOMIC_F32, splits=splits, bn=bn, M=n, N=r)
             col += n
 
     # ------------------------------------------------------------------ blocks

@@ -12,7 +12,7 @@ import torch
 
 from ._lib import R97bGemm, R97bMat, R97bError, check, lib
 
-EPI_STORE_BF16, EPI_STORE_F32, EPI_ATOMIC_F32, EPI_ATOMIC_F32T = 0, 1, 2, 3
+EPI_STORE_BF16, EPI_STORE_F32, EPI_ATOMIC_F32, EPI_ATOMIC_F32T, EPI_SPLIT_BF16 = 0, 1, 2, 3, 4
 
 
 def _stream(stream=None) -> int:
@@ -45,11 +45,12 @@ def _mat(t: torch.Tensor, mn_major: bool, rows: int, k: int, name: str) -> R97bM
 
 
 def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STORE_BF16, alpha=1.0,
-         addend=None, beta=1.0, splits=1, bn=0, M=None, N=None, stream=None):
+         addend=None, beta=1.0, splits=1, bn=0, M=None, N=None, ws=None, stream=None):
     """out (+)= alpha * (A1 B1^T + A2 B2^T) (+ beta * addend); see include/r97b.h (r97b_gemm).
 
     A1 is [M, K1] (K-major) or stored [K1, M] (a_mn); B1 is [N, K1] or stored [K1, N] (b_mn); the optional
-    tail (a2, b2) has the same majorness with its own K2."""
+    tail (a2, b2) has the same majorness with its own K2. EPI_SPLIT_BF16 with splits > 1 needs `ws`, a
+    zero-initialised device buffer of at least r97b_gemm_workspace_bytes bytes (see SplitWorkspace)."""
     if M is None:
         M = a1.shape[1] if a_mn else a1.shape[0]
     if N is None:
@@ -65,7 +66,15 @@ def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STOR
         g.a2 = _mat(a2, a_mn, M, K2, "a2")
         g.b2 = _mat(b2, b_mn, N, K2, "b2")
     g.mode, g.splits, g.alpha, g.beta, g.bn = mode, splits, alpha, beta, bn
-    if mode == EPI_STORE_BF16:
+    if mode == EPI_SPLIT_BF16:
+        need = int(lib().r97b_gemm_workspace_bytes(ctypes.byref(g)))
+        if need < 0:
+            raise R97bError("r97b_gemm: bad split GEMM description")
+        if need > 0:
+            if ws is None or ws.numel() * ws.element_size() < need or ws.device != out.device:
+                raise R97bError(f"r97b_gemm: the split GEMM needs a {need}-byte workspace on {out.device}")
+            g.ws, g.ws_bytes = ws.data_ptr(), ws.numel() * ws.element_size()
+    if mode in (EPI_STORE_BF16, EPI_SPLIT_BF16):
         _need(out, torch.bfloat16, "out")
     else:
         _need(out, torch.float32, "out")
@@ -88,6 +97,35 @@ def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STOR
         e1.record(s)
         prof.append((e0, e1, 2.0 * M * N * (K1 + (g.K2 if a2 is not None else 0))))
     return out
+
+
+def skinny_tiling(M: int, N: int, K: int, sms: int = 148):
+    """(bn, splits) for a GEMM with few output columns (the adapter's shrink and expand products, N = a
+    few x 64, bf16 out): bn 64 up to 64 columns, else 128; the reduction is split in two (EPI_SPLIT_BF16)
+    when the tiles would fill under 100 of the SMs and a split pays for its partial tiles -- always at 64
+    columns, and for wider outputs only with a long reduction (K >= 8192). Measured on B200 at the
+    config-5 shapes (M = 8192)."""
+    bn = 64 if N <= 64 else 128
+    units = -(-M // 128) * -(-N // bn)
+    splits = 2 if units < 100 and (N <= 64 or K >= 8192) else 1
+    return bn, splits
+
+
+def grad_tiling(M: int, N: int) -> tuple:
+    """(bn, splits) for the adapter-gradient GEMMs (f32 atomic accumulation, reduction over the tokens):
+    the fewest splits that give ~128 work units, at most 4 (more splits cost more in atomic traffic than
+    they gain in parallelism; measured on B200 at the config-5 shapes)."""
+    bn = 128 if N >= 128 else 64
+    tiles = -(-M // 128) * -(-N // bn)
+    return bn, max(1, min(4, round(128 / tiles)))
+
+
+class SplitWorkspace:
+    """A zero-initialised device buffer for EPI_SPLIT_BF16 GEMMs on one stream: its tile counters return
+    to zero after every call, so consecutive calls share it; calls on different streams need their own."""
+
+    def __init__(self, device, nbytes: int = 64 << 20):
+        self.buf = torch.zeros(nbytes // 4, dtype=torch.int32, device=device)
 
 
 # When a list, every gemm() appends (start event, end event, algorithmic FLOPs) recorded on its stream (in a

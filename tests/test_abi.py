@@ -34,3 +34,18 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_binding_table_covers_declarations():
     missing = declared() - set(exported_symbols())
     assert not missing, f"declared in include/ but not bound in _lib: {sorted(missing)}"
+
+
+def test_gemm_workspace_bytes_without_a_gpu():
+    """The split-K workspace size is host arithmetic: 256-byte-rounded tile counters, then the f32 partial
+    tiles [splits][tiles][128][bn]; 0 when the call does not split; -1 for a description the GEMM rejects."""
+    from r97training_b200._lib import R97bGemm
+    g = R97bGemm()
+    g.M, g.N, g.K1, g.mode, g.splits, g.bn = 8192, 64, 4096, 4, 2, 64
+    assert lib().r97b_gemm_workspace_bytes(ctypes.byref(g)) == 256 + 2 * 64 * 128 * 64 * 4
+    g.splits = 1
+    assert lib().r97b_gemm_workspace_bytes(ctypes.byref(g)) == 0
+    g.mode, g.splits = 0, 2
+    assert lib().r97b_gemm_workspace_bytes(ctypes.byref(g)) == 0
+    g.mode = 9
+    assert lib().r97b_gemm_workspace_bytes(ctypes.byref(g)) == -1

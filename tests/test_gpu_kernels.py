@@ -142,6 +142,34 @@ def test_gemm_split_k_atomic(cuda, transposed):
     assert rel_l2(to_np(out), want) < 1e-5
 
 
+@pytest.mark.parametrize("b_mn,bn,splits", [(False, 64, 2), (True, 64, 3), (False, 128, 2), (True, 256, 4),
+                                            (False, 64, 1)])
+def test_gemm_split_bf16_deterministic(cuda, b_mn, bn, splits):
+    """EPI_SPLIT_BF16: the reduction split across CTAs, partials summed in split order by the tile's last
+    split -- the adapter's narrow products (t = s x A^T, dt = s dY B). Ragged M and K, the same bits on a
+    repeat, the workspace's counters back at zero afterwards, and a missing workspace rejected."""
+    rs = np.random.RandomState(30 + bn + splits)
+    M, N, K = 1000, 136 if bn > 64 else 64, 1600
+    A, B, C = _bf(rs, (M, K)), _bf(rs, (N, K), 0.05), _bf(rs, (M, N))
+    b_dev = (B.t().contiguous() if b_mn else B).to(cuda)
+    ws = ops.SplitWorkspace(cuda, 8 << 20)
+    outs = []
+    for _ in range(2):
+        out = torch.empty((M, N), dtype=torch.bfloat16, device=cuda)
+        ops.gemm(A.to(cuda), b_dev, out, b_mn=b_mn, N=N, mode=ops.EPI_SPLIT_BF16, splits=splits, bn=bn,
+                 alpha=2.0, addend=C.to(cuda), beta=1.0, ws=ws.buf)
+        outs.append(out)
+    torch.cuda.synchronize()
+    want = 2.0 * (A.double().numpy() @ B.double().numpy().T) + C.double().numpy()
+    assert_close_bf16(to_np(outs[0]), want, rel=4e-3, what="split bf16")
+    assert torch.equal(outs[0], outs[1])
+    cnt = ws.buf[:(-(-M // 128)) * (-(-N // bn))]
+    assert int(cnt.abs().sum()) == 0
+    if splits > 1:
+        with pytest.raises(Exception):
+            ops.gemm(A.to(cuda), b_dev, outs[0], b_mn=b_mn, N=N, mode=ops.EPI_SPLIT_BF16, splits=splits, bn=bn)
+
+
 def test_gemm_ragged_edges(cuda):
     rs = np.random.RandomState(8)
     M, N, K = 200, 136, 200   # none a multiple of the tile
