@@ -137,6 +137,34 @@ int r97b_gemm(const R97bGemm* g, void* stream);
  * -1 for a description r97b_gemm would reject. */
 int64_t r97b_gemm_workspace_bytes(const R97bGemm* g);
 
+/* ------------------------------------------------------------------------------ attention */
+
+/* The backward of causal grouped-query attention softmax(scale q k^T) v, given the forward's output `o` and
+ * its per-row natural-log log-sum-exp `lse` (of the scaled scores): dq, dk, dv. q, o, dout, dq are bf16
+ * [B, Hq, S, D]; k, v, dk, dv bf16 [B, Hkv, S, D]; lse f32 [B, Hq, S]; query head h reads key/value head
+ * h / (Hq / Hkv). S a multiple of 128, D 128 or 256, every pointer 16-byte aligned. `ws` (256-byte
+ * aligned, r97b_attn_bwd_workspace_bytes bytes) holds the P and dS tiles and the row sums dO . O.
+ * Replaces: the reference's attention adjoint (src/adjoint/host/attention.cpp:261-414, the softmax and
+ * value products of attention_host_adjoint; its device twin src/adjoint/device/attention.hip). */
+typedef struct R97bAttnBwd {
+    int32_t B, Hq, Hkv, S, D;
+    float scale;
+    const void* q;
+    const void* k;
+    const void* v;
+    const void* o;
+    const void* dout;
+    const float* lse;
+    void* dq;
+    void* dk;
+    void* dv;
+    void* ws;
+    int64_t ws_bytes;
+} R97bAttnBwd;
+
+int r97b_attn_bwd(const R97bAttnBwd* a, void* stream);
+int64_t r97b_attn_bwd_workspace_bytes(int32_t B, int32_t Hq, int32_t S);
+
 /* ------------------------------------------------------------------------------ norms */
 
 /* y = x * rsqrt(mean(x^2) + eps) * (w + wadd) * mult per row of n (x, y bf16 [rows, n]; w f32 [n] or null;

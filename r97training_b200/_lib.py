@@ -34,6 +34,12 @@ class R97bGemm(ctypes.Structure):
                 ("bn", c_i32), ("_pad", c_i32), ("ws", c_vp), ("ws_bytes", c_i64)]
 
 
+class R97bAttnBwd(ctypes.Structure):
+    _fields_ = [("B", c_i32), ("Hq", c_i32), ("Hkv", c_i32), ("S", c_i32), ("D", c_i32), ("scale", c_f32),
+                ("q", c_vp), ("k", c_vp), ("v", c_vp), ("o", c_vp), ("dout", c_vp), ("lse", c_vp),
+                ("dq", c_vp), ("dk", c_vp), ("dv", c_vp), ("ws", c_vp), ("ws_bytes", c_i64)]
+
+
 class R97IqrDecodeDesc(ctypes.Structure):
     """Field-for-field the C struct of include/r97b_iqr.h (the reference's R97IqrDecodeDesc layout)."""
     _fields_ = [
@@ -57,6 +63,8 @@ _SIGS = {
     "r97b_iqr_dequant_bf16": (c_i32, [c_vp, c_vp, c_i64, c_vp]),
     "r97b_gemm": (c_i32, [c_vp, c_vp]),
     "r97b_gemm_workspace_bytes": (c_i64, [c_vp]),
+    "r97b_attn_bwd": (c_i32, [c_vp, c_vp]),
+    "r97b_attn_bwd_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "r97b_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
     "r97b_rmsnorm_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
     "r97b_gated_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_vp, c_vp, c_i64, c_i64, c_f32, c_i32, c_vp]),

@@ -587,6 +587,8 @@ bool encode_fn() {
     return g_encode != nullptr;
 }
 
+}  // namespace
+
 // A row-major bf16 matrix [outer, inner] (inner contiguous, row stride `ld` elements) as a 2D tensor
 // map with a (box_inner, box_outer) box and the 128-byte swizzle. Out-of-range boxes read zeros.
 bool make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
@@ -620,6 +622,8 @@ int num_sms() {
     }
     return n;
 }
+
+namespace {
 
 // How launch() splits the reduction: k blocks per split and the resulting number of splits.
 void split_geometry(const R97bGemm& g, int& kb_per_split, int& splits) {

@@ -1,6 +1,7 @@
 // r97b_internal.h -- declarations shared by the .cu files of libr97b200.so (not part of the ABI).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -15,6 +16,11 @@ constexpr int kEpiAtomicF32T = R97B_EPI_ATOMIC_F32T;
 constexpr int kEpiSplitBf16 = R97B_EPI_SPLIT_BF16;
 
 int gemm_run(const R97bGemm& g, cudaStream_t stream);
+// A row-major bf16 matrix [outer, inner] (row stride `ld` elements) as a 2D TMA tensor map with a
+// (box_inner, box_outer) box and the 128-byte swizzle (gemm_tc.cu).
+bool make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
+              int box_outer);
+int num_sms();
 int64_t gemm_workspace_bytes(const R97bGemm& g);
 unsigned gemm_error_word();
 

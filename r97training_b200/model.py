@@ -15,8 +15,8 @@ reference's gemm_nt + lora_shrink + lora_expand rows (src/adjoint/host/linear.cp
 The backward is explicit: every layer's forward saves what its adjoint reads (HBM holds a step's
 activations: about 60 GB at config 5), and the reverse walk calls the kernels' adjoints in the
 reverse op order -- the fixed per-layer schedule the reference's backward_block walks over its tape.
-The attention core (softmax(q k^T) v, causal, GQA) is torch's fused SDPA kernel: a library call, the
-one piece of the block that is not this package's own kernel.
+The attention core's forward (softmax(q k^T) v, causal, GQA) is torch's flash kernel -- a library call --
+whose output and log-sum-exp feed this package's own tensor-core backward (csrc/attn.cu).
 """
 from __future__ import annotations
 
@@ -313,6 +313,7 @@ class TrainStep:
         self.grad_hook = None
         self.launches = 0
         self.split_ws = ops.SplitWorkspace(model.device)
+        self.attn_ws = None  # the attention backward's P / dS tiles, allocated at the first attention layer
 
     # ------------------------------------------------------------------ decoded base weights
     def _w_fwd(self, li, g: Group) -> torch.Tensor:
@@ -463,13 +464,16 @@ class TrainStep:
         ops.gate_mul_bwd(sv["attn"], y[:, Dh:], 2 * Dh, Hq, S, dga, dattn, dy[:, Dh:])
         qg, kg, vg = sv["qkv"]
         fa = sv["fa"]
-        dq, dk, dv = torch.ops.aten._scaled_dot_product_flash_attention_backward(
-            dattn, qg, kg, vg, fa[0], fa[1], fa[2], fa[3], fa[4], fa[5], 0.0, True, fa[6], fa[7])
+        # the attention core's adjoint on this package's tensor-core passes (csrc/attn.cu), from the flash
+        # forward's output and log-sum-exp
+        if self.attn_ws is None:
+            self.attn_ws = ops.attn_bwd_workspace(B, Hq, S, x.device)
+        dq, dk, dv = ops.attn_bwd(qg, kg, vg, fa[0], dattn, fa[1], 1.0 / math.sqrt(Dh), self.attn_ws)
         ops.qk_norm_rope_bwd(y, 2 * Dh, Hq, blk["q_norm"], self.model.rope_cos, self.model.rope_sin, cfg.rotary_dim,
-                             S, cfg.eps, dq.contiguous(), dy)
+                             S, cfg.eps, dq, dy)
         ops.qk_norm_rope_bwd(y[:, qn:], Dh, Hkv, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
-                             cfg.rotary_dim, S, cfg.eps, dk.contiguous(), dy[:, qn:])
-        ops.to_bhsd(dy[:, qn + Hkv * Dh:], Dh, Hkv, S, dv.contiguous(), reverse=True)
+                             cfg.rotary_dim, S, cfg.eps, dk, dy[:, qn:])
+        ops.to_bhsd(dy[:, qn + Hkv * Dh:], Dh, Hkv, S, dv, reverse=True)
         W = self._w_bwd(li, g_qkv)
         dn1 = torch.empty_like(x)
         self._lin_bwd(li, g_qkv, sv["n1"], sv["t_qkv"], W, dy, dn1)

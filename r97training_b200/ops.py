@@ -10,7 +10,7 @@ import ctypes
 
 import torch
 
-from ._lib import R97bGemm, R97bMat, R97bError, check, lib
+from ._lib import R97bAttnBwd, R97bGemm, R97bMat, R97bError, check, lib
 
 EPI_STORE_BF16, EPI_STORE_F32, EPI_ATOMIC_F32, EPI_ATOMIC_F32T, EPI_SPLIT_BF16 = 0, 1, 2, 3, 4
 
@@ -315,6 +315,35 @@ def gate_mul_bwd(attn, gate, gate_hs, heads, S, dy, dattn, dgate, stream=None):
     T = dy.shape[0]
     check(lib().r97b_gate_mul_bwd(_ptr(attn), _ptr(gate), gate.stride(0), gate_hs, heads, T, S, _ptr(dy),
                                   _ptr(dattn), _ptr(dgate), dgate.stride(0), _stream(stream)), "r97b_gate_mul_bwd")
+
+
+def attn_bwd_workspace(B: int, Hq: int, S: int, device) -> torch.Tensor:
+    """A device buffer of the bytes r97b_attn_bwd needs for (B, Hq, S) (the P and dS tiles, the row sums)."""
+    n = int(lib().r97b_attn_bwd_workspace_bytes(B, Hq, S))
+    if n < 0:
+        raise R97bError("r97b_attn_bwd_workspace_bytes: bad shape")
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def attn_bwd(q, k, v, o, dout, lse, scale, ws, dq=None, dk=None, dv=None, stream=None):
+    """dq, dk, dv of causal GQA attention softmax(scale q k^T) v (r97b_attn_bwd): q, o, dout [B, Hq, S, D],
+    k, v [B, Hkv, S, D] bf16 contiguous; lse f32 [B, Hq, S] (the forward's natural-log log-sum-exp)."""
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    for t, name, shape in ((q, "q", (B, Hq, S, D)), (k, "k", (B, Hkv, S, D)), (v, "v", (B, Hkv, S, D)),
+                           (o, "o", (B, Hq, S, D)), (dout, "dout", (B, Hq, S, D))):
+        _need(t, torch.bfloat16, name)
+        if tuple(t.shape) != shape or not t.is_contiguous():
+            raise R97bError(f"{name} must be a contiguous {shape} bf16 tensor")
+    if lse.dtype != torch.float32 or lse.dim() != 3 or tuple(lse.shape) != (B, Hq, S) or not lse.is_contiguous():
+        raise R97bError("lse must be a contiguous [B, Hq, S] f32 tensor")
+    dq = torch.empty_like(q) if dq is None else dq
+    dk = torch.empty_like(k) if dk is None else dk
+    dv = torch.empty_like(v) if dv is None else dv
+    a = R97bAttnBwd(B, Hq, Hkv, S, D, float(scale), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(dout), _ptr(lse),
+                    _ptr(dq), _ptr(dk), _ptr(dv), _ptr(ws), ws.numel() * ws.element_size())
+    check(lib().r97b_attn_bwd(ctypes.byref(a), _stream(stream)), "r97b_attn_bwd")
+    return dq, dk, dv
 
 
 def embed(table, ids, out, stream=None):
