@@ -408,6 +408,23 @@ int r97b_embed(const uint16_t* table, int64_t ld, int64_t vocab, const int32_t* 
 int r97b_cast_f32_bf16(const float* src, int64_t ld_src, uint16_t* dst, int64_t ld_dst, int64_t rows, int64_t cols,
                        void* stream);
 
+/* One segment of a batched cast: rows x cols (cols a multiple of 8) f32 -> bf16; `unit0` = the 8-element
+ * units of every segment before it in the table. src and dst rows 16-byte aligned. */
+typedef struct R97bCastSeg {
+    const float* src;
+    int64_t ld_src;
+    void* dst;
+    int64_t ld_dst;
+    int64_t rows;
+    int64_t cols;
+    int64_t unit0;
+} R97bCastSeg;
+
+/* Every segment of a table (in DEVICE memory, nseg entries, `units` = the table's total 8-element units)
+ * cast in one launch: the adapter's bf16 mirrors refreshed after an update (the reference keeps one f32
+ * master per adapter tensor and hands the device its bf16 view, src/delta_lora.cpp). */
+int r97b_cast_segments(const R97bCastSeg* segs, int32_t nseg, int64_t units, void* stream);
+
 /* How many kernels this library has launched in this process (a diagnostic for the bench). */
 uint64_t r97b_launch_count(void);
 

@@ -40,6 +40,11 @@ class R97bAttnBwd(ctypes.Structure):
                 ("dq", c_vp), ("dk", c_vp), ("dv", c_vp), ("ws", c_vp), ("ws_bytes", c_i64)]
 
 
+class R97bCastSeg(ctypes.Structure):
+    _fields_ = [("src", c_vp), ("ld_src", c_i64), ("dst", c_vp), ("ld_dst", c_i64), ("rows", c_i64),
+                ("cols", c_i64), ("unit0", c_i64)]
+
+
 class R97IqrDecodeDesc(ctypes.Structure):
     """Field-for-field the C struct of include/r97b_iqr.h (the reference's R97IqrDecodeDesc layout)."""
     _fields_ = [
@@ -64,6 +69,7 @@ _SIGS = {
     "r97b_gemm": (c_i32, [c_vp, c_vp]),
     "r97b_gemm_workspace_bytes": (c_i64, [c_vp]),
     "r97b_attn_bwd": (c_i32, [c_vp, c_vp]),
+    "r97b_cast_segments": (c_i32, [c_vp, c_i32, c_i64, c_vp]),
     "r97b_attn_bwd_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "r97b_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
     "r97b_rmsnorm_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),

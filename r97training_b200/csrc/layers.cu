@@ -577,6 +577,33 @@ __global__ void cast_2d_kernel(const float* __restrict__ src, int64_t ld_src, __
     dst[r * ld_dst + c] = __float2bfloat16_rn(src[r * ld_src + c]);
 }
 
+// Many casts in one launch: thread u converts the 8 elements of unit u (units counted across the table's
+// segments, each segment's rows of `cols` elements in 8-element units); the segment is found by binary
+// search on the units before it.
+__global__ void cast_segments_kernel(const R97bCastSeg* __restrict__ segs, int nseg, int64_t units) {
+    const int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (u >= units) return;
+    int lo = 0, hi = nseg - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (segs[mid].unit0 <= u) lo = mid;
+        else hi = mid - 1;
+    }
+    const R97bCastSeg sg = segs[lo];
+    const int64_t per_row = sg.cols >> 3;
+    const int64_t k = u - sg.unit0;
+    const int64_t r = k / per_row, c = (k - r * per_row) * 8;
+    const float4 a = *reinterpret_cast<const float4*>(sg.src + r * sg.ld_src + c);
+    const float4 b = *reinterpret_cast<const float4*>(sg.src + r * sg.ld_src + c + 4);
+    uint4 o;
+    __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&o);
+    h[0] = __floats2bfloat162_rn(a.x, a.y);
+    h[1] = __floats2bfloat162_rn(a.z, a.w);
+    h[2] = __floats2bfloat162_rn(b.x, b.y);
+    h[3] = __floats2bfloat162_rn(b.z, b.w);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(sg.dst) + r * sg.ld_dst + c) = o;
+}
+
 unsigned blocks_for(int64_t threads) { return (unsigned)((threads + 255) / 256); }
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -714,5 +741,11 @@ extern "C" int r97b_cast_f32_bf16(const float* src, int64_t ld_src, uint16_t* ds
     cast_2d_kernel<<<blocks_for(rows * cols), 256, 0, as_stream(stream)>>>(src, ld_src,
                                                                          reinterpret_cast<__nv_bfloat16*>(dst), ld_dst,
                                                                          rows, cols);
+    return launch_status();
+}
+
+extern "C" int r97b_cast_segments(const R97bCastSeg* segs, int32_t nseg, int64_t units, void* stream) {
+    if (!segs || nseg <= 0 || units <= 0) return R97B_EINVAL;
+    cast_segments_kernel<<<blocks_for(units), 256, 0, as_stream(stream)>>>(segs, nseg, units);
     return launch_status();
 }

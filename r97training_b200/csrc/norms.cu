@@ -218,6 +218,209 @@ __global__ void __launch_bounds__(256) gated_rmsnorm_bwd_kernel(const __nv_bfloa
     }
 }
 
+// ---- wide rows held in registers: 128 threads a row (two rows a 256-thread block), VPT 8-vectors each
+// (n = 1024 VPT); every load of the row is in flight at once and x is read once.
+template <int VPT>
+__device__ __forceinline__ float row_sum128(float v, float* red) {
+    v = group_sum<32>(v);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    const int b = (threadIdx.x >> 7) * 4;
+    return red[b] + red[b + 1] + red[b + 2] + red[b + 3];
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_row(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                                                       __nv_bfloat16* __restrict__ y, float* __restrict__ rstd,
+                                                       int64_t rows, float eps, float wadd, float mult) {
+    __shared__ float red[8];
+    constexpr int n = VPT * 1024;
+    const int t = threadIdx.x & 127;
+    const int64_t grow = (int64_t)blockIdx.x * 2 + (threadIdx.x >> 7);
+    const bool valid = grow < rows;
+    const int64_t row = valid ? grow : rows - 1;
+    float v[VPT][8];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) load8(x + row * n + (i * 128 + t) * 8, v[i]);
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss = fmaf(v[i][e], v[i][e], ss);
+    ss = row_sum128<VPT>(ss, red);
+    const float s = rsqrtf(ss / (float)n + eps);
+    if (rstd && t == 0 && valid) rstd[row] = s;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int c = (i * 128 + t) * 8;
+        float g[8];
+        if (w) loadw8(w + c, g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[i][e] = v[i][e] * s * (w ? g[e] + wadd : 1.0f) * mult;
+        if (valid) store8(y + row * n + c, v[i]);
+    }
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_row(const __nv_bfloat16* __restrict__ x, const float* __restrict__ w,
+                                                       const __nv_bfloat16* __restrict__ dy,
+                                                       const __nv_bfloat16* __restrict__ addend,
+                                                       __nv_bfloat16* __restrict__ dx, int64_t rows, float eps,
+                                                       float wadd, float mult) {
+    __shared__ float red[2][8];
+    constexpr int n = VPT * 1024;
+    const int t = threadIdx.x & 127;
+    const int64_t grow = (int64_t)blockIdx.x * 2 + (threadIdx.x >> 7);
+    const bool valid = grow < rows;
+    const int64_t row = valid ? grow : rows - 1;
+    float v[VPT][8], d[VPT][8];
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        load8(x + row * n + (i * 128 + t) * 8, v[i]);
+        load8(dy + row * n + (i * 128 + t) * 8, d[i]);
+    }
+    float ss = 0.0f, tt = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        float g[8];
+        if (w) loadw8(w + (i * 128 + t) * 8, g);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            ss = fmaf(v[i][e], v[i][e], ss);
+            tt = fmaf(d[i][e] * v[i][e], w ? g[e] + wadd : 1.0f, tt);
+        }
+    }
+    ss = group_sum<32>(ss);
+    tt = group_sum<32>(tt);
+    if ((threadIdx.x & 31) == 0) {
+        red[0][threadIdx.x >> 5] = ss;
+        red[1][threadIdx.x >> 5] = tt;
+    }
+    __syncthreads();
+    const int b = (threadIdx.x >> 7) * 4;
+    ss = red[0][b] + red[0][b + 1] + red[0][b + 2] + red[0][b + 3];
+    tt = red[1][b] + red[1][b + 1] + red[1][b + 2] + red[1][b + 3];
+    const float s = rsqrtf(ss / (float)n + eps);
+    const float k = s * s * s * tt / (float)n;
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+        const int c = (i * 128 + t) * 8;
+        float g[8], a[8];
+        if (w) loadw8(w + c, g);
+        if (addend) load8(addend + row * n + c, a);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float cc = w ? g[e] + wadd : 1.0f;
+            v[i][e] = mult * (s * cc * d[i][e] - k * v[i][e]) + (addend ? a[e] : 0.0f);
+        }
+        if (valid) store8(dx + row * n + c, v[i]);
+    }
+}
+
+// ---- the gated norm's 128-wide head rows: 16 lanes a row, each lane-group R rows with every load of its
+// rows issued before the first reduction.
+template <int R>
+__global__ void __launch_bounds__(256) gated_fwd128(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ z,
+                                                    const float* __restrict__ w, __nv_bfloat16* __restrict__ o,
+                                                    int64_t rows, float eps, int sig, int64_t zts, int zh) {
+    const int lane = threadIdx.x & 15;
+    const int64_t grp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+    float g[8];
+    loadw8(w + lane * 8, g);
+    float xv[R][8], zv[R][8];
+    int64_t rr[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t row = grp * R + r;
+        rr[r] = row < rows ? row : rows - 1;
+        load8(x + rr[r] * 128 + lane * 8, xv[r]);
+        load8(z + zrow(rr[r], 128, zts, zh) + lane * 8, zv[r]);
+    }
+    float ss[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        ss[r] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss[r] = fmaf(xv[r][e], xv[r][e], ss[r]);
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1)
+#pragma unroll
+        for (int r = 0; r < R; ++r) ss[r] += __shfl_xor_sync(0xFFFFFFFFu, ss[r], off);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const float s = rsqrtf(ss[r] / 128.0f + eps);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float sg = sigmoidf_(zv[r][e]);
+            xv[r][e] = xv[r][e] * s * g[e] * (sig ? sg : zv[r][e] * sg);
+        }
+        if (grp * R + r < rows) store8(o + rr[r] * 128 + lane * 8, xv[r]);
+    }
+}
+
+template <int R>
+__global__ void __launch_bounds__(256) gated_bwd128(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ z,
+                                                    const float* __restrict__ w, const __nv_bfloat16* __restrict__ dout,
+                                                    __nv_bfloat16* __restrict__ dx, __nv_bfloat16* __restrict__ dz,
+                                                    int64_t rows, float eps, int sig, int64_t zts, int zh) {
+    const int lane = threadIdx.x & 15;
+    const int64_t grp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+    float g[8];
+    loadw8(w + lane * 8, g);
+    float xv[R][8], zv[R][8], dv[R][8];
+    int64_t rr[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t row = grp * R + r;
+        rr[r] = row < rows ? row : rows - 1;
+        load8(x + rr[r] * 128 + lane * 8, xv[r]);
+        load8(z + zrow(rr[r], 128, zts, zh) + lane * 8, zv[r]);
+        load8(dout + rr[r] * 128 + lane * 8, dv[r]);
+    }
+    float ss[R], a[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        ss[r] = 0.0f;
+        a[r] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float sg = sigmoidf_(zv[r][e]);
+            const float gate = sig ? sg : zv[r][e] * sg;
+            ss[r] = fmaf(xv[r][e], xv[r][e], ss[r]);
+            a[r] = fmaf(xv[r][e] * dv[r][e], g[e] * gate, a[r]);
+        }
+    }
+#pragma unroll
+    for (int off = 8; off > 0; off >>= 1)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            ss[r] += __shfl_xor_sync(0xFFFFFFFFu, ss[r], off);
+            a[r] += __shfl_xor_sync(0xFFFFFFFFu, a[r], off);
+        }
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const float s = rsqrtf(ss[r] / 128.0f + eps);
+        const float k = s * s * s * a[r] / 128.0f;
+        float ox[8], oz[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const float sg = sigmoidf_(zv[r][e]);
+            const float gate = sig ? sg : zv[r][e] * sg;
+            const float dgate = sig ? sg * (1.0f - sg) : sg * (1.0f + zv[r][e] * (1.0f - sg));
+            ox[e] = g[e] * gate * s * dv[r][e] - xv[r][e] * k;
+            oz[e] = dv[r][e] * xv[r][e] * s * g[e] * dgate;
+        }
+        if (grp * R + r < rows) {
+            store8(dx + rr[r] * 128 + lane * 8, ox);
+            store8(dz + zrow(rr[r], 128, zts, zh) + lane * 8, oz);
+        }
+    }
+}
+
+constexpr int kGatedFwdRows = 4;
+constexpr int kGatedBwdRows = 2;
+
 int group_width(int n) {
     // lanes per row: a full warp once the row has 256+ elements, else one 8-vector per lane
     int w = n / 8;
@@ -248,6 +451,17 @@ extern "C" int r97b_rmsnorm_fwd(const uint16_t* x, const float* w, uint16_t* y, 
                                 float eps, float wadd, float mult, void* stream) {
     if (!x || !y || rows <= 0 || n <= 0 || n % 8 || !aligned16(x) || !aligned16(y) || (w && !aligned16(w)))
         return R97B_EINVAL;
+    if (n == 1024 || n == 2048 || n == 4096 || n == 8192) {
+        const unsigned blocks = (unsigned)((rows + 1) / 2);
+        auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+        auto yb = reinterpret_cast<__nv_bfloat16*>(y);
+        cudaStream_t st = as_stream(stream);
+        if (n == 1024) rmsnorm_fwd_row<1><<<blocks, 256, 0, st>>>(xb, w, yb, rstd, rows, eps, wadd, mult);
+        else if (n == 2048) rmsnorm_fwd_row<2><<<blocks, 256, 0, st>>>(xb, w, yb, rstd, rows, eps, wadd, mult);
+        else if (n == 4096) rmsnorm_fwd_row<4><<<blocks, 256, 0, st>>>(xb, w, yb, rstd, rows, eps, wadd, mult);
+        else rmsnorm_fwd_row<8><<<blocks, 256, 0, st>>>(xb, w, yb, rstd, rows, eps, wadd, mult);
+        return launch_status();
+    }
     const int W = group_width((int)n);
     const int64_t threads = rows * (W ? W : 1);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
@@ -262,6 +476,19 @@ extern "C" int r97b_rmsnorm_bwd(const uint16_t* x, const float* w, const uint16_
     if (!x || !dy || !dx || rows <= 0 || n <= 0 || n % 8 || !aligned16(x) || !aligned16(dy) || !aligned16(dx) ||
         (w && !aligned16(w)) || (addend && !aligned16(addend)))
         return R97B_EINVAL;
+    if (n == 1024 || n == 2048 || n == 4096 || n == 8192) {
+        const unsigned blocks = (unsigned)((rows + 1) / 2);
+        auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+        auto db = reinterpret_cast<const __nv_bfloat16*>(dy);
+        auto ab = reinterpret_cast<const __nv_bfloat16*>(addend);
+        auto ob = reinterpret_cast<__nv_bfloat16*>(dx);
+        cudaStream_t st = as_stream(stream);
+        if (n == 1024) rmsnorm_bwd_row<1><<<blocks, 256, 0, st>>>(xb, w, db, ab, ob, rows, eps, wadd, mult);
+        else if (n == 2048) rmsnorm_bwd_row<2><<<blocks, 256, 0, st>>>(xb, w, db, ab, ob, rows, eps, wadd, mult);
+        else if (n == 4096) rmsnorm_bwd_row<4><<<blocks, 256, 0, st>>>(xb, w, db, ab, ob, rows, eps, wadd, mult);
+        else rmsnorm_bwd_row<8><<<blocks, 256, 0, st>>>(xb, w, db, ab, ob, rows, eps, wadd, mult);
+        return launch_status();
+    }
     const int W = group_width((int)n);
     const int64_t threads = rows * (W ? W : 1);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
@@ -279,6 +506,13 @@ extern "C" int r97b_gated_rmsnorm_fwd(const uint16_t* x, const uint16_t* z, int6
     if (!x || !z || !w || !o || rows <= 0 || n <= 0 || n % 8 || !aligned16(x) || !aligned16(z) || !aligned16(w) ||
         !aligned16(o))
         return R97B_EINVAL;
+    if (n == 128) {
+        const int64_t groups = (rows + kGatedFwdRows - 1) / kGatedFwdRows;
+        gated_fwd128<kGatedFwdRows><<<(unsigned)((groups * 16 + 255) / 256), 256, 0, as_stream(stream)>>>(
+            reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(z), w,
+            reinterpret_cast<__nv_bfloat16*>(o), rows, eps, act_sigmoid, z_tok_stride, z_heads);
+        return launch_status();
+    }
     const int W = group_width((int)n);
     const int64_t threads = rows * (W ? W : 1);
     const unsigned blocks = (unsigned)((threads + 255) / 256);
@@ -296,6 +530,14 @@ extern "C" int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, int6
     if (!x || !z || !w || !dout || !dx || !dz || rows <= 0 || n <= 0 || n % 8 || !aligned16(x) || !aligned16(z) ||
         !aligned16(w) || !aligned16(dout) || !aligned16(dx) || !aligned16(dz))
         return R97B_EINVAL;
+    if (n == 128) {
+        const int64_t groups = (rows + kGatedBwdRows - 1) / kGatedBwdRows;
+        gated_bwd128<kGatedBwdRows><<<(unsigned)((groups * 16 + 255) / 256), 256, 0, as_stream(stream)>>>(
+            reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(z), w,
+            reinterpret_cast<const __nv_bfloat16*>(dout), reinterpret_cast<__nv_bfloat16*>(dx),
+            reinterpret_cast<__nv_bfloat16*>(dz), rows, eps, act_sigmoid, z_tok_stride, z_heads);
+        return launch_status();
+    }
     const int W = group_width((int)n);
     const int64_t threads = rows * (W ? W : 1);
     const unsigned blocks = (unsigned)((threads + 255) / 256);

@@ -212,6 +212,7 @@ class Adapter:
                 self.a_bf[(li, g.name)] = torch.empty((g.r_all * r, g.k), dtype=torch.bfloat16, device=device)
                 self.b_blk[(li, g.name)] = torch.zeros((g.n, g.r_all * r), dtype=torch.bfloat16, device=device)
         self.model = model
+        self._casts = None
         self.refresh_mirrors()
 
     def a_view(self, buf, g):
@@ -222,16 +223,31 @@ class Adapter:
         r, n = self.cfg.rank, g.projs[i][1]
         return buf[g.b_offs[i]:g.b_offs[i] + n * r].view(n, r)
 
-    def refresh_mirrors(self, stream=None):
+    def _mirror_pairs(self):
         r = self.cfg.rank
+        pairs = []
         for li, blk in enumerate(self.model.blocks):
             for g in blk["groups"]:
-                ops.cast_f32_bf16(self.a_view(self.w, g), self.a_bf[(li, g.name)], stream=stream)
+                pairs.append((self.a_view(self.w, g), self.a_bf[(li, g.name)]))
                 row = 0
                 for i, (_, n) in enumerate(g.projs):
-                    dst = self.b_blk[(li, g.name)][row:row + n, i * r:(i + 1) * r]
-                    ops.cast_f32_bf16(self.b_view(self.w, g, i), dst, stream=stream)
+                    pairs.append((self.b_view(self.w, g, i), self.b_blk[(li, g.name)][row:row + n, i * r:(i + 1) * r]))
                     row += n
+        return pairs
+
+    def refresh_mirrors(self, stream=None):
+        """The bf16 mirrors from the f32 master weights: every A_all and B_i block in one launch."""
+        if self._casts is None:
+            pairs = self._mirror_pairs()
+            try:
+                self._casts = ops.CastTable(pairs, self.device)
+            except ops.R97bError:  # a rank that is not a multiple of 8: one cast per block
+                self._casts = pairs
+        if isinstance(self._casts, ops.CastTable):
+            self._casts.run(stream)
+        else:
+            for src, dst in self._casts:
+                ops.cast_f32_bf16(src, dst, stream=stream)
 
     def advance_schedule(self, lr=None, beta1=0.9, beta2=0.999, stream=None):
         """Counts one more step and writes its lr and bias corrections bc1 = 1 - beta1^t, bc2 = 1 - beta2^t

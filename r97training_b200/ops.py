@@ -10,7 +10,7 @@ import ctypes
 
 import torch
 
-from ._lib import R97bAttnBwd, R97bGemm, R97bMat, R97bError, check, lib
+from ._lib import R97bAttnBwd, R97bCastSeg, R97bGemm, R97bMat, R97bError, check, lib
 
 EPI_STORE_BF16, EPI_STORE_F32, EPI_ATOMIC_F32, EPI_ATOMIC_F32T, EPI_SPLIT_BF16 = 0, 1, 2, 3, 4
 
@@ -350,6 +350,30 @@ def embed(table, ids, out, stream=None):
     T, n = out.shape
     check(lib().r97b_embed(_ptr(table), table.stride(0), table.shape[0], _ptr(ids), T, n, _ptr(out),
                            _stream(stream)), "r97b_embed")
+
+
+class CastTable:
+    """A fixed list of f32 -> bf16 casts (2-D views, columns a multiple of 8, rows 16-byte aligned) run as one
+    launch (r97b_cast_segments); the table lives in device memory, built once."""
+
+    def __init__(self, pairs, device):
+        segs = (R97bCastSeg * len(pairs))()
+        units = 0
+        for i, (src, dst) in enumerate(pairs):
+            rows, cols = src.shape
+            if tuple(dst.shape) != (rows, cols) or cols % 8 or src.stride(1) != 1 or dst.stride(1) != 1:
+                raise R97bError("CastTable: views must be row-major with a multiple of 8 columns")
+            if src.data_ptr() % 16 or dst.data_ptr() % 16 or src.stride(0) % 4 or dst.stride(0) % 8:
+                raise R97bError("CastTable: rows must start 16-byte aligned")
+            segs[i] = R97bCastSeg(src.data_ptr(), src.stride(0), dst.data_ptr(), dst.stride(0), rows, cols, units)
+            units += rows * cols // 8
+        raw = bytes(segs)
+        self.table = torch.frombuffer(bytearray(raw), dtype=torch.uint8).to(device)
+        self.n, self.units = len(pairs), units
+        self.keep = pairs
+
+    def run(self, stream=None):
+        check(lib().r97b_cast_segments(_ptr(self.table), self.n, self.units, _stream(stream)), "r97b_cast_segments")
 
 
 def cast_f32_bf16(src, dst, stream=None):

@@ -182,7 +182,7 @@ def test_gemm_ragged_edges(cuda):
 
 # ----------------------------------------------------------------------------- norms
 
-@pytest.mark.parametrize("n", [128, 1024, 4096])
+@pytest.mark.parametrize("n", [128, 1024, 2048, 4096, 8192, 1280])
 def test_rmsnorm(cuda, n):
     rs = np.random.RandomState(n)
     rows = 301
@@ -302,3 +302,21 @@ def test_gated_rmsnorm_strided_z(cuda):
     got = to_np(dwide)
     assert_close_bf16(got[:, pad:pad + H * n].reshape(T * H, n), rdz, rel=5e-3, what="dz")
     assert not got[:, :pad].any() and not got[:, pad + H * n:].any()
+
+
+def test_cast_segments_table(cuda):
+    """r97b_cast_segments: many f32 -> bf16 casts of 2-D views (strided rows, column blocks of a wider
+    destination) in one launch, equal to torch's round-to-nearest-even cast."""
+    rs = np.random.RandomState(3)
+    flat = torch.from_numpy(rs.normal(size=100000).astype(np.float32)).to(cuda)
+    wide = torch.zeros((96, 64), dtype=torch.bfloat16, device=cuda)
+    a_dst = torch.empty((16, 256), dtype=torch.bfloat16, device=cuda)
+    pairs = [(flat[:4096].view(16, 256), a_dst),
+             (flat[4096:4096 + 48 * 32].view(48, 32), wide[:48, :32]),
+             (flat[8192:8192 + 48 * 32].view(48, 32), wide[48:, 32:])]
+    table = ops.CastTable(pairs, cuda)
+    table.run()
+    torch.cuda.synchronize()
+    for src, dst in pairs:
+        assert torch.equal(dst, src.to(torch.bfloat16))
+    assert int(wide[:48, 32:].float().abs().sum()) == 0 and int(wide[48:, :32].float().abs().sum()) == 0
