@@ -101,6 +101,14 @@ enum {
                                * split `splits` ways: each split stores its f32 partial tile in `ws`, and
                                * the last split of a tile to finish sums the partials in split order
                                * (deterministic) and stores the result */
+    R97B_EPI_SWIGLU = 5,      /* the gate/up projection with its SwiGLU: B1 (and B2) hold the gate rows
+                               * [0, F) and the up rows [F, 2F), N = 2F, F a multiple of 128; out = [g | u]
+                               * (bf16, ldo) and out2[m, j] = bf16(silu(g[m, j]) u[m, j]) (ldo2). Each
+                               * 256-column tile of the CTA pair computes gate columns [128 t, 128 t + 128)
+                               * and the matching up columns together. */
+    R97B_EPI_SWIGLU_BWD = 6,  /* the down projection's input adjoint with SwiGLU's: acc = da [M, F];
+                               * addend = [g | u] [M, 2F] (ld_add); out[m, j] = bf16(d u silu'(g)),
+                               * out[m, F + j] = bf16(d silu(g)), d = bf16(alpha acc), F = N */
 };
 
 /* D[M, N] = alpha * (A1[M, K1] B1[N, K1]^T + A2[M, K2] B2[N, K2]^T) (+ beta * addend), on tcgen05 tensor
@@ -129,6 +137,8 @@ typedef struct R97bGemm {
     int32_t _pad;
     void* ws;          /* R97B_EPI_SPLIT_BF16 with splits > 1: the split-K workspace */
     int64_t ws_bytes;
+    void* out2;        /* R97B_EPI_SWIGLU: the SwiGLU output */
+    int64_t ldo2;
 } R97bGemm;
 
 int r97b_gemm(const R97bGemm* g, void* stream);

@@ -31,7 +31,8 @@ class R97bGemm(ctypes.Structure):
                 ("a1", R97bMat), ("b1", R97bMat), ("a2", R97bMat), ("b2", R97bMat),
                 ("mode", c_i32), ("splits", c_i32), ("alpha", c_f32), ("beta", c_f32),
                 ("out", c_vp), ("ldo", c_i64), ("addend", c_vp), ("ld_add", c_i64),
-                ("bn", c_i32), ("_pad", c_i32), ("ws", c_vp), ("ws_bytes", c_i64)]
+                ("bn", c_i32), ("_pad", c_i32), ("ws", c_vp), ("ws_bytes", c_i64),
+                ("out2", c_vp), ("ldo2", c_i64)]
 
 
 class R97bAttnBwd(ctypes.Structure):

@@ -45,7 +45,50 @@ struct KernelArgs {
     int64_t ld_add;
     float* ws_part;  // kEpiSplitBf16: f32 partial tiles [splits][tiles][kBM][BN]
     int* ws_cnt;     // kEpiSplitBf16: per-tile count of finished splits (back to 0 after the tile's fix-up)
+    __nv_bfloat16* out2;  // kEpiSwiglu: silu(g) u
+    int64_t ldo2;
+    int32_t half_n;       // kEpiSwiglu / kEpiSwigluBwd: F, the offset of the up columns
 };
+
+// SwiGLU's pieces, with the arithmetic of the standalone SwiGLU kernels (layers.cu), so the fused
+// epilogues produce the same bits.
+__device__ __forceinline__ float sw_sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float sw_silu(float x) { return x * sw_sigm(x); }
+__device__ __forceinline__ float sw_silu_grad(float x) {
+    const float s = sw_sigm(x);
+    return s * (1.0f + x * (1.0f - s));
+}
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void load32_bf16(const __nv_bfloat16* p, float (&v)[32]) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+        const uint4 q = reinterpret_cast<const uint4*>(p)[w];
+        const uint32_t xs[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[h]));
+            v[w * 8 + 2 * h] = f.x;
+            v[w * 8 + 2 * h + 1] = f.y;
+        }
+    }
+}
+
+__device__ __forceinline__ void store32_bf16(__nv_bfloat16* p, const float (&v)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 8) {
+        uint4 pk;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[i], v[i + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[i + 2], v[i + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[i + 4], v[i + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[i + 6], v[i + 7]);
+        pk.x = *reinterpret_cast<uint32_t*>(&h0);
+        pk.y = *reinterpret_cast<uint32_t*>(&h1);
+        pk.z = *reinterpret_cast<uint32_t*>(&h2);
+        pk.w = *reinterpret_cast<uint32_t*>(&h3);
+        *reinterpret_cast<uint4*>(p + i) = pk;
+    }
+}
 
 // The 128 epilogue threads (warps 4-7) synchronise among themselves on named barrier 1.
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -83,6 +126,29 @@ __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, 
     tn = r / gm;
 }
 
+// v[i] += beta * addend[m, n0 + i]: four 16-byte loads when the 32 columns are in range and aligned.
+__device__ __forceinline__ void add_addend32(const KernelArgs& args, int m, int n0, bool full, float (&v)[32]) {
+    const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
+    if (full && (reinterpret_cast<uintptr_t>(ap) & 15) == 0) {
+        uint4 q[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) q[w] = reinterpret_cast<const uint4*>(ap)[w];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+            const uint32_t xs[4] = {q[w].x, q[w].y, q[w].z, q[w].w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&xs[h]));
+                v[w * 8 + 2 * h] += args.beta * f.x;
+                v[w * 8 + 2 * h + 1] += args.beta * f.y;
+            }
+        }
+    } else {
+        for (int i = 0; i < 32; ++i)
+            if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
+    }
+}
+
 // The epilogue of 32 accumulator columns [n0, n0 + 32) of row m (r = the raw f32 bits), per `mode`.
 __device__ __forceinline__ void epilogue32(const KernelArgs& args, int mode, int m, int n0, const uint32_t (&r)[32]) {
     const bool full = n0 + 32 <= args.N;
@@ -90,12 +156,7 @@ __device__ __forceinline__ void epilogue32(const KernelArgs& args, int mode, int
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
     if (mode == kEpiStoreBf16) {
-        if (args.addend) {
-            const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
-#pragma unroll
-            for (int i = 0; i < 32; ++i)
-                if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
-        }
+        if (args.addend) add_addend32(args, m, n0, full, v);
         __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)m * args.ldo + n0;
         if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
 #pragma unroll
@@ -117,11 +178,7 @@ __device__ __forceinline__ void epilogue32(const KernelArgs& args, int mode, int
         }
     } else if (mode == kEpiStoreF32) {
         float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
-        if (args.addend) {
-            const __nv_bfloat16* ap = args.addend + (int64_t)m * args.ld_add + n0;
-            for (int i = 0; i < 32; ++i)
-                if (full || n0 + i < args.N) v[i] += args.beta * __bfloat162float(ap[i]);
-        }
+        if (args.addend) add_addend32(args, m, n0, full, v);
         if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
 #pragma unroll
             for (int i = 0; i < 32; i += 4)
@@ -129,6 +186,33 @@ __device__ __forceinline__ void epilogue32(const KernelArgs& args, int mode, int
         } else {
             for (int i = 0; i < 32; ++i)
                 if (n0 + i < args.N) op[i] = v[i];
+        }
+    } else if (mode == kEpiSwigluBwd) {
+        // d = the rounded da; dg = d u silu'(g), du = d silu(g)
+        const __nv_bfloat16* gp = args.addend + (int64_t)m * args.ld_add + n0;
+        __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)m * args.ldo + n0;
+        if (full && ((reinterpret_cast<uintptr_t>(gp) | reinterpret_cast<uintptr_t>(op)) & 15) == 0) {
+            float g[32], u[32], og[32];
+            load32_bf16(gp, g);
+            load32_bf16(gp + args.half_n, u);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const float d = bf16_round(v[i]);
+                og[i] = d * u[i] * sw_silu_grad(g[i]);
+                v[i] = d * sw_silu(g[i]);
+            }
+            store32_bf16(op, og);
+            store32_bf16(op + args.half_n, v);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                if (n0 + i < args.N) {
+                    const float d = bf16_round(v[i]);
+                    const float g = __bfloat162float(gp[i]), u = __bfloat162float(gp[args.half_n + i]);
+                    op[i] = __float2bfloat16_rn(d * u * sw_silu_grad(g));
+                    op[args.half_n + i] = __float2bfloat16_rn(d * sw_silu(g));
+                }
+            }
         }
     } else if (mode == kEpiAtomicF32) {
         float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
@@ -474,7 +558,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const CUtensorMap* ma = seg2 ? &tA2 : &tA1;
                 const CUtensorMap* mb = seg2 ? &tB2 : &tB1;
                 const int k = (seg2 ? kb - args.k1_blocks : kb) * kBK;
-                const int m0 = tm * 256 + 128 * (int)rank, n0 = tn * 256 + 128 * (int)rank;
+                const int m0 = tm * 256 + 128 * (int)rank;
+                // SwiGLU: rank 0 brings the tile's gate rows and rank 1 the matching up rows, so the pair's
+                // 256 accumulator columns are [g | u] of the same 128 output columns
+                const int n0 = args.mode == kEpiSwiglu ? (rank ? args.half_n : 0) + tn * 128
+                                                       : tn * 256 + 128 * (int)rank;
                 if (A_MN) {
                     tma_load_2d_pair(sa, ma, bar, m0, k);
                     tma_load_2d_pair(sa + 8192, ma, bar, m0 + 64, k);
@@ -547,15 +635,39 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             tc_fence_after();
             const int m = tm * 256 + 128 * (int)rank + q * 32 + lane;
             const bool mrow = m < args.M;
+            if (args.mode == kEpiSwiglu) {
 #pragma unroll 1
-            for (int c = 0; c < 256 / 32; ++c) {
-                uint32_t r[32];
-                __syncwarp();
-                tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256 + c * 32), r);
-                tmem_ld_wait();
-                const int n0 = tn * 256 + c * 32;
-                if (!mrow || n0 >= args.N) continue;
-                epilogue32(args, args.mode, m, n0, r);
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t rg[32], ru[32];
+                    __syncwarp();
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256 + c * 32), rg);
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256 + 128 + c * 32), ru);
+                    tmem_ld_wait();
+                    if (!mrow) continue;
+                    const int j0 = tn * 128 + c * 32;
+                    float g[32], u[32], a[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        g[i] = bf16_round(__uint_as_float(rg[i]) * args.alpha);
+                        u[i] = bf16_round(__uint_as_float(ru[i]) * args.alpha);
+                        a[i] = sw_silu(g[i]) * u[i];
+                    }
+                    __nv_bfloat16* op = reinterpret_cast<__nv_bfloat16*>(args.out) + (int64_t)m * args.ldo + j0;
+                    store32_bf16(op, g);
+                    store32_bf16(op + args.half_n, u);
+                    store32_bf16(args.out2 + (int64_t)m * args.ldo2 + j0, a);
+                }
+            } else {
+#pragma unroll 1
+                for (int c = 0; c < 256 / 32; ++c) {
+                    uint32_t r[32];
+                    __syncwarp();
+                    tmem_ld32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * 256 + c * 32), r);
+                    tmem_ld_wait();
+                    const int n0 = tn * 256 + c * 32;
+                    if (!mrow || n0 >= args.N) continue;
+                    epilogue32(args, args.mode, m, n0, r);
+                }
             }
             tc_fence_before();
             mbar_arrive_cluster(cluster_addr(&tempty_bar[acc], 0));
@@ -697,6 +809,7 @@ int launch(const R97bGemm& g, cudaStream_t stream) {
     k.ldo = g.ldo;
     k.addend = reinterpret_cast<const __nv_bfloat16*>(g.addend);
     k.ld_add = g.ld_add;
+    k.half_n = (int32_t)g.N;
     const int units = k.tiles_m * k.tiles_n * k.splits;
     int grid = num_sms();
     if (units < grid) grid = units;
@@ -741,6 +854,9 @@ int launch_pair(const R97bGemm& g, cudaStream_t stream) {
     k.ldo = g.ldo;
     k.addend = reinterpret_cast<const __nv_bfloat16*>(g.addend);
     k.ld_add = g.ld_add;
+    k.out2 = reinterpret_cast<__nv_bfloat16*>(g.out2);
+    k.ldo2 = g.ldo2;
+    k.half_n = (int32_t)(g.mode == kEpiSwiglu ? g.N / 2 : g.N);
     const int units = k.tiles_m * k.tiles_n * k.splits;
     int pairs = num_sms() / 2;
     if (units < pairs) pairs = units;
@@ -768,7 +884,7 @@ int dispatch_major(const R97bGemm& g, cudaStream_t s) {
 R97B_ERROR_READER(gemm_error_word)
 
 int64_t gemm_workspace_bytes(const R97bGemm& g) {
-    if (g.M <= 0 || g.N <= 0 || g.K1 <= 0 || g.mode < kEpiStoreBf16 || g.mode > kEpiSplitBf16) return -1;
+    if (g.M <= 0 || g.N <= 0 || g.K1 <= 0 || g.mode < kEpiStoreBf16 || g.mode > kEpiSwigluBwd) return -1;
     const int bn = pick_bn(g);
     if (bn != 64 && bn != 128 && bn != 256 && bn != 512) return -1;
     return split_ws_bytes(g, nullptr);
@@ -778,8 +894,20 @@ int gemm_run(const R97bGemm& g, cudaStream_t stream) {
     if (g.M <= 0 || g.N <= 0 || g.K1 <= 0 || !g.out || !g.a1.ptr || !g.b1.ptr) return R97B_EINVAL;
     if (g.K2 > 0 && (!g.a2.ptr || !g.b2.ptr || g.a2.mn_major != g.a1.mn_major || g.b2.mn_major != g.b1.mn_major))
         return R97B_EINVAL;
-    if (g.mode < kEpiStoreBf16 || g.mode > kEpiSplitBf16) return R97B_EINVAL;
+    if (g.mode < kEpiStoreBf16 || g.mode > kEpiSwigluBwd) return R97B_EINVAL;
     if (g.M > 0x7FFFFFFF || g.N > 0x7FFFFFFF) return R97B_EINVAL;
+    if (g.mode == kEpiSwiglu) {  // the CTA pair only: its two halves of B are the gate and the up rows
+        const int64_t F = g.N / 2;
+        if (g.N % 256 != 0 || !g.out2 || g.ldo % 8 || g.ldo2 % 8 || g.ldo < g.N || g.ldo2 < F || g.addend ||
+            g.splits > 1 || (reinterpret_cast<uintptr_t>(g.out) & 15) || (reinterpret_cast<uintptr_t>(g.out2) & 15))
+            return R97B_EINVAL;
+        const int a = g.a1.mn_major ? 1 : 0, b = g.b1.mn_major ? 1 : 0;
+        if (a == 0 && b == 0) return launch_pair<0, 0>(g, stream);
+        if (a == 0 && b == 1) return launch_pair<0, 1>(g, stream);
+        if (a == 1 && b == 0) return launch_pair<1, 0>(g, stream);
+        return launch_pair<1, 1>(g, stream);
+    }
+    if (g.mode == kEpiSwigluBwd && (!g.addend || g.ld_add < 2 * g.N || g.splits > 1)) return R97B_EINVAL;
     const int bn = pick_bn(g);
     if (bn == 512) {  // the CTA-pair kernel: 256 x 256 tiles over two SMs
         const int a = g.a1.mn_major ? 1 : 0, b = g.b1.mn_major ? 1 : 0;

@@ -14,6 +14,8 @@ constexpr int kEpiStoreF32 = R97B_EPI_STORE_F32;
 constexpr int kEpiAtomicF32 = R97B_EPI_ATOMIC_F32;
 constexpr int kEpiAtomicF32T = R97B_EPI_ATOMIC_F32T;
 constexpr int kEpiSplitBf16 = R97B_EPI_SPLIT_BF16;
+constexpr int kEpiSwiglu = R97B_EPI_SWIGLU;
+constexpr int kEpiSwigluBwd = R97B_EPI_SWIGLU_BWD;
 
 int gemm_run(const R97bGemm& g, cudaStream_t stream);
 // A row-major bf16 matrix [outer, inner] (row stride `ld` elements) as a 2D TMA tensor map with a

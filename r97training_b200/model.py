@@ -349,12 +349,17 @@ class TrainStep:
         return self.w_keep[(li, g.name)][:g.n * g.k].view(g.n, g.k)
 
     # ------------------------------------------------------------------ fused LoRA linear
-    def _lin_fwd(self, li, g: Group, x: torch.Tensor, W: torch.Tensor, out: torch.Tensor, addend=None):
-        """t = s x A_all^T ; out = x W^T + t B_blk^T (+ addend). Returns t (saved for dB)."""
+    def _lin_fwd(self, li, g: Group, x: torch.Tensor, W: torch.Tensor, out: torch.Tensor, addend=None,
+                 swiglu_out=None):
+        """t = s x A_all^T ; out = x W^T + t B_blk^T (+ addend). Returns t (saved for dB). With `swiglu_out`
+        (the gate/up group) the GEMM's epilogue also writes silu(g) u there."""
         cfg, ad = self.cfg, self.adapter
         t = torch.empty((x.shape[0], g.r_all * cfg.rank), dtype=torch.bfloat16, device=x.device)
         self._skinny(x, ad.a_bf[(li, g.name)], t, g.k, False)
-        ops.gemm(x, W, out, a2=t, b2=ad.b_blk[(li, g.name)], addend=addend, beta=1.0)
+        if swiglu_out is not None:
+            ops.gemm(x, W, out, a2=t, b2=ad.b_blk[(li, g.name)], mode=ops.EPI_SWIGLU, out2=swiglu_out)
+        else:
+            ops.gemm(x, W, out, a2=t, b2=ad.b_blk[(li, g.name)], addend=addend, beta=1.0)
         return t
 
     def _skinny(self, a, b, out, K, b_mn):
@@ -366,13 +371,18 @@ class TrainStep:
                  mode=ops.EPI_SPLIT_BF16 if splits > 1 else ops.EPI_STORE_BF16, ws=self.split_ws.buf)
 
     def _lin_bwd(self, li, g: Group, x: torch.Tensor, t: torch.Tensor, W: torch.Tensor, dy: torch.Tensor,
-                 dx_out: torch.Tensor):
-        """dt = s dY B_blk ; dX = dY W + dt A_all ; dA_all += dt^T x ; dB_i += dY_i^T t_i."""
+                 dx_out: torch.Tensor, swiglu_gu=None):
+        """dt = s dY B_blk ; dX = dY W + dt A_all ; dA_all += dt^T x ; dB_i += dY_i^T t_i. With `swiglu_gu`
+        (the down group, whose input is silu(g) u) dx_out receives SwiGLU's adjoint [dg | du] instead."""
         cfg, ad = self.cfg, self.adapter
         r = cfg.rank
         dt = torch.empty((dy.shape[0], g.r_all * r), dtype=torch.bfloat16, device=dy.device)
         self._skinny(dy, ad.b_blk[(li, g.name)], dt, g.n, True)
-        ops.gemm(dy, W, dx_out, b_mn=True, a2=dt, b2=ad.a_bf[(li, g.name)], N=g.k)
+        if swiglu_gu is not None:
+            ops.gemm(dy, W, dx_out, b_mn=True, a2=dt, b2=ad.a_bf[(li, g.name)], N=g.k, mode=ops.EPI_SWIGLU_BWD,
+                     addend=swiglu_gu)
+        else:
+            ops.gemm(dy, W, dx_out, b_mn=True, a2=dt, b2=ad.a_bf[(li, g.name)], N=g.k)
         bn, splits = ops.grad_tiling(g.k, g.r_all * r)
         ops.gemm(x, dt, ad.a_view(ad.g, g), a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32T, splits=splits,
                  bn=bn, M=g.k, N=g.r_all * r)
@@ -501,9 +511,8 @@ class TrainStep:
         n2 = ops.rmsnorm_fwd(h1, blk["w_post"], eps=cfg.eps)
         W = self._w_fwd(li, g_gu)
         y_gu = torch.empty((T, 2 * cfg.ffn), dtype=torch.bfloat16, device=h1.device)
-        t_gu = self._lin_fwd(li, g_gu, n2, W, y_gu)
         a = torch.empty((T, cfg.ffn), dtype=torch.bfloat16, device=h1.device)
-        ops.swiglu_fwd(y_gu, a)
+        t_gu = self._lin_fwd(li, g_gu, n2, W, y_gu, swiglu_out=a)  # SwiGLU in the GEMM's epilogue
         W = self._w_fwd(li, g_d)
         xn = torch.empty_like(h1)
         t_d = self._lin_fwd(li, g_d, a, W, xn, addend=h1)
@@ -514,10 +523,8 @@ class TrainStep:
         cfg, T = self.cfg, self.T
         g_gu, g_d = blk["groups"][2], blk["groups"][3]
         W = self._w_bwd(li, g_d)
-        da = torch.empty((T, cfg.ffn), dtype=torch.bfloat16, device=h1.device)
-        self._lin_bwd(li, g_d, sv["a"], sv["t_d"], W, dxn, da)
         dgu = torch.empty_like(sv["y_gu"])
-        ops.swiglu_bwd(sv["y_gu"], da, dgu)
+        self._lin_bwd(li, g_d, sv["a"], sv["t_d"], W, dxn, dgu, swiglu_gu=sv["y_gu"])  # SwiGLU's adjoint fused
         W = self._w_bwd(li, g_gu)
         dn2 = torch.empty_like(h1)
         self._lin_bwd(li, g_gu, sv["n2"], sv["t_gu"], W, dgu, dn2)

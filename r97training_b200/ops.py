@@ -13,6 +13,7 @@ import torch
 from ._lib import R97bAttnBwd, R97bCastSeg, R97bGemm, R97bMat, R97bError, check, lib
 
 EPI_STORE_BF16, EPI_STORE_F32, EPI_ATOMIC_F32, EPI_ATOMIC_F32T, EPI_SPLIT_BF16 = 0, 1, 2, 3, 4
+EPI_SWIGLU, EPI_SWIGLU_BWD = 5, 6
 
 
 def _stream(stream=None) -> int:
@@ -45,12 +46,14 @@ def _mat(t: torch.Tensor, mn_major: bool, rows: int, k: int, name: str) -> R97bM
 
 
 def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STORE_BF16, alpha=1.0,
-         addend=None, beta=1.0, splits=1, bn=0, M=None, N=None, ws=None, stream=None):
+         addend=None, beta=1.0, splits=1, bn=0, M=None, N=None, ws=None, out2=None, stream=None):
     """out (+)= alpha * (A1 B1^T + A2 B2^T) (+ beta * addend); see include/r97b.h (r97b_gemm).
 
     A1 is [M, K1] (K-major) or stored [K1, M] (a_mn); B1 is [N, K1] or stored [K1, N] (b_mn); the optional
     tail (a2, b2) has the same majorness with its own K2. EPI_SPLIT_BF16 with splits > 1 needs `ws`, a
-    zero-initialised device buffer of at least r97b_gemm_workspace_bytes bytes (see SplitWorkspace)."""
+    zero-initialised device buffer of at least r97b_gemm_workspace_bytes bytes (see SplitWorkspace).
+    EPI_SWIGLU writes [g | u] to `out` and silu(g) u to `out2`; EPI_SWIGLU_BWD reads [g | u] as `addend`
+    and writes [dg | du] to `out` (N = the SwiGLU width)."""
     if M is None:
         M = a1.shape[1] if a_mn else a1.shape[0]
     if N is None:
@@ -74,7 +77,12 @@ def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STOR
             if ws is None or ws.numel() * ws.element_size() < need or ws.device != out.device:
                 raise R97bError(f"r97b_gemm: the split GEMM needs a {need}-byte workspace on {out.device}")
             g.ws, g.ws_bytes = ws.data_ptr(), ws.numel() * ws.element_size()
-    if mode in (EPI_STORE_BF16, EPI_SPLIT_BF16):
+    if mode == EPI_SWIGLU:
+        _need(out2, torch.bfloat16, "out2")
+        if out2.dim() != 2 or out2.stride(1) != 1 or tuple(out2.shape) != (M, N // 2):
+            raise R97bError("out2 must be a row-major [M, N / 2] view")
+        g.out2, g.ldo2 = out2.data_ptr(), out2.stride(0)
+    if mode in (EPI_STORE_BF16, EPI_SPLIT_BF16, EPI_SWIGLU, EPI_SWIGLU_BWD):
         _need(out, torch.bfloat16, "out")
     else:
         _need(out, torch.float32, "out")

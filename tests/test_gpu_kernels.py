@@ -320,3 +320,34 @@ def test_cast_segments_table(cuda):
     for src, dst in pairs:
         assert torch.equal(dst, src.to(torch.bfloat16))
     assert int(wide[:48, 32:].float().abs().sum()) == 0 and int(wide[48:, :32].float().abs().sum()) == 0
+
+
+@pytest.mark.parametrize("M,F,K", [(384, 256, 320), (1000, 512, 448)])
+def test_gemm_swiglu_epilogues_match_unfused(cuda, M, F, K):
+    """EPI_SWIGLU (the gate/up GEMM writing [g | u] and silu(g) u) and EPI_SWIGLU_BWD (the down GEMM's input
+    adjoint writing [dg | du]) give the same bits as the plain GEMM followed by the standalone SwiGLU
+    kernels, with the LoRA tail in the forward."""
+    rs = np.random.RandomState(M + F)
+    r = 64
+    X, W, T, Bl = _bf(rs, (M, K)), _bf(rs, (2 * F, K), 0.05), _bf(rs, (M, 2 * r)), _bf(rs, (2 * F, 2 * r), 0.1)
+    X, W, T, Bl = X.to(cuda), W.to(cuda), T.to(cuda), Bl.to(cuda)
+    gu_ref = torch.empty((M, 2 * F), dtype=torch.bfloat16, device=cuda)
+    ops.gemm(X, W, gu_ref, a2=T, b2=Bl, bn=512)
+    a_ref = torch.empty((M, F), dtype=torch.bfloat16, device=cuda)
+    ops.swiglu_fwd(gu_ref, a_ref)
+    gu = torch.empty_like(gu_ref)
+    a = torch.empty_like(a_ref)
+    ops.gemm(X, W, gu, a2=T, b2=Bl, mode=ops.EPI_SWIGLU, out2=a)
+    # the backward: da = dY Wd (Wd [Kd, F] read MN-major), then SwiGLU's adjoint
+    Kd = 256
+    dY, Wd = _bf(rs, (M, Kd)).to(cuda), _bf(rs, (Kd, F), 0.05).to(cuda)
+    da = torch.empty((M, F), dtype=torch.bfloat16, device=cuda)
+    ops.gemm(dY, Wd, da, b_mn=True, N=F)
+    dgu_ref = torch.empty_like(gu_ref)
+    ops.swiglu_bwd(gu_ref, da, dgu_ref)
+    dgu = torch.empty_like(gu_ref)
+    ops.gemm(dY, Wd, dgu, b_mn=True, N=F, mode=ops.EPI_SWIGLU_BWD, addend=gu_ref)
+    torch.cuda.synchronize()
+    assert torch.equal(gu, gu_ref)
+    assert torch.equal(a, a_ref)
+    assert torch.equal(dgu, dgu_ref)
