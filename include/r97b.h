@@ -231,6 +231,9 @@ int r97b_adamw_step_dev(float* w, float* m, float* v, float* g, int64_t n, const
                         float beta2, float eps, float weight_decay, float inv_k, const float* clip_scale,
                         int32_t zero_grad, void* stream);
 
+/* dst += src over n f32 (the optimiser's gradient accumulation; reference src/optim.cpp:231-244). */
+int r97b_add_f32(float* dst, const float* src, int64_t n, void* stream);
+
 /* Bytes of scratch r97b_global_norm needs for n elements (one f64 per 4096). */
 int64_t r97b_global_norm_scratch_bytes(int64_t n);
 
@@ -359,8 +362,9 @@ int r97b_conv_prep_bwd(const uint16_t* x, int64_t ldx, const float* conv_w, cons
                        int32_t dqk_heads, uint16_t* dx, int64_t lddx, void* stream);
 
 /* beta = sigmoid(b), g = within-chunk running sum of -exp(A_log) softplus(a + dt_bias) (threshold 20), from
- * ba rows (bf16, ldba) holding b in columns [0, H) and a in [H, 2H); chunks from r97b_gdn_chunk_table.
- * Replaces: the gate phase of gdn_conv_prep, src/adjoint/host/gdn_prep.cpp:320-336. */
+ * ba rows (bf16, ldba) holding b in columns [0, H) and a in [H, 2H); chunks (at most 64 tokens each) from
+ * r97b_gdn_chunk_table with chunk 64. Replaces: the gate phase of gdn_conv_prep,
+ * src/adjoint/host/gdn_prep.cpp:320-336. */
 int r97b_gates_fwd(const uint16_t* ba, int64_t ldba, const float* a_log, const float* dt_bias,
                    const int32_t* chunk_tok0, const int32_t* chunk_len, int32_t n_chunks, int32_t H, float* g,
                    float* beta, void* stream);

@@ -34,6 +34,36 @@ void r97host_scratch_stats(int64_t* live, int64_t* peak, int64_t* allocations);
 /* Waits for everything the plugin's rows queued. */
 int r97host_sync(void);
 
+/* ---- the reference's Optimiser over device memory (include/r97/optim.h:26-90, src/optim.cpp) ----
+ * AdamW with the reference's schedule (linear warm-up, cosine to lr * lr_floor_frac at total_steps),
+ * global-norm clipping of the accumulated mean, gradient accumulation over accum_steps calls and weight
+ * decay skipped for parameters whose name contains a no_decay substring. The parameters are one flat f32
+ * device buffer `w` holding the named parameters in order (counts[i] elements each); the optimiser keeps
+ * its moments and accumulation buffer on the device. Its updates are bit-identical to the reference
+ * Optimiser's and its serialised state is the reference's "R97OPT" byte format, so either restores the
+ * other's checkpoint. All work is queued on `stream`; serialise and restore synchronise it. */
+typedef struct R97hostAdamW {
+    float lr, beta1, beta2, eps, weight_decay, clip_norm;
+    int32_t warmup_steps, total_steps;
+    float lr_floor_frac;
+    int32_t accum_steps;
+} R97hostAdamW;
+
+/* A new optimiser, or null (message in r97host_optim_error). */
+void* r97host_optim_create(const R97hostAdamW* cfg, int32_t nparams, const char* const* names, const int64_t* counts,
+                           float* w, const char* const* no_decay, int32_t n_no_decay, void* stream);
+/* Adds `grad` (device, the flat layout of w) into the accumulation; every accum_steps-th call applies one
+ * update. 1: updated, 0: accumulated, -1: error. */
+int r97host_optim_step(void* opt, const float* grad);
+int r97host_optim_state(void* opt, int32_t* updates_done, int32_t* pending);
+/* Writes the serialised state to out when cap is large enough; returns its size in bytes (-1 on error). */
+int64_t r97host_optim_serialise(void* opt, uint8_t* out, int64_t cap);
+/* Replaces the state (weights included) from serialised bytes; 0 on success, 1 (state unchanged) on bad
+ * bytes. */
+int r97host_optim_restore(void* opt, const uint8_t* bytes, int64_t size);
+void r97host_optim_destroy(void* opt);
+const char* r97host_optim_error(void);
+
 #ifdef __cplusplus
 }
 #endif

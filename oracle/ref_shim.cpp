@@ -280,6 +280,56 @@ int ref_adamw(float* w, int64_t n, const float* grads, int steps, float lr, floa
     }
 }
 
+// The reference Optimiser over named parameters (initial values `w0`, concatenated), driven by `steps`
+// step() calls with the concatenated gradients in `grads`; writes its serialised state (Optimiser::serialise)
+// into `out` when `cap` allows and returns the byte count (-1 on a throw). The config fields mirror
+// r97::AdamWConfig; `no_decay` is a list of `n_no_decay` name substrings.
+int64_t ref_optim_serialised(int nparams, const char* const* names, const int64_t* counts, const float* w0,
+                             const float* grads, int steps, float lr, float beta1, float beta2, float eps,
+                             float weight_decay, float clip_norm, int warmup, int total, float floor_frac,
+                             int accum, const char* const* no_decay, int n_no_decay, int threads, uint8_t* out,
+                             int64_t cap) {
+    try {
+        g_error.clear();
+        r97::ParamSet params;
+        int64_t total_n = 0;
+        for (int i = 0; i < nparams; ++i) {
+            params.push_back(r97::Param{names[i], {counts[i]}, std::vector<float>(w0 + total_n, w0 + total_n + counts[i])});
+            total_n += counts[i];
+        }
+        r97::AdamWConfig cfg;
+        cfg.lr = lr;
+        cfg.beta1 = beta1;
+        cfg.beta2 = beta2;
+        cfg.eps = eps;
+        cfg.weight_decay = weight_decay;
+        cfg.clip_norm = clip_norm;
+        cfg.warmup_steps = warmup;
+        cfg.total_steps = total;
+        cfg.lr_floor_frac = floor_frac;
+        cfg.accum_steps = accum;
+        cfg.threads = threads;
+        for (int i = 0; i < n_no_decay; ++i) cfg.no_decay.emplace_back(no_decay[i]);
+        r97::Optimiser opt(params, cfg);
+        for (int s = 0; s < steps; ++s) {
+            r97::ParamSet g;
+            int64_t off = 0;
+            for (int i = 0; i < nparams; ++i) {
+                const float* src = grads + (int64_t)s * total_n + off;
+                g.push_back(r97::Param{names[i], {counts[i]}, std::vector<float>(src, src + counts[i])});
+                off += counts[i];
+            }
+            opt.step(g);
+        }
+        const std::vector<uint8_t> b = opt.serialise();
+        if (out && cap >= (int64_t)b.size()) std::memcpy(out, b.data(), b.size());
+        return (int64_t)b.size();
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return -1;
+    }
+}
+
 float ref_scheduled_lr(float lr, int warmup, int total, float floor_frac, int step) {
     r97::AdamWConfig cfg;
     cfg.lr = lr;

@@ -71,6 +71,7 @@ _SIGS = {
     "r97b_gemm_workspace_bytes": (c_i64, [c_vp]),
     "r97b_attn_bwd": (c_i32, [c_vp, c_vp]),
     "r97b_cast_segments": (c_i32, [c_vp, c_i32, c_i64, c_vp]),
+    "r97b_add_f32": (c_i32, [c_vp, c_vp, c_i64, c_vp]),
     "r97b_attn_bwd_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "r97b_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
     "r97b_rmsnorm_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),

@@ -203,3 +203,28 @@ extern "C" int r97b_global_norm(const float* g, int64_t n, float inv_k, float ma
     norm_finish_kernel<<<1, 32, 0, as_stream(stream)>>>(partials, nchunks, max_norm, out_norm, out_scale);
     return launch_status(2);
 }
+
+namespace r97b {
+namespace {
+__global__ void add_f32_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t n) {
+    const int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+    if (i + 4 <= n && ((reinterpret_cast<uintptr_t>(dst + i) | reinterpret_cast<uintptr_t>(src + i)) & 15) == 0) {
+        float4 a = *reinterpret_cast<float4*>(dst + i);
+        const float4 b = *reinterpret_cast<const float4*>(src + i);
+        a.x += b.x, a.y += b.y, a.z += b.z, a.w += b.w;
+        *reinterpret_cast<float4*>(dst + i) = a;
+    } else {
+        for (int64_t j = i; j < n && j < i + 4; ++j) dst[j] += src[j];
+    }
+}
+}  // namespace
+}  // namespace r97b
+
+// dst += src (f32, element-wise): the optimiser's gradient accumulation (reference src/optim.cpp:231-244).
+extern "C" int r97b_add_f32(float* dst, const float* src, int64_t n, void* stream) {
+    if (!dst || !src || n < 0) return R97B_EINVAL;
+    if (n == 0) return R97B_OK;
+    const int64_t threads = (n + 3) / 4;
+    r97b::add_f32_kernel<<<(unsigned)((threads + 255) / 256), 256, 0, r97b::as_stream(stream)>>>(dst, src, n);
+    return r97b::launch_status();
+}

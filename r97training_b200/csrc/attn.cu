@@ -9,13 +9,13 @@
 //   dS = scale P o (dO V^T - Delta),  Delta = rowsum(dO o O)
 //   dK = dS^T Q,   dQ = dS K
 //
-// as five passes of one persistent, warp-specialised kernel template (warp 0 TMA loads into a ring of
+// as passes of one persistent, warp-specialised kernel template (warp 0 TMA loads into a ring of
 // shared-memory stages, warp 1 issues tcgen05.mma into a double-buffered TMEM accumulator, and EPW warps
 // per TMEM lane quarter (warps 4 ...) drain it with tcgen05.ld, each a slice of the columns, and run the
 // pass's epilogue -- 4 per quarter for the exp / product epilogues of the 128 x 128 tiles):
 //
-//   kP    128 x 128 tiles of S = Q K^T (k = head dim), epilogue P = exp2(S scale log2e - lse log2e), bf16
-//   kDS   128 x 128 tiles of dP = dO V^T, epilogue dS = scale P (dP - Delta) with P read back, bf16
+//   kPDS  128 x 128 causal tiles of S = Q K^T and dP = dO V^T (k = head dim) into two accumulators, epilogue
+//         P = exp2(S scale log2e - lse log2e) and dS = scale P (dP - Delta), both stored bf16
 //   kDKV  128 keys x D tiles of dV = P^T dO (or dK = dS^T Q): P / dS and dO / Q read MN-major, the
 //         reduction running over the group's query heads and the query blocks at or after the key block
 //   kDQ   128 queries x D tiles of dQ = dS K: dS K-major, K MN-major, key blocks up to the query block
@@ -37,7 +37,7 @@ constexpr int kBK = 64;
 constexpr int kABytes = kBM * kBK * 2;  // 16 KiB
 constexpr float kLog2e = 1.4426950408889634f;
 
-enum Kind { kP = 0, kDS = 1, kDKV = 2, kDQ = 3 };
+enum Kind { kPDS = 0, kDKV = 1, kDQ = 2 };
 
 struct AttnArgs {
     int32_t B, Hq, Hkv, S, D, grp, nblk;
@@ -45,24 +45,25 @@ struct AttnArgs {
     float scale;
     const float* lse;            // [B*Hq*S] natural-log log-sum-exp of each query row (scaled scores)
     const float* delta;          // [B*Hq*S] rowsum(dO o O)
-    const __nv_bfloat16* p_in;   // kDS: the P tiles
-    __nv_bfloat16* out;          // kP / kDS: [B*Hq*S, S]; kDKV: [B*Hkv*S, D]; kDQ: [B*Hq*S, D]
+    __nv_bfloat16* out;          // kPDS (P): [B*Hq*S, S]; kDKV: [B*Hkv*S, D]; kDQ: [B*Hq*S, D]
+    __nv_bfloat16* out2;         // kPDS: dS [B*Hq*S, S]
 };
 
-template <int BN>
+template <int BN, int NACC = 1>
 struct ACfg {
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
     static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
-    static constexpr int kTmemCols = 2 * BN;
+    static constexpr int kAccCols = NACC * BN;  // one tile's accumulators (kPDS: S and dP side by side)
+    static constexpr int kTmemCols = 2 * kAccCols;
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
 };
 
-// Unit `t`-th of CTA `c` (of G) in the pass's order: round-robin for the equal tiles of kP / kDS, a snake
+// Unit `t`-th of CTA `c` (of G) in the pass's order: round-robin for the equal tiles of kPDS, a snake
 // over the longest-first order for kDKV / kDQ (a CTA's heavy unit of one round meets a light one in the next).
 template <int KIND>
 __device__ __forceinline__ int unit_of(int t, int c, int G) {
-    if (KIND == kP || KIND == kDS) return t * G + c;
+    if (KIND == kPDS) return t * G + c;
     return t * G + ((t & 1) ? (G - 1 - c) : c);
 }
 
@@ -79,12 +80,12 @@ __device__ __forceinline__ void tri_tile(int u, int nblk, int& bh, int& i, int& 
 }
 
 // The unit's output tile and its number of 64-deep k blocks.
-//   kP / kDS: (bh, i, j)          kDKV: (bg = b * Hkv + g, j = key block)          kDQ: (bh, i = query block)
+//   kPDS: (bh, i, j)          kDKV: (bg = b * Hkv + g, j = key block)          kDQ: (bh, i = query block)
 template <int KIND>
 __device__ __forceinline__ void unit_geom(const AttnArgs& a, int u, int& x0, int& x1, int& x2, int& nk) {
-    if (KIND == kP || KIND == kDS) {
+    if (KIND == kPDS) {  // S's k blocks, then dP's
         tri_tile(u, a.nblk, x0, x1, x2);
-        nk = a.D / kBK;
+        nk = 2 * (a.D / kBK);
     } else if (KIND == kDKV) {
         const int groups = a.B * a.Hkv;
         x1 = u / groups;  // key block, ascending = longest first
@@ -104,8 +105,9 @@ __device__ __forceinline__ void unit_geom(const AttnArgs& a, int u, int& x0, int
 template <int KIND, int BN, int EPW>
 __global__ void __launch_bounds__(128 + 128 * EPW, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
+                    const __grid_constant__ CUtensorMap tA2, const __grid_constant__ CUtensorMap tB2,
                     const AttnArgs args) {
-    using C = ACfg<BN>;
+    using C = ACfg<BN, KIND == kPDS ? 2 : 1>;
     constexpr int A_MN = KIND == kDKV ? 1 : 0;
     constexpr int B_MN = (KIND == kDKV || KIND == kDQ) ? 1 : 0;
     extern __shared__ uint8_t smem_raw[];
@@ -139,6 +141,10 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
     if (warp == 0 && lane == 0) {
         tma_prefetch(&tA);
         tma_prefetch(&tB);
+        if (KIND == kPDS) {
+            tma_prefetch(&tA2);
+            tma_prefetch(&tB2);
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -167,12 +173,15 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
                 uint8_t* sa = smem + stage * C::kStageBytes;
                 uint8_t* sb = sa + kABytes;
                 mbar_expect_tx(&full_bar[stage], C::kStageBytes);
-                if (KIND == kP || KIND == kDS) {
+                if (KIND == kPDS) {
                     const int bh = x0, b = bh / args.Hq, h = bh - b * args.Hq;
                     const int qrow = bh * args.S + x1 * kBM;
                     const int krow = (b * args.Hkv + h / args.grp) * args.S + x2 * kBM;
-                    tma_load_2d(sa, &tA, &full_bar[stage], kb * kBK, qrow);
-                    tma_load_2d(sb, &tB, &full_bar[stage], kb * kBK, krow);
+                    const int nd = args.D / kBK;
+                    const bool second = kb >= nd;  // dO, V after Q, K
+                    const int kc = (second ? kb - nd : kb) * kBK;
+                    tma_load_2d(sa, second ? &tA2 : &tA, &full_bar[stage], kc, qrow);
+                    tma_load_2d(sb, second ? &tB2 : &tB, &full_bar[stage], kc, krow);
                 } else if (KIND == kDKV) {
                     const int bg = x0, b = bg / args.Hkv, g = bg - b * args.Hkv, j = x1;
                     const int per_head = (args.nblk - j) * 2;
@@ -215,7 +224,8 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
             const int acc = local & 1;
             if (!mbar_wait(&tempty_bar[acc], ((local >> 1) & 1) ^ 1u, abort_flag)) break;
             tc_fence_after();
-            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+            const uint32_t d_base = tmem_base + (uint32_t)(acc * C::kAccCols);
+            const int nd = args.D / kBK;
             for (int kb = 0; kb < nk; ++kb) {
                 if (!mbar_wait(&full_bar[stage], phase, abort_flag)) {
                     ok = false;
@@ -224,13 +234,17 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
                 tc_fence_after();
                 const uint32_t sa = smem_u32(smem + stage * C::kStageBytes);
                 const uint32_t sb = sa + kABytes;
+                // kPDS: S accumulates over the first nd k blocks, dP (BN columns further) over the next nd
+                const bool second = KIND == kPDS && kb >= nd;
+                const uint32_t d_tmem = d_base + (second ? (uint32_t)BN : 0u);
+                const int kb0 = second ? nd : 0;
 #pragma unroll
                 for (int kk = 0; kk < kBK / 16; ++kk) {
                     const uint64_t ad = A_MN ? make_sdesc_sw128(sa + kk * 2048, 8192, 1024)
                                              : make_sdesc_sw128(sa + kk * 32, 16, 1024);
                     const uint64_t bd = B_MN ? make_sdesc_sw128(sb + kk * 2048, 8192, 1024)
                                              : make_sdesc_sw128(sb + kk * 32, 16, 1024);
-                    umma_f16(d_tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+                    umma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
                 }
                 umma_commit(&empty_bar[stage]);
                 if (++stage == C::kStages) {
@@ -261,54 +275,48 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
             const int acc = local & 1;
             if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag)) break;
             tc_fence_after();
-            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-            if (KIND == kP || KIND == kDS) {
+            const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * C::kAccCols);
+            if (KIND == kPDS) {
+                // P = exp2(S scale log2e - lse log2e) (causal), dS = scale P (dP - Delta); both stored
                 const int bh = x0, i = x1, j = x2;
                 const int qpos = i * kBM + row;
                 const int64_t grow = (int64_t)bh * args.S + qpos;
-                const float lse2 = KIND == kP ? args.lse[grow] * kLog2e : 0.0f;
-                const float dlt = KIND == kDS ? args.delta[grow] : 0.0f;
+                const float lse2 = args.lse[grow] * kLog2e;
+                const float dlt = args.delta[grow];
                 const float sl2 = args.scale * kLog2e;
                 __nv_bfloat16* op = args.out + grow * args.S + j * kBM;
-                const __nv_bfloat16* pp = KIND == kDS ? args.p_in + grow * args.S + j * kBM : nullptr;
+                __nv_bfloat16* od = args.out2 + grow * args.S + j * kBM;
 #pragma unroll 1
                 for (int cc = c0; cc < c0 + kChunks; ++cc) {
-                    uint32_t r[32];
+                    uint32_t rs[32], rd[32];
                     __syncwarp();
-                    tmem_ld32(tbase + (uint32_t)(cc * 32), r);
+                    tmem_ld32(tbase + (uint32_t)(cc * 32), rs);
+                    tmem_ld32(tbase + (uint32_t)(BN + cc * 32), rd);
                     tmem_ld_wait();
-                    float v[32];
-                    if (KIND == kP) {
+                    float pv[32], dv[32];
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            const int kpos = j * kBM + cc * 32 + e;
-                            v[e] = kpos <= qpos ? exp2f(__uint_as_float(r[e]) * sl2 - lse2) : 0.0f;
-                        }
-                    } else {
-                        const uint4* pv = reinterpret_cast<const uint4*>(pp + cc * 32);
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) {
-                            const uint4 x = pv[w];
-                            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                            for (int h2 = 0; h2 < 4; ++h2) {
-                                const __nv_bfloat162 p2 = *reinterpret_cast<const __nv_bfloat162*>(&xs[h2]);
-                                const int e = w * 8 + h2 * 2;
-                                v[e] = args.scale * __bfloat162float(p2.x) * (__uint_as_float(r[e]) - dlt);
-                                v[e + 1] = args.scale * __bfloat162float(p2.y) * (__uint_as_float(r[e + 1]) - dlt);
-                            }
-                        }
+                    for (int e = 0; e < 32; ++e) {
+                        const int kpos = j * kBM + cc * 32 + e;
+                        const float pe = kpos <= qpos ? exp2f(__uint_as_float(rs[e]) * sl2 - lse2) : 0.0f;
+                        // dS is formed from P as stored (bf16), the P that dV reads
+                        const float pb = __bfloat162float(__float2bfloat16_rn(pe));
+                        pv[e] = pe;
+                        dv[e] = args.scale * pb * (__uint_as_float(rd[e]) - dlt);
                     }
                     uint4* dst = reinterpret_cast<uint4*>(op + cc * 32);
+                    uint4* dsd = reinterpret_cast<uint4*>(od + cc * 32);
 #pragma unroll
                     for (int w = 0; w < 4; ++w) {
-                        uint32_t pk[4];
+                        uint32_t pk[4], dk[4];
 #pragma unroll
                         for (int h2 = 0; h2 < 4; ++h2) {
-                            const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[w * 8 + h2 * 2], v[w * 8 + h2 * 2 + 1]);
+                            const __nv_bfloat162 b2 = __floats2bfloat162_rn(pv[w * 8 + h2 * 2], pv[w * 8 + h2 * 2 + 1]);
+                            const __nv_bfloat162 d2 = __floats2bfloat162_rn(dv[w * 8 + h2 * 2], dv[w * 8 + h2 * 2 + 1]);
                             pk[h2] = *reinterpret_cast<const uint32_t*>(&b2);
+                            dk[h2] = *reinterpret_cast<const uint32_t*>(&d2);
                         }
                         dst[w] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        dsd[w] = make_uint4(dk[0], dk[1], dk[2], dk[3]);
                     }
                 }
             } else {
@@ -373,9 +381,10 @@ __global__ void attn_delta_kernel(const __nv_bfloat16* __restrict__ dout, const 
 }
 
 template <int KIND, int BN>
-int launch_pass(const CUtensorMap& a, const CUtensorMap& b, const AttnArgs& args, cudaStream_t stream) {
-    using C = ACfg<BN>;
-    constexpr int EPW = (KIND == kP || KIND == kDS) ? 4 : 2;
+int launch_pass(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a2, const CUtensorMap& b2,
+                const AttnArgs& args, cudaStream_t stream) {
+    using C = ACfg<BN, KIND == kPDS ? 2 : 1>;
+    constexpr int EPW = KIND == kPDS ? 4 : 2;
     static_assert((BN / 32) % EPW == 0, "column slices");
     auto kern = attn_bwd_kernel<KIND, BN, EPW>;
     static bool attr = false;
@@ -385,7 +394,7 @@ int launch_pass(const CUtensorMap& a, const CUtensorMap& b, const AttnArgs& args
     }
     int grid = num_sms();
     if (args.units < grid) grid = args.units;
-    kern<<<grid, 128 + 128 * EPW, C::kSmemBytes, stream>>>(a, b, args);
+    kern<<<grid, 128 + 128 * EPW, C::kSmemBytes, stream>>>(a, b, a2, b2, args);
     return launch_status();
 }
 
@@ -450,28 +459,26 @@ extern "C" int r97b_attn_bwd(const R97bAttnBwd* a, void* stream) {
         if ((rc = launch_status()) != R97B_OK) return rc;
     }
     const int tri = args.nblk * (args.nblk + 1) / 2;
-    // P tiles
+    // P and dS tiles in one pass (S = Q K^T and dP = dO V^T into two accumulators)
     args.units = B * Hq * tri;
     args.out = P;
-    if ((rc = launch_pass<kP, 128>(mQ, mK, args, st)) != R97B_OK) return rc;
+    args.out2 = dS;
+    if ((rc = launch_pass<kPDS, 128>(mQ, mK, mdO, mV, args, st)) != R97B_OK) return rc;
     // dV = P^T dO
     args.units = B * Hkv * args.nblk;
     args.out = reinterpret_cast<__nv_bfloat16*>(a->dv);
-    rc = D == 256 ? launch_pass<kDKV, 256>(mP_mn, mdO_mn, args, st) : launch_pass<kDKV, 128>(mP_mn, mdO_mn, args, st);
+    rc = D == 256 ? launch_pass<kDKV, 256>(mP_mn, mdO_mn, mP_mn, mdO_mn, args, st)
+                  : launch_pass<kDKV, 128>(mP_mn, mdO_mn, mP_mn, mdO_mn, args, st);
     if (rc != R97B_OK) return rc;
-    // dS tiles
-    args.units = B * Hq * tri;
-    args.out = dS;
-    args.p_in = P;
-    if ((rc = launch_pass<kDS, 128>(mdO, mV, args, st)) != R97B_OK) return rc;
     // dK = dS^T Q
-    args.units = B * Hkv * args.nblk;
     args.out = reinterpret_cast<__nv_bfloat16*>(a->dk);
-    rc = D == 256 ? launch_pass<kDKV, 256>(mdS_mn, mQ_mn, args, st) : launch_pass<kDKV, 128>(mdS_mn, mQ_mn, args, st);
+    rc = D == 256 ? launch_pass<kDKV, 256>(mdS_mn, mQ_mn, mdS_mn, mQ_mn, args, st)
+                  : launch_pass<kDKV, 128>(mdS_mn, mQ_mn, mdS_mn, mQ_mn, args, st);
     if (rc != R97B_OK) return rc;
     // dQ = dS K
     args.units = B * Hq * args.nblk;
     args.out = reinterpret_cast<__nv_bfloat16*>(a->dq);
-    rc = D == 256 ? launch_pass<kDQ, 256>(mdS_k, mK_mn, args, st) : launch_pass<kDQ, 128>(mdS_k, mK_mn, args, st);
+    rc = D == 256 ? launch_pass<kDQ, 256>(mdS_k, mK_mn, mdS_k, mK_mn, args, st)
+                  : launch_pass<kDQ, 128>(mdS_k, mK_mn, mdS_k, mK_mn, args, st);
     return rc;
 }

@@ -319,43 +319,88 @@ __global__ void __launch_bounds__(256) conv_prep_bwd_kernel(ConvArgs a, const fl
 
 // ------------------------------------------------------------------------------------------- gates
 
-// one thread per (chunk, head): beta = sigmoid(b), g = within-chunk running sum of the decay increment
-__global__ void gates_fwd_kernel(const __nv_bfloat16* __restrict__ ba, int64_t ldba, const float* __restrict__ a_log,
-                                 const float* __restrict__ dt_bias, const int* __restrict__ tok0,
-                                 const int* __restrict__ len, int n_chunks, int H, float* __restrict__ g,
-                                 float* __restrict__ beta) {
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= n_chunks * H) return;
-    const int c = idx / H, h = idx % H;
-    const float decay = -expf(a_log[h]);
-    float run = 0.0f;
-    for (int i = 0; i < len[c]; ++i) {
-        const int64_t t = tok0[c] + i;
-        const float bv = __bfloat162float(ba[t * ldba + h]);
-        const float av = __bfloat162float(ba[t * ldba + H + h]);
-        run += decay * softplus(av + dt_bias[h]);
-        g[t * H + h] = run;
-        beta[t * H + h] = sigm(bv);
+// A block per (chunk, 32 heads): thread (h, y) owns tokens [8 y, 8 y + 8) of the chunk for head h; its
+// 8-token sums are combined across y through shared memory (a within-chunk scan over 8 partial sums).
+constexpr int kGateTok = 8;   // tokens a thread owns
+constexpr int kGateGroups = 8; // threads a head (covers the chunk's 64 tokens)
+
+// beta = sigmoid(b); g = within-chunk running sum of the decay increment decay * softplus(a + dt_bias)
+__global__ void __launch_bounds__(256) gates_fwd_kernel(const __nv_bfloat16* __restrict__ ba, int64_t ldba,
+                                                        const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                                                        const int* __restrict__ tok0, const int* __restrict__ len,
+                                                        int n_chunks, int H, float* __restrict__ g,
+                                                        float* __restrict__ beta) {
+    __shared__ float part[kGateGroups][32];
+    const int c = blockIdx.x, hl = threadIdx.x & 31, y = threadIdx.x >> 5;
+    const int h = blockIdx.y * 32 + hl;
+    const bool on = h < H;
+    const int n = len[c];
+    const int64_t t0 = tok0[c];
+    const float decay = on ? -expf(a_log[h]) : 0.0f;
+    const float bias = on ? dt_bias[h] : 0.0f;
+    float inc[kGateTok], run = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kGateTok; ++i) {
+        const int k = y * kGateTok + i;
+        inc[i] = 0.0f;
+        if (on && k < n) {
+            const int64_t t = t0 + k;
+            inc[i] = decay * softplus(__bfloat162float(ba[t * ldba + H + h]) + bias);
+            beta[t * H + h] = sigm(__bfloat162float(ba[t * ldba + h]));
+        }
+        run += inc[i];
+    }
+    part[y][hl] = run;
+    __syncthreads();
+    float base = 0.0f;
+    for (int j = 0; j < y; ++j) base += part[j][hl];
+    run = base;
+#pragma unroll
+    for (int i = 0; i < kGateTok; ++i) {
+        const int k = y * kGateTok + i;
+        run += inc[i];
+        if (on && k < n) g[(t0 + k) * H + h] = run;
     }
 }
 
-__global__ void gates_bwd_kernel(const __nv_bfloat16* __restrict__ ba, int64_t ldba, const float* __restrict__ a_log,
-                                 const float* __restrict__ dt_bias, const int* __restrict__ tok0,
-                                 const int* __restrict__ len, int n_chunks, int H, const float* __restrict__ dg,
-                                 const float* __restrict__ dbeta, __nv_bfloat16* __restrict__ dba, int64_t lddba) {
-    const int idx = blockIdx.x * blockDim.x + threadIdx.x;
-    if (idx >= n_chunks * H) return;
-    const int c = idx / H, h = idx % H;
-    const float decay = -expf(a_log[h]);
-    float tail = 0.0f;
-    for (int i = len[c] - 1; i >= 0; --i) {
-        const int64_t t = tok0[c] + i;
-        tail += dg[t * H + h];
-        const float av = __bfloat162float(ba[t * ldba + H + h]) + dt_bias[h];
-        const float sp = av > 20.0f ? 1.0f : sigm(av);
-        dba[t * lddba + H + h] = __float2bfloat16_rn(tail * decay * sp);
-        const float s = sigm(__bfloat162float(ba[t * ldba + h]));
-        dba[t * lddba + h] = __float2bfloat16_rn(dbeta[t * H + h] * s * (1.0f - s));
+// d(a) = decay * sigmoid(a + dt_bias) * sum_{j >= i in the chunk} dg_j ; d(b) = dbeta * s (1 - s)
+__global__ void __launch_bounds__(256) gates_bwd_kernel(const __nv_bfloat16* __restrict__ ba, int64_t ldba,
+                                                        const float* __restrict__ a_log, const float* __restrict__ dt_bias,
+                                                        const int* __restrict__ tok0, const int* __restrict__ len,
+                                                        int n_chunks, int H, const float* __restrict__ dg,
+                                                        const float* __restrict__ dbeta, __nv_bfloat16* __restrict__ dba,
+                                                        int64_t lddba) {
+    __shared__ float part[kGateGroups][32];
+    const int c = blockIdx.x, hl = threadIdx.x & 31, y = threadIdx.x >> 5;
+    const int h = blockIdx.y * 32 + hl;
+    const bool on = h < H;
+    const int n = len[c];
+    const int64_t t0 = tok0[c];
+    const float decay = on ? -expf(a_log[h]) : 0.0f;
+    const float bias = on ? dt_bias[h] : 0.0f;
+    float d[kGateTok], tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kGateTok; ++i) {
+        const int k = y * kGateTok + i;
+        d[i] = (on && k < n) ? dg[(t0 + k) * H + h] : 0.0f;
+        tot += d[i];
+    }
+    part[y][hl] = tot;
+    __syncthreads();
+    float tail = 0.0f;  // the sum over the later tokens' groups
+    for (int j = y + 1; j < kGateGroups; ++j) tail += part[j][hl];
+#pragma unroll
+    for (int i = kGateTok - 1; i >= 0; --i) {
+        const int k = y * kGateTok + i;
+        tail += d[i];
+        if (on && k < n) {
+            const int64_t t = t0 + k;
+            const float av = __bfloat162float(ba[t * ldba + H + h]) + bias;
+            const float sp = av > 20.0f ? 1.0f : sigm(av);
+            dba[t * lddba + H + h] = __float2bfloat16_rn(tail * decay * sp);
+            const float sg = sigm(__bfloat162float(ba[t * ldba + h]));
+            dba[t * lddba + h] = __float2bfloat16_rn(dbeta[t * H + h] * sg * (1.0f - sg));
+        }
     }
 }
 
@@ -639,7 +684,7 @@ extern "C" int r97b_gates_fwd(const uint16_t* ba, int64_t ldba, const float* a_l
                               float* beta, void* stream) {
     if (!ba || !a_log || !dt_bias || !chunk_tok0 || !chunk_len || !g || !beta || H <= 0) return R97B_EINVAL;
     if (n_chunks <= 0) return R97B_OK;
-    gates_fwd_kernel<<<blocks_for((int64_t)n_chunks * H), 256, 0, as_stream(stream)>>>(
+    gates_fwd_kernel<<<dim3((unsigned)n_chunks, (unsigned)((H + 31) / 32)), 256, 0, as_stream(stream)>>>(
         reinterpret_cast<const __nv_bfloat16*>(ba), ldba, a_log, dt_bias, chunk_tok0, chunk_len, n_chunks, H, g, beta);
     return launch_status();
 }
@@ -649,7 +694,7 @@ extern "C" int r97b_gates_bwd(const uint16_t* ba, int64_t ldba, const float* a_l
                               const float* dg, const float* dbeta, uint16_t* dba, int64_t lddba, void* stream) {
     if (!ba || !a_log || !dt_bias || !chunk_tok0 || !chunk_len || !dg || !dbeta || !dba || H <= 0) return R97B_EINVAL;
     if (n_chunks <= 0) return R97B_OK;
-    gates_bwd_kernel<<<blocks_for((int64_t)n_chunks * H), 256, 0, as_stream(stream)>>>(
+    gates_bwd_kernel<<<dim3((unsigned)n_chunks, (unsigned)((H + 31) / 32)), 256, 0, as_stream(stream)>>>(
         reinterpret_cast<const __nv_bfloat16*>(ba), ldba, a_log, dt_bias, chunk_tok0, chunk_len, n_chunks, H, dg, dbeta,
         reinterpret_cast<__nv_bfloat16*>(dba), lddba);
     return launch_status();

@@ -56,9 +56,12 @@ def test_conv_prep_fwd_bwd(cuda, lens, Hg, H):
         assert not to_np(dx)[:, C:].any()  # columns past the conv channels are not written
 
 
-def test_gates_fwd_bwd(cuda):
-    rs = np.random.RandomState(3)
-    lens, H = (150, 64, 9), 8
+@pytest.mark.parametrize("H", [8, 40])
+def test_gates_fwd_bwd(cuda, H):
+    """ragged chunks (a 9-token sequence, chunk tails of 22 and 9 tokens) and head counts below and past a
+    block's 32 heads"""
+    rs = np.random.RandomState(3 + H)
+    lens = (150, 64, 9)
     T = sum(lens)
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
     ba = _bf(rs.normal(size=(T, 2 * H)) * 2)
