@@ -64,6 +64,33 @@ int r97host_optim_restore(void* opt, const uint8_t* bytes, int64_t size);
 void r97host_optim_destroy(void* opt);
 const char* r97host_optim_error(void);
 
+/* ---- the adapter directory in PEFT's layout (reference include/r97/adapter_io.h, src/adapter_io.cpp) ----
+ * adapter_config.json (PEFT's keys in PEFT's order) and adapter_model.safetensors (tensors sorted by name,
+ * `base_model.model.<module>.lora_A.weight`, f32 or bf16): the files the reference's trainer writes and its
+ * server reads. */
+typedef struct R97hostAdapterConfig {
+    const char* base_model;      /* base_model_name_or_path */
+    int64_t rank;                /* r */
+    double alpha;                /* lora_alpha */
+    const char* const* targets;  /* target_modules */
+    int32_t n_targets;
+    const char* input_basis;     /* radiance_input_basis ("fwht128"), or null / "" for a natural trunk */
+    int32_t dtype;               /* 0: F32, 1: BF16 (round to nearest even) */
+} R97hostAdapterConfig;
+
+/* Writes dir/adapter_config.json and dir/adapter_model.safetensors (dir created if missing) for nparams
+ * parameters named `<module>.lora_A` / `.lora_B` with [rows, cols] shapes (2 int64 each), their f32
+ * values concatenated in that order in `values` -- host memory, or device memory (values_on_device,
+ * copied on `stream`). 0 on success, 1 with a message in r97host_adapter_error. */
+int r97host_adapter_write(const char* dir, const R97hostAdapterConfig* cfg, int32_t nparams, const char* const* names,
+                          const int64_t* shapes, const float* values, int32_t values_on_device, void* stream);
+/* Reads an adapter directory into host `values` laid out as the named parameters in order (each must be in
+ * the file with its shape, and the file must hold no others), with the config's rank and alpha and the
+ * file's dtype (0 F32, 1 BF16; bf16 widened exactly). 0 on success, 1 with a message. */
+int r97host_adapter_read(const char* dir, int32_t nparams, const char* const* names, const int64_t* shapes,
+                         float* values, int64_t* rank, double* alpha, int32_t* dtype);
+const char* r97host_adapter_error(void);
+
 #ifdef __cplusplus
 }
 #endif

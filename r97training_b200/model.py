@@ -88,6 +88,17 @@ def groups_of(cfg: HybridConfig, kind: str):
     return mixer + mlp
 
 
+def module_path(layer: int, kind: str, proj: str) -> str:
+    """The module's path as the reference's container names it (`model.layers.3.self_attn.q_proj`; the
+    GatedDeltaNet mixer's projections under `linear_attn`, the MLP's under `mlp`), the prefix of its
+    adapter parameters `<module>.lora_A` / `<module>.lora_B` (src/delta_lora.cpp:6-13, 130-136)."""
+    if proj in ("gate_proj", "up_proj", "down_proj"):
+        family = "mlp"
+    else:
+        family = "linear_attn" if kind == "gdn" else "self_attn"
+    return f"model.layers.{layer}.{family}.{proj}"
+
+
 # ============================================================================================ weights
 
 @dataclass
@@ -177,13 +188,13 @@ class Adapter:
             for g in blk["groups"]:
                 g.a_off = off
                 for pname, _ in g.projs:
-                    self.names.append(f"model.layers.{li}.{pname}.lora_A")
+                    self.names.append(f"{module_path(li, blk['kind'], pname)}.lora_A")
                     self.shapes.append((r, g.k))
                     self.offsets.append(off)
                     off += r * g.k
                 g.b_offs = []
                 for pname, n in g.projs:
-                    self.names.append(f"model.layers.{li}.{pname}.lora_B")
+                    self.names.append(f"{module_path(li, blk['kind'], pname)}.lora_B")
                     self.shapes.append((n, r))
                     self.offsets.append(off)
                     g.b_offs.append(off)

@@ -70,3 +70,31 @@ def test_graph_replay_matches_eager_steps(cuda):
     spread = float((de - d2).norm() / de.norm())  # two eager runs
     assert cos > 0.99, cos
     assert float((de - dg).norm() / de.norm()) <= max(3 * spread, 0.05), (spread, cos)
+
+
+def test_trained_adapter_saves_and_loads_as_peft(cuda, tmp_path):
+    """The device adapter after a training step written as a PEFT directory straight from device memory
+    (r97host_adapter_write) and loaded into a fresh adapter of the same model: the same f32 master weights,
+    and module paths the reference's container names (`model.layers.<i>.{self_attn,linear_attn,mlp}.<proj>`)."""
+    from r97training_b200 import peft
+    cfg = HybridConfig(hidden=256, layers=4, gdn_heads=4, gdn_qk_heads=2, attn_heads=2, attn_kv_heads=1, ffn=512,
+                       vocab=1024, rank=8, alpha=16, seq=128, micro_batch=2)
+    model = HybridModel(cfg, cuda)
+    ad = Adapter(model, cuda)
+    step = TrainStep(model, ad, head_chunk=128)
+    ids = torch.randint(0, cfg.vocab, (cfg.micro_batch, cfg.seq), device=cuda, dtype=torch.int32)
+    step.run(ids)
+    ad.adamw()
+    torch.cuda.synchronize()
+    assert "model.layers.3.self_attn.q_proj.lora_A" in ad.names
+    assert "model.layers.0.linear_attn.in_proj_qkvz.lora_B" in ad.names
+    assert "model.layers.0.mlp.down_proj.lora_A" in ad.names
+    out = str(tmp_path / "adapter")
+    peft.save_adapter(ad, out, base_model="synthetic-hybrid")
+    fresh = Adapter(model, cuda)
+    rank, alpha, dt = peft.load_adapter(fresh, out)
+    torch.cuda.synchronize()
+    assert (rank, alpha, dt) == (8, 16.0, "f32")
+    assert torch.equal(fresh.w, ad.w)
+    for key in ad.a_bf:
+        assert torch.equal(fresh.a_bf[key], ad.a_bf[key]) and torch.equal(fresh.b_blk[key], ad.b_blk[key])
