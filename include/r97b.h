@@ -175,6 +175,58 @@ typedef struct R97bAttnBwd {
 int r97b_attn_bwd(const R97bAttnBwd* a, void* stream);
 int64_t r97b_attn_bwd_workspace_bytes(int32_t B, int32_t Hq, int32_t S);
 
+/* ------------------------------------------------------------------------------ LoRA linear */
+
+/* One LoRA-adapted linear over a stored weight, forward: W = decode(w) into w_bf16 (skipped when
+ * w_decoded, i.e. w_bf16 already holds this weight -- keep it for the backward), t = scale x A^T,
+ * y = x W^T + t B^T (+ addend). x [M, K], A [rank, K], B [N, rank], t [M, rank], y and addend [M, N], w_bf16
+ * [N, K]: bf16, row-major, dense; K, N and rank multiples of 8. ws: r97b_qlinear_lora_workspace_bytes,
+ * zeroed once before its first use (the split-K GEMM's; reusable, not shared between concurrent calls).
+ * Replaces: the reference's gemm_nt_q + lora_shrink + lora_expand rows for one slot
+ * (src/adjoint/host/linear.cpp:246-317, lora.cpp:226-305, 416-451; device linear.hip, lora.hip K5-K8). */
+typedef struct R97bQLinearLora {
+    int64_t M, N, K;
+    int32_t rank;
+    float scale;                   /* alpha / rank */
+    const R97IqrDecodeDesc* w;     /* the stored weight [N, K] */
+    void* w_bf16;
+    int32_t w_decoded;
+    int32_t _pad;
+    const void* x;
+    const void* A;
+    const void* B;
+    void* t;
+    void* y;
+    const void* addend;
+    void* ws;
+    int64_t ws_bytes;
+} R97bQLinearLora;
+
+/* Its backward: dt = scale dy B, dx = dy W + dt A, dA += dt^T x, dB += dy^T t (dA [rank, K] and dB [N, rank]
+ * f32, accumulated); t is the forward's. Replaces: the same rows' adjoints (linear.cpp:220-243, 246-317,
+ * lora.cpp:320-401, 453-521). */
+typedef struct R97bQLinearLoraBwd {
+    int64_t M, N, K;
+    int32_t rank;
+    float scale;
+    const void* w_bf16;
+    const void* x;
+    const void* A;
+    const void* B;
+    const void* t;
+    const void* dy;
+    void* dt;
+    void* dx;
+    float* dA;
+    float* dB;
+    void* ws;
+    int64_t ws_bytes;
+} R97bQLinearLoraBwd;
+
+int r97b_qlinear_lora_fwd(const R97bQLinearLora* a, void* stream);
+int r97b_qlinear_lora_bwd(const R97bQLinearLoraBwd* a, void* stream);
+int64_t r97b_qlinear_lora_workspace_bytes(int64_t M, int64_t N, int64_t K, int32_t rank);
+
 /* ------------------------------------------------------------------------------ norms */
 
 /* y = x * rsqrt(mean(x^2) + eps) * (w + wadd) * mult per row of n (x, y bf16 [rows, n]; w f32 [n] or null;

@@ -46,6 +46,18 @@ class R97bCastSeg(ctypes.Structure):
                 ("cols", c_i64), ("unit0", c_i64)]
 
 
+class R97bQLinearLora(ctypes.Structure):
+    _fields_ = [("M", c_i64), ("N", c_i64), ("K", c_i64), ("rank", c_i32), ("scale", c_f32), ("w", c_vp),
+                ("w_bf16", c_vp), ("w_decoded", c_i32), ("_pad", c_i32), ("x", c_vp), ("A", c_vp), ("B", c_vp),
+                ("t", c_vp), ("y", c_vp), ("addend", c_vp), ("ws", c_vp), ("ws_bytes", c_i64)]
+
+
+class R97bQLinearLoraBwd(ctypes.Structure):
+    _fields_ = [("M", c_i64), ("N", c_i64), ("K", c_i64), ("rank", c_i32), ("scale", c_f32), ("w_bf16", c_vp),
+                ("x", c_vp), ("A", c_vp), ("B", c_vp), ("t", c_vp), ("dy", c_vp), ("dt", c_vp), ("dx", c_vp),
+                ("dA", c_vp), ("dB", c_vp), ("ws", c_vp), ("ws_bytes", c_i64)]
+
+
 class R97IqrDecodeDesc(ctypes.Structure):
     """Field-for-field the C struct of include/r97b_iqr.h (the reference's R97IqrDecodeDesc layout)."""
     _fields_ = [
@@ -72,6 +84,9 @@ _SIGS = {
     "r97b_attn_bwd": (c_i32, [c_vp, c_vp]),
     "r97b_cast_segments": (c_i32, [c_vp, c_i32, c_i64, c_vp]),
     "r97b_add_f32": (c_i32, [c_vp, c_vp, c_i64, c_vp]),
+    "r97b_qlinear_lora_fwd": (c_i32, [c_vp, c_vp]),
+    "r97b_qlinear_lora_bwd": (c_i32, [c_vp, c_vp]),
+    "r97b_qlinear_lora_workspace_bytes": (c_i64, [c_i64, c_i64, c_i64, c_i32]),
     "r97b_attn_bwd_workspace_bytes": (c_i64, [c_i32, c_i32, c_i32]),
     "r97b_rmsnorm_fwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),
     "r97b_rmsnorm_bwd": (c_i32, [c_vp, c_vp, c_vp, c_vp, c_vp, c_i64, c_i64, c_f32, c_f32, c_f32, c_vp]),

@@ -10,7 +10,8 @@ import ctypes
 
 import torch
 
-from ._lib import R97bAttnBwd, R97bCastSeg, R97bGemm, R97bMat, R97bError, check, lib
+from ._lib import (R97bAttnBwd, R97bCastSeg, R97bError, R97bGemm, R97bMat, R97bQLinearLora,
+                   R97bQLinearLoraBwd, check, lib)
 
 EPI_STORE_BF16, EPI_STORE_F32, EPI_ATOMIC_F32, EPI_ATOMIC_F32T, EPI_SPLIT_BF16 = 0, 1, 2, 3, 4
 EPI_SWIGLU, EPI_SWIGLU_BWD = 5, 6
@@ -323,6 +324,49 @@ def gate_mul_bwd(attn, gate, gate_hs, heads, S, dy, dattn, dgate, stream=None):
     T = dy.shape[0]
     check(lib().r97b_gate_mul_bwd(_ptr(attn), _ptr(gate), gate.stride(0), gate_hs, heads, T, S, _ptr(dy),
                                   _ptr(dattn), _ptr(dgate), dgate.stride(0), _stream(stream)), "r97b_gate_mul_bwd")
+
+
+def qlinear_lora_workspace(M: int, N: int, K: int, rank: int, device) -> torch.Tensor:
+    """The zeroed split-K workspace r97b_qlinear_lora_fwd / _bwd need for these shapes."""
+    n = int(lib().r97b_qlinear_lora_workspace_bytes(M, N, K, rank))
+    if n < 0:
+        raise R97bError("r97b_qlinear_lora_workspace_bytes: bad shape")
+    return torch.zeros(max(n, 256), dtype=torch.uint8, device=device)
+
+
+def qlinear_lora_fwd(w, w_bf16, x, A, B, scale, *, t=None, y=None, addend=None, w_decoded=False, ws=None,
+                     stream=None):
+    """y = x decode(w)^T + (scale x A^T) B^T (+ addend) through r97b_qlinear_lora_fwd; returns (y, t).
+    `w` is an iqr.IqrWeight [N, K]; w_bf16 [N, K] receives (or, with w_decoded, holds) its decode."""
+    from . import iqr as IQ
+    M, K = x.shape
+    N, r = B.shape
+    t = torch.empty((M, r), dtype=torch.bfloat16, device=x.device) if t is None else t
+    y = torch.empty((M, N), dtype=torch.bfloat16, device=x.device) if y is None else y
+    ws = qlinear_lora_workspace(M, N, K, r, x.device) if ws is None else ws
+    for u, nm in ((w_bf16, "w_bf16"), (x, "x"), (A, "A"), (B, "B"), (t, "t"), (y, "y")):
+        _need(u, torch.bfloat16, nm)
+    d = IQ.make_desc(w) if w is not None else None
+    a = R97bQLinearLora(M, N, K, r, float(scale), ctypes.cast(ctypes.pointer(d), ctypes.c_void_p) if d else None,
+                        _ptr(w_bf16), int(w_decoded), 0, _ptr(x), _ptr(A), _ptr(B), _ptr(t), _ptr(y), _ptr(addend),
+                        _ptr(ws), ws.numel())
+    check(lib().r97b_qlinear_lora_fwd(ctypes.byref(a), _stream(stream)), "r97b_qlinear_lora_fwd")
+    return y, t
+
+
+def qlinear_lora_bwd(w_bf16, x, A, B, t, dy, scale, dA, dB, *, dx=None, dt=None, ws=None, stream=None):
+    """dx = dy W + (scale dy B) A; dA += dt^T x; dB += dy^T t (f32) through r97b_qlinear_lora_bwd; returns dx."""
+    M, K = x.shape
+    N, r = B.shape
+    dx = torch.empty((M, K), dtype=torch.bfloat16, device=x.device) if dx is None else dx
+    dt = torch.empty((M, r), dtype=torch.bfloat16, device=x.device) if dt is None else dt
+    ws = qlinear_lora_workspace(M, N, K, r, x.device) if ws is None else ws
+    _need(dA, torch.float32, "dA")
+    _need(dB, torch.float32, "dB")
+    a = R97bQLinearLoraBwd(M, N, K, r, float(scale), _ptr(w_bf16), _ptr(x), _ptr(A), _ptr(B), _ptr(t), _ptr(dy),
+                           _ptr(dt), _ptr(dx), _ptr(dA), _ptr(dB), _ptr(ws), ws.numel())
+    check(lib().r97b_qlinear_lora_bwd(ctypes.byref(a), _stream(stream)), "r97b_qlinear_lora_bwd")
+    return dx
 
 
 def attn_bwd_workspace(B: int, Hq: int, S: int, device) -> torch.Tensor:

@@ -158,3 +158,38 @@ def test_config3_vocab_head_ce_kld_full_size(cuda):
     dh_ref = got_g.astype(np.float64) @ Wn
     assert_close_bf16(to_np(dh[torch.from_numpy(sample).to(cuda)]), dh_ref, what="d(hidden) rows")
     assert math.isfinite(float(dh.float().abs().max()))
+
+
+@pytest.mark.parametrize("M,N,K,r,addend", [(256, 2048, 2048, 16, False), (1000, 1536, 512, 64, True)])
+def test_qlinear_lora_entry_points_vs_oracle(cuda, M, N, K, r, addend):
+    """r97b_qlinear_lora_fwd / _bwd (the decode, the adapter's narrow products and the base product in one
+    call each) against the f64 rows on config 1's distributions; the backward reuses the forward's decode
+    and accumulates into the gradients it is given."""
+    rs = np.random.RandomState(M + r)
+    s = 32.0 / 16.0
+    X = _bf(rs.normal(size=(M, K)))
+    A = _bf(rs.normal(size=(r, K)) / 4.0)
+    B = _bf(rs.normal(size=(N, r)) * 0.01)
+    dY = _bf(rs.normal(size=(M, N)) * 1e-2)
+    C = _bf(rs.normal(size=(M, N))) if addend else None
+    w = IQ.synth_weight(N, K, seed=M + N, device=cuda, scale_std=0.02)
+    wb = torch.empty((N, K), dtype=torch.bfloat16, device=cuda)
+    x, a, b, dy = (u.to(cuda) for u in (X, A, B, dY))
+    y, t = ops.qlinear_lora_fwd(w, wb, x, a, b, s, addend=None if C is None else C.to(cuda))
+    dA0 = torch.from_numpy(rs.normal(size=(r, K)).astype(np.float32)).to(cuda)
+    dB0 = torch.from_numpy(rs.normal(size=(N, r)).astype(np.float32)).to(cuda)
+    dA, dB = dA0.clone(), dB0.clone()
+    dx = ops.qlinear_lora_bwd(wb, x, a, b, t, dy, s, dA, dB)
+    torch.cuda.synchronize()
+    Wn = to_np(IQ.dequant_bf16(w))
+    assert torch.equal(wb, IQ.dequant_bf16(w))
+    xn, an, bnp, dyn = (u.double().numpy() for u in (X, A, B, dY))
+    y_ref, t_ref = R.lora_fwd(xn, Wn, an, bnp, s)
+    if C is not None:
+        y_ref = y_ref + C.double().numpy()
+    dx_ref, dA_ref, dB_ref, _ = R.lora_bwd(xn, Wn, an, bnp, s, t_ref, dyn)
+    assert_close_bf16(to_np(y), y_ref, what="y")
+    assert_close_bf16(to_np(t), s * t_ref, what="t")
+    assert_close_bf16(to_np(dx), dx_ref, what="dx")
+    assert_close_bf16(to_np(dA) - to_np(dA0), dA_ref, what="dA")
+    assert_close_bf16(to_np(dB) - to_np(dB0), dB_ref, what="dB")
