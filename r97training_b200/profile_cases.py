@@ -2,6 +2,8 @@
 
     python -m r97training_b200.profile_cases gemm      # the config-5 gate_up forward GEMM (8192 x 24576 x 4096)
     python -m r97training_b200.profile_cases gemm_dx   # its input adjoint (B operand MN-major)
+    python -m r97training_b200.profile_cases gemm_swiglu  # the gate_up forward as the step runs it: LoRA tail,
+                                                          # SwiGLU in the epilogue (8192 x 24576 x 4096 + 128)
     python -m r97training_b200.profile_cases gdn       # one config-5 GDN layer, forward + backward
     python -m r97training_b200.profile_cases decode    # the IQR decode of a 24576 x 4096 weight
     python -m r97training_b200.profile_cases norms     # rmsnorm fwd/bwd at 8192 x 4096
@@ -26,7 +28,18 @@ import torch
 def main(case: str) -> None:
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
-    if case in ("gemm", "gemm_dx"):
+    if case == "gemm_swiglu":
+        from . import ops
+        M, F, K, r = 8192, 12288, 4096, 128
+        X = torch.randn(M, K, device=dev).bfloat16()
+        W = (torch.randn(2 * F, K, device=dev) * 0.02).bfloat16()
+        t = torch.randn(M, r, device=dev).bfloat16()
+        Bb = (torch.randn(2 * F, r, device=dev) * 0.02).bfloat16()
+        gu = torch.empty(M, 2 * F, device=dev, dtype=torch.bfloat16)
+        a = torch.empty(M, F, device=dev, dtype=torch.bfloat16)
+        for _ in range(3):
+            ops.gemm(X, W, gu, a2=t, b2=Bb, mode=ops.EPI_SWIGLU, out2=a)
+    elif case in ("gemm", "gemm_dx"):
         from . import ops
         M, N, K = 8192, 24576, 4096
         X = torch.randn(M, K, device=dev).bfloat16()
