@@ -10,6 +10,8 @@
 //   embedding   row gather of the tied head weight
 //   casts       f32 -> bf16 2-D strided copies (adapter mirrors)
 #include "r97b_internal.h"
+#include "wmma16.cuh"
+#include "fastmath.cuh"
 
 #include <cuda_bf16.h>
 #include <math.h>
@@ -84,10 +86,9 @@ __device__ __forceinline__ void st4(__nv_bfloat16* p, const float (&v)[4]) {
 // eight warp reductions of a group interleaved, so the shuffles' latency overlaps.
 constexpr int kG = 4;
 constexpr int kRunF = 32;                // tokens a forward thread emits (8 groups)
-constexpr int kRunB = 29;                // tokens a backward thread emits: 29 + 3 = 32 dacc rows = 8 groups
 
 // sigmoid by the fast exponential; silu(x) = x s, silu'(x) = s (1 + x (1 - s))
-__device__ __forceinline__ float sigm_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigm_fast(float x) { return sigmoid_ftz(x); }
 
 struct ConvRun {
     int t_begin, c;
@@ -185,7 +186,7 @@ __global__ void __launch_bounds__(256) conv_prep_fwd_kernel(ConvArgs a, __nv_bfl
         for (int j = 0; j < kG; ++j) {
             const int t = tg + j;
             if (normed) {
-                const float inv = rsqrtf(ss[j] + 1e-6f);
+                const float inv = rsqrt_ftz(ss[j] + 1e-6f);
 #pragma unroll
                 for (int i = 0; i < 4; ++i) u[j][i] *= inv;
             }
@@ -198,124 +199,227 @@ __global__ void __launch_bounds__(256) conv_prep_fwd_kernel(ConvArgs a, __nv_bfl
     }
 }
 
-// The adjoint in one pass: for the dacc rows t' = t_begin .. t_begin + kRunB + 2 (the run plus the three
-// rows dx's taps reach past it) the thread rebuilds the conv output from x, forms dacc(t') (silu's and,
-// for q/k, the L2 norm's backward), and emits dx(t) = sum_{s = 0..3, same sequence} dacc(t + s) w[c, 3 - s]
-// as soon as its four dacc rows are known. dq/dk may still be per value head (grp value heads a key
-// head): the thread sums them as it reads.
-// Three CTAs an SM (the register cap spills a few of the run's rows to L1): measured 7 % faster than two.
-__global__ void __launch_bounds__(256, 3) conv_prep_bwd_kernel(ConvArgs a, const float* __restrict__ dq,
-                                                            const float* __restrict__ dk, const float* __restrict__ dv,
-                                                            int grp, __nv_bfloat16* __restrict__ dx, int64_t lddx) {
-    const ConvRun cr = conv_run(a, kRunB);
-    const int c = cr.c;
-    float w[4][kW];
-    load_w4(a, c, w);
-    const int qk = a.Hg * 128;
-    const bool normed = c < 2 * qk;
-    const float* dsrc;
-    int64_t dstride;
+// The sequence holding token t: cu[s] <= t < cu[s + 1] (binary search over the n_seq + 1 bounds).
+__device__ __forceinline__ void seq_bounds(const ConvArgs& a, int t, int& start, int& end) {
+    int lo = 0, hi = a.n_seq - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (a.cu[mid] <= t) lo = mid;
+        else hi = mid - 1;
+    }
+    start = a.cu[lo];
+    end = a.cu[lo + 1];
+}
+
+// The adjoint by token tiles, persistent and double-buffered. A tile is kConvTT tokens of one 128-channel
+// head; a CTA walks tiles blockIdx.x, + gridDim.x, ... (heads fastest, so the CTAs in flight read whole token
+// rows), staging the next tile's x rows t0 - 3 .. t0 + kConvTT + 2 and d rows (dq/dk per value head: grp
+// slices a row) in shared memory by cp.async while it works on the current one, so HBM streams throughout.
+// On a tile a half-warp takes one token row, a lane 8 channels (two groups of 4, 64 apart, so every shared
+// access of a half-warp is one contiguous run): phase 1 rebuilds the conv output of rows t0 .. t0 + kConvTT + 2
+// and forms dacc (silu's and, for q/k, the L2 norm's backward: two half-warp reductions over the head's row)
+// over the row's first d slice; phase 2 emits dx(t) = sum_{s = 0..3, same sequence} dacc(t + s) w[c, 3 - s].
+constexpr int kConvRows = 32;                   // dacc rows a tile forms: two per warp, twice
+constexpr int kConvTT = kConvRows - (kW - 1);   // tokens a tile emits
+constexpr int kConvXRows = kConvRows + kW - 1;  // x rows it reads
+
+struct ConvStage {  // byte offsets within a stage
+    int ds, seq, bytes;
+};
+__host__ __device__ inline ConvStage conv_stage(int grp) {
+    ConvStage st;
+    st.ds = kConvXRows * 256;                              // x: [kConvXRows][128] bf16
+    st.seq = st.ds + kConvRows * grp * 128 * 4;            // d: [kConvRows][grp * 128] f32
+    st.bytes = (st.seq + 2 * kConvRows * 4 + 15) & ~15;  // sequence start / end of each row's token
+    return st;
+}
+
+__device__ __forceinline__ void cp_async8(void* dst, const void* src, bool pred) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(s_addr(dst)), "l"(src), "r"(pred ? 8 : 0)
+                 : "memory");
+}
+
+struct ConvBwdArgs {
+    const float* dq;
+    const float* dk;
+    const float* dv;
+    int grp, n_tiles;
+    __nv_bfloat16* dx;
+    int64_t lddx;
+};
+
+// Stage a tile: every thread issues its share of the 8-byte x and 16-byte d copies (zeros past the tokens),
+// and threads 0 .. kConvRows - 1 write their row's sequence bounds.
+__device__ __forceinline__ void conv_bwd_issue(const ConvArgs& a, const ConvBwdArgs& b, const ConvStage& sl,
+                                               unsigned char* stage, int tile) {
+    const int heads = a.conv_dim >> 7, head = tile % heads, t0 = (tile / heads) * kConvTT;
+    const int cbase = head * 128, qk = a.Hg * 128;
+    const __nv_bfloat16* xsrc = a.x + cbase + (threadIdx.x & 31) * 4;
+#pragma unroll
+    for (int k = 0; k < (kConvXRows * 32 + 255) / 256; ++k) {
+        const int r = (threadIdx.x >> 5) + 8 * k, tt = t0 - (kW - 1) + r;
+        const bool on = tt >= 0 && tt < a.T;
+        if (r < kConvXRows)
+            cp_async8(stage + r * 256 + (threadIdx.x & 31) * 8, xsrc + (int64_t)(on ? tt : 0) * a.ldx, on);
+    }
+    const float* src;
+    int64_t stride;
     int nsum;
-    if (c < qk) {
-        dsrc = dq + (int64_t)(c >> 7) * grp * 128 + (c & 127);
-        dstride = (int64_t)a.Hg * grp * 128;
-        nsum = grp;
-    } else if (c < 2 * qk) {
-        dsrc = dk + (int64_t)((c - qk) >> 7) * grp * 128 + ((c - qk) & 127);
-        dstride = (int64_t)a.Hg * grp * 128;
-        nsum = grp;
+    if (cbase < 2 * qk) {
+        const int cc = cbase < qk ? cbase : cbase - qk;
+        stride = (int64_t)a.Hg * b.grp * 128;
+        nsum = b.grp;
+        src = (cbase < qk ? b.dq : b.dk) + (int64_t)(cc >> 7) * b.grp * 128;
     } else {
-        dsrc = dv + (c - 2 * qk);
-        dstride = (int64_t)a.H * 128;
+        stride = (int64_t)a.H * 128;
         nsum = 1;
+        src = b.dv + (cbase - 2 * qk);
     }
-    float xr[kW - 1 + kG][4];  // x rows t0 - 3 .. t0 + 3 of the group at t0
-    float dw[kW - 1 + kG][4];  // dacc rows t0 - 3 .. t0 + 3
-#pragma unroll
-    for (int j = 0; j < kW - 1; ++j) {
-        load_x4(a, c, cr.t_begin - (kW - 1) + j, xr[j]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) dw[j][i] = 0.0f;
+    float* ds = reinterpret_cast<float*>(stage + sl.ds) + (threadIdx.x & 31) * 4;
+    src += (threadIdx.x & 31) * 4;
+    const int dw = b.grp * 128;
+    for (int k = threadIdx.x >> 5; k < kConvRows * nsum; k += 8) {
+        const int r = k & (kConvRows - 1), e = k / kConvRows, t = t0 + r;
+        const bool on = t < a.T;
+        cp_async16(ds + r * dw + e * 128, src + (int64_t)(on ? t : 0) * stride + e * 128, on);
     }
-    SeqCursor sa, sb;  // the sequence of t' (conv taps) and of t' - 3 (dx's taps)
-    sa.init(a, cr.t_begin);
-    sb = sa;
-#pragma unroll 1
-    for (int g0 = 0; g0 < kRunB + kW - 1; g0 += kG) {
-        const int tg = cr.t_begin + g0;
-        float d[kG][4];
-#pragma unroll
-        for (int j = 0; j < kG; ++j) {
-            load_x4(a, c, tg + j, xr[kW - 1 + j]);
-            const int tc = tg + j < a.T ? tg + j : a.T - 1;
-            float4 s4 = *reinterpret_cast<const float4*>(dsrc + (int64_t)tc * dstride);
-            for (int e = 1; e < nsum; ++e) {
-                const float4 x4 = *reinterpret_cast<const float4*>(dsrc + (int64_t)tc * dstride + e * 128);
-                s4.x += x4.x, s4.y += x4.y, s4.z += x4.z, s4.w += x4.w;
-            }
-            d[j][0] = s4.x, d[j][1] = s4.y, d[j][2] = s4.z, d[j][3] = s4.w;
-        }
-        float acc[kG][4], sg[kG][4], ss[kG], dot[kG];
-#pragma unroll
-        for (int j = 0; j < kG; ++j) {
-            sa.advance(a, tg + j);
-            ss[j] = 0.0f;
-            dot[j] = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float x = 0.0f;
-#pragma unroll
-                for (int tap = 0; tap < kW; ++tap)
-                    x = fmaf(tg + j - (kW - 1) + tap >= sa.start ? xr[j + tap][i] : 0.0f, w[i][tap], x);
-                acc[j][i] = x;
-                sg[j][i] = sigm_fast(x);
-                const float u = x * sg[j][i];
-                ss[j] = fmaf(u, u, ss[j]);
-                dot[j] = fmaf(u, d[j][i], dot[j]);
-            }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-            for (int j = 0; j < kG; ++j) {
-                ss[j] += __shfl_xor_sync(0xFFFFFFFFu, ss[j], o);
-                dot[j] += __shfl_xor_sync(0xFFFFFFFFu, dot[j], o);
-            }
-#pragma unroll
-        for (int j = 0; j < kG; ++j) {
-            const bool live = tg + j < a.T;
-            const float inv = rsqrtf(ss[j] + 1e-6f), inv3 = inv * inv * inv;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float s = sg[j][i], x = acc[j][i];
-                const float sgrad = s * (1.0f + x * (1.0f - s));
-                const float g = normed ? inv * d[j][i] - inv3 * (x * s) * dot[j] : d[j][i];
-                dw[kW - 1 + j][i] = live ? g * sgrad : 0.0f;
-            }
-        }
-        // dx of tokens tg + j - 3 (j = 0..3) from dacc rows tg + j - 3 .. tg + j
-#pragma unroll
-        for (int j = 0; j < kG; ++j) {
-            const int t = tg + j - (kW - 1);
-            if (t < cr.t_begin) continue;  // the first group's first three: rows before the run
-            sb.advance(a, t);
-            float o[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-            for (int s = 0; s < kW; ++s) {
-                const bool on = t + s < sb.end;
-#pragma unroll
-                for (int i = 0; i < 4; ++i) o[i] = fmaf(on ? dw[j + s][i] : 0.0f, w[i][kW - 1 - s], o[i]);
-            }
-            if (cr.valid && t < a.T) st4(dx + (int64_t)t * lddx + c, o);
-        }
-#pragma unroll
-        for (int j = 0; j < kW - 1; ++j)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                xr[j][i] = xr[kG + j][i];
-                dw[j][i] = dw[kG + j][i];
-            }
+    if (threadIdx.x < kConvRows) {
+        const int t = t0 + threadIdx.x;
+        int start = 0, end = 0;
+        if (t < a.T) seq_bounds(a, t, start, end);
+        int* seq = reinterpret_cast<int*>(stage + sl.seq);
+        seq[threadIdx.x] = start;
+        seq[kConvRows + threadIdx.x] = end;
     }
+}
+
+__device__ __forceinline__ void unpack4(uint2 u, float* v) {
+    const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+    const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+    v[0] = f0.x, v[1] = f0.y, v[2] = f1.x, v[3] = f1.y;
+}
+
+template <bool NORMED>
+__device__ __forceinline__ void conv_bwd_tile(const ConvArgs& a, const ConvBwdArgs& b, const ConvStage& sl,
+                                              unsigned char* stage, int head, int t0) {
+    const int warp = threadIdx.x >> 5, half = (threadIdx.x >> 4) & 1, hl = threadIdx.x & 15;
+    const int c = head * 128 + hl * 4;  // channels c .. c + 3 and c + 64 .. c + 67
+    const int dw = b.grp * 128, nsum = NORMED ? b.grp : 1;
+    const uint2* xs = reinterpret_cast<const uint2*>(stage);
+    float* ds = reinterpret_cast<float*>(stage + sl.ds) + hl * 4;
+    const int* seq = reinterpret_cast<const int*>(stage + sl.seq);
+    float w[8][kW];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(a.w + (c + (i >> 2) * 64 + (i & 3)) * kW);
+        w[i][0] = v.x, w[i][1] = v.y, w[i][2] = v.z, w[i][3] = v.w;
+    }
+    // phase 1: dacc over each row's first slice
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int r = j * 16 + warp * 2 + half, t = t0 + r;
+        uint2 u[kW][2];
+#pragma unroll
+        for (int tap = 0; tap < kW; ++tap) {
+            u[tap][0] = xs[(r + tap) * 32 + hl];
+            u[tap][1] = xs[(r + tap) * 32 + 16 + hl];
+        }
+        const int lim = seq[r] - (t - (kW - 1));  // taps below lim lie before the sequence's start
+        if (lim > 0) {
+#pragma unroll
+            for (int tap = 0; tap < kW; ++tap)
+                if (tap < lim) u[tap][0] = u[tap][1] = make_uint2(0u, 0u);
+        }
+        float d[8];
+        {
+            const float4 d0 = *reinterpret_cast<const float4*>(ds + r * dw);
+            const float4 d1 = *reinterpret_cast<const float4*>(ds + r * dw + 64);
+            d[0] = d0.x, d[1] = d0.y, d[2] = d0.z, d[3] = d0.w, d[4] = d1.x, d[5] = d1.y, d[6] = d1.z, d[7] = d1.w;
+        }
+        for (int e = 1; e < nsum; ++e) {
+            const float4 d0 = *reinterpret_cast<const float4*>(ds + r * dw + e * 128);
+            const float4 d1 = *reinterpret_cast<const float4*>(ds + r * dw + e * 128 + 64);
+            d[0] += d0.x, d[1] += d0.y, d[2] += d0.z, d[3] += d0.w;
+            d[4] += d1.x, d[5] += d1.y, d[6] += d1.z, d[7] += d1.w;
+        }
+        float acc[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int tap = 0; tap < kW; ++tap) {
+            float xv[8];
+            unpack4(u[tap][0], xv);
+            unpack4(u[tap][1], xv + 4);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = fmaf(xv[i], w[i][tap], acc[i]);
+        }
+        float sg[8], o[8], ss = 0.0f, dot = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            sg[i] = sigm_fast(acc[i]);
+            if (NORMED) {
+                const float uu = acc[i] * sg[i];
+                ss = fmaf(uu, uu, ss);
+                dot = fmaf(uu, d[i], dot);
+            }
+        }
+        if (NORMED) {
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) {
+                ss += __shfl_xor_sync(0xFFFFFFFFu, ss, off);
+                dot += __shfl_xor_sync(0xFFFFFFFFu, dot, off);
+            }
+            const float inv = rsqrt_ftz(ss + 1e-6f), k3 = inv * inv * inv * dot;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d[i] = inv * d[i] - k3 * (acc[i] * sg[i]);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = t < a.T ? d[i] * (sg[i] * (1.0f + acc[i] * (1.0f - sg[i]))) : 0.0f;
+        *reinterpret_cast<float4*>(ds + r * dw) = make_float4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<float4*>(ds + r * dw + 64) = make_float4(o[4], o[5], o[6], o[7]);
+    }
+    __syncthreads();
+    // phase 2: the transposed conv
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int r = j * 16 + warp * 2 + half, t = t0 + r;
+        if (r >= kConvTT || t >= a.T) continue;
+        const int end = seq[kConvRows + r];
+        float o[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int s2 = 0; s2 < kW; ++s2) {
+            if (t + s2 < end) {
+                const float4 g0 = *reinterpret_cast<const float4*>(ds + (r + s2) * dw);
+                const float4 g1 = *reinterpret_cast<const float4*>(ds + (r + s2) * dw + 64);
+                const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = fmaf(g[i], w[i][kW - 1 - s2], o[i]);
+            }
+        }
+        __nv_bfloat16* dst = b.dx + (int64_t)t * b.lddx + c;
+        st4(dst, *reinterpret_cast<const float(*)[4]>(o));
+        st4(dst + 64, *reinterpret_cast<const float(*)[4]>(o + 4));
+    }
+}
+
+__global__ void __launch_bounds__(256, 2) conv_prep_bwd_kernel(ConvArgs a, ConvBwdArgs b) {
+    extern __shared__ __align__(16) unsigned char conv_smem[];
+    const ConvStage sl = conv_stage(b.grp);
+    const int heads = a.conv_dim >> 7;
+    int tile = blockIdx.x;
+    if (tile < b.n_tiles) conv_bwd_issue(a, b, sl, conv_smem, tile);
+    cp_async_commit();
+    for (int it = 0; tile < b.n_tiles; ++it, tile += gridDim.x) {
+        if (tile + (int)gridDim.x < b.n_tiles)
+            conv_bwd_issue(a, b, sl, conv_smem + ((it + 1) & 1) * sl.bytes, tile + gridDim.x);
+        cp_async_commit();
+        cp_async_wait_but_one();
+        __syncthreads();
+        unsigned char* stage = conv_smem + (it & 1) * sl.bytes;
+        const int head = tile % heads, t0 = (tile / heads) * kConvTT;
+        if (head < 2 * a.Hg) conv_bwd_tile<true>(a, b, sl, stage, head, t0);
+        else conv_bwd_tile<false>(a, b, sl, stage, head, t0);
+        __syncthreads();  // the stage is refilled next iteration but one
+    }
+    cp_async_wait_all();
 }
 
 // ------------------------------------------------------------------------------------------- gates
@@ -674,9 +778,23 @@ extern "C" int r97b_conv_prep_bwd(const uint16_t* x, int64_t ldx, const float* c
     if (!x || !conv_w || !cu || !dq || !dk || !dv || !dx || T <= 0 || (ldx % 4) || (lddx % 4)) return R97B_EINVAL;
     if (Hg <= 0 || H <= 0 || dqk_heads < Hg || dqk_heads % Hg) return R97B_EINVAL;
     ConvArgs a{reinterpret_cast<const __nv_bfloat16*>(x), ldx, conv_w, cu, n_seq, (int)T, Hg, H, (2 * Hg + H) * 128};
-    const unsigned blocks = blocks_for(((T + kRunB - 1) / kRunB) * (a.conv_dim / 4));
-    conv_prep_bwd_kernel<<<blocks, 256, 0, as_stream(stream)>>>(a, dq, dk, dv, dqk_heads / Hg,
-                                                                reinterpret_cast<__nv_bfloat16*>(dx), lddx);
+    if (n_seq <= 0) return R97B_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(dq) | reinterpret_cast<uintptr_t>(dk) | reinterpret_cast<uintptr_t>(dv)) & 15)
+        return R97B_EINVAL;
+    if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dx)) & 7) return R97B_EINVAL;
+    ConvBwdArgs b{dq, dk, dv, dqk_heads / Hg, 0, reinterpret_cast<__nv_bfloat16*>(dx), lddx};
+    const int64_t tiles = ((T + kConvTT - 1) / kConvTT) * (a.conv_dim / 128);
+    if (tiles > INT32_MAX) return R97B_EINVAL;
+    b.n_tiles = (int)tiles;
+    const int smem = 2 * conv_stage(b.grp).bytes;
+    if (smem > 227 * 1024) return R97B_EINVAL;
+    int per_sm = 0;
+    if (cudaFuncSetAttribute(conv_prep_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, conv_prep_bwd_kernel, 256, smem) != cudaSuccess ||
+        per_sm < 1)
+        return R97B_ELAUNCH;
+    const unsigned grid = (unsigned)std::min<int64_t>(b.n_tiles, (int64_t)r97b::num_sms() * per_sm);
+    conv_prep_bwd_kernel<<<grid, 256, smem, as_stream(stream)>>>(a, b);
     return launch_status();
 }
 

@@ -11,6 +11,7 @@
 //                  dx = w g sc do - x sc^3 / n * sum(x w g do),  dz = do x sc w g'
 //                  (reference src/adjoint/host/gdn_prep.cpp:501-592)
 #include "r97b_internal.h"
+#include "fastmath.cuh"
 
 #include <cuda_bf16.h>
 
@@ -49,7 +50,7 @@ __device__ __forceinline__ float group_sum(float v) {
     return v;
 }
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
+__device__ __forceinline__ float sigmoidf_(float x) { return sigmoid_ftz(x); }
 
 // One row per group of W lanes; VPL = 8-element vectors per lane, runtime loop over the row.
 template <int W>
