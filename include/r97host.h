@@ -91,6 +91,29 @@ int r97host_adapter_read(const char* dir, int32_t nparams, const char* const* na
                          float* values, int64_t* rank, double* alpha, int32_t* dtype);
 const char* r97host_adapter_error(void);
 
+/* ---- the token-budget batcher of the training loop (include/r97/batcher.h:1-102, src/batcher.cpp) ----
+ * Plans each epoch from the sequences' token counts and (seed, epoch) exactly as the reference's
+ * r97::Batcher does -- the same sub-batches of the same sequences in the same order, step for step -- so a
+ * position saved by either resumes on the other. Sequences are named by their input index. */
+/* A batcher over n sequences of lengths[i] tokens; sequences over token_budget are skipped. Null, with the
+ * reason in r97host_batcher_error, for a budget <= 0 or devices < 1 (the reference's invalid_argument). */
+void* r97host_batcher_create(const int64_t* lengths, int64_t n, int64_t token_budget, int32_t devices,
+                             uint64_t seed);
+void r97host_batcher_destroy(void* batcher);
+/* The step at the position (Batcher::next): counts[d] = sequences of sub-batch d (devices entries at most),
+ * indices = their input indices, sub-batch after sub-batch. Returns the sub-batch count and advances; 0 at
+ * the epoch's end (the position stays there); -1 when cap cannot hold the step (nothing consumed). */
+int32_t r97host_batcher_next(void* batcher, int64_t* counts, int64_t* indices, int64_t cap);
+int64_t r97host_batcher_steps_in_epoch(void* batcher, int64_t epoch);
+void r97host_batcher_position(void* batcher, int64_t* epoch, int64_t* step);
+/* Batcher::seek: a negative epoch is the first, the step is clamped into [0, steps_in_epoch]. */
+void r97host_batcher_seek(void* batcher, int64_t epoch, int64_t step);
+void r97host_batcher_reset(void* batcher);
+/* The skipped input indices in input order (the first cap written to out); returns how many there are. */
+int64_t r97host_batcher_skipped(void* batcher, int64_t* out, int64_t cap);
+int64_t r97host_batcher_skipped_tokens(void* batcher);
+const char* r97host_batcher_error(void);
+
 #ifdef __cplusplus
 }
 #endif

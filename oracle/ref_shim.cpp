@@ -10,6 +10,7 @@
 // Only tests/, bench.py's cpu_baseline leg and __graft_entry__.smoke() load this library, and only
 // as a checker or as the timed CPU baseline; the product path never does.
 #include "r97/adjoint.h"
+#include "r97/batcher.h"
 #include "r97/loss.h"
 #include "r97/optim.h"
 
@@ -337,6 +338,57 @@ float ref_scheduled_lr(float lr, int warmup, int total, float floor_frac, int st
     cfg.total_steps = total;
     cfg.lr_floor_frac = floor_frac;
     return r97::scheduled_lr(cfg, step);
+}
+
+// The reference Batcher's plans of epochs [epoch0, epoch0 + epochs) over sequences of the given token counts
+// (src/batcher.cpp), flattened into `out`: per epoch the step count, then per step the sub-batch count and
+// per sub-batch its size and the input indices of its sequences; then the skipped indices' count and the
+// indices. Each sequence carries its own index (in its ids, or in its score bytes when it has no tokens).
+// Returns the number of int64 values (-1 on a throw, message in ref_last_error); writes them when cap allows.
+int64_t ref_batcher_plan(const int64_t* lengths, int64_t n, int64_t budget, int devices, uint64_t seed,
+                         int64_t epoch0, int epochs, int64_t* out, int64_t cap) {
+    try {
+        g_error.clear();
+        std::vector<r97::TokenSeq> seqs((size_t)n);
+        for (int64_t i = 0; i < n; ++i) {
+            seqs[(size_t)i].ids.assign((size_t)lengths[i], (int32_t)i);
+            if (lengths[i] == 0) {
+                seqs[(size_t)i].score.resize(4);
+                std::memcpy(seqs[(size_t)i].score.data(), &i, 4);
+            }
+        }
+        r97::BatcherConfig cfg;
+        cfg.token_budget = budget;
+        cfg.devices = devices;
+        cfg.seed = seed;
+        r97::Batcher b(std::move(seqs), cfg);
+        std::vector<int64_t> flat;
+        auto index_of = [](const r97::TokenSeq& t) -> int64_t {
+            if (!t.ids.empty()) return t.ids[0];
+            int32_t i = 0;
+            std::memcpy(&i, t.score.data(), 4);
+            return i;
+        };
+        for (int64_t e = epoch0; e < epoch0 + epochs; ++e) {
+            b.seek({e, 0});
+            flat.push_back(b.steps_in_epoch(e));
+            std::vector<r97::Batch> step;
+            while (b.next(&step)) {
+                flat.push_back((int64_t)step.size());
+                for (const auto& sub : step) {
+                    flat.push_back((int64_t)sub.size());
+                    for (const auto& t : sub) flat.push_back(index_of(t));
+                }
+            }
+        }
+        flat.push_back((int64_t)b.skipped().size());
+        for (size_t i : b.skipped()) flat.push_back((int64_t)i);
+        if (out && cap >= (int64_t)flat.size()) std::memcpy(out, flat.data(), flat.size() * sizeof(int64_t));
+        return (int64_t)flat.size();
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return -1;
+    }
 }
 
 }  // extern "C"
