@@ -491,6 +491,27 @@ typedef struct R97bCastSeg {
  * master per adapter tensor and hands the device its bf16 view, src/delta_lora.cpp). */
 int r97b_cast_segments(const R97bCastSeg* segs, int32_t nseg, int64_t units, void* stream);
 
+/* ---- the w8a8 trunk's activation quantisers (reference src/adjoint/host/quant.cpp:43-370, the
+ * quant_act_i8g / had_quant_act_i8g records; docs/adjoints/quant.md s1, s3) ----
+ * Per row and group of `group` columns: v = the group, rotated by the unnormalised Walsh-Hadamard matrix of
+ * order `group` (W W = group I) when `rotate`; s = amax|v| / 127 (1 for an all-zero group); codes =
+ * rint(clamp(v / s, -127, 127)), nearest even, as int8; scale[row, g] = s (f32).
+ * x: bf16 [rows, n] (row pitch ldx); codes: int8 [rows, n] (pitch ldc); scale: f32 [rows, ceil(n / group)].
+ * rotate: group a power of two of at most 256 dividing n, n a multiple of 4, x rows 8-byte (16-byte for
+ * 256) aligned, codes rows 4-byte (8-byte) aligned. Not rotated: group <= 0 or > n is one group a row, and a
+ * group that does not divide n leaves a short last group. R97B_EINVAL outside these rules (the reference
+ * twin's std::invalid_argument). */
+int r97b_quant_act_i8g(const uint16_t* x, int64_t ldx, int64_t rows, int64_t n, int64_t group, int32_t rotate,
+                       int8_t* codes, int64_t ldc, float* scale, void* stream);
+/* The straight-through adjoint (quant.cpp quant_adjoint): dx = W (m . g / s), m = 0 where the clamp engaged
+ * (|v / s| > 127, v recomputed from x), W the same rotation (the identity when not rotated); the scale's
+ * cotangent is dropped. g: f32 [rows, n] (pitch ldg), the codes' cotangent; scale: the forward's; dx: f32
+ * [rows, n] (pitch lddx), written, or added to when `accumulate`. g and dx rows 16-byte aligned on the
+ * rotated path. */
+int r97b_quant_act_i8g_bwd(const uint16_t* x, int64_t ldx, int64_t rows, int64_t n, int64_t group, int32_t rotate,
+                           const float* scale, const float* g, int64_t ldg, float* dx, int64_t lddx,
+                           int32_t accumulate, void* stream);
+
 /* How many kernels this library has launched in this process (a diagnostic for the bench). */
 uint64_t r97b_launch_count(void);
 

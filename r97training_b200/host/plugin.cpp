@@ -14,6 +14,7 @@ namespace r97b_host {
 void register_linear_rows();
 void register_norm_rows();
 void register_gdn_rows();
+void register_quant_rows();
 
 namespace {
 
@@ -64,6 +65,7 @@ struct Registration {
         register_linear_rows();
         register_norm_rows();
         register_gdn_rows();
+        register_quant_rows();
         if (r97::head_ce_register) r97::head_ce_register(head_ce_chunk);
         if (r97::register_vocab_head_kernels)
             r97::register_vocab_head_kernels(r97::VocabHeadKernels{vocab_head_transpose, vocab_head_cast});

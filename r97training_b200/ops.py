@@ -432,3 +432,29 @@ def cast_f32_bf16(src, dst, stream=None):
     rows, cols = src.shape
     check(lib().r97b_cast_f32_bf16(_ptr(src), src.stride(0), _ptr(dst), dst.stride(0), rows, cols,
                                    _stream(stream)), "r97b_cast_f32_bf16")
+
+
+def quant_act_i8g(x, group, rotate=True, codes=None, scale=None, stream=None):
+    """The w8a8 trunk's activation quantiser (had_quant_act_i8g when rotate, else quant_act_i8g): x bf16
+    [rows, n] -> (codes int8 [rows, n], scale f32 [rows, ceil(n / group)])."""
+    rows, n = x.shape
+    t = group if (rotate or 0 < group <= n) else n
+    ngrp = (n + t - 1) // t
+    if codes is None:
+        codes = torch.empty((rows, n), dtype=torch.int8, device=x.device)
+    if scale is None:
+        scale = torch.empty((rows, ngrp), dtype=torch.float32, device=x.device)
+    check(lib().r97b_quant_act_i8g(_ptr(x), x.stride(0), rows, n, group, 1 if rotate else 0, _ptr(codes),
+                                   codes.stride(0), _ptr(scale), _stream(stream)), "r97b_quant_act_i8g")
+    return codes, scale
+
+
+def quant_act_i8g_bwd(x, group, scale, g, rotate=True, dx=None, accumulate=False, stream=None):
+    """Its straight-through adjoint: the codes' cotangent g (f32 [rows, n]) -> dx f32 [rows, n]."""
+    rows, n = x.shape
+    if dx is None:
+        dx = torch.empty((rows, n), dtype=torch.float32, device=x.device)
+    check(lib().r97b_quant_act_i8g_bwd(_ptr(x), x.stride(0), rows, n, group, 1 if rotate else 0, _ptr(scale),
+                                       _ptr(g), g.stride(0), _ptr(dx), dx.stride(0), 1 if accumulate else 0,
+                                       _stream(stream)), "r97b_quant_act_i8g_bwd")
+    return dx

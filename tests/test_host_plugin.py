@@ -13,7 +13,8 @@ from r97training_b200 import build as B
 from tests.plugin_util import plugin
 
 # op -> the frozen operand positions the reference registers for it (reference linear.cpp:444-457,
-# lora.cpp:534-538, gdn_kkt.cpp:355, gdn_scan.cpp:584, gdn_prep.cpp:597-600, elementwise.cpp:687)
+# lora.cpp:534-538, gdn_kkt.cpp:355, gdn_scan.cpp:584, gdn_prep.cpp:597-600, elementwise.cpp:687; the quant
+# family's two int8 ops have none, quant.cpp)
 FROZEN = {
     "gemm_nt": [1],
     "lora_shrink": [1, 2, 3],
@@ -23,6 +24,8 @@ FROZEN = {
     "gdn_gated_rmsnorm": [2],
     "gdn_kkt_solve": [3],
     "gdn_chunk_scan": [6, 7, 10],
+    "quant_act_i8g": [],
+    "had_quant_act_i8g": [],
 }
 
 
