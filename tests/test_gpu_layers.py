@@ -17,7 +17,10 @@ def _bf(a):
     return torch.from_numpy(np.asarray(a, np.float32)).to(torch.bfloat16)
 
 
-@pytest.mark.parametrize("lens,Hg,H", [((200, 37, 100), 2, 4), ((4096,), 4, 8)])
+@pytest.mark.parametrize("lens,Hg,H", [((200, 37, 100), 2, 4), ((4096,), 4, 8),
+                                       ((1, 2, 3, 5, 1, 29, 30, 4), 2, 2),  # sequences shorter than the taps and the tiles
+                                       ((7,), 1, 4),                        # one tile, partly past T; four value heads a key head
+                                       ((58, 29, 87), 3, 6)])               # tile-aligned sequence ends
 def test_conv_prep_fwd_bwd(cuda, lens, Hg, H):
     rs = np.random.RandomState(sum(lens))
     K = 128
