@@ -29,12 +29,20 @@
 // Sequences are ragged (cu_seqlens); a sequence's last chunk may be short, and its padded rows are zero
 // so they add nothing. Head dims K = V = 128 and the chunk of 64 are fixed here.
 #include "r97b_internal.h"
+#include "fastmath.cuh"
 #include "wmma16.cuh"
 
 #include <cuda_bf16.h>
 #include <math.h>
 
 namespace r97b {
+namespace {
+// e^x for the decay factors: one ex2 of x log2 e (flush-to-zero). The arguments are within-chunk cumulative
+// log decays or differences of them, at most 0 for a decaying gate, so the result lies in (0, 1]; the
+// approximation's relative error (2 ulp, plus |x| times the rounding of x log2 e) stays below that of the
+// ~16-bit split operands the products carry it into.
+__device__ __forceinline__ float gexp(float x) { return ex2_ftz(x * 1.4426950408889634f); }
+}  // namespace
 namespace {
 
 using bf16 = __nv_bfloat16;
@@ -290,7 +298,7 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
         acc_for<16, 32>(acc, m0, n0, [&](int r, int l, float& x) {
             // only the chunk's own rows: a padded row's g is 0, and e^{0 - g_l} can overflow to inf, whose
             // 0 * inf the blocked inverse would carry into every row
-            Ms[r * F65 + l] = (l < r && r < n) ? bs[r] * x * expf(gs[r] - gs[l]) : 0.0f;
+            Ms[r * F65 + l] = (l < r && r < n) ? bs[r] * x * gexp(gs[r] - gs[l]) : 0.0f;
         });
         __syncthreads();
         // A = (I + M)^-1 by blocks: the four 16x16 diagonal blocks by forward substitution (a warp each),
@@ -301,7 +309,7 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
         const int i = idx >> 6, j = idx & 63;
         const float a = As[i * F65 + j];
         if (i < n && !given) A[((tok0 + i) * dm.H + h) * L + j] = a;
-        const float e = bs[j] * expf(gs[j]);
+        const float e = bs[j] * gexp(gs[j]);
         put_split(a1h, a1l, i * kP64 + j, a * e);
         put_split(a2h, a2l, i * kP64 + j, a * bs[j]);
     }
@@ -402,13 +410,13 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
             acc_pairs<16, 32>(vm0, vn0, [&](int i, int e, int a, int b, int hh) {
                 const float v0 = st.us[i * U68 + e] - acc[a][b][2 * hh];
                 const float v1 = st.us[i * U68 + e + 1] - acc[a][b][2 * hh + 1];
-                const float sc = i < n ? expf(gl - st.gs[i]) : 0.0f;
+                const float sc = i < n ? gexp(gl - st.gs[i]) : 0.0f;
                 if (i < n) put_split2(Vpp.hi, Vpp.lo, ((tok0 + i) * dm.H + h) * D + e0 + e, v0, v1);
                 put_split2(vh, vl, i * P64 + e, v0 * sc, v1 * sc);
             });
         }
         __syncthreads();
-        const float el = expf(gl);
+        const float el = gexp(gl);
 #pragma unroll
         for (int a = 0; a < 2; ++a)
 #pragma unroll
@@ -464,8 +472,8 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
         bf16* P_lo = P_hi + (int64_t)dm.n_chunks * dm.H * L * L;
         const int64_t pbase = ((int64_t)c * dm.H + h) * L * L;
         acc_pairs<16, 32>(m0, n0, [&](int r, int l, int i, int j, int hh) {
-            const float p0 = (l <= r && r < n) ? acc[i][j][2 * hh] * expf(gs[r] - gs[l]) : 0.0f;
-            const float p1 = (l + 1 <= r && r < n) ? acc[i][j][2 * hh + 1] * expf(gs[r] - gs[l + 1]) : 0.0f;
+            const float p0 = (l <= r && r < n) ? acc[i][j][2 * hh] * gexp(gs[r] - gs[l]) : 0.0f;
+            const float p1 = (l + 1 <= r && r < n) ? acc[i][j][2 * hh + 1] * gexp(gs[r] - gs[l + 1]) : 0.0f;
             put_split2(P_hi, P_lo, pbase + r * L + l, p0, p1);
             put_split2(ph, pl, r * kP64 + l, p0, p1);
         });
@@ -478,7 +486,7 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
     mma_split_b<16, 64, 128, false, true>(qsacc, qs, kP128, sh, sl, kP128, m0, n0);
     mma_split_ab<16, 64, 64, false, true>(pvacc, ph, pl, kP64, vh, vl, kP128, m0, n0);
     const int lane = threadIdx.x & 31, gq = lane >> 2;
-    const float eg0 = expf(gs[m0 + gq]), eg1 = expf(gs[m0 + gq + 8]);
+    const float eg0 = gexp(gs[m0 + gq]), eg1 = gexp(gs[m0 + gq + 8]);
     acc_walk<16, 64>(m0, n0, [&](int r, int e, int i, int j, int q) {
         const float y = dm.scale * (qsacc[i][j][q] * ((q >> 1) ? eg1 : eg0) + pvacc[i][j][q]);
         if (r < n) o[((tok0 + r) * dm.H + h) * D + e] = __float2bfloat16_rn(y);
@@ -593,7 +601,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
         const float gl = et.gs[n - 1];
         for (int idx = threadIdx.x; idx < L * VSB / 2; idx += blockDim.x) {
             const int i = idx >> 5, e = (idx & 31) * 2;
-            const float eg = expf(et.gs[i]);
+            const float eg = gexp(et.gs[i]);
             const float2 d2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(et.dos + i * kP64 + e));
             put_split2(egh, egl, i * kP64 + e, d2.x * eg, d2.y * eg);
         }
@@ -605,7 +613,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
             mma_split_a<16, 32, 64, true, true>(a1, et.ph, et.pl, kP64, et.dos, kP64, vm0, vn0);
             mma_split_b<16, 32, 128, false, true>(a2, et.ks, kP128, dsh, dsl, kP64, vm0, vn0);
             acc_pairs<16, 32>(vm0, vn0, [&](int j, int e, int a, int b, int hh) {
-                const float sc = j < n ? expf(gl - et.gs[j]) : 0.0f;
+                const float sc = j < n ? gexp(gl - et.gs[j]) : 0.0f;
                 const float d0 = j < n ? dm.scale * a1[a][b][2 * hh] + sc * a2[a][b][2 * hh] : 0.0f;
                 const float d1 = j < n ? dm.scale * a1[a][b][2 * hh + 1] + sc * a2[a][b][2 * hh + 1] : 0.0f;
                 if (j < n) put_split2(dVpp.hi, dVpp.lo, ((tok0 + j) * dm.H + h) * D + e0 + e, d0, d1);
@@ -615,7 +623,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
         __syncthreads();  // dV' written; chunk c's P, k, dO and g are no longer read
         if (c > c0) b1_issue_early(*early, dm, k, P_hi, P_lo, dO, g, c - 1, h, hk, e0);
         // dS = e^{gL} dS + scale q^T (e^g dO) - w^T dV'
-        const float el = expf(gl);
+        const float el = gexp(gl);
         float t1[2][4][4], t2[2][4][4];
         acc_zero<32, 32>(t1);
         acc_zero<32, 32>(t2);
@@ -680,7 +688,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
         float p0 = 0.0f, p1 = 0.0f;
         acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
             float& x = dq[i][j][q];
-            x *= dm.scale * expf(gs[r]);
+            x *= dm.scale * gexp(gs[r]);
             const float t = __bfloat162float(qs[r * kP128 + d]) * x;
             if (q >> 1) p1 += t; else p0 += t;
         });
@@ -731,7 +739,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
         float p0 = 0.0f, p1 = 0.0f;
         acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
             float& x = dk[i][j][q];
-            x *= r < n ? expf(gl - gs[r]) : 0.0f;
+            x *= r < n ? gexp(gl - gs[r]) : 0.0f;
             const float t = __bfloat162float(xs[r * kP128 + d]) * x;
             if (q >> 1) p1 += t; else p0 += t;
         });
@@ -747,7 +755,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
     if (threadIdx.x == 0) {
         float s = 0.0f;
         for (int i = 0; i < 8; ++i) s += red[i];
-        dgs[n - 1] += expf(gl) * s;
+        dgs[n - 1] += gexp(gl) * s;
     }
     __syncthreads();
     acc_for<16, 64>(dq, m0, n0, [&](int r, int d, float& x) {
@@ -788,7 +796,7 @@ __device__ __forceinline__ void kkt_adjoint(const bf16* ah, const bf16* al, bf16
             const float gg = dm_ * bs[r] * kh;
             if (q >> 1) { b1 += dm_ * kh; g1 += gg; } else { b0 += dm_ * kh; g0 += gg; }
             cs[j][q & 1] -= gg;  // zero off the strict lower block
-            put_split(th, tl, r * kP64 + l, on ? dm_ * bs[r] * expf(gs[r] - gs[l]) : 0.0f);
+            put_split(th, tl, r * kP64 + l, on ? dm_ * bs[r] * gexp(gs[r] - gs[l]) : 0.0f);
         });
         colsum_add(cs, pn0, dgs);
         b0 = quad_sum(b0);
@@ -877,7 +885,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
             const bool on = l <= r && r < n;
             // e^{g_r - g_l} only where l <= r: above the diagonal it can overflow (g decreases within a
             // chunk), and 0 * inf would poison the sums
-            const float phi = on ? expf(gs[r] - gs[l]) : 0.0f;
+            const float phi = on ? gexp(gs[r] - gs[l]) : 0.0f;
             const float dpv = on ? dm.scale * dp[i][j][q] : 0.0f;
             const float dd = dpv * qk[i][j][q] * phi;
             if (q >> 1) r1 += dd; else r0 += dd;
@@ -913,7 +921,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
         mma_split_a<16, 32, 128, false, false>(a1, xh, xl, kP128, ks, kP128, pm0, pn0);
         mma_split_a<16, 32, 128, false, false>(a2, dvh, dvl, kP128, qv, kP128, pm0, pn0);
         acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
-            const float da = bs[l] * (expf(gs[l]) * a1[i][j][q] + a2[i][j][q]);
+            const float da = bs[l] * (gexp(gs[l]) * a1[i][j][q] + a2[i][j][q]);
             if (split) {  // the scan's own cotangent of A, its lower triangle with the diagonal
                 if (r < n) dA_out[((tok0 + r) * dm.H + h) * L + l] = l <= r ? da : 0.0f;
             } else {
@@ -931,13 +939,13 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
             const float x = acc[i][j][q];
             const float t = __bfloat162float(ks[r * kP128 + d]) * x;
             if (q >> 1) p1 += t; else p0 += t;
-            dka[i][j][q] += bs[r] * expf(gs[r]) * x;
+            dka[i][j][q] += bs[r] * gexp(gs[r]) * x;
         });
         p0 = quad_sum(p0);
         p1 = quad_sum(p1);
         if ((lane & 3) == 0) {
             const int ra = m0 + (lane >> 2), rb = ra + 8;
-            const float ea = expf(gs[ra]), eb = expf(gs[rb]);
+            const float ea = gexp(gs[ra]), eb = gexp(gs[rb]);
             atomicAdd(&dbs[ra], ea * p0);
             atomicAdd(&dgs[ra], bs[ra] * ea * p0);
             atomicAdd(&dbs[rb], eb * p1);
@@ -1025,7 +1033,7 @@ __global__ void __launch_bounds__(256) gdn_kkt_bwd(Dims dm, const bf16* __restri
         const int pm0 = (warp & 3) * 16, pn0 = (warp >> 2) * 32;
         warp_mma<16, 32, 128, false, false>(kk, ks, kP128, ks, kP128, pm0, pn0);
         acc_for<16, 32>(kk, pm0, pn0, [&](int r, int l, float& x) {
-            Cs[r * F65 + l] = (l < r && r < n) ? x * expf(gs[r] - gs[l]) : 0.0f;
+            Cs[r * F65 + l] = (l < r && r < n) ? x * gexp(gs[r] - gs[l]) : 0.0f;
         });
     }
     __syncthreads();
