@@ -16,6 +16,7 @@
 // No cluster multicast anywhere: every CTA loads its own tiles.
 #include "sm100.cuh"
 #include "r97b_internal.h"
+#include "fastmath.cuh"
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -52,7 +53,7 @@ struct KernelArgs {
 
 // SwiGLU's pieces, with the arithmetic of the standalone SwiGLU kernels (layers.cu), so the fused
 // epilogues produce the same bits.
-__device__ __forceinline__ float sw_sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float sw_sigm(float x) { return sigmoid_ftz(x); }
 __device__ __forceinline__ float sw_silu(float x) { return x * sw_sigm(x); }
 __device__ __forceinline__ float sw_silu_grad(float x) {
     const float s = sw_sigm(x);

@@ -19,7 +19,7 @@
 namespace r97b {
 namespace {
 
-__device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+__device__ __forceinline__ float sigm(float x) { return sigmoid_ftz(x); }
 __device__ __forceinline__ float silu(float x) { return x * sigm(x); }
 __device__ __forceinline__ float silu_grad(float x) {
     const float s = sigm(x);

@@ -15,6 +15,7 @@
 // CE follows the reference's ce_position (src/loss.cpp:21-39) and its chunk kernel's contract
 // (include/r97/head.h:28-50, HeadChunk); the KL objective has no counterpart in the reference.
 #include "r97b_internal.h"
+#include "fastmath.cuh"
 
 #include <cuda_bf16.h>
 #include <math.h>
@@ -24,6 +25,9 @@ namespace {
 
 constexpr int kThreads = 512;
 
+// e^x as one flush-to-zero ex2 of x log2 e (the arguments are logits less a running max: <= 0).
+__device__ __forceinline__ float fexp(float x) { return ex2_ftz(x * 1.4426950408889634f); }
+
 struct Acc {
     float m, s;       // student: running max and sum of exp(x - m)
     float mt, st, u;  // teacher: running max, sum of exp(t - mt), sum of exp(t - mt) * (t - s)
@@ -31,11 +35,11 @@ struct Acc {
 
 __device__ __forceinline__ void merge(Acc& a, const Acc& b) {
     const float m = fmaxf(a.m, b.m);
-    a.s = (a.m == -INFINITY ? 0.0f : a.s * __expf(a.m - m)) + (b.m == -INFINITY ? 0.0f : b.s * __expf(b.m - m));
+    a.s = (a.m == -INFINITY ? 0.0f : a.s * fexp(a.m - m)) + (b.m == -INFINITY ? 0.0f : b.s * fexp(b.m - m));
     a.m = m;
     const float mt = fmaxf(a.mt, b.mt);
-    const float fa = a.mt == -INFINITY ? 0.0f : __expf(a.mt - mt);
-    const float fb = b.mt == -INFINITY ? 0.0f : __expf(b.mt - mt);
+    const float fa = a.mt == -INFINITY ? 0.0f : fexp(a.mt - mt);
+    const float fb = b.mt == -INFINITY ? 0.0f : fexp(b.mt - mt);
     a.st = a.st * fa + b.st * fb;
     a.u = a.u * fa + b.u * fb;
     a.mt = mt;
@@ -75,9 +79,9 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
 #pragma unroll
         for (int k = 1; k < 8; ++k) mx = fmaxf(mx, v[k]);
         const float m = fmaxf(a.m, mx);
-        float s = a.m == -INFINITY ? 0.0f : a.s * __expf(a.m - m);
+        float s = a.m == -INFINITY ? 0.0f : a.s * fexp(a.m - m);
 #pragma unroll
-        for (int k = 0; k < 8; ++k) s += __expf(v[k] - m);
+        for (int k = 0; k < 8; ++k) s += fexp(v[k] - m);
         a.m = m;
         a.s = s;
         if (kTeacher) {
@@ -87,11 +91,11 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
 #pragma unroll
             for (int k = 1; k < 8; ++k) tm = fmaxf(tm, tv[k]);
             const float mt = fmaxf(a.mt, tm);
-            const float f = a.mt == -INFINITY ? 0.0f : __expf(a.mt - mt);
+            const float f = a.mt == -INFINITY ? 0.0f : fexp(a.mt - mt);
             float st = a.st * f, u = a.u * f;
 #pragma unroll
             for (int k = 0; k < 8; ++k) {
-                const float e = __expf(tv[k] - mt);
+                const float e = fexp(tv[k] - mt);
                 st += e;
                 u = fmaf(e, tv[k] - v[k], u);
             }
@@ -151,9 +155,9 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
         float o[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
-            const float p = __expf(v[k] - lse);
+            const float p = fexp(v[k] - lse);
             float d = ce_w * p;
-            if (kTeacher) d += w_kl * (p - __expf(tv[k] - lse_t));
+            if (kTeacher) d += w_kl * (p - fexp(tv[k] - lse_t));
             if (targets && (int64_t)i * 8 + k == target) d -= ce_w;
             o[k] = d * sc;
         }
@@ -164,9 +168,9 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
         reinterpret_cast<uint4*>(g)[i] = u;
     }
     for (int64_t j = nvec * 8 + threadIdx.x; j < vocab; j += kThreads) {
-        const float p = __expf(__bfloat162float(x[j]) - lse);
+        const float p = fexp(__bfloat162float(x[j]) - lse);
         float d = ce_w * p;
-        if (kTeacher) d += w_kl * (p - __expf(__bfloat162float(t[j]) - lse_t));
+        if (kTeacher) d += w_kl * (p - fexp(__bfloat162float(t[j]) - lse_t));
         if (targets && j == target) d -= ce_w;
         g[j] = __float2bfloat16_rn(d * sc);
     }
