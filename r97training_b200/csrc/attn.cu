@@ -25,6 +25,7 @@
 // longest-first in a snake order across the CTAs. No cluster multicast anywhere.
 #include "sm100.cuh"
 #include "r97b_internal.h"
+#include "fastmath.cuh"
 
 #include <cuda_bf16.h>
 
@@ -297,7 +298,7 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
 #pragma unroll
                     for (int e = 0; e < 32; ++e) {
                         const int kpos = j * kBM + cc * 32 + e;
-                        const float pe = kpos <= qpos ? exp2f(__uint_as_float(rs[e]) * sl2 - lse2) : 0.0f;
+                        const float pe = kpos <= qpos ? ex2_ftz(__uint_as_float(rs[e]) * sl2 - lse2) : 0.0f;
                         // dS is formed from P as stored (bf16), the P that dV reads
                         const float pb = __bfloat162float(__float2bfloat16_rn(pe));
                         pv[e] = pe;
