@@ -217,8 +217,15 @@ __device__ __forceinline__ void epilogue32(const KernelArgs& args, int mode, int
         }
     } else if (mode == kEpiAtomicF32) {
         float* op = reinterpret_cast<float*>(args.out) + (int64_t)m * args.ldo + n0;
-        for (int i = 0; i < 32; ++i)
-            if (full || n0 + i < args.N) atomicAdd(op + i, v[i]);
+        if (full && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
+            // one 16-byte vector reduction per four columns: a quarter of the L2 atomic operations
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+                atomicAdd(reinterpret_cast<float4*>(op + i), make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]));
+        } else {
+            for (int i = 0; i < 32; ++i)
+                if (n0 + i < args.N) atomicAdd(op + i, v[i]);
+        }
     } else {  // kEpiAtomicF32T: out[n, m] += acc[m, n]
         float* op = reinterpret_cast<float*>(args.out) + (int64_t)n0 * args.ldo + m;
         for (int i = 0; i < 32; ++i)

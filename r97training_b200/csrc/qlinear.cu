@@ -22,12 +22,18 @@ void narrow_tiling(int64_t m, int64_t n, int64_t k, int* bn, int* splits) {
     *splits = (units < 100 && (n <= 64 || k >= 8192)) ? 2 : 1;
 }
 
-// (bn, splits) of an adapter-gradient product (f32 atomics, reduction over the tokens).
-void grad_tiling(int64_t m, int64_t n, int* bn, int* splits) {
+// (bn, splits) of an adapter-gradient product (f32 atomics, reduction over k tokens): the split count s
+// (at most 8, and k / s >= 1024) that minimises ceil(tiles s / SMs) / s, the waves of work a tile's share
+// takes, ties to the fewer splits.
+void grad_tiling(int64_t m, int64_t n, int64_t k, int* bn, int* splits) {
     *bn = n >= 128 ? 128 : 64;
     const int64_t tiles = cdiv(m, 128) * cdiv(n, *bn);
-    int s = (int)((128.0 / (double)tiles) + 0.5);
-    *splits = s < 1 ? 1 : (s > 4 ? 4 : s);
+    const int64_t sms = r97b::num_sms();
+    const int smax = (int)std::max<int64_t>(1, std::min<int64_t>(8, k / 1024));
+    int best = 1;
+    for (int s = 2; s <= smax; ++s)
+        if (cdiv(tiles * s, sms) * best < cdiv(tiles * best, sms) * s) best = s;
+    *splits = best;
 }
 
 R97bMat mat(const void* p, int64_t ld, int mn) {
@@ -140,7 +146,7 @@ extern "C" int r97b_qlinear_lora_bwd(const R97bQLinearLoraBwd* a, void* stream) 
     da.K1 = a->M;
     da.a1 = mat(a->x, a->K, 1);
     da.b1 = mat(a->dt, a->rank, 1);
-    grad_tiling(a->K, a->rank, &bn, &sp);
+    grad_tiling(a->K, a->rank, a->M, &bn, &sp);
     da.bn = bn;
     da.splits = sp;
     da.mode = R97B_EPI_ATOMIC_F32T;
@@ -155,7 +161,7 @@ extern "C" int r97b_qlinear_lora_bwd(const R97bQLinearLoraBwd* a, void* stream) 
     db.K1 = a->M;
     db.a1 = mat(a->dy, a->N, 1);
     db.b1 = mat(a->t, a->rank, 1);
-    grad_tiling(a->N, a->rank, &bn, &sp);
+    grad_tiling(a->N, a->rank, a->M, &bn, &sp);
     db.bn = bn;
     db.splits = sp;
     db.mode = R97B_EPI_ATOMIC_F32;

@@ -394,12 +394,12 @@ class TrainStep:
                      addend=swiglu_gu)
         else:
             ops.gemm(dy, W, dx_out, b_mn=True, a2=dt, b2=ad.a_bf[(li, g.name)], N=g.k)
-        bn, splits = ops.grad_tiling(g.k, g.r_all * r)
+        bn, splits = ops.grad_tiling(g.k, g.r_all * r, dy.shape[0])
         ops.gemm(x, dt, ad.a_view(ad.g, g), a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32T, splits=splits,
                  bn=bn, M=g.k, N=g.r_all * r)
         col = 0
         for i, (_, n) in enumerate(g.projs):
-            bn, splits = ops.grad_tiling(n, r)
+            bn, splits = ops.grad_tiling(n, r, dy.shape[0])
             ops.gemm(dy[:, col:col + n], t[:, i * r:(i + 1) * r], ad.b_view(ad.g, g, i), a_mn=True, b_mn=True,
                      mode=ops.EPI_ATOMIC_F32, splits=splits, bn=bn, M=n, N=r)
             col += n

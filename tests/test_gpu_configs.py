@@ -52,10 +52,10 @@ def test_config1_lora_linear_full_size(cuda):
     dx = torch.empty((M, K), dtype=torch.bfloat16, device=cuda)
     ops.gemm(dy, Wd, dx, b_mn=True, a2=dt, b2=a, N=K)
     dA = torch.zeros((r, K), dtype=torch.float32, device=cuda)
-    bn, sp = ops.grad_tiling(K, r)
+    bn, sp = ops.grad_tiling(K, r, M)
     ops.gemm(x, dt, dA, a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32T, splits=sp, bn=bn, M=K, N=r)
     dB = torch.zeros((N, r), dtype=torch.float32, device=cuda)
-    bn, sp = ops.grad_tiling(N, r)
+    bn, sp = ops.grad_tiling(N, r, M)
     ops.gemm(dy, t, dB, a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32, splits=sp, bn=bn, M=N, N=r)
     torch.cuda.synchronize()
     Wn = to_np(Wd)

@@ -124,22 +124,35 @@ def test_gemm_dx_form_mn_major_weight(cuda):
     assert_close_bf16(to_np(out), want, rel=4e-3, what="dx")
 
 
-@pytest.mark.parametrize("transposed", [False, True])
-def test_gemm_split_k_atomic(cuda, transposed):
-    # the adapter-gradient form: reduce over tokens (both operands MN-major), split-K into f32
-    rs = np.random.RandomState(7)
-    T, K, r = 2048, 256, 64
+@pytest.mark.parametrize("transposed,T,splits,r", [(False, 2048, 4, 64), (True, 2048, 4, 64), (False, 8192, 3, 64),
+                                                    (True, 8192, 3, 64), (False, 8192, 8, 64), (True, 8192, 5, 192),
+                                                    (False, 1000, 3, 64)])
+def test_gemm_split_k_atomic(cuda, transposed, T, splits, r):
+    # the adapter-gradient form: reduce over tokens (both operands MN-major), split-K into f32 -- splits that
+    # do not divide the token blocks evenly, the vector-atomic row-major epilogue and a ragged token count
+    rs = np.random.RandomState(7 + T + splits)
+    K = 256
     X, dt = _bf(rs, (T, K)), _bf(rs, (T, r))
     if transposed:   # dA [r, K] += (X^T dt)^T
         out = torch.zeros((r, K), dtype=torch.float32, device=cuda)
-        ops.gemm(X.to(cuda), dt.to(cuda), out, a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32T, splits=4)
+        ops.gemm(X.to(cuda), dt.to(cuda), out, a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32T, splits=splits)
         want = dt.double().numpy().T @ X.double().numpy()
     else:            # [K, r]
         out = torch.zeros((K, r), dtype=torch.float32, device=cuda)
-        ops.gemm(X.to(cuda), dt.to(cuda), out, a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32, splits=4)
+        ops.gemm(X.to(cuda), dt.to(cuda), out, a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32, splits=splits)
         want = X.double().numpy().T @ dt.double().numpy()
     torch.cuda.synchronize()
     assert rel_l2(to_np(out), want) < 1e-5
+
+
+def test_grad_tiling_rule():
+    """The adapter-gradient tiling at the config-5 shapes: the split counts measured best on B200."""
+    assert ops.grad_tiling(12288, 64) == (64, 3)
+    assert ops.grad_tiling(4096, 64) == (64, 4)
+    assert ops.grad_tiling(8192, 64) == (64, 2)
+    assert ops.grad_tiling(4096, 192) == (128, 2)
+    assert ops.grad_tiling(64, 64) == (64, 8)
+    assert ops.grad_tiling(64, 64, K=2048) == (64, 2)   # K / s >= 1024
 
 
 @pytest.mark.parametrize("b_mn,bn,splits", [(False, 64, 2), (True, 64, 3), (False, 128, 2), (True, 256, 4),
