@@ -227,14 +227,15 @@ def test_gated_rmsnorm(cuda, sig):
 
 # ----------------------------------------------------------------------------- CE / KLD
 
-@pytest.mark.parametrize("vocab", [1000, 151936])
-def test_ce_kld(cuda, vocab):
-    rs = np.random.RandomState(vocab % 1000)
-    rows = 17
+@pytest.mark.parametrize("vocab,rows", [(1000, 17), (151936, 17), (1003, 700)])
+def test_ce_kld(cuda, vocab, rows):
+    # 700 rows with a ragged vocabulary (no 16-byte rows: one value a load)
+    rs = np.random.RandomState(vocab % 1000 + rows)
     s = _bf(rs, (rows, vocab), 2.0)
     t = _bf(rs, (rows, vocab), 2.0)
     tg = rs.randint(0, vocab, size=rows).astype(np.int32)
     tg[3] = -1
+    tg[rows - 2] = -1
     sd = s.to(cuda)
     grad = torch.empty_like(sd)
     lce, lkl = ops.ce_kld(sd, torch.from_numpy(tg).to(cuda), t.to(cuda), grad=grad, grad_scale=0.5, w_ce=1.0,
