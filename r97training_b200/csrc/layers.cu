@@ -564,12 +564,25 @@ struct QkArgs {
     float eps;
 };
 
+// q = row / d, r = row % d in 32-bit arithmetic when row fits (a 64-bit division is a long subroutine).
+__device__ __forceinline__ void split_row(int64_t row, int d, int& q, int& r) {
+    if (row <= 0xFFFFFFFFll) {
+        const uint32_t qq = (uint32_t)row / (uint32_t)d;
+        q = (int)qq;
+        r = (int)((uint32_t)row - qq * (uint32_t)d);
+    } else {
+        q = (int)(row / d);
+        r = (int)(row % d);
+    }
+}
+
 __global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(QkArgs a, __nv_bfloat16* __restrict__ out) {
     const int lane = threadIdx.x & 31;
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (row >= (int64_t)a.T * a.heads) return;
-    const int t = (int)(row / a.heads), h = (int)(row % a.heads);
-    const int b = t / a.S, s = t % a.S;
+    int t, h, b, s;
+    split_row(row, a.heads, t, h);
+    split_row(t, a.S, b, s);
     float v[8], w[8];
     ld8(a.x + (int64_t)t * a.row_stride + h * a.head_stride + lane * 8, v);
     ld8f(a.w + lane * 8, w);
@@ -604,8 +617,9 @@ __global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(QkArgs a, const _
     const int lane = threadIdx.x & 31;
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (row >= (int64_t)a.T * a.heads) return;
-    const int t = (int)(row / a.heads), h = (int)(row % a.heads);
-    const int b = t / a.S, s = t % a.S;
+    int t, h, b, s;
+    split_row(row, a.heads, t, h);
+    split_row(t, a.S, b, s);
     float d[8], x[8], w[8];
     ld8(dout + (((int64_t)b * a.heads + h) * a.S + s) * 256 + lane * 8, d);
     ld8(a.x + (int64_t)t * a.row_stride + h * a.head_stride + lane * 8, x);
@@ -647,8 +661,9 @@ __global__ void __launch_bounds__(256) to_bhsd_kernel(const __nv_bfloat16* __res
     if (gid >= (int64_t)T * heads * 32) return;
     const int lane = (int)(gid & 31);
     const int64_t row = gid >> 5;
-    const int t = (int)(row / heads), h = (int)(row % heads);
-    const int b = t / S, s = t % S;
+    int t, h, b, s;
+    split_row(row, heads, t, h);
+    split_row(t, S, b, s);
     const int64_t at_bhsd = (((int64_t)b * heads + h) * S + s) * 256 + lane * 8;
     const int64_t at_row = (int64_t)t * row_stride + (int64_t)h * head_stride + lane * 8;
     if (reverse)
@@ -666,8 +681,9 @@ __global__ void __launch_bounds__(256) gate_mul_fwd_kernel(const __nv_bfloat16* 
     if (gid >= (int64_t)T * heads * 32) return;
     const int lane = (int)(gid & 31);
     const int64_t row = gid >> 5;
-    const int t = (int)(row / heads), h = (int)(row % heads);
-    const int b = t / S, s = t % S;
+    int t, h, b, s;
+    split_row(row, heads, t, h);
+    split_row(t, S, b, s);
     float av[8], gv[8];
     ld8(attn + (((int64_t)b * heads + h) * S + s) * 256 + lane * 8, av);
     ld8(gate + (int64_t)t * gate_stride + (int64_t)h * gate_hs + lane * 8, gv);
@@ -686,8 +702,9 @@ __global__ void __launch_bounds__(256) gate_mul_bwd_kernel(const __nv_bfloat16* 
     if (gid >= (int64_t)T * heads * 32) return;
     const int lane = (int)(gid & 31);
     const int64_t row = gid >> 5;
-    const int t = (int)(row / heads), h = (int)(row % heads);
-    const int b = t / S, s = t % S;
+    int t, h, b, s;
+    split_row(row, heads, t, h);
+    split_row(t, S, b, s);
     const int64_t at = (((int64_t)b * heads + h) * S + s) * 256 + lane * 8;
     float av[8], gv[8], d[8], da[8], dg[8];
     ld8(attn + at, av);

@@ -128,8 +128,12 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const __nv_bfloat16* _
 }
 
 // z rows may live inside a wider token row: row r of z is at (r / zh) * zts + (r % zh) * n when zh > 0
+// The z row of gated row r: token r / zh (row stride zts), head r % zh (n columns each); 32-bit division
+// (the launchers keep rows below 2^32).
 __device__ __forceinline__ int64_t zrow(int64_t r, int n, int64_t zts, int zh) {
-    return zh > 0 ? (r / zh) * zts + (r % zh) * (int64_t)n : r * (int64_t)n;
+    if (zh <= 0) return r * (int64_t)n;
+    const uint32_t q = (uint32_t)r / (uint32_t)zh, m = (uint32_t)r - q * (uint32_t)zh;
+    return (int64_t)q * zts + (int64_t)m * n;
 }
 
 template <int W>
@@ -370,23 +374,24 @@ __global__ void __launch_bounds__(256) gated_bwd128(const __nv_bfloat16* __restr
     float g[8];
     loadw8(w + lane * 8, g);
     float xv[R][8], zv[R][8], dv[R][8];
-    int64_t rr[R];
+    int64_t rr[R], zr[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         const int64_t row = grp * R + r;
         rr[r] = row < rows ? row : rows - 1;
+        zr[r] = zrow(rr[r], 128, zts, zh);
         load8(x + rr[r] * 128 + lane * 8, xv[r]);
-        load8(z + zrow(rr[r], 128, zts, zh) + lane * 8, zv[r]);
+        load8(z + zr[r] + lane * 8, zv[r]);
         load8(dout + rr[r] * 128 + lane * 8, dv[r]);
     }
-    float ss[R], a[R];
+    float ss[R], a[R], sgv[R][8];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
         ss[r] = 0.0f;
         a[r] = 0.0f;
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            const float sg = sigmoidf_(zv[r][e]);
+            const float sg = sgv[r][e] = sigmoidf_(zv[r][e]);
             const float gate = sig ? sg : zv[r][e] * sg;
             ss[r] = fmaf(xv[r][e], xv[r][e], ss[r]);
             a[r] = fmaf(xv[r][e] * dv[r][e], g[e] * gate, a[r]);
@@ -406,7 +411,7 @@ __global__ void __launch_bounds__(256) gated_bwd128(const __nv_bfloat16* __restr
         float ox[8], oz[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-            const float sg = sigmoidf_(zv[r][e]);
+            const float sg = sgv[r][e];
             const float gate = sig ? sg : zv[r][e] * sg;
             const float dgate = sig ? sg * (1.0f - sg) : sg * (1.0f + zv[r][e] * (1.0f - sg));
             ox[e] = g[e] * gate * s * dv[r][e] - xv[r][e] * k;
@@ -414,7 +419,7 @@ __global__ void __launch_bounds__(256) gated_bwd128(const __nv_bfloat16* __restr
         }
         if (grp * R + r < rows) {
             store8(dx + rr[r] * 128 + lane * 8, ox);
-            store8(dz + zrow(rr[r], 128, zts, zh) + lane * 8, oz);
+            store8(dz + zr[r] + lane * 8, oz);
         }
     }
 }
@@ -504,6 +509,7 @@ extern "C" int r97b_gated_rmsnorm_fwd(const uint16_t* x, const uint16_t* z, int6
                                       const float* w, uint16_t* o, int64_t rows, int64_t n, float eps,
                                       int32_t act_sigmoid, void* stream) {
     if (z_heads < 0 || (z_heads > 0 && (rows % z_heads || z_tok_stride % 8))) return R97B_EINVAL;
+    if (rows > (int64_t)UINT32_MAX) return R97B_EINVAL;  // zrow divides in 32 bits
     if (!x || !z || !w || !o || rows <= 0 || n <= 0 || n % 8 || !aligned16(x) || !aligned16(z) || !aligned16(w) ||
         !aligned16(o))
         return R97B_EINVAL;
@@ -528,6 +534,7 @@ extern "C" int r97b_gated_rmsnorm_bwd(const uint16_t* x, const uint16_t* z, int6
                                       const float* w, const uint16_t* dout, uint16_t* dx, uint16_t* dz, int64_t rows,
                                       int64_t n, float eps, int32_t act_sigmoid, void* stream) {
     if (z_heads < 0 || (z_heads > 0 && (rows % z_heads || z_tok_stride % 8))) return R97B_EINVAL;
+    if (rows > (int64_t)UINT32_MAX) return R97B_EINVAL;  // zrow divides in 32 bits
     if (!x || !z || !w || !dout || !dx || !dz || rows <= 0 || n <= 0 || n % 8 || !aligned16(x) || !aligned16(z) ||
         !aligned16(w) || !aligned16(dout) || !aligned16(dx) || !aligned16(dz))
         return R97B_EINVAL;
