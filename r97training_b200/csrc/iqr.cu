@@ -197,9 +197,18 @@ __global__ void __launch_bounds__(256, 3) iqr_decode_u4(const R97IqrDecodeDesc d
     const int64_t nruns = (d.rows + d.run_rows - 1) / d.run_rows;
     const int64_t total = groups * nruns * nseg_per_run;
     if (gid >= total) return;
-    const int64_t g = gid % groups;
-    const int64_t seg = (gid / groups) % nseg_per_run;
-    const int64_t run = gid / (groups * nseg_per_run);
+    int64_t g, seg, run;
+    if (total <= 0xFFFFFFFFll) {  // 32-bit splits: a 64-bit division is a long subroutine
+        const uint32_t ng = (uint32_t)groups, ns = (uint32_t)nseg_per_run;
+        const uint32_t q = (uint32_t)gid / ng, q2 = q / ns;
+        g = (uint32_t)gid - q * ng;
+        seg = q - q2 * ns;
+        run = q2;
+    } else {
+        g = gid % groups;
+        seg = (gid / groups) % nseg_per_run;
+        run = gid / (groups * nseg_per_run);
+    }
     const int64_t r0 = d.row0 + run * d.run_rows;
     int64_t r1 = r0 + d.run_rows;
     if (r1 > d.rows_all) r1 = d.rows_all;
