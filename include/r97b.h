@@ -360,7 +360,9 @@ typedef struct R97bGdnFwd {
 } R97bGdnFwd;
 
 /* Backward operands: the forward's inputs and saved A, w, S, Vp, P; dO bf16 [T, H, 128]; dht f32 or null.
- * Scratch: dS f32 [n_chunks, H, 128, 128], dVp, dw, pdq, pdk f32 [T, H, 128], pdg f32 [T, H].
+ * Scratch: dS f32 [n_chunks, H, 128, 128], dVp, dw f32 [T, H, 128]. pdq, pdk, pdg are not read: the
+ * partial sums of the state-reading pass accumulate in dq, dk and dg; the fields keep the struct's layout
+ * and may be null.
  * Outputs: dq, dk f32 [T, H, 128] per VALUE head (sum the heads sharing a key head with
  * r97b_gdn_sum_heads), dv f32 [T, H, 128], dbeta, dg f32 [T, H], dh0 f32 or null. */
 typedef struct R97bGdnBwd {

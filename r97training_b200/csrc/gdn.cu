@@ -642,8 +642,10 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
         });
 }
 
-// B2a: per (chunk, value head): the state-reading terms. Its operands arrive in three cp.async groups:
-// what dQ~ and dw read (S, dO, q, dV', g), then dS_next, then (into the tiles dQ~ and dw free) V' and k.
+// B2a: per (chunk, value head): the state-reading terms, written as partials of dq, dk, dg (pdq, pdk, pdg:
+// the launcher passes the outputs themselves, which B2b then adds to). Its operands arrive in three
+// cp.async groups: what dQ~ and dw read (S, dO, q, dV', g), then dS_next, then (into the tiles dQ~ and dw
+// free) V' and k.
 __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                  const float* __restrict__ g, const float* __restrict__ S_all,
                                                  const float* __restrict__ Vp, const bf16* __restrict__ dO,
@@ -821,8 +823,7 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
                                                  const float* __restrict__ beta, const float* __restrict__ A,
                                                  const float* __restrict__ Vp, const bf16* __restrict__ dO,
                                                  const float* __restrict__ dVp, const float* __restrict__ dw,
-                                                 const float* __restrict__ pdq, const float* __restrict__ pdk,
-                                                 const float* __restrict__ pdg, float* __restrict__ dq_out,
+                                                 float* __restrict__ dq_out,
                                                  float* __restrict__ dk_out, float* __restrict__ dv_out,
                                                  float* __restrict__ dbeta_out, float* __restrict__ dg_out,
                                                  float* __restrict__ dA_out) {
@@ -970,21 +971,17 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
     __syncthreads();
     if (!split) kkt_adjoint(ah, al, th, tl, yh, yl, ks, Cs, gs, bs, dgs, dbs, n, dka);
     __syncthreads();
+    // B2a left its partials in dq, dk and dg: one reduction each adds this kernel's terms (fire-and-forget,
+    // and with a single add per element the sum is the same as loading the partial and storing the total)
     acc_for<16, 64>(dqa, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) {
-            const int64_t at = ((tok0 + r) * dm.H + h) * D + d;
-            dq_out[at] = x + pdq[at];
-        }
+        if (r < n) atomicAdd(dq_out + ((tok0 + r) * dm.H + h) * D + d, x);
     });
     acc_for<16, 64>(dka, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) {
-            const int64_t at = ((tok0 + r) * dm.H + h) * D + d;
-            dk_out[at] = x + pdk[at];
-        }
+        if (r < n) atomicAdd(dk_out + ((tok0 + r) * dm.H + h) * D + d, x);
     });
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int64_t at = (tok0 + i) * dm.H + h;
-        dg_out[at] = dgs[i] + pdg[at];
+        atomicAdd(dg_out + at, dgs[i]);
         dbeta_out[at] = dbs[i];
     }
 }
@@ -1145,7 +1142,7 @@ extern "C" int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* a, void* 
 extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* stream) {
     if (!dims || !a || !dims_ok(*dims)) return R97B_EINVAL;
     if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->A || !a->w || !a->S || !a->Vp || !a->P || !a->dO ||
-        !a->dS || !a->dVp || !a->dw || !a->pdq || !a->pdk || !a->pdg || !a->dq || !a->dk || !a->dv || !a->dbeta ||
+        !a->dS || !a->dVp || !a->dw || !a->dq || !a->dk || !a->dv || !a->dbeta ||
         !a->dg)
         return R97B_EINVAL;
     if ((dims->flags & R97B_GDN_SPLIT_KKT) && !a->dA) return R97B_EINVAL;
@@ -1159,11 +1156,11 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
     gdn_bwd_state<<<dim3(dm.n_seq, dm.H, D / VSB), 256, kSmemBState, s>>>(dm, q, k, a->g, a->w, a->P, dO, a->dht,
                                                                         a->dS, a->dVp, a->dh0);
     if (dm.n_chunks > 0) {
+        // B2a writes its partials of dq, dk, dg into the outputs; B2b adds its own terms to them
         gdn_bwd_a<<<dim3(dm.n_chunks, dm.H), 256, kSmemBA, s>>>(dm, q, k, a->g, a->S, a->Vp, dO, a->dS, a->dVp, a->dw,
-                                                                a->pdq, a->pdk, a->pdg);
+                                                                a->dq, a->dk, a->dg);
         gdn_bwd_b<<<dim3(dm.n_chunks, dm.H), 256, kSmemBB, s>>>(dm, q, k, v, a->g, a->beta, a->A, a->Vp, dO, a->dVp,
-                                                                a->dw, a->pdq, a->pdk, a->pdg, a->dq, a->dk, a->dv,
-                                                                a->dbeta, a->dg, a->dA);
+                                                                a->dw, a->dq, a->dk, a->dv, a->dbeta, a->dg, a->dA);
     }
     return launch_status(dm.n_chunks > 0 ? 3 : 1);
 }

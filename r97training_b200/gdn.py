@@ -85,14 +85,13 @@ class GdnPlan:
     def backward(self, sv, dO, dht=None, want_dh0=False, stream=None, sum_heads=True):
         T, H, n = self.T, self.H, self.n_chunks
         dS = self._f32(max(n, 1), H, 128, 128)
-        dVp, dw, pdq, pdk = (self._f32(T, H, 128) for _ in range(4))
-        pdg = self._f32(T, H)
+        dVp, dw = (self._f32(T, H, 128) for _ in range(2))
         dq, dk, dv = (self._f32(T, H, 128) for _ in range(3))
         dbeta, dg = self._f32(T, H), self._f32(T, H)
         dh0 = self._f32(self.n_seq, H, 128, 128) if want_dh0 else None
         a = R97bGdnBwd(_p(sv["q"]), _p(sv["k"]), _p(sv["v"]), _p(sv["g"]), _p(sv["beta"]), _p(sv["A"]), _p(sv["w"]),
-                       _p(sv["S"]), _p(sv["Vp"]), _p(sv["P"]), _p(dO), _p(dht), _p(dS), _p(dVp), _p(dw), _p(pdq),
-                       _p(pdk), _p(pdg), _p(dq), _p(dk), _p(dv), _p(dbeta), _p(dg), _p(dh0))
+                       _p(sv["S"]), _p(sv["Vp"]), _p(sv["P"]), _p(dO), _p(dht), _p(dS), _p(dVp), _p(dw), None,
+                       None, None, _p(dq), _p(dk), _p(dv), _p(dbeta), _p(dg), _p(dh0))
         s = (stream or torch.cuda.current_stream()).cuda_stream
         check(lib().r97b_gdn_bwd(ctypes.byref(self.dims), ctypes.byref(a), c_vp(s)), "r97b_gdn_bwd")
         if sum_heads and self.H != self.Hg:

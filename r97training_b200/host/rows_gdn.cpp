@@ -190,8 +190,8 @@ void scan_device(const AdjointCall& call) {
 
     DevBuf dOd = upload_bf16(d_o.value.data(), 1, T * H * kD, T * H * kD);
     DevBuf dhtd = upload_f32(dht.data(), 1, N * per, N * per);
-    DevBuf dS(n_chunks * H * kD * kD * 4), dVp(T * H * kD * 4), dw(T * H * kD * 4), pdq(T * H * kD * 4);
-    DevBuf pdk(T * H * kD * 4), pdg(T * H * 4), dqh(T * H * kD * 4), dkh(T * H * kD * 4), dvd(T * H * kD * 4);
+    DevBuf dS(n_chunks * H * kD * kD * 4), dVp(T * H * kD * 4), dw(T * H * kD * 4);
+    DevBuf dqh(T * H * kD * 4), dkh(T * H * kD * 4), dvd(T * H * kD * 4);
     DevBuf dbd(T * H * 4), dgd(T * H * 4), dAd(T * H * kChunk * 4);
     dAd.zero();
     R97bGdnBwd ba{};
@@ -210,9 +210,6 @@ void scan_device(const AdjointCall& call) {
     ba.dS = dS.as<float>();
     ba.dVp = dVp.as<float>();
     ba.dw = dw.as<float>();
-    ba.pdq = pdq.as<float>();
-    ba.pdk = pdk.as<float>();
-    ba.pdg = pdg.as<float>();
     ba.dq = dqh.as<float>();
     ba.dk = dkh.as<float>();
     ba.dv = dvd.as<float>();
