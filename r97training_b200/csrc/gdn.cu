@@ -487,9 +487,12 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
     mma_split_ab<16, 64, 64, false, true>(pvacc, ph, pl, kP64, vh, vl, kP128, m0, n0);
     const int lane = threadIdx.x & 31, gq = lane >> 2;
     const float eg0 = gexp(gs[m0 + gq]), eg1 = gexp(gs[m0 + gq + 8]);
-    acc_walk<16, 64>(m0, n0, [&](int r, int e, int i, int j, int q) {
-        const float y = dm.scale * (qsacc[i][j][q] * ((q >> 1) ? eg1 : eg0) + pvacc[i][j][q]);
-        if (r < n) o[((tok0 + r) * dm.H + h) * D + e] = __float2bfloat16_rn(y);
+    acc_pairs<16, 64>(m0, n0, [&](int r, int e, int i, int j, int hh) {  // two columns a 4-byte store
+        const float eg = hh ? eg1 : eg0;
+        const float y0 = dm.scale * (qsacc[i][j][2 * hh] * eg + pvacc[i][j][2 * hh]);
+        const float y1 = dm.scale * (qsacc[i][j][2 * hh + 1] * eg + pvacc[i][j][2 * hh + 1]);
+        if (r < n)
+            *reinterpret_cast<__nv_bfloat162*>(o + ((tok0 + r) * dm.H + h) * D + e) = __floats2bfloat162_rn(y0, y1);
     });
 }
 
@@ -955,11 +958,15 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
         acc_zero<16, 64>(acc);
         mma_split_ab<16, 64, 64, true, true>(acc, ah, al, kP64, dvh, dvl, kP128, m0, n0);
         p0 = p1 = 0.0f;
-        acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
-            const float x = acc[i][j][q];
-            const float t = __bfloat162float(qv[r * kP128 + d]) * x;
-            if (q >> 1) p1 += t; else p0 += t;
-            if (r < n) dv_out[((tok0 + r) * dm.H + h) * D + d] = bs[r] * x;
+        acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {  // two columns an 8-byte store
+            const float x0 = acc[i][j][2 * hh], x1 = acc[i][j][2 * hh + 1];
+            float& p = hh ? p1 : p0;
+            const float t0 = __bfloat162float(qv[r * kP128 + d]) * x0;
+            p += t0;
+            const float t1 = __bfloat162float(qv[r * kP128 + d + 1]) * x1;
+            p += t1;
+            if (r < n)
+                *reinterpret_cast<float2*>(dv_out + ((tok0 + r) * dm.H + h) * D + d) = make_float2(bs[r] * x0, bs[r] * x1);
         });
         p0 = quad_sum(p0);
         p1 = quad_sum(p1);
