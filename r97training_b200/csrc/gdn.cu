@@ -325,8 +325,10 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
     });
     acc_zero<16, 64>(acc);
     mma_split_a<16, 64, 64, false, true>(acc, a2h, a2l, kP64, vs, kP128, m0, n0);
-    acc_for<16, 64>(acc, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) u[((tok0 + r) * dm.H + h) * D + d] = x;
+    acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {
+        if (r < n)
+            *reinterpret_cast<float2*>(u + ((tok0 + r) * dm.H + h) * D + d) =
+                make_float2(acc[i][j][2 * hh], acc[i][j][2 * hh + 1]);
     });
 }
 
@@ -763,11 +765,12 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
         dgs[n - 1] += gexp(gl) * s;
     }
     __syncthreads();
-    acc_for<16, 64>(dq, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) pdq[((tok0 + r) * dm.H + h) * D + d] = x;
-    });
-    acc_for<16, 64>(dk, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) pdk[((tok0 + r) * dm.H + h) * D + d] = x;
+    acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {  // two columns an 8-byte store
+        if (r < n) {
+            const int64_t at = ((tok0 + r) * dm.H + h) * D + d;
+            *reinterpret_cast<float2*>(pdq + at) = make_float2(dq[i][j][2 * hh], dq[i][j][2 * hh + 1]);
+            *reinterpret_cast<float2*>(pdk + at) = make_float2(dk[i][j][2 * hh], dk[i][j][2 * hh + 1]);
+        }
     });
     for (int i = threadIdx.x; i < n; i += blockDim.x) pdg[(tok0 + i) * dm.H + h] = dgs[i];
 }
@@ -980,11 +983,12 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
     __syncthreads();
     // B2a left its partials in dq, dk and dg: one reduction each adds this kernel's terms (fire-and-forget,
     // and with a single add per element the sum is the same as loading the partial and storing the total)
-    acc_for<16, 64>(dqa, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) atomicAdd(dq_out + ((tok0 + r) * dm.H + h) * D + d, x);
-    });
-    acc_for<16, 64>(dka, m0, n0, [&](int r, int d, float& x) {
-        if (r < n) atomicAdd(dk_out + ((tok0 + r) * dm.H + h) * D + d, x);
+    acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {  // two columns an 8-byte reduction
+        if (r < n) {
+            const int64_t at = ((tok0 + r) * dm.H + h) * D + d;
+            atomicAdd(reinterpret_cast<float2*>(dq_out + at), make_float2(dqa[i][j][2 * hh], dqa[i][j][2 * hh + 1]));
+            atomicAdd(reinterpret_cast<float2*>(dk_out + at), make_float2(dka[i][j][2 * hh], dka[i][j][2 * hh + 1]));
+        }
     });
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
         const int64_t at = (tok0 + i) * dm.H + h;
