@@ -693,9 +693,11 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
         acc_zero<16, 64>(dq);
         mma_split_b<16, 64, 128, false, false>(dq, xs, kP128, sh, sl, kP128, m0, n0);
         float p0 = 0.0f, p1 = 0.0f;
+        const int gq = lane >> 2;  // this lane's two rows: m0 + gq and m0 + gq + 8
+        const float f0 = dm.scale * gexp(gs[m0 + gq]), f1 = dm.scale * gexp(gs[m0 + gq + 8]);
         acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
             float& x = dq[i][j][q];
-            x *= dm.scale * gexp(gs[r]);
+            x *= (q >> 1) ? f1 : f0;
             const float t = __bfloat162float(qs[r * kP128 + d]) * x;
             if (q >> 1) p1 += t; else p0 += t;
         });
@@ -744,9 +746,11 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
         acc_zero<16, 64>(dk);
         mma_split_ab<16, 64, 128, false, false>(dk, yh, yl, kP128, th, tl, kP128, m0, n0);
         float p0 = 0.0f, p1 = 0.0f;
+        const int gq = lane >> 2, ra = m0 + gq, rb = ra + 8;
+        const float f0 = ra < n ? gexp(gl - gs[ra]) : 0.0f, f1 = rb < n ? gexp(gl - gs[rb]) : 0.0f;
         acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
             float& x = dk[i][j][q];
-            x *= r < n ? gexp(gl - gs[r]) : 0.0f;
+            x *= (q >> 1) ? f1 : f0;
             const float t = __bfloat162float(xs[r * kP128 + d]) * x;
             if (q >> 1) p1 += t; else p0 += t;
         });
@@ -927,8 +931,17 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
         acc_zero<16, 32>(a2);
         mma_split_a<16, 32, 128, false, false>(a1, xh, xl, kP128, ks, kP128, pm0, pn0);
         mma_split_a<16, 32, 128, false, false>(a2, dvh, dvl, kP128, qv, kP128, pm0, pn0);
+        float el[4][2], bl[4][2];  // this lane's eight columns l = pn0 + 8 j + 2 (lane % 4) + b
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int b = 0; b < 2; ++b) {
+                const int l = pn0 + 8 * j + 2 * (lane & 3) + b;
+                el[j][b] = gexp(gs[l]);
+                bl[j][b] = bs[l];
+            }
         acc_walk<16, 32>(pm0, pn0, [&](int r, int l, int i, int j, int q) {
-            const float da = bs[l] * (gexp(gs[l]) * a1[i][j][q] + a2[i][j][q]);
+            const float da = bl[j][q & 1] * (el[j][q & 1] * a1[i][j][q] + a2[i][j][q]);
             if (split) {  // the scan's own cotangent of A, its lower triangle with the diagonal
                 if (r < n) dA_out[((tok0 + r) * dm.H + h) * L + l] = l <= r ? da : 0.0f;
             } else {
@@ -942,11 +955,13 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
         acc_zero<16, 64>(acc);
         mma_split_ab<16, 64, 64, true, true>(acc, ah, al, kP64, xh, xl, kP128, m0, n0);
         float p0 = 0.0f, p1 = 0.0f;
+        const int gq = lane >> 2;  // this lane's two rows: m0 + gq and m0 + gq + 8
+        const float f0 = bs[m0 + gq] * gexp(gs[m0 + gq]), f1 = bs[m0 + gq + 8] * gexp(gs[m0 + gq + 8]);
         acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
             const float x = acc[i][j][q];
             const float t = __bfloat162float(ks[r * kP128 + d]) * x;
             if (q >> 1) p1 += t; else p0 += t;
-            dka[i][j][q] += bs[r] * gexp(gs[r]) * x;
+            dka[i][j][q] += ((q >> 1) ? f1 : f0) * x;
         });
         p0 = quad_sum(p0);
         p1 = quad_sum(p1);
