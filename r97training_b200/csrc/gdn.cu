@@ -617,8 +617,10 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
             acc_zero<16, 32>(a2);
             mma_split_a<16, 32, 64, true, true>(a1, et.ph, et.pl, kP64, et.dos, kP64, vm0, vn0);
             mma_split_b<16, 32, 128, false, true>(a2, et.ks, kP128, dsh, dsl, kP64, vm0, vn0);
+            const int ja = vm0 + ((threadIdx.x & 31) >> 2), jb = ja + 8;  // this lane's two rows
+            const float sca = ja < n ? gexp(gl - et.gs[ja]) : 0.0f, scb = jb < n ? gexp(gl - et.gs[jb]) : 0.0f;
             acc_pairs<16, 32>(vm0, vn0, [&](int j, int e, int a, int b, int hh) {
-                const float sc = j < n ? gexp(gl - et.gs[j]) : 0.0f;
+                const float sc = hh ? scb : sca;
                 const float d0 = j < n ? dm.scale * a1[a][b][2 * hh] + sc * a2[a][b][2 * hh] : 0.0f;
                 const float d1 = j < n ? dm.scale * a1[a][b][2 * hh + 1] + sc * a2[a][b][2 * hh + 1] : 0.0f;
                 if (j < n) put_split2(dVpp.hi, dVpp.lo, ((tok0 + j) * dm.H + h) * D + e0 + e, d0, d1);
@@ -1149,6 +1151,8 @@ extern "C" int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* a, void* 
     if (!dims || !a || !dims_ok(*dims)) return R97B_EINVAL;
     if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->A || !a->w || !a->u || !a->S || !a->Vp || !a->P || !a->o)
         return R97B_EINVAL;
+    // u and o are written two columns at a time
+    if ((reinterpret_cast<uintptr_t>(a->u) & 7) || (reinterpret_cast<uintptr_t>(a->o) & 3)) return R97B_EINVAL;
     set_attrs();
     const Dims dm = to_dims(*dims);
     cudaStream_t s = as_stream(stream);
@@ -1170,6 +1174,9 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
     if (!a->q || !a->k || !a->v || !a->g || !a->beta || !a->A || !a->w || !a->S || !a->Vp || !a->P || !a->dO ||
         !a->dS || !a->dVp || !a->dw || !a->dq || !a->dk || !a->dv || !a->dbeta ||
         !a->dg)
+        return R97B_EINVAL;
+    // dq, dk, dv are written two columns at a time (8-byte stores and reductions)
+    if ((reinterpret_cast<uintptr_t>(a->dq) | reinterpret_cast<uintptr_t>(a->dk) | reinterpret_cast<uintptr_t>(a->dv)) & 7)
         return R97B_EINVAL;
     if ((dims->flags & R97B_GDN_SPLIT_KKT) && !a->dA) return R97B_EINVAL;
     set_attrs();
