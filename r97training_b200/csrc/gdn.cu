@@ -189,16 +189,28 @@ __device__ __forceinline__ void mma_split_ab(float (&acc)[WM / 16][WN / 8][4], c
 
 // ------------------------------------------------------------------------------ the chunk's solve
 
-// dst[i][j] = sign * sum_l X[i][l] Y[l][j] for N x N blocks (pitches px, py, pd), by the whole CTA.
+// dst[i][j] = sign * sum_l X[i][l] Y[l][j] for N x N blocks (pitches px, py, pd), by the whole CTA: a thread
+// a 2 x 2 tile of dst, so each shared load feeds two multiply-adds (the product is shared-load bound).
 template <int N>
 __device__ __forceinline__ void block_product(const float* X, int px, const float* Y, int py, float* dst, int pd,
                                               float sign) {
-    for (int e = threadIdx.x; e < N * N; e += blockDim.x) {
-        const int i = e / N, j = e % N;
-        float acc = 0.0f;
+    constexpr int T = N / 2;  // tiles a side
+    for (int e = threadIdx.x; e < T * T; e += blockDim.x) {
+        const int i = (e / T) * 2, j = (e % T) * 2;
+        float a00 = 0.0f, a01 = 0.0f, a10 = 0.0f, a11 = 0.0f;
 #pragma unroll 8
-        for (int l = 0; l < N; ++l) acc = fmaf(X[i * px + l], Y[l * py + j], acc);
-        dst[i * pd + j] = sign * acc;
+        for (int l = 0; l < N; ++l) {
+            const float x0 = X[i * px + l], x1 = X[(i + 1) * px + l];
+            const float y0 = Y[l * py + j], y1 = Y[l * py + j + 1];
+            a00 = fmaf(x0, y0, a00);
+            a01 = fmaf(x0, y1, a01);
+            a10 = fmaf(x1, y0, a10);
+            a11 = fmaf(x1, y1, a11);
+        }
+        dst[i * pd + j] = sign * a00;
+        dst[i * pd + j + 1] = sign * a01;
+        dst[(i + 1) * pd + j] = sign * a10;
+        dst[(i + 1) * pd + j + 1] = sign * a11;
     }
 }
 
