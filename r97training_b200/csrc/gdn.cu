@@ -244,23 +244,45 @@ __device__ __forceinline__ void invert_unit_lower(const float* Ms, float* As, fl
     __syncthreads();
     // 16 -> 32: blocks (1,0) and (3,2) (pair p: rows r0 = 16 or 48, columns c0 = 0 or 32);
     // T = M21 A11 into scratch, then X21 = -A22 T
-    for (int e = threadIdx.x; e < 512; e += blockDim.x) {
-        const int p = e >> 8, i = (e >> 4) & 15, j = e & 15;
+    // (2 x 2 output tiles a thread, as block_product: each shared load feeds two multiply-adds)
+    if (threadIdx.x < 128) {
+        const int e = threadIdx.x, p = e >> 6, i = ((e >> 3) & 7) * 2, j = (e & 7) * 2;
         const int r0 = p ? 48 : 16, c0 = p ? 32 : 0;
-        float acc = 0.0f;
+        float a00 = 0.0f, a01 = 0.0f, a10 = 0.0f, a11 = 0.0f;
 #pragma unroll 8
-        for (int l = 0; l < 16; ++l) acc = fmaf(Ms[(r0 + i) * F65 + c0 + l], As[(c0 + l) * F65 + c0 + j], acc);
-        scratch[p * 16 * 17 + i * 17 + j] = acc;
+        for (int l = 0; l < 16; ++l) {
+            const float x0 = Ms[(r0 + i) * F65 + c0 + l], x1 = Ms[(r0 + i + 1) * F65 + c0 + l];
+            const float y0 = As[(c0 + l) * F65 + c0 + j], y1 = As[(c0 + l) * F65 + c0 + j + 1];
+            a00 = fmaf(x0, y0, a00);
+            a01 = fmaf(x0, y1, a01);
+            a10 = fmaf(x1, y0, a10);
+            a11 = fmaf(x1, y1, a11);
+        }
+        float* t = scratch + p * 16 * 17;
+        t[i * 17 + j] = a00;
+        t[i * 17 + j + 1] = a01;
+        t[(i + 1) * 17 + j] = a10;
+        t[(i + 1) * 17 + j + 1] = a11;
     }
     __syncthreads();
-    for (int e = threadIdx.x; e < 512; e += blockDim.x) {
-        const int p = e >> 8, i = (e >> 4) & 15, j = e & 15;
+    if (threadIdx.x < 128) {
+        const int e = threadIdx.x, p = e >> 6, i = ((e >> 3) & 7) * 2, j = (e & 7) * 2;
         const int r0 = p ? 48 : 16, c0 = p ? 32 : 0;
         const float* t = scratch + p * 16 * 17;
-        float acc = 0.0f;
+        float a00 = 0.0f, a01 = 0.0f, a10 = 0.0f, a11 = 0.0f;
 #pragma unroll 8
-        for (int l = 0; l < 16; ++l) acc = fmaf(As[(r0 + i) * F65 + r0 + l], t[l * 17 + j], acc);
-        As[(r0 + i) * F65 + c0 + j] = -acc;
+        for (int l = 0; l < 16; ++l) {
+            const float x0 = As[(r0 + i) * F65 + r0 + l], x1 = As[(r0 + i + 1) * F65 + r0 + l];
+            const float y0 = t[l * 17 + j], y1 = t[l * 17 + j + 1];
+            a00 = fmaf(x0, y0, a00);
+            a01 = fmaf(x0, y1, a01);
+            a10 = fmaf(x1, y0, a10);
+            a11 = fmaf(x1, y1, a11);
+        }
+        As[(r0 + i) * F65 + c0 + j] = -a00;
+        As[(r0 + i) * F65 + c0 + j + 1] = -a01;
+        As[(r0 + i + 1) * F65 + c0 + j] = -a10;
+        As[(r0 + i + 1) * F65 + c0 + j + 1] = -a11;
     }
     __syncthreads();
     // 32 -> 64: block (1,0) of 32x32 blocks; T = M[32:64][0:32] A[0:32][0:32], X = -A[32:64][32:64] T
