@@ -339,13 +339,15 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
         // then 16 -> 32 -> 64 with X21 = -A22 (M21 A11) (the inverse of a block lower-triangular matrix)
         invert_unit_lower(Ms, As, reinterpret_cast<float*>(a1h));
     }
-    for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
-        const int i = idx >> 6, j = idx & 63;
-        const float a = As[i * F65 + j];
-        if (i < n && !given) A[((tok0 + i) * dm.H + h) * L + j] = a;
-        const float e = bs[j] * gexp(gs[j]);
-        put_split(a1h, a1l, i * kP64 + j, a * e);
-        put_split(a2h, a2l, i * kP64 + j, a * bs[j]);
+    {
+        const int j = threadIdx.x & 63;  // a thread keeps its column (the stride is a multiple of 64)
+        const float e = bs[j] * gexp(gs[j]), bj = bs[j];
+        for (int i = threadIdx.x >> 6; i < L; i += blockDim.x >> 6) {
+            const float a = As[i * F65 + j];
+            if (i < n && !given) A[((tok0 + i) * dm.H + h) * L + j] = a;
+            put_split(a1h, a1l, i * kP64 + j, a * e);
+            put_split(a2h, a2l, i * kP64 + j, a * bj);
+        }
     }
     __syncthreads();
     const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
@@ -908,9 +910,17 @@ __global__ void __launch_bounds__(256) gdn_bwd_b(Dims dm, const bf16* __restrict
     async_gb(gs, bs, g, beta, tok0, n, dm.H, h);
     cp_async_commit();
     // A (the caller's f32) is split by hand while the copies fly
-    for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
-        const int i = idx >> 6, j = idx & 63;
-        put_split(ah, al, i * kP64 + j, i < n ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f);
+    {
+        // a thread's 16 loads issued together (a loop of load-then-split would wait out each one in turn)
+        const int j = threadIdx.x & 63, i0 = threadIdx.x >> 6;  // 256 threads: rows i0, i0 + 4, ...
+        float av[L / 4];
+#pragma unroll
+        for (int q = 0; q < L / 4; ++q) {
+            const int i = i0 + 4 * q;
+            av[q] = i < n ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < L / 4; ++q) put_split(ah, al, (i0 + 4 * q) * kP64 + j, av[q]);
     }
     for (int i = threadIdx.x; i < L; i += blockDim.x) {
         dgs[i] = 0.0f;
@@ -1074,12 +1084,23 @@ __global__ void __launch_bounds__(256) gdn_kkt_bwd(Dims dm, const bf16* __restri
     const int warp = threadIdx.x >> 5;
     stage_bf16(ks, k, tok0, n, dm.Hg, hk);
     load_gb(gs, bs, g, beta, tok0, n, dm.H, h);
-    for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
-        const int i = idx >> 6, j = idx & 63;
-        const bool on = i < n && j <= i;
-        const int64_t at = ((tok0 + i) * dm.H + h) * L + j;
-        put_split(ah, al, i * kP64 + j, on ? A[at] : 0.0f);
-        put_split(th, tl, i * kP64 + j, on ? dA[at] : 0.0f);
+    {
+        // a thread's loads issued together, as in B2b
+        const int j = threadIdx.x & 63, i0 = threadIdx.x >> 6;  // 256 threads: rows i0, i0 + 4, ...
+        float av[L / 4], dv[L / 4];
+#pragma unroll
+        for (int q = 0; q < L / 4; ++q) {
+            const int i = i0 + 4 * q;
+            const bool on = i < n && j <= i;
+            const int64_t at = ((tok0 + i) * dm.H + h) * L + j;
+            av[q] = on ? A[at] : 0.0f;
+            dv[q] = on ? dA[at] : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < L / 4; ++q) {
+            put_split(ah, al, (i0 + 4 * q) * kP64 + j, av[q]);
+            put_split(th, tl, (i0 + 4 * q) * kP64 + j, dv[q]);
+        }
     }
     for (int i = threadIdx.x; i < L; i += blockDim.x) {
         dgs[i] = 0.0f;
