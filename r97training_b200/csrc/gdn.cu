@@ -62,30 +62,11 @@ struct Dims {
 
 // ------------------------------------------------------------------------------------------ staging
 
-// rows [0, 64) of one head of a token-major bf16 tensor [T, heads, 128] -> bf16 tile (pitch kP128);
-// rows >= n are zero
-__device__ __forceinline__ void stage_bf16(bf16* dst, const bf16* src, int64_t tok0, int n, int heads, int head) {
-    for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
-        const int i = idx >> 4, c = (idx & 15) * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (i < n) v = *reinterpret_cast<const uint4*>(src + ((tok0 + i) * heads + head) * D + c);
-        *reinterpret_cast<uint4*>(dst + i * kP128 + c) = v;
-    }
-}
-
 __device__ __forceinline__ void put_split(bf16* hi, bf16* lo, int64_t at, float x) {
     bf16 h, l;
     split_bf16(x, h, l);
     hi[at] = h;
     lo[at] = l;
-}
-
-__device__ __forceinline__ void load_gb(float* gs, float* bs, const float* g, const float* beta, int64_t tok0, int n,
-                                        int H, int h) {
-    for (int i = threadIdx.x; i < L; i += blockDim.x) {
-        gs[i] = i < n ? g[(tok0 + i) * H + h] : 0.0f;
-        if (bs) bs[i] = i < n ? beta[(tok0 + i) * H + h] : 0.0f;
-    }
 }
 
 // ---- asynchronous staging (cp.async): every f32 intermediate the kernels hand each other (V', S, dV', dS,
@@ -314,14 +295,22 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
     const int n = dm.len[c];
     const int warp = threadIdx.x >> 5;
     const bool given = (dm.flags & R97B_GDN_A_GIVEN) != 0;
-    stage_bf16(ks, k, tok0, n, dm.Hg, hk);
-    stage_bf16(vs, v, tok0, n, dm.H, h);
-    load_gb(gs, bs, g, beta, tok0, n, dm.H, h);
-    if (given)  // the caller's solve: its lower triangle, diagonal included, for the chunk's rows
-        for (int idx = threadIdx.x; idx < L * L; idx += blockDim.x) {
-            const int i = idx >> 6, j = idx & 63;
-            As[i * F65 + j] = (i < n && j <= i) ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f;
+    async_rows(ks, k, tok0, n, dm.Hg, hk);
+    async_rows(vs, v, tok0, n, dm.H, h);
+    async_gb(gs, bs, g, beta, tok0, n, dm.H, h);
+    cp_async_commit();
+    if (given) {  // the caller's solve: its lower triangle, diagonal included, for the chunk's rows
+        const int j = threadIdx.x & 63, i0 = threadIdx.x >> 6;  // 256 threads: rows i0, i0 + 4, ...
+        float av[L / 4];
+#pragma unroll
+        for (int q = 0; q < L / 4; ++q) {  // every load issued before the first store
+            const int i = i0 + 4 * q;
+            av[q] = (i < n && j <= i) ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f;
         }
+#pragma unroll
+        for (int q = 0; q < L / 4; ++q) As[(i0 + 4 * q) * F65 + j] = av[q];
+    }
+    cp_async_wait_all();
     __syncthreads();
     if (!given) {
         // M = strict lower of beta_i (k_i . k_l) e^{g_i - g_l}
@@ -1082,8 +1071,9 @@ __global__ void __launch_bounds__(256) gdn_kkt_bwd(Dims dm, const bf16* __restri
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
     const int warp = threadIdx.x >> 5;
-    stage_bf16(ks, k, tok0, n, dm.Hg, hk);
-    load_gb(gs, bs, g, beta, tok0, n, dm.H, h);
+    async_rows(ks, k, tok0, n, dm.Hg, hk);
+    async_gb(gs, bs, g, beta, tok0, n, dm.H, h);
+    cp_async_commit();
     {
         // a thread's loads issued together, as in B2b
         const int j = threadIdx.x & 63, i0 = threadIdx.x >> 6;  // 256 threads: rows i0, i0 + 4, ...
@@ -1106,6 +1096,7 @@ __global__ void __launch_bounds__(256) gdn_kkt_bwd(Dims dm, const bf16* __restri
         dgs[i] = 0.0f;
         dbs[i] = 0.0f;
     }
+    cp_async_wait_all();
     __syncthreads();
     {
         float kk[1][4][4];
