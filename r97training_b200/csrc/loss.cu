@@ -72,9 +72,10 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
     const int64_t nvec = vec ? vocab / 8 : 0;
 
     Acc a{-INFINITY, 0.0f, -INFINITY, 0.0f, 0.0f};
-    for (int64_t i = threadIdx.x; i < nvec; i += kThreads) {
+    // one 8-value vector of the row (and the teacher's) into the running sums
+    auto fold = [&](const uint4& xs, const uint4& ts) {
         float v[8];
-        unpack8(reinterpret_cast<const uint4*>(x)[i], v);
+        unpack8(xs, v);
         float mx = v[0];
 #pragma unroll
         for (int k = 1; k < 8; ++k) mx = fmaxf(mx, v[k]);
@@ -86,7 +87,7 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
         a.s = s;
         if (kTeacher) {
             float tv[8];
-            unpack8(reinterpret_cast<const uint4*>(t)[i], tv);
+            unpack8(ts, tv);
             float tm = tv[0];
 #pragma unroll
             for (int k = 1; k < 8; ++k) tm = fmaxf(tm, tv[k]);
@@ -103,7 +104,21 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
             a.st = st;
             a.u = u;
         }
+    };
+    const uint4* xv = reinterpret_cast<const uint4*>(x);
+    const uint4* tvp = kTeacher ? reinterpret_cast<const uint4*>(t) : nullptr;
+    int64_t i = threadIdx.x;
+    for (; i + 3 * kThreads < nvec; i += 4 * kThreads) {  // four vectors in flight a thread
+        uint4 xs[4], ts[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            xs[q] = xv[i + q * kThreads];
+            ts[q] = kTeacher ? tvp[i + q * kThreads] : xs[q];
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) fold(xs[q], ts[q]);
     }
+    for (; i < nvec; i += kThreads) fold(xv[i], kTeacher ? tvp[i] : xv[i]);
     // the ragged tail (vocab not a multiple of 8), one element a thread
     for (int64_t j = nvec * 8 + threadIdx.x; j < vocab; j += kThreads) {
         const float v = __bfloat162float(x[j]);
@@ -148,25 +163,38 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
     __nv_bfloat16* g = grad + row * ld;
     const float ce_w = targets ? w_ce : 0.0f;
     const float sc = scored ? grad_scale : 0.0f;
-    for (int64_t i = threadIdx.x; i < nvec; i += kThreads) {
+    // one 8-value vector of the gradient from the row (and the teacher's)
+    auto emit = [&](int64_t iv, const uint4& xs, const uint4& ts) {
         float v[8], tv[8];
-        unpack8(reinterpret_cast<const uint4*>(x)[i], v);
-        if (kTeacher) unpack8(reinterpret_cast<const uint4*>(t)[i], tv);
+        unpack8(xs, v);
+        if (kTeacher) unpack8(ts, tv);
         float o[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const float p = fexp(v[k] - lse);
             float d = ce_w * p;
             if (kTeacher) d += w_kl * (p - fexp(tv[k] - lse_t));
-            if (targets && (int64_t)i * 8 + k == target) d -= ce_w;
+            if (targets && iv * 8 + k == target) d -= ce_w;
             o[k] = d * sc;
         }
         uint4 u;
         __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
 #pragma unroll
         for (int k = 0; k < 4; ++k) h[k] = __floats2bfloat162_rn(o[2 * k], o[2 * k + 1]);
-        reinterpret_cast<uint4*>(g)[i] = u;
+        reinterpret_cast<uint4*>(g)[iv] = u;
+    };
+    i = threadIdx.x;
+    for (; i + 3 * kThreads < nvec; i += 4 * kThreads) {  // four vectors in flight a thread
+        uint4 xs[4], ts[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            xs[q] = xv[i + q * kThreads];
+            ts[q] = kTeacher ? tvp[i + q * kThreads] : xs[q];
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) emit(i + q * kThreads, xs[q], ts[q]);
     }
+    for (; i < nvec; i += kThreads) emit(i, xv[i], kTeacher ? tvp[i] : xv[i]);
     for (int64_t j = nvec * 8 + threadIdx.x; j < vocab; j += kThreads) {
         const float p = fexp(__bfloat162float(x[j]) - lse);
         float d = ce_w * p;
