@@ -278,12 +278,15 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_row(const __nv_bfloat16* __re
     const int64_t grow = (int64_t)blockIdx.x * 2 + (threadIdx.x >> 7);
     const bool valid = grow < rows;
     const int64_t row = valid ? grow : rows - 1;
-    float v[VPT][8], d[VPT][8];
+    float v[VPT][8], d[VPT][8], ad[VPT][8];
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
         load8(x + row * n + (i * 128 + t) * 8, v[i]);
         load8(dy + row * n + (i * 128 + t) * 8, d[i]);
     }
+    if (addend)  // the residual addend's loads fly during the reduction
+#pragma unroll
+        for (int i = 0; i < VPT; ++i) load8(addend + row * n + (i * 128 + t) * 8, ad[i]);
     float ss = 0.0f, tt = 0.0f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
@@ -310,13 +313,12 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_row(const __nv_bfloat16* __re
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
         const int c = (i * 128 + t) * 8;
-        float g[8], a[8];
+        float g[8];
         if (w) loadw8(w + c, g);
-        if (addend) load8(addend + row * n + c, a);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
             const float cc = w ? g[e] + wadd : 1.0f;
-            v[i][e] = mult * (s * cc * d[i][e] - k * v[i][e]) + (addend ? a[e] : 0.0f);
+            v[i][e] = mult * (s * cc * d[i][e] - k * v[i][e]) + (addend ? ad[i][e] : 0.0f);
         }
         if (valid) store8(dx + row * n + c, v[i]);
     }
