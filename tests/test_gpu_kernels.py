@@ -145,16 +145,6 @@ def test_gemm_split_k_atomic(cuda, transposed, T, splits, r):
     assert rel_l2(to_np(out), want) < 1e-5
 
 
-def test_grad_tiling_rule():
-    """The adapter-gradient tiling at the config-5 shapes: the split counts measured best on B200."""
-    assert ops.grad_tiling(12288, 64) == (64, 3)
-    assert ops.grad_tiling(4096, 64) == (64, 4)
-    assert ops.grad_tiling(8192, 64) == (64, 2)
-    assert ops.grad_tiling(4096, 192) == (128, 2)
-    assert ops.grad_tiling(64, 64) == (64, 8)
-    assert ops.grad_tiling(64, 64, K=2048) == (64, 2)   # K / s >= 1024
-
-
 @pytest.mark.parametrize("b_mn,bn,splits", [(False, 64, 2), (True, 64, 3), (False, 128, 2), (True, 256, 4),
                                             (False, 64, 1)])
 def test_gemm_split_bf16_deterministic(cuda, b_mn, bn, splits):
