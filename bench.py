@@ -1,6 +1,7 @@
 """bench.py -- LoRA fwd+bwd+AdamW step throughput of the 9B-class synthetic hybrid model on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--config 5|4]
+    python bench.py --case NAME      # one small kernel case to profile under ncu (profile_case)
 
 One process per GPU (torchrun for N > 1, NCCL over NVLink). Each rank trains its own micro-batch of
 seq 4096 x 2 (config 5) on the same frozen IQR base and the same adapter; the adapter gradient is
@@ -345,6 +346,152 @@ def b200_arm(args):
     return 0
 
 
+def profile_case(case: str) -> None:
+    """One small, self-contained case of a hot kernel, for profiling a few launches under ncu
+    (`python bench.py --case NAME`): two or three launches of the kernel at a config-5 shape on operands
+    larger than the 126 MB L2, then exit. NAME is one of
+
+    gemm, gemm_dx   the config-5 gate_up forward GEMM (8192 x 24576 x 4096) / its input adjoint (B MN-major)
+    gemm_swiglu     the gate_up forward as the step runs it: LoRA tail, SwiGLU in the epilogue
+    gdn             one config-5 GDN layer, forward + backward
+    decode          the IQR decode of a 24576 x 4096 weight
+    norms / gnorm   rmsnorm fwd/bwd at 8192 x 4096 / gated rmsnorm at 8192 tokens x 32 heads x 128
+    swiglu          SwiGLU fwd/bwd at 8192 x 12288
+    loss            CE over 2048 x 151936 bf16 logits (one head chunk)
+    adamw           AdamW over the config-5 adapter (160.4 M f32 params)
+    conv            GDN conv prep fwd + bwd at 8192 tokens, 8192 channels
+    step            one config-5 training step after one warm-up step, inside an NVTX range "step"
+    """
+    import torch
+
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    if case == "gemm_swiglu":
+        from r97training_b200 import ops
+        M, F, K, r = 8192, 12288, 4096, 128
+        X = torch.randn(M, K, device=dev).bfloat16()
+        W = (torch.randn(2 * F, K, device=dev) * 0.02).bfloat16()
+        t = torch.randn(M, r, device=dev).bfloat16()
+        Bb = (torch.randn(2 * F, r, device=dev) * 0.02).bfloat16()
+        gu = torch.empty(M, 2 * F, device=dev, dtype=torch.bfloat16)
+        a = torch.empty(M, F, device=dev, dtype=torch.bfloat16)
+        for _ in range(3):
+            ops.gemm(X, W, gu, a2=t, b2=Bb, mode=ops.EPI_SWIGLU, out2=a)
+    elif case in ("gemm", "gemm_dx"):
+        from r97training_b200 import ops
+        M, N, K = 8192, 24576, 4096
+        X = torch.randn(M, K, device=dev).bfloat16()
+        W = (torch.randn(N, K, device=dev) * 0.02).bfloat16()
+        if case == "gemm":
+            Y = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            for _ in range(3):
+                ops.gemm(X, W, Y)
+        else:
+            dY = torch.randn(M, N, device=dev).bfloat16()
+            dX = torch.empty(M, K, device=dev, dtype=torch.bfloat16)
+            for _ in range(3):
+                ops.gemm(dY, W, dX, b_mn=True, N=K)
+    elif case == "gdn":
+        from r97training_b200.gdn import GdnPlan
+        T, H, Hg = 8192, 32, 16
+        q = torch.nn.functional.normalize(torch.randn(T, Hg, 128, device=dev), dim=-1).bfloat16()
+        k = torch.nn.functional.normalize(torch.randn(T, Hg, 128, device=dev), dim=-1).bfloat16()
+        v = torch.randn(T, H, 128, device=dev).bfloat16()
+        g = (-torch.nn.functional.softplus(torch.randn(T, H, device=dev))).view(-1, 64, H).cumsum(1).view(T, H)
+        beta = torch.sigmoid(torch.randn(T, H, device=dev))
+        do = (torch.randn(T, H, 128, device=dev) * 1e-2).bfloat16()
+        plan = GdnPlan([0, 4096, 8192], H, Hg, dev)
+        for _ in range(2):
+            o, _, sv = plan.forward(q, k, v, g.contiguous(), beta)
+            plan.backward(sv, do)
+    elif case == "decode":
+        from r97training_b200 import iqr as IQ
+        w = IQ.synth_weight(24576, 4096, seed=1, device=dev)
+        out = torch.empty(24576, 4096, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):
+            IQ.dequant_bf16(w, out=out)
+    elif case == "norms":
+        from r97training_b200 import ops
+        x = torch.randn(8192, 4096, device=dev).bfloat16()
+        dy = torch.randn(8192, 4096, device=dev).bfloat16()
+        w = torch.ones(4096, device=dev)
+        for _ in range(3):
+            ops.rmsnorm_fwd(x, w)
+            ops.rmsnorm_bwd(x, w, dy, addend=dy)
+    elif case == "gnorm":
+        from r97training_b200 import ops
+        T, H = 8192, 32
+        x = torch.randn(T * H, 128, device=dev).bfloat16()
+        z = torch.randn(T, H * 128, device=dev).bfloat16()
+        do = torch.randn(T * H, 128, device=dev).bfloat16()
+        w = torch.ones(128, device=dev)
+        dx, dz = torch.empty_like(x), torch.empty_like(z)
+        for _ in range(3):
+            ops.gated_rmsnorm_fwd(x, z, w)
+            ops.gated_rmsnorm_bwd(x, z, w, do, dx=dx, dz=dz)
+    elif case == "swiglu":
+        from r97training_b200 import ops
+        T, F = 8192, 12288
+        gu = torch.randn(T, 2 * F, device=dev).bfloat16()
+        y = torch.empty(T, F, device=dev, dtype=torch.bfloat16)
+        dy = torch.randn(T, F, device=dev).bfloat16()
+        dgu = torch.empty_like(gu)
+        for _ in range(3):
+            ops.swiglu_fwd(gu, y)
+            ops.swiglu_bwd(gu, dy, dgu)
+    elif case == "loss":
+        from r97training_b200 import ops
+        rows, vocab = 2048, 151936
+        logits = (torch.randn(rows, vocab, device=dev) * 2).bfloat16()
+        tgt = torch.randint(0, vocab, (rows,), device=dev, dtype=torch.int32)
+        loss = torch.empty(rows, device=dev)
+        grad = torch.empty_like(logits)
+        for _ in range(3):
+            ops.ce_kld(logits, tgt, loss_ce=loss, grad=grad, grad_scale=1.0 / rows)
+    elif case == "adamw":
+        from r97training_b200 import ops
+        n = 160_432_128
+        w = torch.randn(n, device=dev) * 0.01
+        m, v, g = torch.zeros_like(w), torch.zeros_like(w), torch.randn(n, device=dev) * 1e-3
+        for i in range(3):
+            ops.adamw_step(w, m, v, g, lr=1e-4, beta1=0.9, beta2=0.999, eps=1e-8, weight_decay=0.0,
+                           bc1=1.0 - 0.9 ** (i + 1), bc2=1.0 - 0.999 ** (i + 1))
+    elif case == "conv":
+        from r97training_b200 import ops
+        T, Hg, H = 8192, 16, 32
+        C = (2 * Hg + H) * 128
+        x = torch.randn(T, C + 8256, device=dev).bfloat16()
+        cw = torch.randn(C, 4, device=dev) * 0.5
+        cu = torch.tensor([0, 4096, 8192], dtype=torch.int32, device=dev)
+        q = torch.empty(T, Hg, 128, device=dev, dtype=torch.bfloat16)
+        k, v = torch.empty_like(q), torch.empty(T, H, 128, device=dev, dtype=torch.bfloat16)
+        dq, dk, dv = (torch.randn(T, H, 128, device=dev) for _ in range(3))
+        dx = torch.zeros_like(x)
+        for _ in range(3):
+            ops.conv_prep_fwd(x, cw, cu, 2, Hg, H, q, k, v)
+            ops.conv_prep_bwd(x, cw, cu, 2, Hg, H, dq, dk, dv, dx)
+    elif case == "step":
+        from r97training_b200.model import CONFIG5, Adapter, HybridModel, TrainStep
+        model = HybridModel(CONFIG5, dev)
+        adapter = Adapter(model, dev)
+        step = TrainStep(model, adapter)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        ids = torch.randint(0, CONFIG5.vocab, (CONFIG5.micro_batch, CONFIG5.seq), device=dev, generator=gen,
+                            dtype=torch.int32)
+        step.run(ids)
+        adapter.adamw()
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("step")
+        step.run(ids)
+        adapter.adamw()
+        torch.cuda.nvtx.range_pop()
+    else:
+        raise SystemExit(f"unknown case {case}")
+    torch.cuda.synchronize()
+
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -355,7 +502,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host each step "
                     "instead of replaying the step captured as a CUDA graph")
+    ap.add_argument("--case", default=None, help="run one small kernel case for ncu instead of the bench "
+                    "(see profile_case)")
     args = ap.parse_args()
+    if args.case:
+        profile_case(args.case)
+        return 0
     if args.impl == "reference":
         return reference_arm(args)
     return b200_arm(args)

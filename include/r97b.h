@@ -301,8 +301,9 @@ int r97b_global_norm(const float* g, int64_t n, float inv_k, float max_norm, dou
 /* r97b_global_norm for callers that cannot allocate device memory -- a host framework whose allocator
  * already owns the device's memory, or a loop that cannot afford cudaMalloc / cudaFree (cudaFree
  * synchronises the whole device). It takes no scratch argument and allocates nothing: its f64 partials
- * live in a fixed 512 KiB array inside the library, reserved on every GPU that loads the library until the
- * process exits. Same results as r97b_global_norm (the same kernels, bit for bit).
+ * live in a fixed 512 KiB array inside the library. A GPU holds that array from the first time it uses the
+ * library's kernels (at the latest, this entry point's first call on it) until the process exits. Same
+ * results as r97b_global_norm (the same kernels, bit for bit).
  *  - n > R97B_GLOBAL_NORM_NOALLOC_MAX_ELEMS (268,435,456) returns R97B_ETOOLARGE and launches nothing.
  *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that
  *    device current; make that first call before any stream capture.

@@ -114,8 +114,10 @@ __global__ void norm_finish_kernel(const double* __restrict__ partials, int64_t 
 //
 // Some callers of this library cannot allocate device memory: a host framework whose allocator already
 // owns the whole device budget, or a loop that must not pay cudaMalloc / cudaFree (cudaFree synchronises
-// the device). r97b_global_norm_noalloc serves them with the scratch below, reserved when the library is
-// loaded: every GPU that loads the library holds these 512 KiB until the process exits.
+// the device). r97b_global_norm_noalloc serves them with the scratch below. The array belongs to this
+// library's device module, which CUDA loads on a device when that device first uses the module (at the
+// latest, the first no-alloc call's address lookup); from then on that GPU holds these 512 KiB until the
+// process exits.
 constexpr int64_t kNoAllocMaxChunks = R97B_GLOBAL_NORM_NOALLOC_MAX_ELEMS / kNormChunk;
 static __device__ __align__(256) double g_noalloc_partials[kNoAllocMaxChunks];
 

@@ -388,11 +388,7 @@ int launch_pass(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& a
     constexpr int EPW = KIND == kPDS ? 4 : 2;
     static_assert((BN / 32) % EPW == 0, "column slices");
     auto kern = attn_bwd_kernel<KIND, BN, EPW>;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-        attr = true;
-    }
+    if (!smem_opt_in(kern, (int)C::kSmemBytes)) return R97B_ELAUNCH;
     int grid = num_sms();
     if (args.units < grid) grid = args.units;
     kern<<<grid, 128 + 128 * EPW, C::kSmemBytes, stream>>>(a, b, a2, b2, args);

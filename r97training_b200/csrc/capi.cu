@@ -3,12 +3,28 @@
 #include "r97b_internal.h"
 
 #include <atomic>
+#include <mutex>
+#include <set>
+#include <tuple>
 
 namespace r97b {
 namespace {
 std::atomic<unsigned long long> g_launches{0};
 }
 void add_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+bool smem_opt_in(const void* fn, int bytes) {
+    static std::mutex mu;
+    static std::set<std::tuple<const void*, int, int>> done;  // (kernel, device, bytes)
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return false;
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_tuple(fn, dev, bytes);
+    if (done.count(key)) return true;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
+    done.insert(key);
+    return true;
+}
 }  // namespace r97b
 
 extern "C" uint64_t r97b_launch_count(void) { return r97b::g_launches.load(std::memory_order_relaxed); }

@@ -1147,18 +1147,12 @@ constexpr size_t kSmemBA = (4 * D * kP128 + 4 * L * kP128) * 2 + (2 * L + 8) * 4
 constexpr size_t kSmemBB = (7 * L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 constexpr size_t kSmemKB = (L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 
-bool g_attr = false;
-
-void set_attrs() {
-    if (g_attr) return;
-    cudaFuncSetAttribute(gdn_fwd_prep, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemPrep);
-    cudaFuncSetAttribute(gdn_fwd_state, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemState);
-    cudaFuncSetAttribute(gdn_fwd_out, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemOut);
-    cudaFuncSetAttribute(gdn_bwd_state, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBState);
-    cudaFuncSetAttribute(gdn_bwd_a, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBA);
-    cudaFuncSetAttribute(gdn_bwd_b, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBB);
-    cudaFuncSetAttribute(gdn_kkt_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemKB);
-    g_attr = true;
+// Each kernel's dynamic shared-memory opt-in on the current device; false when the runtime refuses one.
+bool set_attrs() {
+    return smem_opt_in(gdn_fwd_prep, (int)kSmemPrep) && smem_opt_in(gdn_fwd_state, (int)kSmemState) &&
+           smem_opt_in(gdn_fwd_out, (int)kSmemOut) && smem_opt_in(gdn_bwd_state, (int)kSmemBState) &&
+           smem_opt_in(gdn_bwd_a, (int)kSmemBA) && smem_opt_in(gdn_bwd_b, (int)kSmemBB) &&
+           smem_opt_in(gdn_kkt_bwd, (int)kSmemKB);
 }
 
 bool dims_ok(const R97bGdnDims& d) {
@@ -1199,7 +1193,7 @@ extern "C" int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* a, void* 
         return R97B_EINVAL;
     // u and o are written two columns at a time
     if ((reinterpret_cast<uintptr_t>(a->u) & 7) || (reinterpret_cast<uintptr_t>(a->o) & 3)) return R97B_EINVAL;
-    set_attrs();
+    if (!set_attrs()) return R97B_ELAUNCH;
     const Dims dm = to_dims(*dims);
     cudaStream_t s = as_stream(stream);
     const auto* q = reinterpret_cast<const bf16*>(a->q);
@@ -1225,7 +1219,7 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
     if ((reinterpret_cast<uintptr_t>(a->dq) | reinterpret_cast<uintptr_t>(a->dk) | reinterpret_cast<uintptr_t>(a->dv)) & 7)
         return R97B_EINVAL;
     if ((dims->flags & R97B_GDN_SPLIT_KKT) && !a->dA) return R97B_EINVAL;
-    set_attrs();
+    if (!set_attrs()) return R97B_ELAUNCH;
     const Dims dm = to_dims(*dims);
     cudaStream_t s = as_stream(stream);
     const auto* q = reinterpret_cast<const bf16*>(a->q);
@@ -1248,7 +1242,7 @@ extern "C" int r97b_gdn_kkt_bwd(const R97bGdnDims* dims, const uint16_t* k, cons
                                 const float* A, const float* dA, float* dk, float* dbeta, float* dg, void* stream) {
     if (!dims || !dims_ok(*dims) || !k || !g || !beta || !A || !dA || !dk || !dbeta || !dg) return R97B_EINVAL;
     if (dims->n_chunks == 0) return R97B_OK;
-    set_attrs();
+    if (!set_attrs()) return R97B_ELAUNCH;
     const Dims dm = to_dims(*dims);
     gdn_kkt_bwd<<<dim3(dm.n_chunks, dm.H), 256, kSmemKB, as_stream(stream)>>>(
         dm, reinterpret_cast<const bf16*>(k), g, beta, A, dA, dk, dbeta, dg);

@@ -21,6 +21,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -733,12 +734,16 @@ bool operand_map(CUtensorMap* map, const R97bMat& m, int64_t rows, int64_t K, in
 }
 
 int num_sms() {
-    static int n = 0;
+    // per device: a process may drive GPUs of different SM counts
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    int n = cache[dev].load(std::memory_order_relaxed);
     if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
         if (n <= 0) n = 148;
+        cache[dev].store(n, std::memory_order_relaxed);
     }
     return n;
 }
@@ -822,11 +827,7 @@ int launch(const R97bGemm& g, cudaStream_t stream) {
     int grid = num_sms();
     if (units < grid) grid = units;
     auto kern = gemm_kernel<BN, A_MN, B_MN>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-        attr_set = true;
-    }
+    if (!smem_opt_in(kern, (int)C::kSmemBytes)) return R97B_ELAUNCH;
     kern<<<grid, kThreads, C::kSmemBytes, stream>>>(a1, b1, a2, b2, k);
     return launch_status();
 }
@@ -869,11 +870,7 @@ int launch_pair(const R97bGemm& g, cudaStream_t stream) {
     int pairs = num_sms() / 2;
     if (units < pairs) pairs = units;
     auto kern = gemm_pair_kernel<A_MN, B_MN>;
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
-        attr_set = true;
-    }
+    if (!smem_opt_in(kern, (int)C::kSmemBytes)) return R97B_ELAUNCH;
     kern<<<2 * pairs, kThreads, C::kSmemBytes, stream>>>(a1, b1, a2, b2, k);
     return launch_status();
 }

@@ -154,7 +154,9 @@ __global__ void __launch_bounds__(kThreads) ce_kld_kernel(const __nv_bfloat16* _
         const float lse_t = kTeacher ? r.mt + logf(r.st) : 0.0f;
         bc[0] = lse;
         bc[1] = lse_t;
-        if (loss_ce) loss_ce[row] = scored && targets ? lse - __bfloat162float(x[target]) : 0.0f;
+        // log(s) - (x_t - m), not lse - x_t: with a large row maximum, adding m first would round log(s)
+        // away (the reference's ce_position keeps this order, src/loss.cpp:21-39)
+        if (loss_ce) loss_ce[row] = scored && targets ? logf(r.s) - (__bfloat162float(x[target]) - r.m) : 0.0f;
         if (loss_kl) loss_kl[row] = kTeacher && scored ? r.u / r.st - lse_t + lse : 0.0f;
     }
     __syncthreads();

@@ -23,6 +23,14 @@ int gemm_run(const R97bGemm& g, cudaStream_t stream);
 bool make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
               int box_outer);
 int num_sms();
+// Opts kernel `fn` into `bytes` of dynamic shared memory on the device that is current. The runtime keeps
+// this attribute per device, so it is set once per (kernel, device, size), under a lock; returns false
+// when the runtime refuses it (capi.cu).
+bool smem_opt_in(const void* fn, int bytes);
+template <typename F>
+inline bool smem_opt_in(F* fn, int bytes) {
+    return smem_opt_in(reinterpret_cast<const void*>(fn), bytes);
+}
 int64_t gemm_workspace_bytes(const R97bGemm& g);
 unsigned gemm_error_word();
 

@@ -1,6 +1,7 @@
 // common.cpp -- the plugin's shared plumbing (common.h) and the device memory the rows use: the scratch
-// allocator with its high-water mark and the step's gradient stage (reference src/adjoint/device/
-// scratch.h and grad_stage.h, the API the reference's device rows allocate through).
+// allocator (a stream-ordered block pool with live / peak / allocation counters) and the step's gradient
+// stage. The API is the reference's (src/adjoint/device/scratch.h and grad_stage.h: the calls its
+// device rows allocate through); the pool behind it is this library's own.
 #include "common.h"
 
 #include <algorithm>
@@ -200,14 +201,106 @@ namespace r97 {
 namespace device {
 
 namespace {
-struct ScratchLedger {
-    std::mutex mu;
-    std::unordered_map<void*, int64_t> live;
-    ScratchStats stats;
+// The scratch allocator is a block pool rather than a ledger over raw allocations. Every row of this
+// process queues on the one row stream, so a block handed back by scratch_free can serve the next
+// scratch_alloc at once: the kernels that still read it are ahead of any new user in that stream's
+// order. Freed blocks therefore stay with the pool (no cudaFree, which would wait for the whole
+// device), sized up to a granule so near sizes share blocks, and go back to the device only when an
+// allocation cannot be met or the idle total passes a cap.
+class ScratchPool {
+public:
+    void* take(int64_t bytes) {
+        const int64_t cap = granule(bytes);
+        std::lock_guard<std::mutex> lock(mu_);
+        void* p = reuse(cap);
+        if (!p) p = fresh(cap);
+        if (!p) return nullptr;
+        held_[p] = Held{cap, bytes};
+        counters_.live_bytes += bytes;
+        counters_.peak_bytes = std::max(counters_.peak_bytes, counters_.live_bytes);
+        counters_.allocations += 1;
+        return p;
+    }
+
+    void give(void* p) {
+        std::lock_guard<std::mutex> lock(mu_);
+        auto it = held_.find(p);
+        if (it == held_.end()) return;  // not one of this pool's blocks
+        counters_.live_bytes -= it->second.asked;
+        idle_.emplace(it->second.cap, p);
+        idle_bytes_ += it->second.cap;
+        held_.erase(it);
+        if (idle_bytes_ > kIdleCap) shrink(kIdleCap / 2);
+    }
+
+    ScratchStats counters() {
+        std::lock_guard<std::mutex> lock(mu_);
+        return counters_;
+    }
+
+    void reset() {
+        std::lock_guard<std::mutex> lock(mu_);
+        if (!held_.empty())
+            throw std::runtime_error("device scratch: reset with " + std::to_string(held_.size()) +
+                                     " block(s) (" + std::to_string(counters_.live_bytes) +
+                                     " bytes) still taken");
+        shrink(0);
+        counters_ = ScratchStats{};
+    }
+
+private:
+    struct Held {
+        int64_t cap;    // the block's size
+        int64_t asked;  // what the caller asked for (the counters count this)
+    };
+    static constexpr int64_t kSmall = 1 << 20;             // below: 256-byte granules
+    static constexpr int64_t kIdleCap = int64_t(1) << 30;  // idle bytes kept before blocks go back
+
+    static int64_t granule(int64_t bytes) {
+        const int64_t g = bytes < kSmall ? 256 : kSmall;
+        return (bytes + g - 1) / g * g;
+    }
+
+    // The smallest idle block that fits and wastes at most half of itself.
+    void* reuse(int64_t cap) {
+        auto it = idle_.lower_bound(cap);
+        if (it == idle_.end() || it->first > 2 * cap) return nullptr;
+        void* p = it->second;
+        idle_bytes_ -= it->first;
+        idle_.erase(it);
+        return p;
+    }
+
+    void* fresh(int64_t cap) {
+        void* p = nullptr;
+        if (r97b_mem_alloc(&p, cap) == R97B_OK && p) return p;
+        shrink(0);  // the device may be full of idle blocks: hand them back and ask once more
+        p = nullptr;
+        return (r97b_mem_alloc(&p, cap) == R97B_OK) ? p : nullptr;
+    }
+
+    // Gives idle blocks back to the device, largest first, until at most `keep` idle bytes remain.
+    void shrink(int64_t keep) {
+        if (idle_bytes_ <= keep) return;
+        r97b_stream_sync(r97b_host::row_stream());  // the last readers of an idle block may still run
+        while (idle_bytes_ > keep && !idle_.empty()) {
+            auto last = std::prev(idle_.end());
+            idle_bytes_ -= last->first;
+            r97b_mem_free(last->second);
+            idle_.erase(last);
+        }
+    }
+
+    std::mutex mu_;
+    std::multimap<int64_t, void*> idle_;  // size -> block
+    std::unordered_map<void*, Held> held_;
+    int64_t idle_bytes_ = 0;
+    ScratchStats counters_;
 };
-ScratchLedger& ledger() {
-    static ScratchLedger l;
-    return l;
+
+ScratchPool& pool() {
+    static ScratchPool p;
+    return p;
 }
 
 struct StageLeaf {
@@ -227,47 +320,14 @@ Stage& stage() {
 }
 }  // namespace
 
-ScratchStats scratch_stats() {
-    ScratchLedger& l = ledger();
-    std::lock_guard<std::mutex> lock(l.mu);
-    return l.stats;
-}
+ScratchStats scratch_stats() { return pool().counters(); }
 
-void scratch_reset() {
-    ScratchLedger& l = ledger();
-    std::lock_guard<std::mutex> lock(l.mu);
-    if (l.stats.live_bytes != 0)
-        throw std::runtime_error("device scratch: " + std::to_string(l.stats.live_bytes) +
-                                 " bytes still held at reset");
-    l.stats = ScratchStats{};
-}
+void scratch_reset() { pool().reset(); }
 
-void* scratch_alloc(int64_t bytes) {
-    if (bytes <= 0) return nullptr;
-    void* p = nullptr;
-    if (r97b_mem_alloc(&p, bytes) != R97B_OK || !p) return nullptr;
-    ScratchLedger& l = ledger();
-    std::lock_guard<std::mutex> lock(l.mu);
-    l.live[p] = bytes;
-    l.stats.live_bytes += bytes;
-    l.stats.peak_bytes = std::max(l.stats.peak_bytes, l.stats.live_bytes);
-    ++l.stats.allocations;
-    return p;
-}
+void* scratch_alloc(int64_t bytes) { return bytes > 0 ? pool().take(bytes) : nullptr; }
 
 void scratch_free(void* p) {
-    if (!p) return;
-    {
-        ScratchLedger& l = ledger();
-        std::lock_guard<std::mutex> lock(l.mu);
-        auto it = l.live.find(p);
-        if (it == l.live.end()) return;  // not ours
-        l.stats.live_bytes -= it->second;
-        l.live.erase(it);
-    }
-    // the rows' kernels may still read the block: let the row stream drain before it goes
-    r97b_stream_sync(r97b_host::row_stream());
-    r97b_mem_free(p);
+    if (p) pool().give(p);
 }
 
 float* grad_stage_slot(const std::string& name, const std::vector<int64_t>& shape) {

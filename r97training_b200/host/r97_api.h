@@ -147,6 +147,10 @@ struct ScratchStats {
 };
 ScratchStats scratch_stats();
 void scratch_reset();
+// A block of at least `bytes` (256-byte aligned), or null when the device has no room. Blocks are
+// stream-ordered on the plugin's row stream: a freed block may serve the next allocation before the
+// kernels queued on that stream finish, so a caller that reads a block from another stream synchronises
+// that stream before scratch_free.
 void* scratch_alloc(int64_t bytes);
 void scratch_free(void* p);
 

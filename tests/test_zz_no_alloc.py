@@ -60,6 +60,28 @@ def test_no_alloc_matches_scratch_version_on_two_calls(cuda):
         assert abs(float(o[0]) - float(ref)) <= 1e-6 * float(ref)
 
 
+def test_no_alloc_calls_queued_back_to_back(cuda):
+    """Three calls of different sizes queued on one stream with no host wait between them, each writing
+    its own output slots, then one synchronise: stream order alone must keep each call's partials from
+    the next call's, so every result equals the scratch version's bit for bit."""
+    rs = np.random.RandomState(7)
+    sizes = ((4_194_305, 1.0, 0.0), (65_537, 0.25, 1e-3), (1_048_576, 1.0, 0.5))
+    gs = [torch.from_numpy((rs.normal(size=n) * 1e-2).astype(np.float32)).to(cuda) for n, _, _ in sizes]
+    wants = [_with_scratch(g, k, c) for g, (_, k, c) in zip(gs, sizes)]
+    torch.cuda.synchronize()
+    out = torch.zeros(2 * len(sizes), dtype=torch.float32, device=cuda)
+    s = torch.cuda.current_stream().cuda_stream
+    for i, (g, (n, inv_k, max_norm)) in enumerate(zip(gs, sizes)):
+        rc = lib().r97b_global_norm_noalloc(ctypes.c_void_p(g.data_ptr()), n, inv_k, max_norm,
+                                            ctypes.c_void_p(out.data_ptr() + 8 * i),
+                                            ctypes.c_void_p(out.data_ptr() + 8 * i + 4), ctypes.c_void_p(s))
+        assert rc == 0
+    torch.cuda.synchronize()
+    got = out.cpu().numpy().reshape(len(sizes), 2)
+    for i, w in enumerate(wants):
+        assert np.array_equal(w.cpu().numpy().view(np.uint32), got[i].view(np.uint32)), (i, w, got[i])
+
+
 def test_no_alloc_rejects_inputs_beyond_its_capacity(cuda):
     out = torch.zeros(2, dtype=torch.float32, device=cuda)
     g = torch.zeros(1, dtype=torch.float32, device=cuda)  # never read: the size check comes first
