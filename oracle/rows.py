@@ -193,12 +193,12 @@ def ce_rows(logits, targets, grad_scale=1.0):
     m = x.max(-1, keepdims=True)
     e = np.exp(x - m)
     s = e.sum(-1, keepdims=True)
-    lse = m + np.log(s)
     p = e / s
     rows = np.arange(x.shape[0])
     scored = targets >= 0
     tt = np.where(scored, targets, 0)
-    loss = np.where(scored, lse[:, 0] - x[rows, tt], 0.0)
+    # log(s) - (x_t - m): the reference's order, which keeps log(s) when m is large
+    loss = np.where(scored, np.log(s[:, 0]) - (x[rows, tt] - m[:, 0]), 0.0)
     grad = p.copy()
     grad[rows, tt] -= 1.0
     grad *= grad_scale
@@ -358,3 +358,99 @@ def gates_bwd(a, b, a_log, dt_bias, cu, dg, dbeta, chunk=64):
     sp = np.where(av > 20.0, 1.0, 1.0 / (1.0 + np.exp(-av)))
     sb = 1.0 / (1.0 + np.exp(-b))
     return tail * (-np.exp(a_log))[None, :] * sp, dbeta * sb * (1.0 - sb)
+
+
+# ----------------------------------------------------------------------------- gated attention
+
+def rope_fwd(x, positions, rotary_dim, theta, head_dim, scale=1.0):
+    """Partial NeoX rotary embedding of every head of x [T, heads * head_dim]: within each head the pairs
+    (i, i + rotary_dim/2), i < rotary_dim/2, turn by position * theta^(-2i/rotary_dim); the columns past
+    rotary_dim pass through (reference src/adjoint/host/qk.cpp:54-112, rope.cpp:72-90)."""
+    T = x.shape[0]
+    xh = x.reshape(T, -1, head_dim)
+    half = rotary_dim // 2
+    inv = theta ** (-2.0 * np.arange(half) / rotary_dim)
+    ang = (np.asarray(positions, np.float64) / scale)[:, None] * inv[None, :]
+    c, s = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+    out = xh.copy()
+    x0, x1 = xh[..., :half], xh[..., half:rotary_dim]
+    out[..., :half] = x0 * c - x1 * s
+    out[..., half:rotary_dim] = x0 * s + x1 * c
+    return out.reshape(x.shape)
+
+
+def rope_bwd(dy, positions, rotary_dim, theta, head_dim, scale=1.0):
+    """The transposed rotation (reference src/adjoint/host/qk.cpp:114-150, rope.cpp:92-106)."""
+    T = dy.shape[0]
+    dh = dy.reshape(T, -1, head_dim)
+    half = rotary_dim // 2
+    inv = theta ** (-2.0 * np.arange(half) / rotary_dim)
+    ang = (np.asarray(positions, np.float64) / scale)[:, None] * inv[None, :]
+    c, s = np.cos(ang)[:, None, :], np.sin(ang)[:, None, :]
+    out = dh.copy()
+    y0, y1 = dh[..., :half], dh[..., half:rotary_dim]
+    out[..., :half] = c * y0 + s * y1
+    out[..., half:rotary_dim] = -s * y0 + c * y1
+    return out.reshape(dy.shape)
+
+
+def _attn_rows(cu, T):
+    return [(int(cu[i]), int(cu[i + 1])) for i in range(len(cu) - 1)] if cu is not None else [(0, T)]
+
+
+def attention_fwd(q, k, v, scale=None, cu=None):
+    """Causal grouped-query softmax attention per sequence: q [T, Hq, D], k, v [T, Hkv, D], query head h
+    reads key/value head h // (Hq / Hkv); out[t, h] = sum_{j <= t} softmax_j(scale q_t . k_j) v_j (reference
+    src/adjoint/host/attention.cpp:261-313, the `attn_paged` twin over a pool that holds each sequence's
+    keys at their positions)."""
+    T, Hq, D = q.shape
+    grp = Hq // k.shape[1]
+    scale = 1.0 / np.sqrt(D) if scale is None else scale
+    out = np.zeros_like(q, dtype=np.float64)
+    for a, b in _attn_rows(cu, T):
+        n = b - a
+        mask = np.triu(np.ones((n, n), bool), 1)
+        for h in range(Hq):
+            s = (q[a:b, h] @ k[a:b, h // grp].T) * scale
+            s = np.where(mask, -np.inf, s)
+            p = np.exp(s - s.max(-1, keepdims=True))
+            p /= p.sum(-1, keepdims=True)
+            out[a:b, h] = p @ v[a:b, h // grp]
+    return out
+
+
+def attention_bwd(q, k, v, dy, scale=None, cu=None):
+    """The adjoint: with p the row's weights and G_j = dy . v_j, ds_j = p_j (G_j - sum_k p_k G_k); dq = scale
+    ds k, dk = scale ds^T q, dv = p^T dy, the key/value cotangents summed over the query heads of a group
+    (reference src/adjoint/host/attention.cpp:322-407)."""
+    T, Hq, D = q.shape
+    grp = Hq // k.shape[1]
+    scale = 1.0 / np.sqrt(D) if scale is None else scale
+    dq, dk, dv = np.zeros_like(q, np.float64), np.zeros_like(k, np.float64), np.zeros_like(v, np.float64)
+    for a, b in _attn_rows(cu, T):
+        n = b - a
+        mask = np.triu(np.ones((n, n), bool), 1)
+        for h in range(Hq):
+            kh = h // grp
+            s = (q[a:b, h] @ k[a:b, kh].T) * scale
+            s = np.where(mask, -np.inf, s)
+            p = np.exp(s - s.max(-1, keepdims=True))
+            p /= p.sum(-1, keepdims=True)
+            G = dy[a:b, h] @ v[a:b, kh].T
+            ds = p * (G - (p * G).sum(-1, keepdims=True))
+            dq[a:b, h] += scale * ds @ k[a:b, kh]
+            dk[a:b, kh] += scale * ds.T @ q[a:b, h]
+            dv[a:b, kh] += p.T @ dy[a:b, h]
+    return dq, dk, dv
+
+
+def gate_fwd(o, gate):
+    """The attention output gate: o * sigmoid(gate) (reference elementwise.cpp `sigmoid` then `mul`,
+    :234-242 and :169-183)."""
+    return o * _sigmoid(gate)
+
+
+def gate_bwd(o, gate, dy):
+    """d o = dy sigmoid(gate); d gate = dy o s (1 - s) (reference elementwise.cpp:185-251)."""
+    s = _sigmoid(gate)
+    return dy * s, dy * o * s * (1.0 - s)
