@@ -238,7 +238,11 @@ def test_ce_kld(cuda, vocab, rows):
     l1, g1 = R.ce_rows(sn, tg, 0.5)
     l2, g2 = R.kld_rows(sn, tn, 0.5, targets=tg)
     np.testing.assert_allclose(lce.cpu().numpy(), l1, rtol=1e-4, atol=1e-4)
-    np.testing.assert_allclose(lkl.cpu().numpy(), l2, rtol=1e-3, atol=1e-4)
+    # the KL sum carries t - s, which row 5's offset makes ~1.6e4: f32 keeps ~2e-3 of it absolute there
+    kl = lkl.cpu().numpy()
+    keep = np.arange(rows) != 5
+    np.testing.assert_allclose(kl[keep], l2[keep], rtol=1e-3, atol=1e-4)
+    assert abs(kl[5] - l2[5]) <= 4e-3, (kl[5], l2[5])
     assert_close_bf16(to_np(grad), g1 + 0.3 * g2, rel=5e-3, what="ce+kl grad")
     # in place
     lce2, _ = ops.ce_kld(sd, torch.from_numpy(tg).to(cuda), grad=sd, grad_scale=0.5)

@@ -32,11 +32,13 @@ def test_small_hybrid_steps_are_finite_and_learn(cuda):
 
 
 def test_graph_replay_matches_eager_steps(cuda):
-    """The step captured as one CUDA graph (forward, backward, AdamW) and replayed gives the eager steps'
-    losses and the same adapter updates from the same start. The GDN adjoint sums some per-row terms
-    with shared-memory float atomics, so two eager runs differ in the last bits too, and early AdamW
-    steps move every weight by about lr whatever the gradient's size: the updates are compared by
-    direction and size, against the spread of two eager runs."""
+    """The step captured as one CUDA graph and replayed gives the eager step's results from the same start:
+    one step's adapter gradient (captured without the update) and the losses of four steps with AdamW
+    inside the graph. The runs are not bit-identical: the GDN adjoint adds some per-row terms with
+    shared-memory float atomics and the adapter-gradient GEMMs reduce their split-K partials with float
+    atomics, so sums land in a different order from run to run. That changes the last bits of f32 sums
+    only, so the gradient is held to relative L2 <= 1e-4 and cosine >= 0.9999, well inside the north star's
+    bar (1e-2 and 0.999), and two eager runs are held to the same."""
     from r97training_b200.model import GraphStep
     cfg = HybridConfig(hidden=512, layers=4, gdn_heads=4, gdn_qk_heads=2, attn_heads=2, attn_kv_heads=1, ffn=1024,
                        vocab=4096, rank=16, alpha=32, seq=256, micro_batch=2, lr=1e-3)
@@ -44,32 +46,45 @@ def test_graph_replay_matches_eager_steps(cuda):
     gen.manual_seed(7)
     batches = [torch.randint(0, cfg.vocab, (cfg.micro_batch, cfg.seq), device=cuda, generator=gen,
                              dtype=torch.int32) for _ in range(4)]
-    runs = []
-    for graph in (False, False, True):
+
+    def fresh():
         model = HybridModel(cfg, cuda)
         ad = Adapter(model, cuda)
-        step = TrainStep(model, ad, head_chunk=256)
-        w0 = ad.w.clone()
-        losses = [float(step.run(batches[0]))]
+        return ad, TrainStep(model, ad, head_chunk=256)
+
+    grads = []
+    for graph in (False, False, True):
+        ad, step = fresh()
+        step.run(batches[0])  # eager first: attributes, encoders and buffers are set up outside a capture
+        if graph:
+            ad.g.zero_()
+            gs = GraphStep(step, batches[0], update=False)
+            gs.replay(batches[0])
+        torch.cuda.synchronize()
+        grads.append(ad.g.double().clone())
+    for other, what in ((grads[1], "eager vs eager"), (grads[2], "graph vs eager")):
+        rel = float((other - grads[0]).norm() / grads[0].norm())
+        cos = float((other * grads[0]).sum() / (other.norm() * grads[0].norm()))
+        assert rel <= 1e-4 and cos >= 0.9999, (what, rel, cos)
+
+    losses = []
+    for graph in (False, True):
+        ad, step = fresh()
+        ls = [float(step.run(batches[0]))]
         ad.adamw()
         if graph:
             gs = GraphStep(step, batches[1])
             for b in batches[1:]:
-                losses.append(float(gs.replay(b)))
+                ls.append(float(gs.replay(b)))
         else:
             for b in batches[1:]:
-                losses.append(float(step.run(b)))
+                ls.append(float(step.run(b)))
                 ad.adamw()
         torch.cuda.synchronize()
-        runs.append((losses, (ad.w - w0).double(), ad.step))
-    (le, de, se), (l2, d2, s2), (lg, dg, sg) = runs
-    assert se == s2 == sg == 4
-    for a, b in zip(le, lg):
-        assert abs(a - b) <= 1e-3 * abs(a), (le, lg)
-    cos = float((de * dg).sum() / (de.norm() * dg.norm()))
-    spread = float((de - d2).norm() / de.norm())  # two eager runs
-    assert cos > 0.99, cos
-    assert float((de - dg).norm() / de.norm()) <= max(3 * spread, 0.05), (spread, cos)
+        assert ad.step == 4
+        losses.append(ls)
+    for a, b in zip(*losses):
+        assert abs(a - b) <= 1e-3 * abs(a), losses
 
 
 def test_trained_adapter_saves_and_loads_as_peft(cuda, tmp_path):

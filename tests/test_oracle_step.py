@@ -59,3 +59,19 @@ def test_composed_reference_step_matches_finite_differences():
         fd = (lp - lm) / (2 * eps)
         # the gradient is stored as f32 (the reference's ParamSet): compare at f32 resolution
         assert abs(fd - g) <= 2e-5 * max(abs(fd), abs(g)) + 1e-9, (name, idx, fd, g)
+
+
+def test_bf16_storage_replay_is_deterministic_and_scoped():
+    """The rows replayed at the B200 step's storage precision: the same loss and gradients on a second call
+    (the reference's rows are deterministic), a loss within bf16 rounding of the exact step's, and the mode
+    ends with the call."""
+    if not oracle.ref_available():
+        pytest.skip("reference host library not built and reference tree absent")
+    from oracle import step as S
+    m, ids, tg = _tiny()
+    l0, _ = S.reference_step(m, ids, tg, backward=False)
+    l1, g1 = S.reference_step(m, ids, tg, bf16_store=True)
+    l2, g2 = S.reference_step(m, ids, tg, bf16_store=True)
+    assert l1 == l2 and all(np.array_equal(g1[n], g2[n]) for n in g1)
+    assert abs(l1 - l0) <= 1e-2 * abs(l0), (l0, l1)
+    assert S._store is S._exact
