@@ -50,15 +50,16 @@ def _cfg_dict(cfg, model_groups, base_weights, adapter_params):
 
 
 def _static_sizes(cfg):
-    from r97training_b200.model import groups_of
+    from r97training_b200.model import groups_of, has_lora
     groups = {k: groups_of(cfg, k) for k in ("gdn", "attn")}
     base = cfg.vocab * cfg.hidden
     adapter = 0
     for kind in cfg.kinds:
-        for _, k, projs in groups[kind]:
+        for gname, k, projs in groups[kind]:
             for _, n in projs:
                 base += n * k
-                adapter += cfg.rank * (n + k)
+                if has_lora(cfg, gname):
+                    adapter += cfg.rank * (n + k)
     return groups, base, adapter
 
 

@@ -439,34 +439,37 @@ int r97b_swiglu_fwd(const uint16_t* gu, int64_t ldgu, int64_t rows, int64_t n, u
 int r97b_swiglu_bwd(const uint16_t* gu, int64_t ldgu, int64_t rows, int64_t n, const uint16_t* dy, int64_t lddy,
                     uint16_t* dgu, int64_t lddgu, void* stream);
 
-/* Per (token, head) row of 256: RMSNorm (gain w f32 [256], eps) then NeoX RoPE on the first `rot` dims
- * (cos / sin tables f32 [S, rot/2]), from rows of x (row_stride, head h at h * head_stride) into
- * out[b, head, s, :] for a fixed-length batch (T = B * S). Replaces: the q/k norm + rope forward,
+/* Per (token, head) row of head_dim (128 or 256): RMSNorm (gain w f32 [head_dim], eps) then NeoX RoPE on the
+ * first `rot` dims (cos / sin tables f32 [S, rot/2]), from rows of x (row_stride, head h at h * head_stride)
+ * into out[b, head, s, :] for a fixed-length batch (T = B * S). rot / 2 / (head_dim / 32) must be a power of
+ * two up to 16 (rot 16..256 at head_dim 256, 8..128 at 128). Replaces: the q/k norm + rope forward,
  * src/adjoint/host/qk.cpp and rope.cpp. */
 int r97b_qk_norm_rope_fwd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
-                          const float* w, const float* cos_tab, const float* sin_tab, int32_t rot, int64_t T,
-                          int32_t S, float eps, uint16_t* out, void* stream);
+                          int32_t head_dim, const float* w, const float* cos_tab, const float* sin_tab, int32_t rot,
+                          int64_t T, int32_t S, float eps, uint16_t* out, void* stream);
 
 /* Its adjoint into dx (rows of dx_stride, the same head layout). Replaces: qk_adjoint_kernel,
  * src/adjoint/device/qk.hip:254-488. */
 int r97b_qk_norm_rope_bwd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
-                          const float* w, const float* cos_tab, const float* sin_tab, int32_t rot, int64_t T,
-                          int32_t S, float eps, const uint16_t* dout, uint16_t* dx, int64_t dx_stride,
+                          int32_t head_dim, const float* w, const float* cos_tab, const float* sin_tab, int32_t rot,
+                          int64_t T, int32_t S, float eps, const uint16_t* dout, uint16_t* dx, int64_t dx_stride,
                           void* stream);
 
-/* [T, heads, 256] rows -> [B, heads, S, 256] (reverse = 1: back into the rows). */
-int r97b_to_bhsd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads, int64_t T, int32_t S,
-                 uint16_t* out, int32_t reverse, void* stream);
+/* [T, heads, head_dim] rows -> [B, heads, S, head_dim] (reverse = 1: back into the rows); head_dim 128 or
+ * 256. */
+int r97b_to_bhsd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads, int32_t head_dim,
+                 int64_t T, int32_t S, uint16_t* out, int32_t reverse, void* stream);
 
-/* y[t, h * 256 + d] = attn[b, h, s, d] * sigmoid(gate[t, h * gate_hs + d]): the gated attention's output
- * gate. Replaces: the gate half of attention.cpp's twin and gate_ste_kernel, attention.hip:562. */
+/* y[t, h * head_dim + d] = attn[b, h, s, d] * sigmoid(gate[t, h * gate_hs + d]): the gated attention's
+ * output gate (head_dim 128 or 256). Replaces: the gate half of attention.cpp's twin and gate_ste_kernel,
+ * attention.hip:562. */
 int r97b_gate_mul_fwd(const uint16_t* attn, const uint16_t* gate, int64_t gate_stride, int32_t gate_hs,
-                      int32_t heads, int64_t T, int32_t S, uint16_t* y, void* stream);
+                      int32_t heads, int32_t head_dim, int64_t T, int32_t S, uint16_t* y, void* stream);
 
-/* Its adjoint: dattn [B, heads, S, 256] and dgate (rows of dgate_stride). */
+/* Its adjoint: dattn [B, heads, S, head_dim] and dgate (rows of dgate_stride). */
 int r97b_gate_mul_bwd(const uint16_t* attn, const uint16_t* gate, int64_t gate_stride, int32_t gate_hs,
-                      int32_t heads, int64_t T, int32_t S, const uint16_t* dy, uint16_t* dattn, uint16_t* dgate,
-                      int64_t dgate_stride, void* stream);
+                      int32_t heads, int32_t head_dim, int64_t T, int32_t S, const uint16_t* dy, uint16_t* dattn,
+                      uint16_t* dgate, int64_t dgate_stride, void* stream);
 
 /* out[t, :] = table[ids[t], :] (bf16, zero for an id outside [0, vocab)). Replaces: embed_lookup's twin,
  * src/adjoint/host/linear.cpp:388-418 (a stop: no adjoint). */

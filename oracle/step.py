@@ -56,6 +56,10 @@ def _linear_fwd(x, projs, lora, scale):
         g_ops = [Operand("a", "bf16", (M, K)), b_op, Operand("y", "bf16", (M, n), written=True)]
         g_par = {"M": M, "N": n, "K": K}
         y = ref_twin("gemm_nt", g_par, g_ops, {"a": x, "b": b_val})["y"]
+        if prefix + ".lora_A" not in lora:  # a projection without an adapter
+            outs.append(y)
+            saved.append((prefix, g_ops, g_par, dict(a=x, b=b_val, y=y), None, None, None, None))
+            continue
         # the GEMMs read the factors' bf16 mirrors
         A, B = _store(lora[prefix + ".lora_A"]), _store(lora[prefix + ".lora_B"])
         r = A.shape[0]
@@ -81,6 +85,10 @@ def _linear_bwd(saved, dy, grads):
         n = g_ops[1].shape[0]
         d = dy[:, col:col + n]
         col += n
+        if sh_ops is None:
+            part = ref_adjoint("gemm_nt", g_par, g_ops, g_fwd, {"y": d})[0]["a"]
+            dx = part if dx is None else dx + part
+            continue
         dc_ex, gr = ref_adjoint("lora_expand", {}, ex_ops, ex_fwd, {"y": d}, prefix=prefix)
         grads.update(gr)
         dc_sh, gr = ref_adjoint("lora_shrink", {}, sh_ops, sh_fwd, {"t": _store(dc_ex["t"])}, prefix=prefix)

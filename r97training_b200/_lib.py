@@ -122,13 +122,14 @@ _SIGS = {
     "r97b_gates_bwd": (c_i32, [c_vp, c_i64, c_vp, c_vp, c_vp, c_vp, c_i32, c_i32, c_vp, c_vp, c_vp, c_i64, c_vp]),
     "r97b_swiglu_fwd": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp]),
     "r97b_swiglu_bwd": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp]),
-    "r97b_qk_norm_rope_fwd": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i64, c_i32, c_f32, c_vp,
-                                      c_vp]),
-    "r97b_qk_norm_rope_bwd": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i64, c_i32, c_f32, c_vp,
-                                      c_vp, c_i64, c_vp]),
-    "r97b_to_bhsd": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_i64, c_i32, c_vp, c_i32, c_vp]),
-    "r97b_gate_mul_fwd": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_i32, c_i64, c_i32, c_vp, c_vp]),
-    "r97b_gate_mul_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_i32, c_i64, c_i32, c_vp, c_vp, c_vp, c_i64, c_vp]),
+    "r97b_qk_norm_rope_fwd": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i64, c_i32, c_f32,
+                                      c_vp, c_vp]),
+    "r97b_qk_norm_rope_bwd": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_i32, c_vp, c_vp, c_vp, c_i32, c_i64, c_i32, c_f32,
+                                      c_vp, c_vp, c_i64, c_vp]),
+    "r97b_to_bhsd": (c_i32, [c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_i32, c_vp, c_i32, c_vp]),
+    "r97b_gate_mul_fwd": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_i32, c_vp, c_vp]),
+    "r97b_gate_mul_bwd": (c_i32, [c_vp, c_vp, c_i64, c_i32, c_i32, c_i32, c_i64, c_i32, c_vp, c_vp, c_vp, c_i64,
+                                  c_vp]),
     "r97b_embed": (c_i32, [c_vp, c_i64, c_i64, c_vp, c_i64, c_i64, c_vp, c_vp]),
     "r97b_cast_f32_bf16": (c_i32, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_vp]),
     "r97b_launch_count": (ctypes.c_uint64, []),

@@ -29,7 +29,7 @@ bool smem_opt_in(const void* fn, int bytes) {
 
 extern "C" uint64_t r97b_launch_count(void) { return r97b::g_launches.load(std::memory_order_relaxed); }
 
-extern "C" int r97b_abi_version(void) { return 3; }
+extern "C" int r97b_abi_version(void) { return 4; }
 
 extern "C" int r97b_device_error(unsigned int* out_bits) {
     unsigned bits = r97b::gemm_error_word();

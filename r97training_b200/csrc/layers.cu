@@ -549,14 +549,15 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const __nv_bfloat16* __
 
 // ------------------------------------------------------------------------------------------- attention prep
 
-// One warp per (token, head) row of 256: RMSNorm (eps) with gain w, then NeoX RoPE on the first
-// `rot` dims (lanes 0..rot/8-1), into out[b, head, s, :] with b, s from the token's sequence.
+// One warp per (token, head) row of D = 32 NV (128 or 256): RMSNorm (eps) with gain w, then NeoX RoPE on the
+// first `rot` dims (lanes 0..rot/NV-1), into out[b, head, s, :] with b, s from the token's sequence. Each
+// lane holds NV consecutive values of the row.
 struct QkArgs {
     const __nv_bfloat16* x;  // rows of `row_stride`, head h at h * head_stride
     int64_t row_stride;
     int head_stride;
     int heads;
-    const float* w;          // [256]
+    const float* w;          // [D]
     const float* cosb;       // [S, rot/2]
     const float* sinb;
     int rot;
@@ -576,63 +577,101 @@ __device__ __forceinline__ void split_row(int64_t row, int d, int& q, int& r) {
     }
 }
 
+// NV consecutive bf16 values (NV = 8: one 16-byte load; NV = 4: one 8-byte load) and f32 gains.
+template <int NV>
+__device__ __forceinline__ void ldv(const __nv_bfloat16* p, float (&v)[NV]) {
+    if constexpr (NV == 8) {
+        ld8(p, v);
+    } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(p);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+        v[0] = a.x, v[1] = a.y, v[2] = b.x, v[3] = b.y;
+    }
+}
+template <int NV>
+__device__ __forceinline__ void stv(__nv_bfloat16* p, const float (&v)[NV]) {
+    if constexpr (NV == 8) {
+        st8(p, v);
+    } else {
+        uint2 u;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+        h[0] = __floats2bfloat162_rn(v[0], v[1]);
+        h[1] = __floats2bfloat162_rn(v[2], v[3]);
+        *reinterpret_cast<uint2*>(p) = u;
+    }
+}
+template <int NV>
+__device__ __forceinline__ void ldvf(const float* p, float (&v)[NV]) {
+    if constexpr (NV == 8) {
+        ld8f(p, v);
+    } else {
+        const float4 a = *reinterpret_cast<const float4*>(p);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+    }
+}
+
+template <int NV>
 __global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(QkArgs a, __nv_bfloat16* __restrict__ out) {
+    constexpr int D = 32 * NV;
     const int lane = threadIdx.x & 31;
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (row >= (int64_t)a.T * a.heads) return;
     int t, h, b, s;
     split_row(row, a.heads, t, h);
     split_row(t, a.S, b, s);
-    float v[8], w[8];
-    ld8(a.x + (int64_t)t * a.row_stride + h * a.head_stride + lane * 8, v);
-    ld8f(a.w + lane * 8, w);
+    float v[NV], w[NV];
+    ldv<NV>(a.x + (int64_t)t * a.row_stride + h * a.head_stride + lane * NV, v);
+    ldvf<NV>(a.w + lane * NV, w);
     float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss = fmaf(v[i], v[i], ss);
+    for (int i = 0; i < NV; ++i) ss = fmaf(v[i], v[i], ss);
     ss = sum32(ss);
-    const float r = rsqrtf(ss / 256.0f + a.eps);
+    const float r = rsqrtf(ss / (float)D + a.eps);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] *= r * w[i];
+    for (int i = 0; i < NV; ++i) v[i] *= r * w[i];
     const int half = a.rot / 2;          // rotary pairs (i, i + half)
-    const int pl = half / 8;             // lanes holding the first half
-    float o[8];
+    const int pl = half / NV;            // lanes holding the first half
+    float o[NV];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, v[i], pl);  // every lane joins
+    for (int i = 0; i < NV; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, v[i], pl);  // every lane joins
     if (lane < 2 * pl) {
         const bool first = lane < pl;
-        const int j0 = (first ? lane : lane - pl) * 8;
+        const int j0 = (first ? lane : lane - pl) * NV;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < NV; ++i) {
             const float cs = a.cosb[s * half + j0 + i], sn = a.sinb[s * half + j0 + i];
             v[i] = first ? v[i] * cs - o[i] * sn : v[i] * cs + o[i] * sn;
         }
     }
-    st8(out + (((int64_t)b * a.heads + h) * a.S + s) * 256 + lane * 8, v);
+    stv<NV>(out + (((int64_t)b * a.heads + h) * a.S + s) * D + lane * NV, v);
 }
 
 // The adjoint: inverse rotation of dout, then the RMSNorm adjoint against the saved pre-norm row;
 // dx into rows of `dx_stride` (the projection's cotangent buffer).
+template <int NV>
 __global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(QkArgs a, const __nv_bfloat16* __restrict__ dout,
                                                                __nv_bfloat16* __restrict__ dx, int64_t dx_stride) {
+    constexpr int D = 32 * NV;
     const int lane = threadIdx.x & 31;
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     if (row >= (int64_t)a.T * a.heads) return;
     int t, h, b, s;
     split_row(row, a.heads, t, h);
     split_row(t, a.S, b, s);
-    float d[8], x[8], w[8];
-    ld8(dout + (((int64_t)b * a.heads + h) * a.S + s) * 256 + lane * 8, d);
-    ld8(a.x + (int64_t)t * a.row_stride + h * a.head_stride + lane * 8, x);
-    ld8f(a.w + lane * 8, w);
-    const int half = a.rot / 2, pl = half / 8;
-    float o[8];
+    float d[NV], x[NV], w[NV];
+    ldv<NV>(dout + (((int64_t)b * a.heads + h) * a.S + s) * D + lane * NV, d);
+    ldv<NV>(a.x + (int64_t)t * a.row_stride + h * a.head_stride + lane * NV, x);
+    ldvf<NV>(a.w + lane * NV, w);
+    const int half = a.rot / 2, pl = half / NV;
+    float o[NV];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, d[i], pl);
+    for (int i = 0; i < NV; ++i) o[i] = __shfl_xor_sync(0xFFFFFFFFu, d[i], pl);
     if (lane < 2 * pl) {
         const bool first = lane < pl;
-        const int j0 = (first ? lane : lane - pl) * 8;
+        const int j0 = (first ? lane : lane - pl) * NV;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < NV; ++i) {
             const float cs = a.cosb[s * half + j0 + i], sn = a.sinb[s * half + j0 + i];
             // y1 = x1 c - x2 s, y2 = x2 c + x1 s  =>  dx1 = dy1 c + dy2 s, dx2 = dy2 c - dy1 s
             d[i] = first ? d[i] * cs + o[i] * sn : d[i] * cs - o[i] * sn;
@@ -640,23 +679,25 @@ __global__ void __launch_bounds__(256) qk_norm_rope_bwd_kernel(QkArgs a, const _
     }
     float ss = 0.0f, tt = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < NV; ++i) {
         ss = fmaf(x[i], x[i], ss);
         tt = fmaf(d[i] * x[i], w[i], tt);
     }
     ss = sum32(ss);
     tt = sum32(tt);
-    const float r = rsqrtf(ss / 256.0f + a.eps);
-    const float kk = r * r * r * tt / 256.0f;
+    const float r = rsqrtf(ss / (float)D + a.eps);
+    const float kk = r * r * r * tt / (float)D;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) d[i] = r * w[i] * d[i] - kk * x[i];
-    st8(dx + (int64_t)t * dx_stride + h * a.head_stride + lane * 8, d);
+    for (int i = 0; i < NV; ++i) d[i] = r * w[i] * d[i] - kk * x[i];
+    stv<NV>(dx + (int64_t)t * dx_stride + h * a.head_stride + lane * NV, d);
 }
 
-// [T, heads, 256] rows (row stride) -> [B, heads, S, 256] and back
+// [T, heads, D] rows (row stride) -> [B, heads, S, D] and back
+template <int NV>
 __global__ void __launch_bounds__(256) to_bhsd_kernel(const __nv_bfloat16* __restrict__ x, int64_t row_stride,
                                                       int head_stride, int heads, int T, int S,
                                                       __nv_bfloat16* __restrict__ out, int reverse) {
+    constexpr int D = 32 * NV;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)T * heads * 32) return;
     const int lane = (int)(gid & 31);
@@ -664,19 +705,25 @@ __global__ void __launch_bounds__(256) to_bhsd_kernel(const __nv_bfloat16* __res
     int t, h, b, s;
     split_row(row, heads, t, h);
     split_row(t, S, b, s);
-    const int64_t at_bhsd = (((int64_t)b * heads + h) * S + s) * 256 + lane * 8;
-    const int64_t at_row = (int64_t)t * row_stride + (int64_t)h * head_stride + lane * 8;
-    if (reverse)
-        *reinterpret_cast<uint4*>(const_cast<__nv_bfloat16*>(x) + at_row) = *reinterpret_cast<const uint4*>(out + at_bhsd);
-    else
-        *reinterpret_cast<uint4*>(out + at_bhsd) = *reinterpret_cast<const uint4*>(x + at_row);
+    const int64_t at_bhsd = (((int64_t)b * heads + h) * S + s) * D + lane * NV;
+    const int64_t at_row = (int64_t)t * row_stride + (int64_t)h * head_stride + lane * NV;
+    float v[NV];
+    if (reverse) {
+        ldv<NV>(out + at_bhsd, v);
+        stv<NV>(const_cast<__nv_bfloat16*>(x) + at_row, v);
+    } else {
+        ldv<NV>(x + at_row, v);
+        stv<NV>(out + at_bhsd, v);
+    }
 }
 
-// y[t, h*256 + d] = attn[b, h, s, d] * sigmoid(gate[t, h]) ; gate rows of `gate_stride`, head at h*gate_hs
+// y[t, h*D + d] = attn[b, h, s, d] * sigmoid(gate[t, h * gate_hs + d]) ; gate rows of `gate_stride`
+template <int NV>
 __global__ void __launch_bounds__(256) gate_mul_fwd_kernel(const __nv_bfloat16* __restrict__ attn,
                                                            const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
                                                            int gate_hs, int heads, int T, int S,
                                                            __nv_bfloat16* __restrict__ y) {
+    constexpr int D = 32 * NV;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)T * heads * 32) return;
     const int lane = (int)(gid & 31);
@@ -684,20 +731,22 @@ __global__ void __launch_bounds__(256) gate_mul_fwd_kernel(const __nv_bfloat16* 
     int t, h, b, s;
     split_row(row, heads, t, h);
     split_row(t, S, b, s);
-    float av[8], gv[8];
-    ld8(attn + (((int64_t)b * heads + h) * S + s) * 256 + lane * 8, av);
-    ld8(gate + (int64_t)t * gate_stride + (int64_t)h * gate_hs + lane * 8, gv);
+    float av[NV], gv[NV];
+    ldv<NV>(attn + (((int64_t)b * heads + h) * S + s) * D + lane * NV, av);
+    ldv<NV>(gate + (int64_t)t * gate_stride + (int64_t)h * gate_hs + lane * NV, gv);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) av[i] *= sigm(gv[i]);
-    st8(y + ((int64_t)t * heads + h) * 256 + lane * 8, av);
+    for (int i = 0; i < NV; ++i) av[i] *= sigm(gv[i]);
+    stv<NV>(y + ((int64_t)t * heads + h) * D + lane * NV, av);
 }
 
+template <int NV>
 __global__ void __launch_bounds__(256) gate_mul_bwd_kernel(const __nv_bfloat16* __restrict__ attn,
                                                            const __nv_bfloat16* __restrict__ gate, int64_t gate_stride,
                                                            int gate_hs, int heads, int T, int S,
                                                            const __nv_bfloat16* __restrict__ dy,
                                                            __nv_bfloat16* __restrict__ dattn,
                                                            __nv_bfloat16* __restrict__ dgate, int64_t dgate_stride) {
+    constexpr int D = 32 * NV;
     const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (gid >= (int64_t)T * heads * 32) return;
     const int lane = (int)(gid & 31);
@@ -705,19 +754,19 @@ __global__ void __launch_bounds__(256) gate_mul_bwd_kernel(const __nv_bfloat16* 
     int t, h, b, s;
     split_row(row, heads, t, h);
     split_row(t, S, b, s);
-    const int64_t at = (((int64_t)b * heads + h) * S + s) * 256 + lane * 8;
-    float av[8], gv[8], d[8], da[8], dg[8];
-    ld8(attn + at, av);
-    ld8(gate + (int64_t)t * gate_stride + (int64_t)h * gate_hs + lane * 8, gv);
-    ld8(dy + ((int64_t)t * heads + h) * 256 + lane * 8, d);
+    const int64_t at = (((int64_t)b * heads + h) * S + s) * D + lane * NV;
+    float av[NV], gv[NV], d[NV], da[NV], dg[NV];
+    ldv<NV>(attn + at, av);
+    ldv<NV>(gate + (int64_t)t * gate_stride + (int64_t)h * gate_hs + lane * NV, gv);
+    ldv<NV>(dy + ((int64_t)t * heads + h) * D + lane * NV, d);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
+    for (int i = 0; i < NV; ++i) {
         const float sg = sigm(gv[i]);
         da[i] = d[i] * sg;
         dg[i] = d[i] * av[i] * sg * (1.0f - sg);
     }
-    st8(dattn + at, da);
-    st8(dgate + (int64_t)t * dgate_stride + (int64_t)h * gate_hs + lane * 8, dg);
+    stv<NV>(dattn + at, da);
+    stv<NV>(dgate + (int64_t)t * dgate_stride + (int64_t)h * gate_hs + lane * NV, dg);
 }
 
 // ------------------------------------------------------------------------------------------- misc
@@ -853,58 +902,103 @@ extern "C" int r97b_swiglu_bwd(const uint16_t* gu, int64_t ldgu, int64_t rows, i
     return launch_status();
 }
 
+namespace {
+// head_dim 128 or 256; the rotated width a whole number of lanes whose count, and its pairing partner, a
+// power of two (rot / 2 / (head_dim / 32) in {1, 2, 4, 8, 16})
+bool qk_shape_ok(int32_t head_dim, int32_t rot) {
+    if (head_dim != 128 && head_dim != 256) return false;
+    const int nv = head_dim / 32;
+    if (rot <= 0 || rot > head_dim || rot % (2 * nv)) return false;
+    const int pl = rot / 2 / nv;
+    return (pl & (pl - 1)) == 0 && pl <= 16;
+}
+}  // namespace
+
 extern "C" int r97b_qk_norm_rope_fwd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
-                                     const float* w, const float* cos_tab, const float* sin_tab, int32_t rot,
-                                     int64_t T, int32_t S, float eps, uint16_t* out, void* stream) {
-    if (!x || !w || !cos_tab || !sin_tab || !out || T <= 0 || S <= 0 || T % S || rot % 16 || rot > 256 ||
+                                     int32_t head_dim, const float* w, const float* cos_tab, const float* sin_tab,
+                                     int32_t rot, int64_t T, int32_t S, float eps, uint16_t* out, void* stream) {
+    if (!x || !w || !cos_tab || !sin_tab || !out || T <= 0 || S <= 0 || T % S || !qk_shape_ok(head_dim, rot) ||
         head_stride % 8 || row_stride % 8)
         return R97B_EINVAL;
     QkArgs a{reinterpret_cast<const __nv_bfloat16*>(x), row_stride, head_stride, heads, w, cos_tab, sin_tab, rot,
              (int)T, S, eps};
-    qk_norm_rope_fwd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
-        a, reinterpret_cast<__nv_bfloat16*>(out));
+    if (head_dim == 256)
+        qk_norm_rope_fwd_kernel<8><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+            a, reinterpret_cast<__nv_bfloat16*>(out));
+    else
+        qk_norm_rope_fwd_kernel<4><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+            a, reinterpret_cast<__nv_bfloat16*>(out));
     return launch_status();
 }
 
 extern "C" int r97b_qk_norm_rope_bwd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
-                                     const float* w, const float* cos_tab, const float* sin_tab, int32_t rot,
-                                     int64_t T, int32_t S, float eps, const uint16_t* dout, uint16_t* dx,
+                                     int32_t head_dim, const float* w, const float* cos_tab, const float* sin_tab,
+                                     int32_t rot, int64_t T, int32_t S, float eps, const uint16_t* dout, uint16_t* dx,
                                      int64_t dx_stride, void* stream) {
-    if (!x || !w || !cos_tab || !sin_tab || !dout || !dx || T <= 0 || S <= 0 || T % S || rot % 16 || rot > 256)
+    if (!x || !w || !cos_tab || !sin_tab || !dout || !dx || T <= 0 || S <= 0 || T % S ||
+        !qk_shape_ok(head_dim, rot) || head_stride % 8 || row_stride % 8 || dx_stride % 8)
         return R97B_EINVAL;
     QkArgs a{reinterpret_cast<const __nv_bfloat16*>(x), row_stride, head_stride, heads, w, cos_tab, sin_tab, rot,
              (int)T, S, eps};
-    qk_norm_rope_bwd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
-        a, reinterpret_cast<const __nv_bfloat16*>(dout), reinterpret_cast<__nv_bfloat16*>(dx), dx_stride);
+    if (head_dim == 256)
+        qk_norm_rope_bwd_kernel<8><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+            a, reinterpret_cast<const __nv_bfloat16*>(dout), reinterpret_cast<__nv_bfloat16*>(dx), dx_stride);
+    else
+        qk_norm_rope_bwd_kernel<4><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+            a, reinterpret_cast<const __nv_bfloat16*>(dout), reinterpret_cast<__nv_bfloat16*>(dx), dx_stride);
     return launch_status();
 }
 
-extern "C" int r97b_to_bhsd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads, int64_t T,
-                            int32_t S, uint16_t* out, int32_t reverse, void* stream) {
-    if (!x || !out || T <= 0 || S <= 0 || T % S || head_stride % 8 || row_stride % 8) return R97B_EINVAL;
-    to_bhsd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x), row_stride, head_stride, heads, (int)T, S,
-        reinterpret_cast<__nv_bfloat16*>(out), reverse);
+extern "C" int r97b_to_bhsd(const uint16_t* x, int64_t row_stride, int32_t head_stride, int32_t heads,
+                            int32_t head_dim, int64_t T, int32_t S, uint16_t* out, int32_t reverse, void* stream) {
+    if (!x || !out || T <= 0 || S <= 0 || T % S || head_stride % 8 || row_stride % 8 ||
+        (head_dim != 128 && head_dim != 256))
+        return R97B_EINVAL;
+    const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x);
+    auto* op = reinterpret_cast<__nv_bfloat16*>(out);
+    if (head_dim == 256)
+        to_bhsd_kernel<8><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(xp, row_stride, head_stride, heads,
+                                                                                   (int)T, S, op, reverse);
+    else
+        to_bhsd_kernel<4><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(xp, row_stride, head_stride, heads,
+                                                                                   (int)T, S, op, reverse);
     return launch_status();
 }
 
 extern "C" int r97b_gate_mul_fwd(const uint16_t* attn, const uint16_t* gate, int64_t gate_stride, int32_t gate_hs,
-                                 int32_t heads, int64_t T, int32_t S, uint16_t* y, void* stream) {
-    if (!attn || !gate || !y || T <= 0 || S <= 0 || T % S) return R97B_EINVAL;
-    gate_mul_fwd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
-        reinterpret_cast<const __nv_bfloat16*>(attn), reinterpret_cast<const __nv_bfloat16*>(gate), gate_stride, gate_hs,
-        heads, (int)T, S, reinterpret_cast<__nv_bfloat16*>(y));
+                                 int32_t heads, int32_t head_dim, int64_t T, int32_t S, uint16_t* y, void* stream) {
+    if (!attn || !gate || !y || T <= 0 || S <= 0 || T % S || (head_dim != 128 && head_dim != 256) ||
+        gate_stride % 8 || gate_hs % 8)
+        return R97B_EINVAL;
+    const auto* ap = reinterpret_cast<const __nv_bfloat16*>(attn);
+    const auto* gp = reinterpret_cast<const __nv_bfloat16*>(gate);
+    auto* yp = reinterpret_cast<__nv_bfloat16*>(y);
+    if (head_dim == 256)
+        gate_mul_fwd_kernel<8><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(ap, gp, gate_stride, gate_hs,
+                                                                                        heads, (int)T, S, yp);
+    else
+        gate_mul_fwd_kernel<4><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(ap, gp, gate_stride, gate_hs,
+                                                                                        heads, (int)T, S, yp);
     return launch_status();
 }
 
 extern "C" int r97b_gate_mul_bwd(const uint16_t* attn, const uint16_t* gate, int64_t gate_stride, int32_t gate_hs,
-                                 int32_t heads, int64_t T, int32_t S, const uint16_t* dy, uint16_t* dattn,
-                                 uint16_t* dgate, int64_t dgate_stride, void* stream) {
-    if (!attn || !gate || !dy || !dattn || !dgate || T <= 0 || S <= 0 || T % S) return R97B_EINVAL;
-    gate_mul_bwd_kernel<<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
-        reinterpret_cast<const __nv_bfloat16*>(attn), reinterpret_cast<const __nv_bfloat16*>(gate), gate_stride, gate_hs,
-        heads, (int)T, S, reinterpret_cast<const __nv_bfloat16*>(dy), reinterpret_cast<__nv_bfloat16*>(dattn),
-        reinterpret_cast<__nv_bfloat16*>(dgate), dgate_stride);
+                                 int32_t heads, int32_t head_dim, int64_t T, int32_t S, const uint16_t* dy,
+                                 uint16_t* dattn, uint16_t* dgate, int64_t dgate_stride, void* stream) {
+    if (!attn || !gate || !dy || !dattn || !dgate || T <= 0 || S <= 0 || T % S ||
+        (head_dim != 128 && head_dim != 256) || gate_stride % 8 || gate_hs % 8 || dgate_stride % 8)
+        return R97B_EINVAL;
+    const auto* ap = reinterpret_cast<const __nv_bfloat16*>(attn);
+    const auto* gp = reinterpret_cast<const __nv_bfloat16*>(gate);
+    const auto* dp = reinterpret_cast<const __nv_bfloat16*>(dy);
+    auto* dap = reinterpret_cast<__nv_bfloat16*>(dattn);
+    auto* dgp = reinterpret_cast<__nv_bfloat16*>(dgate);
+    if (head_dim == 256)
+        gate_mul_bwd_kernel<8><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+            ap, gp, gate_stride, gate_hs, heads, (int)T, S, dp, dap, dgp, dgate_stride);
+    else
+        gate_mul_bwd_kernel<4><<<blocks_for(T * heads * 32), 256, 0, as_stream(stream)>>>(
+            ap, gp, gate_stride, gate_hs, heads, (int)T, S, dp, dap, dgp, dgate_stride);
     return launch_status();
 }
 

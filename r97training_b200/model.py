@@ -53,6 +53,7 @@ class HybridConfig:
     micro_batch: int = 2
     lr: float = 1e-4
     seed: int = 1234
+    lora_mlp: bool = True      # adapters on the MLP projections too (config 4 names only the mixers')
 
     @property
     def kinds(self):
@@ -69,8 +70,11 @@ class HybridConfig:
 
 
 CONFIG5 = HybridConfig()
+# config 4 as BASELINE.json states it: attention head dim 128 (rotary on the first 64 dims); GDN head counts are
+# not stated there: 8 value heads and 4 key heads of 128
+# and LoRA on q/k/v/o and the GDN in / out projections only
 CONFIG4 = HybridConfig(hidden=1024, layers=24, gdn_heads=8, gdn_qk_heads=4, attn_heads=8, attn_kv_heads=2,
-                       attn_head_dim=256, ffn=3584, rank=32, alpha=64.0, micro_batch=4)
+                       attn_head_dim=128, ffn=3584, rank=32, alpha=64.0, micro_batch=4, lora_mlp=False)
 
 
 def groups_of(cfg: HybridConfig, kind: str):
@@ -86,6 +90,11 @@ def groups_of(cfg: HybridConfig, kind: str):
                  ("o", cfg.attn_heads * Dh, [("o_proj", d)])]
     mlp = [("gu", d, [("gate_proj", cfg.ffn), ("up_proj", cfg.ffn)]), ("down", cfg.ffn, [("down_proj", d)])]
     return mixer + mlp
+
+
+def has_lora(cfg: HybridConfig, group: str) -> bool:
+    """Whether the projection group carries adapters: every group, or the mixers' only (cfg.lora_mlp)."""
+    return cfg.lora_mlp or group not in ("gu", "down")
 
 
 def module_path(layer: int, kind: str, proj: str) -> str:
@@ -107,6 +116,7 @@ class Group:
     k: int                     # input width
     projs: list                # [(name, out width)]
     iqr: list = field(default_factory=list)  # IqrWeight per projection
+    lora: bool = True          # carries adapters
     # adapter views into the flat buffers (set by Adapter)
     a_off: int = 0
     b_offs: list = field(default_factory=list)
@@ -132,7 +142,7 @@ class HybridModel:
         for li, kind in enumerate(cfg.kinds):
             blk = dict(kind=kind, groups=[])
             for gname, k, projs in groups_of(cfg, kind):
-                g = Group(gname, k, projs)
+                g = Group(gname, k, projs, lora=has_lora(cfg, gname))
                 for pname, n in projs:
                     seed += 1
                     # scales ~ |N(0, s)| with s chosen so the dequantised weight has std ~ 1/sqrt(fan_in)
@@ -186,6 +196,8 @@ class Adapter:
         for li, blk in enumerate(model.blocks):
             start = off
             for g in blk["groups"]:
+                if not g.lora:
+                    continue
                 g.a_off = off
                 for pname, _ in g.projs:
                     self.names.append(f"{module_path(li, blk['kind'], pname)}.lora_A")
@@ -220,6 +232,8 @@ class Adapter:
         self.a_bf, self.b_blk = {}, {}
         for li, blk in enumerate(model.blocks):
             for g in blk["groups"]:
+                if not g.lora:
+                    continue
                 self.a_bf[(li, g.name)] = torch.empty((g.r_all * r, g.k), dtype=torch.bfloat16, device=device)
                 self.b_blk[(li, g.name)] = torch.zeros((g.n, g.r_all * r), dtype=torch.bfloat16, device=device)
         self.model = model
@@ -239,6 +253,8 @@ class Adapter:
         pairs = []
         for li, blk in enumerate(self.model.blocks):
             for g in blk["groups"]:
+                if not g.lora:
+                    continue
                 pairs.append((self.a_view(self.w, g), self.a_bf[(li, g.name)]))
                 row = 0
                 for i, (_, n) in enumerate(g.projs):
@@ -365,12 +381,20 @@ class TrainStep:
         """t = s x A_all^T ; out = x W^T + t B_blk^T (+ addend). Returns t (saved for dB). With `swiglu_out`
         (the gate/up group) the GEMM's epilogue also writes silu(g) u there."""
         cfg, ad = self.cfg, self.adapter
+        if not g.lora:
+            if swiglu_out is not None:
+                ops.gemm(x, W, out, mode=ops.EPI_SWIGLU, out2=swiglu_out)
+            else:
+                ops.gemm(x, W, out, addend=addend, beta=1.0)
+            return None
         t = torch.empty((x.shape[0], g.r_all * cfg.rank), dtype=torch.bfloat16, device=x.device)
         self._skinny(x, ad.a_bf[(li, g.name)], t, g.k, False)
+        # the tail's B is block-diagonal: each output column has `rank` non-zero tail entries
+        work = 2.0 * x.shape[0] * g.n * (g.k + cfg.rank)
         if swiglu_out is not None:
-            ops.gemm(x, W, out, a2=t, b2=ad.b_blk[(li, g.name)], mode=ops.EPI_SWIGLU, out2=swiglu_out)
+            ops.gemm(x, W, out, a2=t, b2=ad.b_blk[(li, g.name)], mode=ops.EPI_SWIGLU, out2=swiglu_out, flops=work)
         else:
-            ops.gemm(x, W, out, a2=t, b2=ad.b_blk[(li, g.name)], addend=addend, beta=1.0)
+            ops.gemm(x, W, out, a2=t, b2=ad.b_blk[(li, g.name)], addend=addend, beta=1.0, flops=work)
         return t
 
     def _skinny(self, a, b, out, K, b_mn):
@@ -387,6 +411,12 @@ class TrainStep:
         (the down group, whose input is silu(g) u) dx_out receives SwiGLU's adjoint [dg | du] instead."""
         cfg, ad = self.cfg, self.adapter
         r = cfg.rank
+        if not g.lora:
+            if swiglu_gu is not None:
+                ops.gemm(dy, W, dx_out, b_mn=True, N=g.k, mode=ops.EPI_SWIGLU_BWD, addend=swiglu_gu)
+            else:
+                ops.gemm(dy, W, dx_out, b_mn=True, N=g.k)
+            return
         dt = torch.empty((dy.shape[0], g.r_all * r), dtype=torch.bfloat16, device=dy.device)
         self._skinny(dy, ad.b_blk[(li, g.name)], dt, g.n, True)
         if swiglu_gu is not None:
@@ -470,17 +500,17 @@ class TrainStep:
         qr = torch.empty((B, Hq, S, Dh), dtype=torch.bfloat16, device=x.device)
         kr = torch.empty((B, Hkv, S, Dh), dtype=torch.bfloat16, device=x.device)
         vt = torch.empty((B, Hkv, S, Dh), dtype=torch.bfloat16, device=x.device)
-        ops.qk_norm_rope_fwd(y, 2 * Dh, Hq, blk["q_norm"], self.model.rope_cos, self.model.rope_sin, cfg.rotary_dim,
-                             S, cfg.eps, qr)
-        ops.qk_norm_rope_fwd(y[:, qn:], Dh, Hkv, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
+        ops.qk_norm_rope_fwd(y, 2 * Dh, Hq, Dh, blk["q_norm"], self.model.rope_cos, self.model.rope_sin,
+                             cfg.rotary_dim, S, cfg.eps, qr)
+        ops.qk_norm_rope_fwd(y[:, qn:], Dh, Hkv, Dh, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
                              cfg.rotary_dim, S, cfg.eps, kr)
-        ops.to_bhsd(y[:, qn + Hkv * Dh:], Dh, Hkv, S, vt)
+        ops.to_bhsd(y[:, qn + Hkv * Dh:], Dh, Hkv, Dh, S, vt)
         # the attention core is the flash kernel's forward (GQA native), called without autograd so the
         # step stays on this stream and capturable; its saved state feeds the matching backward below
         fa = torch.ops.aten._scaled_dot_product_flash_attention(qr, kr, vt, 0.0, True, False)
         attn = fa[0]
         ga = torch.empty((T, Hq * Dh), dtype=torch.bfloat16, device=x.device)
-        ops.gate_mul_fwd(attn, y[:, Dh:], 2 * Dh, Hq, S, ga)
+        ops.gate_mul_fwd(attn, y[:, Dh:], 2 * Dh, Hq, Dh, S, ga)
         W = self._w_fwd(li, g_o)
         h1 = torch.empty_like(x)
         t_o = self._lin_fwd(li, g_o, ga, W, h1, addend=x)
@@ -498,7 +528,7 @@ class TrainStep:
         y = sv["y"]
         dy = torch.empty_like(y)
         dattn = torch.empty((B, Hq, S, Dh), dtype=torch.bfloat16, device=x.device)
-        ops.gate_mul_bwd(sv["attn"], y[:, Dh:], 2 * Dh, Hq, S, dga, dattn, dy[:, Dh:])
+        ops.gate_mul_bwd(sv["attn"], y[:, Dh:], 2 * Dh, Hq, Dh, S, dga, dattn, dy[:, Dh:])
         qg, kg, vg = sv["qkv"]
         fa = sv["fa"]
         # the attention core's adjoint on this package's tensor-core passes (csrc/attn.cu), from the flash
@@ -506,11 +536,11 @@ class TrainStep:
         if self.attn_ws is None:
             self.attn_ws = ops.attn_bwd_workspace(B, Hq, S, x.device)
         dq, dk, dv = ops.attn_bwd(qg, kg, vg, fa[0], dattn, fa[1], 1.0 / math.sqrt(Dh), self.attn_ws)
-        ops.qk_norm_rope_bwd(y, 2 * Dh, Hq, blk["q_norm"], self.model.rope_cos, self.model.rope_sin, cfg.rotary_dim,
-                             S, cfg.eps, dq, dy)
-        ops.qk_norm_rope_bwd(y[:, qn:], Dh, Hkv, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
+        ops.qk_norm_rope_bwd(y, 2 * Dh, Hq, Dh, blk["q_norm"], self.model.rope_cos, self.model.rope_sin,
+                             cfg.rotary_dim, S, cfg.eps, dq, dy)
+        ops.qk_norm_rope_bwd(y[:, qn:], Dh, Hkv, Dh, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
                              cfg.rotary_dim, S, cfg.eps, dk, dy[:, qn:])
-        ops.to_bhsd(dy[:, qn + Hkv * Dh:], Dh, Hkv, S, dv, reverse=True)
+        ops.to_bhsd(dy[:, qn + Hkv * Dh:], Dh, Hkv, Dh, S, dv, reverse=True)
         W = self._w_bwd(li, g_qkv)
         dn1 = torch.empty_like(x)
         self._lin_bwd(li, g_qkv, sv["n1"], sv["t_qkv"], W, dy, dn1)
@@ -638,10 +668,11 @@ def flops_per_token(cfg: HybridConfig) -> float:
     d, r = cfg.hidden, cfg.rank
     lin = lora = 0
     for kind in cfg.kinds:
-        for _, k, projs in groups_of(cfg, kind):
+        for gname, k, projs in groups_of(cfg, kind):
             for _, n in projs:
                 lin += n * k
-                lora += r * (n + k)
+                if has_lora(cfg, gname):
+                    lora += r * (n + k)
     head = cfg.vocab * d
     f = 4.0 * lin + 4.0 * head + 6.0 * lora * 2 / 2 * 1.0
     # attention core: fwd 4 S/2 Dh per head per token (QK^T and PV, causal half), bwd 2.5x fwd

@@ -47,14 +47,15 @@ def _mat(t: torch.Tensor, mn_major: bool, rows: int, k: int, name: str) -> R97bM
 
 
 def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STORE_BF16, alpha=1.0,
-         addend=None, beta=1.0, splits=1, bn=0, M=None, N=None, ws=None, out2=None, stream=None):
+         addend=None, beta=1.0, splits=1, bn=0, M=None, N=None, ws=None, out2=None, stream=None, flops=None):
     """out (+)= alpha * (A1 B1^T + A2 B2^T) (+ beta * addend); see include/r97b.h (r97b_gemm).
 
     A1 is [M, K1] (K-major) or stored [K1, M] (a_mn); B1 is [N, K1] or stored [K1, N] (b_mn); the optional
     tail (a2, b2) has the same majorness with its own K2. EPI_SPLIT_BF16 with splits > 1 needs `ws`, a
     zero-initialised device buffer of at least r97b_gemm_workspace_bytes bytes (see SplitWorkspace).
     EPI_SWIGLU writes [g | u] to `out` and silu(g) u to `out2`; EPI_SWIGLU_BWD reads [g | u] as `addend`
-    and writes [dg | du] to `out` (N = the SwiGLU width)."""
+    and writes [dg | du] to `out` (N = the SwiGLU width). `flops` is the algorithmic work the profile
+    (GEMM_PROFILE) counts for this call when it is less than 2 M N (K1 + K2) (a block-diagonal tail)."""
     if M is None:
         M = a1.shape[1] if a_mn else a1.shape[0]
     if N is None:
@@ -104,7 +105,8 @@ def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STOR
     check(lib().r97b_gemm(ctypes.byref(g), _stream(stream)), "r97b_gemm")
     if prof is not None:
         e1.record(s)
-        prof.append((e0, e1, 2.0 * M * N * (K1 + (g.K2 if a2 is not None else 0))))
+        full = 2.0 * M * N * (K1 + (g.K2 if a2 is not None else 0))
+        prof.append((e0, e1, full if flops is None else float(flops)))
     return out
 
 
@@ -300,34 +302,37 @@ def swiglu_bwd(gu, dy, dgu, stream=None):
                                 _stream(stream)), "r97b_swiglu_bwd")
 
 
-def qk_norm_rope_fwd(x, head_stride, heads, w, cos_t, sin_t, rot, S, eps, out, stream=None):
+def qk_norm_rope_fwd(x, head_stride, heads, head_dim, w, cos_t, sin_t, rot, S, eps, out, stream=None):
+    """Per (token, head) row of head_dim: RMSNorm with gain w, NeoX RoPE on the first rot dims, into
+    out [B, heads, S, head_dim]."""
     T = x.shape[0]
-    check(lib().r97b_qk_norm_rope_fwd(_ptr(x), x.stride(0), head_stride, heads, _ptr(w), _ptr(cos_t), _ptr(sin_t),
-                                      rot, T, S, eps, _ptr(out), _stream(stream)), "r97b_qk_norm_rope_fwd")
+    check(lib().r97b_qk_norm_rope_fwd(_ptr(x), x.stride(0), head_stride, heads, head_dim, _ptr(w), _ptr(cos_t),
+                                      _ptr(sin_t), rot, T, S, eps, _ptr(out), _stream(stream)),
+          "r97b_qk_norm_rope_fwd")
 
 
-def qk_norm_rope_bwd(x, head_stride, heads, w, cos_t, sin_t, rot, S, eps, dout, dx, stream=None):
+def qk_norm_rope_bwd(x, head_stride, heads, head_dim, w, cos_t, sin_t, rot, S, eps, dout, dx, stream=None):
     T = x.shape[0]
-    check(lib().r97b_qk_norm_rope_bwd(_ptr(x), x.stride(0), head_stride, heads, _ptr(w), _ptr(cos_t), _ptr(sin_t),
-                                      rot, T, S, eps, _ptr(dout), _ptr(dx), dx.stride(0), _stream(stream)),
-          "r97b_qk_norm_rope_bwd")
+    check(lib().r97b_qk_norm_rope_bwd(_ptr(x), x.stride(0), head_stride, heads, head_dim, _ptr(w), _ptr(cos_t),
+                                      _ptr(sin_t), rot, T, S, eps, _ptr(dout), _ptr(dx), dx.stride(0),
+                                      _stream(stream)), "r97b_qk_norm_rope_bwd")
 
 
-def to_bhsd(x, head_stride, heads, S, out, reverse=False, stream=None):
+def to_bhsd(x, head_stride, heads, head_dim, S, out, reverse=False, stream=None):
     T = x.shape[0]
-    check(lib().r97b_to_bhsd(_ptr(x), x.stride(0), head_stride, heads, T, S, _ptr(out), int(reverse),
+    check(lib().r97b_to_bhsd(_ptr(x), x.stride(0), head_stride, heads, head_dim, T, S, _ptr(out), int(reverse),
                              _stream(stream)), "r97b_to_bhsd")
 
 
-def gate_mul_fwd(attn, gate, gate_hs, heads, S, y, stream=None):
+def gate_mul_fwd(attn, gate, gate_hs, heads, head_dim, S, y, stream=None):
     T = y.shape[0]
-    check(lib().r97b_gate_mul_fwd(_ptr(attn), _ptr(gate), gate.stride(0), gate_hs, heads, T, S, _ptr(y),
+    check(lib().r97b_gate_mul_fwd(_ptr(attn), _ptr(gate), gate.stride(0), gate_hs, heads, head_dim, T, S, _ptr(y),
                                   _stream(stream)), "r97b_gate_mul_fwd")
 
 
-def gate_mul_bwd(attn, gate, gate_hs, heads, S, dy, dattn, dgate, stream=None):
+def gate_mul_bwd(attn, gate, gate_hs, heads, head_dim, S, dy, dattn, dgate, stream=None):
     T = dy.shape[0]
-    check(lib().r97b_gate_mul_bwd(_ptr(attn), _ptr(gate), gate.stride(0), gate_hs, heads, T, S, _ptr(dy),
+    check(lib().r97b_gate_mul_bwd(_ptr(attn), _ptr(gate), gate.stride(0), gate_hs, heads, head_dim, T, S, _ptr(dy),
                                   _ptr(dattn), _ptr(dgate), dgate.stride(0), _stream(stream)), "r97b_gate_mul_bwd")
 
 

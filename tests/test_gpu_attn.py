@@ -73,7 +73,8 @@ def _rope(x, cos, sin, rot):
     return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin, rest], dim=-1)
 
 
-def test_attention_block_vs_fp32(cuda):
+@pytest.mark.parametrize("Dh,rot", [(256, 64), (128, 64), (128, 32)])
+def test_attention_block_vs_fp32(cuda, Dh, rot):
     """The whole gated-attention sublayer of the model step -- RMSNorm, the fused q(+gate)/k/v projection with
     its LoRA tail, q/k RMSNorm, partial NeoX RoPE, causal GQA attention (flash forward, this package's
     backward), the sigmoid output gate, the o projection with its LoRA tail and the residual -- forward and
@@ -82,7 +83,7 @@ def test_attention_block_vs_fp32(cuda):
     from r97training_b200 import iqr as IQ
     from r97training_b200.model import Adapter, HybridConfig, HybridModel, TrainStep
     cfg = HybridConfig(hidden=512, layers=4, gdn_heads=4, gdn_qk_heads=2, attn_heads=4, attn_kv_heads=2, ffn=512,
-                       vocab=512, rank=8, alpha=16, seq=256, micro_batch=2)
+                       vocab=512, rank=8, alpha=16, seq=256, micro_batch=2, attn_head_dim=Dh, rotary_dim=rot)
     model = HybridModel(cfg, cuda)
     ad = Adapter(model, cuda, b_std=0.05)
     step = TrainStep(model, ad, head_chunk=128)

@@ -33,10 +33,10 @@ CFG = dict(hidden=256, layers=4, gdn_heads=4, gdn_qk_heads=2, attn_heads=2, attn
            rank=8, alpha=16.0, seq=128, micro_batch=2)
 
 
-def _run(cuda, seed, b_std, bf16_store):
+def _run(cuda, seed, b_std, bf16_store, shape="cfg5"):
     from oracle import step as S
     from r97training_b200.model import Adapter, HybridConfig, HybridModel, TrainStep
-    cfg = HybridConfig(**CFG)
+    cfg = HybridConfig(**(CFG if shape == "cfg5" else dict(CFG, attn_head_dim=128, lora_mlp=False)))
     model = HybridModel(cfg, cuda)
     ad = Adapter(model, cuda, b_std=b_std)
     step = TrainStep(model, ad, head_chunk=128)
@@ -64,12 +64,14 @@ def _need_ref():
         pytest.skip("reference host library not built and reference tree absent")
 
 
-@pytest.mark.parametrize("b_std", [1e-3, 2e-2])
-def test_step_vs_reference_rows_at_the_steps_storage_precision(cuda, b_std):
+@pytest.mark.parametrize("b_std,shape", [(1e-3, "cfg5"), (2e-2, "cfg5"), (2e-2, "cfg4")])
+def test_step_vs_reference_rows_at_the_steps_storage_precision(cuda, b_std, shape):
+    """cfg5: the config-5 block structure (attention head dim 256, adapters on every projection); cfg4: config
+    4's (head dim 128, adapters on q/k/v/o and the GDN in / out projections only)."""
     _need_ref()
-    loss, ref_loss, same, rows, whole = _run(cuda, 11, b_std, bf16_store=True)
+    loss, ref_loss, same, rows, whole = _run(cuda, 11, b_std, bf16_store=True, shape=shape)
     worst = sorted(rows, reverse=True)[:4]
-    print(f"\nstep parity, bf16 storage (B std {b_std}): loss {loss:.6f} vs {ref_loss:.6f}; whole cos {whole:.6f}; "
+    print(f"\nstep parity, bf16 storage ({shape}, B std {b_std}): loss {loss:.6f} vs {ref_loss:.6f}; whole cos {whole:.6f}; "
           "worst " + "; ".join(f"{n} rel {r:.2e} cos {c:.6f}" for r, c, n in worst))
     assert same
     assert abs(loss - ref_loss) <= 1e-4 * abs(ref_loss), (loss, ref_loss)
