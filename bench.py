@@ -63,7 +63,14 @@ def _static_sizes(cfg):
     return groups, base, adapter
 
 
-def cpu_reference(cfg, sample_tokens=None):
+# The CPU sample's token count, the same for the cpu_baseline leg and (as the middle of its sweep) the
+# reference arm; oracle.cpu_baseline fits each part between 8 tokens and this many, so the figure does not
+# depend on it beyond timing noise.
+CPU_SAMPLE_TOKENS = 64
+CPU_SWEEP = (32, 64, 128)
+
+
+def cpu_reference(cfg, sample_tokens=CPU_SAMPLE_TOKENS):
     """tokens/s of the reference's own host rows on a bounded sample (rank 0, N = 1 only)."""
     import oracle
     from oracle import cpu_baseline as CB
@@ -71,7 +78,7 @@ def cpu_reference(cfg, sample_tokens=None):
         return None, None
     threads = CB.threads()
     os.environ.setdefault("R97_THREADS", str(threads))
-    M = sample_tokens or max(16, min(64, 2 * threads))
+    M = sample_tokens
     groups, base, adapter = _static_sizes(cfg)
     parts = CB.sample_step(_cfg_dict(cfg, groups, base, adapter), M)
     return 1.0 / parts["seconds_per_token"], dict(parts=parts, M=M, threads=threads)
@@ -93,16 +100,19 @@ def reference_arm(args):
     os.environ.setdefault("R97_THREADS", str(threads))
     groups, base, adapter = _static_sizes(cfg)
     cd = _cfg_dict(cfg, groups, base, adapter)
-    M = 16
-    for _ in range(args.warmup):
-        CB.sample_step(cd, M, seed=1)
-    per_tok = []
+    for _ in range(min(args.warmup, 1)):  # the rows are plain host code: one warm-up settles the caches
+        CB.sample_step(cd, CPU_SAMPLE_TOKENS, seed=1)
+    per_tok, sweep = [], {}
     t0 = time.perf_counter()
     for i in range(args.steps):
-        per_tok.append(CB.sample_step(cd, M, seed=2 + i)["seconds_per_token"])
+        M = CPU_SWEEP[i % len(CPU_SWEEP)]  # each step samples another token count of the sweep
+        sp = CB.sample_step(cd, M, seed=2 + i)["seconds_per_token"]
+        per_tok.append(sp)
+        sweep.setdefault(str(M), []).append(sp)
     wall = time.perf_counter() - t0
     sec = sum(per_tok) / len(per_tok)
     value = 1.0 / sec
+    M = "/".join(sorted(sweep, key=int))
     step_tokens = cfg.tokens
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": 0,
@@ -113,8 +123,10 @@ def reference_arm(args):
                    "synthetic small hybrid", "global_batch": cfg.micro_batch, "seq_len": cfg.seq,
                    "parallelism": "host threads"},
         "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "reference",
-                         "sample": f"{M} tokens of one GDN and one attention block, one 64-token GDN chunk, the "
-                                   "head, one 4096x4096 decode and a 16M AdamW, extrapolated per token"},
+                         "sample": f"one GDN and one attention block's rows and the head fitted between 8 and {M} "
+                                   "tokens (per-token slope + fixed per-call cost once a step), one 64-token GDN "
+                                   "chunk, one 4096x4096 decode and a 16M AdamW, extrapolated per token",
+                         "seconds_per_token_by_M": {k: sum(v) / len(v) for k, v in sweep.items()}},
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "wall_s": wall,
     }
@@ -333,9 +345,11 @@ def b200_arm(args):
                 if v is not None:
                     line["cpu_baseline"] = {"value": v, "unit": "tokens/s", "cores": info["threads"],
                                             "kind": "reference",
-                                            "sample": f"{info['M']} tokens through one GDN and one attention block's "
-                                                      "reference host rows, one 64-token GDN chunk, the head, one "
-                                                      "4096x4096 decode and a 16M AdamW, extrapolated per token"}
+                                            "sample": f"one GDN and one attention block's reference host rows and "
+                                                      f"the head fitted between 8 and {info['M']} tokens (per-token "
+                                                      "slope + fixed per-call cost once a step), one 64-token GDN "
+                                                      "chunk, one 4096x4096 decode and a 16M AdamW, extrapolated "
+                                                      "per token"}
             except Exception as e:  # the baseline is reported, not required
                 line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
         line["gpu_launches"] = own_launches

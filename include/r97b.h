@@ -173,6 +173,24 @@ typedef struct R97bAttnBwd {
 } R97bAttnBwd;
 
 int r97b_attn_bwd(const R97bAttnBwd* a, void* stream);
+
+/* The forward of causal grouped-query attention: q [B, Hq, S, D], k and v [B, Hkv, S, D] (bf16, dense; query
+ * head h reads key/value head h / (Hq / Hkv)), o [B, Hq, S, D] bf16 and lse [B * Hq * S] f32, the natural-log
+ * log-sum-exp of each query row's scaled scores (what r97b_attn_bwd reads). S a multiple of 128, D 128 or
+ * 256. tcgen05 tensor cores, two passes over each 128-row query block's keys (the row statistics, then the
+ * normalised P V). Replaces: attention_twin, src/adjoint/host/attention.cpp:261-313, and the prefill kernels
+ * of the reference's device attention row. */
+typedef struct R97bAttnFwd {
+    int32_t B, Hq, Hkv, S, D;
+    float scale;
+    const void* q;
+    const void* k;
+    const void* v;
+    void* o;
+    float* lse;
+} R97bAttnFwd;
+
+int r97b_attn_fwd(const R97bAttnFwd* a, void* stream);
 int64_t r97b_attn_bwd_workspace_bytes(int32_t B, int32_t Hq, int32_t S);
 
 /* ------------------------------------------------------------------------------ LoRA linear */

@@ -41,6 +41,11 @@ class R97bAttnBwd(ctypes.Structure):
                 ("dq", c_vp), ("dk", c_vp), ("dv", c_vp), ("ws", c_vp), ("ws_bytes", c_i64)]
 
 
+class R97bAttnFwd(ctypes.Structure):
+    _fields_ = [("B", c_i32), ("Hq", c_i32), ("Hkv", c_i32), ("S", c_i32), ("D", c_i32), ("scale", c_f32),
+                ("q", c_vp), ("k", c_vp), ("v", c_vp), ("o", c_vp), ("lse", c_vp)]
+
+
 class R97bCastSeg(ctypes.Structure):
     _fields_ = [("src", c_vp), ("ld_src", c_i64), ("dst", c_vp), ("ld_dst", c_i64), ("rows", c_i64),
                 ("cols", c_i64), ("unit0", c_i64)]
@@ -82,6 +87,7 @@ _SIGS = {
     "r97b_gemm": (c_i32, [c_vp, c_vp]),
     "r97b_gemm_workspace_bytes": (c_i64, [c_vp]),
     "r97b_attn_bwd": (c_i32, [c_vp, c_vp]),
+    "r97b_attn_fwd": (c_i32, [c_vp, c_vp]),
     "r97b_cast_segments": (c_i32, [c_vp, c_i32, c_i64, c_vp]),
     "r97b_add_f32": (c_i32, [c_vp, c_vp, c_i64, c_vp]),
     "r97b_quant_act_i8g": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp, c_i64, c_vp, c_vp]),

@@ -15,8 +15,8 @@ reference's gemm_nt + lora_shrink + lora_expand rows (src/adjoint/host/linear.cp
 The backward is explicit: every layer's forward saves what its adjoint reads (HBM holds a step's
 activations: about 60 GB at config 5), and the reverse walk calls the kernels' adjoints in the
 reverse op order -- the fixed per-layer schedule the reference's backward_block walks over its tape.
-The attention core's forward (softmax(q k^T) v, causal, GQA) is torch's flash kernel -- a library call --
-whose output and log-sum-exp feed this package's own tensor-core backward (csrc/attn.cu).
+The attention core (softmax(q k^T) v, causal, GQA) runs on this package's tcgen05 kernels: the forward
+(csrc/attn_fwd.cu) saves its output and per-row log-sum-exp for the backward (csrc/attn.cu).
 """
 from __future__ import annotations
 
@@ -505,10 +505,10 @@ class TrainStep:
         ops.qk_norm_rope_fwd(y[:, qn:], Dh, Hkv, Dh, blk["k_norm"], self.model.rope_cos, self.model.rope_sin,
                              cfg.rotary_dim, S, cfg.eps, kr)
         ops.to_bhsd(y[:, qn + Hkv * Dh:], Dh, Hkv, Dh, S, vt)
-        # the attention core is the flash kernel's forward (GQA native), called without autograd so the
-        # step stays on this stream and capturable; its saved state feeds the matching backward below
-        fa = torch.ops.aten._scaled_dot_product_flash_attention(qr, kr, vt, 0.0, True, False)
-        attn = fa[0]
+        # the attention core on this package's tcgen05 kernel (csrc/attn_fwd.cu); its output and per-row
+        # log-sum-exp feed the matching backward below
+        attn, lse = ops.attn_fwd(qr, kr, vt, 1.0 / math.sqrt(Dh))
+        fa = (attn, lse)
         ga = torch.empty((T, Hq * Dh), dtype=torch.bfloat16, device=x.device)
         ops.gate_mul_fwd(attn, y[:, Dh:], 2 * Dh, Hq, Dh, S, ga)
         W = self._w_fwd(li, g_o)
@@ -531,7 +531,7 @@ class TrainStep:
         ops.gate_mul_bwd(sv["attn"], y[:, Dh:], 2 * Dh, Hq, Dh, S, dga, dattn, dy[:, Dh:])
         qg, kg, vg = sv["qkv"]
         fa = sv["fa"]
-        # the attention core's adjoint on this package's tensor-core passes (csrc/attn.cu), from the flash
+        # the attention core's adjoint on this package's tensor-core passes (csrc/attn.cu), from the
         # forward's output and log-sum-exp
         if self.attn_ws is None:
             self.attn_ws = ops.attn_bwd_workspace(B, Hq, S, x.device)

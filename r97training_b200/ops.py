@@ -10,7 +10,7 @@ import ctypes
 
 import torch
 
-from ._lib import (R97bAttnBwd, R97bCastSeg, R97bError, R97bGemm, R97bMat, R97bQLinearLora,
+from ._lib import (R97bAttnBwd, R97bAttnFwd, R97bCastSeg, R97bError, R97bGemm, R97bMat, R97bQLinearLora,
                    R97bQLinearLoraBwd, check, lib)
 
 EPI_STORE_BF16, EPI_STORE_F32, EPI_ATOMIC_F32, EPI_ATOMIC_F32T, EPI_SPLIT_BF16 = 0, 1, 2, 3, 4
@@ -377,6 +377,23 @@ def qlinear_lora_bwd(w_bf16, x, A, B, t, dy, scale, dA, dB, *, dx=None, dt=None,
                            _ptr(dt), _ptr(dx), _ptr(dA), _ptr(dB), _ptr(ws), ws.numel())
     check(lib().r97b_qlinear_lora_bwd(ctypes.byref(a), _stream(stream)), "r97b_qlinear_lora_bwd")
     return dx
+
+
+def attn_fwd(q, k, v, scale, o=None, lse=None, stream=None):
+    """Causal GQA attention softmax(scale q k^T) v on this package's tcgen05 kernel (r97b_attn_fwd): q
+    [B, Hq, S, D], k, v [B, Hkv, S, D] bf16 contiguous. Returns (o [B, Hq, S, D] bf16, lse [B, Hq, S] f32, the
+    natural-log log-sum-exp r97b_attn_bwd reads)."""
+    B, Hq, S, D = q.shape
+    Hkv = k.shape[1]
+    for t, name, shape in ((q, "q", (B, Hq, S, D)), (k, "k", (B, Hkv, S, D)), (v, "v", (B, Hkv, S, D))):
+        _need(t, torch.bfloat16, name)
+        if tuple(t.shape) != shape or not t.is_contiguous():
+            raise R97bError(f"{name} must be a contiguous {shape} bf16 tensor")
+    o = torch.empty_like(q) if o is None else o
+    lse = torch.empty((B, Hq, S), dtype=torch.float32, device=q.device) if lse is None else lse
+    a = R97bAttnFwd(B, Hq, Hkv, S, D, float(scale), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _ptr(lse))
+    check(lib().r97b_attn_fwd(ctypes.byref(a), _stream(stream)), "r97b_attn_fwd")
+    return o, lse
 
 
 def attn_bwd_workspace(B: int, Hq: int, S: int, device) -> torch.Tensor:

@@ -1,12 +1,16 @@
-"""GPU parity of the attention backward (r97b_attn_bwd, the tcgen05 passes of csrc/attn.cu) against a plain
-PyTorch fp32 reference of causal grouped-query attention, through the C ABI. The forward's output and
-log-sum-exp come from torch's flash kernel, as in the model step. Tolerance: the north star's bf16 bar
-(per-tensor relative L2 <= 1e-2, cosine >= 0.999)."""
+"""GPU parity of the attention core on this package's tcgen05 kernels, through the C ABI: the forward
+(r97b_attn_fwd, csrc/attn_fwd.cu) against the oracle's attention restatement (oracle/rows.py attention_fwd,
+pinned to the reference's own attn_paged twin) and a plain PyTorch fp32 reference, and the backward
+(r97b_attn_bwd, csrc/attn.cu) from that forward's output and log-sum-exp, against fp32 autograd and the
+oracle's attention_bwd (pinned to the reference's host adjoint). Tolerance: the north star's bf16 bar (per-tensor
+relative L2 <= 1e-2, cosine >= 0.999); the log-sum-exp, an f32 output, to 1e-4 absolute."""
 import math
 
+import numpy as np
 import pytest
 import torch
 
+from oracle import rows as R
 from r97training_b200 import ops
 from tests.gpu_util import assert_close_bf16, to_np
 
@@ -36,14 +40,13 @@ def test_attn_bwd_vs_fp32(cuda, B, Hq, Hkv, S, D):
     v = torch.randn(B, Hkv, S, D, device=cuda, generator=g).bfloat16()
     do = (torch.randn(B, Hq, S, D, device=cuda, generator=g) * 0.1).bfloat16()
     scale = 1.0 / math.sqrt(D)
-    fa = torch.ops.aten._scaled_dot_product_flash_attention(q, k, v, 0.0, True, False)
-    o, lse = fa[0], fa[1]
+    o, lse = ops.attn_fwd(q, k, v, scale)
     assert o.is_contiguous() and tuple(lse.shape) == (B, Hq, S)
     ws = ops.attn_bwd_workspace(B, Hq, S, cuda)
     dq, dk, dv = ops.attn_bwd(q, k, v, o, do, lse.contiguous(), scale, ws)
     o_ref, dq_ref, dk_ref, dv_ref = _ref_grads(q, k, v, do, scale)
     torch.cuda.synchronize()
-    assert_close_bf16(to_np(o), to_np(o_ref), what="o (flash forward)")
+    assert_close_bf16(to_np(o), to_np(o_ref), what="o (forward)")
     assert_close_bf16(to_np(dv), to_np(dv_ref), what="dv")
     assert_close_bf16(to_np(dk), to_np(dk_ref), what="dk")
     assert_close_bf16(to_np(dq), to_np(dq_ref), what="dq")
@@ -51,6 +54,43 @@ def test_attn_bwd_vs_fp32(cuda, B, Hq, Hkv, S, D):
     dq2, dk2, dv2 = ops.attn_bwd(q, k, v, o, do, lse.contiguous(), scale, ws)
     torch.cuda.synchronize()
     assert torch.equal(dq, dq2) and torch.equal(dk, dk2) and torch.equal(dv, dv2)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,S,D", [(1, 2, 1, 128, 256), (2, 4, 2, 384, 128), (1, 3, 3, 256, 256),
+                                          (1, 4, 1, 640, 128)])
+def test_attn_fwd_vs_oracle(cuda, B, Hq, Hkv, S, D):
+    """The forward's output and log-sum-exp against the oracle's f64 attention (the reference's attn_paged
+    twin's arithmetic) on the same bf16 inputs, plus a second call into fresh outputs giving the same bits."""
+    rs = np.random.RandomState(B * 7 + Hq * 5 + S + D)
+    qn = rs.normal(size=(B, Hq, S, D))
+    kn = rs.normal(size=(B, Hkv, S, D))
+    vn = rs.normal(size=(B, Hkv, S, D))
+    q, k, v = (torch.from_numpy(a).float().bfloat16().to(cuda) for a in (qn, kn, vn))
+    scale = 1.0 / math.sqrt(D)
+    o, lse = ops.attn_fwd(q, k, v, scale)
+    o2, lse2 = ops.attn_fwd(q, k, v, scale)
+    torch.cuda.synchronize()
+    assert torch.equal(o, o2) and torch.equal(lse, lse2)
+    qf, kf, vf = (t.double().cpu().numpy() for t in (q, k, v))
+    for b in range(B):
+        # the oracle's layout: [tokens, heads, D]
+        want = R.attention_fwd(qf[b].transpose(1, 0, 2), kf[b].transpose(1, 0, 2), vf[b].transpose(1, 0, 2),
+                               scale).transpose(1, 0, 2)
+        assert_close_bf16(to_np(o[b]), want, what=f"o[{b}]")
+        s_ = np.einsum("hsd,htd->hst", qf[b], np.repeat(kf[b], Hq // Hkv, axis=0)) * scale
+        s_ = np.where(np.triu(np.ones((S, S), bool), 1)[None], -np.inf, s_)
+        mx = s_.max(-1)
+        want_lse = mx + np.log(np.exp(s_ - mx[..., None]).sum(-1))
+        np.testing.assert_allclose(lse[b].cpu().numpy(), want_lse, rtol=0, atol=1e-4)
+
+
+def test_attn_fwd_rejects_bad_shapes(cuda):
+    q = torch.zeros(1, 2, 100, 256, device=cuda, dtype=torch.bfloat16)  # S not a multiple of 128
+    with pytest.raises(Exception):
+        ops.attn_fwd(q, q[:, :1], q[:, :1], 0.0625)
+    q = torch.zeros(1, 2, 128, 192, device=cuda, dtype=torch.bfloat16)  # D neither 128 nor 256
+    with pytest.raises(Exception):
+        ops.attn_fwd(q, q[:, :1].contiguous(), q[:, :1].contiguous(), 0.0625)
 
 
 def test_attn_bwd_rejects_bad_shapes(cuda):
@@ -76,7 +116,7 @@ def _rope(x, cos, sin, rot):
 @pytest.mark.parametrize("Dh,rot", [(256, 64), (128, 64), (128, 32)])
 def test_attention_block_vs_fp32(cuda, Dh, rot):
     """The whole gated-attention sublayer of the model step -- RMSNorm, the fused q(+gate)/k/v projection with
-    its LoRA tail, q/k RMSNorm, partial NeoX RoPE, causal GQA attention (flash forward, this package's
+    its LoRA tail, q/k RMSNorm, partial NeoX RoPE, causal GQA attention (this package's forward and
     backward), the sigmoid output gate, the o projection with its LoRA tail and the residual -- forward and
     backward through TrainStep, against an fp32 autograd restatement on the same decoded weights and adapter
     (the reference's attention twin/adjoint arithmetic, src/adjoint/host/attention.cpp:261-414)."""
