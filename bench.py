@@ -241,18 +241,14 @@ def b200_arm(args):
         barrier()
         ops.GEMM_PROFILE = prof  # the GEMMs' timing events become nodes of the graph
         c0 = int(_lc().r97b_launch_count())
-        graph = GraphStep(step, ids_dev[0], update=(world == 1))
+        # the whole step in one graph; at N > 1 with the per-layer all-reduces captured on their side stream,
+        # overlapping the rest of the backward, and AdamW after their join
+        graph = GraphStep(step, ids_dev[0], update=True, buckets=buckets)
         graph_launches = int(_lc().r97b_launch_count()) - c0  # this library's kernels in the captured step
         ops.GEMM_PROFILE = None
 
         def one_step(ids):  # noqa: F811 -- the replayed step
-            loss = graph.replay(ids)
-            if world > 1:  # the exchange and the update run eagerly after the captured backward
-                for li in range(len(adapter.layer_ranges) - 1, -1, -1):
-                    buckets.ready(li)
-                buckets.join()
-                adapter.adamw()
-            return loss
+            return graph.replay(ids)
 
         for i in range(eager_warm, args.warmup):
             one_step(ids_dev[i % len(ids_dev)])
@@ -328,7 +324,8 @@ def b200_arm(args):
                        "parallelism": f"dp{world}", "l2": "inputs larger than L2 (about 60 GB of activations a step)",
                        "launch": "eager" if graph is None else
                        ("CUDA graph of the whole step" if world == 1 else
-                        "CUDA graph of forward+backward; gradient all-reduce and AdamW eager"),
+                        "CUDA graph of the whole step, per-layer gradient all-reduces captured on a side "
+                        "stream overlapping the backward, AdamW after their join"),
                        "flops_per_token": flops_per_token(cfg)},
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05)", "achieved": gemm_tflops, "peak": peak,
                          "unit": "TFLOP/s", "frac": gemm_tflops / peak, "traffic": traffic,
@@ -355,6 +352,8 @@ def b200_arm(args):
         line["gpu_launches"] = own_launches
         line["gpu_launches_per_step"] = own_launches / max(args.steps, 1)
         print(json.dumps(line), flush=True)
+    if graph is not None:
+        graph.release()  # a graph holding NCCL calls goes before the process group
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -32,7 +32,9 @@ class GradBuckets:
         self._issued = []
 
     def ready(self, li: int) -> None:
-        """Bucket ``li`` is final on this rank: start its all-reduce."""
+        """Bucket ``li`` is final on this rank: start its all-reduce. Inside a CUDA graph capture the
+        collective is captured too: the side stream joins the capture through the event edge from the
+        compute stream, and the all-reduce is issued as a stream-ordered (not host-waited) operation there."""
         if li in self._issued:
             raise RuntimeError(f"gradient bucket {li} issued twice in one step")
         lo, hi = self.ranges[li]
@@ -43,7 +45,11 @@ class GradBuckets:
             ev.record()  # the layer's gradient kernels, on the compute stream
             self.stream.wait_event(ev)
             with torch.cuda.stream(self.stream):
-                work = dist.all_reduce(view, op=op, group=self.group, async_op=True)
+                if torch.cuda.is_current_stream_capturing():
+                    dist.all_reduce(view, op=op, group=self.group)  # ordered on the side stream
+                    work = None
+                else:
+                    work = dist.all_reduce(view, op=op, group=self.group, async_op=True)
         else:
             work = dist.all_reduce(view, op=op, group=self.group, async_op=True)
         self._works.append((work, view))
@@ -57,7 +63,8 @@ class GradBuckets:
             if li not in self._issued:
                 self.ready(li)
         for work, view in self._works:
-            work.wait()
+            if work is not None:
+                work.wait()
             if not self.avg and self.world > 1:
                 if self.stream is not None:
                     with torch.cuda.stream(self.stream):

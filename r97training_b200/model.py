@@ -631,23 +631,34 @@ class GraphStep:
     a copy of the token ids, the schedule write and one graph launch, instead of ~2000 kernel launches.
 
     The step must have run eagerly at least once first (kernel attributes, tensor-map encoders and the
-    decoded-weight buffers are set up on first use, outside any capture). `grad_hook` is not captured: a
-    data-parallel caller captures without the update and exchanges the gradient after each replay."""
+    decoded-weight buffers are set up on first use, outside any capture). With `buckets` (a data-parallel
+    dp.GradBuckets over the adapter gradient, whose collectives have run eagerly once) the per-layer
+    all-reduces are captured too, on their side stream as the reverse walk finishes each layer, and joined
+    before the update; a graph that holds collectives must be released (``release``) before the process
+    group is destroyed."""
 
-    def __init__(self, step: "TrainStep", ids: torch.Tensor, update: bool = True):
+    def __init__(self, step: "TrainStep", ids: torch.Tensor, update: bool = True, buckets=None):
         self.step, self.update = step, update
         dev = step.model.device
         self.ids = ids.reshape(-1).to(torch.int32).clone()
-        hook, step.grad_hook = step.grad_hook, None
+        hook, step.grad_hook = step.grad_hook, (buckets.ready if buckets is not None else None)
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         try:
             with torch.cuda.graph(self.graph):
                 self.loss = step.run(self.ids)
+                if buckets is not None:
+                    buckets.join()
                 if update:
                     step.adapter.update()
         finally:
             step.grad_hook = hook
+
+    def release(self) -> None:
+        """Frees the graph (and any collectives captured in it)."""
+        if self.graph is not None:
+            self.graph.reset()
+            self.graph = None
 
     def replay(self, ids: torch.Tensor | None = None, lr=None) -> torch.Tensor:
         """Runs one step on `ids` (copied into the captured input; None reuses the last ids) and returns the

@@ -8,12 +8,13 @@ Two references.
 (1) The rows replayed with the B200 step's storage precision: every activation, cotangent, weight and LoRA
 mirror that the step keeps in bf16 is rounded to bf16 where the step stores it, so what differs is arithmetic
 order, f32 against f64, and the roundings inside fused kernels (the attention's P and dS tiles). Measured:
-loss to 2e-5 relative, every leaf at cosine >= 0.9994 and relative L2 <= 3.4e-2, the whole gradient at
-cosine >= 0.9996. Held to the north star's cosine (>= 0.999 per leaf), the loss within 1e-4, the whole
-gradient at cosine >= 0.9995 and every leaf at relative L2 <= 5e-2: per leaf the north star's 1e-2 is not
-met, because a bf16 step's gradients carry bf16 noise of about that size once a rounding anywhere upstream
-lands differently (replaying the rows with a 1e-6 relative nudge before each backward rounding alone moves
-the leaves by 1 %).
+loss to 2.6e-5 (config-5 shape) and 1.3e-4 (config-4 shape) relative, every leaf at cosine >= 0.9995 and
+relative L2 <= 3.1e-2, the whole gradient at cosine >= 0.9995. Held to the north star's cosine (>= 0.999 per
+leaf), the loss within 5e-4, the whole gradient at cosine >= 0.9995 and every leaf at relative L2 <= 5e-2:
+the north star's 1e-2 per leaf is not met, because a bf16 step carries bf16 noise of about that size once a
+rounding anywhere upstream lands differently (replaying the rows with a 1e-6 relative nudge before each
+rounding moves the loss by 1.5-3.2e-4, and a nudge before the backward's roundings alone moves the leaves
+by 1 %).
 
 (2) The exact f64 step. Measured: loss to 1.2e-4, whole-gradient cosine 0.967 (B ~ N(0, 1e-3)) and 0.993
 (N(0, 2e-2)), leaves 0.945-1.0. The gate and state gradients of a GatedDeltaNet are near-cancelling sums
@@ -74,7 +75,7 @@ def test_step_vs_reference_rows_at_the_steps_storage_precision(cuda, b_std, shap
     print(f"\nstep parity, bf16 storage ({shape}, B std {b_std}): loss {loss:.6f} vs {ref_loss:.6f}; whole cos {whole:.6f}; "
           "worst " + "; ".join(f"{n} rel {r:.2e} cos {c:.6f}" for r, c, n in worst))
     assert same
-    assert abs(loss - ref_loss) <= 1e-4 * abs(ref_loss), (loss, ref_loss)
+    assert abs(loss - ref_loss) <= 5e-4 * abs(ref_loss), (loss, ref_loss)
     assert whole >= 0.9995, whole
     bad = [(n, r, c) for r, c, n in rows if not (r <= 5e-2 and c >= 0.999)]
     assert not bad, bad
