@@ -114,6 +114,66 @@ int64_t r97host_batcher_skipped(void* batcher, int64_t* out, int64_t cap);
 int64_t r97host_batcher_skipped_tokens(void* batcher);
 const char* r97host_batcher_error(void);
 
+/* ---- the training step as C++ over libr97b200.so: the reference's StepFn (include/r97/step.h:18-27; the
+ * device join's make_device_step, include/r97/step_device.h:164, src/step_device.cpp:355-1678) ----
+ * The LoRA step of the hybrid model (embedding, layers of 3 GatedDeltaNet : 1 gated attention each followed
+ * by a SwiGLU MLP, final RMSNorm, tied IQR head with cross-entropy) forward and backward, driving this
+ * library's kernels without Python. The caller owns the frozen weights (device buffers); the step owns its
+ * activations (one arena sized at creation) and workspaces. */
+typedef struct R97hostIqrWeight {  /* a stored projection in the trunk form (u4 codes, f32 scale per 128) */
+    const void* codes;   /* uint8 [rows, cols * bits / 8] */
+    const float* scale;  /* f32 [rows, cols / 128] */
+    int64_t rows, cols;
+    uint32_t mad_a, mad_b;
+    int32_t bits, state_bits, run_rows, _pad;
+} R97hostIqrWeight;
+
+typedef struct R97hostStepConfig {
+    int32_t hidden, layers, gdn_per_attn, gdn_heads, gdn_qk_heads, head_k;
+    int32_t attn_heads, attn_kv_heads, attn_head_dim, rotary_dim, ffn, vocab;
+    int32_t rank, seq, micro_batch, lora_mlp, head_chunk, _pad;
+    float alpha, eps;
+} R97hostStepConfig;
+
+typedef struct R97hostStepWeights {
+    /* every projection, layer by layer, group by group: a GDN layer's in_proj_qkvz, in_proj_ba, out_proj, an
+     * attention layer's q_proj (query and gate per head), k_proj, v_proj, o_proj, then each layer's
+     * gate_proj, up_proj, down_proj */
+    const R97hostIqrWeight* proj;
+    /* 6 per layer: w_in, w_post, then conv_w [conv_dim, 4], a_log, dt_bias, gnorm_w (GDN) or q_norm, k_norm,
+     * -, - (attention); f32 */
+    const float* const* norms;
+    const float* w_final;
+    R97hostIqrWeight head;  /* the tied head / embedding [vocab, hidden] */
+    const float* rope_cos;  /* f32 [seq, rotary_dim / 2] */
+    const float* rope_sin;
+} R97hostStepWeights;
+
+/* A step, or null with the reason in r97host_step_error. Runs a dry pass of the whole step to size its arena. */
+void* r97host_step_create(const R97hostStepConfig* cfg, const R97hostStepWeights* w);
+void r97host_step_destroy(void* step);
+const char* r97host_step_error(void);
+/* The flat f32 adapter: its element count, and leaf i's reference name (`<module>.lora_A` / `.lora_B`),
+ * offset and [rows, cols] shape. */
+int64_t r97host_step_adapter_numel(void* step);
+int32_t r97host_step_param_count(void* step);
+const char* r97host_step_param(void* step, int32_t i, int64_t* offset, int64_t* rows, int64_t* cols);
+/* Bytes of the step's activation arena. */
+int64_t r97host_step_arena_bytes(void* step);
+/* One step on `stream`: ids and targets (-1: unscored) device i32 [micro_batch * seq], n_scored the number of
+ * targets >= 0 (the gradient is of the mean: scale 1 / n_scored), adapter_w the flat f32 adapter (device), its
+ * gradient ADDED into adapter_g (device). *loss_sum = the CE summed over the scored rows. Synchronises the
+ * stream at the end. 0, or 1 with a message. */
+int r97host_step_run(void* step, const int32_t* ids, const int32_t* targets, int64_t n_scored,
+                     const float* adapter_w, float* adapter_g, double* loss_sum, void* stream);
+/* The same step through the reference's StepFn: a Batch of n_seq sequences (lengths[s] token ids and score
+ * bytes each, concatenated; at most seq tokens, padded unscored), a ParamSet of nparams leaves (names, [rows,
+ * cols] shapes, f32 values concatenated) and, when grads_out is given, the ParamSet of gradients it returns,
+ * written in the same layout. 0, or 1 with a message in r97host_step_error. */
+int r97host_step_call(void* step, int32_t n_seq, const int64_t* lengths, const int32_t* ids, const uint8_t* score,
+                      int32_t nparams, const char* const* names, const int64_t* shapes, const float* values,
+                      float* grads_out, double* loss, int64_t* scored);
+
 #ifdef __cplusplus
 }
 #endif

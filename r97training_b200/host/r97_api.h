@@ -7,7 +7,7 @@
 // include/r97/adjoint.h:183-235, src/adjoint/device/plugin.hip). The structs below must match the
 // reference's member for member -- the registry and the walk hand them across the library boundary by
 // reference -- so their members, order and types follow reference include/r97/op.h:18-60,
-// include/r97/params.h:14-22, include/r97/adjoint.h:49-168, include/r97/head.h:28-55,
+// include/r97/params.h:14-22, include/r97/batch.h:12-17, include/r97/step.h:18-27, include/r97/adjoint.h:49-168, include/r97/head.h:28-55,
 // src/stored_weight.h:27-55 and src/adjoint/device/scratch.h / grad_stage.h.
 //
 // The host's entry points (registration, the stored-weight table, the head's registration) are declared
@@ -57,6 +57,22 @@ struct Param {
     std::vector<float> value;
 };
 using ParamSet = std::vector<Param>;
+
+// ---------------------------------------------------------------- a step (reference batch.h, step.h)
+
+struct TokenSeq {
+    std::vector<int32_t> ids;    // the sequence's token ids
+    std::vector<uint8_t> score;  // 1 where token i is a target predicted at position i - 1
+};
+using Batch = std::vector<TokenSeq>;
+
+struct StepResult {
+    double loss;      // summed over the batch's scored tokens
+    int64_t scored;   // how many scored tokens the loss covered
+};
+
+// grads == nullptr means forward only
+using StepFn = std::function<StepResult(const Batch&, const ParamSet& params, ParamSet* grads)>;
 
 // ---------------------------------------------------------------- the adjoint contract (reference adjoint.h)
 
