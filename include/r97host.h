@@ -173,6 +173,11 @@ int r97host_step_run(void* step, const int32_t* ids, const int32_t* targets, int
 int r97host_step_call(void* step, int32_t n_seq, const int64_t* lengths, const int32_t* ids, const uint8_t* score,
                       int32_t nparams, const char* const* names, const int64_t* shapes, const float* values,
                       float* grads_out, double* loss, int64_t* scored);
+/* For a C++ caller with the reference's headers -- its Trainer (include/r97/trainer.h), which takes a StepFn: a
+ * heap-allocated r97::StepFn over the step (cast to r97::StepFn* and copy), freed with r97host_step_fn_free.
+ * A Batch may hold up to micro_batch sequences of up to seq tokens each. */
+void* r97host_step_fn_new(void* step);
+void r97host_step_fn_free(void* fn);
 
 #ifdef __cplusplus
 }

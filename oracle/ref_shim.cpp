@@ -13,12 +13,15 @@
 #include "r97/batcher.h"
 #include "r97/loss.h"
 #include "r97/optim.h"
+#include "r97/trainer.h"
 
 #include "iqr_decode.h"
 #include "stored_weight.h"
 
 #include <algorithm>
 #include <cstdint>
+#include <filesystem>
+#include <fstream>
 #include <cstring>
 #include <exception>
 #include <string>
@@ -392,3 +395,76 @@ int64_t ref_batcher_plan(const int64_t* lengths, int64_t n, int64_t budget, int 
 }
 
 }  // extern "C"
+
+// The reference's own training loop (src/trainer.cpp: Trainer, its Optimiser, Batcher, checkpoint and resume)
+// over a StepFn it is handed -- `stepfn` points at an r97::StepFn, e.g. the B200 step's from libr97host.so
+// (r97host_step_fn_new). The parameters are `nparams` named leaves ([rows, cols] shapes, f32 values in and
+// out); the data `nseq` sequences of `lengths[i]` token ids, every token but the first scored. Resumes from
+// `resume_dir` when it is non-empty, runs `count` steps of a run of `total_steps` (checkpointing at its end),
+// writes the losses of the steps it ran (StepResult.loss / scored) into `losses` and the last checkpoint's
+// directory into `ckpt_out`. Returns the steps run, or -1 on a throw (message in ref_last_error).
+extern "C" int64_t ref_trainer_run(void* stepfn, int nparams, const char* const* names, const int64_t* shapes, float* values,
+                        int64_t nseq, const int64_t* lengths, const int32_t* ids, int64_t token_budget, double lr,
+                        int64_t total_steps, int64_t count, const char* out_dir, const char* resume_dir,
+                        double* losses, char* ckpt_out, int64_t ckpt_cap) {
+    try {
+        g_error.clear();
+        r97::ParamSet params;
+        int64_t off = 0;
+        for (int i = 0; i < nparams; ++i) {
+            const int64_t n = shapes[2 * i] * shapes[2 * i + 1];
+            params.push_back(r97::Param{names[i], {shapes[2 * i], shapes[2 * i + 1]},
+                                        std::vector<float>(values + off, values + off + n)});
+            off += n;
+        }
+        std::vector<r97::TokenSeq> seqs((size_t)nseq);
+        int64_t at = 0;
+        for (int64_t s = 0; s < nseq; ++s) {
+            seqs[(size_t)s].ids.assign(ids + at, ids + at + lengths[s]);
+            seqs[(size_t)s].score.assign((size_t)lengths[s], 1);
+            seqs[(size_t)s].score[0] = 0;
+            at += lengths[s];
+        }
+        r97::Config cfg;
+        cfg.out = out_dir;
+        cfg.lr = lr;
+        cfg.token_budget = token_budget;
+        cfg.accumulation = 1;
+        cfg.steps = total_steps;
+        cfg.seed = 7;
+        cfg.base_id = "synthetic-hybrid";
+        r97::BatcherConfig bc;
+        bc.token_budget = token_budget;
+        bc.devices = 1;
+        bc.seed = 11;
+        r97::Batcher batcher(std::move(seqs), bc);
+        r97::Optimiser opt(params, r97::optimiser_config(cfg));
+        std::vector<double> seen;
+        const r97::StepFn inner = *static_cast<const r97::StepFn*>(stepfn);
+        r97::StepFn recording = [&](const r97::Batch& b, const r97::ParamSet& p, r97::ParamSet* g) {
+            const r97::StepResult r = inner(b, p, g);
+            seen.push_back(r.scored > 0 ? r.loss / (double)r.scored : 0.0);
+            return r;
+        };
+        r97::TrainerOptions topt;
+        topt.config = cfg;
+        topt.write_adapter = [](const r97::ParamSet&, const std::string& dir) {
+            std::ofstream((std::filesystem::path(dir) / "adapter.marker").string()) << "adapter\n";
+        };
+        r97::Trainer trainer(recording, r97::StepFn{}, params, opt, batcher, topt);
+        if (resume_dir && *resume_dir) trainer.resume(resume_dir);
+        const int64_t taken = trainer.run_steps(count);
+        const std::string ckpt = trainer.save_checkpoint();
+        if (ckpt_out && ckpt_cap > (int64_t)ckpt.size()) std::memcpy(ckpt_out, ckpt.c_str(), ckpt.size() + 1);
+        for (size_t i = 0; i < seen.size(); ++i) losses[i] = seen[i];
+        off = 0;
+        for (const r97::Param& p : params) {
+            std::memcpy(values + off, p.value.data(), p.value.size() * sizeof(float));
+            off += (int64_t)p.value.size();
+        }
+        return taken;
+    } catch (const std::exception& e) {
+        g_error = e.what();
+        return -1;
+    }
+}

@@ -911,13 +911,13 @@ struct StepBinding {
 
     r97::StepResult operator()(const r97::Batch& batch, const r97::ParamSet& params, r97::ParamSet* grads) {
         const R97hostStepConfig& c = step->c_;
-        if ((int64_t)batch.size() != c.micro_batch)
+        if ((int64_t)batch.size() > c.micro_batch)  // fewer: the missing rows run unscored
             throw std::runtime_error("r97b step: the batch holds " + std::to_string(batch.size()) +
-                                     " sequences, the step takes " + std::to_string(c.micro_batch));
+                                     " sequences, the step takes at most " + std::to_string(c.micro_batch));
         const int64_t T = step->tokens();
         std::vector<int32_t> ids((size_t)T, 0), tg((size_t)T, -1);
         int64_t scored = 0;
-        for (int64_t s = 0; s < c.micro_batch; ++s) {
+        for (int64_t s = 0; s < (int64_t)batch.size(); ++s) {
             const r97::TokenSeq& q = batch[(size_t)s];
             if ((int64_t)q.ids.size() > c.seq)
                 throw std::runtime_error("r97b step: a sequence is longer than the step's length");
@@ -1046,6 +1046,17 @@ extern "C" int r97host_step_run(void* step, const int32_t* ids, const int32_t* t
         return 1;
     }
 }
+
+// A heap copy of the step's r97::StepFn for a C++ caller that holds the reference's headers (its Trainer):
+// cast the result to r97::StepFn*, copy it, and free it with r97host_step_fn_free.
+extern "C" void* r97host_step_fn_new(void* step) {
+    auto* h = static_cast<StepHandle*>(step);
+    if (!h) return nullptr;
+    if (!h->fn) h->fn = r97b_host::make_device_step(h->step);
+    return new r97::StepFn(h->fn);
+}
+
+extern "C" void r97host_step_fn_free(void* fn) { delete static_cast<r97::StepFn*>(fn); }
 
 extern "C" int r97host_step_call(void* step, int32_t n_seq, const int64_t* lengths, const int32_t* ids,
                                  const uint8_t* score, int32_t nparams, const char* const* names,
