@@ -374,6 +374,8 @@ def profile_case(case: str) -> None:
     loss            CE over 2048 x 151936 bf16 logits (one head chunk)
     adamw           AdamW over the config-5 adapter (160.4 M f32 params)
     conv            GDN conv prep fwd + bwd at 8192 tokens, 8192 channels
+    attn            one config-5 attention core (B 2, 16 / 4 heads, S 4096, D 256), forward + backward;
+                    attn_small the same at B 1, S 2048
     step            one config-5 training step after one warm-up step, inside an NVTX range "step"
     """
     import torch
@@ -484,6 +486,29 @@ def profile_case(case: str) -> None:
         for _ in range(3):
             ops.conv_prep_fwd(x, cw, cu, 2, Hg, H, q, k, v)
             ops.conv_prep_bwd(x, cw, cu, 2, Hg, H, dq, dk, dv, dx)
+    elif case in ("attn", "attn_small"):
+        from r97training_b200 import ops
+        B, Hq, Hkv, S, D = (2, 16, 4, 4096, 256) if case == "attn" else (1, 16, 4, 2048, 256)
+        q = torch.randn(B, Hq, S, D, device=dev).bfloat16()
+        k = torch.randn(B, Hkv, S, D, device=dev).bfloat16()
+        v = torch.randn(B, Hkv, S, D, device=dev).bfloat16()
+        do = (torch.randn(B, Hq, S, D, device=dev) * 0.1).bfloat16()
+        ws = ops.attn_bwd_workspace(B, Hq, S, dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        fw, bw = [], []
+        for _ in range(3):
+            ev[0].record()
+            o, lse = ops.attn_fwd(q, k, v, D ** -0.5)
+            ev[1].record()
+            ops.attn_bwd(q, k, v, o, do, lse, D ** -0.5, ws)
+            ev[2].record()
+            torch.cuda.synchronize()
+            fw.append(ev[0].elapsed_time(ev[1]))
+            bw.append(ev[1].elapsed_time(ev[2]))
+        causal = 4.0 * B * Hq * (S * (S + 128) / 2) * D  # QK^T and PV over the causal tiles (128-row blocks)
+        print(f"attention B{B} Hq{Hq} Hkv{Hkv} S{S} D{D}: forward {min(fw):.3f} ms "
+              f"({causal / min(fw) / 1e9:.0f} TFLOP/s of the causal 2-product work), backward {min(bw):.3f} ms "
+              f"({2.5 * causal / min(bw) / 1e9:.0f} TFLOP/s of 2.5 x that)")
     elif case == "step":
         from r97training_b200.model import CONFIG5, Adapter, HybridModel, TrainStep
         model = HybridModel(CONFIG5, dev)

@@ -348,9 +348,12 @@ private:
     }
 
     // -------------------------------------------------------------------- launch helpers
-    void k(int status, const char* what) {
-        if (!dry_) check(status, what);
-    }
+// K(call, what): the call runs only outside the dry pass -- the dry pass hands out fake addresses, and must
+// evaluate no launch at all, so this is a macro around the call rather than a function taking its status.
+#define K(call, what)               \
+    do {                            \
+        if (!dry_) check((call), (what)); \
+    } while (0)
     uint16_t* bf(int64_t rows, int64_t cols) { return static_cast<uint16_t*>(arena_.take(rows * cols * 2)); }
     float* f32(int64_t n) { return static_cast<float*>(arena_.take(n * 4)); }
     View vbf(int64_t rows, int64_t cols) { return View{bf(rows, cols), rows, cols, cols}; }
@@ -395,7 +398,7 @@ private:
             g.ws = split_ws_;
             g.ws_bytes = split_ws_bytes_;
         }
-        k(r97b_gemm(&g, stream_), "gemm");
+        K(r97b_gemm(&g, stream_), "gemm");
     }
 
     // (bn, splits) rules of r97training_b200.ops: skinny_tiling for the adapter's narrow products and
@@ -458,7 +461,7 @@ private:
             d.scale_dtype = 0;  // f32
             d.scale_block_cols = 128;
             d.scale_row_bytes = P.w.cols / 128 * 4;
-            k(r97b_iqr_dequant_bf16(&d, grp.w_keep + row * grp.k, grp.k, stream_), "iqr dequant");
+            K(r97b_iqr_dequant_bf16(&d, grp.w_keep + row * grp.k, grp.k, stream_), "iqr dequant");
             row += P.n;
         }
     }
@@ -553,11 +556,11 @@ private:
 
     View rmsnorm_fwd(View x, const float* w) {
         View y = vbf(x.rows, x.cols);
-        k(r97b_rmsnorm_fwd(x.p, w, y.p, nullptr, x.rows, x.cols, c_.eps, 0.0f, 1.0f, stream_), "rmsnorm fwd");
+        K(r97b_rmsnorm_fwd(x.p, w, y.p, nullptr, x.rows, x.cols, c_.eps, 0.0f, 1.0f, stream_), "rmsnorm fwd");
         return y;
     }
     void rmsnorm_bwd(View x, const float* w, View dy, const uint16_t* addend, uint16_t* dx) {
-        k(r97b_rmsnorm_bwd(x.p, w, dy.p, addend, dx, x.rows, x.cols, c_.eps, 0.0f, 1.0f, stream_), "rmsnorm bwd");
+        K(r97b_rmsnorm_bwd(x.p, w, dy.p, addend, dx, x.rows, x.cols, c_.eps, 0.0f, 1.0f, stream_), "rmsnorm bwd");
     }
 
     R97bGdnDims gdn_dims(int32_t flags = 0) const {
@@ -589,13 +592,13 @@ private:
         s.q = bf(T, qk);
         s.k = bf(T, qk);
         s.v = bf(T, H * K);
-        k(r97b_conv_prep_fwd(s.y.p, s.y.ld, L.conv_w, cu_dev_, c_.micro_batch, T, (int32_t)Hg, (int32_t)H, s.q, s.k,
+        K(r97b_conv_prep_fwd(s.y.p, s.y.ld, L.conv_w, cu_dev_, c_.micro_batch, T, (int32_t)Hg, (int32_t)H, s.q, s.k,
                              s.v, stream_),
           "conv prep fwd");
         s.g = f32(T * H);
         s.beta = f32(T * H);
         const uint16_t* ba = s.y.p + 2 * qk + 2 * H * K;
-        k(r97b_gates_fwd(ba, s.y.ld, L.a_log, L.dt_bias, tok0_dev_, len_dev_, n_chunks_, (int32_t)H, s.g, s.beta,
+        K(r97b_gates_fwd(ba, s.y.ld, L.a_log, L.dt_bias, tok0_dev_, len_dev_, n_chunks_, (int32_t)H, s.g, s.beta,
                          stream_),
           "gates fwd");
         const int64_t nc = std::max<int32_t>(n_chunks_, 1);
@@ -608,10 +611,10 @@ private:
         s.o = bf(T, H * K);
         R97bGdnDims dm = gdn_dims();
         R97bGdnFwd fa{s.q, s.k, s.v, s.g, s.beta, nullptr, s.A, s.w, u, s.S, s.Vp, s.P, s.o, nullptr};
-        k(r97b_gdn_fwd(&dm, &fa, stream_), "gdn fwd");
+        K(r97b_gdn_fwd(&dm, &fa, stream_), "gdn fwd");
         const uint16_t* z = s.y.p + 2 * qk + H * K;
         s.on = vbf(T, H * K);
-        k(r97b_gated_rmsnorm_fwd(s.o, z, s.y.ld, (int32_t)H, L.gnorm_w, s.on.p, T * H, K, c_.eps, 0, stream_),
+        K(r97b_gated_rmsnorm_fwd(s.o, z, s.y.ld, (int32_t)H, L.gnorm_w, s.on.p, T * H, K, c_.eps, 0, stream_),
           "gated rmsnorm fwd");
         decode_group(go);
         View h1 = vbf(T, c_.hidden);
@@ -628,7 +631,7 @@ private:
         View dyin = vbf(T, gi.n);
         uint16_t* dO = bf(T, H * K);
         const uint16_t* z = s.y.p + 2 * qk + H * K;
-        k(r97b_gated_rmsnorm_bwd(s.o, z, s.y.ld, (int32_t)H, L.gnorm_w, don.p, dO, dyin.p + 2 * qk + H * K, T * H, K,
+        K(r97b_gated_rmsnorm_bwd(s.o, z, s.y.ld, (int32_t)H, L.gnorm_w, don.p, dO, dyin.p + 2 * qk + H * K, T * H, K,
                                  c_.eps, 0, stream_),
           "gated rmsnorm bwd");
         const int64_t nc = std::max<int32_t>(n_chunks_, 1);
@@ -661,13 +664,13 @@ private:
         ba.dv = dv;
         ba.dbeta = dbeta;
         ba.dg = dg;
-        k(r97b_gdn_bwd(&dm, &ba, stream_), "gdn bwd");
+        K(r97b_gdn_bwd(&dm, &ba, stream_), "gdn bwd");
         // dq, dk per value head: the conv adjoint sums each key head's value heads as it reads them
-        k(r97b_conv_prep_bwd(s.y.p, s.y.ld, L.conv_w, cu_dev_, c_.micro_batch, T, (int32_t)Hg, (int32_t)H, dq, dk, dv,
+        K(r97b_conv_prep_bwd(s.y.p, s.y.ld, L.conv_w, cu_dev_, c_.micro_batch, T, (int32_t)Hg, (int32_t)H, dq, dk, dv,
                              (int32_t)H, dyin.p, dyin.ld, stream_),
           "conv prep bwd");
         const uint16_t* bap = s.y.p + 2 * qk + 2 * H * K;
-        k(r97b_gates_bwd(bap, s.y.ld, L.a_log, L.dt_bias, tok0_dev_, len_dev_, n_chunks_, (int32_t)H, dg, dbeta,
+        K(r97b_gates_bwd(bap, s.y.ld, L.a_log, L.dt_bias, tok0_dev_, len_dev_, n_chunks_, (int32_t)H, dg, dbeta,
                          dyin.p + 2 * qk + 2 * H * K, dyin.ld, stream_),
           "gates bwd");
         View dn1 = vbf(T, c_.hidden);
@@ -687,22 +690,22 @@ private:
         s.qr = bf(B * Hq * S, Dh);
         s.kr = bf(B * Hkv * S, Dh);
         s.vt = bf(B * Hkv * S, Dh);
-        k(r97b_qk_norm_rope_fwd(s.y.p, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, L.q_norm, rope_cos_,
+        K(r97b_qk_norm_rope_fwd(s.y.p, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, L.q_norm, rope_cos_,
                                 rope_sin_, c_.rotary_dim, T, (int32_t)S, c_.eps, s.qr, stream_),
           "q norm rope");
-        k(r97b_qk_norm_rope_fwd(s.y.p + qn, s.y.ld, (int32_t)Dh, (int32_t)Hkv, (int32_t)Dh, L.k_norm, rope_cos_,
+        K(r97b_qk_norm_rope_fwd(s.y.p + qn, s.y.ld, (int32_t)Dh, (int32_t)Hkv, (int32_t)Dh, L.k_norm, rope_cos_,
                                 rope_sin_, c_.rotary_dim, T, (int32_t)S, c_.eps, s.kr, stream_),
           "k norm rope");
-        k(r97b_to_bhsd(s.y.p + qn + Hkv * Dh, s.y.ld, (int32_t)Dh, (int32_t)Hkv, (int32_t)Dh, T, (int32_t)S, s.vt, 0,
+        K(r97b_to_bhsd(s.y.p + qn + Hkv * Dh, s.y.ld, (int32_t)Dh, (int32_t)Hkv, (int32_t)Dh, T, (int32_t)S, s.vt, 0,
                        stream_),
           "v layout");
         s.attn = bf(B * Hq * S, Dh);
         s.lse = f32(B * Hq * S);
         R97bAttnFwd af{(int32_t)B, (int32_t)Hq, (int32_t)Hkv, (int32_t)S, (int32_t)Dh, 1.0f / std::sqrt((float)Dh),
                        s.qr, s.kr, s.vt, s.attn, s.lse};
-        k(r97b_attn_fwd(&af, stream_), "attention fwd");
+        K(r97b_attn_fwd(&af, stream_), "attention fwd");
         s.ga = vbf(T, Hq * Dh);
-        k(r97b_gate_mul_fwd(s.attn, s.y.p + Dh, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, T, (int32_t)S,
+        K(r97b_gate_mul_fwd(s.attn, s.y.p + Dh, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, T, (int32_t)S,
                             s.ga.p, stream_),
           "gate fwd");
         decode_group(go);
@@ -720,7 +723,7 @@ private:
         lin_bwd(go, s.ga, s.t[1], dh1, dga, nullptr, grad);
         View dy = vbf(T, gq.n);
         uint16_t* dattn = bf(B * Hq * S, Dh);
-        k(r97b_gate_mul_bwd(s.attn, s.y.p + Dh, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, T, (int32_t)S,
+        K(r97b_gate_mul_bwd(s.attn, s.y.p + Dh, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, T, (int32_t)S,
                             dga.p, dattn, dy.p + Dh, dy.ld, stream_),
           "gate bwd");
         uint16_t* dq = bf(B * Hq * S, Dh);
@@ -728,14 +731,14 @@ private:
         uint16_t* dv = bf(B * Hkv * S, Dh);
         R97bAttnBwd ab{(int32_t)B, (int32_t)Hq, (int32_t)Hkv, (int32_t)S, (int32_t)Dh, 1.0f / std::sqrt((float)Dh),
                        s.qr, s.kr, s.vt, s.attn, dattn, s.lse, dq, dk, dv, attn_ws_, attn_ws_bytes_};
-        k(r97b_attn_bwd(&ab, stream_), "attention bwd");
-        k(r97b_qk_norm_rope_bwd(s.y.p, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, L.q_norm, rope_cos_,
+        K(r97b_attn_bwd(&ab, stream_), "attention bwd");
+        K(r97b_qk_norm_rope_bwd(s.y.p, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, L.q_norm, rope_cos_,
                                 rope_sin_, c_.rotary_dim, T, (int32_t)S, c_.eps, dq, dy.p, dy.ld, stream_),
           "q norm rope bwd");
-        k(r97b_qk_norm_rope_bwd(s.y.p + qn, s.y.ld, (int32_t)Dh, (int32_t)Hkv, (int32_t)Dh, L.k_norm, rope_cos_,
+        K(r97b_qk_norm_rope_bwd(s.y.p + qn, s.y.ld, (int32_t)Dh, (int32_t)Hkv, (int32_t)Dh, L.k_norm, rope_cos_,
                                 rope_sin_, c_.rotary_dim, T, (int32_t)S, c_.eps, dk, dy.p + qn, dy.ld, stream_),
           "k norm rope bwd");
-        k(r97b_to_bhsd(dy.p + qn + Hkv * Dh, dy.ld, (int32_t)Dh, (int32_t)Hkv, (int32_t)Dh, T, (int32_t)S, dv, 1,
+        K(r97b_to_bhsd(dy.p + qn + Hkv * Dh, dy.ld, (int32_t)Dh, (int32_t)Hkv, (int32_t)Dh, T, (int32_t)S, dv, 1,
                        stream_),
           "v layout bwd");
         View dn1 = vbf(T, c_.hidden);
@@ -789,10 +792,10 @@ private:
             dd.scale = reinterpret_cast<const uint8_t*>(head_.scale);
             dd.scale_block_cols = 128;
             dd.scale_row_bytes = head_.cols / 128 * 4;
-            k(r97b_iqr_dequant_bf16(&dd, head_w_, d, stream_), "head dequant");
+            K(r97b_iqr_dequant_bf16(&dd, head_w_, d, stream_), "head dequant");
         }
         View x = vbf(T, d);
-        k(r97b_embed(head_w_, d, V, ids, T, d, x.p, stream_), "embed");
+        K(r97b_embed(head_w_, d, V, ids, T, d, x.p, stream_), "embed");
         std::vector<Saved> saved(layers_.size());
         for (size_t li = 0; li < layers_.size(); ++li) {
             Layer& L = layers_[li];
@@ -815,7 +818,7 @@ private:
             lg.out = logits_;
             lg.ldo = V;
             gemm(lg);
-            k(r97b_ce_kld(logits_, nullptr, targets ? targets + r0 : nullptr, logits_, loss_rows_ + r0, nullptr, rows, V,
+            K(r97b_ce_kld(logits_, nullptr, targets ? targets + r0 : nullptr, logits_, loss_rows_ + r0, nullptr, rows, V,
                           V, 0, gscale, 1.0f, 0.0f, stream_),
               "ce");
             G dh{rows, d};
