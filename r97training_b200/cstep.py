@@ -55,6 +55,9 @@ def lib():
         L.r97host_step_arena_bytes.argtypes = [c_vp]
         L.r97host_step_run.restype = c_i32
         L.r97host_step_run.argtypes = [c_vp, c_vp, c_vp, c_i64, c_vp, c_vp, c_vp, c_vp]
+        L.r97host_step_fn_new.restype = c_vp
+        L.r97host_step_fn_new.argtypes = [c_vp]
+        L.r97host_step_fn_free.argtypes = [c_vp]
         L.r97host_step_call.restype = c_i32
         L.r97host_step_call.argtypes = [c_vp, c_i32, c_vp, c_vp, c_vp, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]
         _lib = L

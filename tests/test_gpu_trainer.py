@@ -19,6 +19,10 @@ pytestmark = pytest.mark.gpu
 def _run(cs, values, seqs, out, resume, count, total):
     lib = oracle.ref_lib()
     lib.ref_trainer_run.restype = ctypes.c_int64
+    lib.ref_trainer_run.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                    ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_double,
+                                    ctypes.c_int64, ctypes.c_int64, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_void_p,
+                                    ctypes.c_char_p, ctypes.c_int64]
     names = [n for n, _, _ in cs.params]
     shapes = np.array([s for _, _, s in cs.params], np.int64).reshape(-1)
     cnames = (ctypes.c_char_p * len(names))(*[n.encode() for n in names])
@@ -29,14 +33,14 @@ def _run(cs, values, seqs, out, resume, count, total):
     ckpt = ctypes.create_string_buffer(4096)
     from r97training_b200.cstep import lib as hlib
     fn = hlib().r97host_step_fn_new(cs.handle)
-    hlib().r97host_step_fn_free.argtypes = [ctypes.c_void_p]
+    assert fn
     try:
-        taken = lib.ref_trainer_run(ctypes.c_void_p(fn), len(names), cnames, shapes.ctypes.data, vals.ctypes.data,
-                                    len(seqs), lengths.ctypes.data, ids.ctypes.data, ctypes.c_int64(256),
-                                    ctypes.c_double(1e-3), ctypes.c_int64(total), ctypes.c_int64(count),
-                                    out.encode(), (resume or "").encode(), losses.ctypes.data, ckpt, 4096)
+        taken = lib.ref_trainer_run(fn, len(names), ctypes.cast(cnames, ctypes.c_void_p), shapes.ctypes.data,
+                                    vals.ctypes.data, len(seqs), lengths.ctypes.data, ids.ctypes.data, 256, 1e-3,
+                                    total, count, out.encode(), (resume or "").encode(), losses.ctypes.data, ckpt,
+                                    4096)
     finally:
-        hlib().r97host_step_fn_free(ctypes.c_void_p(fn))
+        hlib().r97host_step_fn_free(fn)
     assert taken == count, lib.ref_last_error().decode()
     res, off = {}, 0
     for n, _, (r, c) in cs.params:
