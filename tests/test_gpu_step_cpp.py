@@ -1,8 +1,9 @@
 """The C++ training step (host/step.cpp, the reference's StepFn over libr97b200.so) against the Python step
 (model.TrainStep) on the same model, adapter and batch: the same kernels in the same order, so the same loss
 and gradients up to the float atomics whose summation order varies from run to run (the adapter-gradient
-GEMMs' split-K and the GDN adjoint's per-row sums) -- held to relative L2 <= 1e-4 per leaf and the loss to
-1e-5. Checked twice: through r97host_step_run on device buffers, and through the StepFn the reference's trainer
+GEMMs' split-K and the GDN adjoint's per-row sums). The loss is held to 1e-5 relative and every leaf to three
+times the spread of two runs of the Python step itself (at least 1e-4): measured, 1e-5 to 4e-4, largest on
+the first layer's GDN in-projection, whose gradient passes every layer's near-cancelling GDN sums. Checked twice: through r97host_step_run on device buffers, and through the StepFn the reference's trainer
 calls (r97host_step_call: a Batch with score masks, a ParamSet by name, the gradient ParamSet back)."""
 import numpy as np
 import pytest
@@ -37,14 +38,19 @@ def test_cpp_step_matches_python_step(cuda, shape):
     tg_d = torch.from_numpy(tg.reshape(-1)).to(cuda)
     loss_py = float(step.run(ids_d, tg_d, n_scored=n_scored)) * n_scored
     g_py = ad.g.clone()
+    ad.g.zero_()
+    step.run(ids_d, tg_d, n_scored=n_scored)
+    g_py2 = ad.g.clone()
     g_c = torch.zeros_like(ad.g)
     loss_c = cs.run(ids_d.reshape(-1), tg_d, n_scored, ad.w, g_c)
     torch.cuda.synchronize()
     assert abs(loss_c - loss_py) <= 1e-5 * abs(loss_py), (loss_c, loss_py)
-    gp, gc = g_py.cpu().numpy(), g_c.cpu().numpy()
+    gp, gc, gp2 = g_py.cpu().numpy(), g_c.cpu().numpy(), g_py2.cpu().numpy()
+    spread = max(rel_l2(gp2[o:o + r * c], gp[o:o + r * c]) for _, o, (r, c) in cs.params)
+    bound = max(3 * spread, 1e-4)
     for name, off, (r, c) in cs.params:
         a, b = gc[off:off + r * c], gp[off:off + r * c]
-        assert rel_l2(a, b) <= 1e-4, (name, rel_l2(a, b))
+        assert rel_l2(a, b) <= bound, (name, rel_l2(a, b), spread)
     # through the StepFn
     w = ad.w.cpu().numpy()
     values = {n: w[o:o + r * c] for n, o, (r, c) in cs.params}
@@ -52,7 +58,7 @@ def test_cpp_step_matches_python_step(cuda, shape):
     assert scored == n_scored
     assert abs(loss_f - loss_py) <= 1e-5 * abs(loss_py), (loss_f, loss_py)
     for name, off, (r, c) in cs.params:
-        assert rel_l2(grads[name].ravel(), gp[off:off + r * c]) <= 1e-4, name
+        assert rel_l2(grads[name].ravel(), gp[off:off + r * c]) <= bound, name
     cs.close()
 
 
