@@ -573,7 +573,7 @@ private:
         d.chunk = 64;
         d.flags = flags;
         d.T = T_;
-        d.scale = 1.0f / std::sqrt((float)c_.head_k);
+        d.scale = (float)(1.0 / std::sqrt((double)c_.head_k));  // rounded once, as the Python step passes it
         d.chunk_tok0 = tok0_dev_;
         d.chunk_len = len_dev_;
         d.seq_chunk0 = sc0_dev_;
@@ -701,7 +701,7 @@ private:
           "v layout");
         s.attn = bf(B * Hq * S, Dh);
         s.lse = f32(B * Hq * S);
-        R97bAttnFwd af{(int32_t)B, (int32_t)Hq, (int32_t)Hkv, (int32_t)S, (int32_t)Dh, 1.0f / std::sqrt((float)Dh),
+        R97bAttnFwd af{(int32_t)B, (int32_t)Hq, (int32_t)Hkv, (int32_t)S, (int32_t)Dh, (float)(1.0 / std::sqrt((double)Dh)),
                        s.qr, s.kr, s.vt, s.attn, s.lse};
         K(r97b_attn_fwd(&af, stream_), "attention fwd");
         s.ga = vbf(T, Hq * Dh);
@@ -729,7 +729,7 @@ private:
         uint16_t* dq = bf(B * Hq * S, Dh);
         uint16_t* dk = bf(B * Hkv * S, Dh);
         uint16_t* dv = bf(B * Hkv * S, Dh);
-        R97bAttnBwd ab{(int32_t)B, (int32_t)Hq, (int32_t)Hkv, (int32_t)S, (int32_t)Dh, 1.0f / std::sqrt((float)Dh),
+        R97bAttnBwd ab{(int32_t)B, (int32_t)Hq, (int32_t)Hkv, (int32_t)S, (int32_t)Dh, (float)(1.0 / std::sqrt((double)Dh)),
                        s.qr, s.kr, s.vt, s.attn, dattn, s.lse, dq, dk, dv, attn_ws_, attn_ws_bytes_};
         K(r97b_attn_bwd(&ab, stream_), "attention bwd");
         K(r97b_qk_norm_rope_bwd(s.y.p, s.y.ld, (int32_t)(2 * Dh), (int32_t)Hq, (int32_t)Dh, L.q_norm, rope_cos_,
