@@ -374,8 +374,8 @@ def profile_case(case: str) -> None:
     loss            CE over 2048 x 151936 bf16 logits (one head chunk)
     adamw           AdamW over the config-5 adapter (160.4 M f32 params)
     conv            GDN conv prep fwd + bwd at 8192 tokens, 8192 channels
-    attn            one config-5 attention core (B 2, 16 / 4 heads, S 4096, D 256), forward + backward;
-                    attn_small the same at B 1, S 2048
+    attn            one config-5 attention core (B 2, 16 / 4 heads, S 4096, D 256), forward + backward, with
+                    CUDA-event timings; attn_small the same at B 1, S 2048; attn_fwd the forward alone
     step            one config-5 training step after one warm-up step, inside an NVTX range "step"
     """
     import torch
@@ -486,6 +486,14 @@ def profile_case(case: str) -> None:
         for _ in range(3):
             ops.conv_prep_fwd(x, cw, cu, 2, Hg, H, q, k, v)
             ops.conv_prep_bwd(x, cw, cu, 2, Hg, H, dq, dk, dv, dx)
+    elif case == "attn_fwd":
+        from r97training_b200 import ops
+        B, Hq, Hkv, S, D = 2, 16, 4, 4096, 256
+        q = torch.randn(B, Hq, S, D, device=dev).bfloat16()
+        k = torch.randn(B, Hkv, S, D, device=dev).bfloat16()
+        v = torch.randn(B, Hkv, S, D, device=dev).bfloat16()
+        for _ in range(3):
+            ops.attn_fwd(q, k, v, D ** -0.5)
     elif case in ("attn", "attn_small"):
         from r97training_b200 import ops
         B, Hq, Hkv, S, D = (2, 16, 4, 4096, 256) if case == "attn" else (1, 16, 4, 2048, 256)
