@@ -37,8 +37,9 @@ def test_graph_replay_matches_eager_steps(cuda):
     inside the graph. The runs are not bit-identical: the GDN adjoint adds some per-row terms with
     shared-memory float atomics and the adapter-gradient GEMMs reduce their split-K partials with float
     atomics, so sums land in a different order from run to run. That changes the last bits of f32 sums
-    only, so the gradient is held to relative L2 <= 1e-4 and cosine >= 0.9999, well inside the north star's
-    bar (1e-2 and 0.999), and two eager runs are held to the same."""
+    (now and then flipping a bf16 rounding downstream), so the gradient is held to relative L2 <= 5e-4 and
+    cosine >= 0.9999, well inside the north star's bar (1e-2 and 0.999), and two eager runs are held to the
+    same."""
     from r97training_b200.model import GraphStep
     cfg = HybridConfig(hidden=512, layers=4, gdn_heads=4, gdn_qk_heads=2, attn_heads=2, attn_kv_heads=1, ffn=1024,
                        vocab=4096, rank=16, alpha=32, seq=256, micro_batch=2, lr=1e-3)
@@ -65,7 +66,7 @@ def test_graph_replay_matches_eager_steps(cuda):
     for other, what in ((grads[1], "eager vs eager"), (grads[2], "graph vs eager")):
         rel = float((other - grads[0]).norm() / grads[0].norm())
         cos = float((other * grads[0]).sum() / (other.norm() * grads[0].norm()))
-        assert rel <= 1e-4 and cos >= 0.9999, (what, rel, cos)
+        assert rel <= 5e-4 and cos >= 0.9999, (what, rel, cos)
 
     losses = []
     for graph in (False, True):

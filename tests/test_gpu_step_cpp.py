@@ -2,8 +2,10 @@
 (model.TrainStep) on the same model, adapter and batch: the same kernels in the same order, so the same loss
 and gradients up to the float atomics whose summation order varies from run to run (the adapter-gradient
 GEMMs' split-K and the GDN adjoint's per-row sums). The loss is held to 1e-5 relative and every leaf to three
-times the spread of two runs of the Python step itself (at least 1e-4): measured, 1e-5 to 4e-4, largest on
-the first layer's GDN in-projection, whose gradient passes every layer's near-cancelling GDN sums. Checked twice: through r97host_step_run on device buffers, and through the StepFn the reference's trainer
+times the spread of two runs of the Python step itself, at least 1e-3. Measured: most runs bit-identical; now
+and then one shared-memory atomic sum in the GDN adjoint lands one ulp apart, a bf16 rounding downstream flips,
+and the first layer's GDN in-projection leaves (whose gradient passes every layer's near-cancelling GDN sums)
+move by 3.6e-4 -- the same outcome whichever of the two steps it happens in. Checked twice: through r97host_step_run on device buffers, and through the StepFn the reference's trainer
 calls (r97host_step_call: a Batch with score masks, a ParamSet by name, the gradient ParamSet back)."""
 import numpy as np
 import pytest
@@ -47,7 +49,7 @@ def test_cpp_step_matches_python_step(cuda, shape):
     assert abs(loss_c - loss_py) <= 1e-5 * abs(loss_py), (loss_c, loss_py)
     gp, gc, gp2 = g_py.cpu().numpy(), g_c.cpu().numpy(), g_py2.cpu().numpy()
     spread = max(rel_l2(gp2[o:o + r * c], gp[o:o + r * c]) for _, o, (r, c) in cs.params)
-    bound = max(3 * spread, 1e-4)
+    bound = max(3 * spread, 1e-3)
     for name, off, (r, c) in cs.params:
         a, b = gc[off:off + r * c], gp[off:off + r * c]
         assert rel_l2(a, b) <= bound, (name, rel_l2(a, b), spread)
