@@ -417,9 +417,17 @@ def profile_case(case: str) -> None:
         beta = torch.sigmoid(torch.randn(T, H, device=dev))
         do = (torch.randn(T, H, 128, device=dev) * 1e-2).bfloat16()
         plan = GdnPlan([0, 4096, 8192], H, Hg, dev)
-        for _ in range(2):
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        fwd = bwd = 0.0
+        for it in range(2):
+            ev[0].record()
             o, _, sv = plan.forward(q, k, v, g.contiguous(), beta)
+            ev[1].record()
             plan.backward(sv, do)
+            ev[2].record()
+            torch.cuda.synchronize()
+            fwd, bwd = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+        print(f"gdn layer T {T} H {H} Hg {Hg}: forward {fwd:.3f} ms, backward {bwd:.3f} ms (second pass)")
     elif case == "decode":
         from r97training_b200 import iqr as IQ
         w = IQ.synth_weight(24576, 4096, seed=1, device=dev)

@@ -32,7 +32,8 @@ extern "C" uint64_t r97b_launch_count(void) { return r97b::g_launches.load(std::
 extern "C" int r97b_abi_version(void) { return 4; }
 
 extern "C" int r97b_device_error(unsigned int* out_bits) {
-    unsigned bits = r97b::gemm_error_word();
+    unsigned bits = r97b::gemm_error_word() | r97b::attn_error_word() | r97b::attn_fwd_error_word() |
+                    r97b::gdn_error_word();
     if (out_bits) *out_bits = bits;
     return cudaGetLastError() == cudaSuccess ? R97B_OK : R97B_ELAUNCH;
 }

@@ -20,17 +20,21 @@
 //   B2b gdn_bwd_b    (chunk, head)        the intra-chunk terms: dP, dA = dw kb^T + dV' vb^T, A^T dw, A^T dV',
 //                                          and the solve's adjoint dM = -A^T dA A^T (the kkt adjoint)
 //
-// Every product runs on the tensor cores (wmma16.cuh: mma.sync m16n8k16, bf16 in, f32 accumulate).
-// q, k, v and dO are bf16 already and enter exactly; an f32 operand (a state, A, P, V', w, dV', ...) is
-// split into bf16 hi + lo tiles and its product takes two or three passes, which keeps ~16 bits of the
-// operand. The sequential passes keep their state in the f32 MMA accumulators. Only the 64-step forward
-// substitution of the solve runs on CUDA cores.
+// Every product runs on the tensor cores, bf16 in and f32 accumulate. F1, F2, F3, B1 and B2a are tcgen05
+// kernels (tc_tile.cuh: swizzled shared-memory tiles, one thread issuing the MMAs, f32 accumulators in
+// TMEM; the state passes keep their state in registers laid out as the accumulator); B2b and the
+// standalone solve adjoint B3 use warp mma.sync (wmma16.cuh), whose register-resident 64 x 64 products
+// measured faster for B2b's chain of small intra-chunk products than a tcgen05 form (668 against 1008 us
+// for a config-5 layer). q, k, v and dO are bf16 already and enter exactly; an f32 operand (a state, A, P,
+// V', w, dV', ...) is split into bf16 hi + lo tiles and its product takes two or three passes, which keeps
+// ~16 bits of the operand. Only the 64-step forward substitution of the solve runs on CUDA cores.
 //
 // Sequences are ragged (cu_seqlens); a sequence's last chunk may be short, and its padded rows are zero
 // so they add nothing. Head dims K = V = 128 and the chunk of 64 are fixed here.
 #include "r97b_internal.h"
 #include "fastmath.cuh"
 #include "wmma16.cuh"
+#include "tc_tile.cuh"
 
 #include <cuda_bf16.h>
 #include <math.h>
@@ -97,17 +101,6 @@ __device__ __forceinline__ void async_rows_pair(bf16* dh, bf16* dl, Pair src, in
                                                 int head) {
     async_rows(dh, src.hi, tok0, n, heads, head);
     async_rows(dl, src.lo, tok0, n, heads, head);
-}
-
-// one (chunk, head)'s [128][128] block of a pair buffer [chunks, H, 128, 128] -> [128][kP128] tiles
-__device__ __forceinline__ void async_block_pair(bf16* dh, bf16* dl, Pair src, int64_t block) {
-    const bf16* h = src.hi + block * D * D;
-    const bf16* l = src.lo + block * D * D;
-    for (int idx = threadIdx.x; idx < D * 16; idx += blockDim.x) {
-        const int r = idx >> 4, x = (idx & 15) * 8;
-        cp_async16(dh + r * kP128 + x, h + r * D + x, true);
-        cp_async16(dl + r * kP128 + x, l + r * D + x, true);
-    }
 }
 
 // g (and beta) of the chunk's rows; zero past its end
@@ -274,59 +267,104 @@ __device__ __forceinline__ void invert_unit_lower(const float* Ms, float* As, fl
     __syncthreads();
 }
 
-// F1: per (chunk, value head): A = (I + M)^-1, w = (A diag(beta e^g)) k, u = (A diag(beta)) v.
+// F1: per (chunk, value head): A = (I + M)^-1, w = (A diag(beta e^g)) k, u = (A diag(beta)) v, on tcgen05
+// for the products: k k^T (M = 128 rows of which the chunk's 64 are read), then w^T = k^T (A diag(beta e^g))^T
+// and u^T = v^T (A diag(beta))^T with the 128 lanes as M (the A factors as bf16 (hi, lo) tiles, two passes).
+// The solve stays on CUDA cores in f32. TMEM: k k^T at column 0, w^T at 64, u^T at 128.
+namespace f1 {
+constexpr int kK = 0;
+constexpr int kV = kK + tc::kRowTile;
+constexpr int kA1h = kV + tc::kRowTile;     // A diag(beta e^g) hi/lo [64][64]; before the solve ends, its scratch
+constexpr int kA1l = kA1h + tc::kSqTile;
+constexpr int kA2h = kA1l + tc::kSqTile;    // A diag(beta) hi/lo
+constexpr int kA2l = kA2h + tc::kSqTile;
+constexpr int kMs = kA2l + tc::kSqTile;     // f32 [64][65]
+constexpr int kAs = kMs + L * F65 * 4;      // f32 [64][65]
+constexpr int kG = kAs + L * F65 * 4;       // g, beta [64] each
+constexpr int kBar = kG + 2 * L * 4;
+constexpr int kUsed = kBar + 16;
+}  // namespace f1
+
 __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restrict__ k, const bf16* __restrict__ v,
                                                     const float* __restrict__ g, const float* __restrict__ beta,
                                                     float* __restrict__ A, float* __restrict__ w, float* __restrict__ u) {
-    extern __shared__ __align__(16) unsigned char smraw[];
-    bf16* ks = reinterpret_cast<bf16*>(smraw);          // [64][136]
-    bf16* vs = ks + L * kP128;                           // [64][136]
-    bf16* a1h = vs + L * kP128;                          // [64][72]  A diag(beta e^g), hi/lo
-    bf16* a1l = a1h + L * kP64;
-    bf16* a2h = a1l + L * kP64;                          // A diag(beta), hi/lo
-    bf16* a2l = a2h + L * kP64;
-    float* Ms = reinterpret_cast<float*>(a2l + L * kP64);  // [64][65]
-    float* As = Ms + L * F65;                              // [64][65]
-    float* red = As + L * F65;                             // [4][64]
-    float* gs = red + 4 * L;
+    using namespace f1;
+    extern __shared__ unsigned char smraw[];
+    unsigned char* sm = tc::align1024(smraw);
+    unsigned char *Ks = sm + kK, *Vs = sm + kV, *A1h = sm + kA1h, *A1l = sm + kA1l, *A2h = sm + kA2h, *A2l = sm + kA2l;
+    float* Ms = reinterpret_cast<float*>(sm + kMs);
+    float* As = reinterpret_cast<float*>(sm + kAs);
+    float* gs = reinterpret_cast<float*>(sm + kG);
     float* bs = gs + L;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBar);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kBar + 8);
     const int c = blockIdx.x, h = blockIdx.y, hk = h / dm.grp;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
-    const int warp = threadIdx.x >> 5;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3, ch = warp >> 2;
     const bool given = (dm.flags & R97B_GDN_A_GIVEN) != 0;
-    async_rows(ks, k, tok0, n, dm.Hg, hk);
-    async_rows(vs, v, tok0, n, dm.H, h);
+    tc::stage_rows(Ks, k, tok0, n, dm.Hg, hk);
+    tc::stage_rows(Vs, v, tok0, n, dm.H, h);
     async_gb(gs, bs, g, beta, tok0, n, dm.H, h);
     cp_async_commit();
     if (given) {  // the caller's solve: its lower triangle, diagonal included, for the chunk's rows
         const int j = threadIdx.x & 63, i0 = threadIdx.x >> 6;  // 256 threads: rows i0, i0 + 4, ...
         float av[L / 4];
 #pragma unroll
-        for (int q = 0; q < L / 4; ++q) {  // every load issued before the first store
-            const int i = i0 + 4 * q;
-            av[q] = (i < n && j <= i) ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f;
+        for (int s = 0; s < L / 4; ++s) {  // every load issued before the first store
+            const int i = i0 + 4 * s;
+            av[s] = (i < n && j <= i) ? A[((tok0 + i) * dm.H + h) * L + j] : 0.0f;
         }
 #pragma unroll
-        for (int q = 0; q < L / 4; ++q) As[(i0 + 4 * q) * F65 + j] = av[q];
+        for (int s = 0; s < L / 4; ++s) As[(i0 + 4 * s) * F65 + j] = av[s];
+    }
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (warp == 0) {
+        tmem_alloc(tslot, 256);
+        tmem_relinquish();
     }
     cp_async_wait_all();
+    tc::fence_proxy_async();
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = *tslot;
+    const uint32_t tq = tm + ((uint32_t)(32 * qd) << 16) + (uint32_t)(32 * ch);
+    constexpr uint32_t id = make_idesc_bf16(128, 64, 0, 0);
+    constexpr uint32_t id_a = make_idesc_bf16(128, 64, 1, 0);  // A MN-major
+    const uint32_t sk = smem_u32(Ks), sv = smem_u32(Vs);
+    uint32_t phase = 0;
+    bool ok = true;
     if (!given) {
         // M = strict lower of beta_i (k_i . k_l) e^{g_i - g_l}
-        float acc[1][4][4];
-        acc_zero<16, 32>(acc);
-        const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
-        warp_mma<16, 32, 128, false, false>(acc, ks, kP128, ks, kP128, m0, n0);
-        acc_for<16, 32>(acc, m0, n0, [&](int r, int l, float& x) {
-            // only the chunk's own rows: a padded row's g is 0, and e^{0 - g_l} can overflow to inf, whose
-            // 0 * inf the blocked inverse would carry into every row
-            Ms[r * F65 + l] = (l < r && r < n) ? bs[r] * x * gexp(gs[r] - gs[l]) : 0.0f;
-        });
+        if (threadIdx.x == 0) {
+            for (int kk = 0; kk < 8; ++kk)
+                umma_f16(tm, tc::kdesc(sk, 64, 0, kk), tc::kdesc(sk, 64, 0, kk), id, kk > 0 ? 1u : 0u);
+            umma_commit(bar);
+        }
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar, phase, nullptr));
+        phase ^= 1u;
+        tc_fence_after();
+        if (ok && qd < 2) {
+            const int r = 32 * qd + lane;
+            float x[32];
+            tc::tmem_row32(tq, x);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+                const int l = 32 * ch + i;
+                // only the chunk's own rows: a padded row's g is 0, and e^{0 - g_l} can overflow to inf, whose
+                // 0 * inf the blocked inverse would carry into every row
+                Ms[r * F65 + l] = (l < r && r < n) ? bs[r] * x[i] * gexp(gs[r] - gs[l]) : 0.0f;
+            }
+        }
         __syncthreads();
         // A = (I + M)^-1 by blocks: the four 16x16 diagonal blocks by forward substitution (a warp each),
         // then 16 -> 32 -> 64 with X21 = -A22 (M21 A11) (the inverse of a block lower-triangular matrix)
-        invert_unit_lower(Ms, As, reinterpret_cast<float*>(a1h));
+        invert_unit_lower(Ms, As, reinterpret_cast<float*>(A1h));
     }
     {
         const int j = threadIdx.x & 63;  // a thread keeps its column (the stride is a multiple of 64)
@@ -334,60 +372,96 @@ __global__ void __launch_bounds__(256) gdn_fwd_prep(Dims dm, const bf16* __restr
         for (int i = threadIdx.x >> 6; i < L; i += blockDim.x >> 6) {
             const float a = As[i * F65 + j];
             if (i < n && !given) A[((tok0 + i) * dm.H + h) * L + j] = a;
-            put_split(a1h, a1l, i * kP64 + j, a * e);
-            put_split(a2h, a2l, i * kP64 + j, a * bj);
+            __nv_bfloat16 hi, lo;
+            const uint32_t o = tc::elem_off(64, i, j);
+            split_bf16(a * e, hi, lo);
+            *reinterpret_cast<__nv_bfloat16*>(A1h + o) = hi;
+            *reinterpret_cast<__nv_bfloat16*>(A1l + o) = lo;
+            split_bf16(a * bj, hi, lo);
+            *reinterpret_cast<__nv_bfloat16*>(A2h + o) = hi;
+            *reinterpret_cast<__nv_bfloat16*>(A2l + o) = lo;
         }
     }
+    tc::fence_proxy_async();
+    tc_fence_before();
     __syncthreads();
-    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
-    float acc[1][8][4];
-    acc_zero<16, 64>(acc);
-    mma_split_a<16, 64, 64, false, true>(acc, a1h, a1l, kP64, ks, kP128, m0, n0);
-    bf16* w_hi = reinterpret_cast<bf16*>(w);             // w is kept as a bf16 (hi, lo) pair in the
-    bf16* w_lo = w_hi + (int64_t)dm.T * dm.H * D;         // bytes of an f32 [T, H, 128] buffer
-    acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {
-        if (r < n) put_split2(w_hi, w_lo, ((tok0 + r) * dm.H + h) * D + d, acc[i][j][2 * hh], acc[i][j][2 * hh + 1]);
-    });
-    acc_zero<16, 64>(acc);
-    mma_split_a<16, 64, 64, false, true>(acc, a2h, a2l, kP64, vs, kP128, m0, n0);
-    acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {
-        if (r < n)
-            *reinterpret_cast<float2*>(u + ((tok0 + r) * dm.H + h) * D + d) =
-                make_float2(acc[i][j][2 * hh], acc[i][j][2 * hh + 1]);
-    });
+    tc_fence_after();
+    if (threadIdx.x == 0 && ok) {
+        const uint32_t a1h = smem_u32(A1h), a1l = smem_u32(A1l), a2h = smem_u32(A2h), a2l = smem_u32(A2l);
+        // w^T = k^T a1^T, u^T = v^T a2^T (a1, a2: hi, lo)
+        for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tm + 64, tc::mdesc(sk, 64, 0, kk), tc::kdesc(a1h, 64, 0, kk), id_a, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) umma_f16(tm + 64, tc::mdesc(sk, 64, 0, kk), tc::kdesc(a1l, 64, 0, kk), id_a, 1u);
+        for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tm + 128, tc::mdesc(sv, 64, 0, kk), tc::kdesc(a2h, 64, 0, kk), id_a, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) umma_f16(tm + 128, tc::mdesc(sv, 64, 0, kk), tc::kdesc(a2l, 64, 0, kk), id_a, 1u);
+        umma_commit(bar);
+    }
+    ok = __all_sync(0xFFFFFFFFu, ok && mbar_wait(bar, phase, nullptr));
+    tc_fence_after();
+    if (ok) {
+        // lane d = 32 (warp % 4) + lane of the chunk's tokens 32 (warp / 4) ..: w as a (hi, lo) pair in the
+        // bytes of an f32 [T, H, 128] buffer, u in f32
+        const int d = 32 * qd + lane;
+        bf16* w_hi = reinterpret_cast<bf16*>(w);
+        bf16* w_lo = w_hi + (int64_t)dm.T * dm.H * D;
+        float x[32];
+        tc::tmem_row32(tq + 64, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int r = 32 * ch + i;
+            if (r < n) put_split(w_hi, w_lo, ((tok0 + r) * dm.H + h) * D + d, x[i]);
+        }
+        tc::tmem_row32(tq + 128, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int r = 32 * ch + i;
+            if (r < n) u[((tok0 + r) * dm.H + h) * D + d] = x[i];
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, 256);
 }
 
-// F2: per (sequence, value head, 64 value lanes): the state pass over the sequence's chunks. The state
-// slice S[128][64] lives in the f32 accumulators of its own product (S += k^T V''); each chunk's operands
-// (w as a bf16 hi/lo pair, k, the u slice, g) stream into a double-buffered stage with cp.async while the
-// previous chunk computes.
-constexpr int VS2 = 64;   // value lanes per forward-state CTA
-constexpr int P64 = 72;   // bf16 pitch of a [*, 64] tile (== kP64)
-constexpr int U68 = 68;   // f32 pitch of the u slice
+// F2: per (sequence, value head, 64 value lanes): the state pass over the sequence's chunks, on tcgen05.
+// The state slice S[128 key lanes][64 value lanes] stays in registers in the accumulator's TMEM layout (key
+// lane d = 32 (warp % 4) + lane, value lanes 32 (warp / 4) .. + 31), and each chunk takes two products:
+// W' = w S (M = the chunk's 64 tokens, the upper half of the 128-row MMA unused; w and S as bf16 (hi, lo)
+// tiles, three passes), giving V' = u - W' and V'' = e^{gL - g} V'; then k^T V'' (M = the 128 key lanes,
+// two passes), added to e^{gL} S. A chunk's w pair, k, u slice and g stream into a double-buffered stage
+// by cp.async while the previous chunk computes. TMEM: W' at column 0, k^T V'' at 64.
+namespace f2 {
+constexpr int kWh = 0;
+constexpr int kWl = kWh + tc::kRowTile;
+constexpr int kK = kWl + tc::kRowTile;
+constexpr int kU = kK + tc::kRowTile;        // u slice, f32 [64][68]
+constexpr int kUP = 68;                       // its pitch: a quarter-warp's 16-byte row reads hit distinct banks
+constexpr int kG = kU + L * kUP * 4;
+constexpr int kStage = ((kG + L * 4) + 1023) & ~1023;
+constexpr int kSh = 2 * kStage;               // S hi/lo [128][64]
+constexpr int kSl = kSh + 128 * 64 * 2;
+constexpr int kVh = kSl + 128 * 64 * 2;       // V'' hi/lo [64][64]
+constexpr int kVl = kVh + tc::kSqTile;
+constexpr int kBar = kVl + tc::kSqTile;       // mbarrier, abort flag, TMEM slot
+constexpr int kUsed = kBar + 16;
+}  // namespace f2
 
-struct F2Stage {
-    bf16 wh[L * kP128], wl[L * kP128], ks[L * kP128];
-    float us[L * U68];
-    float gs[L];
-};
-
-__device__ __forceinline__ void f2_issue(F2Stage& st, const Dims& dm, const bf16* w_hi, const bf16* w_lo,
+__device__ __forceinline__ void f2_issue(unsigned char* st, const Dims& dm, const bf16* w_hi, const bf16* w_lo,
                                          const bf16* k, const float* u, const float* g, int c, int h, int hk, int e0) {
+    using namespace f2;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
+    tc::stage_rows(st + kWh, w_hi, tok0, n, dm.H, h);
+    tc::stage_rows(st + kWl, w_lo, tok0, n, dm.H, h);
+    tc::stage_rows(st + kK, k, tok0, n, dm.Hg, hk);
+    float* us = reinterpret_cast<float*>(st + kU);
     for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
-        const int i = idx >> 4, q = (idx & 15) * 8;
+        const int i = idx >> 4, q = (idx & 15) * 4;
         const bool on = i < n;
-        const int64_t row = on ? tok0 + i : tok0;
-        cp_async16(&st.wh[i * kP128 + q], w_hi + (row * dm.H + h) * D + q, on);
-        cp_async16(&st.wl[i * kP128 + q], w_lo + (row * dm.H + h) * D + q, on);
-        cp_async16(&st.ks[i * kP128 + q], k + (row * dm.Hg + hk) * D + q, on);
-        cp_async16(&st.us[i * U68 + (q >> 1)], u + (row * dm.H + h) * D + e0 + (q >> 1), on);
+        cp_async16(us + i * kUP + q, u + ((on ? tok0 + i : tok0) * dm.H + h) * D + e0 + q, on);
     }
-    for (int i = threadIdx.x; i < L; i += blockDim.x) {
-        const bool on = i < n;
-        cp_async4(&st.gs[i], g + ((on ? tok0 + i : tok0) * dm.H + h), on);
-    }
+    async_gb(reinterpret_cast<float*>(st + kG), nullptr, g, nullptr, tok0, n, dm.H, h);
     cp_async_commit();
 }
 
@@ -395,188 +469,307 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
                                                      const float* __restrict__ w, const float* __restrict__ u,
                                                      const float* __restrict__ h0, float* __restrict__ S_all,
                                                      float* __restrict__ Vp, float* __restrict__ ht) {
-    extern __shared__ __align__(16) unsigned char smraw[];
-    F2Stage* stage = reinterpret_cast<F2Stage*>(smraw);           // [2]
-    bf16* sh = reinterpret_cast<bf16*>(smraw + 2 * sizeof(F2Stage));  // S hi/lo [128][72]
-    bf16* sl = sh + D * P64;
-    bf16* vh = sl + D * P64;                                       // V'' = e^{gL-g} V' hi/lo [64][72]
-    bf16* vl = vh + L * P64;
+    using namespace f2;
+    extern __shared__ unsigned char smraw[];
+    unsigned char* sm = tc::align1024(smraw);
+    unsigned char *Sh = sm + kSh, *Sl = sm + kSl, *Vh = sm + kVh, *Vl = sm + kVl;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBar);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + kBar + 8);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kBar + 12);
     const bf16* w_hi = reinterpret_cast<const bf16*>(w);
     const bf16* w_lo = w_hi + dm.T * dm.H * D;
-    const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VS2, hk = h / dm.grp;
-    const int warp = threadIdx.x >> 5;
-    const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 32;  // this warp's S tile (32 x 32)
-    const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 32;  // this warp's V' tile (16 x 32)
+    const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * 64, hk = h / dm.grp;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3, ch = warp >> 2;
+    const int d = 32 * qd + lane;  // this thread's key lane; its value lanes are e0 + 32 ch .. + 31
     const int c0 = dm.seq_c0[seq], c1 = dm.seq_c0[seq + 1];
-    if (c0 < c1) f2_issue(stage[0], dm, w_hi, w_lo, k, u, g, c0, h, hk, e0);
-    float S[2][4][4];
-    acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) {
-        x = h0 ? h0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
-    });
-    acc_pairs<32, 32>(sm0, sn0, [&](int d, int e, int i, int j, int hh) {
-        put_split2(sh, sl, d * P64 + e, S[i][j][2 * hh], S[i][j][2 * hh + 1]);
-    });
+    if (c0 < c1) f2_issue(sm, dm, w_hi, w_lo, k, u, g, c0, h, hk, e0);
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (warp == 0) {
+        tmem_alloc(tslot, 128);
+        tmem_relinquish();
+    }
+    float S[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        S[i] = h0 ? h0[(((int64_t)seq * dm.H + h) * D + e0 + 32 * ch + i) * D + d] : 0.0f;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = *tslot;
+    const uint32_t tq = tm + ((uint32_t)(32 * qd) << 16) + (uint32_t)(32 * ch);
+    constexpr uint32_t id_b = make_idesc_bf16(128, 64, 0, 1);   // B MN-major
+    constexpr uint32_t id_ab = make_idesc_bf16(128, 64, 1, 1);  // A, B MN-major
     const Pair Sp = pair_of(S_all, (int64_t)dm.n_chunks * dm.H * D * D);
     const Pair Vpp = pair_of(Vp, dm.T * dm.H * D);
+    uint32_t phase = 0;
     for (int c = c0; c < c1; ++c) {
-        F2Stage& st = stage[(c - c0) & 1];
+        unsigned char* st = sm + ((c - c0) & 1) * kStage;
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
-        const int64_t sb = ((int64_t)c * dm.H + h) * D * D;
-        acc_pairs<32, 32>(sm0, sn0, [&](int d, int e, int i, int j, int hh) {
-            put_split2(Sp.hi, Sp.lo, sb + d * D + e0 + e, S[i][j][2 * hh], S[i][j][2 * hh + 1]);
-        });
+        // the state entering chunk c: its tiles, and S_all[c]
+        tc::put_row32(Sh, Sl, 128, d, 32 * ch, S);
+        tc::put_global32(Sp.hi, Sp.lo, ((int64_t)c * dm.H + h) * D * D + d * D + e0 + 32 * ch, S);
         cp_async_wait_all();
-        __syncthreads();  // stage c landed; S split written; every warp is past chunk c-1's products
-        if (c + 1 < c1) f2_issue(stage[(c + 1 - c0) & 1], dm, w_hi, w_lo, k, u, g, c + 1, h, hk, e0);
-        const float gl = st.gs[n - 1];
-        {
-            float acc[1][4][4];
-            acc_zero<16, 32>(acc);
-            mma_split_ab<16, 32, 128, false, true>(acc, st.wh, st.wl, kP128, sh, sl, P64, vm0, vn0);
-            acc_pairs<16, 32>(vm0, vn0, [&](int i, int e, int a, int b, int hh) {
-                const float v0 = st.us[i * U68 + e] - acc[a][b][2 * hh];
-                const float v1 = st.us[i * U68 + e + 1] - acc[a][b][2 * hh + 1];
-                const float sc = i < n ? gexp(gl - st.gs[i]) : 0.0f;
-                if (i < n) put_split2(Vpp.hi, Vpp.lo, ((tok0 + i) * dm.H + h) * D + e0 + e, v0, v1);
-                put_split2(vh, vl, i * P64 + e, v0 * sc, v1 * sc);
-            });
+        tc::fence_proxy_async();
+        tc_fence_before();
+        __syncthreads();  // chunk c's stage landed; the S tiles written; chunk c-1's products are done
+        tc_fence_after();
+        if (*abort_flag) break;
+        if (c + 1 < c1) f2_issue(sm + ((c + 1 - c0) & 1) * kStage, dm, w_hi, w_lo, k, u, g, c + 1, h, hk, e0);
+        const uint32_t swh = smem_u32(st + kWh), swl = smem_u32(st + kWl), sk = smem_u32(st + kK);
+        const uint32_t ssh = smem_u32(Sh), ssl = smem_u32(Sl), svh = smem_u32(Vh), svl = smem_u32(Vl);
+        if (threadIdx.x == 0) {
+            // W' = w S: hi hi, lo hi, hi lo
+            for (int kk = 0; kk < 8; ++kk)
+                umma_f16(tm, tc::kdesc(swh, 64, 0, kk), tc::mdesc(ssh, 128, 0, kk), id_b, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 8; ++kk) umma_f16(tm, tc::kdesc(swl, 64, 0, kk), tc::mdesc(ssh, 128, 0, kk), id_b, 1u);
+            for (int kk = 0; kk < 8; ++kk) umma_f16(tm, tc::kdesc(swh, 64, 0, kk), tc::mdesc(ssl, 128, 0, kk), id_b, 1u);
+            umma_commit(bar);
         }
+        bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar, phase, abort_flag));
+        phase ^= 1u;
+        tc_fence_after();
+        const float* gs = reinterpret_cast<const float*>(st + kG);
+        const float gl = gs[n - 1];
+        if (ok && qd < 2) {
+            // V' = u - w S for token i = d (lanes 0 .. 63 hold the chunk's rows), value lanes 32 ch ..
+            const int i = d;
+            float x[32];
+            tc::tmem_row32(tq, x);
+            const float* ur = reinterpret_cast<const float*>(st + kU) + i * kUP + 32 * ch;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                const float4 u4 = *reinterpret_cast<const float4*>(ur + 4 * j);
+                x[4 * j] = u4.x - x[4 * j];
+                x[4 * j + 1] = u4.y - x[4 * j + 1];
+                x[4 * j + 2] = u4.z - x[4 * j + 2];
+                x[4 * j + 3] = u4.w - x[4 * j + 3];
+            }
+            if (i < n) tc::put_global32(Vpp.hi, Vpp.lo, ((tok0 + i) * dm.H + h) * D + e0 + 32 * ch, x);
+            const float sc = i < n ? gexp(gl - gs[i]) : 0.0f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[j] *= sc;
+            tc::put_row32(Vh, Vl, 64, i, 32 * ch, x);
+        }
+        tc::fence_proxy_async();
+        tc_fence_before();
         __syncthreads();
-        const float el = gexp(gl);
+        tc_fence_after();
+        if (threadIdx.x == 0 && !*abort_flag) {
+            // k^T V'' (V'': hi, lo)
+            for (int kk = 0; kk < 4; ++kk)
+                umma_f16(tm + 64, tc::mdesc(sk, 64, 0, kk), tc::mdesc(svh, 64, 0, kk), id_ab, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) umma_f16(tm + 64, tc::mdesc(sk, 64, 0, kk), tc::mdesc(svl, 64, 0, kk), id_ab, 1u);
+            umma_commit(bar);
+        }
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar, phase, abort_flag));
+        phase ^= 1u;
+        tc_fence_after();
+        if (ok) {
+            const float el = gexp(gl);
+            float p[32];
+            tc::tmem_row32(tq + 64, p);
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
-#pragma unroll
-            for (int b = 0; b < 4; ++b)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) S[a][b][e] *= el;
-        mma_split_b<32, 32, 64, true, true>(S, st.ks, kP128, vh, vl, P64, sm0, sn0);
-        // the next chunk's S operand (sh/sl were last read before the sync above)
-        acc_pairs<32, 32>(sm0, sn0, [&](int d, int e, int i, int j, int hh) {
-            put_split2(sh, sl, d * P64 + e, S[i][j][2 * hh], S[i][j][2 * hh + 1]);
-        });
+            for (int j = 0; j < 32; ++j) S[j] = el * S[j] + p[j];
+        }
     }
     if (ht)
-        acc_for<32, 32>(S, sm0, sn0, [&](int d, int e, float& x) {
-            ht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] = x;
-        });
+#pragma unroll
+        for (int i = 0; i < 32; ++i) ht[(((int64_t)seq * dm.H + h) * D + e0 + 32 * ch + i) * D + d] = S[i];
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, 128);
 }
 
-// F3: per (chunk, value head): P and the output rows.
+// F3: per (chunk, value head): P and the output rows, on tcgen05. [q; k] k^T (M = 128, one [128][128] tile
+// of q over k) gives q k^T in its first 64 rows; the output is formed transposed, value lanes as M:
+// o^T = scale (S^T q^T e^g + V'^T P^T), the two products in separate TMEM blocks because only the first is
+// scaled per token. S, V' and P enter as bf16 (hi, lo) tiles: two passes for S^T q^T, three for V'^T P^T.
+// TMEM: q k^T at column 0, S^T q^T at 64, V'^T P^T at 128.
+namespace f3 {
+constexpr int kQK = 0;
+constexpr int kSh = kQK + tc::kBlockTile;
+constexpr int kSl = kSh + tc::kBlockTile;
+constexpr int kVh = kSl + tc::kBlockTile;
+constexpr int kVl = kVh + tc::kRowTile;
+constexpr int kPh = kVl + tc::kRowTile;
+constexpr int kPl = kPh + tc::kSqTile;
+constexpr int kG = kPl + tc::kSqTile;
+constexpr int kBar = kG + L * 4;
+constexpr int kUsed = kBar + 16;
+}  // namespace f3
+
 __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                    const float* __restrict__ g, const float* __restrict__ S_all,
                                                    const float* __restrict__ Vp, float* __restrict__ P_all,
                                                    bf16* __restrict__ o) {
-    extern __shared__ __align__(16) unsigned char smraw[];
-    bf16* qs = reinterpret_cast<bf16*>(smraw);   // [64][136]
-    bf16* ks = qs + L * kP128;                   // [64][136]
-    bf16* vh = ks + L * kP128;                   // V' hi/lo [64][136]
-    bf16* vl = vh + L * kP128;
-    bf16* sh = vl + L * kP128;                   // S hi/lo [128][136]
-    bf16* sl = sh + D * kP128;
-    bf16* ph = sl + D * kP128;                   // P hi/lo [64][72]
-    bf16* pl = ph + L * kP64;
-    float* gs = reinterpret_cast<float*>(pl + L * kP64);
+    using namespace f3;
+    extern __shared__ unsigned char smraw[];
+    unsigned char* sm = tc::align1024(smraw);
+    unsigned char *QK = sm + kQK, *Sh = sm + kSh, *Sl = sm + kSl, *Vh = sm + kVh, *Vl = sm + kVl, *Ph = sm + kPh,
+                  *Pl = sm + kPl;
+    float* gs = reinterpret_cast<float*>(sm + kG);
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBar);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
     const int c = blockIdx.x, h = blockIdx.y, hk = h / dm.grp;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
-    const int warp = threadIdx.x >> 5;
-    async_rows(qs, q, tok0, n, dm.Hg, hk);
-    async_rows(ks, k, tok0, n, dm.Hg, hk);
-    async_rows_pair(vh, vl, pair_of(Vp, dm.T * dm.H * D), tok0, n, dm.H, h);
-    async_block_pair(sh, sl, pair_of(S_all, (int64_t)dm.n_chunks * dm.H * D * D), (int64_t)c * dm.H + h);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t nb = (int64_t)dm.n_chunks * dm.H * D * D, nt = dm.T * dm.H * D;
+    const int64_t blk = (int64_t)c * dm.H + h;
+    const Pair Sp = pair_of(S_all, nb), Vpp = pair_of(Vp, nt);
+    tc::stage_rows(QK, q, tok0, n, dm.Hg, hk, 128, 0);
+    tc::stage_rows(QK, k, tok0, n, dm.Hg, hk, 128, 64);
     async_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
     cp_async_commit();
-    cp_async_wait_all();
-    __syncthreads();
-    {
-        float acc[1][4][4];
-        acc_zero<16, 32>(acc);
-        const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
-        warp_mma<16, 32, 128, false, false>(acc, qs, kP128, ks, kP128, m0, n0);
-        // P is kept as a bf16 (hi, lo) pair in the bytes of an f32 [chunks, H, 64, 64] buffer
-        bf16* P_hi = reinterpret_cast<bf16*>(P_all);
-        bf16* P_lo = P_hi + (int64_t)dm.n_chunks * dm.H * L * L;
-        const int64_t pbase = ((int64_t)c * dm.H + h) * L * L;
-        acc_pairs<16, 32>(m0, n0, [&](int r, int l, int i, int j, int hh) {
-            const float p0 = (l <= r && r < n) ? acc[i][j][2 * hh] * gexp(gs[r] - gs[l]) : 0.0f;
-            const float p1 = (l + 1 <= r && r < n) ? acc[i][j][2 * hh + 1] * gexp(gs[r] - gs[l + 1]) : 0.0f;
-            put_split2(P_hi, P_lo, pbase + r * L + l, p0, p1);
-            put_split2(ph, pl, r * kP64 + l, p0, p1);
-        });
+    tc::stage_block(Sh, Sp.hi + blk * D * D);
+    tc::stage_block(Sl, Sp.lo + blk * D * D);
+    tc::stage_rows(Vh, Vpp.hi, tok0, n, dm.H, h);
+    tc::stage_rows(Vl, Vpp.lo, tok0, n, dm.H, h);
+    cp_async_commit();
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
     }
+    __syncwarp();
+    if (warp == 0) {
+        tmem_alloc(tslot, 256);
+        tmem_relinquish();
+    }
+    cp_async_wait_but_one();
+    tc::fence_proxy_async();
+    tc_fence_before();
     __syncthreads();
-    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
-    float qsacc[1][8][4], pvacc[1][8][4];
-    acc_zero<16, 64>(qsacc);
-    acc_zero<16, 64>(pvacc);
-    mma_split_b<16, 64, 128, false, true>(qsacc, qs, kP128, sh, sl, kP128, m0, n0);
-    mma_split_ab<16, 64, 64, false, true>(pvacc, ph, pl, kP64, vh, vl, kP128, m0, n0);
-    const int lane = threadIdx.x & 31, gq = lane >> 2;
-    const float eg0 = gexp(gs[m0 + gq]), eg1 = gexp(gs[m0 + gq + 8]);
-    acc_pairs<16, 64>(m0, n0, [&](int r, int e, int i, int j, int hh) {  // two columns a 4-byte store
-        const float eg = hh ? eg1 : eg0;
-        const float y0 = dm.scale * (qsacc[i][j][2 * hh] * eg + pvacc[i][j][2 * hh]);
-        const float y1 = dm.scale * (qsacc[i][j][2 * hh + 1] * eg + pvacc[i][j][2 * hh + 1]);
-        if (r < n)
-            *reinterpret_cast<__nv_bfloat162*>(o + ((tok0 + r) * dm.H + h) * D + e) = __floats2bfloat162_rn(y0, y1);
-    });
+    tc_fence_after();
+    const uint32_t tm = *tslot;
+    constexpr uint32_t id = make_idesc_bf16(128, 64, 0, 0);
+    constexpr uint32_t id_m = make_idesc_bf16(128, 64, 1, 0);
+    const uint32_t sQK = smem_u32(QK), sSh = smem_u32(Sh), sSl = smem_u32(Sl), sVh = smem_u32(Vh),
+                   sVl = smem_u32(Vl), sPh = smem_u32(Ph), sPl = smem_u32(Pl);
+    if (threadIdx.x == 0) {
+        for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tm, tc::kdesc(sQK, 128, 0, kk), tc::kdesc(sQK, 128, 64, kk), id, kk > 0 ? 1u : 0u);
+        umma_commit(bar);
+    }
+    bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar, 0, nullptr));
+    tc_fence_after();
+    const int qd = warp & 3, ch = warp >> 2;
+    const uint32_t tq = tm + ((uint32_t)(32 * qd) << 16) + (uint32_t)(32 * ch);
+    if (ok && qd < 2) {
+        // P = causal(q k^T e^{g_r - g_l}), kept as a bf16 (hi, lo) pair in the bytes of an f32
+        // [chunks, H, 64, 64] buffer, and as the tiles the P V' product reads
+        const int r = 32 * qd + lane;
+        float p[32];
+        tc::tmem_row32(tq, p);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int l = 32 * ch + i;
+            p[i] = (l <= r && r < n) ? p[i] * gexp(gs[r] - gs[l]) : 0.0f;
+        }
+        tc::put_row32(Ph, Pl, 64, r, 32 * ch, p);
+        const Pair Pp = pair_of(P_all, (int64_t)dm.n_chunks * dm.H * L * L);
+        tc::put_global32(Pp.hi, Pp.lo, blk * L * L + r * L + 32 * ch, p);
+    }
+    cp_async_wait_all();
+    tc::fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0 && ok) {
+        // S^T q^T (S: hi, lo) ; V'^T P^T (hi hi, lo hi, hi lo)
+        for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tm + 64, tc::mdesc(sSh, 128, 0, kk), tc::kdesc(sQK, 128, 0, kk), id_m, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) umma_f16(tm + 64, tc::mdesc(sSl, 128, 0, kk), tc::kdesc(sQK, 128, 0, kk), id_m, 1u);
+        for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tm + 128, tc::mdesc(sVh, 64, 0, kk), tc::kdesc(sPh, 64, 0, kk), id_m, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 4; ++kk) umma_f16(tm + 128, tc::mdesc(sVl, 64, 0, kk), tc::kdesc(sPh, 64, 0, kk), id_m, 1u);
+        for (int kk = 0; kk < 4; ++kk) umma_f16(tm + 128, tc::mdesc(sVh, 64, 0, kk), tc::kdesc(sPl, 64, 0, kk), id_m, 1u);
+        umma_commit(bar);
+    }
+    ok = __all_sync(0xFFFFFFFFu, ok && mbar_wait(bar, 1, nullptr));
+    tc_fence_after();
+    if (ok) {
+        // o = scale (e^g q S + P V'): value lane e = 32 (warp % 4) + lane, tokens 32 (warp / 4) ..
+        const int e = 32 * qd + lane;
+        float a[32], b[32];
+        tc::tmem_row32(tq + 64, a);
+        tc::tmem_row32(tq + 128, b);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int r = 32 * ch + i;
+            if (r < n) o[((tok0 + r) * dm.H + h) * D + e] = __float2bfloat16_rn(dm.scale * (a[i] * gexp(gs[r]) + b[i]));
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, 256);
 }
 
 // ============================================================================================ backward
 
-// B1: per (sequence, value head, 64 value lanes): the reverse state pass; dS lives in the accumulators.
-// Each chunk's operands stream in with cp.async: the ones read late in a chunk (w as a bf16 hi/lo pair, q)
-// are double-buffered and fetched a whole chunk ahead; the ones only the dV' products read (P as a pair,
-// k, the dO slice, g) have one buffer, refilled for the next chunk as soon as those products are done.
-constexpr int VSB = 64;  // value lanes per backward-state CTA
+// B1: per (sequence, value head, 64 value lanes): the reverse state pass, on tcgen05. dS[128 key lanes]
+// [64 value lanes] stays in registers in the accumulator's TMEM layout (as F2's S), and each chunk takes
+// two rounds of products: dV' = scale P^T dO + e^{gL - g} (k dS) (M = the chunk's 64 tokens, the upper half
+// of the 128-row MMA unused; P and dS as bf16 (hi, lo) tiles, two passes each); then q^T (e^g dO) and
+// w^T dV' (M = the 128 key lanes; two and three passes), which update dS = e^{gL} dS + scale q^T (e^g dO)
+// - w^T dV'. The operands read late in a chunk (w as a pair, q) are double-buffered and fetched a whole
+// chunk ahead; the ones the dV' products read (P as a pair, k, the dO slice, g) have one buffer, refilled
+// for the next chunk as soon as those products are done. TMEM: P^T dO 0, k dS 64, q^T (e^g dO) 128,
+// w^T dV' 192.
+namespace b1 {
+constexpr int kLateWh = 0;                        // a late stage: w hi/lo, q [64][128]
+constexpr int kLateWl = kLateWh + tc::kRowTile;
+constexpr int kLateQ = kLateWl + tc::kRowTile;
+constexpr int kLate = kLateQ + tc::kRowTile;
+constexpr int kEarly = 2 * kLate;                 // P hi/lo [64][64], k [64][128], dO slice [64][64], g
+constexpr int kPh = kEarly;
+constexpr int kPl = kPh + tc::kSqTile;
+constexpr int kK = kPl + tc::kSqTile;
+constexpr int kDO = kK + tc::kRowTile;
+constexpr int kG = kDO + tc::kSqTile;
+constexpr int kDSh = (kG + L * 4 + 1023) & ~1023; // dS hi/lo [128][64]
+constexpr int kDSl = kDSh + 128 * 64 * 2;
+constexpr int kEGh = kDSl + 128 * 64 * 2;         // e^g dO hi/lo [64][64]
+constexpr int kEGl = kEGh + tc::kSqTile;
+constexpr int kDVh = kEGl + tc::kSqTile;          // dV' hi/lo [64][64]
+constexpr int kDVl = kDVh + tc::kSqTile;
+constexpr int kBar = kDVl + tc::kSqTile;          // mbarrier, abort flag, TMEM slot
+constexpr int kUsed = kBar + 16;
+}  // namespace b1
 
-struct B1Late {
-    bf16 wh[L * kP128], wl[L * kP128], qs[L * kP128];
-};
-struct B1Early {
-    bf16 ph[L * kP64], pl[L * kP64];
-    bf16 ks[L * kP128];
-    bf16 dos[L * kP64];
-    float gs[L];
-};
-
-__device__ __forceinline__ void b1_issue_late(B1Late& st, const Dims& dm, const bf16* q, const bf16* w_hi,
+__device__ __forceinline__ void b1_issue_late(unsigned char* st, const Dims& dm, const bf16* q, const bf16* w_hi,
                                               const bf16* w_lo, int c, int h, int hk) {
+    using namespace b1;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
-    for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
-        const int i = idx >> 4, x = (idx & 15) * 8;
-        const bool on = i < n;
-        const int64_t row = on ? tok0 + i : tok0;
-        cp_async16(&st.wh[i * kP128 + x], w_hi + (row * dm.H + h) * D + x, on);
-        cp_async16(&st.wl[i * kP128 + x], w_lo + (row * dm.H + h) * D + x, on);
-        cp_async16(&st.qs[i * kP128 + x], q + (row * dm.Hg + hk) * D + x, on);
-    }
+    tc::stage_rows(st + kLateWh, w_hi, tok0, n, dm.H, h);
+    tc::stage_rows(st + kLateWl, w_lo, tok0, n, dm.H, h);
+    tc::stage_rows(st + kLateQ, q, tok0, n, dm.Hg, hk);
     cp_async_commit();
 }
 
-__device__ __forceinline__ void b1_issue_early(B1Early& st, const Dims& dm, const bf16* k, const bf16* P_hi,
+__device__ __forceinline__ void b1_issue_early(unsigned char* sm, const Dims& dm, const bf16* k, const bf16* P_hi,
                                                const bf16* P_lo, const bf16* dO, const float* g, int c, int h,
                                                int hk, int e0) {
+    using namespace b1;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
     const int64_t pbase = ((int64_t)c * dm.H + h) * L * L;
-    for (int idx = threadIdx.x; idx < L * 16; idx += blockDim.x) {
-        const int i = idx >> 4, x = (idx & 15) * 8;
+    tc::stage_rows(sm + kK, k, tok0, n, dm.Hg, hk);
+    for (int idx = threadIdx.x; idx < L * 8; idx += blockDim.x) {
+        const int i = idx >> 3, j = idx & 7;
         const bool on = i < n;
-        const int64_t row = on ? tok0 + i : tok0;
-        cp_async16(&st.ks[i * kP128 + x], k + (row * dm.Hg + hk) * D + x, on);
-        if (x < L) {
-            cp_async16(&st.ph[i * kP64 + x], P_hi + pbase + i * L + x, true);
-            cp_async16(&st.pl[i * kP64 + x], P_lo + pbase + i * L + x, true);
-            cp_async16(&st.dos[i * kP64 + x], dO + (row * dm.H + h) * D + e0 + x, on);
-        }
+        const uint32_t o = tc::chunk_off(64, i, j);
+        cp_async16(sm + kPh + o, P_hi + pbase + i * L + j * 8, true);
+        cp_async16(sm + kPl + o, P_lo + pbase + i * L + j * 8, true);
+        cp_async16(sm + kDO + o, dO + ((on ? tok0 + i : tok0) * dm.H + h) * D + e0 + j * 8, on);
     }
-    for (int i = threadIdx.x; i < L; i += blockDim.x) {
-        const bool on = i < n;
-        cp_async4(&st.gs[i], g + ((on ? tok0 + i : tok0) * dm.H + h), on);
-    }
+    async_gb(reinterpret_cast<float*>(sm + kG), nullptr, g, nullptr, tok0, n, dm.H, h);
     cp_async_commit();
 }
 
@@ -585,209 +778,319 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
                                                      const float* __restrict__ P_all, const bf16* __restrict__ dO,
                                                      const float* __restrict__ dht, float* __restrict__ dS_all,
                                                      float* __restrict__ dVp, float* __restrict__ dh0) {
-    extern __shared__ __align__(16) unsigned char smraw[];
-    B1Late* late = reinterpret_cast<B1Late*>(smraw);                          // [2]
-    B1Early* early = reinterpret_cast<B1Early*>(smraw + 2 * sizeof(B1Late));  // [1]
-    bf16* dsh = reinterpret_cast<bf16*>(smraw + 2 * sizeof(B1Late) + sizeof(B1Early));  // dS hi/lo [128][72]
-    bf16* dsl = dsh + D * kP64;
-    bf16* egh = dsl + D * kP64;  // e^g dO hi/lo [64][72]
-    bf16* egl = egh + L * kP64;
-    bf16* dvh = egl + L * kP64;  // dV' hi/lo [64][72]
-    bf16* dvl = dvh + L * kP64;
+    using namespace b1;
+    extern __shared__ unsigned char smraw[];
+    unsigned char* sm = tc::align1024(smraw);
+    unsigned char *DSh = sm + kDSh, *DSl = sm + kDSl, *EGh = sm + kEGh, *EGl = sm + kEGl, *DVh = sm + kDVh,
+                  *DVl = sm + kDVl;
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBar);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + kBar + 8);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kBar + 12);
     const bf16* w_hi = reinterpret_cast<const bf16*>(w);
     const bf16* w_lo = w_hi + dm.T * dm.H * D;
     const bf16* P_hi = reinterpret_cast<const bf16*>(P_all);
     const bf16* P_lo = P_hi + (int64_t)dm.n_chunks * dm.H * L * L;
-    const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * VSB, hk = h / dm.grp;
-    const int warp = threadIdx.x >> 5;
-    const int sm0 = (warp & 3) * 32, sn0 = (warp >> 2) * 32;  // this warp's dS tile (32 x 32)
-    const int vm0 = (warp & 3) * 16, vn0 = (warp >> 2) * 32;  // this warp's dV' tile (16 x 32)
+    const int seq = blockIdx.x, h = blockIdx.y, e0 = blockIdx.z * 64, hk = h / dm.grp;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, qd = warp & 3, ch = warp >> 2;
+    const int d = 32 * qd + lane;  // this thread's key lane; its value lanes are e0 + 32 ch .. + 31
     const Pair dSp = pair_of(dS_all, (int64_t)dm.n_chunks * dm.H * D * D);
     const Pair dVpp = pair_of(dVp, dm.T * dm.H * D);
     const int c0 = dm.seq_c0[seq], c1 = dm.seq_c0[seq + 1];
     if (c0 < c1) {
-        b1_issue_late(late[0], dm, q, w_hi, w_lo, c1 - 1, h, hk);
-        b1_issue_early(*early, dm, k, P_hi, P_lo, dO, g, c1 - 1, h, hk, e0);
+        b1_issue_late(sm, dm, q, w_hi, w_lo, c1 - 1, h, hk);
+        b1_issue_early(sm, dm, k, P_hi, P_lo, dO, g, c1 - 1, h, hk, e0);
     }
-    float dS[2][4][4];
-    acc_for<32, 32>(dS, sm0, sn0, [&](int d, int e, float& x) {
-        x = dht ? dht[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] : 0.0f;
-    });
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (warp == 0) {
+        tmem_alloc(tslot, 256);
+        tmem_relinquish();
+    }
+    float dS[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+        dS[i] = dht ? dht[(((int64_t)seq * dm.H + h) * D + e0 + 32 * ch + i) * D + d] : 0.0f;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tm = *tslot;
+    const uint32_t tq = tm + ((uint32_t)(32 * qd) << 16) + (uint32_t)(32 * ch);
+    constexpr uint32_t id_b = make_idesc_bf16(128, 64, 0, 1);   // B MN-major
+    constexpr uint32_t id_ab = make_idesc_bf16(128, 64, 1, 1);  // A, B MN-major
+    const uint32_t sph = smem_u32(sm + kPh), spl = smem_u32(sm + kPl), sk = smem_u32(sm + kK),
+                   sdo = smem_u32(sm + kDO), sdsh = smem_u32(DSh), sdsl = smem_u32(DSl), segh = smem_u32(EGh),
+                   segl = smem_u32(EGl), sdvh = smem_u32(DVh), sdvl = smem_u32(DVl);
+    const float* gs = reinterpret_cast<const float*>(sm + kG);
+    uint32_t phase = 0;
     for (int c = c1 - 1; c >= c0; --c) {
-        B1Late& lt = late[(c1 - 1 - c) & 1];
-        B1Early& et = *early;
+        unsigned char* lt = sm + ((c1 - 1 - c) & 1) * kLate;
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
-        const int64_t sb = ((int64_t)c * dm.H + h) * D * D;
-        // dsh/dsl were last read by the previous chunk's dV' products, before its middle barrier
-        acc_pairs<32, 32>(sm0, sn0, [&](int d, int e, int i, int j, int hh) {
-            const float x0 = dS[i][j][2 * hh], x1 = dS[i][j][2 * hh + 1];
-            put_split2(dSp.hi, dSp.lo, sb + d * D + e0 + e, x0, x1);
-            put_split2(dsh, dsl, d * kP64 + e, x0, x1);
-        });
+        // dS entering (from the right) chunk c: its tiles, and dS_all[c]
+        tc::put_row32(DSh, DSl, 128, d, 32 * ch, dS);
+        tc::put_global32(dSp.hi, dSp.lo, ((int64_t)c * dm.H + h) * D * D + d * D + e0 + 32 * ch, dS);
         cp_async_wait_all();
-        __syncthreads();  // chunk c's operands landed; dS split written; chunk c+1's products are done
-        if (c > c0) b1_issue_late(late[(c1 - c) & 1], dm, q, w_hi, w_lo, c - 1, h, hk);
-        const float gl = et.gs[n - 1];
-        for (int idx = threadIdx.x; idx < L * VSB / 2; idx += blockDim.x) {
-            const int i = idx >> 5, e = (idx & 31) * 2;
-            const float eg = gexp(et.gs[i]);
-            const float2 d2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(et.dos + i * kP64 + e));
-            put_split2(egh, egl, i * kP64 + e, d2.x * eg, d2.y * eg);
+        tc::fence_proxy_async();
+        tc_fence_before();
+        __syncthreads();  // chunk c's operands landed; the dS tiles written; chunk c+1's products are done
+        tc_fence_after();
+        if (*abort_flag) break;
+        if (c > c0) b1_issue_late(sm + ((c1 - c) & 1) * kLate, dm, q, w_hi, w_lo, c - 1, h, hk);
+        if (threadIdx.x == 0) {
+            // P^T dO (P: hi, lo) ; k dS (dS: hi, lo)
+            for (int kk = 0; kk < 4; ++kk)
+                umma_f16(tm, tc::mdesc(sph, 64, 0, kk), tc::mdesc(sdo, 64, 0, kk), id_ab, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) umma_f16(tm, tc::mdesc(spl, 64, 0, kk), tc::mdesc(sdo, 64, 0, kk), id_ab, 1u);
+            for (int kk = 0; kk < 8; ++kk)
+                umma_f16(tm + 64, tc::kdesc(sk, 64, 0, kk), tc::mdesc(sdsh, 128, 0, kk), id_b, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 8; ++kk) umma_f16(tm + 64, tc::kdesc(sk, 64, 0, kk), tc::mdesc(sdsl, 128, 0, kk), id_b, 1u);
+            umma_commit(bar);
         }
-        {
-            // dV' = scale P^T dO + e^{gL - g} (k dS)
-            float a1[1][4][4], a2[1][4][4];
-            acc_zero<16, 32>(a1);
-            acc_zero<16, 32>(a2);
-            mma_split_a<16, 32, 64, true, true>(a1, et.ph, et.pl, kP64, et.dos, kP64, vm0, vn0);
-            mma_split_b<16, 32, 128, false, true>(a2, et.ks, kP128, dsh, dsl, kP64, vm0, vn0);
-            const int ja = vm0 + ((threadIdx.x & 31) >> 2), jb = ja + 8;  // this lane's two rows
-            const float sca = ja < n ? gexp(gl - et.gs[ja]) : 0.0f, scb = jb < n ? gexp(gl - et.gs[jb]) : 0.0f;
-            acc_pairs<16, 32>(vm0, vn0, [&](int j, int e, int a, int b, int hh) {
-                const float sc = hh ? scb : sca;
-                const float d0 = j < n ? dm.scale * a1[a][b][2 * hh] + sc * a2[a][b][2 * hh] : 0.0f;
-                const float d1 = j < n ? dm.scale * a1[a][b][2 * hh + 1] + sc * a2[a][b][2 * hh + 1] : 0.0f;
-                if (j < n) put_split2(dVpp.hi, dVpp.lo, ((tok0 + j) * dm.H + h) * D + e0 + e, d0, d1);
-                put_split2(dvh, dvl, j * kP64 + e, d0, d1);
-            });
+        const float gl = gs[n - 1];
+        // e^g dO as (hi, lo) tiles for the dS products, while the dV' products run
+        for (int idx = threadIdx.x; idx < L * 8; idx += blockDim.x) {
+            const int i = idx >> 3, j = idx & 7;
+            const float eg = gexp(gs[i]);
+            const uint32_t o = tc::chunk_off(64, i, j);
+            const uint4 raw = *reinterpret_cast<const uint4*>(sm + kDO + o);
+            const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+            uint32_t hw[4], lw[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(x2[e]);
+                const float a = f.x * eg, b = f.y * eg;
+                const __nv_bfloat162 hh = __floats2bfloat162_rn(a, b);
+                const float2 hf = __bfloat1622float2(hh);
+                const __nv_bfloat162 ll = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+                hw[e] = *reinterpret_cast<const uint32_t*>(&hh);
+                lw[e] = *reinterpret_cast<const uint32_t*>(&ll);
+            }
+            *reinterpret_cast<uint4*>(EGh + o) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            *reinterpret_cast<uint4*>(EGl + o) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
-        __syncthreads();  // dV' written; chunk c's P, k, dO and g are no longer read
-        if (c > c0) b1_issue_early(*early, dm, k, P_hi, P_lo, dO, g, c - 1, h, hk, e0);
-        // dS = e^{gL} dS + scale q^T (e^g dO) - w^T dV'
-        const float el = gexp(gl);
-        float t1[2][4][4], t2[2][4][4];
-        acc_zero<32, 32>(t1);
-        acc_zero<32, 32>(t2);
-        mma_split_b<32, 32, 64, true, true>(t1, lt.qs, kP128, egh, egl, kP64, sm0, sn0);
-        mma_split_ab<32, 32, 64, true, true>(t2, lt.wh, lt.wl, kP128, dvh, dvl, kP64, sm0, sn0);
+        bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar, phase, abort_flag));
+        phase ^= 1u;
+        tc_fence_after();
+        if (ok && qd < 2) {
+            // dV' = scale P^T dO + e^{gL - g} (k dS) for token j = d, value lanes 32 ch ..
+            const int j = d;
+            float a1[32], a2[32];
+            tc::tmem_row32(tq, a1);
+            tc::tmem_row32(tq + 64, a2);
+            const float sc = j < n ? gexp(gl - gs[j]) : 0.0f;
 #pragma unroll
-        for (int a = 0; a < 2; ++a)
+            for (int e = 0; e < 32; ++e) a1[e] = j < n ? dm.scale * a1[e] + sc * a2[e] : 0.0f;
+            if (j < n) tc::put_global32(dVpp.hi, dVpp.lo, ((tok0 + j) * dm.H + h) * D + e0 + 32 * ch, a1);
+            tc::put_row32(DVh, DVl, 64, j, 32 * ch, a1);
+        }
+        tc::fence_proxy_async();
+        tc_fence_before();
+        __syncthreads();  // dV' and e^g dO written; chunk c's P, k, dO and g are no longer read
+        tc_fence_after();
+        if (threadIdx.x == 0 && !*abort_flag) {
+            // q^T (e^g dO) (hi, lo) ; w^T dV' (hi hi, lo hi, hi lo)
+            const uint32_t sq = smem_u32(lt + kLateQ), swh = smem_u32(lt + kLateWh), swl = smem_u32(lt + kLateWl);
+            for (int kk = 0; kk < 4; ++kk)
+                umma_f16(tm + 128, tc::mdesc(sq, 64, 0, kk), tc::mdesc(segh, 64, 0, kk), id_ab, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) umma_f16(tm + 128, tc::mdesc(sq, 64, 0, kk), tc::mdesc(segl, 64, 0, kk), id_ab, 1u);
+            for (int kk = 0; kk < 4; ++kk)
+                umma_f16(tm + 192, tc::mdesc(swh, 64, 0, kk), tc::mdesc(sdvh, 64, 0, kk), id_ab, kk > 0 ? 1u : 0u);
+            for (int kk = 0; kk < 4; ++kk) umma_f16(tm + 192, tc::mdesc(swl, 64, 0, kk), tc::mdesc(sdvh, 64, 0, kk), id_ab, 1u);
+            for (int kk = 0; kk < 4; ++kk) umma_f16(tm + 192, tc::mdesc(swh, 64, 0, kk), tc::mdesc(sdvl, 64, 0, kk), id_ab, 1u);
+            umma_commit(bar);
+        }
+        if (c > c0) b1_issue_early(sm, dm, k, P_hi, P_lo, dO, g, c - 1, h, hk, e0);
+        ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar, phase, abort_flag));
+        phase ^= 1u;
+        tc_fence_after();
+        if (ok) {
+            const float el = gexp(gl);
+            float t1[32], t2[32];
+            tc::tmem_row32(tq + 128, t1);
+            tc::tmem_row32(tq + 192, t2);
 #pragma unroll
-            for (int b = 0; b < 4; ++b)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) dS[a][b][e] = el * dS[a][b][e] + dm.scale * t1[a][b][e] - t2[a][b][e];
+            for (int e = 0; e < 32; ++e) dS[e] = el * dS[e] + dm.scale * t1[e] - t2[e];
+        }
     }
     if (dh0)
-        acc_for<32, 32>(dS, sm0, sn0, [&](int d, int e, float& x) {
-            dh0[(((int64_t)seq * dm.H + h) * D + e0 + e) * D + d] = x;
-        });
+#pragma unroll
+        for (int i = 0; i < 32; ++i) dh0[(((int64_t)seq * dm.H + h) * D + e0 + 32 * ch + i) * D + d] = dS[i];
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, 256);
 }
 
 // B2a: per (chunk, value head): the state-reading terms, written as partials of dq, dk, dg (pdq, pdk, pdg:
-// the launcher passes the outputs themselves, which B2b then adds to). Its operands arrive in three
-// cp.async groups: what dQ~ and dw read (S, dO, q, dV', g), then dS_next, then (into the tiles dQ~ and dw
-// free) V' and k.
+// the launcher passes the outputs themselves, which B2b then adds to). On tcgen05, transposed so the 128
+// key lanes are the MMA's M (every TMEM lane busy, and a token column of the accumulator stores as one
+// coalesced row): Q~^T = S dO^T, W^T = S dV'^T and K~^T = dS_next V'^T, [128 x 64] each, f32 in TMEM
+// columns 0, 64 and 128. The f32 states and V', dV' enter as their stored bf16 (hi, lo) planes, so the
+// products take two or three passes (hi hi, lo hi, hi lo), as the mma.sync forms did. Operands arrive in
+// three cp.async groups: S, dO, q, dV', g; then dS_next; then (into the tiles dO and dV' held, once the
+// first products have read them) V' and k.
+constexpr int kBaTmemCols = 256;
+
 __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict__ q, const bf16* __restrict__ k,
                                                  const float* __restrict__ g, const float* __restrict__ S_all,
                                                  const float* __restrict__ Vp, const bf16* __restrict__ dO,
                                                  const float* __restrict__ dS_all, const float* __restrict__ dVp,
                                                  float* __restrict__ dw, float* __restrict__ pdq, float* __restrict__ pdk,
                                                  float* __restrict__ pdg) {
-    extern __shared__ __align__(16) unsigned char smraw[];
-    bf16* sh = reinterpret_cast<bf16*>(smraw);   // S hi/lo [128][136]
-    bf16* sl = sh + D * kP128;
-    bf16* th = sl + D * kP128;                   // dS_next hi/lo [128][136]
-    bf16* tl = th + D * kP128;
-    bf16* xs = tl + D * kP128;                   // dO [64][136], then k
-    bf16* qs = xs + L * kP128;                   // q [64][136]
-    bf16* yh = qs + L * kP128;                   // dV' hi/lo [64][136], then V' hi/lo
-    bf16* yl = yh + L * kP128;
-    float* gs = reinterpret_cast<float*>(yl + L * kP128);
+    extern __shared__ unsigned char smraw[];
+    unsigned char* sm = tc::align1024(smraw);
+    unsigned char* Sh = sm;                              // S hi/lo [128][128]
+    unsigned char* Sl = Sh + tc::kBlockTile;
+    unsigned char* Th = Sl + tc::kBlockTile;             // dS_next hi/lo [128][128]
+    unsigned char* Tl = Th + tc::kBlockTile;
+    unsigned char* Xs = Tl + tc::kBlockTile;             // dO [64][128], then k
+    unsigned char* Yh = Xs + tc::kRowTile;               // dV' hi/lo [64][128], then V' hi/lo
+    unsigned char* Yl = Yh + tc::kRowTile;
+    unsigned char* Qs = Yl + tc::kRowTile;               // q [64][128]
+    float* gs = reinterpret_cast<float*>(Qs + tc::kRowTile);
     float* dgs = gs + L;
-    float* red = dgs + L;  // [8]
+    float* red = dgs + L;                                // [8]
+    uint64_t* bar = reinterpret_cast<uint64_t*>(red + 8);
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(bar + 1);
     const int c = blockIdx.x, h = blockIdx.y, hk = h / dm.grp;
     const int64_t tok0 = dm.tok0[c];
     const int n = dm.len[c];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 64;
     const int64_t nb = (int64_t)dm.n_chunks * dm.H * D * D, nt = dm.T * dm.H * D;
     const int64_t blk = (int64_t)c * dm.H + h;
-    async_block_pair(sh, sl, pair_of(S_all, nb), blk);
-    async_rows(xs, dO, tok0, n, dm.H, h);
-    async_rows(qs, q, tok0, n, dm.Hg, hk);
-    async_rows_pair(yh, yl, pair_of(dVp, nt), tok0, n, dm.H, h);
+    const Pair Sp = pair_of(S_all, nb), Tp = pair_of(dS_all, nb), dVpp = pair_of(dVp, nt), Vpp = pair_of(Vp, nt);
+    tc::stage_block(Sh, Sp.hi + blk * D * D);
+    tc::stage_block(Sl, Sp.lo + blk * D * D);
+    tc::stage_rows(Xs, dO, tok0, n, dm.H, h);
+    tc::stage_rows(Qs, q, tok0, n, dm.Hg, hk);
+    tc::stage_rows(Yh, dVpp.hi, tok0, n, dm.H, h);
+    tc::stage_rows(Yl, dVpp.lo, tok0, n, dm.H, h);
     async_gb(gs, nullptr, g, nullptr, tok0, n, dm.H, h);
     cp_async_commit();
-    async_block_pair(th, tl, pair_of(dS_all, nb), blk);
+    tc::stage_block(Th, Tp.hi + blk * D * D);
+    tc::stage_block(Tl, Tp.lo + blk * D * D);
     cp_async_commit();
-    for (int i = threadIdx.x; i < L; i += blockDim.x) dgs[i] = 0.0f;
+    if (threadIdx.x < L) dgs[threadIdx.x] = 0.0f;
+    if (threadIdx.x == 0) {
+        mbar_init(bar, 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    if (warp == 0) {
+        tmem_alloc(tslot, kBaTmemCols);
+        tmem_relinquish();
+    }
     cp_async_wait_but_one();
+    tc::fence_proxy_async();
+    tc_fence_before();
     __syncthreads();
-    float dq[1][8][4];
-    {
-        // dQ~ = scale dO S^T ; dq = e^g dQ~ ; dg_i += e^{g_i} q_i . dQ~_i
-        acc_zero<16, 64>(dq);
-        mma_split_b<16, 64, 128, false, false>(dq, xs, kP128, sh, sl, kP128, m0, n0);
-        float p0 = 0.0f, p1 = 0.0f;
-        const int gq = lane >> 2;  // this lane's two rows: m0 + gq and m0 + gq + 8
-        const float f0 = dm.scale * gexp(gs[m0 + gq]), f1 = dm.scale * gexp(gs[m0 + gq + 8]);
-        acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
-            float& x = dq[i][j][q];
-            x *= (q >> 1) ? f1 : f0;
-            const float t = __bfloat162float(qs[r * kP128 + d]) * x;
-            if (q >> 1) p1 += t; else p0 += t;
-        });
-        p0 = quad_sum(p0);
-        p1 = quad_sum(p1);
-        if ((lane & 3) == 0) {
-            atomicAdd(&dgs[m0 + (lane >> 2)], p0);
-            atomicAdd(&dgs[m0 + (lane >> 2) + 8], p1);
+    tc_fence_after();
+    const uint32_t tm = *tslot;
+    constexpr uint32_t idesc = make_idesc_bf16(128, 64, 0, 0);
+    if (threadIdx.x == 0) {
+        const uint32_t sh = smem_u32(Sh), sl = smem_u32(Sl), xs = smem_u32(Xs), yh = smem_u32(Yh), yl = smem_u32(Yl);
+        // Q~^T = S dO^T (S: hi, lo)
+        for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tm, tc::kdesc(sh, 128, 0, kk), tc::kdesc(xs, 64, 0, kk), idesc, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) umma_f16(tm, tc::kdesc(sl, 128, 0, kk), tc::kdesc(xs, 64, 0, kk), idesc, 1u);
+        // W^T = S dV'^T (hi hi, lo hi, hi lo)
+        for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tm + 64, tc::kdesc(sh, 128, 0, kk), tc::kdesc(yh, 64, 0, kk), idesc, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) umma_f16(tm + 64, tc::kdesc(sl, 128, 0, kk), tc::kdesc(yh, 64, 0, kk), idesc, 1u);
+        for (int kk = 0; kk < 8; ++kk) umma_f16(tm + 64, tc::kdesc(sh, 128, 0, kk), tc::kdesc(yl, 64, 0, kk), idesc, 1u);
+        umma_commit(bar);
+    }
+    bool ok = __all_sync(0xFFFFFFFFu, mbar_wait(bar, 0, nullptr));  // warp-uniform: the TMEM loads are .aligned
+    tc_fence_after();
+    // the products have read dO and dV': V' and k take their tiles
+    tc::stage_rows(Yh, Vpp.hi, tok0, n, dm.H, h);
+    tc::stage_rows(Yl, Vpp.lo, tok0, n, dm.H, h);
+    tc::stage_rows(Xs, k, tok0, n, dm.Hg, hk);
+    cp_async_commit();
+    // a warp reads its lane quarter (key lanes d = 32 (warp % 4) + lane) over token columns 32 (warp / 4) ..
+    const int d = 32 * (warp & 3) + lane, t0 = 32 * (warp >> 2);
+    const uint32_t tq = tm + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)t0;
+    if (ok) {
+        // dq = scale e^g dQ~ ; dg_i += q_i . dq_i
+        float x[32], p[32];
+        tc::tmem_row32(tq, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int r = t0 + i;
+            x[i] *= dm.scale * gexp(gs[r]);
+            p[i] = tc::ld_elem(Qs, 64, r, d) * x[i];
+            if (r < n) pdq[((tok0 + r) * dm.H + h) * D + d] = x[i];
+        }
+        atomicAdd(&dgs[t0 + lane], tc::transpose_sum(p));
+        // dw = -dV' S^T, kept as a (hi, lo) pair
+        const Pair dwp = pair_of(dw, nt);
+        tc::tmem_row32(tq + 64, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int r = t0 + i;
+            if (r < n) put_split(dwp.hi, dwp.lo, ((tok0 + r) * dm.H + h) * D + d, -x[i]);
         }
     }
-    {
-        // dw = -dV' S^T
-        const Pair dwp = pair_of(dw, nt);
-        float acc[1][8][4];
-        acc_zero<16, 64>(acc);
-        mma_split_ab<16, 64, 128, false, false>(acc, yh, yl, kP128, sh, sl, kP128, m0, n0);
-        acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {
-            if (r < n) put_split2(dwp.hi, dwp.lo, ((tok0 + r) * dm.H + h) * D + d, -acc[i][j][2 * hh], -acc[i][j][2 * hh + 1]);
-        });
-    }
-    __syncthreads();  // dO and dV' are no longer read
-    async_rows_pair(yh, yl, pair_of(Vp, nt), tok0, n, dm.H, h);
-    async_rows(xs, k, tok0, n, dm.Hg, hk);
-    cp_async_commit();
     cp_async_wait_but_one();  // dS_next landed
     __syncthreads();
-    // <S, dS_next> from the pairs, while V' and k land
-    float sdot = 0.0f;
-    for (int idx = threadIdx.x; idx < D * D / 2; idx += blockDim.x) {
-        const int r = (idx * 2) >> 7, cc = (idx * 2) & 127;
-        const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sh + r * kP128 + cc));
-        const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sl + r * kP128 + cc));
-        const float2 x = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(th + r * kP128 + cc));
-        const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(tl + r * kP128 + cc));
-        sdot += (a.x + b.x) * (x.x + y.x) + (a.y + b.y) * (x.y + y.y);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xFFFFFFFFu, sdot, o);
-    if (lane == 0) red[warp] = sdot;
-    cp_async_wait_all();
-    __syncthreads();
-    const float gl = gs[n - 1];
-    float dk[1][8][4];
+    // <S, dS_next> from the pairs (the two tiles share one layout), while V' and k land
     {
-        // dK~ = V' dS_next^T ; dk_j = e^{gL-gj} dK~_j ; dg_j -= K~_j . dK~_j ; dg_L += their sum
-        acc_zero<16, 64>(dk);
-        mma_split_ab<16, 64, 128, false, false>(dk, yh, yl, kP128, th, tl, kP128, m0, n0);
-        float p0 = 0.0f, p1 = 0.0f;
-        const int gq = lane >> 2, ra = m0 + gq, rb = ra + 8;
-        const float f0 = ra < n ? gexp(gl - gs[ra]) : 0.0f, f1 = rb < n ? gexp(gl - gs[rb]) : 0.0f;
-        acc_walk<16, 64>(m0, n0, [&](int r, int d, int i, int j, int q) {
-            float& x = dk[i][j][q];
-            x *= (q >> 1) ? f1 : f0;
-            const float t = __bfloat162float(xs[r * kP128 + d]) * x;
-            if (q >> 1) p1 += t; else p0 += t;
-        });
-        p0 = quad_sum(p0);
-        p1 = quad_sum(p1);
-        if ((lane & 3) == 0) {
-            atomicAdd(&dgs[m0 + (lane >> 2)], -p0);
-            atomicAdd(&dgs[m0 + (lane >> 2) + 8], -p1);
-            atomicAdd(&dgs[n - 1], p0 + p1);
+        float sdot = 0.0f;
+        for (int idx = threadIdx.x; idx < D * D / 8; idx += blockDim.x) {
+            const uint4 a = reinterpret_cast<const uint4*>(Sh)[idx], b = reinterpret_cast<const uint4*>(Sl)[idx];
+            const uint4 x = reinterpret_cast<const uint4*>(Th)[idx], y = reinterpret_cast<const uint4*>(Tl)[idx];
+            const __nv_bfloat162* ah = reinterpret_cast<const __nv_bfloat162*>(&a);
+            const __nv_bfloat162* bh = reinterpret_cast<const __nv_bfloat162*>(&b);
+            const __nv_bfloat162* xh = reinterpret_cast<const __nv_bfloat162*>(&x);
+            const __nv_bfloat162* yh = reinterpret_cast<const __nv_bfloat162*>(&y);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 fa = __bfloat1622float2(ah[e]), fb = __bfloat1622float2(bh[e]);
+                const float2 fx = __bfloat1622float2(xh[e]), fy = __bfloat1622float2(yh[e]);
+                sdot += (fa.x + fb.x) * (fx.x + fy.x) + (fa.y + fb.y) * (fx.y + fy.y);
+            }
         }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sdot += __shfl_xor_sync(0xFFFFFFFFu, sdot, o);
+        if (lane == 0) red[warp] = sdot;
+    }
+    cp_async_wait_all();
+    tc::fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (threadIdx.x == 0 && ok) {
+        const uint32_t th = smem_u32(Th), tl = smem_u32(Tl), yh = smem_u32(Yh), yl = smem_u32(Yl);
+        // K~^T = dS_next V'^T (hi hi, lo hi, hi lo)
+        for (int kk = 0; kk < 8; ++kk)
+            umma_f16(tm + 128, tc::kdesc(th, 128, 0, kk), tc::kdesc(yh, 64, 0, kk), idesc, kk > 0 ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk) umma_f16(tm + 128, tc::kdesc(tl, 128, 0, kk), tc::kdesc(yh, 64, 0, kk), idesc, 1u);
+        for (int kk = 0; kk < 8; ++kk) umma_f16(tm + 128, tc::kdesc(th, 128, 0, kk), tc::kdesc(yl, 64, 0, kk), idesc, 1u);
+        umma_commit(bar);
+    }
+    ok = __all_sync(0xFFFFFFFFu, ok && mbar_wait(bar, 1, nullptr));
+    tc_fence_after();
+    const float gl = gs[n - 1];
+    if (ok) {
+        // dk_j = e^{gL-gj} dK~_j ; dg_j -= k_j . dk_j ; dg_L += their sum
+        float x[32], p[32];
+        tc::tmem_row32(tq + 128, x);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            const int r = t0 + i;
+            x[i] *= r < n ? gexp(gl - gs[r]) : 0.0f;
+            p[i] = tc::ld_elem(Xs, 64, r, d) * x[i];
+            if (r < n) pdk[((tok0 + r) * dm.H + h) * D + d] = x[i];
+        }
+        const float s = tc::transpose_sum(p);
+        atomicAdd(&dgs[t0 + lane], -s);
+        float tot = s;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tot += __shfl_xor_sync(0xFFFFFFFFu, tot, o);
+        if (lane == 0) atomicAdd(&dgs[n - 1], tot);
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -796,14 +1099,10 @@ __global__ void __launch_bounds__(256) gdn_bwd_a(Dims dm, const bf16* __restrict
         dgs[n - 1] += gexp(gl) * s;
     }
     __syncthreads();
-    acc_pairs<16, 64>(m0, n0, [&](int r, int d, int i, int j, int hh) {  // two columns an 8-byte store
-        if (r < n) {
-            const int64_t at = ((tok0 + r) * dm.H + h) * D + d;
-            *reinterpret_cast<float2*>(pdq + at) = make_float2(dq[i][j][2 * hh], dq[i][j][2 * hh + 1]);
-            *reinterpret_cast<float2*>(pdk + at) = make_float2(dk[i][j][2 * hh], dk[i][j][2 * hh + 1]);
-        }
-    });
     for (int i = threadIdx.x; i < n; i += blockDim.x) pdg[(tok0 + i) * dm.H + h] = dgs[i];
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tm, kBaTmemCols);
 }
 
 // The solve's adjoint for one (chunk, head), shared by B2b and B3 (reference gdn_kkt.cpp:272-352): with
@@ -1139,11 +1438,13 @@ __global__ void gdn_sum_heads_kernel(const float* __restrict__ src, float* __res
     *reinterpret_cast<float4*>(dst + (t * Hg + hk) * D + d4) = s;
 }
 
-constexpr size_t kSmemPrep = (2 * L * kP128 + 4 * L * kP64) * 2 + (2 * L * F65 + 4 * L + 2 * L) * 4;
-constexpr size_t kSmemState = 2 * sizeof(F2Stage) + (2 * D * P64 + 2 * L * P64) * 2;
-constexpr size_t kSmemOut = (4 * L * kP128 + 2 * D * kP128 + 2 * L * kP64) * 2 + L * 4;
-constexpr size_t kSmemBState = 2 * sizeof(B1Late) + sizeof(B1Early) + (2 * D * kP64 + 4 * L * kP64) * 2;
-constexpr size_t kSmemBA = (4 * D * kP128 + 4 * L * kP128) * 2 + (2 * L + 8) * 4;
+constexpr size_t kSmemPrep = f1::kUsed + 1024;  // and the slack that aligns the tiles to 1024 bytes
+constexpr size_t kSmemState = f2::kUsed + 1024;  // and the slack that aligns the tiles to 1024 bytes
+constexpr size_t kSmemOut = f3::kUsed + 1024;  // and the slack that aligns the tiles to 1024 bytes
+constexpr size_t kSmemBState = b1::kUsed + 1024;  // and the slack that aligns the tiles to 1024 bytes
+// four [128][128] state tiles, four [64][128] row tiles, g, dg, the warp sums, the barrier and TMEM slot,
+// and the slack that aligns the tiles to 1024 bytes
+constexpr size_t kSmemBA = 4 * tc::kBlockTile + 4 * tc::kRowTile + (2 * L + 8) * 4 + 16 + 1024;
 constexpr size_t kSmemBB = (7 * L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 constexpr size_t kSmemKB = (L * kP128 + 6 * L * kP64) * 2 + (L * F65 + 4 * L) * 4;
 
@@ -1166,6 +1467,9 @@ Dims to_dims(const R97bGdnDims& d) {
 }
 
 }  // namespace
+
+R97B_ERROR_READER(gdn_error_word)
+
 }  // namespace r97b
 
 using namespace r97b;
@@ -1201,7 +1505,7 @@ extern "C" int r97b_gdn_fwd(const R97bGdnDims* dims, const R97bGdnFwd* a, void* 
     const auto* v = reinterpret_cast<const bf16*>(a->v);
     if (dm.n_chunks > 0)
         gdn_fwd_prep<<<dim3(dm.n_chunks, dm.H), 256, kSmemPrep, s>>>(dm, k, v, a->g, a->beta, a->A, a->w, a->u);
-    gdn_fwd_state<<<dim3(dm.n_seq, dm.H, D / VS2), 256, kSmemState, s>>>(dm, k, a->g, a->w, a->u, a->h0, a->S, a->Vp,
+    gdn_fwd_state<<<dim3(dm.n_seq, dm.H, D / 64), 256, kSmemState, s>>>(dm, k, a->g, a->w, a->u, a->h0, a->S, a->Vp,
                                                                        a->ht);
     if (dm.n_chunks > 0)
         gdn_fwd_out<<<dim3(dm.n_chunks, dm.H), 256, kSmemOut, s>>>(dm, q, k, a->g, a->S, a->Vp, a->P,
@@ -1226,7 +1530,7 @@ extern "C" int r97b_gdn_bwd(const R97bGdnDims* dims, const R97bGdnBwd* a, void* 
     const auto* k = reinterpret_cast<const bf16*>(a->k);
     const auto* v = reinterpret_cast<const bf16*>(a->v);
     const auto* dO = reinterpret_cast<const bf16*>(a->dO);
-    gdn_bwd_state<<<dim3(dm.n_seq, dm.H, D / VSB), 256, kSmemBState, s>>>(dm, q, k, a->g, a->w, a->P, dO, a->dht,
+    gdn_bwd_state<<<dim3(dm.n_seq, dm.H, D / 64), 256, kSmemBState, s>>>(dm, q, k, a->g, a->w, a->P, dO, a->dht,
                                                                         a->dS, a->dVp, a->dh0);
     if (dm.n_chunks > 0) {
         // B2a writes its partials of dq, dk, dg into the outputs; B2b adds its own terms to them

@@ -32,7 +32,11 @@ inline bool smem_opt_in(F* fn, int bytes) {
     return smem_opt_in(reinterpret_cast<const void*>(fn), bytes);
 }
 int64_t gemm_workspace_bytes(const R97bGemm& g);
+// Each tcgen05 translation unit's error word (sm100.cuh), read and cleared.
 unsigned gemm_error_word();
+unsigned attn_error_word();
+unsigned attn_fwd_error_word();
+unsigned gdn_error_word();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
