@@ -204,9 +204,9 @@ def b200_arm(args):
     step = TrainStep(model, adapter)
 
     buckets = None
-    if world > 1:  # a layer's adapter gradient is final: all-reduce its bucket while the walk goes on
+    if world > 1:  # the adapter gradient's all-reduce: per layer while the walk goes on, or once at the end
         from r97training_b200.dp import GradBuckets
-        buckets = GradBuckets(adapter.g, adapter.layer_ranges)
+        buckets = GradBuckets(adapter.g, adapter.layer_ranges, overlap=args.dp_overlap)
         step.grad_hook = buckets.ready
 
     def one_step(ids):
@@ -325,7 +325,9 @@ def b200_arm(args):
                        "launch": "eager" if graph is None else
                        ("CUDA graph of the whole step" if world == 1 else
                         "CUDA graph of the whole step, per-layer gradient all-reduces captured on a side "
-                        "stream overlapping the backward, AdamW after their join"),
+                        "stream overlapping the backward, AdamW after their join" if args.dp_overlap else
+                        "CUDA graph of the whole step, one all-reduce of the gradient after the backward, "
+                        "then AdamW"),
                        "flops_per_token": flops_per_token(cfg)},
             "roofline": {"bound": "tensor", "kernel": "gemm_kernel (tcgen05)", "achieved": gemm_tflops, "peak": peak,
                          "unit": "TFLOP/s", "frac": gemm_tflops / peak, "traffic": traffic,
@@ -555,6 +557,9 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--dp-overlap", type=int, default=1,
+                    help="N > 1: 1 = per-layer gradient all-reduces on a side stream during the backward, "
+                         "0 = one all-reduce of the whole gradient after it")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host each step "
                     "instead of replaying the step captured as a CUDA graph")
     ap.add_argument("--case", default=None, help="run one small kernel case for ncu instead of the bench "

@@ -19,12 +19,17 @@ import torch.distributed as dist
 
 
 class GradBuckets:
-    """Per-layer all-reduce (mean over ranks) of ``grad[lo:hi]`` for each ``(lo, hi)`` in ``ranges``."""
+    """Per-layer all-reduce (mean over ranks) of ``grad[lo:hi]`` for each ``(lo, hi)`` in ``ranges``.
 
-    def __init__(self, grad: torch.Tensor, ranges, group=None):
+    With ``overlap=False`` the walk's reports are only recorded and ``join`` exchanges the whole buffer in
+    one all-reduce on the compute stream: no collective kernel then shares the SMs with the backward's
+    persistent kernels (which size their grids to every SM), at the cost of the exchange's time."""
+
+    def __init__(self, grad: torch.Tensor, ranges, group=None, overlap: bool = True):
         self.grad = grad
         self.ranges = [(int(lo), int(hi)) for lo, hi in ranges]
         self.group = group
+        self.overlap = overlap
         self.world = dist.get_world_size(group)
         self.avg = dist.get_backend(group) == "nccl"  # NCCL averages in the collective; gloo sums
         self.stream = torch.cuda.Stream(device=grad.device) if grad.is_cuda else None
@@ -37,6 +42,9 @@ class GradBuckets:
         compute stream, and the all-reduce is issued as a stream-ordered (not host-waited) operation there."""
         if li in self._issued:
             raise RuntimeError(f"gradient bucket {li} issued twice in one step")
+        if not self.overlap:
+            self._issued.append(li)
+            return
         lo, hi = self.ranges[li]
         view = self.grad[lo:hi]
         op = dist.ReduceOp.AVG if self.avg else dist.ReduceOp.SUM
@@ -62,6 +70,17 @@ class GradBuckets:
         for li in range(len(self.ranges)):
             if li not in self._issued:
                 self.ready(li)
+        if not self.overlap:
+            op = dist.ReduceOp.AVG if self.avg else dist.ReduceOp.SUM
+            if self.grad.is_cuda and torch.cuda.is_current_stream_capturing():
+                dist.all_reduce(self.grad, op=op, group=self.group)
+            else:
+                dist.all_reduce(self.grad, op=op, group=self.group, async_op=True).wait()
+            if not self.avg and self.world > 1:
+                self.grad.div_(self.world)
+            order = list(self._issued)
+            self._issued.clear()
+            return order
         for work, view in self._works:
             if work is not None:
                 work.wait()

@@ -23,14 +23,14 @@ def _port():
 RANGES = [(0, 7), (7, 300), (300, 301), (301, 1000), (1000, 4096)]
 
 
-def _exchange(rank, world, port, results, skip):
+def _exchange(rank, world, port, results, skip, overlap):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         from r97training_b200.dp import GradBuckets
         g = torch.arange(4096, dtype=torch.float32) * (rank + 1) + rank
-        buckets = GradBuckets(g, RANGES)
+        buckets = GradBuckets(g, RANGES, overlap=overlap)
         for li in reversed(range(len(RANGES))):
             if skip and li == 2:
                 continue  # the walk never reported bucket 2 (on every rank alike)
@@ -43,12 +43,14 @@ def _exchange(rank, world, port, results, skip):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("skip", [False, True])
-def test_bucketed_allreduce_two_ranks(skip):
+@pytest.mark.parametrize("skip,overlap", [(False, True), (True, True), (True, False)])
+def test_bucketed_allreduce_two_ranks(skip, overlap):
+    """overlap=False: the reports are recorded and the join exchanges the whole buffer at once."""
     ctx = mp.get_context("spawn")
     with ctx.Manager() as m:
         results = m.dict()
-        mp.start_processes(_exchange, args=(2, _port(), results, skip), nprocs=2, join=True, start_method="spawn")
+        mp.start_processes(_exchange, args=(2, _port(), results, skip, overlap), nprocs=2, join=True,
+                           start_method="spawn")
         assert results[0][0] and results[1][0], dict(results)
         for r in range(2):
             assert results[r][1] == ([4, 3, 1, 0, 2] if skip else [4, 3, 2, 1, 0])
