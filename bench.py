@@ -393,8 +393,15 @@ def profile_case(case: str) -> None:
         Bb = (torch.randn(2 * F, r, device=dev) * 0.02).bfloat16()
         gu = torch.empty(M, 2 * F, device=dev, dtype=torch.bfloat16)
         a = torch.empty(M, F, device=dev, dtype=torch.bfloat16)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         for _ in range(3):
+            ev[0].record()
             ops.gemm(X, W, gu, a2=t, b2=Bb, mode=ops.EPI_SWIGLU, out2=a)
+            ev[1].record()
+        torch.cuda.synchronize()
+        ms = ev[0].elapsed_time(ev[1])
+        print(f"gate_up + SwiGLU {M} x {2 * F} x {K + r}: {ms * 1e3:.1f} us, "
+              f"{2 * M * 2 * F * (K + r) / ms / 1e9:.0f} TFLOP/s (third launch)")
     elif case in ("gemm", "gemm_dx"):
         from r97training_b200 import ops
         M, N, K = 8192, 24576, 4096
@@ -434,8 +441,13 @@ def profile_case(case: str) -> None:
         from r97training_b200 import iqr as IQ
         w = IQ.synth_weight(24576, 4096, seed=1, device=dev)
         out = torch.empty(24576, 4096, dtype=torch.bfloat16, device=dev)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         for _ in range(3):
+            ev[0].record()
             IQ.dequant_bf16(w, out=out)
+            ev[1].record()
+        torch.cuda.synchronize()
+        print(f"iqr decode 24576 x 4096 -> bf16: {ev[0].elapsed_time(ev[1]) * 1e3:.1f} us (third launch)")
     elif case == "norms":
         from r97training_b200 import ops
         x = torch.randn(8192, 4096, device=dev).bfloat16()
@@ -472,8 +484,15 @@ def profile_case(case: str) -> None:
         tgt = torch.randint(0, vocab, (rows,), device=dev, dtype=torch.int32)
         loss = torch.empty(rows, device=dev)
         grad = torch.empty_like(logits)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
         for _ in range(3):
+            ev[0].record()
             ops.ce_kld(logits, tgt, loss_ce=loss, grad=grad, grad_scale=1.0 / rows)
+            ev[1].record()
+        torch.cuda.synchronize()
+        us = ev[0].elapsed_time(ev[1]) * 1e3
+        print(f"CE {rows} x {vocab} bf16 logits: {us:.1f} us, {2 * 2 * rows * vocab / us / 1e3:.0f} GB/s "
+              "(logits read + gradient written, third launch)")
     elif case == "adamw":
         from r97training_b200 import ops
         n = 160_432_128
@@ -493,9 +512,16 @@ def profile_case(case: str) -> None:
         k, v = torch.empty_like(q), torch.empty(T, H, 128, device=dev, dtype=torch.bfloat16)
         dq, dk, dv = (torch.randn(T, H, 128, device=dev) for _ in range(3))
         dx = torch.zeros_like(x)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         for _ in range(3):
+            ev[0].record()
             ops.conv_prep_fwd(x, cw, cu, 2, Hg, H, q, k, v)
+            ev[1].record()
             ops.conv_prep_bwd(x, cw, cu, 2, Hg, H, dq, dk, dv, dx)
+            ev[2].record()
+        torch.cuda.synchronize()
+        print(f"conv prep {T} tokens x {C} channels: forward {ev[0].elapsed_time(ev[1]) * 1e3:.1f} us, "
+              f"backward {ev[1].elapsed_time(ev[2]) * 1e3:.1f} us (third pass)")
     elif case == "attn_fwd":
         from r97training_b200 import ops
         B, Hq, Hkv, S, D = 2, 16, 4, 4096, 256
@@ -557,9 +583,10 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--dp-overlap", type=int, default=1,
+    ap.add_argument("--dp-overlap", type=int, default=0,
                     help="N > 1: 1 = per-layer gradient all-reduces on a side stream during the backward, "
-                         "0 = one all-reduce of the whole gradient after it")
+                         "0 = one all-reduce of the whole gradient after it (measured no slower at 8 GPUs: the "
+                         "collective's kernels slow the backward's persistent kernels as much as they hide)")
     ap.add_argument("--eager", action="store_true", help="launch every kernel from the host each step "
                     "instead of replaying the step captured as a CUDA graph")
     ap.add_argument("--case", default=None, help="run one small kernel case for ncu instead of the bench "

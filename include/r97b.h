@@ -39,6 +39,11 @@ int r97b_abi_version(void);
  * arguments) -- read and cleared. Synchronises the current device. */
 int r97b_device_error(unsigned int* out_bits);
 
+/* The CUDA runtime error (a cudaError_t value) behind the most recent R97B_ELAUNCH of any entry point, read
+ * and cleared (0 when none since the last read), and the runtime's name for such a value. */
+int r97b_last_launch_error(void);
+const char* r97b_launch_error_name(int code);
+
 /* ------------------------------------------------------------------------------ plumbing */
 /* Device memory and streams for a C++ host that drives the kernels (the adjoint-row plugin,
  * libr97host.so), so that it needs no CUDA headers of its own. Replace: the reference's rad_dev_alloc /

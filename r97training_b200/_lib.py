@@ -82,6 +82,8 @@ class R97IqrDecodeDesc(ctypes.Structure):
 _SIGS = {
     "r97b_abi_version": (c_i32, []),
     "r97b_device_error": (c_i32, [c_vp]),
+    "r97b_last_launch_error": (c_i32, []),
+    "r97b_launch_error_name": (ctypes.c_char_p, [c_i32]),
     "r97_iqr_decode": (c_i32, [c_vp, c_vp]),
     "r97b_iqr_dequant_bf16": (c_i32, [c_vp, c_vp, c_i64, c_vp]),
     "r97b_gemm": (c_i32, [c_vp, c_vp]),
@@ -171,7 +173,11 @@ def lib():
 
 def check(rc: int, what: str) -> None:
     if rc != 0:
-        raise R97bError(f"{what} returned status {rc}")
+        detail = ""
+        if rc == 2 and _lib is not None:  # R97B_ELAUNCH: name the CUDA error behind it
+            code = int(_lib.r97b_last_launch_error())
+            detail = f" ({_lib.r97b_launch_error_name(code).decode()})" if code else ""
+        raise R97bError(f"{what} returned status {rc}{detail}")
 
 
 def exported_symbols():

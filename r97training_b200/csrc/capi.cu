@@ -3,9 +3,9 @@
 #include "r97b_internal.h"
 
 #include <atomic>
+#include <map>
 #include <mutex>
-#include <set>
-#include <tuple>
+#include <utility>
 
 namespace r97b {
 namespace {
@@ -13,27 +13,46 @@ std::atomic<unsigned long long> g_launches{0};
 }
 void add_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
 
+namespace {
+std::atomic<int> g_launch_error{0};
+}
+void note_launch_error(cudaError_t e) { g_launch_error.store((int)e, std::memory_order_relaxed); }
+
+// The attribute is a ceiling, so it only ever rises: a kernel launched with several sizes keeps the largest
+// it has been given (lowering it for a small launch would fail a later large one that found its size
+// recorded).
 bool smem_opt_in(const void* fn, int bytes) {
     static std::mutex mu;
-    static std::set<std::tuple<const void*, int, int>> done;  // (kernel, device, bytes)
+    static std::map<std::pair<const void*, int>, int> ceiling;  // (kernel, device) -> bytes set
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return false;
     std::lock_guard<std::mutex> lock(mu);
-    const auto key = std::make_tuple(fn, dev, bytes);
-    if (done.count(key)) return true;
-    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) return false;
-    done.insert(key);
+    const auto key = std::make_pair(fn, dev);
+    const auto it = ceiling.find(key);
+    if (it != ceiling.end() && it->second >= bytes) return true;
+    const cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) {
+        note_launch_error(e);
+        cudaGetLastError();  // not sticky: clear it so the next launch's check does not see it
+        return false;
+    }
+    ceiling[key] = bytes;
     return true;
 }
 }  // namespace r97b
 
 extern "C" uint64_t r97b_launch_count(void) { return r97b::g_launches.load(std::memory_order_relaxed); }
 
-extern "C" int r97b_abi_version(void) { return 4; }
+extern "C" int r97b_abi_version(void) { return 5; }
+
+// The CUDA error (cudaError_t) behind the most recent R97B_ELAUNCH, and its name; 0 / "cudaSuccess" when
+// none has occurred since the last read, which clears it.
+extern "C" int r97b_last_launch_error(void) { return r97b::g_launch_error.exchange(0); }
+extern "C" const char* r97b_launch_error_name(int code) { return cudaGetErrorName((cudaError_t)code); }
 
 extern "C" int r97b_device_error(unsigned int* out_bits) {
     unsigned bits = r97b::gemm_error_word() | r97b::attn_error_word() | r97b::attn_fwd_error_word() |
-                    r97b::gdn_error_word();
+                    r97b::gdn_error_word() | r97b::loss_error_word();
     if (out_bits) *out_bits = bits;
     return cudaGetLastError() == cudaSuccess ? R97B_OK : R97B_ELAUNCH;
 }

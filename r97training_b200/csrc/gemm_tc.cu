@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -39,6 +40,7 @@ struct KernelArgs {
     int32_t k1_blocks, k2_blocks;
     int32_t kb_per_split, splits;
     int32_t tiles_m, tiles_n;
+    int32_t band;  // M-tiles a band of the tile order walks (tile_coords)
     int32_t mode;
     float alpha, beta;
     void* out;
@@ -115,15 +117,14 @@ struct Cfg {
     static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
-// The tile order: bands of up to 16 M-tiles, N-tiles walked inside a band with M fastest, so one wave of
+// The tile order: bands of up to `band` M-tiles, N-tiles walked inside a band with M fastest, so one wave of
 // persistent CTAs works on a band's A rows (which stay in L2 across the band's waves) against a few
 // N-tiles of B, instead of all of A against two or three N-tiles.
-__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
-    constexpr int kBand = 16;
-    const int band = tile / (kBand * tiles_n);
-    const int m_base = band * kBand;
-    const int gm = min(kBand, tiles_m - m_base);
-    const int r = tile - band * kBand * tiles_n;
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int band, int& tm, int& tn) {
+    const int b = tile / (band * tiles_n);
+    const int m_base = b * band;
+    const int gm = min(band, tiles_m - m_base);
+    const int r = tile - b * band * tiles_n;
     tm = m_base + r % gm;
     tn = r / gm;
 }
@@ -295,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int split = u / tiles;
             const int tile = u % tiles;
             int tm, tn;
-            tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+            tile_coords(tile, args.tiles_m, args.tiles_n, args.band, tm, tn);
             const int kb0 = split * args.kb_per_split;
             const int kb1 = min(k_total, kb0 + args.kb_per_split);
             bool ok = true;
@@ -379,7 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
             const int tile = u % tiles;
             int tm, tn;
-            tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+            tile_coords(tile, args.tiles_m, args.tiles_n, args.band, tm, tn);
             const int acc = local & 1;
             bool ok = mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag);
             if (split_mode) ok = epi_all(ok);  // the fix-up below syncs the four warps: they leave together
@@ -550,7 +551,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int split = u / tiles;
             const int tile = u % tiles;
             int tm, tn;
-            tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+            tile_coords(tile, args.tiles_m, args.tiles_n, args.band, tm, tn);
             const int kb0 = split * args.kb_per_split;
             const int kb1 = min(k_total, kb0 + args.kb_per_split);
             bool ok = true;
@@ -638,7 +639,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         for (int u = pair; u < units; u += pairs, ++local) {
             const int tile = u % tiles;
             int tm, tn;
-            tile_coords(tile, args.tiles_m, args.tiles_n, tm, tn);
+            tile_coords(tile, args.tiles_m, args.tiles_n, args.band, tm, tn);
             const int acc = local & 1;
             if (!mbar_wait(&tfull_bar[acc], (local >> 1) & 1, abort_flag)) break;
             tc_fence_after();
@@ -780,6 +781,16 @@ int64_t split_ws_bytes(const R97bGemm& g, int64_t* cnt_bytes) {
     return cb + (int64_t)splits * tiles * kBM * bn * 4;
 }
 
+// M-tiles a band of the tile order walks: 16 unless R97B_GEMM_BAND (1 .. 64) says otherwise, read once.
+int tile_band() {
+    static const int band = [] {
+        const char* e = getenv("R97B_GEMM_BAND");
+        const int v = e ? atoi(e) : 0;
+        return v >= 1 && v <= 64 ? v : 16;
+    }();
+    return band;
+}
+
 template <int BN, int A_MN, int B_MN>
 int launch(const R97bGemm& g, cudaStream_t stream) {
     using C = Cfg<BN>;
@@ -804,6 +815,7 @@ int launch(const R97bGemm& g, cudaStream_t stream) {
     k.splits = splits;
     k.tiles_m = (int32_t)((g.M + kBM - 1) / kBM);
     k.tiles_n = (int32_t)((g.N + BN - 1) / BN);
+    k.band = tile_band();
     k.mode = g.mode;
     if (g.mode == kEpiSplitBf16) {
         if (splits <= 1) {
@@ -856,6 +868,7 @@ int launch_pair(const R97bGemm& g, cudaStream_t stream) {
     k.splits = splits;
     k.tiles_m = (int32_t)((g.M + 255) / 256);
     k.tiles_n = (int32_t)((g.N + 255) / 256);
+    k.band = tile_band();
     k.mode = g.mode;
     k.alpha = g.alpha;
     k.beta = g.beta;

@@ -23,9 +23,9 @@ int gemm_run(const R97bGemm& g, cudaStream_t stream);
 bool make_map(CUtensorMap* map, const void* ptr, int64_t inner, int64_t outer, int64_t ld, int box_inner,
               int box_outer);
 int num_sms();
-// Opts kernel `fn` into `bytes` of dynamic shared memory on the device that is current. The runtime keeps
-// this attribute per device, so it is set once per (kernel, device, size), under a lock; returns false
-// when the runtime refuses it (capi.cu).
+// Opts kernel `fn` into at least `bytes` of dynamic shared memory on the device that is current. The
+// runtime keeps this attribute per device; it is raised (never lowered) per (kernel, device), under a lock;
+// returns false when the runtime refuses it (capi.cu).
 bool smem_opt_in(const void* fn, int bytes);
 template <typename F>
 inline bool smem_opt_in(F* fn, int bytes) {
@@ -37,14 +37,22 @@ unsigned gemm_error_word();
 unsigned attn_error_word();
 unsigned attn_fwd_error_word();
 unsigned gdn_error_word();
+unsigned loss_error_word();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // Counts this library's kernel launches (r97b_launch_count); `n` = the launches the caller just queued.
 void add_launches(int n);
 
+// Records the CUDA error behind an R97B_ELAUNCH (r97b_last_launch_error reads it).
+void note_launch_error(cudaError_t e);
+
 inline int launch_status(int n = 1) {
-    if (cudaGetLastError() != cudaSuccess) return R97B_ELAUNCH;
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) {
+        note_launch_error(e);
+        return R97B_ELAUNCH;
+    }
     add_launches(n);
     return R97B_OK;
 }
