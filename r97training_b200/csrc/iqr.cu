@@ -247,11 +247,16 @@ __global__ void __launch_bounds__(256, 4) iqr_decode_u4(const R97IqrDecodeDesc d
                          : bf16_bits_to_f32(*reinterpret_cast<const uint16_t*>(sp + rb * srb));
         }
     }
-    uint32_t st[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-        st[i] = (((halo[0] >> (4 * i)) & 15u) << 8) | (((halo[1] >> (4 * i)) & 15u) << 4) |
-                ((halo[2] >> (4 * i)) & 15u);
+    // A column's 16-bit state at row r is its nibbles of rows r-3 .. r. They are formed from "pair bytes":
+    // for rows (a, b), E holds (a's nibble << 4 | b's nibble) of the even columns (byte j: column 2j) and O
+    // of the odd ones (byte j: column 2j + 1); the state of column 2j is then E(r-3, r-2).byte_j << 8 |
+    // E(r-1, r).byte_j -- one byte permute yields two columns' states, so a row's eight states take four
+    // permutes and eight half-extractions instead of a shift / mask / merge chain per column.
+    auto pair_e = [](uint32_t a, uint32_t b) { return ((a << 4) & 0xF0F0F0F0u) | (b & 0x0F0F0F0Fu); };
+    auto pair_o = [](uint32_t a, uint32_t b) { return (a & 0xF0F0F0F0u) | ((b >> 4) & 0x0F0F0F0Fu); };
+    uint32_t e2 = pair_e(halo[0], halo[1]), o2 = pair_o(halo[0], halo[1]);  // rows (r-3, r-2)
+    uint32_t e1 = pair_e(halo[1], halo[2]), o1 = pair_o(halo[1], halo[2]);  // rows (r-2, r-1)
+    uint32_t prev = halo[2];
     const uint32_t A = d.mad_a & 0xFFFFFFu, B = d.mad_b;
     uint16_t* wrow = kBf16Out ? s.w + (sr0 - d.row0) * s.ld_w + j0 : nullptr;
 #pragma unroll
@@ -259,6 +264,16 @@ __global__ void __launch_bounds__(256, 4) iqr_decode_u4(const R97IqrDecodeDesc d
         if (b >= nrow) break;
         const uint32_t w = wb[b];
         const int64_t lr = sr0 + b - d.row0;
+        const uint32_t e0 = pair_e(prev, w), o0 = pair_o(prev, w);  // rows (r-1, r)
+        const uint32_t pe01 = __byte_perm(e0, e2, 0x5140u), pe23 = __byte_perm(e0, e2, 0x7362u);
+        const uint32_t po01 = __byte_perm(o0, o2, 0x5140u), po23 = __byte_perm(o0, o2, 0x7362u);
+        const uint32_t st[8] = {pe01 & 0xFFFFu, po01 & 0xFFFFu, pe01 >> 16, po01 >> 16,
+                                pe23 & 0xFFFFu, po23 & 0xFFFFu, pe23 >> 16, po23 >> 16};
+        e2 = e1;
+        o2 = o1;
+        e1 = e0;
+        o1 = o0;
+        prev = w;
         if (kBf16Out) {
             // value = (byte sum of the hash) - 126, formed exactly as a float: the dot product's
             // accumulator starts at 2^23's bit pattern, so the sum lands in the mantissa
@@ -266,7 +281,6 @@ __global__ void __launch_bounds__(256, 4) iqr_decode_u4(const R97IqrDecodeDesc d
             float vf[8];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                st[i] = ((st[i] << 4) | ((w >> (4 * i)) & 15u)) & 0xFFFFu;
                 const uint32_t h = (st[i] * A + B) & 0x3F3F3F3Fu;
                 vf[i] = __uint_as_float(__dp4a(h, 0x01010101u, 0x4B000000u)) - 8388734.0f;
             }
@@ -283,10 +297,7 @@ __global__ void __launch_bounds__(256, 4) iqr_decode_u4(const R97IqrDecodeDesc d
         } else {
             int32_t v[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                st[i] = ((st[i] << 4) | ((w >> (4 * i)) & 15u)) & 0xFFFFu;
-                v[i] = mad_value(st[i], A, B);
-            }
+            for (int i = 0; i < 8; ++i) v[i] = mad_value(st[i], A, B);
             uint32_t lo = 0, hi = 0;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
