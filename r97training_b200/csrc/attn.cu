@@ -54,10 +54,14 @@ template <int BN, int NACC = 1>
 struct ACfg {
     static constexpr int kBBytes = BN * kBK * 2;
     static constexpr int kStageBytes = kABytes + kBBytes;
-    static constexpr int kStages = (200 * 1024) / kStageBytes > 8 ? 8 : (200 * 1024) / kStageBytes;
+    // kPDS (two accumulators): a 4 KB staging slot per epilogue warp for its P and dS rows (32 rows of 64 B
+    // each, pitch 80 B), so the tiles leave as coalesced rows; that space comes out of the ring
+    static constexpr int kStageOut = NACC == 2 ? 16 * 32 * 80 * 2 : 0;
+    static constexpr int kRing = NACC == 2 ? 224 * 1024 - kStageOut : 200 * 1024;
+    static constexpr int kStages = kRing / kStageBytes > 8 ? 8 : kRing / kStageBytes;
     static constexpr int kAccCols = NACC * BN;  // one tile's accumulators (kPDS: S and dP side by side)
     static constexpr int kTmemCols = 2 * kAccCols;
-    static constexpr int kSmemBytes = kStages * kStageBytes + 1024 + 256;
+    static constexpr int kSmemBytes = kStages * kStageBytes + kStageOut + 1024 + 256;
 };
 
 // Unit `t`-th of CTA `c` (of G) in the pass's order: round-robin for the equal tiles of kPDS, a snake
@@ -114,7 +118,8 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
     extern __shared__ uint8_t smem_raw[];
     const uint32_t base_u32 = smem_u32(smem_raw);
     uint8_t* smem = smem_raw + ((1024u - (base_u32 & 1023u)) & 1023u);
-    uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes);
+    uint8_t* stage_out = smem + C::kStages * C::kStageBytes;  // kPDS: the epilogue warps' staging slots
+    uint64_t* full_bar = reinterpret_cast<uint64_t*>(stage_out + C::kStageOut);
     uint64_t* empty_bar = full_bar + C::kStages;
     uint64_t* tfull_bar = empty_bar + C::kStages;
     uint64_t* tempty_bar = tfull_bar + 2;
@@ -285,8 +290,10 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
                 const float lse2 = args.lse[grow] * kLog2e;
                 const float dlt = args.delta[grow];
                 const float sl2 = args.scale * kLog2e;
-                __nv_bfloat16* op = args.out + grow * args.S + j * kBM;
-                __nv_bfloat16* od = args.out2 + grow * args.S + j * kBM;
+                // this warp's staging slot: its 32 rows' 32 values of P, then of dS, as bf16 rows of 64 B at an
+                // 80-byte pitch (a quarter-warp's 16-byte accesses then fall in distinct banks)
+                uint8_t* slot = stage_out + (warp - 4) * (32 * 80 * 2);
+                const int64_t grow0 = (int64_t)bh * args.S + i * kBM + q * 32;  // the warp's first row
 #pragma unroll 1
                 for (int cc = c0; cc < c0 + kChunks; ++cc) {
                     uint32_t rs[32], rd[32];
@@ -304,8 +311,6 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
                         pv[e] = pe;
                         dv[e] = args.scale * pb * (__uint_as_float(rd[e]) - dlt);
                     }
-                    uint4* dst = reinterpret_cast<uint4*>(op + cc * 32);
-                    uint4* dsd = reinterpret_cast<uint4*>(od + cc * 32);
 #pragma unroll
                     for (int w = 0; w < 4; ++w) {
                         uint32_t pk[4], dk[4];
@@ -316,8 +321,19 @@ __global__ void __launch_bounds__(128 + 128 * EPW, 1)
                             pk[h2] = *reinterpret_cast<const uint32_t*>(&b2);
                             dk[h2] = *reinterpret_cast<const uint32_t*>(&d2);
                         }
-                        dst[w] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                        dsd[w] = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+                        *reinterpret_cast<uint4*>(slot + lane * 80 + w * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        *reinterpret_cast<uint4*>(slot + 32 * 80 + lane * 80 + w * 16) = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+                    }
+                    __syncwarp();
+                    // out: four lanes a row (64 contiguous bytes), eight rows a store
+#pragma unroll
+                    for (int s8 = 0; s8 < 4; ++s8) {
+                        const int r = s8 * 8 + (lane >> 2), part = lane & 3;
+                        const uint4 vp = *reinterpret_cast<const uint4*>(slot + r * 80 + part * 16);
+                        const uint4 vd = *reinterpret_cast<const uint4*>(slot + 32 * 80 + r * 80 + part * 16);
+                        const int64_t at = (grow0 + r) * args.S + j * kBM + cc * 32 + part * 8;
+                        *reinterpret_cast<uint4*>(args.out + at) = vp;
+                        *reinterpret_cast<uint4*>(args.out2 + at) = vd;
                     }
                 }
             } else {
