@@ -443,7 +443,9 @@ constexpr int kSh = 2 * kStage;               // S hi/lo [128][64]
 constexpr int kSl = kSh + 128 * 64 * 2;
 constexpr int kVh = kSl + 128 * 64 * 2;       // V'' hi/lo [64][64]
 constexpr int kVl = kVh + tc::kSqTile;
-constexpr int kBar = kVl + tc::kSqTile;       // mbarrier, abort flag, TMEM slot
+constexpr int kOh = kVl + tc::kSqTile;        // V' hi/lo [64][64], staged for its coalesced copy out
+constexpr int kOl = kOh + tc::kSqTile;
+constexpr int kBar = kOl + tc::kSqTile;       // mbarrier, abort flag, TMEM slot
 constexpr int kUsed = kBar + 16;
 }  // namespace f2
 
@@ -472,7 +474,7 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
     using namespace f2;
     extern __shared__ unsigned char smraw[];
     unsigned char* sm = tc::align1024(smraw);
-    unsigned char *Sh = sm + kSh, *Sl = sm + kSl, *Vh = sm + kVh, *Vl = sm + kVl;
+    unsigned char *Sh = sm + kSh, *Sl = sm + kSl, *Vh = sm + kVh, *Vl = sm + kVl, *Oh = sm + kOh, *Ol = sm + kOl;
     uint64_t* bar = reinterpret_cast<uint64_t*>(sm + kBar);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(sm + kBar + 8);
     uint32_t* tslot = reinterpret_cast<uint32_t*>(sm + kBar + 12);
@@ -511,15 +513,15 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
         unsigned char* st = sm + ((c - c0) & 1) * kStage;
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
-        // the state entering chunk c: its tiles, and S_all[c]
+        // the state entering chunk c: its tiles, then S_all[c] copied out of them
         tc::put_row32(Sh, Sl, 128, d, 32 * ch, S);
-        tc::put_global32(Sp.hi, Sp.lo, ((int64_t)c * dm.H + h) * D * D + d * D + e0 + 32 * ch, S);
         cp_async_wait_all();
         tc::fence_proxy_async();
         tc_fence_before();
         __syncthreads();  // chunk c's stage landed; the S tiles written; chunk c-1's products are done
         tc_fence_after();
         if (*abort_flag) break;
+        tc::tile_to_global(Sh, Sl, 128, 128, Sp.hi, Sp.lo, ((int64_t)c * dm.H + h) * D * D + e0, D);
         if (c + 1 < c1) f2_issue(sm + ((c + 1 - c0) & 1) * kStage, dm, w_hi, w_lo, k, u, g, c + 1, h, hk, e0);
         const uint32_t swh = smem_u32(st + kWh), swl = smem_u32(st + kWl), sk = smem_u32(st + kK);
         const uint32_t ssh = smem_u32(Sh), ssl = smem_u32(Sl), svh = smem_u32(Vh), svl = smem_u32(Vl);
@@ -550,7 +552,7 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
                 x[4 * j + 2] = u4.z - x[4 * j + 2];
                 x[4 * j + 3] = u4.w - x[4 * j + 3];
             }
-            if (i < n) tc::put_global32(Vpp.hi, Vpp.lo, ((tok0 + i) * dm.H + h) * D + e0 + 32 * ch, x);
+            tc::put_row32(Oh, Ol, 64, i, 32 * ch, x);
             const float sc = i < n ? gexp(gl - gs[i]) : 0.0f;
 #pragma unroll
             for (int j = 0; j < 32; ++j) x[j] *= sc;
@@ -560,6 +562,7 @@ __global__ void __launch_bounds__(256) gdn_fwd_state(Dims dm, const bf16* __rest
         tc_fence_before();
         __syncthreads();
         tc_fence_after();
+        tc::tile_to_global(Oh, Ol, 64, n, Vpp.hi, Vpp.lo, (tok0 * dm.H + h) * D + e0, (int64_t)dm.H * D);
         if (threadIdx.x == 0 && !*abort_flag) {
             // k^T V'' (V'': hi, lo)
             for (int kk = 0; kk < 4; ++kk)
@@ -672,14 +675,16 @@ __global__ void __launch_bounds__(256) gdn_fwd_out(Dims dm, const bf16* __restri
             p[i] = (l <= r && r < n) ? p[i] * gexp(gs[r] - gs[l]) : 0.0f;
         }
         tc::put_row32(Ph, Pl, 64, r, 32 * ch, p);
-        const Pair Pp = pair_of(P_all, (int64_t)dm.n_chunks * dm.H * L * L);
-        tc::put_global32(Pp.hi, Pp.lo, blk * L * L + r * L + 32 * ch, p);
     }
     cp_async_wait_all();
     tc::fence_proxy_async();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    {
+        const Pair Pp = pair_of(P_all, (int64_t)dm.n_chunks * dm.H * L * L);
+        tc::tile_to_global(Ph, Pl, 64, 64, Pp.hi, Pp.lo, blk * L * L, L);
+    }
     if (threadIdx.x == 0 && ok) {
         // S^T q^T (S: hi, lo) ; V'^T P^T (hi hi, lo hi, hi lo)
         for (int kk = 0; kk < 8; ++kk)
@@ -830,15 +835,15 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
         unsigned char* lt = sm + ((c1 - 1 - c) & 1) * kLate;
         const int64_t tok0 = dm.tok0[c];
         const int n = dm.len[c];
-        // dS entering (from the right) chunk c: its tiles, and dS_all[c]
+        // dS entering (from the right) chunk c: its tiles, then dS_all[c] copied out of them
         tc::put_row32(DSh, DSl, 128, d, 32 * ch, dS);
-        tc::put_global32(dSp.hi, dSp.lo, ((int64_t)c * dm.H + h) * D * D + d * D + e0 + 32 * ch, dS);
         cp_async_wait_all();
         tc::fence_proxy_async();
         tc_fence_before();
         __syncthreads();  // chunk c's operands landed; the dS tiles written; chunk c+1's products are done
         tc_fence_after();
         if (*abort_flag) break;
+        tc::tile_to_global(DSh, DSl, 128, 128, dSp.hi, dSp.lo, ((int64_t)c * dm.H + h) * D * D + e0, D);
         if (c > c0) b1_issue_late(sm + ((c1 - c) & 1) * kLate, dm, q, w_hi, w_lo, c - 1, h, hk);
         if (threadIdx.x == 0) {
             // P^T dO (P: hi, lo) ; k dS (dS: hi, lo)
@@ -884,13 +889,13 @@ __global__ void __launch_bounds__(256) gdn_bwd_state(Dims dm, const bf16* __rest
             const float sc = j < n ? gexp(gl - gs[j]) : 0.0f;
 #pragma unroll
             for (int e = 0; e < 32; ++e) a1[e] = j < n ? dm.scale * a1[e] + sc * a2[e] : 0.0f;
-            if (j < n) tc::put_global32(dVpp.hi, dVpp.lo, ((tok0 + j) * dm.H + h) * D + e0 + 32 * ch, a1);
             tc::put_row32(DVh, DVl, 64, j, 32 * ch, a1);
         }
         tc::fence_proxy_async();
         tc_fence_before();
         __syncthreads();  // dV' and e^g dO written; chunk c's P, k, dO and g are no longer read
         tc_fence_after();
+        tc::tile_to_global(DVh, DVl, 64, n, dVpp.hi, dVpp.lo, (tok0 * dm.H + h) * D + e0, (int64_t)dm.H * D);
         if (threadIdx.x == 0 && !*abort_flag) {
             // q^T (e^g dO) (hi, lo) ; w^T dV' (hi hi, lo hi, hi lo)
             const uint32_t sq = smem_u32(lt + kLateQ), swh = smem_u32(lt + kLateWh), swl = smem_u32(lt + kLateWl);

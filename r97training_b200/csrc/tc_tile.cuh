@@ -109,6 +109,20 @@ __device__ __forceinline__ void put_global32(__nv_bfloat16* hi, __nv_bfloat16* l
     }
 }
 
+// The first `rows` rows of an R-row, 64-column tile pair (hi, lo) copied to global bf16 planes at
+// hi/lo[at + r * ld + 0 .. 63]: each row leaves as one 128-byte run, a warp storing four rows at once (a
+// thread that owned a row would store 32 rows' pieces in one instruction). The whole CTA calls it after the
+// barrier that follows the tiles' writes.
+__device__ __forceinline__ void tile_to_global(const unsigned char* th, const unsigned char* tl, int R, int rows,
+                                               __nv_bfloat16* hi, __nv_bfloat16* lo, int64_t at, int64_t ld) {
+    for (int idx = threadIdx.x; idx < 2 * R * 8; idx += blockDim.x) {
+        const int plane = idx / (R * 8), r = (idx >> 3) % R, j = idx & 7;
+        if (r >= rows) continue;
+        const uint4 v = *reinterpret_cast<const uint4*>((plane ? tl : th) + chunk_off(R, r, j));
+        *reinterpret_cast<uint4*>((plane ? lo : hi) + at + r * ld + j * 8) = v;
+    }
+}
+
 // 32 TMEM columns of this warp's lane quarter, as floats.
 __device__ __forceinline__ void tmem_row32(uint32_t taddr, float (&v)[32]) {
     uint32_t r[32];
