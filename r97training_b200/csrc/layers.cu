@@ -855,7 +855,7 @@ extern "C" int r97b_conv_prep_bwd(const uint16_t* x, int64_t ldx, const float* c
     const int smem = 2 * conv_stage(b.grp).bytes;
     if (smem > 227 * 1024) return R97B_EINVAL;
     int per_sm = 0;
-    if (cudaFuncSetAttribute(conv_prep_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+    if (!smem_opt_in(conv_prep_bwd_kernel, smem) ||
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, conv_prep_bwd_kernel, 256, smem) != cudaSuccess ||
         per_sm < 1)
         return R97B_ELAUNCH;
