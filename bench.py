@@ -273,6 +273,10 @@ def b200_arm(args):
     clocks = sampler.stop()
     ms = e0.elapsed_time(e1)
     launches, gemm_ms, gemm_flops = ops.gemm_profile_summary(prof)
+    if args.gemm_shapes and rank == 0:  # one step's GEMMs by shape, to stderr
+        for shape, (n, gms, fl) in sorted(ops.gemm_profile_by_shape(prof).items(), key=lambda kv: -kv[1][1]):
+            print(f"gemm {shape:48s} x{n:4d} {gms:8.3f} ms {fl / gms / 1e9 if gms else 0:7.0f} TFLOP/s",
+                  file=sys.stderr)
     if graph is not None:  # the graph's events hold the last timed replay: one step's GEMMs
         launches, gemm_ms, gemm_flops = launches * args.steps, gemm_ms * args.steps, gemm_flops * args.steps
     t = torch.tensor([ms], device=dev)
@@ -583,6 +587,7 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="5")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemm-shapes", action="store_true", help="print one step's GEMM time by shape to stderr")
     ap.add_argument("--dp-overlap", type=int, default=0,
                     help="N > 1: 1 = per-layer gradient all-reduces on a side stream during the backward, "
                          "0 = one all-reduce of the whole gradient after it (measured no slower at 8 GPUs: the "

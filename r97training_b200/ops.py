@@ -106,7 +106,8 @@ def gemm(a1, b1, out, *, a_mn=False, b_mn=False, a2=None, b2=None, mode=EPI_STOR
     if prof is not None:
         e1.record(s)
         full = 2.0 * M * N * (K1 + (g.K2 if a2 is not None else 0))
-        prof.append((e0, e1, full if flops is None else float(flops)))
+        shape = f"{M}x{N}x{K1}+{g.K2 if a2 is not None else 0} mode {mode} mn {int(a_mn)}{int(b_mn)}"
+        prof.append((e0, e1, full if flops is None else float(flops), shape))
     return out
 
 
@@ -144,7 +145,7 @@ class SplitWorkspace:
         self.buf = torch.zeros(nbytes // 4, dtype=torch.int32, device=device)
 
 
-# When a list, every gemm() appends (start event, end event, algorithmic FLOPs) recorded on its stream (in a
+# When a list, every gemm() appends (start event, end event, algorithmic FLOPs, shape) recorded on its stream (in a
 # captured graph: recorded again by every replay, so a summary after replays reads the last one):
 # bench.py's live measurement of the tensor-core GEMM's launch durations.
 GEMM_PROFILE = None
@@ -153,8 +154,18 @@ GEMM_PROFILE = None
 def gemm_profile_summary(prof):
     """(launches, total device ms, total FLOPs) of a recorded profile (synchronises)."""
     torch.cuda.synchronize()
-    ms = sum(a.elapsed_time(b) for a, b, _ in prof)
-    return len(prof), ms, sum(f for _, _, f in prof)
+    ms = sum(e[0].elapsed_time(e[1]) for e in prof)
+    return len(prof), ms, sum(e[2] for e in prof)
+
+
+def gemm_profile_by_shape(prof):
+    """{shape: (launches, device ms, FLOPs)} of a recorded profile (synchronises)."""
+    torch.cuda.synchronize()
+    out = {}
+    for e0, e1, f, shape in prof:
+        n, ms, fl = out.get(shape, (0, 0.0, 0.0))
+        out[shape] = (n + 1, ms + e0.elapsed_time(e1), fl + f)
+    return out
 
 
 # ------------------------------------------------------------------------------------------ norms
