@@ -373,6 +373,7 @@ def profile_case(case: str) -> None:
 
     gemm, gemm_dx   the config-5 gate_up forward GEMM (8192 x 24576 x 4096) / its input adjoint (B MN-major)
     gemm_swiglu     the gate_up forward as the step runs it: LoRA tail, SwiGLU in the epilogue
+    gemm_swiglu_bwd the down projection's input adjoint with SwiGLU's adjoint in the epilogue (B MN-major)
     gdn             one config-5 GDN layer, forward + backward
     decode          the IQR decode of a 24576 x 4096 weight
     norms / gnorm   rmsnorm fwd/bwd at 8192 x 4096 / gated rmsnorm at 8192 tokens x 32 heads x 128
@@ -406,6 +407,24 @@ def profile_case(case: str) -> None:
         ms = ev[0].elapsed_time(ev[1])
         print(f"gate_up + SwiGLU {M} x {2 * F} x {K + r}: {ms * 1e3:.1f} us, "
               f"{2 * M * 2 * F * (K + r) / ms / 1e9:.0f} TFLOP/s (third launch)")
+    elif case == "gemm_swiglu_bwd":
+        from r97training_b200 import ops
+        M, F, K, r = 8192, 12288, 4096, 64
+        dY = torch.randn(M, K, device=dev).bfloat16()
+        W = (torch.randn(K, F, device=dev) * 0.02).bfloat16()  # the down projection [out K][in F]
+        dt = torch.randn(M, r, device=dev).bfloat16()
+        A = (torch.randn(r, F, device=dev) * 0.02).bfloat16()
+        gu = torch.randn(M, 2 * F, device=dev).bfloat16()
+        dgu = torch.empty(M, 2 * F, device=dev, dtype=torch.bfloat16)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        for _ in range(3):
+            ev[0].record()
+            ops.gemm(dY, W, dgu, b_mn=True, a2=dt, b2=A, N=F, mode=ops.EPI_SWIGLU_BWD, addend=gu)
+            ev[1].record()
+        torch.cuda.synchronize()
+        ms = ev[0].elapsed_time(ev[1])
+        print(f"down-projection dX + SwiGLU adjoint {M} x {F} x {K + r}: {ms * 1e3:.1f} us, "
+              f"{2 * M * F * (K + r) / ms / 1e9:.0f} TFLOP/s (third launch)")
     elif case in ("gemm", "gemm_dx"):
         from r97training_b200 import ops
         M, N, K = 8192, 24576, 4096
