@@ -487,9 +487,16 @@ def profile_case(case: str) -> None:
         do = torch.randn(T * H, 128, device=dev).bfloat16()
         w = torch.ones(128, device=dev)
         dx, dz = torch.empty_like(x), torch.empty_like(z)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         for _ in range(3):
+            ev[0].record()
             ops.gated_rmsnorm_fwd(x, z, w)
+            ev[1].record()
             ops.gated_rmsnorm_bwd(x, z, w, do, dx=dx, dz=dz)
+            ev[2].record()
+        torch.cuda.synchronize()
+        print(f"gated rmsnorm {T * H} rows x 128: forward {ev[0].elapsed_time(ev[1]) * 1e3:.1f} us, "
+              f"backward {ev[1].elapsed_time(ev[2]) * 1e3:.1f} us (third pass)")
     elif case == "swiglu":
         from r97training_b200 import ops
         T, F = 8192, 12288

@@ -426,8 +426,8 @@ __global__ void __launch_bounds__(256) gated_bwd128(const __nv_bfloat16* __restr
     }
 }
 
-constexpr int kGatedFwdRows = 4;
-constexpr int kGatedBwdRows = 2;
+constexpr int kGatedFwdRows = 2;
+constexpr int kGatedBwdRows = 1;
 
 int group_width(int n) {
     // lanes per row: a full warp once the row has 256+ elements, else one 8-vector per lane
