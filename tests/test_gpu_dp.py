@@ -1,6 +1,7 @@
 """Data parallelism on two GPUs (skipped on a one-GPU box): two NCCL ranks, each its own micro-batch through
-the same base and adapter, the step captured as one CUDA graph with the per-layer gradient all-reduces
-captured on their side stream (dp.GradBuckets inside model.GraphStep).
+the same base and adapter, the step captured as one CUDA graph with the gradient exchange captured in it
+(dp.GradBuckets inside model.GraphStep): per-layer all-reduces on a side stream, or one all-reduce after the
+backward (the bench's default).
 
 Checked: the gradient each rank holds after a captured step with the exchange equals the mean of the two
 ranks' own eager gradients (exchanged with a plain all-gather), and after steps with AdamW inside the graph
@@ -24,7 +25,7 @@ def _port():
     return p
 
 
-def _rank(rank, world, port, out):
+def _rank(rank, world, port, out, overlap):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
@@ -52,7 +53,7 @@ def _rank(rank, world, port, out):
         mean = sum(both) / world
         ad.g.zero_()
         # the eager exchange once (collectives and buffers set up outside any capture)
-        buckets = GradBuckets(ad.g, ad.layer_ranges)
+        buckets = GradBuckets(ad.g, ad.layer_ranges, overlap=overlap)
         step.grad_hook = buckets.ready
         step.run(ids[0])
         buckets.join()
@@ -81,7 +82,8 @@ def _rank(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def test_two_rank_captured_exchange():
+@pytest.mark.parametrize("overlap", [True, False])
+def test_two_rank_captured_exchange(overlap):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
@@ -89,7 +91,7 @@ def test_two_rank_captured_exchange():
     with ctx.Manager() as m:
         out = m.dict()
         port = _port()
-        procs = [ctx.Process(target=_rank, args=(r, 2, port, out)) for r in range(2)]
+        procs = [ctx.Process(target=_rank, args=(r, 2, port, out, overlap)) for r in range(2)]
         for p in procs:
             p.start()
         for p in procs:
