@@ -374,6 +374,8 @@ def profile_case(case: str) -> None:
     gemm, gemm_dx   the config-5 gate_up forward GEMM (8192 x 24576 x 4096) / its input adjoint (B MN-major)
     gemm_swiglu     the gate_up forward as the step runs it: LoRA tail, SwiGLU in the epilogue
     gemm_swiglu_bwd the down projection's input adjoint with SwiGLU's adjoint in the epilogue (B MN-major)
+    gemm_i8         the w8a8 trunk's int8 products at config-5 shapes: gemm_nt_q (8192 x 4096 x 4096) and the
+                    gated fold with its Hadamard quantiser (8192 x 24576 x 4096), with CUDA-event timings
     gdn             one config-5 GDN layer, forward + backward
     decode          the IQR decode of a 24576 x 4096 weight
     norms / gnorm   rmsnorm fwd/bwd at 8192 x 4096 / gated rmsnorm at 8192 tokens x 32 heads x 128
@@ -425,6 +427,27 @@ def profile_case(case: str) -> None:
         ms = ev[0].elapsed_time(ev[1])
         print(f"down-projection dX + SwiGLU adjoint {M} x {F} x {K + r}: {ms * 1e3:.1f} us, "
               f"{2 * M * F * (K + r) / ms / 1e9:.0f} TFLOP/s (third launch)")
+    elif case == "gemm_i8":
+        from r97training_b200 import ops
+        M, K = 8192, 4096
+        a = torch.randint(-127, 128, (M, K), device=dev, dtype=torch.int8)
+        sa = torch.rand(M, K // 128, device=dev) * 0.01
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        for N, gated in ((4096, False), (24576, True)):
+            b = torch.randint(-127, 128, (N, K), device=dev, dtype=torch.int8)
+            sb = torch.rand(N, K // 128, device=dev) * 0.002
+            y = None if gated else torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            for _ in range(3):
+                ev[0].record()
+                if gated:
+                    ops.gemm_i8g_gated(a, sa, b, sb)
+                else:
+                    ops.gemm_i8g(a, sa, b, sb, y=y)
+                ev[1].record()
+            torch.cuda.synchronize()
+            ms = ev[0].elapsed_time(ev[1])
+            print(f"int8 {'gated fold' if gated else 'gemm_nt_q'} {M} x {N} x {K}: {ms * 1e3:.1f} us, "
+                  f"{2 * M * N * K / ms / 1e9:.0f} TOP/s (third launch)")
     elif case in ("gemm", "gemm_dx"):
         from r97training_b200 import ops
         M, N, K = 8192, 24576, 4096

@@ -541,6 +541,27 @@ int r97b_quant_act_i8g_bwd(const uint16_t* x, int64_t ldx, int64_t rows, int64_t
                            const float* scale, const float* g, int64_t ldg, float* dx, int64_t lddx,
                            int32_t accumulate, void* stream);
 
+/* ---- the w8a8 trunk's int8 product (tcgen05 kind::i8), groups of 128 along K ----
+ * y[m, n] = sum_g a_scale[m, g] b_scale[n, g] sum_{k in g} a[m, k] b[n, k]: gemm_nt_q at dtype i8a8h
+ * (reference src/adjoint/host/linear.cpp:246-282; its device row src/adjoint/device/linear.hip:748-760 serves
+ * group 128 only). a: int8 [M, K] (pitch lda), b: int8 [N, K] (pitch ldb), both 16-byte aligned with K, lda,
+ * ldb multiples of 16; a_scale: f32 [M, ceil(K / 128)] (pitch ld_as), b_scale: f32 [N, ceil(K / 128)]
+ * (pitch ld_bs). y: [M, N] (pitch ldy, N and ldy multiples of 4), f32, or bf16 when y_bf16 (16- / 8-byte
+ * aligned). Products accumulate exactly in s32 per group and in f32 across groups. */
+int r97b_gemm_i8g(const int8_t* a, int64_t lda, const float* a_scale, int64_t ld_as, const int8_t* b, int64_t ldb,
+                  const float* b_scale, int64_t ld_bs, int64_t M, int64_t N, int64_t K, void* y, int64_t ldy,
+                  int32_t y_bf16, void* stream);
+/* The gated narrow fold, gemm_nt_q_gated (reference src/adjoint/host/gemm_nt_q_gated.cpp:11-14, 256-320): the
+ * same product over b = [gate rows; up rows] (N = 2 n, n a multiple of 128), p[m, j] = act(z[m, j]) z[m, n + j]
+ * (act: silu, or the sigmoid when act_sigmoid), and per 128-wide group of p the rotated quantiser of
+ * had_quant_act_i8g: v = W p, s = amax|v| / 127 (1 for an all-zero group), q = rint(clamp(v / s, +-127)).
+ * q: int8 [M, n] (pitch ldq, a multiple of 4, 4-byte aligned); q_scale: f32 [M, n / 128] (pitch ld_qs);
+ * out_bf16: the unrotated p as bf16 [M, n] (pitch ld_ob, a multiple of 4, 8-byte aligned), or null. */
+int r97b_gemm_i8g_gated(const int8_t* a, int64_t lda, const float* a_scale, int64_t ld_as, const int8_t* b,
+                        int64_t ldb, const float* b_scale, int64_t ld_bs, int64_t M, int64_t N, int64_t K,
+                        int32_t act_sigmoid, int8_t* q, int64_t ldq, float* q_scale, int64_t ld_qs,
+                        uint16_t* out_bf16, int64_t ld_ob, void* stream);
+
 /* How many kernels this library has launched in this process (a diagnostic for the bench). */
 uint64_t r97b_launch_count(void);
 

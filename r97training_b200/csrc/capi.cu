@@ -43,7 +43,7 @@ bool smem_opt_in(const void* fn, int bytes) {
 
 extern "C" uint64_t r97b_launch_count(void) { return r97b::g_launches.load(std::memory_order_relaxed); }
 
-extern "C" int r97b_abi_version(void) { return 5; }
+extern "C" int r97b_abi_version(void) { return 6; }
 
 // The CUDA error (cudaError_t) behind the most recent R97B_ELAUNCH, and its name; 0 / "cudaSuccess" when
 // none has occurred since the last read, which clears it.
@@ -52,7 +52,7 @@ extern "C" const char* r97b_launch_error_name(int code) { return cudaGetErrorNam
 
 extern "C" int r97b_device_error(unsigned int* out_bits) {
     unsigned bits = r97b::gemm_error_word() | r97b::attn_error_word() | r97b::attn_fwd_error_word() |
-                    r97b::gdn_error_word() | r97b::loss_error_word();
+                    r97b::gdn_error_word() | r97b::loss_error_word() | r97b::gemm_i8_error_word();
     if (out_bits) *out_bits = bits;
     return cudaGetLastError() == cudaSuccess ? R97B_OK : R97B_ELAUNCH;
 }

@@ -38,6 +38,7 @@ unsigned attn_error_word();
 unsigned attn_fwd_error_word();
 unsigned gdn_error_word();
 unsigned loss_error_word();
+unsigned gemm_i8_error_word();
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

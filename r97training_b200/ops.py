@@ -496,3 +496,32 @@ def quant_act_i8g_bwd(x, group, scale, g, rotate=True, dx=None, accumulate=False
                                        _ptr(g), g.stride(0), _ptr(dx), dx.stride(0), 1 if accumulate else 0,
                                        _stream(stream)), "r97b_quant_act_i8g_bwd")
     return dx
+
+
+def gemm_i8g(a, a_scale, b, b_scale, out_dtype=torch.float32, y=None, stream=None):
+    """The w8a8 trunk's int8 product (gemm_nt_q at i8a8h): a int8 [M, K], b int8 [N, K], a_scale f32
+    [M, ceil(K / 128)], b_scale f32 [N, ceil(K / 128)] -> y [M, N] = sum_g sa sb (a_g . b_g), f32 or bf16."""
+    M, K = a.shape
+    N = b.shape[0]
+    if y is None:
+        y = torch.empty((M, N), dtype=out_dtype, device=a.device)
+    check(lib().r97b_gemm_i8g(_ptr(a), a.stride(0), _ptr(a_scale), a_scale.stride(0), _ptr(b), b.stride(0),
+                              _ptr(b_scale), b_scale.stride(0), M, N, K, _ptr(y), y.stride(0),
+                              1 if y.dtype == torch.bfloat16 else 0, _stream(stream)), "r97b_gemm_i8g")
+    return y
+
+
+def gemm_i8g_gated(a, a_scale, b, b_scale, act="silu", want_bf16=False, stream=None):
+    """The gated narrow fold (gemm_nt_q_gated): b int8 [2 n, K] = [gate; up] -> (q int8 [M, n], scale f32
+    [M, n / 128], and the unrotated product bf16 [M, n] when want_bf16, else None)."""
+    M, K = a.shape
+    N = b.shape[0]
+    n = N // 2
+    q = torch.empty((M, n), dtype=torch.int8, device=a.device)
+    qs = torch.empty((M, max(1, n // 128)), dtype=torch.float32, device=a.device)
+    ob = torch.empty((M, n), dtype=torch.bfloat16, device=a.device) if want_bf16 else None
+    check(lib().r97b_gemm_i8g_gated(_ptr(a), a.stride(0), _ptr(a_scale), a_scale.stride(0), _ptr(b), b.stride(0),
+                                    _ptr(b_scale), b_scale.stride(0), M, N, K, 1 if act == "sigmoid" else 0,
+                                    _ptr(q), q.stride(0), _ptr(qs), qs.stride(0), _ptr(ob),
+                                    ob.stride(0) if ob is not None else 0, _stream(stream)), "r97b_gemm_i8g_gated")
+    return q, qs, ob
