@@ -541,6 +541,13 @@ int r97b_quant_act_i8g_bwd(const uint16_t* x, int64_t ldx, int64_t rows, int64_t
                            const float* scale, const float* g, int64_t ldg, float* dx, int64_t lddx,
                            int32_t accumulate, void* stream);
 
+/* y[r, c] = x[r, c] s[r, c / group]: f32 x [rows, cols] (pitch ldx), f32 s [rows, ceil(cols / group)] (pitch
+ * lds), y [rows, cols] (pitch ldy) f32 (may be x) or bf16 when y_bf16. The group scales of the int8 trunk's
+ * products on a float operand or result: the dequantised weight code[n, k] b_scale[n, k / 128] and the
+ * activation scale a dX takes (reference src/adjoint/host/linear.cpp:286-317, gemm_nt_q_adjoint). */
+int r97b_group_scale(const float* x, int64_t ldx, int64_t rows, int64_t cols, int64_t group, const float* s,
+                     int64_t lds, void* y, int64_t ldy, int32_t y_bf16, void* stream);
+
 /* ---- the w8a8 trunk's int8 product (tcgen05 kind::i8), groups of 128 along K ----
  * y[m, n] = sum_g a_scale[m, g] b_scale[n, g] sum_{k in g} a[m, k] b[n, k]: gemm_nt_q at dtype i8a8h
  * (reference src/adjoint/host/linear.cpp:246-282; its device row src/adjoint/device/linear.hip:748-760 serves

@@ -244,6 +244,19 @@ __global__ void __launch_bounds__(256) quant_plain_bwd_kernel(QuantArgs a, const
     dx[r * lddx + c] = d;
 }
 
+// y[r, c] = x[r, c] s[r, c / group], f32 in, f32 or bf16 out (y may be x for f32): the group scales of the
+// int8 trunk's products applied to a float operand or result.
+__global__ void __launch_bounds__(256) group_scale_kernel(const float* __restrict__ x, int64_t ldx, int64_t rows,
+                                                          int64_t cols, int64_t group, const float* __restrict__ s,
+                                                          int64_t lds, void* y, int64_t ldy, int y_bf16) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows * cols) return;
+    const int64_t r = i / cols, c = i % cols;
+    const float v = x[r * ldx + c] * s[r * lds + c / group];
+    if (y_bf16) reinterpret_cast<__nv_bfloat16*>(y)[r * ldy + c] = __float2bfloat16_rn(v);
+    else reinterpret_cast<float*>(y)[r * ldy + c] = v;
+}
+
 unsigned blocks_of_warps(int64_t warps) { return (unsigned)((warps * 32 + 255) / 256); }
 
 // One block a row and 8 chunks of `cols` columns.
@@ -334,5 +347,18 @@ extern "C" int r97b_quant_act_i8g_bwd(const uint16_t* x, int64_t ldx, int64_t ro
     } else {
         return R97B_EINVAL;
     }
+    return launch_status();
+}
+
+extern "C" int r97b_group_scale(const float* x, int64_t ldx, int64_t rows, int64_t cols, int64_t group, const float* s,
+                                int64_t lds, void* y, int64_t ldy, int32_t y_bf16, void* stream) {
+    if (!x || !s || !y || rows < 0 || cols < 0 || group <= 0 || ldx < cols || ldy < cols ||
+        lds < (cols + group - 1) / group)
+        return R97B_EINVAL;
+    if (rows == 0 || cols == 0) return R97B_OK;
+    const int64_t blocks = (rows * cols + 255) / 256;
+    if (blocks > INT32_MAX) return R97B_EINVAL;
+    group_scale_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(x, ldx, rows, cols, group, s, lds, y, ldy,
+                                                                        y_bf16 ? 1 : 0);
     return launch_status();
 }

@@ -1,5 +1,6 @@
-// rows_linear.cpp -- device adjoint rows of the frozen linear and its LoRA branch: gemm_nt, lora_shrink
-// (the float-trunk form) and lora_expand / lora_expand_mm, on the tcgen05 GEMM of libr97b200.so.
+// rows_linear.cpp -- device adjoint rows of the frozen linear and its LoRA branch: gemm_nt, gemm_nt_q (the
+// int8 trunk's form at i8a8h), lora_shrink (the float-trunk form) and lora_expand / lora_expand_mm, on the
+// tcgen05 GEMM of libr97b200.so.
 //
 // The arithmetic each row serves is the reference's host row's (src/adjoint/host/linear.cpp:193-243,
 // src/adjoint/host/lora.cpp:226-523): operands are rounded to bf16 on the way in (the dtype the GEMM
@@ -8,6 +9,7 @@
 // (src/adjoint/device/lora.hip:125-154), under the names the host rows give them.
 #include "common.h"
 
+#include <algorithm>
 #include <cmath>
 
 namespace r97b_host {
@@ -64,6 +66,94 @@ void gemm_nt_device(const AdjointCall& call) {
     DevBuf out(M * ldK * 4);
     // D[M, K] = dY[M, N] . W^T where the GEMM's B operand is W read MN-major ([N, K] = [reduction, cols])
     gemm_f32(M, K, N, Opnd{d.get(), ldN, false}, Opnd{w.get(), ldK, true}, out.as<float>(), ldK, false);
+    add_f32(dx.value.data(), out, M, K, ldK);
+}
+
+// ------------------------------------------------------------------------------------------ gemm_nt_q
+
+// The group scale of `rows` rows over `groups` K blocks as a dense [rows, groups] array, by the host rows'
+// rule for reading one (reference linear.cpp:101-111 scale_at): per (row, block), per block, per row, one
+// for the whole operand, or 1 when absent. An index selection only.
+std::vector<double> dense_scale(const AdValue* s, int64_t rows, int64_t groups) {
+    std::vector<double> out((size_t)(rows * groups), 1.0);
+    if (s == nullptr || s->value.empty()) return out;
+    const int64_t n = (int64_t)s->value.size();
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t g = 0; g < groups; ++g) {
+            int64_t at;
+            if (n == 1) at = 0;
+            else if (n == rows * groups) at = r * groups + g;
+            else if (n == groups) at = g;
+            else if (n == rows) at = r;
+            else at = std::min<int64_t>(r * groups + g, n - 1);
+            out[(size_t)(r * groups + g)] = s->value[(size_t)at];
+        }
+    return out;
+}
+
+// The int8 trunk's linear at dtype i8a8h with the device's K block of 128 (reference
+// src/adjoint/device/linear.hip:748-751 serves_i8a8h).
+bool serves_i8a8h(const std::vector<OpParam>& params) {
+    bool dtype = false, group = false;
+    for (const OpParam& p : params) {
+        if (p.first == "dtype") {
+            const auto* d = std::get_if<std::string>(&p.second);
+            dtype = d && *d == "i8a8h";
+        } else if (p.first == "group") {
+            const auto* g = std::get_if<int64_t>(&p.second);
+            group = g && *g == 128;
+        }
+    }
+    return dtype && group;
+}
+
+// dX[M, K] += s_a[m, k / 128] (dY W)[m, k], W[n, k] = b[n, k] s_b[n, k / 128] -- the cotangent in the codes'
+// activation basis that the upstream quantiser consumes (reference linear.cpp:286-317 gemm_nt_q_adjoint; the
+// device row linear.hip:461-665). The weight is dequantised on the device: a stored one from its decoded
+// codes and bf16 scale, a values one from the tape's codes and b_scale; dY enters as bf16, the product
+// accumulates in f32 and the activation's group scale is applied to it before the f64 add.
+void gemm_nt_q_device(const AdjointCall& call) {
+    if (!call.dc || call.cot.empty()) return;
+    const int ia = operand_pos(call.rec, "a"), ib = operand_pos(call.rec, "b");
+    const int ias = operand_pos(call.rec, "a_scale"), ibs = operand_pos(call.rec, "b_scale");
+    if (ia < 0 || ib < 0 || (size_t)ia >= call.dc->size()) return;
+    const AdValue& a = call.fwd[(size_t)ia];
+    const AdValue& b = call.fwd[(size_t)ib];
+    const AdValue* as = ias >= 0 ? &call.fwd[(size_t)ias] : nullptr;
+    const AdValue* bs = ibs >= 0 ? &call.fwd[(size_t)ibs] : nullptr;
+    const AdValue& dy = call.cot[0];
+    const int64_t K = int_param(call.rec, "K", a.shape.size() >= 2 ? a.shape[1] : 0);
+    const int64_t N = int_param(call.rec, "N", b.shape.size() >= 2 ? b.shape[0] : 0);
+    const int64_t M = a.shape.empty() ? int_param(call.rec, "M", 0) : a.shape[0];
+    const int64_t group = int_param(call.rec, "group", 128);
+    AdValue& dx = (*call.dc)[(size_t)ia];
+    if (M <= 0 || N <= 0 || K <= 0 || group != 128 || (int64_t)dy.value.size() != M * N ||
+        (int64_t)dx.value.size() != M * K)
+        return;
+    const int64_t G = (K + group - 1) / group;
+    const int64_t ldN = round_up(N, kPad), ldK = round_up(K, kPad);
+    DevBuf w;
+    if (b.raw != nullptr) {
+        w = weight_operand(call, ib, N, K, ldK);
+    } else {
+        if ((int64_t)b.value.size() != N * K) return;
+        DevBuf codes = upload_f32(b.value.data(), N, K, ldK);
+        const std::vector<double> sb = dense_scale(bs, N, G);
+        DevBuf sbd = upload_f32(sb.data(), N, G, G);
+        w = DevBuf(N * ldK * 2);
+        w.zero();
+        check(r97b_group_scale(codes.as<float>(), ldK, N, K, group, sbd.as<float>(), G, w.get(), ldK, 1,
+                               row_stream()),
+              "weight group scale");
+    }
+    if (!w.get()) return;
+    DevBuf d = upload_bf16(dy.value.data(), M, N, ldN);
+    DevBuf out(M * ldK * 4);
+    gemm_f32(M, K, N, Opnd{d.get(), ldN, false}, Opnd{w.get(), ldK, true}, out.as<float>(), ldK, false);
+    const std::vector<double> sa = dense_scale(as, M, G);
+    DevBuf sad = upload_f32(sa.data(), M, G, G);
+    check(r97b_group_scale(out.as<float>(), ldK, M, K, group, sad.as<float>(), G, out.get(), ldK, 0, row_stream()),
+          "activation group scale");
     add_f32(dx.value.data(), out, M, K, ldK);
 }
 
@@ -226,6 +316,7 @@ void lora_expand_device(const AdjointCall& call) {
 void register_linear_rows() {
     if (!r97::adjoint_register) return;
     r97::adjoint_register("gemm_nt", r97::Side::device, gemm_nt_device, {1}, nullptr);
+    r97::adjoint_register("gemm_nt_q", r97::Side::device, gemm_nt_q_device, {1, 2, 3}, serves_i8a8h);
     // the float-trunk form only: a coded record finds no device row here and the walk runs the host's
     r97::adjoint_register("lora_shrink", r97::Side::device, lora_shrink_device, {1, 2, 3}, float_act);
     r97::adjoint_register("lora_expand", r97::Side::device, lora_expand_device, {1, 2, 3}, nullptr);

@@ -1,7 +1,8 @@
 """The drop-in boundary on the GPU: every device adjoint row the plugin (libr97host.so) registers into the
 reference's own registry, run through that registry exactly as the reference's walk would find it
 (adjoint_find(op, Side::device)), against the reference's own f64 host row for the same record. The bar is
-the north star's: per-tensor relative L2 <= 1e-2 and cosine >= 0.999 for every cotangent and gradient.
+the north star's: per-tensor relative L2 <= 1e-2 and cosine >= 0.999 for every cotangent and gradient
+(gemm_nt_q at i8a8h included).
 Also the plugin's HeadCeKernel against the reference's ce_position."""
 import ctypes
 
@@ -57,6 +58,29 @@ def test_gemm_nt_device_row(cuda, stored):
     (hdc, _), (ddc, _) = both("gemm_nt", params, ops, fwd, {"y": dy})
     assert np.abs(hdc["a"]).max() > 0
     assert_parity(ddc["a"], hdc["a"], "gemm_nt dX")
+
+
+@pytest.mark.parametrize("stored", [False, True])
+def test_gemm_nt_q_device_row(cuda, stored):
+    """The int8 trunk's linear at i8a8h: dX = s_a (dY W) with W the codes times their group scale -- the
+    tape's b_scale for a values weight, the stored plane's own bf16 scale for a stored one."""
+    M, N, K = 96, 384, 384
+    G = K // 128
+    rs = np.random.RandomState(4)
+    a = rs.randint(-127, 128, size=(M, K)).astype(np.float64)
+    sa = np.abs(rs.normal(size=(M, G))) * 0.01 + 1e-4
+    dy = bf16_round(rs.normal(size=(M, N)) * 1e-2)
+    codes, sbits = _stored_weight(N, K, 5)
+    sb = R.bf16_bits_to_f64(sbits) if stored else np.abs(rs.normal(size=(N, G))) * 0.002 + 1e-5
+    b = Operand("b", "iqr", (N, K), stored=(codes, sbits)) if stored else Operand("b", "i8", (N, K))
+    ops = [Operand("a", "i8", (M, K)), Operand("a_scale", "f32", (M, G)), b, Operand("b_scale", "f32", (N, G)),
+           Operand("y", "bf16", (M, N), written=True)]
+    params = {"M": M, "N": N, "K": K, "group": 128, "dtype": "i8a8h"}
+    fwd = {"a": a, "a_scale": sa, "b": None if stored else codes.astype(np.float64), "b_scale": sb,
+           "y": np.zeros((M, N))}
+    (hdc, _), (ddc, _) = both("gemm_nt_q", params, ops, fwd, {"y": dy})
+    assert np.abs(hdc["a"]).max() > 0
+    assert_parity(ddc["a"], hdc["a"], "gemm_nt_q dX")
 
 
 @pytest.mark.parametrize("fused", [False, True])

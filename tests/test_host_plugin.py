@@ -12,11 +12,13 @@ import oracle
 from r97training_b200 import build as B
 from tests.plugin_util import plugin
 
-# op -> the frozen operand positions the reference registers for it (reference linear.cpp:444-457,
+# op -> the frozen operand positions the reference registers for it (reference linear.cpp:444-457 and
+# device/linear.hip:760,
 # lora.cpp:534-538, gdn_kkt.cpp:355, gdn_scan.cpp:584, gdn_prep.cpp:597-600, elementwise.cpp:687; the quant
 # family's two int8 ops have none, quant.cpp)
 FROZEN = {
     "gemm_nt": [1],
+    "gemm_nt_q": [1, 2, 3],
     "lora_shrink": [1, 2, 3],
     "lora_expand": [1, 2, 3],
     "lora_expand_mm": [1, 2, 3],
