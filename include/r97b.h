@@ -541,6 +541,32 @@ int r97b_quant_act_i8g_bwd(const uint16_t* x, int64_t ldx, int64_t rows, int64_t
                            const float* scale, const float* g, int64_t ldg, float* dx, int64_t lddx,
                            int32_t accumulate, void* stream);
 
+/* ---- the int8 trunk's fused producers: an elementwise part, then the rotated quantiser above over the part's
+ * f32 value (reference src/adjoint/host/quant.cpp:821-1100, rmsnorm_had_quant_i8g / gated_had_quant_i8g /
+ * gate_had_quant_i8g; device src/adjoint/device/quant.hip) ----
+ * part R97B_PART_RMSNORM:     v = x s (w + wadd) mult, s = 1 / sqrt(mean(x^2) + eps); x bf16 [rows, n], w f32
+ *                             [n] or null (then wadd must be 0)
+ * part R97B_PART_SILU_MUL:    v = silu(g) u; x = gate_up bf16 [rows, 2 n] (pitch ldx >= 2 n), the gate first
+ * part R97B_PART_SIGMOID_MUL: v = sigmoid(a) b; x = a, x2 = b, bf16 [rows, n]
+ * codes: int8 [rows, n] (pitch ldc, a multiple of 8, 8-byte aligned); scale: f32 [rows, n / group] (pitch lds);
+ * out: v as bf16 [rows, n] (pitch ldo, a multiple of 8, 16-byte aligned) or null. group: a power of two of at
+ * most 256 dividing n; n a multiple of 8; x / x2 rows 16-byte aligned. */
+enum { R97B_PART_RMSNORM = 0, R97B_PART_SILU_MUL = 1, R97B_PART_SIGMOID_MUL = 2 };
+int r97b_fused_quant_i8g(int32_t part, const uint16_t* x, int64_t ldx, const uint16_t* x2, int64_t ldx2,
+                         const float* w, float eps, float wadd, float mult, int64_t rows, int64_t n, int64_t group,
+                         int8_t* codes, int64_t ldc, float* scale, int64_t lds, uint16_t* out, int64_t ldo,
+                         void* stream);
+/* Their adjoint: dv = W (m . g / s) + g_out (m = 0 where |v / s| > 127, v recomputed; g the codes' cotangent
+ * f32 [rows, n], g_out the `out` write's or null), then the part's adjoint into dx (rmsnorm: dx [rows, n];
+ * silu_mul: d gate_up [rows, 2 n]; sigmoid mul: da in dx, db in dx2), written or added to when `accumulate`.
+ * The gain is not differentiated (the record's frozen operand). g, g_out, dx, dx2 rows 16-byte aligned (pitches
+ * multiples of 4); the rmsnorm part takes n <= 16384. */
+int r97b_fused_quant_i8g_bwd(int32_t part, const uint16_t* x, int64_t ldx, const uint16_t* x2, int64_t ldx2,
+                             const float* w, float eps, float wadd, float mult, int64_t rows, int64_t n,
+                             int64_t group, const float* scale, int64_t lds, const float* g, int64_t ldg,
+                             const float* g_out, int64_t ldgo, float* dx, int64_t lddx, float* dx2, int64_t lddx2,
+                             int32_t accumulate, void* stream);
+
 /* y[r, c] = x[r, c] s[r, c / group]: f32 x [rows, cols] (pitch ldx), f32 s [rows, ceil(cols / group)] (pitch
  * lds), y [rows, cols] (pitch ldy) f32 (may be x) or bf16 when y_bf16. The group scales of the int8 trunk's
  * products on a float operand or result: the dequantised weight code[n, k] b_scale[n, k / 128] and the

@@ -95,6 +95,11 @@ _SIGS = {
     "r97b_quant_act_i8g": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp, c_i64, c_vp, c_vp]),
     "r97b_quant_act_i8g_bwd": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_i64, c_vp, c_i64,
                                        c_i32, c_vp]),
+    "r97b_fused_quant_i8g": (c_i32, [c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_f32, c_f32, c_f32, c_i64, c_i64, c_i64,
+                                     c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp]),
+    "r97b_fused_quant_i8g_bwd": (c_i32, [c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_f32, c_f32, c_f32, c_i64, c_i64,
+                                         c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i32,
+                                         c_vp]),
     "r97b_group_scale": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_i32, c_vp]),
     "r97b_gemm_i8g": (c_i32, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64,
                               c_i32, c_vp]),

@@ -257,6 +257,218 @@ __global__ void __launch_bounds__(256) group_scale_kernel(const float* __restric
     else reinterpret_cast<float*>(y)[r * ldy + c] = v;
 }
 
+// ------------------------------------------------------------------------ the fused int8 producers
+// rmsnorm_had_quant_i8g, gated_had_quant_i8g, gate_had_quant_i8g (reference src/adjoint/host/quant.cpp:821-1100,
+// fused_twin / fused_adjoint): an elementwise part, then the rotated quantiser above over the part's f32 value,
+// which is also stored as bf16 when the caller asks (the record's `out` write):
+//   part 0  rmsnorm      v = x s (w + wadd) mult, s = 1 / sqrt(mean(x^2) + eps)  (elementwise.cpp:459-530)
+//   part 1  silu_mul     v = silu(g) u, g and u the halves of one [rows, 2 n] row  (elementwise.cpp:278-293)
+//   part 2  sigmoid mul  v = sigmoid(a) b                                          (act_mul, act "sigmoid")
+// The adjoint recomputes v, takes the codes' cotangent straight through (masked where |v / s| > 127, over s,
+// rotated back), adds the `out` write's cotangent, and then applies the part's adjoint:
+//   rmsnorm  dx_j = mult (s c_j dv_j - (s^3 x_j / n) sum_i dv_i x_i c_i), c = w + wadd   (elementwise.cpp:531-541)
+//   silu_mul dg = dv u silu'(g), du = dv silu(g);   sigmoid mul da = dv b sig'(a), db = dv sig(a)
+// One CTA a row, a warp a 256-column chunk (8 columns a lane, the rotation's stages below 8 in-lane, the rest
+// shuffles); the rmsnorm adjoint holds the row's dv in shared memory between its two passes.
+struct FusedArgs {
+    int part;
+    const __nv_bfloat16* x;
+    int64_t ldx;
+    const __nv_bfloat16* x2;
+    int64_t ldx2;
+    const float* w;
+    float eps, wadd, mult;
+    int64_t n;
+    int t, lt;
+};
+
+__device__ __forceinline__ float silu_of(float g) { return g / (1.0f + __expf(-g)); }
+__device__ __forceinline__ float sig_of(float a) { return 1.0f / (1.0f + __expf(-a)); }
+
+// The row's rmsnorm factor 1 / sqrt(mean(x^2) + eps), every thread of the block.
+__device__ float row_rstd(const FusedArgs& a, int64_t r, float* red) {
+    float ss = 0.0f;
+    for (int64_t c = (int64_t)threadIdx.x * 8; c < a.n; c += 256 * 8) {
+        float x[8];
+        load_bf16<8>(a.x + r * a.ldx + c, x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) ss = fmaf(x[i], x[i], ss);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xFFFFFFFFu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    __syncthreads();
+    return 1.0f / sqrtf(tot / (float)a.n + a.eps);
+}
+
+// The part's inputs and value at columns c0 .. c0 + 7 of row r: p = x (part 0), the gate (1), a (2); u = the
+// up half (1), b (2).
+__device__ __forceinline__ void part_value(const FusedArgs& a, int64_t r, int64_t c0, float rstd, float (&p)[8],
+                                           float (&u)[8], float (&v)[8]) {
+    load_bf16<8>(a.x + r * a.ldx + c0, p);
+    if (a.part == 0) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = p[i] * rstd * (a.w ? a.w[c0 + i] + a.wadd : 1.0f) * a.mult;
+    } else {
+        load_bf16<8>(a.part == 1 ? a.x + r * a.ldx + a.n + c0 : a.x2 + r * a.ldx2 + c0, u);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = (a.part == 1 ? silu_of(p[i]) : sig_of(p[i])) * u[i];
+    }
+}
+
+__device__ __forceinline__ void load8f(const float* src, float (&d)[8]) {
+    const float4 x = *reinterpret_cast<const float4*>(src), y = *reinterpret_cast<const float4*>(src + 4);
+    d[0] = x.x, d[1] = x.y, d[2] = x.z, d[3] = x.w, d[4] = y.x, d[5] = y.y, d[6] = y.z, d[7] = y.w;
+}
+__device__ __forceinline__ void store8f(float* dst, const float (&v)[8], int accumulate) {
+    float o[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i] = v[i];
+    if (accumulate) {
+        float prev[8];
+        load8f(dst, prev);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] += prev[i];
+    }
+    *reinterpret_cast<float4*>(dst) = make_float4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<float4*>(dst + 4) = make_float4(o[4], o[5], o[6], o[7]);
+}
+
+__global__ void __launch_bounds__(256) fused_quant_fwd_kernel(FusedArgs a, int8_t* __restrict__ codes, int64_t ldc,
+                                                              float* __restrict__ scale, int64_t lds,
+                                                              __nv_bfloat16* __restrict__ out, int64_t ldo) {
+    __shared__ float red[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t r = blockIdx.x;
+    const float rstd = a.part == 0 ? row_rstd(a, r, red) : 1.0f;
+    for (int64_t ch = warp; ch * 256 < a.n; ch += 8) {  // whole warps: the rotation shuffles
+        const int64_t c0 = ch * 256 + (int64_t)lane * 8;
+        const bool on = c0 < a.n;  // n % 8 == 0: a lane is all in or out
+        float p[8], u[8], v[8];
+        if (on) {
+            part_value(a, r, c0, rstd, p, u, v);
+            if (out) {
+                uint32_t w4[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const __nv_bfloat162 b2 = __floats2bfloat162_rn(v[2 * k], v[2 * k + 1]);
+                    w4[k] = *reinterpret_cast<const uint32_t*>(&b2);
+                }
+                *reinterpret_cast<uint4*>(out + r * ldo + c0) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+        }
+        fwht_warp<8>(v, a.t, lane);
+        float em[8];
+        group_amax<8>(v, a.t, em);
+        int q[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float inv = 1.0f / scale_of_amax(em[i]);
+            q[i] = __float2int_rn(fminf(fmaxf(v[i] * inv, -kTop), kTop));
+        }
+        if (!on) continue;
+        store_codes<8>(codes + r * ldc + c0, q);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (((c0 + i) & (a.t - 1)) == 0) scale[r * lds + ((c0 + i) >> a.lt)] = scale_of_amax(em[i]);
+    }
+}
+
+__global__ void __launch_bounds__(256) fused_quant_bwd_kernel(FusedArgs a, const float* __restrict__ scale,
+                                                              int64_t lds, const float* __restrict__ g, int64_t ldg,
+                                                              const float* __restrict__ go, int64_t ldgo,
+                                                              float* __restrict__ dx, int64_t lddx,
+                                                              float* __restrict__ dx2, int64_t lddx2, int accumulate) {
+    extern __shared__ float dv_row[];  // part 0: the row's dv
+    __shared__ float red[8];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t r = blockIdx.x;
+    const float rstd = a.part == 0 ? row_rstd(a, r, red) : 1.0f;
+    float dot = 0.0f;  // part 0: this thread's share of sum_i dv_i x_i c_i
+    for (int64_t ch = warp; ch * 256 < a.n; ch += 8) {
+        const int64_t c0 = ch * 256 + (int64_t)lane * 8;
+        const bool on = c0 < a.n;
+        float p[8], u[8], v[8], d[8];
+        if (on) {
+            part_value(a, r, c0, rstd, p, u, v);
+            load8f(g + r * ldg + c0, d);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) p[i] = u[i] = v[i] = d[i] = 0.0f;
+        }
+        float vr[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) vr[i] = v[i];
+        fwht_warp<8>(vr, a.t, lane);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float inv = on ? 1.0f / scale[r * lds + ((c0 + i) >> a.lt)] : 1.0f;
+            d[i] = fabsf(vr[i] * inv) > kTop ? 0.0f : d[i] * inv;
+        }
+        fwht_warp<8>(d, a.t, lane);
+        if (!on) continue;
+        if (go) {
+            float o[8];
+            load8f(go + r * ldgo + c0, o);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d[i] += o[i];
+        }
+        if (a.part == 0) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                dv_row[c0 + i] = d[i];
+                dot = fmaf(d[i] * p[i], a.w ? a.w[c0 + i] + a.wadd : 1.0f, dot);
+            }
+        } else if (a.part == 1) {
+            float dg[8], du[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float s = sig_of(p[i]);
+                dg[i] = d[i] * u[i] * (s * (1.0f + p[i] * (1.0f - s)));
+                du[i] = d[i] * (p[i] * s);
+            }
+            store8f(dx + r * lddx + c0, dg, accumulate);
+            store8f(dx + r * lddx + a.n + c0, du, accumulate);
+        } else {
+            float da[8], db[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float s = sig_of(p[i]);
+                da[i] = d[i] * u[i] * (s * (1.0f - s));
+                db[i] = d[i] * s;
+            }
+            store8f(dx + r * lddx + c0, da, accumulate);
+            store8f(dx2 + r * lddx2 + c0, db, accumulate);
+        }
+    }
+    if (a.part != 0) return;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xFFFFFFFFu, dot, o);
+    if (lane == 0) red[warp] = dot;
+    __syncthreads();  // also: the row's dv is complete
+    float S = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) S += red[i];
+    const float k2 = rstd * rstd * rstd / (float)a.n * S;
+    for (int64_t c = (int64_t)threadIdx.x * 8; c < a.n; c += 256 * 8) {
+        float x[8], o[8];
+        load_bf16<8>(a.x + r * a.ldx + c, x);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const float cg = a.w ? a.w[c + i] + a.wadd : 1.0f;
+            o[i] = a.mult * (rstd * cg * dv_row[c + i] - k2 * x[i]);
+        }
+        store8f(dx + r * lddx + c, o, accumulate);
+    }
+}
+
 unsigned blocks_of_warps(int64_t warps) { return (unsigned)((warps * 32 + 255) / 256); }
 
 // One block a row and 8 chunks of `cols` columns.
@@ -360,5 +572,64 @@ extern "C" int r97b_group_scale(const float* x, int64_t ldx, int64_t rows, int64
     if (blocks > INT32_MAX) return R97B_EINVAL;
     group_scale_kernel<<<(unsigned)blocks, 256, 0, as_stream(stream)>>>(x, ldx, rows, cols, group, s, lds, y, ldy,
                                                                         y_bf16 ? 1 : 0);
+    return launch_status();
+}
+
+namespace {
+
+// The rules both fused entry points share; fills the geometry.
+int fused_args(int32_t part, const uint16_t* x, int64_t ldx, const uint16_t* x2, int64_t ldx2, const float* w,
+               float eps, float wadd, float mult, int64_t rows, int64_t n, int64_t group, FusedArgs* a) {
+    if (part < 0 || part > 2 || !x || rows < 0 || n <= 0 || n % 8 || group <= 0 || group > 256 ||
+        (group & (group - 1)) || n % group || ldx % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+        ldx < (part == 1 ? 2 * n : n) || rows > INT32_MAX)
+        return R97B_EINVAL;
+    if (part == 2 && (!x2 || ldx2 < n || ldx2 % 8 || (reinterpret_cast<uintptr_t>(x2) & 15))) return R97B_EINVAL;
+    if (part == 0 && !w && wadd != 0.0f) return R97B_EINVAL;  // an offset without a gain (the twin refuses it)
+    a->part = part, a->x = reinterpret_cast<const __nv_bfloat16*>(x), a->ldx = ldx;
+    a->x2 = reinterpret_cast<const __nv_bfloat16*>(x2), a->ldx2 = ldx2;
+    a->w = part == 0 ? w : nullptr, a->eps = eps, a->wadd = wadd, a->mult = mult;
+    a->n = n, a->t = (int)group, a->lt = 0;
+    while ((1 << (a->lt + 1)) <= group) ++a->lt;
+    return R97B_OK;
+}
+
+bool al16(const void* p, int64_t ld) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0 && ld % 4 == 0; }
+
+}  // namespace
+
+extern "C" int r97b_fused_quant_i8g(int32_t part, const uint16_t* x, int64_t ldx, const uint16_t* x2, int64_t ldx2,
+                                    const float* w, float eps, float wadd, float mult, int64_t rows, int64_t n,
+                                    int64_t group, int8_t* codes, int64_t ldc, float* scale, int64_t lds,
+                                    uint16_t* out, int64_t ldo, void* stream) {
+    FusedArgs a{};
+    if (fused_args(part, x, ldx, x2, ldx2, w, eps, wadd, mult, rows, n, group, &a) != R97B_OK) return R97B_EINVAL;
+    if (!codes || !scale || ldc < n || ldc % 8 || (reinterpret_cast<uintptr_t>(codes) & 7) || lds < n / group)
+        return R97B_EINVAL;
+    if (out && (ldo < n || ldo % 8 || (reinterpret_cast<uintptr_t>(out) & 15))) return R97B_EINVAL;
+    if (rows == 0) return R97B_OK;
+    fused_quant_fwd_kernel<<<(unsigned)rows, 256, 0, as_stream(stream)>>>(
+        a, codes, ldc, scale, lds, reinterpret_cast<__nv_bfloat16*>(out), ldo);
+    return launch_status();
+}
+
+extern "C" int r97b_fused_quant_i8g_bwd(int32_t part, const uint16_t* x, int64_t ldx, const uint16_t* x2,
+                                        int64_t ldx2, const float* w, float eps, float wadd, float mult, int64_t rows,
+                                        int64_t n, int64_t group, const float* scale, int64_t lds, const float* g,
+                                        int64_t ldg, const float* g_out, int64_t ldgo, float* dx, int64_t lddx,
+                                        float* dx2, int64_t lddx2, int32_t accumulate, void* stream) {
+    FusedArgs a{};
+    if (fused_args(part, x, ldx, x2, ldx2, w, eps, wadd, mult, rows, n, group, &a) != R97B_OK) return R97B_EINVAL;
+    if (!scale || lds < n / group || !g || ldg < n || !al16(g, ldg) || !dx || !al16(dx, lddx) ||
+        lddx < (part == 1 ? 2 * n : n))
+        return R97B_EINVAL;
+    if (g_out && (ldgo < n || !al16(g_out, ldgo))) return R97B_EINVAL;
+    if (part == 2 && (!dx2 || lddx2 < n || !al16(dx2, lddx2))) return R97B_EINVAL;
+    const int smem = part == 0 ? (int)(n * 4) : 0;
+    if (part == 0 && n > 16384) return R97B_EINVAL;
+    if (rows == 0) return R97B_OK;
+    if (smem > 48 * 1024 && !smem_opt_in(fused_quant_bwd_kernel, smem)) return R97B_ELAUNCH;
+    fused_quant_bwd_kernel<<<(unsigned)rows, 256, smem, as_stream(stream)>>>(a, scale, lds, g, ldg, g_out, ldgo, dx,
+                                                                             lddx, dx2, lddx2, accumulate ? 1 : 0);
     return launch_status();
 }

@@ -525,3 +525,40 @@ def gemm_i8g_gated(a, a_scale, b, b_scale, act="silu", want_bf16=False, stream=N
                                     _ptr(q), q.stride(0), _ptr(qs), qs.stride(0), _ptr(ob),
                                     ob.stride(0) if ob is not None else 0, _stream(stream)), "r97b_gemm_i8g_gated")
     return q, qs, ob
+
+
+FUSED_PARTS = {"rmsnorm": 0, "silu_mul": 1, "sigmoid_mul": 2}
+
+
+def fused_quant_i8g(part, x, group, x2=None, w=None, eps=1e-6, wadd=0.0, mult=1.0, want_out=True, stream=None):
+    """The int8 trunk's fused producers (rmsnorm / silu_mul / sigmoid_mul, then the rotated quantiser): x bf16
+    [rows, n] (gate_up [rows, 2 n] for silu_mul), x2 bf16 [rows, n] (sigmoid_mul's b), w f32 [n] (rmsnorm's
+    gain) -> (codes int8 [rows, n], scale f32 [rows, n / group], the part's value bf16 [rows, n] or None)."""
+    pid = FUSED_PARTS[part]
+    rows = x.shape[0]
+    n = x.shape[1] // 2 if pid == 1 else x.shape[1]
+    codes = torch.empty((rows, n), dtype=torch.int8, device=x.device)
+    scale = torch.empty((rows, n // group), dtype=torch.float32, device=x.device)
+    out = torch.empty((rows, n), dtype=torch.bfloat16, device=x.device) if want_out else None
+    check(lib().r97b_fused_quant_i8g(pid, _ptr(x), x.stride(0), _ptr(x2), x2.stride(0) if x2 is not None else 0,
+                                     _ptr(w), eps, wadd, mult, rows, n, group, _ptr(codes), codes.stride(0),
+                                     _ptr(scale), scale.stride(0), _ptr(out), out.stride(0) if out is not None else 0,
+                                     _stream(stream)), "r97b_fused_quant_i8g")
+    return codes, scale, out
+
+
+def fused_quant_i8g_bwd(part, x, group, scale, g, g_out=None, x2=None, w=None, eps=1e-6, wadd=0.0, mult=1.0,
+                        stream=None):
+    """Its adjoint: the codes' cotangent g (f32 [rows, n]) and the part value's g_out -> dx (f32, x's shape) and,
+    for sigmoid_mul, db (f32 [rows, n]); returns (dx, db or None)."""
+    pid = FUSED_PARTS[part]
+    rows = x.shape[0]
+    n = x.shape[1] // 2 if pid == 1 else x.shape[1]
+    dx = torch.zeros((rows, x.shape[1]), dtype=torch.float32, device=x.device)
+    dx2 = torch.zeros((rows, n), dtype=torch.float32, device=x.device) if pid == 2 else None
+    check(lib().r97b_fused_quant_i8g_bwd(pid, _ptr(x), x.stride(0), _ptr(x2), x2.stride(0) if x2 is not None else 0,
+                                         _ptr(w), eps, wadd, mult, rows, n, group, _ptr(scale), scale.stride(0),
+                                         _ptr(g), g.stride(0), _ptr(g_out), g_out.stride(0) if g_out is not None else 0,
+                                         _ptr(dx), dx.stride(0), _ptr(dx2), dx2.stride(0) if dx2 is not None else 0,
+                                         0, _stream(stream)), "r97b_fused_quant_i8g_bwd")
+    return dx, dx2

@@ -83,6 +83,34 @@ def test_gemm_nt_q_device_row(cuda, stored):
     assert_parity(ddc["a"], hdc["a"], "gemm_nt_q dX")
 
 
+@pytest.mark.parametrize("part", ["rmsnorm", "silu_mul", "sigmoid_mul"])
+def test_fused_quant_device_rows(cuda, part):
+    """The int8 trunk's fused producers (rmsnorm_had_quant_i8g, gated_had_quant_i8g, gate_had_quant_i8g) on the
+    records the reference's own quant test builds, with the `out` write's cotangent beside the codes'."""
+    from tests.test_gpu_quant_fused import OPS, _near_clamp, _record
+    rows, n, group = 24, 512, 128
+    params, ops = _record(part, rows, n, group, 1 if part == "rmsnorm" else 0)
+    rs = np.random.RandomState(9)
+    if part == "rmsnorm":
+        host = {"x": bf16_round(rs.normal(size=(rows, n))), "w": rs.normal(size=n) * 0.1}
+    elif part == "silu_mul":
+        host = {"gate_up": bf16_round(rs.normal(size=(rows, 2 * n)) * 2.0)}
+    else:
+        host = {"a": bf16_round(rs.normal(size=(rows, n)) * 2.0), "b": bf16_round(rs.normal(size=(rows, n)))}
+    want = ref_twin(OPS[part], params, ops, host)
+    fwd = dict(host)
+    fwd.update({"codes": want["codes"], "scale": want["scale"], "out": want["out"]})
+    g = rs.normal(size=(rows, n))
+    g[_near_clamp(want["out"], want["scale"], group)] = 0.0  # the f32 and f64 masks may differ only there
+    cots = {"codes": g, "scale": np.zeros_like(want["scale"]), "out": rs.normal(size=(rows, n)) * 0.1}
+    (hdc, _), (ddc, _) = both(OPS[part], params, ops, fwd, cots)
+    for name in ([r.buffer for r in ops if not r.written][:1 if part != "sigmoid_mul" else 2]):
+        assert np.abs(hdc[name]).max() > 0
+        assert_parity(ddc[name], hdc[name], f"{OPS[part]} d{name}")
+    if part == "rmsnorm":
+        assert not np.abs(ddc["w"]).any()  # the gain is frozen
+
+
 @pytest.mark.parametrize("fused", [False, True])
 def test_lora_device_rows(cuda, fused):
     M, K, N, r, S = 80, 256, 192, 16, 2

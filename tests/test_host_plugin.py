@@ -15,7 +15,7 @@ from tests.plugin_util import plugin
 # op -> the frozen operand positions the reference registers for it (reference linear.cpp:444-457 and
 # device/linear.hip:760,
 # lora.cpp:534-538, gdn_kkt.cpp:355, gdn_scan.cpp:584, gdn_prep.cpp:597-600, elementwise.cpp:687; the quant
-# family's two int8 ops have none, quant.cpp)
+# family's two int8 ops have none and its fused rmsnorm producer freezes the gain, quant.cpp:1518-1533)
 FROZEN = {
     "gemm_nt": [1],
     "gemm_nt_q": [1, 2, 3],
@@ -28,6 +28,9 @@ FROZEN = {
     "gdn_chunk_scan": [6, 7, 10],
     "quant_act_i8g": [],
     "had_quant_act_i8g": [],
+    "rmsnorm_had_quant_i8g": [1],
+    "gated_had_quant_i8g": [],
+    "gate_had_quant_i8g": [],
 }
 
 
