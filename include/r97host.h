@@ -114,6 +114,29 @@ int64_t r97host_batcher_skipped(void* batcher, int64_t* out, int64_t cap);
 int64_t r97host_batcher_skipped_tokens(void* batcher);
 const char* r97host_batcher_error(void);
 
+/* ---- chat JSONL to token ids with an assistant loss mask (include/r97/chatdata.h, src/chatdata.cpp) ----
+ * The reference's ChatData: a conversation is kept through its last assistant turn, trailing assistant turns
+ * are dropped until its render fits max_tokens (none left: skipped), and each kept assistant turn scores the
+ * tokens from the end of its generation prompt to its last control token. The renderer (chat template and
+ * tokenizer) is the container's in the reference (radiance, not in this tree); this library ships the
+ * ChatML renderer over a byte vocabulary (ids 0-255 the bytes, 256 <|im_start|>, 257 <|im_end|>, both
+ * control tokens) that the reference's mask test states its expectations in. */
+void* r97host_chatdata_create_chatml_bytes(void);
+void r97host_chatdata_destroy(void* chatdata);
+/* Reads a JSONL document of len bytes ({"messages": [{"role", "content"}, ...]} a line), appending the kept
+ * sequences and adding {conversations, kept, shortened, skipped, tokens, scored} into stats[6]. 1, or 0 with
+ * "line N: <why>" in r97host_chatdata_error (the lines before it kept). */
+int32_t r97host_chatdata_read(void* chatdata, const char* text, int64_t len, int32_t max_tokens, int64_t* stats);
+int32_t r97host_chatdata_read_file(void* chatdata, const char* path, int32_t max_tokens, int64_t* stats);
+/* One JSONL line rendered and scored, not appended: 0 kept, 1 shortened, 2 skipped, 3 error; the first cap
+ * ids and scores written, the sequence's length in *n. */
+int32_t r97host_chatdata_line(void* chatdata, const char* text, int64_t len, int32_t max_tokens, int32_t* ids,
+                              uint8_t* score, int64_t cap, int64_t* n);
+int64_t r97host_chatdata_count(void* chatdata);
+int64_t r97host_chatdata_seq_len(void* chatdata, int64_t i);
+void r97host_chatdata_seq(void* chatdata, int64_t i, int32_t* ids, uint8_t* score);
+const char* r97host_chatdata_error(void* chatdata);
+
 /* ---- the training step as C++ over libr97b200.so: the reference's StepFn (include/r97/step.h:18-27; the
  * device join's make_device_step, include/r97/step_device.h:164, src/step_device.cpp:355-1678) ----
  * The LoRA step of the hybrid model (embedding, layers of 3 GatedDeltaNet : 1 gated attention each followed

@@ -1,4 +1,12 @@
-"""Training data into steps: the token-budget batcher and the step's input rows.
+"""Training data into steps: chat JSONL to scored token sequences, the token-budget batcher and the step's
+input rows.
+
+``ChatData`` mirrors the reference's ``r97::ChatData`` (include/r97/chatdata.h, src/chatdata.cpp): one
+conversation a JSONL line, kept through its last assistant turn, trailing assistant turns dropped until the
+render fits, and each assistant turn's generated tokens scored (libr97host.so, host/chatdata.cpp). The
+reference renders with its container's chat template and tokenizer (radiance, not in this tree); the
+library's renderer is ChatML over a byte vocabulary, the form the reference's own mask test states its
+expectations in.
 
 ``Batcher`` mirrors the reference's ``r97::Batcher`` (include/r97/batcher.h:46-100, src/batcher.cpp): one
 ``TokenSeq`` per example, ``BatcherConfig(token_budget, devices, seed)``, ``next()`` handing out one
@@ -46,6 +54,21 @@ def host():
         lib.r97host_batcher_skipped_tokens.restype = i64
         lib.r97host_batcher_skipped_tokens.argtypes = [vp]
         lib.r97host_batcher_error.restype = ctypes.c_char_p
+        lib.r97host_chatdata_create_chatml_bytes.restype = vp
+        lib.r97host_chatdata_destroy.argtypes = [vp]
+        lib.r97host_chatdata_read.restype = ctypes.c_int32
+        lib.r97host_chatdata_read.argtypes = [vp, ctypes.c_char_p, i64, ctypes.c_int32, p64]
+        lib.r97host_chatdata_read_file.restype = ctypes.c_int32
+        lib.r97host_chatdata_read_file.argtypes = [vp, ctypes.c_char_p, ctypes.c_int32, p64]
+        lib.r97host_chatdata_line.restype = ctypes.c_int32
+        lib.r97host_chatdata_line.argtypes = [vp, ctypes.c_char_p, i64, ctypes.c_int32, vp, vp, i64, p64]
+        lib.r97host_chatdata_count.restype = i64
+        lib.r97host_chatdata_count.argtypes = [vp]
+        lib.r97host_chatdata_seq_len.restype = i64
+        lib.r97host_chatdata_seq_len.argtypes = [vp, i64]
+        lib.r97host_chatdata_seq.argtypes = [vp, i64, vp, vp]
+        lib.r97host_chatdata_error.restype = ctypes.c_char_p
+        lib.r97host_chatdata_error.argtypes = [vp]
         _host = lib
     return _host
 
@@ -55,6 +78,94 @@ class TokenSeq:
     """One example: token ids and, per token, 1 where it is a target predicted at the position before."""
     ids: list = field(default_factory=list)
     score: list = field(default_factory=list)
+
+
+# ChatData outcomes (include/r97/chatdata.h ChatDataOutcome)
+KEPT, SHORTENED, SKIPPED, ERROR = 0, 1, 2, 3
+IM_START, IM_END = 256, 257  # the ChatML byte renderer's two control tokens
+
+
+class ChatDataError(RuntimeError):
+    pass
+
+
+class ChatData:
+    """Chat JSONL to TokenSeqs with the assistant loss mask (the reference's r97::ChatData), over the ChatML
+    byte-vocabulary renderer. ``read`` / ``read_file`` return the kept sequences and add the outcome counts
+    into ``stats`` (conversations, kept, shortened, skipped, tokens, scored); a malformed line raises
+    ChatDataError("line N: ...") after the lines before it were kept."""
+
+    DEFAULT_MAX_TOKENS = 4096
+    STATS = ("conversations", "kept", "shortened", "skipped", "tokens", "scored")
+
+    def __init__(self):
+        self._lib = host()
+        self._h = self._lib.r97host_chatdata_create_chatml_bytes()
+        self._taken = 0
+        self.stats = dict.fromkeys(self.STATS, 0)
+
+    def __del__(self):
+        if getattr(self, "_h", None):
+            self._lib.r97host_chatdata_destroy(self._h)
+            self._h = None
+
+    def _error(self):
+        return self._lib.r97host_chatdata_error(self._h).decode()
+
+    def _new(self):
+        out = []
+        n = int(self._lib.r97host_chatdata_count(self._h))
+        for i in range(self._taken, n):
+            k = int(self._lib.r97host_chatdata_seq_len(self._h, i))
+            ids = np.zeros(k, np.int32)
+            score = np.zeros(k, np.uint8)
+            self._lib.r97host_chatdata_seq(self._h, i, ids.ctypes.data, score.ctypes.data)
+            out.append(TokenSeq(ids.tolist(), score.tolist()))
+        self._taken = n
+        return out
+
+    def _count(self, st):
+        for k, v in zip(self.STATS, st):
+            self.stats[k] += int(v)
+
+    def read(self, text: str, max_tokens: int = DEFAULT_MAX_TOKENS):
+        b = text.encode()
+        st = (ctypes.c_int64 * 6)()
+        ok = self._lib.r97host_chatdata_read(self._h, b, len(b), max_tokens, st)
+        self._count(st)
+        seqs = self._new()
+        if not ok:
+            raise ChatDataError(self._error())
+        return seqs
+
+    def read_file(self, path: str, max_tokens: int = DEFAULT_MAX_TOKENS):
+        st = (ctypes.c_int64 * 6)()
+        ok = self._lib.r97host_chatdata_read_file(self._h, os.fsencode(path), max_tokens, st)
+        self._count(st)
+        seqs = self._new()
+        if not ok:
+            raise ChatDataError(self._error())
+        return seqs
+
+    def line(self, text: str, max_tokens: int = DEFAULT_MAX_TOKENS):
+        """One conversation: (outcome, TokenSeq); the sequence is not appended to the read ones."""
+        b = text.encode()
+        n = ctypes.c_int64()
+        cap = max(16, 4 * len(b) + 64)
+        ids = np.zeros(cap, np.int32)
+        score = np.zeros(cap, np.uint8)
+        o = int(self._lib.r97host_chatdata_line(self._h, b, len(b), max_tokens, ids.ctypes.data, score.ctypes.data,
+                                                cap, ctypes.byref(n)))
+        if o == ERROR:
+            raise ChatDataError(self._error())
+        k = min(int(n.value), cap)
+        return o, TokenSeq(ids[:k].tolist(), score[:k].tolist())
+
+    def render(self, messages, max_tokens: int = DEFAULT_MAX_TOKENS):
+        """A conversation given as [(role, content), ...] or [{"role", "content"}, ...]."""
+        import json
+        msgs = [m if isinstance(m, dict) else {"role": m[0], "content": m[1]} for m in messages]
+        return self.line(json.dumps({"messages": msgs}), max_tokens)
 
 
 @dataclass
