@@ -71,6 +71,55 @@ typedef struct R97IqrDecodeDesc {
 
 typedef void* R97IqrStream;
 
+/* ---- a stored weight's encoding, read as the description above (reference src/iqr_form.h) ----
+ * The fields of a container encoding (radiance's RadEncoding; not in this tree) that the derivation reads:
+ * each plane's role ("codes", "scale", "trellis", "trellis.mad", "zero", "scale.1", "scale.col"), its
+ * element type, its block (block[0] rows, block[1] columns an element; 0 = the whole extent) and, for a
+ * table, its extent (extent[0] entries). */
+enum R97bEncDtype {
+    R97B_ENC_U1 = 1, /* .. R97B_ENC_U12 = 12: packed unsigned codes of that many bits */
+    R97B_ENC_U12 = 12,
+    R97B_ENC_I8 = 20,
+    R97B_ENC_U32 = 21,
+    R97B_ENC_F32 = 30,
+    R97B_ENC_BF16 = 31,
+    R97B_ENC_F16 = 32,
+    R97B_ENC_F8E4M3 = 33,
+};
+#define R97B_ENC_MAX_PLANES 8
+typedef struct R97bEncPlane {
+    char role[24];
+    int32_t dtype;
+    int64_t block[2];
+    int64_t extent[2];
+} R97bEncPlane;
+typedef struct R97bEncoding {
+    int32_t n_planes;
+    R97bEncPlane plane[R97B_ENC_MAX_PLANES];
+} R97bEncoding;
+/* One encoding plane's bytes as stored (rows of packed elements, each row rounded up to a byte); a plane the
+ * caller does not hold is {null, 0}. */
+typedef struct R97bStoredPlane {
+    const void* data;
+    int64_t bytes;
+} R97bStoredPlane;
+
+/* The description of the whole weight [rows, cols] from an encoding's planes (plane[i] = encoding plane i):
+ * the form is derived from the planes by role (codes -> bits; a trellis table -> state_bits = log2(extent),
+ * run_rows, rb; a zero plane -> the affine grid; scale / scale.1 layouts; trellis.mad -> the computed
+ * codebook; trellis.mad or scale.col -> rounded codes). 0, or 1 when the encoding is not a form the decode
+ * reads or a plane it needs is missing or short. planes_on_device: the planes are device memory (the
+ * computed codebook's A and B are then read with one copy). The output pointers are left to the caller.
+ * Replaces: reference src/iqr_form.h:87-175 r97_iqr_desc_from_planes. */
+int r97b_iqr_desc_from_planes(const R97bEncoding* enc, const R97bStoredPlane* plane, int64_t rows, int64_t cols,
+                              int32_t planes_on_device, R97IqrDecodeDesc* out);
+/* The whole weight decoded on the device from device planes: out_codes int8 [rows, cols], out_scale bf16 bits
+ * [rows, cols / 128], with a scale.col plane's factor folded into the scale as bf16(row f32 x factor), one
+ * rounding (it is refused beside any scale but an f32 one a row). 0, or 1 as above.
+ * Replaces: reference src/iqr_form.h:189-217 r97_iqr_decode_planes (host), on the device. */
+int r97b_iqr_decode_planes(const R97bEncoding* enc, const R97bStoredPlane* plane, int64_t rows, int64_t cols,
+                           int8_t* out_codes, uint16_t* out_scale, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

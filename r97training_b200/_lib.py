@@ -79,6 +79,19 @@ class R97IqrDecodeDesc(ctypes.Structure):
     ]
 
 
+class R97bEncPlane(ctypes.Structure):
+    _fields_ = [("role", ctypes.c_char * 24), ("dtype", c_i32), ("block", c_i64 * 2), ("extent", c_i64 * 2)]
+
+
+class R97bEncoding(ctypes.Structure):
+    """include/r97b_iqr.h R97bEncoding: the encoding fields the IQR form derivation reads."""
+    _fields_ = [("n_planes", c_i32), ("plane", R97bEncPlane * 8)]
+
+
+class R97bStoredPlane(ctypes.Structure):
+    _fields_ = [("data", c_vp), ("bytes", c_i64)]
+
+
 _SIGS = {
     "r97b_abi_version": (c_i32, []),
     "r97b_device_error": (c_i32, [c_vp]),
@@ -100,6 +113,8 @@ _SIGS = {
     "r97b_fused_quant_i8g_bwd": (c_i32, [c_i32, c_vp, c_i64, c_vp, c_i64, c_vp, c_f32, c_f32, c_f32, c_i64, c_i64,
                                          c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i32,
                                          c_vp]),
+    "r97b_iqr_desc_from_planes": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_i32, c_vp]),
+    "r97b_iqr_decode_planes": (c_i32, [c_vp, c_vp, c_i64, c_i64, c_vp, c_vp, c_vp]),
     "r97b_group_scale": (c_i32, [c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64, c_vp, c_i64, c_i32, c_vp]),
     "r97b_gemm_i8g": (c_i32, [c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i64, c_vp, c_i64,
                               c_i32, c_vp]),

@@ -13,7 +13,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
-from ._lib import R97IqrDecodeDesc, check, lib
+from ._lib import R97bEncoding, R97bStoredPlane, R97IqrDecodeDesc, check, lib
 
 R97_IQR_F32, R97_IQR_BF16, R97_IQR_F8E4M3, R97_IQR_F16 = 0, 1, 2, 3
 
@@ -99,3 +99,108 @@ def dequant_bf16(w: IqrWeight, out: torch.Tensor | None = None, stream=None) -> 
     check(lib().r97b_iqr_dequant_bf16(ctypes.byref(d), ctypes.c_void_p(out.data_ptr()), out.stride(0),
                                       ctypes.c_void_p(s)), "r97b_iqr_dequant_bf16")
     return out
+
+
+# ------------------------------------------------------------------------------- encodings -> descriptions
+# The container's encoding of a stored weight (radiance's RadEncoding; here its fields the derivation reads)
+# and the planes it names, turned into the decode's description by r97b_iqr_desc_from_planes (the reference's
+# src/iqr_form.h). Element types: ENC_U(bits) packed codes, ENC_I8, ENC_U32, ENC_F32, ENC_BF16, ENC_F16,
+# ENC_F8E4M3.
+ENC_I8, ENC_U32, ENC_F32, ENC_BF16, ENC_F16, ENC_F8E4M3 = 20, 21, 30, 31, 32, 33
+
+
+def ENC_U(bits: int) -> int:
+    return bits
+
+
+def enc_bits(dtype: int) -> int:
+    if 1 <= dtype <= 12:
+        return dtype
+    return {ENC_I8: 8, ENC_F8E4M3: 8, ENC_BF16: 16, ENC_F16: 16, ENC_F32: 32, ENC_U32: 32}[dtype]
+
+
+def enc_row_bytes(dtype: int, n: int) -> int:
+    """Bytes of a stored row of n elements: packed bits, rounded up to a byte."""
+    return (n * enc_bits(dtype) + 7) // 8
+
+
+class Encoding:
+    """An encoding under construction: planes (an element a block[0] rows x block[1] columns of the weight,
+    0 = the whole extent) and tables (extent[0] x extent[1] elements)."""
+
+    def __init__(self):
+        self.c = R97bEncoding()
+        self.c.n_planes = 0
+
+    def _add(self, role, dtype):
+        i = self.c.n_planes
+        if i >= 8:
+            raise ValueError("an encoding holds at most 8 planes")
+        p = self.c.plane[i]
+        p.role = role.encode()
+        p.dtype = dtype
+        self.c.n_planes = i + 1
+        return i
+
+    def add_plane(self, role, dtype, block_rows, block_cols):
+        i = self._add(role, dtype)
+        self.c.plane[i].block[0], self.c.plane[i].block[1] = block_rows, block_cols
+        return i
+
+    def add_table(self, role, dtype, n0, n1):
+        i = self._add(role, dtype)
+        self.c.plane[i].extent[0], self.c.plane[i].extent[1] = n0, n1
+        return i
+
+    def index(self, role):
+        for i in range(self.c.n_planes):
+            if self.c.plane[i].role.decode() == role:
+                return i
+        return -1
+
+    def plane_shape(self, i, rows, cols):
+        """(stored rows, elements a stored row) of plane i over a [rows, cols] weight."""
+        p = self.c.plane[i]
+        if p.extent[0] > 0:
+            return 1, p.extent[0] * max(1, p.extent[1])
+        prows = 1 if p.block[0] == 0 else -(-rows // p.block[0])
+        pcols = 1 if p.block[1] == 0 else -(-cols // p.block[1])
+        return prows, pcols
+
+    def plane_bytes(self, i, rows, cols):
+        prows, pcols = self.plane_shape(i, rows, cols)
+        return prows * enc_row_bytes(self.c.plane[i].dtype, pcols)
+
+
+def stored_planes(planes):
+    """A ctypes array of R97bStoredPlane over host numpy arrays or device torch tensors (None: not held)."""
+    arr = (R97bStoredPlane * max(1, len(planes)))()
+    for i, p in enumerate(planes):
+        if p is None:
+            continue
+        if isinstance(p, torch.Tensor):
+            arr[i].data, arr[i].bytes = p.data_ptr(), p.numel() * p.element_size()
+        else:
+            arr[i].data, arr[i].bytes = p.ctypes.data, p.nbytes
+    return arr
+
+
+def desc_from_planes(enc: Encoding, planes, rows: int, cols: int, on_device: bool = False):
+    """The decode's description derived from the encoding's planes, or None when it is refused."""
+    d = R97IqrDecodeDesc()
+    rc = lib().r97b_iqr_desc_from_planes(ctypes.byref(enc.c), stored_planes(planes), rows, cols,
+                                         1 if on_device else 0, ctypes.byref(d))
+    return d if rc == 0 else None
+
+
+def decode_planes(enc: Encoding, planes, rows: int, cols: int, stream=None):
+    """The whole weight decoded on the device from its device planes: (int8 codes [rows, cols], bf16-bit
+    scale [rows, cols / 128] as int16), or None when the encoding is refused."""
+    dev = next(p.device for p in planes if p is not None)
+    codes = torch.empty((rows, cols), dtype=torch.int8, device=dev)
+    scale = torch.empty((rows, cols // 128), dtype=torch.int16, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream if stream is None else stream
+    rc = lib().r97b_iqr_decode_planes(ctypes.byref(enc.c), stored_planes(planes), rows, cols,
+                                      ctypes.c_void_p(codes.data_ptr()), ctypes.c_void_p(scale.data_ptr()),
+                                      ctypes.c_void_p(s))
+    return (codes, scale) if rc == 0 else None
