@@ -15,9 +15,15 @@
 // scales while the next group's MMAs run into the other half of tensor memory:
 //   warp 0     TMA producer: per group a [128 x 128] int8 box of a and two of b, into a 4-deep ring
 //   warp 1     MMA issuer: 4 x tcgen05.mma.kind::i8 (M 128, N 256, K 32) per group into TMEM buffer g & 1
-//   warps 2-9  epilogue: warp w owns TMEM lanes 32 (w % 4) .. + 31 (its rows) and columns 128 ((w - 2) / 4)
-//              .. + 127; per element t = f32(s32) -- exact, |s32| <= 128 * 127 * 127 < 2^22, converted by
-//              the integer add of the bits of 1.5 * 2^23 -- then acc += (t sb[n]) sa[m]
+//              (warps 2 and 3 only complete warpgroup 0, whose registers go to the epilogue: setmaxnreg)
+//   warps 4-11 epilogue: warp w owns TMEM lanes 32 (w % 4) .. + 31 (its rows) and columns 128 ((w - 4) / 4)
+//              .. + 127; per element acc += (t sb[n]) sa[m], t the group's exact integer sum as f32
+// The conversion costs one add: every accumulator starts a group holding the bits of 1.5 * 2^23 (the epilogue
+// writes them back as soon as it has drained a chunk), the MMAs add the group's sum to those bits as an
+// integer (|sum| <= 128 * 127 * 127 < 2^22: no carry leaves the mantissa), and the bits read back are the float
+// 1.5 * 2^23 + sum exactly. The fold runs on packed f32x2 instructions (two columns each); the TMEM loads are
+// 16-column chunks with the next one in flight while the current one is folded in, which the 232 registers
+// an epilogue thread gets (setmaxnreg, below) leave room for beside the 128 accumulators.
 // One CTA per 128 x 256 output tile (for the fold: 128 gate columns and the 128 up columns they pair with),
 // one CTA an SM (196 KB of shared memory, all 512 TMEM columns). The int8 operands are addressed through
 // bf16-typed tensor maps of half the width: the 128-byte swizzle moves the same bytes either way.
@@ -37,7 +43,7 @@ constexpr int kStageBytes = kABytes + kBN * kGroup;  // 48 KB
 constexpr int kScaleOff = kStages * kStageBytes;     // column scales [2][256] f32
 constexpr int kBarOff = kScaleOff + 2 * kBN * 4;
 constexpr int kSmem = kBarOff + 128 + 1024;          // + barriers, + the 1024-byte alignment slack
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;  // warpgroup 0: producer, MMA issuer, two idle warps; 1-2: epilogue
 constexpr int kPitch = 132;                          // f32 row pitch of the epilogue's staging rows
 constexpr float kTop = 127.0f;
 
@@ -82,7 +88,8 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t adesc, uint64_
         : "memory");
 }
 
-// 32 lanes x 16 consecutive 32-bit columns of TMEM into 16 registers of each thread.
+constexpr uint32_t kBiasBits = 0x4B400000u;  // the float 1.5 * 2^23
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
@@ -90,15 +97,55 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_bias16(uint32_t taddr) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(
+                     taddr),
+                 "r"(kBiasBits)
+                 : "memory");
+}
+
+// Writes the bias bits into 32 consecutive columns of the warp's 32 TMEM lanes.
+__device__ __forceinline__ void tmem_bias32(uint32_t taddr) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,"
+        "%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1,%1};" ::"r"(taddr),
+        "r"(kBiasBits)
+        : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Packed f32 pairs (sm_100 f32x2 arithmetic, round to nearest).
+__device__ __forceinline__ uint64_t pk(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ uint64_t pk_bits(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+__device__ __forceinline__ void unpk(uint64_t v, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
 
 // The 256 epilogue threads' own barrier (named barrier 1).
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
-
-// An s32 of magnitude below 2^22 as f32, exactly: the bits of 1.5 * 2^23 plus the integer are the float
-// 1.5 * 2^23 + x.
-__device__ __forceinline__ float s32_to_f32(uint32_t x) {
-    return __int_as_float((int)(x + 0x4B400000u)) - 12582912.0f;
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB, const I8Args args) {
@@ -145,7 +192,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-
+    // The launch gives every thread 168 registers; warpgroup 0 (one elected thread a role) gives 128 of its
+    // back and each epilogue warpgroup takes 64 more: 128 x 40 + 256 x 232 = 384 x 168, the launch's total
+    // (per SM sub-partition: one warp of warpgroup 0 and two epilogue warps, (40 + 2 x 232) x 32 = 16128).
+    if (warp < 4) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 40;" ::: "memory");
     if (warp == 0 && lane == 0) {
         // ------------------------------------------------------------- TMA producer
         for (int g = 0; g < G; ++g) {
@@ -163,20 +214,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         constexpr uint32_t idesc = make_idesc_i8(kBM, kBN);
         for (int g = 0; g < G; ++g) {
             const int s = g % kStages, b = g & 1;
-            if (!mbar_wait(&acc_empty[b], ((g >> 1) & 1) ^ 1u, abort_flag)) break;
+            if (!mbar_wait(&acc_empty[b], (g >> 1) & 1, abort_flag)) break;
             if (!mbar_wait(&full_bar[s], (g / kStages) & 1, abort_flag)) break;
             tc_fence_after();
             const uint32_t sa = smem_u32(smem + s * kStageBytes), sb = sa + kABytes;
 #pragma unroll
             for (int kk = 0; kk < kGroup / 32; ++kk)
                 umma_i8(tmem + (uint32_t)(b * kBN), make_sdesc_sw128(sa + kk * 32, 16, 1024),
-                        make_sdesc_sw128(sb + kk * 32, 16, 1024), idesc, kk > 0 ? 1u : 0u);
+                        make_sdesc_sw128(sb + kk * 32, 16, 1024), idesc, 1u);  // onto the bias bits
             umma_commit(&empty_bar[s]);
             umma_commit(&acc_full[b]);
         }
-    } else if (warp >= 2) {
+    }
+    } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 232;" ::: "memory");
         // ------------------------------------------------------------- epilogue
-        const int e = warp - 2, qd = warp & 3, h = e >> 2, et = threadIdx.x - 64;
+        const int e = warp - 4, qd = warp & 3, h = e >> 2, et = threadIdx.x - 128;
         const int row = 32 * qd + lane;
         const int64_t m = m0 + row;
         const bool mrow = m < args.M;
@@ -184,12 +237,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool bok = brow < args.N;
         const float* sa_row = args.a_scale + (mrow ? m : 0) * args.ld_as;
         const float* sb_row = args.b_scale + (bok ? brow : 0) * args.ld_bs;
-        float acc[128];
+        uint64_t acc2[64];  // column pairs (2 i, 2 i + 1)
 #pragma unroll
-        for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+        for (int i = 0; i < 64; ++i) acc2[i] = 0;
         float sa_nx = mrow ? sa_row[0] : 0.0f, sb_nx = bok ? sb_row[0] : 0.0f;
         bool ok = true;
         const uint32_t tlane = tmem + ((uint32_t)(32 * qd) << 16) + (uint32_t)(h * 128);
+        // both accumulator buffers start at the bias; the MMA issuer's first wait on each is this arrival
+#pragma unroll
+        for (int c = 0; c < 8; ++c) tmem_bias32(tlane + (uint32_t)((c >> 2) * kBN + (c & 3) * 32));
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+            mbar_arrive(&acc_empty[0]);
+            mbar_arrive(&acc_empty[1]);
+        }
+        const uint64_t neg_bias = pk(-12582912.0f, -12582912.0f);
 #pragma unroll 1
         for (int g = 0; g < G; ++g) {
             const int b = g & 1;
@@ -205,25 +269,42 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_after();
             if (ok) {
                 const float* sc = sbs + b * kBN + h * 128;
+                const uint64_t sa2 = pk(sa_g, sa_g);
+                // 16-column chunks: each written back to the bias as soon as it is drained, the next one's load
+                // in flight while this one is folded in
+                uint32_t ra[16], rb[16];
+                const uint32_t tb = tlane + (uint32_t)(b * kBN);
+                auto fold = [&](const uint32_t(&r)[16], int c) {
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t r[16];
-                    tmem_ld16(tlane + (uint32_t)(b * kBN + c * 16), r);
-                    tmem_ld_wait();
-#pragma unroll
-                    for (int i = 0; i < 16; i += 4) {
-                        const float4 s4 = *reinterpret_cast<const float4*>(sc + c * 16 + i);
-                        acc[c * 16 + i] = fmaf(s32_to_f32(r[i]) * s4.x, sa_g, acc[c * 16 + i]);
-                        acc[c * 16 + i + 1] = fmaf(s32_to_f32(r[i + 1]) * s4.y, sa_g, acc[c * 16 + i + 1]);
-                        acc[c * 16 + i + 2] = fmaf(s32_to_f32(r[i + 2]) * s4.z, sa_g, acc[c * 16 + i + 2]);
-                        acc[c * 16 + i + 3] = fmaf(s32_to_f32(r[i + 3]) * s4.w, sa_g, acc[c * 16 + i + 3]);
+                    for (int i = 0; i < 4; ++i) {
+                        const float4 s4 = *reinterpret_cast<const float4*>(sc + c * 16 + 4 * i);
+                        acc2[c * 8 + 2 * i] = fma2(mul2(add2(pk_bits(r[4 * i], r[4 * i + 1]), neg_bias),
+                                                        pk(s4.x, s4.y)), sa2, acc2[c * 8 + 2 * i]);
+                        acc2[c * 8 + 2 * i + 1] = fma2(mul2(add2(pk_bits(r[4 * i + 2], r[4 * i + 3]), neg_bias),
+                                                            pk(s4.z, s4.w)), sa2, acc2[c * 8 + 2 * i + 1]);
                     }
+                };
+                tmem_ld16(tb, ra);
+#pragma unroll
+                for (int c = 0; c < 8; c += 2) {
+                    tmem_ld_wait();
+                    tmem_bias16(tb + (uint32_t)(c * 16));
+                    tmem_ld16(tb + (uint32_t)((c + 1) * 16), rb);
+                    fold(ra, c);
+                    tmem_ld_wait();
+                    tmem_bias16(tb + (uint32_t)((c + 1) * 16));
+                    if (c + 2 < 8) tmem_ld16(tb + (uint32_t)((c + 2) * 16), ra);
+                    fold(rb, c + 1);
                 }
+                tmem_st_wait();
             }
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[b]);
         }
+        float acc[128];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) unpk(acc2[i], acc[2 * i], acc[2 * i + 1]);
         // every MMA has completed (each warp saw the last group's commit): the ring is free for staging
         float* ring = reinterpret_cast<float*>(smem);
         if (!args.gated) {
