@@ -20,6 +20,7 @@ The attention core (softmax(q k^T) v, causal, GQA) runs on this package's tcgen0
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass, field
 
@@ -356,6 +357,8 @@ class TrainStep:
         self.grad_hook = None
         self.launches = 0
         self.split_ws = ops.SplitWorkspace(model.device)
+        # the side stream the GDN layers' out-projection adapter gradients run on (None: all on one stream)
+        self.side = torch.cuda.Stream(device=model.device) if model.device.type == "cuda" else None
         self.attn_ws = None  # the attention backward's P / dS tiles, allocated at the first attention layer
 
     # ------------------------------------------------------------------ decoded base weights
@@ -406,9 +409,11 @@ class TrainStep:
                  mode=ops.EPI_SPLIT_BF16 if splits > 1 else ops.EPI_STORE_BF16, ws=self.split_ws.buf)
 
     def _lin_bwd(self, li, g: Group, x: torch.Tensor, t: torch.Tensor, W: torch.Tensor, dy: torch.Tensor,
-                 dx_out: torch.Tensor, swiglu_gu=None):
+                 dx_out: torch.Tensor, swiglu_gu=None, side=None):
         """dt = s dY B_blk ; dX = dY W + dt A_all ; dA_all += dt^T x ; dB_i += dY_i^T t_i. With `swiglu_gu`
-        (the down group, whose input is silu(g) u) dx_out receives SwiGLU's adjoint [dg | du] instead."""
+        (the down group, whose input is silu(g) u) dx_out receives SwiGLU's adjoint [dg | du] instead. With
+        `side` (a stream), the two adapter-gradient products are issued there, ordered after dt, and the
+        caller joins it before the layer's gradient is read."""
         cfg, ad = self.cfg, self.adapter
         r = cfg.rank
         if not g.lora:
@@ -424,15 +429,22 @@ class TrainStep:
                      addend=swiglu_gu)
         else:
             ops.gemm(dy, W, dx_out, b_mn=True, a2=dt, b2=ad.a_bf[(li, g.name)], N=g.k)
-        bn, splits = ops.grad_tiling(g.k, g.r_all * r, dy.shape[0])
-        ops.gemm(x, dt, ad.a_view(ad.g, g), a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32T, splits=splits,
-                 bn=bn, M=g.k, N=g.r_all * r)
-        col = 0
-        for i, (_, n) in enumerate(g.projs):
-            bn, splits = ops.grad_tiling(n, r, dy.shape[0])
-            ops.gemm(dy[:, col:col + n], t[:, i * r:(i + 1) * r], ad.b_view(ad.g, g, i), a_mn=True, b_mn=True,
-                     mode=ops.EPI_ATOMIC_F32, splits=splits, bn=bn, M=n, N=r)
-            col += n
+        if side is not None:
+            ev = torch.cuda.Event()
+            ev.record()
+            side.wait_event(ev)
+            for u in (x, t, dy, dt):
+                u.record_stream(side)
+        with torch.cuda.stream(side) if side is not None else contextlib.nullcontext():
+            bn, splits = ops.grad_tiling(g.k, g.r_all * r, dy.shape[0])
+            ops.gemm(x, dt, ad.a_view(ad.g, g), a_mn=True, b_mn=True, mode=ops.EPI_ATOMIC_F32T, splits=splits,
+                     bn=bn, M=g.k, N=g.r_all * r)
+            col = 0
+            for i, (_, n) in enumerate(g.projs):
+                bn, splits = ops.grad_tiling(n, r, dy.shape[0])
+                ops.gemm(dy[:, col:col + n], t[:, i * r:(i + 1) * r], ad.b_view(ad.g, g, i), a_mn=True,
+                         b_mn=True, mode=ops.EPI_ATOMIC_F32, splits=splits, bn=bn, M=n, N=r)
+                col += n
 
     # ------------------------------------------------------------------ blocks
     def _gdn_fwd(self, li, blk, x, sv):
@@ -468,7 +480,9 @@ class TrainStep:
         qk = Hg * K
         W = self._w_bwd(li, g_out)
         don = torch.empty((T, H * K), dtype=torch.bfloat16, device=x.device)
-        self._lin_bwd(li, g_out, sv["on"], sv["t_out"], W, dh1, don)
+        # the out-projection's adapter gradients need nothing the GDN adjoint computes: on the side stream they
+        # run beside it (its state passes hold 128 of the SMs), joined before the layer's gradient is read
+        self._lin_bwd(li, g_out, sv["on"], sv["t_out"], W, dh1, don, side=self.side)
         y_in = sv["y_in"]
         zsl = slice(2 * qk + H * K, 2 * qk + 2 * H * K)
         d_yin = torch.empty_like(y_in)
@@ -486,6 +500,8 @@ class TrainStep:
         W = self._w_bwd(li, g_in)
         dn1 = torch.empty_like(x)
         self._lin_bwd(li, g_in, sv["n1"], sv["t_in"], W, d_yin, dn1)
+        if self.side is not None:
+            torch.cuda.current_stream().wait_stream(self.side)
         return ops.rmsnorm_bwd(x, blk["w_in"], dn1, addend=dh1, eps=cfg.eps)
 
     def _attn_fwd(self, li, blk, x, sv):
