@@ -157,3 +157,30 @@ def test_markers_in_content_are_parsed_as_control_tokens():
     assert seq.ids.count(IM_END) == 3
     scored = [i for i, s in zip(seq.ids, seq.score) if s]
     assert scored == [ord("A"), IM_END, ord("B"), IM_END]
+
+
+def test_random_conversations_round_trip():
+    """Seeded random conversations -- any code point (surrogate pairs included), escapes, extra keys and
+    whitespace -- written by Python's json and read back: ids and mask as the template and the byte
+    vocabulary give them."""
+    import random
+    rnd = random.Random(7)
+    alphabet = list("ab /{}[]:,<|>") + ["\n", "\t", '"', "\\", "é", "中", "\U0001F600", "\u0007"]
+    cd = ChatData()
+    for _ in range(200):
+        msgs = []
+        for k in range(rnd.randint(1, 6)):
+            role = rnd.choice(["system", "user", "assistant"]) if k else rnd.choice(["system", "user"])
+            content = "".join(rnd.choice(alphabet) for _ in range(rnd.randint(0, 12)))
+            msgs.append((role, content))
+        doc = {"meta": {"n": rnd.random(), "tags": [1, None, True]},
+               "messages": [{"role": r, "content": c, "extra": [1.5e-3]} for r, c in msgs]}
+        line = json.dumps(doc, ensure_ascii=rnd.random() < 0.5, indent=rnd.choice([None, 1]))
+        line = line.replace("\n", " ")
+        o, seq = cd.line(line)
+        last = max((i for i, (r, _) in enumerate(msgs) if r == "assistant"), default=-1)
+        if last < 0:
+            assert o == SKIPPED
+            continue
+        assert o == KEPT
+        check(seq, expected(msgs[:last + 1]))
