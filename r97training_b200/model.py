@@ -349,6 +349,7 @@ class TrainStep:
         # decode of every weight); False decodes into one shared scratch in both passes.
         self.keep_decoded = keep_decoded
         self.w_keep = {}
+        self.w_pending = {}  # (layer, group) -> the side-stream event its prefetched decode completes
         cfg = self.cfg
         self.T = cfg.tokens
         cu = np.arange(0, self.T + 1, cfg.seq, dtype=np.int32)
@@ -363,14 +364,38 @@ class TrainStep:
 
     # ------------------------------------------------------------------ decoded base weights
     def _w_fwd(self, li, g: Group) -> torch.Tensor:
-        """The group's base weight for the forward: decoded now."""
+        """The group's base weight for the forward: decoded now, or by `_prefetch` on the side stream."""
         if not self.keep_decoded:
             return decode_group(g, self.ws.w_scratch)
+        ev = self.w_pending.pop((li, g.name), None)
+        if ev is not None:
+            torch.cuda.current_stream().wait_event(ev)
+            return self.w_keep[(li, g.name)][:g.n * g.k].view(g.n, g.k)
         buf = self.w_keep.get((li, g.name))
         if buf is None:
             buf = torch.empty(g.n * g.k, dtype=torch.bfloat16, device=self.model.device)
             self.w_keep[(li, g.name)] = buf
         return decode_group(g, buf)
+
+    def _prefetch(self, li, groups):
+        """Decodes `groups` of layer li on the side stream (ordered after the work queued so far), for a
+        `_w_fwd` of the same layer to wait on instead of decoding: during a GDN state pass, which holds 128 of
+        the SMs, the decode runs on the rest."""
+        if not self.keep_decoded or self.side is None:
+            return
+        ev0 = torch.cuda.Event()
+        ev0.record()
+        self.side.wait_event(ev0)
+        for g in groups:
+            buf = self.w_keep.get((li, g.name))
+            if buf is None:
+                buf = torch.empty(g.n * g.k, dtype=torch.bfloat16, device=self.model.device)
+                self.w_keep[(li, g.name)] = buf
+            with torch.cuda.stream(self.side):
+                decode_group(g, buf)
+                ev = torch.cuda.Event()
+                ev.record()
+            self.w_pending[(li, g.name)] = ev
 
     def _w_bwd(self, li, g: Group) -> torch.Tensor:
         """The group's base weight for the backward: this step's forward decode, or decoded again."""
@@ -464,6 +489,8 @@ class TrainStep:
         beta = torch.empty_like(gg)
         ba = y_in[:, 2 * qk + 2 * H * K:]
         ops.gates_fwd(ba, blk["a_log"], blk["dt_bias"], self.plan, gg, beta)
+        # the block's remaining weights decode on the side stream while the GDN state pass holds 128 SMs
+        self._prefetch(li, [g_out, blk["groups"][2], blk["groups"][3]])
         o, _, gsv = self.plan.forward(q, k, v, gg, beta)
         z = y_in[:, 2 * qk + H * K:2 * qk + 2 * H * K]  # read in place (strided), no copy
         on = ops.gated_rmsnorm_fwd(o.view(T * H, K), z, blk["gnorm_w"], eps=cfg.eps).view(T, H * K)
