@@ -489,8 +489,11 @@ class TrainStep:
         beta = torch.empty_like(gg)
         ba = y_in[:, 2 * qk + 2 * H * K:]
         ops.gates_fwd(ba, blk["a_log"], blk["dt_bias"], self.plan, gg, beta)
-        # the block's remaining weights decode on the side stream while the GDN state pass holds 128 SMs
+        # the block's remaining weights, and the next block's input projection, decode on the side stream
+        # while the GDN state pass holds 128 SMs
         self._prefetch(li, [g_out, blk["groups"][2], blk["groups"][3]])
+        if li + 1 < len(self.model.blocks):
+            self._prefetch(li + 1, [self.model.blocks[li + 1]["groups"][0]])
         o, _, gsv = self.plan.forward(q, k, v, gg, beta)
         z = y_in[:, 2 * qk + H * K:2 * qk + 2 * H * K]  # read in place (strided), no copy
         on = ops.gated_rmsnorm_fwd(o.view(T * H, K), z, blk["gnorm_w"], eps=cfg.eps).view(T, H * K)
