@@ -197,35 +197,35 @@ __global__ void __launch_bounds__(kThreads, 1)
     // (per SM sub-partition: one warp of warpgroup 0 and two epilogue warps, (40 + 2 x 232) x 32 = 16128).
     if (warp < 4) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 40;" ::: "memory");
-    if (warp == 0 && lane == 0) {
-        // ------------------------------------------------------------- TMA producer
-        for (int g = 0; g < G; ++g) {
-            const int s = g % kStages;
-            if (!mbar_wait(&empty_bar[s], ((g / kStages) & 1) ^ 1u, abort_flag)) break;
-            uint8_t* st = smem + s * kStageBytes;
-            mbar_expect_tx(&full_bar[s], kStageBytes);
-            const int x = g * (kGroup / 2);  // in the maps' bf16 units
-            tma_load_2d(st, &tA, &full_bar[s], x, (int32_t)m0);
-            tma_load_2d(st + kABytes, &tB, &full_bar[s], x, (int32_t)b_lo);
-            tma_load_2d(st + kABytes + 128 * kGroup, &tB, &full_bar[s], x, (int32_t)b_hi);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // ------------------------------------------------------------- MMA issuer
-        constexpr uint32_t idesc = make_idesc_i8(kBM, kBN);
-        for (int g = 0; g < G; ++g) {
-            const int s = g % kStages, b = g & 1;
-            if (!mbar_wait(&acc_empty[b], (g >> 1) & 1, abort_flag)) break;
-            if (!mbar_wait(&full_bar[s], (g / kStages) & 1, abort_flag)) break;
-            tc_fence_after();
-            const uint32_t sa = smem_u32(smem + s * kStageBytes), sb = sa + kABytes;
+        if (warp == 0 && lane == 0) {
+            // ------------------------------------------------------------- TMA producer
+            for (int g = 0; g < G; ++g) {
+                const int s = g % kStages;
+                if (!mbar_wait(&empty_bar[s], ((g / kStages) & 1) ^ 1u, abort_flag)) break;
+                uint8_t* st = smem + s * kStageBytes;
+                mbar_expect_tx(&full_bar[s], kStageBytes);
+                const int x = g * (kGroup / 2);  // in the maps' bf16 units
+                tma_load_2d(st, &tA, &full_bar[s], x, (int32_t)m0);
+                tma_load_2d(st + kABytes, &tB, &full_bar[s], x, (int32_t)b_lo);
+                tma_load_2d(st + kABytes + 128 * kGroup, &tB, &full_bar[s], x, (int32_t)b_hi);
+            }
+        } else if (warp == 1 && lane == 0) {
+            // ------------------------------------------------------------- MMA issuer
+            constexpr uint32_t idesc = make_idesc_i8(kBM, kBN);
+            for (int g = 0; g < G; ++g) {
+                const int s = g % kStages, b = g & 1;
+                if (!mbar_wait(&acc_empty[b], (g >> 1) & 1, abort_flag)) break;
+                if (!mbar_wait(&full_bar[s], (g / kStages) & 1, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t sa = smem_u32(smem + s * kStageBytes), sb = sa + kABytes;
 #pragma unroll
-            for (int kk = 0; kk < kGroup / 32; ++kk)
-                umma_i8(tmem + (uint32_t)(b * kBN), make_sdesc_sw128(sa + kk * 32, 16, 1024),
-                        make_sdesc_sw128(sb + kk * 32, 16, 1024), idesc, 1u);  // onto the bias bits
-            umma_commit(&empty_bar[s]);
-            umma_commit(&acc_full[b]);
+                for (int kk = 0; kk < kGroup / 32; ++kk)
+                    umma_i8(tmem + (uint32_t)(b * kBN), make_sdesc_sw128(sa + kk * 32, 16, 1024),
+                            make_sdesc_sw128(sb + kk * 32, 16, 1024), idesc, 1u);  // onto the bias bits
+                umma_commit(&empty_bar[s]);
+                umma_commit(&acc_full[b]);
+            }
         }
-    }
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 232;" ::: "memory");
         // ------------------------------------------------------------- epilogue
