@@ -109,7 +109,8 @@ typedef struct R97bStoredPlane {
  * run_rows, rb; a zero plane -> the affine grid; scale / scale.1 layouts; trellis.mad -> the computed
  * codebook; trellis.mad or scale.col -> rounded codes). 0, or 1 when the encoding is not a form the decode
  * reads or a plane it needs is missing or short. planes_on_device: the planes are device memory (the
- * computed codebook's A and B are then read with one copy). The output pointers are left to the caller.
+ * computed codebook's A and B are then read with one blocking copy, so the planes must already be written,
+ * not pending on another stream). The output pointers are left to the caller.
  * Replaces: reference src/iqr_form.h:87-175 r97_iqr_desc_from_planes. */
 int r97b_iqr_desc_from_planes(const R97bEncoding* enc, const R97bStoredPlane* plane, int64_t rows, int64_t cols,
                               int32_t planes_on_device, R97IqrDecodeDesc* out);
